@@ -1,0 +1,872 @@
+// attention.cu -- paged decode attention (GQA, causal for Lq > 1) over bf16
+// pages and over TurboQuant 4-bit pages.
+//
+// Reference op replaced: fast::scaled_dot_product_attention (utils.rs:45-60)
+// with the decode masks of utils.rs:64-125; the contiguous per-sequence cache
+// of cache.rs:130-312 is the special case of a block table whose pages are
+// consecutive (page_stride / head_stride describe either layout).
+//
+// Design:
+//  * grid (splits, Hkv, B), 4 warps per CTA.  The query rows of one kv head
+//    (G = Hq/Hkv heads x Lq query tokens) form a 16- or 32-row MMA tile, so
+//    K and V bytes are read once for all heads of the group;
+//  * each warp streams its own pages (16 tokens) into shared memory with
+//    cp.async (double-buffered, XOR-swizzled rows), computes S = Q K^T and
+//    O += P V with mma.sync m16n8k16 and an online softmax in base 2;
+//  * the 4 warps merge in shared memory; with several splits each CTA writes
+//    a normalised partial (O, log-sum-exp) to the workspace and the last CTA of
+//    a (sequence, kv head) to arrive -- counted with an atomic -- merges them,
+//    so no second kernel is launched;
+//  * TurboQuant pages: K codes feed the MMA directly as bf16 (128 + c) against
+//    the rotated query (the constant offset is removed per row), V codes are
+//    expanded to exact bf16 (c - 8) in shared memory with the per-token scale
+//    folded into P, and the merged output is rotated back with the inverse
+//    Hadamard transform.
+#include "common.cuh"
+
+namespace higgs {
+
+constexpr int kAttnThreads = 128;
+constexpr int kCounterBytes = 4096;
+constexpr int kTargetCtas = 2 * 148;
+
+struct AttnArgs {
+  const uint16_t* q;
+  int B, Lq, Hq, Hkv;
+  int tq0, lq_chunk;  // query tokens [tq0, tq0 + lq_chunk) of Lq handled by this launch
+  const uint16_t* kc;
+  const uint16_t* vc;
+  const uint8_t* kcode;
+  const __half* kscale;
+  const uint8_t* vcode;
+  const __half* vscale;
+  const int8_t* signs;
+  int64_t page_stride, head_stride;
+  const int32_t* bt;
+  int max_blocks;
+  const int32_t* seq_lens;
+  float scale_log2;
+  uint16_t* out;
+  int splits, pages_per_split;
+  float* ws_o;
+  float* ws_lse;
+  int* counters;
+};
+
+__device__ __forceinline__ int swz(int row, int chunk) { return chunk ^ (row & 7); }
+
+// Loads one page (16 rows x D bf16) into a swizzled smem tile; rows >= valid
+// are zero-filled so masked garbage can never become NaN in P*V.
+template <int D>
+__device__ __forceinline__ void load_page_bf16(uint16_t* dst, const uint16_t* src, int valid,
+                                               int lane) {
+  constexpr int CH = D / 8;
+#pragma unroll
+  for (int i = 0; i < (16 * CH) / 32; ++i) {
+    const int qd = lane + 32 * i;
+    const int r = qd / CH, c = qd % CH;
+    const uint32_t sdst = smem_u32(dst + r * D + swz(r, c) * 8);
+    const void* gsrc = src + r * D + c * 8;
+    const int bytes = r < valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sdst), "l"(gsrc),
+                 "r"(bytes));
+  }
+}
+
+__device__ __forceinline__ void row_stats_update(float (&m)[2], float (&l)[2], float (&s)[2][4],
+                                                 float (&alpha)[2]) {
+#pragma unroll
+  for (int hlf = 0; hlf < 2; ++hlf) {
+    float mx = fmaxf(fmaxf(s[0][2 * hlf], s[0][2 * hlf + 1]), fmaxf(s[1][2 * hlf], s[1][2 * hlf + 1]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mn = fmaxf(m[hlf], mx);
+    alpha[hlf] = (mn == -INFINITY) ? 1.0f : exp2f(m[hlf] - mn);
+    m[hlf] = mn;
+    float rs = 0.0f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float& v = s[nt][2 * hlf + e];
+        v = (mn == -INFINITY) ? 0.0f : exp2f(v - mn);
+        rs += v;
+      }
+    l[hlf] = l[hlf] * alpha[hlf] + rs;
+  }
+}
+
+// Common tail: CTA-level merge of the 4 warps, then either the final store or a
+// split partial plus the last-CTA merge.  o_sm rows are in "physical" d order;
+// `finish` converts a merged f32 row to the bf16 output (TurboQuant rotates
+// back there).
+template <int D, int MT, typename Finish>
+__device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][2],
+                                              float (&l)[MT][2], float (&o)[MT][D / 8][4],
+                                              float* smem_f, int b, int h, int split, int R,
+                                              Finish finish) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int RP = 16 * MT;
+  float* sm_m = smem_f;                    // [4][RP]
+  float* sm_l = sm_m + 4 * RP;             // [4][RP]
+  float* sm_lse = sm_l + 4 * RP;           // [RP]
+  float* sm_o = sm_lse + RP;               // [4][RP][D]
+  __syncthreads();  // page buffers are dead from here on
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+    for (int hlf = 0; hlf < 2; ++hlf) {
+      float lv = l[mt][hlf];
+      lv += __shfl_xor_sync(0xffffffffu, lv, 1);
+      lv += __shfl_xor_sync(0xffffffffu, lv, 2);
+      const int row = mt * 16 + g + 8 * hlf;
+      if (t == 0) {
+        sm_m[warp * RP + row] = m[mt][hlf];
+        sm_l[warp * RP + row] = lv;
+      }
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          sm_o[(warp * RP + row) * D + dt * 8 + 2 * t + e] = o[mt][dt][2 * hlf + e];
+    }
+  __syncthreads();
+  // merge the 4 warps into warp 0's slot, normalised; each (row, d) is read and
+  // written by one thread only
+  for (int i = threadIdx.x; i < R * D; i += kAttnThreads) {
+    const int row = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w * RP + row]);
+    float L = 0.0f, O = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sm_m[w * RP + row];
+      const float sc = (mw == -INFINITY) ? 0.0f : exp2f(mw - M);
+      L += sc * sm_l[w * RP + row];
+      O += sc * sm_o[(w * RP + row) * D + d];
+    }
+    sm_o[row * D + d] = L > 0.0f ? O / L : 0.0f;
+    if (d == 0) sm_lse[row] = L > 0.0f ? M + log2f(L) : -INFINITY;
+  }
+  __syncthreads();
+  const int bh = b * a.Hkv + h;
+  if (a.splits == 1) {
+    finish(sm_o, R, b, h);
+    return;
+  }
+  // write the split partial (valid rows only)
+  float* po = a.ws_o + ((size_t)bh * a.splits + split) * RP * D;
+  float* pl = a.ws_lse + ((size_t)bh * a.splits + split) * RP;
+  for (int i = threadIdx.x; i < R * D; i += kAttnThreads) po[i] = sm_o[i];
+  for (int i = threadIdx.x; i < R; i += kAttnThreads) pl[i] = sm_lse[i];
+  __threadfence();
+  __syncthreads();
+  __shared__ int is_last;
+  if (threadIdx.x == 0) is_last = (atomicAdd(a.counters + bh, 1) == a.splits - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  const float* base_o = a.ws_o + (size_t)bh * a.splits * RP * D;
+  const float* base_l = a.ws_lse + (size_t)bh * a.splits * RP;
+  for (int i = threadIdx.x; i < R * D; i += kAttnThreads) {
+    const int row = i / D;
+    float M = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, __ldcg(base_l + s * RP + row));
+    float W = 0.0f, O = 0.0f;
+    for (int s = 0; s < a.splits; ++s) {
+      const float ls = __ldcg(base_l + s * RP + row);
+      const float w = (ls == -INFINITY) ? 0.0f : exp2f(ls - M);
+      W += w;
+      O += w * __ldcg(base_o + (size_t)s * RP * D + i);
+    }
+    sm_o[i] = W > 0.0f ? O / W : 0.0f;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) a.counters[bh] = 0;
+  finish(sm_o, R, b, h);
+}
+
+template <int D>
+struct FinishBf16 {
+  const AttnArgs* a;
+  __device__ void operator()(const float* sm_o, int R, int b, int h) const {
+    const int G = a->Hq / a->Hkv;
+    for (int i = threadIdx.x; i < R * (D / 2); i += kAttnThreads) {
+      const int row = i / (D / 2), d = 2 * (i % (D / 2));
+      const int tq = a->tq0 + row / G, hq = h * G + row % G;
+      uint16_t* op = a->out + (((size_t)b * a->Lq + tq) * a->Hq + hq) * D + d;
+      *reinterpret_cast<uint32_t*>(op) = pack_bf2(sm_o[row * D + d], sm_o[row * D + d + 1]);
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// bf16 pages
+// ---------------------------------------------------------------------------
+template <int D, int MT>
+__global__ void __launch_bounds__(kAttnThreads) paged_attn_bf16_kernel(AttnArgs a) {
+  constexpr int RP = 16 * MT;
+  constexpr int PAGE_ELEMS = 16 * D;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint16_t* Qs = reinterpret_cast<uint16_t*>(smem_raw);              // [RP][D]
+  uint16_t* KV = Qs + RP * D;                                         // [4 warps][2 stages][K|V]
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int G = a.Hq / a.Hkv;
+  const int R = G * a.lq_chunk;
+
+  pdl_wait();
+  const int L = a.seq_lens[b];
+  const int n_pages = min((L + 15) / 16, a.max_blocks);
+  const int pg0 = split * a.pages_per_split;
+  const int pg1 = min(n_pages, pg0 + a.pages_per_split);
+
+  // Q tile (rows >= R zero)
+  for (int i = threadIdx.x; i < RP * (D / 8); i += kAttnThreads) {
+    const int row = i / (D / 8), c = i % (D / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < R) {
+      const int tq = a.tq0 + row / G, hq = h * G + row % G;
+      v = *reinterpret_cast<const uint4*>(a.q + (((size_t)b * a.Lq + tq) * a.Hq + hq) * D + c * 8);
+    }
+    *reinterpret_cast<uint4*>(Qs + row * D + swz(row, c) * 8) = v;
+  }
+  __syncthreads();
+
+  float m[MT][2], l[MT][2], o[MT][D / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    m[mt][0] = m[mt][1] = -INFINITY;
+    l[mt][0] = l[mt][1] = 0.0f;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[mt][dt][c] = 0.0f;
+  }
+
+  uint16_t* my = KV + warp * 2 * 2 * PAGE_ELEMS;
+  auto kbuf = [&](int st) { return my + st * 2 * PAGE_ELEMS; };
+  auto vbuf = [&](int st) { return my + st * 2 * PAGE_ELEMS + PAGE_ELEMS; };
+  auto issue = [&](int pg, int st) {
+    const int pid = a.bt[(size_t)b * a.max_blocks + pg];
+    const size_t off = (size_t)pid * a.page_stride + (size_t)h * a.head_stride;
+    const int valid = min(16, L - pg * 16);
+    load_page_bf16<D>(kbuf(st), a.kc + off, valid, lane);
+    load_page_bf16<D>(vbuf(st), a.vc + off, valid, lane);
+  };
+
+  int stage = 0;
+  int pg = pg0 + warp;
+  if (pg < pg1) issue(pg, 0);
+  cp_async_commit();
+  for (; pg < pg1; pg += 4) {
+    if (pg + 4 < pg1) issue(pg + 4, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    const uint16_t* Ks = kbuf(stage);
+    const uint16_t* Vs = vbuf(stage);
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kt = 0; kt < D / 16; ++kt) {
+        uint32_t qa[4], kb[4];
+        {
+          const int mi = lane >> 3;
+          const int row = mt * 16 + (mi & 1) * 8 + (lane & 7);
+          ldmatrix_x4(qa, Qs + row * D + swz(row, 2 * kt + (mi >> 1)) * 8);
+          const int tok = (mi >> 1) * 8 + (lane & 7);
+          ldmatrix_x4(kb, Ks + tok * D + swz(tok, 2 * kt + (mi & 1)) * 8);
+        }
+        mma_bf16_16816(s[0], qa[0], qa[1], qa[2], qa[3], kb[0], kb[1]);
+        mma_bf16_16816(s[1], qa[0], qa[1], qa[2], qa[3], kb[2], kb[3]);
+      }
+      // scale + causal mask
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = pg * 16 + nt * 8 + 2 * t + (c & 1);
+          const int row = mt * 16 + g + 8 * (c >> 1);
+          const int qpos = L - a.Lq + a.tq0 + row / G;
+          const bool ok = row < R && j <= qpos;
+          s[nt][c] = ok ? s[nt][c] * a.scale_log2 : -INFINITY;
+        }
+      float alpha[2];
+      row_stats_update(m[mt], l[mt], s, alpha);
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) {
+        o[mt][dt][0] *= alpha[0];
+        o[mt][dt][1] *= alpha[0];
+        o[mt][dt][2] *= alpha[1];
+        o[mt][dt][3] *= alpha[1];
+      }
+      const uint32_t pa0 = pack_bf2(s[0][0], s[0][1]), pa1 = pack_bf2(s[0][2], s[0][3]);
+      const uint32_t pa2 = pack_bf2(s[1][0], s[1][1]), pa3 = pack_bf2(s[1][2], s[1][3]);
+#pragma unroll
+      for (int d2 = 0; d2 < D / 16; ++d2) {
+        uint32_t vb[4];
+        const int mi = lane >> 3;
+        const int tok = (mi & 1) * 8 + (lane & 7);
+        ldmatrix_x4_trans(vb, Vs + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
+        mma_bf16_16816(o[mt][2 * d2], pa0, pa1, pa2, pa3, vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], pa0, pa1, pa2, pa3, vb[2], vb[3]);
+      }
+    }
+    __syncwarp();
+    stage ^= 1;
+  }
+  cp_async_wait<0>();
+  pdl_launch();
+
+  float* smem_f = reinterpret_cast<float*>(KV);
+  FinishBf16<D> fin{&a};
+  attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
+}
+
+// ---------------------------------------------------------------------------
+// TurboQuant pages (D = 128)
+// ---------------------------------------------------------------------------
+// Physical position j within an 8-wide d chunk holds natural nibble kPerm[j].
+__device__ __constant__ int kPerm[8] = {0, 4, 1, 5, 2, 6, 3, 7};
+
+// Inverse rotation R^T = diag(sign) H / sqrt(128) of one row held as lane l:
+// natural elements 2l, 2l+1, 64+2l, 65+2l.
+__device__ __forceinline__ void tq_unrotate_lane(float (&f)[4], const int8_t* signs, int lane) {
+  {
+    float a0 = f[0], b0 = f[1];
+    f[0] = a0 + b0;
+    f[1] = a0 - b0;
+    a0 = f[2];
+    b0 = f[3];
+    f[2] = a0 + b0;
+    f[3] = a0 - b0;
+  }
+#pragma unroll
+  for (int hl = 1; hl <= 16; hl <<= 1) {
+    const bool upper = (lane & hl) != 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, f[e], hl);
+      f[e] = upper ? other - f[e] : f[e] + other;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float a0 = f[e], b0 = f[e + 2];
+    f[e] = a0 + b0;
+    f[e + 2] = a0 - b0;
+  }
+  const int idx[4] = {2 * lane, 2 * lane + 1, 64 + 2 * lane, 65 + 2 * lane};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    f[e] *= 0.0883883476483184406f;
+    if (signs[idx[e]] < 0) f[e] = -f[e];
+  }
+}
+
+__device__ __forceinline__ void tq_rotate_lane(float (&f)[4], const int8_t* signs, int lane) {
+  const int idx[4] = {2 * lane, 2 * lane + 1, 64 + 2 * lane, 65 + 2 * lane};
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    if (signs[idx[e]] < 0) f[e] = -f[e];
+  {
+    float a0 = f[0], b0 = f[1];
+    f[0] = a0 + b0;
+    f[1] = a0 - b0;
+    a0 = f[2];
+    b0 = f[3];
+    f[2] = a0 + b0;
+    f[3] = a0 - b0;
+  }
+#pragma unroll
+  for (int hl = 1; hl <= 16; hl <<= 1) {
+    const bool upper = (lane & hl) != 0;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float other = __shfl_xor_sync(0xffffffffu, f[e], hl);
+      f[e] = upper ? other - f[e] : f[e] + other;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float a0 = f[e], b0 = f[e + 2];
+    f[e] = a0 + b0;
+    f[e + 2] = a0 - b0;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) f[e] *= 0.0883883476483184406f;
+}
+
+struct FinishTq4 {
+  const AttnArgs* a;
+  __device__ void operator()(const float* sm_o, int R, int b, int h) const {
+    const int G = a->Hq / a->Hkv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int row = warp; row < R; row += 4) {
+      // gather natural order from the physical (chunk-permuted) layout
+      auto phys = [](int d) {
+        const int c = d >> 3, n = d & 7;
+        // natural nibble n sits at physical j with kPerm[j] == n
+        const int j = (n < 4) ? 2 * n : 2 * (n - 4) + 1;
+        return c * 8 + j;
+      };
+      const float* r = sm_o + row * 128;
+      float f[4] = {r[phys(2 * lane)], r[phys(2 * lane + 1)], r[phys(64 + 2 * lane)],
+                    r[phys(65 + 2 * lane)]};
+      tq_unrotate_lane(f, a->signs, lane);
+      const int tq = a->tq0 + row / G, hq = h * G + row % G;
+      uint16_t* op = a->out + (((size_t)b * a->Lq + tq) * a->Hq + hq) * 128;
+      *reinterpret_cast<uint32_t*>(op + 2 * lane) = pack_bf2(f[0], f[1]);
+      *reinterpret_cast<uint32_t*>(op + 64 + 2 * lane) = pack_bf2(f[2], f[3]);
+    }
+  }
+};
+
+template <int MT>
+__global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a) {
+  constexpr int D = 128;
+  constexpr int RP = 16 * MT;
+  // smem: qfrag [MT][8 kt][32 lanes][4] u32 | qsum [RP] f32 |
+  //       per warp 2 stages x {kcodes 1 KB, vcodes 1 KB, kscale 32 B, vscale 32 B, vtile bf16 4 KB}
+  constexpr int STAGE_BYTES = 1024 + 1024 + 32 + 32;
+  constexpr int WARP_BYTES = 2 * STAGE_BYTES + 16 * D * 2;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem_raw);
+  float* qsum = reinterpret_cast<float*>(qfrag + MT * 8 * 32 * 4);
+  float* qrot = qsum + RP;  // [RP][128] f32 scratch, reused as per-warp buffers later
+  uint8_t* wbase = reinterpret_cast<uint8_t*>(qrot);
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int G = a.Hq / a.Hkv;
+  const int R = G * a.lq_chunk;
+
+  pdl_wait();
+  const int L = a.seq_lens[b];
+  const int n_pages = min((L + 15) / 16, a.max_blocks);
+  const int pg0 = split * a.pages_per_split;
+  const int pg1 = min(n_pages, pg0 + a.pages_per_split);
+
+  // rotate the query rows: q' = R q, rounded to bf16 (the MMA operand), and
+  // the per-row sum of the rounded q' (removes the +136 code offset)
+  for (int row = warp; row < RP; row += 4) {
+    float f[4] = {0.f, 0.f, 0.f, 0.f};
+    if (row < R) {
+      const int tq = a.tq0 + row / G, hq = h * G + row % G;
+      const uint16_t* qp = a.q + (((size_t)b * a.Lq + tq) * a.Hq + hq) * D;
+      f[0] = bf2f(qp[2 * lane]);
+      f[1] = bf2f(qp[2 * lane + 1]);
+      f[2] = bf2f(qp[64 + 2 * lane]);
+      f[3] = bf2f(qp[65 + 2 * lane]);
+      tq_rotate_lane(f, a.signs, lane);
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      f[e] = round_bf(f[e]);
+      sum += f[e];
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) qsum[row] = sum;
+    float* dst = qrot + row * D;
+    dst[2 * lane] = f[0];
+    dst[2 * lane + 1] = f[1];
+    dst[64 + 2 * lane] = f[2];
+    dst[65 + 2 * lane] = f[3];
+  }
+  __syncthreads();
+  // A fragments in the code-nibble k order: tile kt, lane (g, t):
+  //   lo = 32t + 8(kt>>1) + 2(kt&1): a0 = (lo, lo+4), a2 = (lo+1, lo+5); a1/a3 row g+8
+  for (int i = threadIdx.x; i < MT * 8 * 32; i += kAttnThreads) {
+    const int mt = i / 256, kt = (i / 32) % 8, ln = i % 32;
+    const int gg = ln >> 2, tt = ln & 3;
+    const int lo = 32 * tt + 8 * (kt >> 1) + 2 * (kt & 1);
+    const float* r0 = qrot + (mt * 16 + gg) * D;
+    const float* r1 = qrot + (mt * 16 + gg + 8) * D;
+    uint32_t* dst = qfrag + (size_t)i * 4;
+    dst[0] = pack_bf2(r0[lo], r0[lo + 4]);
+    dst[1] = pack_bf2(r1[lo], r1[lo + 4]);
+    dst[2] = pack_bf2(r0[lo + 1], r0[lo + 5]);
+    dst[3] = pack_bf2(r1[lo + 1], r1[lo + 5]);
+  }
+  __syncthreads();
+
+  float m[MT][2], l[MT][2], o[MT][D / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    m[mt][0] = m[mt][1] = -INFINITY;
+    l[mt][0] = l[mt][1] = 0.0f;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[mt][dt][c] = 0.0f;
+  }
+  float qs[MT][2];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    qs[mt][0] = qsum[mt * 16 + g];
+    qs[mt][1] = qsum[mt * 16 + g + 8];
+  }
+
+  uint8_t* my = wbase + warp * WARP_BYTES;
+  uint16_t* vtile = reinterpret_cast<uint16_t*>(my + 2 * STAGE_BYTES);
+  auto kcb = [&](int st) { return my + st * STAGE_BYTES; };
+  auto vcb = [&](int st) { return my + st * STAGE_BYTES + 1024; };
+  auto ksb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2048); };
+  auto vsb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2080); };
+  auto issue = [&](int pg, int st) {
+    const int pid = a.bt[(size_t)b * a.max_blocks + pg];
+    const size_t off = (size_t)pid * a.page_stride + (size_t)h * a.head_stride;
+    const size_t soff = (size_t)pid * (a.page_stride / 64) + (size_t)h * (a.head_stride / 64);
+    const int valid = min(16, L - pg * 16);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int qd = lane + 32 * i;  // 64 chunks of 16 B = 16 rows x 64 B
+      const int r = qd >> 2;
+      const int bytes = r < valid ? 16 : 0;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(kcb(st) + qd * 16)),
+                   "l"(a.kcode + off + qd * 16), "r"(bytes));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vcb(st) + qd * 16)),
+                   "l"(a.vcode + off + qd * 16), "r"(bytes));
+    }
+    if (lane < 2) {
+      const int bytes = (lane * 8 < valid) ? 16 : 0;  // each 16 B chunk = 8 scales
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(ksb(st) + lane * 8)),
+                   "l"(a.kscale + soff + lane * 8), "r"(bytes));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vsb(st) + lane * 8)),
+                   "l"(a.vscale + soff + lane * 8), "r"(bytes));
+    }
+  };
+
+  int stage = 0;
+  int pg = pg0 + warp;
+  if (pg < pg1) issue(pg, 0);
+  cp_async_commit();
+  for (; pg < pg1; pg += 4) {
+    if (pg + 4 < pg1) issue(pg + 4, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    const uint8_t* kc = kcb(stage);
+    const uint8_t* vcc = vcb(stage);
+    const __half* ks = ksb(stage);
+    const __half* vs = vsb(stage);
+    const int valid = min(16, L - pg * 16);
+    // expand V codes to exact bf16 (c - 8): lane -> token lane/2, half lane&1
+    {
+      const int r = lane >> 1, hlf = lane & 1;
+      const uint4* src = reinterpret_cast<const uint4*>(vcc + r * 64 + hlf * 32);
+#pragma unroll
+      for (int v4 = 0; v4 < 2; ++v4) {
+        const uint4 w4 = src[v4];
+        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          const int chunk = hlf * 8 + v4 * 4 + wi;
+          const uint32_t off136 = 0x43084308u;  // bf16 pair (136, 136)
+          uint4 outv;
+          uint32_t p0 = nib_pair_bf16<0>(ws[wi]), p1 = nib_pair_bf16<4>(ws[wi]);
+          uint32_t p2 = nib_pair_bf16<8>(ws[wi]), p3 = nib_pair_bf16<12>(ws[wi]);
+          __nv_bfloat162 o0 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p0),
+                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
+          __nv_bfloat162 o1 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p1),
+                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
+          __nv_bfloat162 o2 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p2),
+                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
+          __nv_bfloat162 o3 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p3),
+                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
+          outv.x = *reinterpret_cast<uint32_t*>(&o0);
+          outv.y = *reinterpret_cast<uint32_t*>(&o1);
+          outv.z = *reinterpret_cast<uint32_t*>(&o2);
+          outv.w = *reinterpret_cast<uint32_t*>(&o3);
+          *reinterpret_cast<uint4*>(vtile + r * D + swz(r, chunk) * 8) = outv;
+        }
+      }
+    }
+    __syncwarp();
+    // per-token scales for the S columns this lane owns
+    float ksc[2][2], vsc[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = nt * 8 + 2 * t + e;
+        ksc[nt][e] = j < valid ? __half2float(ks[j]) : 0.0f;
+        vsc[nt][e] = j < valid ? __half2float(vs[j]) : 0.0f;
+      }
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint4 kw = *reinterpret_cast<const uint4*>(kc + (nt * 8 + g) * 64 + 16 * t);
+        const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w};
+#pragma unroll
+        for (int kt = 0; kt < 8; ++kt) {
+          const uint4 qa = *reinterpret_cast<const uint4*>(qfrag + ((mt * 8 + kt) * 32 + lane) * 4);
+          const uint32_t w = kws[kt >> 1];
+          const uint32_t b0 = (kt & 1) ? nib_pair_bf16<8>(w) : nib_pair_bf16<0>(w);
+          const uint32_t b1 = (kt & 1) ? nib_pair_bf16<12>(w) : nib_pair_bf16<4>(w);
+          mma_bf16_16816(s[nt], qa.x, qa.y, qa.z, qa.w, b0, b1);
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = pg * 16 + nt * 8 + 2 * t + (c & 1);
+          const int row = mt * 16 + g + 8 * (c >> 1);
+          const int qpos = L - a.Lq + a.tq0 + row / G;
+          const bool ok = row < R && j <= qpos;
+          const float raw = s[nt][c] - 136.0f * qs[mt][c >> 1];
+          s[nt][c] = ok ? raw * ksc[nt][c & 1] * a.scale_log2 : -INFINITY;
+        }
+      float alpha[2];
+      row_stats_update(m[mt], l[mt], s, alpha);
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) {
+        o[mt][dt][0] *= alpha[0];
+        o[mt][dt][1] *= alpha[0];
+        o[mt][dt][2] *= alpha[1];
+        o[mt][dt][3] *= alpha[1];
+      }
+      // P scaled by the per-token V scale
+      const uint32_t pa0 = pack_bf2(s[0][0] * vsc[0][0], s[0][1] * vsc[0][1]);
+      const uint32_t pa1 = pack_bf2(s[0][2] * vsc[0][0], s[0][3] * vsc[0][1]);
+      const uint32_t pa2 = pack_bf2(s[1][0] * vsc[1][0], s[1][1] * vsc[1][1]);
+      const uint32_t pa3 = pack_bf2(s[1][2] * vsc[1][0], s[1][3] * vsc[1][1]);
+#pragma unroll
+      for (int d2 = 0; d2 < D / 16; ++d2) {
+        uint32_t vb[4];
+        const int mi = lane >> 3;
+        const int tok = (mi & 1) * 8 + (lane & 7);
+        ldmatrix_x4_trans(vb, vtile + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
+        mma_bf16_16816(o[mt][2 * d2], pa0, pa1, pa2, pa3, vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], pa0, pa1, pa2, pa3, vb[2], vb[3]);
+      }
+    }
+    __syncwarp();
+    stage ^= 1;
+  }
+  cp_async_wait<0>();
+  pdl_launch();
+
+  float* smem_f = reinterpret_cast<float*>(qrot);
+  FinishTq4 fin{&a};
+  attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct SplitPlan {
+  int splits, pps, rows_pad, lq_chunk, chunks;
+};
+
+static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len) {
+  SplitPlan p;
+  const int G = Hq / Hkv;
+  // query tokens per launch so that G * chunk <= 32 rows
+  p.lq_chunk = G >= 32 ? 1 : (32 / G < Lq ? 32 / G : Lq);
+  p.chunks = (Lq + p.lq_chunk - 1) / p.lq_chunk;
+  p.rows_pad = (G * p.lq_chunk <= 16) ? 16 : 32;
+  const int max_pages = (max_seq_len + 15) / 16 > 0 ? (max_seq_len + 15) / 16 : 1;
+  int want = (kTargetCtas + B * Hkv - 1) / (B * Hkv);
+  if (want < 1) want = 1;
+  // at least 4 pages (one per warp) per split
+  int pps = (max_pages + want - 1) / want;
+  if (pps < 4) pps = 4;
+  p.pps = pps;
+  p.splits = (max_pages + pps - 1) / pps;
+  return p;
+}
+
+static size_t attn_ws_bytes(const SplitPlan& p, int B, int Hkv, int D) {
+  if (p.splits == 1) return kCounterBytes;
+  return kCounterBytes + (size_t)B * Hkv * p.splits * p.rows_pad * (D + 1) * sizeof(float);
+}
+
+static size_t smem_bf16(int D, int MT) {
+  const size_t q = (size_t)16 * MT * D * 2;
+  const size_t kv = (size_t)4 * 2 * 2 * 16 * D * 2;
+  const size_t merge = (size_t)(9 * 16 * MT + 4 * 16 * MT * D) * 4;
+  return q + (kv > merge ? kv : merge);
+}
+
+static size_t smem_tq4(int MT) {
+  const size_t head = (size_t)MT * 8 * 32 * 4 * 4 + 16 * MT * 4;
+  const size_t warps = (size_t)4 * (2 * (1024 + 1024 + 32 + 32) + 16 * 128 * 2);
+  const size_t qrot = (size_t)16 * MT * 128 * 4;
+  const size_t merge = (size_t)(9 * 16 * MT + 4 * 16 * MT * 128) * 4;
+  size_t body = warps;
+  if (qrot > body) body = qrot;
+  if (merge > body) body = merge;
+  return head + body;
+}
+
+static cudaError_t g_prepare_status = cudaSuccess;
+
+// Raise the dynamic shared-memory limit of every attention instantiation once,
+// outside any stream capture.
+void attention_prepare() {
+  static bool done = false;
+  if (done) return;
+  done = true;
+  cudaError_t e = cudaSuccess;
+  auto set = [&](void (*k)(AttnArgs), size_t smem) {
+    cudaError_t r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (r != cudaSuccess) e = r;
+  };
+  set(paged_attn_bf16_kernel<64, 1>, smem_bf16(64, 1));
+  set(paged_attn_bf16_kernel<64, 2>, smem_bf16(64, 2));
+  set(paged_attn_bf16_kernel<128, 1>, smem_bf16(128, 1));
+  set(paged_attn_bf16_kernel<128, 2>, smem_bf16(128, 2));
+  set(paged_attn_tq4_kernel<1>, smem_tq4(1));
+  set(paged_attn_tq4_kernel<2>, smem_tq4(2));
+  g_prepare_status = e;
+}
+
+template <typename K>
+static cudaError_t launch_attn(K kernel, size_t smem, const AttnArgs& a, const SplitPlan& p,
+                               cudaStream_t st) {
+  attention_prepare();
+  if (g_prepare_status != cudaSuccess) return g_prepare_status;
+  cudaError_t e = cudaSuccess;
+  for (int c = 0; c < p.chunks; ++c) {
+    AttnArgs ac = a;
+    ac.tq0 = c * p.lq_chunk;
+    ac.lq_chunk = (a.Lq - ac.tq0) < p.lq_chunk ? (a.Lq - ac.tq0) : p.lq_chunk;
+    e = launch_pdl(kernel, dim3(p.splits, a.Hkv, a.B), dim3(kAttnThreads), smem, st, ac);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace higgs
+
+using namespace higgs;
+
+extern "C" size_t higgs_paged_attention_workspace_size(int B, int Lq, int Hq, int Hkv, int D,
+                                                       int max_seq_len) {
+  if (B <= 0 || Lq <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
+  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
+  return attn_ws_bytes(p, B, Hkv, D);
+}
+
+extern "C" size_t higgs_paged_attention_tq4_workspace_size(int B, int Lq, int Hq, int Hkv,
+                                                           int max_seq_len) {
+  return higgs_paged_attention_workspace_size(B, Lq, Hq, Hkv, 128, max_seq_len);
+}
+
+static int validate_attn(int B, int Lq, int Hq, int Hkv, int max_blocks, int max_seq_len,
+                         size_t ws_bytes, size_t need) {
+  HG_CHECK_ARG(B > 0 && Lq > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
+               "paged attention: bad batch / head shape");
+  HG_CHECK_ARG(B * Hkv * 1 <= kCounterBytes / 4, "paged attention: B * Hkv exceeds 1024");
+  HG_CHECK_ARG(max_seq_len >= Lq, "paged attention: max_seq_len < Lq");
+  HG_CHECK_ARG((int64_t)max_blocks * 16 >= max_seq_len, "paged attention: block table too short");
+  if (ws_bytes < need)
+    return fail(HIGGS_ERR_WORKSPACE, "paged attention: workspace too small (need " +
+                                         std::to_string(need) + " bytes)");
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq, int Hkv,
+                                     int D, const void* k_cache, const void* v_cache,
+                                     int64_t page_stride, int64_t head_stride,
+                                     const int32_t* block_table, int max_blocks,
+                                     const int32_t* seq_lens, int max_seq_len, float scale,
+                                     void* out, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  HG_CHECK_ARG(ctx && q && k_cache && v_cache && block_table && seq_lens && out && workspace,
+               "higgs_paged_attention: null argument");
+  HG_CHECK_ARG(D == 64 || D == 128, "higgs_paged_attention: D must be 64 or 128");
+  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
+  int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
+                         attn_ws_bytes(p, B, Hkv, D));
+  if (rc) return rc;
+  AttnArgs a = {};
+  a.q = (const uint16_t*)q;
+  a.B = B;
+  a.Lq = Lq;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.kc = (const uint16_t*)k_cache;
+  a.vc = (const uint16_t*)v_cache;
+  a.page_stride = page_stride;
+  a.head_stride = head_stride;
+  a.bt = block_table;
+  a.max_blocks = max_blocks;
+  a.seq_lens = seq_lens;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = (uint16_t*)out;
+  a.splits = p.splits;
+  a.pages_per_split = p.pps;
+  a.counters = (int*)workspace;
+  a.ws_lse = (float*)((char*)workspace + kCounterBytes);
+  a.ws_o = a.ws_lse + (size_t)B * Hkv * p.splits * p.rows_pad;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int MT = p.rows_pad / 16;
+  cudaError_t e;
+  if (D == 64)
+    e = MT == 1 ? launch_attn(paged_attn_bf16_kernel<64, 1>, smem_bf16(64, 1), a, p, st)
+                : launch_attn(paged_attn_bf16_kernel<64, 2>, smem_bf16(64, 2), a, p, st);
+  else
+    e = MT == 1 ? launch_attn(paged_attn_bf16_kernel<128, 1>, smem_bf16(128, 1), a, p, st)
+                : launch_attn(paged_attn_bf16_kernel<128, 2>, smem_bf16(128, 2), a, p, st);
+  HG_CUDA(e);
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq,
+                                         int Hkv, const uint8_t* k_codes, const void* k_scales,
+                                         const uint8_t* v_codes, const void* v_scales,
+                                         int64_t page_stride, int64_t head_stride,
+                                         const int32_t* block_table, int max_blocks,
+                                         const int32_t* seq_lens, int max_seq_len,
+                                         const int8_t* signs, float scale, void* out,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+  HG_CHECK_ARG(ctx && q && k_codes && k_scales && v_codes && v_scales && block_table && seq_lens &&
+                   out && workspace && signs,
+               "higgs_paged_attention_tq4: null argument");
+  HG_CHECK_ARG(page_stride % 64 == 0 && head_stride % 64 == 0,
+               "higgs_paged_attention_tq4: strides must be multiples of 64 bytes");
+  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
+  int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
+                         attn_ws_bytes(p, B, Hkv, 128));
+  if (rc) return rc;
+  AttnArgs a = {};
+  a.q = (const uint16_t*)q;
+  a.B = B;
+  a.Lq = Lq;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.kcode = k_codes;
+  a.kscale = (const __half*)k_scales;
+  a.vcode = v_codes;
+  a.vscale = (const __half*)v_scales;
+  a.signs = signs;
+  a.page_stride = page_stride;
+  a.head_stride = head_stride;
+  a.bt = block_table;
+  a.max_blocks = max_blocks;
+  a.seq_lens = seq_lens;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = (uint16_t*)out;
+  a.splits = p.splits;
+  a.pages_per_split = p.pps;
+  a.counters = (int*)workspace;
+  a.ws_lse = (float*)((char*)workspace + kCounterBytes);
+  a.ws_o = a.ws_lse + (size_t)B * Hkv * p.splits * p.rows_pad;
+  cudaStream_t st = (cudaStream_t)stream;
+  const int MT = p.rows_pad / 16;
+  cudaError_t e = MT == 1 ? launch_attn(paged_attn_tq4_kernel<1>, smem_tq4(1), a, p, st)
+                          : launch_attn(paged_attn_tq4_kernel<2>, smem_tq4(2), a, p, st);
+  HG_CUDA(e);
+  return HIGGS_OK;
+}

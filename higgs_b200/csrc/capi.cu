@@ -1,0 +1,59 @@
+// capi.cu -- context lifetime and the thread-local error channel of the C ABI.
+#include <string>
+
+#include "common.cuh"
+
+struct higgs_ctx {
+  int device;
+  int sms;
+};
+
+namespace higgs {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  g_last_error = std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+  return HIGGS_ERR_CUDA;
+}
+
+}  // namespace higgs
+
+using namespace higgs;
+
+extern "C" int higgs_version(void) { return 1; }
+
+extern "C" const char* higgs_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int higgs_init(int device, higgs_ctx** out) {
+  HG_CHECK_ARG(out != nullptr, "higgs_init: out is null");
+  *out = nullptr;
+  int n = 0;
+  HG_CUDA(cudaGetDeviceCount(&n));
+  HG_CHECK_ARG(device >= 0 && device < n, "higgs_init: no such device");
+  HG_CUDA(cudaSetDevice(device));
+  int major = 0, minor = 0, sms = 0;
+  HG_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+  HG_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+  HG_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+  if (major != 10 || minor != 0)
+    return fail(HIGGS_ERR_UNSUPPORTED, "higgs_init: device is sm_" + std::to_string(major) +
+                                           std::to_string(minor) + ", this build targets sm_100a");
+  higgs_ctx* c = new higgs_ctx;
+  c->device = device;
+  c->sms = sms;
+  *out = c;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_destroy(higgs_ctx* ctx) {
+  delete ctx;
+  return HIGGS_OK;
+}

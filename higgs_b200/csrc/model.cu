@@ -1,0 +1,474 @@
+// model.cu -- native decode/verify/prefill step of the dense transformer
+// (Llama / Mistral / Qwen2 / Qwen3) over a paged KV cache, and CUDA-graph
+// capture of that step.
+//
+// Mirrors Model::forward / forward_batched of the reference
+// (crates/higgs-models/src/transformer.rs:487-526, 663-827): embedding ->
+// N x [RMSNorm -> q|k|v -> (qk-norm) -> RoPE -> KV append -> SDPA -> o_proj +
+// residual -> RMSNorm -> SwiGLU MLP + residual] -> RMSNorm -> LM head (tied to
+// the embedding when tie_word_embeddings, transformer.rs:830-838).  The
+// per-request host loop of forward_batched (transformer.rs:747-802) is gone:
+// RoPE positions, cache slots and sequence lengths are device vectors, so one
+// launch sequence serves any mix of sequence lengths and the whole step can be
+// captured once and replayed.
+//
+// Weights are caller-owned device tensors registered under their MLX
+// safetensors names (lib.rs:604-723 loads the same keys); nothing is copied.
+#include <cmath>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace higgs {
+
+struct TensorRef {
+  const void* ptr = nullptr;
+  int dtype = 0;  // HIGGS_DTYPE_*
+  std::vector<int64_t> shape;
+};
+
+struct QW {
+  const uint32_t* w = nullptr;
+  const uint16_t* s = nullptr;
+  const uint16_t* b = nullptr;
+  int N = 0, K = 0;
+};
+
+struct LayerW {
+  const uint16_t* ln_in = nullptr;
+  const uint16_t* ln_post = nullptr;
+  QW q, k, v, o, gate, up, down;
+  const uint16_t* qn = nullptr;
+  const uint16_t* kn = nullptr;
+};
+
+void attention_prepare();
+
+}  // namespace higgs
+
+using namespace higgs;
+
+struct higgs_model {
+  higgs_ctx* ctx = nullptr;
+  higgs_model_config cfg{};
+  std::unordered_map<std::string, TensorRef> tensors;
+  bool finalized = false;
+  std::vector<LayerW> layers;
+  QW embed, head;
+  const uint16_t* final_norm = nullptr;
+  float* inv_freq = nullptr;  // device [D/2]
+  // KV pools
+  void* k_pool = nullptr;
+  void* v_pool = nullptr;
+  void* k_scales = nullptr;
+  void* v_scales = nullptr;
+  const int8_t* signs = nullptr;
+  int64_t num_pages = 0;
+};
+
+struct higgs_graph {
+  cudaGraphExec_t exec = nullptr;
+};
+
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+struct WsLayout {
+  size_t h, x, qkv, q, attn, act, xl, logits, attn_ws, total;
+};
+
+WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, bool last_only) {
+  const size_t T = (size_t)B * Lq;
+  const size_t rows_lm = last_only ? (size_t)B : T;
+  const int D = c.head_dim;
+  WsLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align_up(bytes);
+    return o;
+  };
+  L.h = take(T * c.hidden * 2);
+  L.x = take(T * c.hidden * 2);
+  L.qkv = take(T * (size_t)(c.heads + 2 * c.kv_heads) * D * 2);
+  L.q = take(T * (size_t)c.heads * D * 2);
+  L.attn = take(T * (size_t)c.heads * D * 2);
+  L.act = take(T * (size_t)c.intermediate * 2);
+  L.xl = take(rows_lm * c.hidden * 2);
+  L.logits = take(rows_lm * (size_t)c.vocab * 4);
+  const size_t aws = higgs_paged_attention_workspace_size(B, Lq, c.heads, c.kv_heads, D, max_seq_len);
+  L.attn_ws = take(aws);
+  L.total = off;
+  return L;
+}
+
+int get_q(higgs_model* m, const std::string& base, int N, int K, QW& out) {
+  auto it_w = m->tensors.find(base + ".weight");
+  auto it_s = m->tensors.find(base + ".scales");
+  auto it_b = m->tensors.find(base + ".biases");
+  if (it_w == m->tensors.end() || it_s == m->tensors.end() || it_b == m->tensors.end())
+    return fail(HIGGS_ERR_STATE, "model: missing quantized tensor " + base + ".{weight,scales,biases}");
+  const TensorRef& w = it_w->second;
+  const TensorRef& s = it_s->second;
+  const TensorRef& b = it_b->second;
+  auto shape_is = [](const TensorRef& t, int64_t a, int64_t bb) {
+    return t.shape.size() == 2 && t.shape[0] == a && t.shape[1] == bb;
+  };
+  if (w.dtype != HIGGS_DTYPE_U32 || !shape_is(w, N, K / 8))
+    return fail(HIGGS_ERR_INVALID_ARG, "model: " + base + ".weight must be u32 [" +
+                                           std::to_string(N) + ", " + std::to_string(K / 8) + "]");
+  if (s.dtype != HIGGS_DTYPE_BF16 || !shape_is(s, N, K / 64) || b.dtype != HIGGS_DTYPE_BF16 ||
+      !shape_is(b, N, K / 64))
+    return fail(HIGGS_ERR_INVALID_ARG, "model: " + base + ".{scales,biases} must be bf16 [" +
+                                           std::to_string(N) + ", " + std::to_string(K / 64) + "]");
+  out.w = (const uint32_t*)w.ptr;
+  out.s = (const uint16_t*)s.ptr;
+  out.b = (const uint16_t*)b.ptr;
+  out.N = N;
+  out.K = K;
+  return HIGGS_OK;
+}
+
+int get_vec(higgs_model* m, const std::string& name, int n, const uint16_t*& out) {
+  auto it = m->tensors.find(name);
+  if (it == m->tensors.end()) return fail(HIGGS_ERR_STATE, "model: missing tensor " + name);
+  const TensorRef& t = it->second;
+  if (t.dtype != HIGGS_DTYPE_BF16 || t.shape.size() != 1 || t.shape[0] != n)
+    return fail(HIGGS_ERR_INVALID_ARG, "model: " + name + " must be bf16 [" + std::to_string(n) + "]");
+  out = (const uint16_t*)t.ptr;
+  return HIGGS_OK;
+}
+
+cudaError_t qlin(const QW& w, const uint16_t* x, int M, uint16_t* y, float* yf,
+                 const uint16_t* residual, cudaStream_t st) {
+  QLinArgs a{};
+  a.x = x;
+  a.M = M;
+  a.K = w.K;
+  a.N = w.N;
+  a.w = w.w;
+  a.s = w.s;
+  a.b = w.b;
+  a.nseg = 1;
+  a.y = y;
+  a.y_f32 = yf;
+  a.residual = residual;
+  return launch_qlinear(a, EPI_STORE, st);
+}
+
+int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
+  const higgs_model_config& c = m->cfg;
+  const int B = f->B, Lq = f->Lq;
+  const int T = B * Lq;
+  const int D = c.head_dim, H = c.hidden;
+  const bool tq = c.kv_mode == HIGGS_KV_TQ4;
+  const int n_layers = f->n_layers > 0 ? f->n_layers : c.layers;
+  const WsLayout L = layout(c, B, Lq, f->max_seq_len, f->last_only != 0);
+  if (f->workspace_bytes < L.total)
+    return fail(HIGGS_ERR_WORKSPACE, "higgs_model_forward: workspace too small (need " +
+                                         std::to_string(L.total) + " bytes)");
+  char* ws = (char*)f->workspace;
+  uint16_t* h = (uint16_t*)(ws + L.h);
+  uint16_t* x = (uint16_t*)(ws + L.x);
+  uint16_t* qkv = (uint16_t*)(ws + L.qkv);
+  uint16_t* q = (uint16_t*)(ws + L.q);
+  uint16_t* attn = (uint16_t*)(ws + L.attn);
+  uint16_t* act = (uint16_t*)(ws + L.act);
+  uint16_t* xl = (uint16_t*)(ws + L.xl);
+  float* logits = f->logits ? f->logits : (float*)(ws + L.logits);
+  void* aws = ws + L.attn_ws;
+  const size_t aws_bytes = L.total - L.attn_ws;
+  const float scale = 1.0f / std::sqrt((float)D);
+  const int64_t kv_layer_elems = m->num_pages * c.kv_heads * HIGGS_PAGE_SIZE * (int64_t)D;
+  const int64_t tq_layer_bytes = m->num_pages * c.kv_heads * HIGGS_PAGE_SIZE * 64;
+  const int64_t tq_layer_scales = m->num_pages * c.kv_heads * HIGGS_PAGE_SIZE;
+
+  int rc = higgs_embed_gather_w4(m->ctx, f->tokens, T, m->embed.w, m->embed.s, m->embed.b, c.vocab,
+                                 H, h, st);
+  if (rc) return rc;
+  for (int li = 0; li < n_layers; ++li) {
+    const LayerW& Lw = m->layers[li];
+    rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_in, c.rms_eps, x, nullptr, st);
+    if (rc) return rc;
+    {
+      QLinArgs a{};
+      a.x = x;
+      a.M = T;
+      a.K = H;
+      a.N = Lw.q.N + Lw.k.N + Lw.v.N;
+      a.w = Lw.q.w;
+      a.s = Lw.q.s;
+      a.b = Lw.q.b;
+      a.nseg = 3;
+      a.seg_end[0] = Lw.q.N;
+      a.seg_end[1] = Lw.q.N + Lw.k.N;
+      a.seg_end[2] = a.N;
+      a.wseg[0] = Lw.q.w;
+      a.sseg[0] = Lw.q.s;
+      a.bseg[0] = Lw.q.b;
+      a.wseg[1] = Lw.k.w;
+      a.sseg[1] = Lw.k.s;
+      a.bseg[1] = Lw.k.b;
+      a.wseg[2] = Lw.v.w;
+      a.sseg[2] = Lw.v.s;
+      a.bseg[2] = Lw.v.b;
+      a.y = qkv;
+      HG_CUDA(launch_qlinear(a, EPI_STORE, st));
+    }
+    if (tq) {
+      rc = higgs_qknorm_rope_kv_write_tq4(
+          m->ctx, qkv, T, c.heads, c.kv_heads, Lw.qn, Lw.kn, c.rms_eps, f->positions, m->inv_freq,
+          f->slot_mapping, m->signs, (uint8_t*)m->k_pool + li * tq_layer_bytes,
+          (uint16_t*)m->k_scales + li * tq_layer_scales, (uint8_t*)m->v_pool + li * tq_layer_bytes,
+          (uint16_t*)m->v_scales + li * tq_layer_scales, c.kv_heads * HIGGS_PAGE_SIZE * 64,
+          HIGGS_PAGE_SIZE * 64, q, st);
+      if (rc) return rc;
+      rc = higgs_paged_attention_tq4(
+          m->ctx, q, B, Lq, c.heads, c.kv_heads, (const uint8_t*)m->k_pool + li * tq_layer_bytes,
+          (const uint16_t*)m->k_scales + li * tq_layer_scales,
+          (const uint8_t*)m->v_pool + li * tq_layer_bytes,
+          (const uint16_t*)m->v_scales + li * tq_layer_scales, c.kv_heads * HIGGS_PAGE_SIZE * 64,
+          HIGGS_PAGE_SIZE * 64, f->block_table, f->max_blocks, f->seq_lens, f->max_seq_len,
+          m->signs, scale, attn, aws, aws_bytes, st);
+      if (rc) return rc;
+    } else {
+      uint16_t* kc = (uint16_t*)m->k_pool + li * kv_layer_elems;
+      uint16_t* vc = (uint16_t*)m->v_pool + li * kv_layer_elems;
+      rc = higgs_qknorm_rope_kv_write(m->ctx, qkv, T, c.heads, c.kv_heads, D, Lw.qn, Lw.kn,
+                                      c.rms_eps, f->positions, m->inv_freq, f->slot_mapping, kc, vc,
+                                      (int64_t)c.kv_heads * HIGGS_PAGE_SIZE * D,
+                                      (int64_t)HIGGS_PAGE_SIZE * D, q, st);
+      if (rc) return rc;
+      rc = higgs_paged_attention(m->ctx, q, B, Lq, c.heads, c.kv_heads, D, kc, vc,
+                                 (int64_t)c.kv_heads * HIGGS_PAGE_SIZE * D,
+                                 (int64_t)HIGGS_PAGE_SIZE * D, f->block_table, f->max_blocks,
+                                 f->seq_lens, f->max_seq_len, scale, attn, aws, aws_bytes, st);
+      if (rc) return rc;
+    }
+    // h = h + o_proj(attn)   (in place: each element read then written by one thread)
+    HG_CUDA(qlin(Lw.o, attn, T, h, nullptr, h, st));
+    rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_post, c.rms_eps, x, nullptr, st);
+    if (rc) return rc;
+    {
+      QLinArgs a{};
+      a.x = x;
+      a.M = T;
+      a.K = H;
+      a.N = c.intermediate;
+      a.w = Lw.gate.w;
+      a.s = Lw.gate.s;
+      a.b = Lw.gate.b;
+      a.w2 = Lw.up.w;
+      a.s2 = Lw.up.s;
+      a.b2 = Lw.up.b;
+      a.nseg = 1;
+      a.y = act;
+      HG_CUDA(launch_qlinear(a, EPI_SWIGLU, st));
+    }
+    HG_CUDA(qlin(Lw.down, act, T, h, nullptr, h, st));
+  }
+  // final norm (+ last-token selection) and LM head
+  const int rows_lm = f->last_only ? B : T;
+  if (f->last_only) {
+    rc = higgs_rmsnorm_strided(m->ctx, h + (size_t)(Lq - 1) * H, (int64_t)Lq * H, B, H,
+                               m->final_norm, c.rms_eps, xl, st);
+  } else {
+    rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, m->final_norm, c.rms_eps, xl, nullptr, st);
+  }
+  if (rc) return rc;
+  if (f->logits || f->argmax) {
+    HG_CUDA(qlin(m->head, xl, rows_lm, nullptr, logits, nullptr, st));
+  }
+  if (f->argmax) {
+    rc = higgs_argmax(m->ctx, logits, rows_lm, c.vocab, f->argmax, st);
+    if (rc) return rc;
+  }
+  if (f->hidden_out) {
+    HG_CUDA(cudaMemcpyAsync(f->hidden_out, xl, (size_t)rows_lm * H * 2, cudaMemcpyDeviceToDevice, st));
+  }
+  return HIGGS_OK;
+}
+
+int validate_forward(higgs_model* m, const higgs_forward_args* f) {
+  HG_CHECK_ARG(m && f, "higgs_model_forward: null argument");
+  if (!m->finalized) return fail(HIGGS_ERR_STATE, "higgs_model_forward: call higgs_model_finalize first");
+  if (!m->k_pool || !m->v_pool) return fail(HIGGS_ERR_STATE, "higgs_model_forward: no KV cache set");
+  HG_CHECK_ARG(f->B > 0 && f->Lq > 0, "higgs_model_forward: B and Lq must be positive");
+  HG_CHECK_ARG(f->tokens && f->positions && f->slot_mapping && f->block_table && f->seq_lens,
+               "higgs_model_forward: null input vector");
+  HG_CHECK_ARG(f->n_layers >= 0 && f->n_layers <= m->cfg.layers, "higgs_model_forward: bad n_layers");
+  HG_CHECK_ARG(f->max_seq_len >= f->Lq && (int64_t)f->max_blocks * HIGGS_PAGE_SIZE >= f->max_seq_len,
+               "higgs_model_forward: max_seq_len / max_blocks inconsistent");
+  HG_CHECK_ARG(f->workspace, "higgs_model_forward: null workspace");
+  return HIGGS_OK;
+}
+
+}  // namespace
+
+extern "C" int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg, higgs_model** out) {
+  HG_CHECK_ARG(ctx && cfg && out, "higgs_model_create: null argument");
+  *out = nullptr;
+  const higgs_model_config& c = *cfg;
+  HG_CHECK_ARG(c.hidden > 0 && c.hidden % 256 == 0, "higgs_model_create: hidden must be a multiple of 256");
+  HG_CHECK_ARG(c.layers > 0 && c.heads > 0 && c.kv_heads > 0 && c.heads % c.kv_heads == 0,
+               "higgs_model_create: bad layer / head counts");
+  HG_CHECK_ARG(c.head_dim == 64 || c.head_dim == 128, "higgs_model_create: head_dim must be 64 or 128");
+  HG_CHECK_ARG(c.intermediate > 0 && c.intermediate % 256 == 0,
+               "higgs_model_create: intermediate must be a multiple of 256");
+  HG_CHECK_ARG(c.vocab > 0 && c.vocab % 16 == 0, "higgs_model_create: vocab must be a multiple of 16");
+  HG_CHECK_ARG((c.heads * c.head_dim) % 256 == 0, "higgs_model_create: heads*head_dim must be a multiple of 256");
+  HG_CHECK_ARG(c.kv_mode == HIGGS_KV_BF16 || (c.kv_mode == HIGGS_KV_TQ4 && c.head_dim == 128),
+               "higgs_model_create: TurboQuant KV needs head_dim 128");
+  higgs_model* m = new higgs_model;
+  m->ctx = ctx;
+  m->cfg = c;
+  *out = m;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_model_destroy(higgs_model* m) {
+  if (!m) return HIGGS_OK;
+  if (m->inv_freq) cudaFree(m->inv_freq);
+  delete m;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_model_set_tensor(higgs_model* m, const char* name, const void* ptr, int dtype,
+                                      const int64_t* shape, int ndim) {
+  HG_CHECK_ARG(m && name && ptr && (ndim == 0 || shape) && ndim >= 0 && ndim <= 4,
+               "higgs_model_set_tensor: bad argument");
+  HG_CHECK_ARG(dtype == HIGGS_DTYPE_U32 || dtype == HIGGS_DTYPE_BF16 || dtype == HIGGS_DTYPE_F32,
+               "higgs_model_set_tensor: unknown dtype");
+  TensorRef t;
+  t.ptr = ptr;
+  t.dtype = dtype;
+  t.shape.assign(shape, shape + ndim);
+  m->tensors[name] = t;
+  m->finalized = false;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_model_finalize(higgs_model* m) {
+  HG_CHECK_ARG(m, "higgs_model_finalize: null model");
+  const higgs_model_config& c = m->cfg;
+  const int H = c.hidden, D = c.head_dim;
+  int rc = get_q(m, "model.embed_tokens", c.vocab, H, m->embed);
+  if (rc) return rc;
+  if (c.tie_word_embeddings) {
+    m->head = m->embed;
+  } else {
+    rc = get_q(m, "lm_head", c.vocab, H, m->head);
+    if (rc) return rc;
+  }
+  rc = get_vec(m, "model.norm.weight", H, m->final_norm);
+  if (rc) return rc;
+  m->layers.assign(c.layers, LayerW{});
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "model.layers." + std::to_string(i) + ".";
+    LayerW& L = m->layers[i];
+    if ((rc = get_vec(m, p + "input_layernorm.weight", H, L.ln_in))) return rc;
+    if ((rc = get_vec(m, p + "post_attention_layernorm.weight", H, L.ln_post))) return rc;
+    if ((rc = get_q(m, p + "self_attn.q_proj", c.heads * D, H, L.q))) return rc;
+    if ((rc = get_q(m, p + "self_attn.k_proj", c.kv_heads * D, H, L.k))) return rc;
+    if ((rc = get_q(m, p + "self_attn.v_proj", c.kv_heads * D, H, L.v))) return rc;
+    if ((rc = get_q(m, p + "self_attn.o_proj", H, c.heads * D, L.o))) return rc;
+    if (c.qk_norm) {
+      if ((rc = get_vec(m, p + "self_attn.q_norm.weight", D, L.qn))) return rc;
+      if ((rc = get_vec(m, p + "self_attn.k_norm.weight", D, L.kn))) return rc;
+    }
+    if ((rc = get_q(m, p + "mlp.gate_proj", c.intermediate, H, L.gate))) return rc;
+    if ((rc = get_q(m, p + "mlp.up_proj", c.intermediate, H, L.up))) return rc;
+    if ((rc = get_q(m, p + "mlp.down_proj", H, c.intermediate, L.down))) return rc;
+  }
+  if (!m->inv_freq) {
+    std::vector<float> f(D / 2);
+    for (int i = 0; i < D / 2; ++i) f[i] = (float)std::pow((double)c.rope_theta, -(2.0 * i) / D);
+    HG_CUDA(cudaMalloc(&m->inv_freq, f.size() * sizeof(float)));
+    HG_CUDA(cudaMemcpy(m->inv_freq, f.data(), f.size() * sizeof(float), cudaMemcpyHostToDevice));
+  }
+  attention_prepare();
+  m->finalized = true;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_model_set_kv_cache(higgs_model* m, void* k_pool, void* v_pool,
+                                        int64_t num_pages) {
+  HG_CHECK_ARG(m && k_pool && v_pool && num_pages > 0, "higgs_model_set_kv_cache: bad argument");
+  HG_CHECK_ARG(m->cfg.kv_mode == HIGGS_KV_BF16, "higgs_model_set_kv_cache: model uses TurboQuant KV");
+  m->k_pool = k_pool;
+  m->v_pool = v_pool;
+  m->num_pages = num_pages;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_model_set_kv_cache_tq4(higgs_model* m, uint8_t* k_codes, void* k_scales,
+                                            uint8_t* v_codes, void* v_scales, int64_t num_pages,
+                                            const int8_t* signs) {
+  HG_CHECK_ARG(m && k_codes && k_scales && v_codes && v_scales && signs && num_pages > 0,
+               "higgs_model_set_kv_cache_tq4: bad argument");
+  HG_CHECK_ARG(m->cfg.kv_mode == HIGGS_KV_TQ4, "higgs_model_set_kv_cache_tq4: model uses bf16 KV");
+  m->k_pool = k_codes;
+  m->v_pool = v_codes;
+  m->k_scales = k_scales;
+  m->v_scales = v_scales;
+  m->signs = signs;
+  m->num_pages = num_pages;
+  return HIGGS_OK;
+}
+
+extern "C" size_t higgs_model_workspace_size(const higgs_model* m, int B, int Lq, int max_seq_len,
+                                             int last_only) {
+  if (!m || B <= 0 || Lq <= 0) return 0;
+  return layout(m->cfg, B, Lq, max_seq_len, last_only != 0).total;
+}
+
+extern "C" int higgs_model_forward(higgs_model* m, const higgs_forward_args* f, void* stream) {
+  int rc = validate_forward(m, f);
+  if (rc) return rc;
+  return forward_impl(m, f, (cudaStream_t)stream);
+}
+
+extern "C" int higgs_model_capture(higgs_model* m, const higgs_forward_args* f, void* stream,
+                                   higgs_graph** out) {
+  HG_CHECK_ARG(out && stream, "higgs_model_capture: needs a non-default stream and an out pointer");
+  *out = nullptr;
+  int rc = validate_forward(m, f);
+  if (rc) return rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  HG_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+  rc = forward_impl(m, f, st);
+  cudaGraph_t graph = nullptr;
+  cudaError_t e = cudaStreamEndCapture(st, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  cudaGraphExec_t exec = nullptr;
+  e = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
+  higgs_graph* g = new higgs_graph;
+  g->exec = exec;
+  *out = g;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_graph_launch(higgs_graph* g, void* stream) {
+  HG_CHECK_ARG(g && g->exec, "higgs_graph_launch: null graph");
+  HG_CUDA(cudaGraphLaunch(g->exec, (cudaStream_t)stream));
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_graph_destroy(higgs_graph* g) {
+  if (!g) return HIGGS_OK;
+  if (g->exec) cudaGraphExecDestroy(g->exec);
+  delete g;
+  return HIGGS_OK;
+}

@@ -1,0 +1,130 @@
+"""ctypes binding of libhiggs_cuda.so (the C ABI declared in include/higgs_cuda.h).
+
+The library is built in-tree by ``higgs_b200.build``; importing an op without
+it raises ``HiggsUnavailable`` -- there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libhiggs_cuda.so")
+
+P = ctypes.c_void_p
+I = ctypes.c_int
+I64 = ctypes.c_int64
+F = ctypes.c_float
+SZ = ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/higgs_cuda.h
+SIGNATURES: dict[str, tuple] = {
+    "higgs_init": (I, [I, ctypes.POINTER(P)]),
+    "higgs_destroy": (I, [P]),
+    "higgs_last_error": (ctypes.c_char_p, []),
+    "higgs_version": (I, []),
+    "higgs_w4_dequantize": (I, [P, P, P, P, I, I, P, P]),
+    "higgs_embed_gather_w4": (I, [P, P, I, P, P, P, I, I, P, P]),
+    "higgs_qlinear_w4g64": (I, [P, P, I, I, P, P, P, I, P, P, P, P]),
+    "higgs_qlinear_gate_up_swiglu": (I, [P, P, I, I, P, P, P, P, P, P, I, P, P]),
+    "higgs_rmsnorm": (I, [P, P, P, I, I, P, F, P, P, P]),
+    "higgs_rope": (I, [P, P, I, I, I, P, P, P, P]),
+    "higgs_qknorm_rope_kv_write": (I, [P, P, I, I, I, I, P, P, F, P, P, P, P, P, I64, I64, P, P]),
+    "higgs_paged_attention_workspace_size": (SZ, [I, I, I, I, I, I]),
+    "higgs_paged_attention": (I, [P, P, I, I, I, I, I, P, P, I64, I64, P, I, P, I, F, P, P, SZ, P]),
+    "higgs_tq4_encode": (I, [P, P, I64, P, P, P, P]),
+    "higgs_qknorm_rope_kv_write_tq4": (I, [P, P, I, I, I, P, P, F, P, P, P, P, P, P, P, P, I64, I64, P, P]),
+    "higgs_paged_attention_tq4_workspace_size": (SZ, [I, I, I, I, I]),
+    "higgs_paged_attention_tq4": (I, [P, P, I, I, I, I, P, P, P, P, I64, I64, P, I, P, I, P, F, P, P, SZ, P]),
+    "higgs_argmax": (I, [P, P, I, I, P, P]),
+    "higgs_sample": (I, [P, P, I, I, F, P, P, P]),
+    "higgs_spec_accept": (I, [P, P, P, P, I, I, I, F, P, P, P, P, P]),
+    "higgs_apply_penalties": (I, [P, P, I, I, P, P, I, F, F, F, P]),
+    "higgs_rmsnorm_strided": (I, [P, P, I64, I, I, P, F, P, P]),
+    "higgs_model_create": (I, [P, P, ctypes.POINTER(P)]),
+    "higgs_model_set_tensor": (I, [P, ctypes.c_char_p, P, I, ctypes.POINTER(I64), I]),
+    "higgs_model_finalize": (I, [P]),
+    "higgs_model_destroy": (I, [P]),
+    "higgs_model_set_kv_cache": (I, [P, P, P, I64]),
+    "higgs_model_set_kv_cache_tq4": (I, [P, P, P, P, P, I64, P]),
+    "higgs_model_workspace_size": (SZ, [P, I, I, I, I]),
+    "higgs_model_forward": (I, [P, P, P]),
+    "higgs_model_capture": (I, [P, P, P, ctypes.POINTER(P)]),
+    "higgs_graph_launch": (I, [P, P]),
+    "higgs_graph_destroy": (I, [P]),
+}
+
+
+class ModelConfig(ctypes.Structure):
+    """higgs_model_config (include/higgs_cuda.h)."""
+    _fields_ = [("hidden", I), ("layers", I), ("intermediate", I), ("heads", I), ("kv_heads", I),
+                ("head_dim", I), ("vocab", I), ("rms_eps", F), ("rope_theta", F),
+                ("tie_word_embeddings", I), ("qk_norm", I), ("kv_mode", I)]
+
+
+class ForwardArgs(ctypes.Structure):
+    """higgs_forward_args (include/higgs_cuda.h)."""
+    _fields_ = [("B", I), ("Lq", I), ("tokens", P), ("positions", P), ("slot_mapping", P),
+                ("block_table", P), ("max_blocks", I), ("seq_lens", P), ("max_seq_len", I),
+                ("n_layers", I), ("last_only", I), ("logits", P), ("argmax", P), ("hidden_out", P),
+                ("workspace", P), ("workspace_bytes", SZ)]
+
+
+DTYPE_U32, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
+KV_BF16, KV_TQ4 = 0, 1
+
+
+class HiggsUnavailable(RuntimeError):
+    """libhiggs_cuda.so is missing or cannot be loaded."""
+
+
+class HiggsError(RuntimeError):
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn} failed ({code}): {msg}")
+        self.code = code
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the library once and attach the declared signatures."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise HiggsUnavailable(
+                f"{path} not found: build it with `python -m higgs_b200.build` (no CPU fallback)")
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def call(name: str, *args) -> int:
+    lib = load()
+    rc = getattr(lib, name)(*args)
+    if rc != 0:
+        raise HiggsError(name, rc, lib.higgs_last_error().decode())
+    return rc
+
+
+_ctx: dict[int, int] = {}
+
+
+def ctx(device: int) -> int:
+    """Per-device context handle (created on first use)."""
+    if device not in _ctx:
+        lib = load()
+        h = P()
+        rc = lib.higgs_init(device, ctypes.byref(h))
+        if rc != 0:
+            raise HiggsError("higgs_init", rc, lib.higgs_last_error().decode())
+        _ctx[device] = h.value
+    return _ctx[device]

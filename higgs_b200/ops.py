@@ -1,0 +1,261 @@
+"""Torch-facing wrappers of the C ABI, named after the mlx-rs ops they replace.
+
+Every function takes CUDA tensors, enqueues on torch's current stream and
+returns new tensors (or fills ``out``).  bf16 activations, u32 packed weights
+and bf16 scales/biases follow the MLX affine layout (see include/higgs_cuda.h).
+Reference call sites are cited per function.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ffi
+
+PAGE = 16
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _st(dev: torch.device):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _ctx(t: torch.Tensor) -> int:
+    if not t.is_cuda:
+        raise ValueError("higgs ops take CUDA tensors (there is no CPU fallback)")
+    return ffi.ctx(t.device.index)
+
+
+def _chk(t: torch.Tensor, dtype, name: str):
+    if t.dtype != dtype:
+        raise TypeError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+# ---- a1/a2 ----------------------------------------------------------------
+
+def quantized_matmul(x, w, scales, biases, transpose: bool = True, group_size: int = 64,
+                     bits: int = 4, *, residual=None, out_f32: bool = False):
+    """ops::quantized_matmul (qwen3_next.rs:174-183): y = x . dequant(w)^T.
+
+    x bf16 [..., K]; w u32 [N, K/8]; scales/biases bf16 [N, K/64].
+    Returns bf16 [..., N] (f32 when out_f32).  ``residual`` (bf16 [..., N])
+    is added after rounding the product to bf16 (TransformerBlock residual).
+    """
+    if not transpose or group_size != 64 or bits != 4:
+        raise NotImplementedError("only transpose=True, group_size=64, bits=4 (MLX affine W4 g64)")
+    _chk(x, torch.bfloat16, "x")
+    K = x.shape[-1]
+    N = w.shape[0]
+    if w.shape[1] * 8 != K:
+        raise ValueError(f"w has {w.shape[1] * 8} inputs, x has {K}")
+    M = x.numel() // K
+    y = torch.empty(*x.shape[:-1], N, dtype=torch.float32 if out_f32 else torch.bfloat16,
+                    device=x.device)
+    ffi.call("higgs_qlinear_w4g64", _ctx(x), _p(x), M, K, _p(w), _p(scales), _p(biases), N,
+             None if out_f32 else _p(y), _p(y) if out_f32 else None, _p(residual), _st(x.device))
+    return y
+
+
+def gate_up_swiglu(x, wg, sg, bg, wu, su, bu):
+    """swiglu(gate_proj(x), up_proj(x)) fused (transformer.rs:349-353, qwen3_next.rs:275-277)."""
+    _chk(x, torch.bfloat16, "x")
+    K = x.shape[-1]
+    N = wg.shape[0]
+    M = x.numel() // K
+    y = torch.empty(*x.shape[:-1], N, dtype=torch.bfloat16, device=x.device)
+    ffi.call("higgs_qlinear_gate_up_swiglu", _ctx(x), _p(x), M, K, _p(wg), _p(sg), _p(bg),
+             _p(wu), _p(su), _p(bu), N, _p(y), _st(x.device))
+    return y
+
+
+def dequantize(w, scales, biases, group_size: int = 64, bits: int = 4):
+    """ops::dequantize (qwen3_next.rs:249-256): bf16 [N, K]."""
+    if group_size != 64 or bits != 4:
+        raise NotImplementedError("only group_size=64, bits=4")
+    N, K = w.shape[0], w.shape[1] * 8
+    out = torch.empty(N, K, dtype=torch.bfloat16, device=w.device)
+    ffi.call("higgs_w4_dequantize", _ctx(w), _p(w), _p(scales), _p(biases), N, K, _p(out),
+             _st(w.device))
+    return out
+
+
+def embed_gather(ids, w, scales, biases):
+    """QEmbedding::forward (qwen3_next.rs:248-257): bf16 [*ids.shape, H]."""
+    _chk(ids, torch.int32, "ids")
+    V, H = w.shape[0], w.shape[1] * 8
+    out = torch.empty(*ids.shape, H, dtype=torch.bfloat16, device=ids.device)
+    ffi.call("higgs_embed_gather_w4", _ctx(ids), _p(ids), ids.numel(), _p(w), _p(scales),
+             _p(biases), V, H, _p(out), _st(ids.device))
+    return out
+
+
+# ---- a3/a4 ------------------------------------------------------------------
+
+def rms_norm(x, weight, eps: float, residual=None, want_h: bool = False):
+    """fast::rms_norm (transformer.rs:375-377): returns y, or (y, h) with h = x + residual."""
+    _chk(x, torch.bfloat16, "x")
+    H = x.shape[-1]
+    rows = x.numel() // H
+    y = torch.empty_like(x)
+    h = torch.empty_like(x) if (residual is not None and want_h) else None
+    ffi.call("higgs_rmsnorm", _ctx(x), _p(x), _p(residual), rows, H, _p(weight), float(eps),
+             _p(y), _p(h), _st(x.device))
+    return (y, h) if want_h else y
+
+
+def rope_inv_freq(dims: int, base: float, device=None) -> torch.Tensor:
+    """inv_freq[i] = base^(-2i/dims), computed in f64 and rounded to f32."""
+    f = [base ** (-(2.0 * i) / dims) for i in range(dims // 2)]
+    return torch.tensor(f, dtype=torch.float32, device=device)
+
+
+def rope(x, positions, inv_freq):
+    """fast::rope(traditional=false, scale=1) (utils.rs:16-26); x bf16 [rows, heads, D]."""
+    _chk(x, torch.bfloat16, "x")
+    rows, heads, D = x.shape
+    y = torch.empty_like(x)
+    ffi.call("higgs_rope", _ctx(x), _p(x), rows, heads, D, _p(positions), _p(inv_freq), _p(y),
+             _st(x.device))
+    return y
+
+
+def qknorm_rope_kv_write(qkv, Hq: int, Hkv: int, D: int, q_norm_w, k_norm_w, eps: float,
+                         positions, inv_freq, slot_mapping, k_cache, v_cache, page_stride=None,
+                         head_stride=None):
+    """Attention front half + cache append (transformer.rs:246-289, cache.rs:236-311).
+
+    Caches are [num_pages, Hkv, 16, D] bf16 unless strides are given.  Returns q bf16 [T, Hq, D].
+    """
+    T = qkv.shape[0]
+    if page_stride is None:
+        page_stride = Hkv * PAGE * D
+    if head_stride is None:
+        head_stride = PAGE * D
+    q = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=qkv.device)
+    ffi.call("higgs_qknorm_rope_kv_write", _ctx(qkv), _p(qkv), T, Hq, Hkv, D, _p(q_norm_w),
+             _p(k_norm_w), float(eps), _p(positions), _p(inv_freq), _p(slot_mapping), _p(k_cache),
+             _p(v_cache), int(page_stride), int(head_stride), _p(q), _st(qkv.device))
+    return q
+
+
+# ---- a6/a13/a14 -------------------------------------------------------------
+
+def attention_workspace(B, Lq, Hq, Hkv, D, max_seq_len, device) -> torch.Tensor:
+    n = ffi.load().higgs_paged_attention_workspace_size(B, Lq, Hq, Hkv, D, max_seq_len)
+    return torch.zeros(max(n, 4096), dtype=torch.uint8, device=device)
+
+
+def paged_attention(q, k_cache, v_cache, block_table, seq_lens, max_seq_len: int, scale=None,
+                    page_stride=None, head_stride=None, workspace=None):
+    """fast::scaled_dot_product_attention over a paged cache (utils.rs:45-60, masks 64-125).
+
+    q bf16 [B, Lq, Hq, D]; caches [num_pages, Hkv, 16, D] (or explicit strides);
+    block_table int32 [B, max_blocks]; seq_lens int32 [B].
+    """
+    B, Lq, Hq, D = q.shape
+    Hkv = k_cache.shape[1] if head_stride is None else None
+    if Hkv is None:
+        raise ValueError("give Hkv through the cache shape")
+    if page_stride is None:
+        page_stride = Hkv * PAGE * D
+    if head_stride is None:
+        head_stride = PAGE * D
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if workspace is None:
+        workspace = attention_workspace(B, Lq, Hq, Hkv, D, max_seq_len, q.device)
+    out = torch.empty_like(q)
+    ffi.call("higgs_paged_attention", _ctx(q), _p(q), B, Lq, Hq, Hkv, D, _p(k_cache),
+             _p(v_cache), int(page_stride), int(head_stride), _p(block_table),
+             block_table.shape[1], _p(seq_lens), int(max_seq_len), float(scale), _p(out),
+             _p(workspace), workspace.numel(), _st(q.device))
+    return out
+
+
+def tq4_encode(x, signs):
+    """TurboQuant encode of bf16 [n, 128] -> (codes u8 [n, 64], scales fp16 [n])."""
+    n = x.numel() // 128
+    codes = torch.empty(n, 64, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(n, dtype=torch.float16, device=x.device)
+    ffi.call("higgs_tq4_encode", _ctx(x), _p(x), n, _p(signs), _p(codes), _p(scales),
+             _st(x.device))
+    return codes, scales
+
+
+def qknorm_rope_kv_write_tq4(qkv, Hq: int, Hkv: int, q_norm_w, k_norm_w, eps: float, positions,
+                             inv_freq, slot_mapping, signs, k_codes, k_scales, v_codes, v_scales):
+    """As qknorm_rope_kv_write, storing TurboQuant codes [pages, Hkv, 16, 64] + fp16 scales."""
+    T = qkv.shape[0]
+    q = torch.empty(T, Hq, 128, dtype=torch.bfloat16, device=qkv.device)
+    ffi.call("higgs_qknorm_rope_kv_write_tq4", _ctx(qkv), _p(qkv), T, Hq, Hkv, _p(q_norm_w),
+             _p(k_norm_w), float(eps), _p(positions), _p(inv_freq), _p(slot_mapping), _p(signs),
+             _p(k_codes), _p(k_scales), _p(v_codes), _p(v_scales), Hkv * PAGE * 64, PAGE * 64,
+             _p(q), _st(qkv.device))
+    return q
+
+
+def paged_attention_tq4(q, k_codes, k_scales, v_codes, v_scales, block_table, seq_lens,
+                        max_seq_len: int, signs, scale=None, workspace=None):
+    """Decode attention over TurboQuant pages [num_pages, Hkv, 16, 64] (+ fp16 scales)."""
+    B, Lq, Hq, D = q.shape
+    assert D == 128
+    Hkv = k_codes.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if workspace is None:
+        workspace = attention_workspace(B, Lq, Hq, Hkv, 128, max_seq_len, q.device)
+    out = torch.empty_like(q)
+    ffi.call("higgs_paged_attention_tq4", _ctx(q), _p(q), B, Lq, Hq, Hkv, _p(k_codes),
+             _p(k_scales), _p(v_codes), _p(v_scales), Hkv * PAGE * 64, PAGE * 64,
+             _p(block_table), block_table.shape[1], _p(seq_lens), int(max_seq_len), _p(signs),
+             float(scale), _p(out), _p(workspace), workspace.numel(), _st(q.device))
+    return out
+
+
+# ---- a10/a15 ----------------------------------------------------------------
+
+def argmax(logits):
+    """sample() at T=0 (lib.rs:373-377); logits f32 [B, V] -> int32 [B], ties -> first."""
+    _chk(logits, torch.float32, "logits")
+    B, V = logits.shape
+    out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    ffi.call("higgs_argmax", _ctx(logits), _p(logits), B, V, _p(out), _st(logits.device))
+    return out
+
+
+def sample(logits, temperature: float, uniforms=None):
+    """sample() (lib.rs:373-385) with explicit uniforms [B] for T > 0."""
+    _chk(logits, torch.float32, "logits")
+    B, V = logits.shape
+    out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    ffi.call("higgs_sample", _ctx(logits), _p(logits), B, V, float(temperature), _p(uniforms),
+             _p(out), _st(logits.device))
+    return out
+
+
+def spec_accept(target_logits, draft_logits, draft_tokens, temperature: float,
+                accept_uniforms=None, sample_uniforms=None):
+    """Speculative acceptance: (accepted int32 [B], out_tokens int32 [B, k+1])."""
+    B, k1, V = target_logits.shape
+    k = k1 - 1
+    acc = torch.empty(B, dtype=torch.int32, device=target_logits.device)
+    toks = torch.empty(B, k1, dtype=torch.int32, device=target_logits.device)
+    ffi.call("higgs_spec_accept", _ctx(target_logits), _p(target_logits), _p(draft_logits),
+             _p(draft_tokens), B, k, V, float(temperature), _p(accept_uniforms),
+             _p(sample_uniforms), _p(acc), _p(toks), _st(target_logits.device))
+    return acc, toks
+
+
+def apply_penalties(logits, history, hist_lens, rep: float = 1.0, freq: float = 0.0,
+                    pres: float = 0.0):
+    """apply_penalties (lib.rs:278-363), in place on f32 [B, V]."""
+    B, V = logits.shape
+    ffi.call("higgs_apply_penalties", _ctx(logits), _p(logits), B, V, _p(history), _p(hist_lens),
+             history.shape[1], float(rep), float(freq), float(pres), _st(logits.device))
+    return logits

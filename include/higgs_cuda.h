@@ -1,0 +1,314 @@
+/*
+ * higgs_cuda.h -- C ABI of libhiggs_cuda.so, the B200 (sm_100a) decode hot
+ * path for higgs.
+ *
+ * Each entry point replaces one mlx-rs / mlx-sys op that higgs-models calls
+ * today; the citation above each declaration is the reference call site it
+ * replaces (paths relative to the higgs repository).
+ *
+ * Conventions
+ *   - Every function returns 0 on success or a negative HIGGS_ERR_* code and
+ *     never aborts; higgs_last_error() returns the calling thread's message
+ *     for the most recent failure.
+ *   - All tensor arguments are caller-owned DEVICE pointers on the context's
+ *     device, row-major and densely packed unless a stride says otherwise.
+ *     "bf16" / "fp16" buffers are passed as void*.
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls only
+ *     enqueue work; they do not synchronise.  Device memory is allocated only
+ *     by higgs_init() and higgs_model_finalize() (a RoPE table); every other
+ *     call takes its scratch from caller-provided workspace whose size a
+ *     *_workspace_size() query returns.
+ *   - A context may be used by one host thread at a time; distinct contexts
+ *     are independent.
+ *   - Quantized weights use the MLX affine layout: weight u32 [N, K/8] with
+ *     element k of a row in word k/8 at bits 4*(k%8); scales and biases bf16
+ *     [N, K/64]; w = scale * q + bias (group size 64, 4 bits).
+ */
+#ifndef HIGGS_CUDA_H
+#define HIGGS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define HIGGS_OK 0
+#define HIGGS_ERR_INVALID_ARG -1
+#define HIGGS_ERR_CUDA -2
+#define HIGGS_ERR_UNSUPPORTED -3
+#define HIGGS_ERR_WORKSPACE -4
+#define HIGGS_ERR_TIMEOUT -5
+#define HIGGS_ERR_STATE -6
+
+#define HIGGS_PAGE_SIZE 16 /* tokens per KV page */
+
+#define HIGGS_DTYPE_U32 0
+#define HIGGS_DTYPE_BF16 1
+#define HIGGS_DTYPE_F32 2
+
+#define HIGGS_KV_BF16 0 /* bf16 pages [pages, Hkv, 16, D] */
+#define HIGGS_KV_TQ4 1  /* TurboQuant pages: codes [pages, Hkv, 16, 64] + fp16 scales */
+
+typedef struct higgs_ctx higgs_ctx;
+typedef struct higgs_model higgs_model;
+typedef struct higgs_graph higgs_graph;
+
+/* ---- context and errors ------------------------------------------------ */
+
+/* Replaces the process-global MLX error handler registration
+ * (crates/higgs-models/src/qwen3_next.rs:29-51) and default-stream setup
+ * (crates/higgs-engine/src/simple.rs:450-452). */
+int higgs_init(int device, higgs_ctx** out);
+int higgs_destroy(higgs_ctx* ctx);
+/* Message of the calling thread's last failure ("" if none).  Replaces the
+ * error text captured at crates/higgs-models/src/qwen3_next.rs:337-360. */
+const char* higgs_last_error(void);
+int higgs_version(void);
+
+/* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
+
+/* ops::dequantize (crates/higgs-models/src/qwen3_next.rs:249-256):
+ * out bf16 [N, K] = bf16(scale * q + bias). */
+int higgs_w4_dequantize(higgs_ctx* ctx, const uint32_t* w, const void* scales, const void* biases,
+                        int N, int K, void* out, void* stream);
+
+/* QEmbedding::forward (crates/higgs-models/src/qwen3_next.rs:248-257):
+ * out bf16 [n_ids, H] = dequantized rows ids[i] of the [V, H] table.  Ids
+ * outside [0, V) produce zero rows. */
+int higgs_embed_gather_w4(higgs_ctx* ctx, const int32_t* ids, int n_ids, const uint32_t* w,
+                          const void* scales, const void* biases, int V, int H, void* out,
+                          void* stream);
+
+/* ops::quantized_matmul(x, w, scales, biases, transpose=true, 64, 4)
+ * (crates/higgs-models/src/qwen3_next.rs:174-183, QLinear::forward 211-220;
+ * MaybeQuantized<nn::Linear> crates/higgs-models/src/transformer.rs:943-951;
+ * tied head QEmbedding::as_linear qwen3_next.rs:259-268).
+ *   x bf16 [M, K]; y = x . W^T with W [N, K].
+ *   y       bf16 [M, N] (may be NULL when y_f32 is given)
+ *   y_f32   f32  [M, N] (optional, unrounded accumulator)
+ *   residual bf16 [M, N] (optional): y = bf16(bf16(x W^T) + residual), the
+ *            residual add of TransformerBlock::forward transformer.rs:410,417.
+ * K must be a multiple of 256; any M >= 1. */
+int higgs_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, const uint32_t* w,
+                        const void* scales, const void* biases, int N, void* y, float* y_f32,
+                        const void* residual, void* stream);
+
+/* Mlp::forward gate/up half (crates/higgs-models/src/transformer.rs:349-353,
+ * swiglu qwen3_next.rs:275-277): y bf16 [M, N] = silu(x Wg^T) * (x Wu^T),
+ * both projections rounded to bf16 first, one bf16 rounding of the product. */
+int higgs_qlinear_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M, int K,
+                                 const uint32_t* w_gate, const void* s_gate, const void* b_gate,
+                                 const uint32_t* w_up, const void* s_up, const void* b_up, int N,
+                                 void* y, void* stream);
+
+/* ---- a3/a4: norms and RoPE ---------------------------------------------- */
+
+/* nn::RmsNorm / fast::rms_norm (crates/higgs-models/src/transformer.rs:375-377,
+ * 407, 415, 525): y = bf16(h * rsqrt(mean(h^2) + eps) * weight), rows x H,
+ * with h = bf16(x + residual) when residual != NULL (written to h_out when
+ * h_out != NULL), else h = x. */
+int higgs_rmsnorm(higgs_ctx* ctx, const void* x, const void* residual, int rows, int H,
+                  const void* weight, float eps, void* y, void* h_out, void* stream);
+
+/* higgs_rmsnorm over rows that are in_stride elements apart (e.g. the last
+ * token of each sequence before the LM head, transformer.rs:525); y dense
+ * [rows, H]. */
+int higgs_rmsnorm_strided(higgs_ctx* ctx, const void* x, int64_t in_stride, int rows, int H,
+                          const void* weight, float eps, void* y, void* stream);
+
+/* fast::rope, traditional=false, scale=1 (crates/higgs-models/src/utils.rs:16-26):
+ * x, y bf16 [rows, heads, D]; row r rotated at absolute position positions[r];
+ * inv_freq f32 [D/2] = base^(-2i/D). */
+int higgs_rope(higgs_ctx* ctx, const void* x, int rows, int heads, int D,
+               const int32_t* positions, const float* inv_freq, void* y, void* stream);
+
+/* Attention::forward front half (crates/higgs-models/src/transformer.rs:246-289)
+ * fused with the cache append of SteppingKeyValueCache::update_and_fetch
+ * (crates/higgs-models/src/cache.rs:236-311), on a paged cache:
+ *   qkv bf16 [T, (Hq + 2 Hkv) * D]  (the fused q|k|v projection output)
+ *   q/k head RMSNorm with q_norm_w / k_norm_w bf16 [D] when non-NULL (Qwen3,
+ *   transformer.rs:193-207), then RoPE at positions[t], then
+ *   q_out bf16 [T, Hq, D]; K and V of token t stored at page
+ *   slot_mapping[t] / 16, slot slot_mapping[t] % 16: element
+ *   page * page_stride + h * head_stride + slot * D of k_cache / v_cache.
+ *   slot_mapping[t] < 0 skips the store. */
+int higgs_qknorm_rope_kv_write(higgs_ctx* ctx, const void* qkv, int T, int Hq, int Hkv, int D,
+                               const void* q_norm_w, const void* k_norm_w, float eps,
+                               const int32_t* positions, const float* inv_freq,
+                               const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                               int64_t page_stride, int64_t head_stride, void* q_out,
+                               void* stream);
+
+/* ---- a5/a6/a13: paged decode attention ----------------------------------- */
+
+/* fast::scaled_dot_product_attention with GQA (crates/higgs-models/src/utils.rs:45-60)
+ * and the masks of utils.rs:64-125, over a paged KV cache.
+ *   q   bf16 [B, Lq, Hq, D] (D = 64 or 128; Hq / Hkv * Lq <= 64)
+ *   query t of sequence b sits at position seq_lens[b] - Lq + t and attends
+ *   to keys 0..that position (causal, includes itself).
+ *   block_table int32 [B, max_blocks]; page p of the cache holds key/value
+ *   slot s of kv head h at element p * page_stride + h * head_stride + s * D.
+ *   out bf16 [B, Lq, Hq, D].
+ * max_seq_len bounds every seq_lens[b] (it sizes the split-K grid; the
+ * kernel reads the real lengths on the device, so a captured graph stays valid
+ * while lengths grow up to that bound).  workspace: at least
+ * higgs_paged_attention_workspace_size() bytes; its first 4096 bytes hold
+ * split counters that must be zero before the first call (each call leaves
+ * them zero). */
+size_t higgs_paged_attention_workspace_size(int B, int Lq, int Hq, int Hkv, int D,
+                                            int max_seq_len);
+int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq, int Hkv, int D,
+                          const void* k_cache, const void* v_cache, int64_t page_stride,
+                          int64_t head_stride, const int32_t* block_table, int max_blocks,
+                          const int32_t* seq_lens, int max_seq_len, float scale, void* out,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- a14: TurboQuant-style 4-bit KV (no reference counterpart; the
+ * KeyValueCache trait only reserves is_quantized/group_size/bits hooks,
+ * crates/higgs-models/src/cache.rs:4-18) ------------------------------------ */
+
+/* Encode n head vectors x bf16 [n, 128]: v' = H diag(signs) x / sqrt(128)
+ * (signs int8 [128] of +-1), fp16 scale s = max|v'| / 7,
+ * code = clamp(rint(v'/s), -8, 7) + 8, byte j = c[2j] | c[2j+1] << 4.
+ * codes u8 [n, 64], scales fp16 [n]. */
+int higgs_tq4_encode(higgs_ctx* ctx, const void* x, int64_t n, const int8_t* signs,
+                     uint8_t* codes, void* scales, void* stream);
+
+/* higgs_qknorm_rope_kv_write with a TurboQuant cache (D = 128): codes of token
+ * t, kv head h go to byte page * page_stride + h * head_stride + slot * 64 of
+ * k_codes / v_codes, scales (fp16) to element
+ * page * (page_stride / 64) + h * (head_stride / 64) + slot. */
+int higgs_qknorm_rope_kv_write_tq4(higgs_ctx* ctx, const void* qkv, int T, int Hq, int Hkv,
+                                   const void* q_norm_w, const void* k_norm_w, float eps,
+                                   const int32_t* positions, const float* inv_freq,
+                                   const int64_t* slot_mapping, const int8_t* signs,
+                                   uint8_t* k_codes, void* k_scales, uint8_t* v_codes,
+                                   void* v_scales, int64_t page_stride, int64_t head_stride,
+                                   void* q_out, void* stream);
+
+/* Decode attention over TurboQuant pages (D = 128), same semantics and
+ * workspace rules as higgs_paged_attention; the query is rotated into the
+ * code basis in-kernel and the output rotated back. */
+size_t higgs_paged_attention_tq4_workspace_size(int B, int Lq, int Hq, int Hkv, int max_seq_len);
+int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq, int Hkv,
+                              const uint8_t* k_codes, const void* k_scales,
+                              const uint8_t* v_codes, const void* v_scales, int64_t page_stride,
+                              int64_t head_stride, const int32_t* block_table, int max_blocks,
+                              const int32_t* seq_lens, int max_seq_len, const int8_t* signs,
+                              float scale, void* out, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
+/* ---- a10/a15: token selection -------------------------------------------- */
+
+/* sample() at temperature 0 (crates/higgs-models/src/lib.rs:373-377):
+ * out[b] = argmax_j logits[b, j], ties -> lowest index (lib.rs:838-843). */
+int higgs_argmax(higgs_ctx* ctx, const float* logits, int B, int V, int32_t* out, void* stream);
+
+/* sample() at temperature > 0 (crates/higgs-models/src/lib.rs:379-384,
+ * categorical(logits / T)): inverse-CDF draw with the caller's uniforms[b]
+ * in [0, 1) over a fixed-point softmax (exact integer prefix sums), so the
+ * token is a deterministic function of (logits, T, u).  T == 0 -> argmax. */
+int higgs_sample(higgs_ctx* ctx, const float* logits, int B, int V, float temperature,
+                 const float* uniforms, int32_t* out, void* stream);
+
+/* Speculative acceptance (no reference counterpart).  target_logits f32
+ * [B, k+1, V], draft_logits f32 [B, k, V], draft_tokens int32 [B, k]:
+ * accept draft i while u_i * q_i(x_i) < p_i(x_i) (p, q the temperature
+ * softmaxes), resample the first rejected position from norm(max(p - q, 0)),
+ * or draw a bonus token from p_k when all k are accepted.  accepted int32 [B];
+ * out_tokens int32 [B, k+1] (accepted drafts, then the corrected / bonus
+ * token, then -1).  temperature 0 = greedy verification. */
+int higgs_spec_accept(higgs_ctx* ctx, const float* target_logits, const float* draft_logits,
+                      const int32_t* draft_tokens, int B, int k, int V, float temperature,
+                      const float* accept_uniforms, const float* sample_uniforms,
+                      int32_t* accepted, int32_t* out_tokens, void* stream);
+
+/* apply_penalties (crates/higgs-models/src/lib.rs:278-363), in place on
+ * logits f32 [B, V]; history int32 [B, max_hist] with hist_lens[b] valid
+ * entries.  rep = 1, freq = 0, pres = 0 disable the respective penalty. */
+int higgs_apply_penalties(higgs_ctx* ctx, float* logits, int B, int V, const int32_t* history,
+                          const int32_t* hist_lens, int max_hist, float rep, float freq,
+                          float pres, void* stream);
+
+/* ---- a7/a11: native decode step (transformer.rs Model) ------------------ */
+
+/* ModelArgs (crates/higgs-models/src/transformer.rs:69-97) reduced to what the
+ * step needs.  qk_norm = 1 for model_type "qwen3" (transformer.rs:193). */
+typedef struct {
+  int hidden, layers, intermediate, heads, kv_heads, head_dim, vocab;
+  float rms_eps, rope_theta;
+  int tie_word_embeddings;
+  int qk_norm;
+  int kv_mode; /* HIGGS_KV_BF16 or HIGGS_KV_TQ4 */
+} higgs_model_config;
+
+/* One forward over B sequences x Lq new tokens (Lq = 1 decode, k+1 verify,
+ * larger for a prefill chunk).  All vectors are device memory:
+ *   tokens, positions int32 [B*Lq]; slot_mapping int64 [B*Lq] (page*16+slot,
+ *   <0 = do not store); block_table int32 [B, max_blocks]; seq_lens int32 [B]
+ *   (cache length after this step).  max_seq_len bounds seq_lens.
+ *   n_layers > 0 runs only the first n_layers (layer-skip draft), 0 = all.
+ *   last_only = 1 applies the LM head to the last token of each sequence only.
+ *   logits f32 [rows, V] and/or argmax int32 [rows] (rows = B or B*Lq);
+ *   hidden_out bf16 [rows, hidden] (optional) receives the final-norm output. */
+typedef struct {
+  int B, Lq;
+  const int32_t* tokens;
+  const int32_t* positions;
+  const int64_t* slot_mapping;
+  const int32_t* block_table;
+  int max_blocks;
+  const int32_t* seq_lens;
+  int max_seq_len;
+  int n_layers;
+  int last_only;
+  float* logits;
+  int32_t* argmax;
+  void* hidden_out;
+  void* workspace;
+  size_t workspace_bytes;
+} higgs_forward_args;
+
+/* Model::new + load_model (crates/higgs-models/src/transformer.rs:552, 922-960).
+ * Tensors are registered by their MLX safetensors names (lib.rs:604-723), e.g.
+ * "model.layers.3.self_attn.q_proj.weight" u32 [N, K/8], "...scales" bf16;
+ * nothing is copied: pointers must stay valid for the model's lifetime. */
+int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg, higgs_model** out);
+int higgs_model_set_tensor(higgs_model* m, const char* name, const void* ptr, int dtype,
+                           const int64_t* shape, int ndim);
+int higgs_model_finalize(higgs_model* m);
+int higgs_model_destroy(higgs_model* m);
+
+/* Paged KV pools for all layers: bf16 [layers, pages, Hkv, 16, D] each; or
+ * TurboQuant codes u8 [layers, pages, Hkv, 16, 64] + fp16 scales
+ * [layers, pages, Hkv, 16] with the Hadamard signs int8 [128].  Replaces the
+ * per-request SteppingKeyValueCache (crates/higgs-models/src/cache.rs:130-312). */
+int higgs_model_set_kv_cache(higgs_model* m, void* k_pool, void* v_pool, int64_t num_pages);
+int higgs_model_set_kv_cache_tq4(higgs_model* m, uint8_t* k_codes, void* k_scales,
+                                 uint8_t* v_codes, void* v_scales, int64_t num_pages,
+                                 const int8_t* signs);
+
+/* Bytes of scratch higgs_model_forward needs for (B, Lq, max_seq_len, last_only). */
+size_t higgs_model_workspace_size(const higgs_model* m, int B, int Lq, int max_seq_len,
+                                  int last_only);
+
+/* AnyModel::forward / forward_batched (crates/higgs-models/src/lib.rs:123,165;
+ * transformer.rs:590-598, 663-827) on the device; enqueues only. */
+int higgs_model_forward(higgs_model* m, const higgs_forward_args* args, void* stream);
+
+/* Capture one higgs_model_forward into a CUDA graph (replaces the per-token
+ * async_eval submission, crates/higgs-engine/src/simple.rs:539-562).  The
+ * graph re-reads the argument vectors on every launch, so updating tokens /
+ * positions / slots / lengths in place and relaunching runs the next step. */
+int higgs_model_capture(higgs_model* m, const higgs_forward_args* args, void* stream,
+                        higgs_graph** out);
+int higgs_graph_launch(higgs_graph* g, void* stream);
+int higgs_graph_destroy(higgs_graph* g);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HIGGS_CUDA_H */

@@ -1,0 +1,72 @@
+"""CPU: the C-ABI library builds/loads and exports every symbol include/*.h declares."""
+import ctypes
+import glob
+import os
+import re
+
+import pytest
+
+from tests.conftest import ROOT
+
+HEADERS = sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))
+LIB = os.path.join(ROOT, "higgs_b200", "libhiggs_cuda.so")
+
+
+def declared_functions():
+    names = set()
+    for h in HEADERS:
+        src = open(h).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"\b(higgs_[a-z0-9_]+)\s*\(", src):
+            names.add(m.group(1))
+    return sorted(names)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(LIB):
+        from higgs_b200 import build
+        build.build()
+    return ctypes.CDLL(LIB)
+
+
+def test_headers_present():
+    assert HEADERS, "no include/*.h"
+    assert len(declared_functions()) >= 20
+
+
+def test_every_declared_symbol_exported(lib):
+    missing = [n for n in declared_functions() if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_ffi_signature_table_matches_header():
+    from higgs_b200 import ffi
+    assert set(ffi.SIGNATURES) == set(declared_functions())
+
+
+def test_no_device_errors_cleanly(lib):
+    """Without a GPU, init fails with a status code and a message; it never aborts."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("GPU present")
+    lib.higgs_init.restype = ctypes.c_int
+    lib.higgs_last_error.restype = ctypes.c_char_p
+    h = ctypes.c_void_p()
+    rc = lib.higgs_init(0, ctypes.byref(h))
+    assert rc < 0
+    assert lib.higgs_last_error().decode()
+
+
+def test_argument_validation_without_device(lib):
+    """Shape checks run before any CUDA call and report HIGGS_ERR_INVALID_ARG (-1)."""
+    lib.higgs_qlinear_w4g64.restype = ctypes.c_int
+    lib.higgs_last_error.restype = ctypes.c_char_p
+    fake = ctypes.c_void_p(16)
+    # K not a multiple of 256
+    rc = lib.higgs_qlinear_w4g64(fake, fake, 1, 100, fake, fake, fake, 16, fake, None, None, None)
+    assert rc == -1
+    assert b"K must be a multiple of 256" in lib.higgs_last_error()
+    # null context
+    rc = lib.higgs_qlinear_w4g64(None, fake, 1, 256, fake, fake, fake, 16, fake, None, None, None)
+    assert rc == -1

@@ -1,0 +1,432 @@
+"""GPU parity: every C-ABI kernel against the CPU oracle on the same seeded inputs.
+
+Bars: bit-exact for integer/byte work (unpack/dequant, embedding rows, cache
+slots, TurboQuant codes, sampled / accepted tokens given uniforms); floating
+point within the stated tolerance (north star: max-abs 2e-2 / rel 1e-2 in bf16;
+the per-op bounds below are tighter).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+def ops():
+    from higgs_b200 import ops as o
+    return o
+
+
+def t(a, dtype=None):
+    x = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        x = x.view(dtype)
+    return x.to(DEV)
+
+
+def bf(a):
+    return t(np.ascontiguousarray(a, dtype=np.uint16), torch.bfloat16)
+
+
+def to_np_bf(x):
+    return x.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def qweights(rng, N, K, sd=0.02):
+    w = rng.normal(0, sd, size=(N, K)).astype(np.float32)
+    return orc.w4_quantize(w)
+
+
+def bf_ulps(a_bits, b_bits):
+    """distance in bf16 ulps between two bf16 bit arrays (sign-magnitude aware)."""
+    def key(x):
+        x = x.astype(np.int32)
+        return np.where(x & 0x8000, -(x & 0x7FFF), x)
+    return np.abs(key(a_bits) - key(b_bits))
+
+
+# ---- a1/a2 --------------------------------------------------------------------
+
+@pytest.mark.parametrize("M,K,N", [(1, 256, 16), (1, 4096, 1024), (3, 2048, 512), (8, 4096, 256),
+                                   (13, 1024, 128), (32, 2048, 64), (40, 512, 96), (1, 12288, 256)])
+def test_qlinear_vs_oracle(M, K, N):
+    rng = np.random.default_rng(M * 1000 + K + N)
+    q, s, b = qweights(rng, N, K)
+    x = orc.f32_to_bf16(rng.normal(0, 1, size=(M, K)))
+    yb_ref, yf_ref = orc.qmatmul(x, q, s, b, want_f32=True)
+    o = ops()
+    yf = o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b), out_f32=True).cpu().numpy()
+    scale = np.abs(yf_ref).max()
+    np.testing.assert_allclose(yf, yf_ref, rtol=1e-3, atol=1e-4 * scale + 1e-6)
+    yb = to_np_bf(o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b)))
+    assert bf_ulps(yb, yb_ref).max() <= 1
+
+
+def test_qlinear_golden(golden):
+    g = golden
+    o = ops()
+    yb = to_np_bf(o.quantized_matmul(bf(g["qm_x"]), t(g["qm_q"].view(np.int32)), bf(g["qm_s"]),
+                                     bf(g["qm_b"])))
+    assert bf_ulps(yb, g["qm_yb"]).max() <= 1
+
+
+def test_qlinear_residual_epilogue():
+    rng = np.random.default_rng(11)
+    M, K, N = 2, 1024, 256
+    q, s, b = qweights(rng, N, K)
+    x = orc.f32_to_bf16(rng.normal(size=(M, K)))
+    r = orc.f32_to_bf16(rng.normal(size=(M, N)))
+    yb_ref = orc.qmatmul(x, q, s, b)
+    ref = orc.f32_to_bf16(orc.bf16_to_f32(yb_ref) + orc.bf16_to_f32(r))
+    got = to_np_bf(ops().quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b), residual=bf(r)))
+    assert bf_ulps(got, ref).max() <= 1
+
+
+@pytest.mark.parametrize("M", [1, 5, 17])
+def test_gate_up_swiglu(M):
+    rng = np.random.default_rng(12 + M)
+    K, N = 2048, 512
+    qg, sg, bg = qweights(rng, N, K)
+    qu, su, bu = qweights(rng, N, K)
+    x = orc.f32_to_bf16(rng.normal(size=(M, K)))
+    ref = orc.silu_mul(orc.qmatmul(x, qg, sg, bg), orc.qmatmul(x, qu, su, bu))
+    got = to_np_bf(ops().gate_up_swiglu(bf(x), t(qg.view(np.int32)), bf(sg), bf(bg),
+                                        t(qu.view(np.int32)), bf(su), bf(bu)))
+    # gate/up are rounded to bf16 before the product: a 1-ulp flip there moves the output by ~2 ulps
+    assert np.percentile(bf_ulps(got, ref), 99) <= 2
+    np.testing.assert_allclose(orc.bf16_to_f32(got), orc.bf16_to_f32(ref), atol=2e-3, rtol=2e-2)
+
+
+def test_dequantize_and_embed_bit_exact():
+    rng = np.random.default_rng(13)
+    V, H = 300, 512
+    q, s, b = qweights(rng, V, H)
+    o = ops()
+    deq = to_np_bf(o.dequantize(t(q.view(np.int32)), bf(s), bf(b)))
+    assert np.array_equal(deq, orc.w4_dequantize(q, s, b))
+    ids = np.array([0, 299, 17, -1, 300, 17], np.int32)
+    got = to_np_bf(o.embed_gather(t(ids), t(q.view(np.int32)), bf(s), bf(b)))
+    assert np.array_equal(got, orc.embed_gather(ids, q, s, b))
+    assert not got[3].any() and not got[4].any()
+
+
+# ---- a3/a4 --------------------------------------------------------------------------
+
+@pytest.mark.parametrize("H", [64, 2048, 4096])
+def test_rmsnorm(H, golden):
+    rng = np.random.default_rng(H)
+    x = orc.f32_to_bf16(rng.normal(size=(3, H)))
+    r = orc.f32_to_bf16(rng.normal(size=(3, H)))
+    w = orc.f32_to_bf16(rng.uniform(0.5, 1.5, size=H))
+    y_ref, h_ref = orc.rmsnorm(x, w, 1e-6, r)
+    y, h = ops().rms_norm(bf(x), bf(w), 1e-6, residual=bf(r), want_h=True)
+    assert np.array_equal(to_np_bf(h), h_ref)
+    assert bf_ulps(to_np_bf(y), y_ref).max() <= 1
+    y2 = ops().rms_norm(bf(x), bf(w), 1e-5)
+    assert bf_ulps(to_np_bf(y2), orc.rmsnorm(x, w, 1e-5)[0]).max() <= 1
+    g = golden
+    yg, hg = ops().rms_norm(bf(g["rn_x"]), bf(g["rn_w"]), 1e-6, residual=bf(g["rn_r"]), want_h=True)
+    assert np.array_equal(to_np_bf(hg), g["rn_h"]) and bf_ulps(to_np_bf(yg), g["rn_y"]).max() <= 1
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_rope(D):
+    rng = np.random.default_rng(D)
+    x = orc.f32_to_bf16(rng.normal(size=(5, 3, D)))
+    pos = np.array([0, 1, 127, 2048, 32767], np.int32)
+    inv = orc.rope_inv_freq(D, 500000.0)
+    ref = orc.rope(x, pos, inv)
+    got = to_np_bf(ops().rope(bf(x), t(pos), t(inv)))
+    assert bf_ulps(got, ref).max() <= 1
+
+
+def _kvwrite_case(rng, T, Hq, Hkv, D, qknorm):
+    nh = Hq + 2 * Hkv
+    qkv = orc.f32_to_bf16(rng.normal(size=(T, nh * D)))
+    qn = orc.f32_to_bf16(rng.uniform(0.5, 1.5, size=D)) if qknorm else None
+    kn = orc.f32_to_bf16(rng.uniform(0.5, 1.5, size=D)) if qknorm else None
+    pos = rng.integers(0, 4000, size=T).astype(np.int32)
+    inv = orc.rope_inv_freq(D, 1000000.0)
+    return qkv, qn, kn, pos, inv
+
+
+def _kvwrite_ref(qkv, qn, kn, pos, inv, T, Hq, Hkv, D):
+    x = qkv.reshape(T, Hq + 2 * Hkv, D)
+    qh, kh, vh = x[:, :Hq], x[:, Hq:Hq + Hkv], x[:, Hq + Hkv:]
+    if qn is not None:
+        qh = orc.rmsnorm(qh.reshape(-1, D), qn, 1e-6)[0].reshape(T, Hq, D)
+        kh = orc.rmsnorm(kh.reshape(-1, D), kn, 1e-6)[0].reshape(T, Hkv, D)
+    return orc.rope(qh, pos, inv), orc.rope(np.ascontiguousarray(kh), pos, inv), vh
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,qknorm", [(32, 8, 64, False), (16, 8, 128, True), (32, 4, 128, True)])
+def test_qknorm_rope_kv_write(Hq, Hkv, D, qknorm):
+    rng = np.random.default_rng(Hq + Hkv + D)
+    T = 5
+    qkv, qn, kn, pos, inv = _kvwrite_case(rng, T, Hq, Hkv, D, qknorm)
+    P = 4
+    sentinel = 0x3F80  # bf16 1.0
+    kc = torch.full((P, Hkv, 16, D), 1.0, dtype=torch.bfloat16, device=DEV)
+    vc = torch.full((P, Hkv, 16, D), 1.0, dtype=torch.bfloat16, device=DEV)
+    slots = np.array([3 * 16 + 0, 0 * 16 + 15, -1, 2 * 16 + 7, 1 * 16 + 1], np.int64)
+    q = ops().qknorm_rope_kv_write(bf(qkv), Hq, Hkv, D, None if qn is None else bf(qn),
+                                   None if kn is None else bf(kn), 1e-6, t(pos), t(inv), t(slots), kc, vc)
+    q_ref, k_ref, v_ref = _kvwrite_ref(qkv, qn, kn, pos, inv, T, Hq, Hkv, D)
+    assert bf_ulps(to_np_bf(q), q_ref).max() <= 1
+    kcn, vcn = to_np_bf(kc), to_np_bf(vc)
+    written = np.zeros((P, 16), bool)
+    for i, sl in enumerate(slots):
+        if sl < 0:
+            continue
+        p, s = sl // 16, sl % 16
+        written[p, s] = True
+        assert bf_ulps(kcn[p, :, s], k_ref[i]).max() <= 1
+        assert np.array_equal(vcn[p, :, s], v_ref[i])
+    kt_, vt_ = kcn.transpose(0, 2, 1, 3), vcn.transpose(0, 2, 1, 3)  # [P, 16, Hkv, D]
+    assert np.all(kt_[~written] == sentinel) and np.all(vt_[~written] == sentinel)
+
+
+# ---- a6/a13: paged attention ---------------------------------------------------------------
+
+def _paged_case(rng, B, Lq, Hq, Hkv, D, lens, shuffle=True):
+    maxb = max((l + 15) // 16 for l in lens)
+    P = B * maxb + 3
+    kc = orc.f32_to_bf16(rng.normal(size=(P, Hkv, 16, D)))
+    vc = orc.f32_to_bf16(rng.normal(size=(P, Hkv, 16, D)))
+    perm = rng.permutation(P) if shuffle else np.arange(P)
+    bt = perm[:B * maxb].reshape(B, maxb).astype(np.int32)
+    q = orc.f32_to_bf16(rng.normal(size=(B, Lq, Hq, D)))
+    return q, kc, vc, bt, np.array(lens, np.int32)
+
+
+@pytest.mark.parametrize("B,Lq,Hq,Hkv,D,lens", [
+    (1, 1, 32, 8, 128, [1]),
+    (1, 1, 32, 8, 128, [2048]),
+    (2, 1, 16, 8, 128, [37, 512]),
+    (3, 1, 32, 8, 64, [130, 7, 16]),
+    (4, 6, 32, 8, 128, [300, 1000, 64, 6]),
+    (2, 1, 32, 4, 128, [4096, 100]),
+    (1, 6, 32, 4, 128, [257]),
+    (2, 2, 8, 8, 64, [3, 33]),
+])
+def test_paged_attention(B, Lq, Hq, Hkv, D, lens):
+    rng = np.random.default_rng(B * 7 + Lq + D + sum(lens))
+    q, kc, vc, bt, sl = _paged_case(rng, B, Lq, Hq, Hkv, D, lens)
+    ref = orc.bf16_to_f32(orc.paged_attention(q, kc, vc, bt, sl))
+    got = ops().paged_attention(bf(q), bf(kc), bf(vc), t(bt), t(sl), max(lens))
+    got = orc.bf16_to_f32(to_np_bf(got))
+    np.testing.assert_allclose(got, ref, atol=1e-2, rtol=1e-2)
+    # a second call reuses the workspace counters (they must be left at zero)
+    ws = ops().attention_workspace(B, Lq, Hq, Hkv, D, max(lens), DEV)
+    o = ops()
+    a1 = to_np_bf(o.paged_attention(bf(q), bf(kc), bf(vc), t(bt), t(sl), max(lens), workspace=ws))
+    a2 = to_np_bf(o.paged_attention(bf(q), bf(kc), bf(vc), t(bt), t(sl), max(lens), workspace=ws))
+    assert np.array_equal(a1, a2)
+
+
+def test_paged_attention_golden(golden):
+    g = golden
+    got = ops().paged_attention(bf(g["at_q"]), bf(g["at_k"]), bf(g["at_v"]), t(g["at_bt"]),
+                                t(g["at_sl"]), int(g["at_sl"].max()))
+    np.testing.assert_allclose(orc.bf16_to_f32(to_np_bf(got)), orc.bf16_to_f32(g["at_out"]),
+                               atol=1e-2, rtol=1e-2)
+
+
+def test_contiguous_layout_strides():
+    """A contiguous [B, Hkv, S_cap, D] cache (cache.rs:130-312) through page/head strides."""
+    rng = np.random.default_rng(21)
+    B, Hkv, Hq, D, S_cap = 2, 2, 8, 64, 256
+    lens = [100, 256]
+    k = orc.f32_to_bf16(rng.normal(size=(B, Hkv, S_cap, D)))
+    v = orc.f32_to_bf16(rng.normal(size=(B, Hkv, S_cap, D)))
+    q = orc.f32_to_bf16(rng.normal(size=(B, 1, Hq, D)))
+    nb = S_cap // 16
+    bt = np.array([[b * Hkv * nb + i for i in range(nb)] for b in range(B)], np.int32)
+    # reference through explicit pages
+    kp = k.reshape(B, Hkv, nb, 16, D).transpose(0, 2, 1, 3, 4).reshape(B * nb, Hkv, 16, D)
+    vp = v.reshape(B, Hkv, nb, 16, D).transpose(0, 2, 1, 3, 4).reshape(B * nb, Hkv, 16, D)
+    btp = np.arange(B * nb, dtype=np.int32).reshape(B, nb)
+    ref = orc.bf16_to_f32(orc.paged_attention(q, kp, vp, btp, np.array(lens, np.int32)))
+    o = ops()
+    ws = o.attention_workspace(B, 1, Hq, Hkv, D, S_cap, DEV)
+    out = torch.empty(B, 1, Hq, D, dtype=torch.bfloat16, device=DEV)
+    from higgs_b200 import ffi
+    qt, kt, vt = bf(q), bf(k), bf(v)
+    btt, slt = t(bt), t(np.array(lens, np.int32))
+    ffi.call("higgs_paged_attention", ffi.ctx(0), qt.data_ptr(), B, 1, Hq, Hkv, D, kt.data_ptr(),
+             vt.data_ptr(), 16 * D, S_cap * D, btt.data_ptr(), nb, slt.data_ptr(), S_cap,
+             float(1 / np.sqrt(D)), out.data_ptr(), ws.data_ptr(), ws.numel(),
+             torch.cuda.current_stream().cuda_stream)
+    np.testing.assert_allclose(orc.bf16_to_f32(to_np_bf(out)), ref, atol=1e-2, rtol=1e-2)
+
+
+def test_cache_append_values_preserved(kat):
+    """cache.rs:469-493 on the device: append 2 ones then 1 two, read back 1,1,2."""
+    case = kat["cache_values_preserved"][0]
+    D = 64
+    kc = torch.zeros(1, 1, 16, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    inv = t(orc.rope_inv_freq(D, 10000.0))
+    o = ops()
+    pos0 = 0
+    for app in case["appends"]:
+        n = len(app)
+        rows = np.zeros((n, 3 * D), np.float32)
+        for i in range(n):
+            rows[i, 2 * D:2 * D + 4] = app[i]  # the V head (no RoPE) carries the values
+        o.qknorm_rope_kv_write(bf(orc.f32_to_bf16(rows)), 1, 1, D, None, None, 1e-6,
+                               t(np.arange(pos0, pos0 + n, dtype=np.int32)), inv,
+                               t(np.arange(pos0, pos0 + n, dtype=np.int64)), kc, vc)
+        pos0 += n
+    first = vc[0, 0, :pos0, 0].float().cpu().numpy()
+    assert first.tolist() == case["expect_first"]
+
+
+# ---- a14: TurboQuant ---------------------------------------------------------------------
+
+def test_tq4_encode_bit_exact(golden):
+    g = golden
+    codes, scales = ops().tq4_encode(bf(g["tq_x"]), t(g["tq_signs"]))
+    assert np.array_equal(codes.cpu().numpy(), g["tq_codes"])
+    assert np.array_equal(scales.cpu().numpy().view(np.uint16), g["tq_scales"].view(np.uint16))
+    rng = np.random.default_rng(31)
+    signs = np.where(rng.random(128) < 0.5, -1, 1).astype(np.int8)
+    x = orc.f32_to_bf16(np.concatenate([rng.normal(0, 1, size=(500, 128)),
+                                        rng.normal(0, 300, size=(20, 128)),
+                                        rng.normal(0, 1e-3, size=(20, 128))]))
+    c_ref, s_ref = orc.tq4_encode(x, signs)
+    c, s = ops().tq4_encode(bf(x), t(signs))
+    assert np.array_equal(c.cpu().numpy(), c_ref)
+    assert np.array_equal(s.cpu().numpy().view(np.uint16), s_ref.view(np.uint16))
+
+
+def test_tq4_kv_write_bit_exact():
+    rng = np.random.default_rng(32)
+    T, Hq, Hkv, D = 4, 16, 8, 128
+    qkv, qn, kn, pos, inv = _kvwrite_case(rng, T, Hq, Hkv, D, True)
+    signs = np.where(rng.random(128) < 0.5, -1, 1).astype(np.int8)
+    P = 3
+    kcode = torch.zeros(P, Hkv, 16, 64, dtype=torch.uint8, device=DEV)
+    vcode = torch.zeros_like(kcode)
+    ksc = torch.zeros(P, Hkv, 16, dtype=torch.float16, device=DEV)
+    vsc = torch.zeros_like(ksc)
+    slots = np.array([5, 16 + 3, 2 * 16 + 15, 0], np.int64)
+    o = ops()
+    q = o.qknorm_rope_kv_write_tq4(bf(qkv), Hq, Hkv, bf(qn), bf(kn), 1e-6, t(pos), t(inv), t(slots),
+                                   t(signs), kcode, ksc, vcode, vsc)
+    # the K that was encoded: same device code path, bf16 cache
+    kc = torch.zeros(P, Hkv, 16, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    q2 = o.qknorm_rope_kv_write(bf(qkv), Hq, Hkv, D, bf(qn), bf(kn), 1e-6, t(pos), t(inv), t(slots), kc, vc)
+    assert torch.equal(q, q2)
+    kcn, vcn = to_np_bf(kc), to_np_bf(vc)
+    for i, sl in enumerate(slots):
+        p, s = sl // 16, sl % 16
+        ck, sk = orc.tq4_encode(kcn[p, :, s], signs)
+        cv, sv = orc.tq4_encode(vcn[p, :, s], signs)
+        assert np.array_equal(kcode[p, :, s].cpu().numpy(), ck)
+        assert np.array_equal(vcode[p, :, s].cpu().numpy(), cv)
+        assert np.array_equal(ksc[p, :, s].cpu().numpy().view(np.uint16), sk.view(np.uint16))
+        assert np.array_equal(vsc[p, :, s].cpu().numpy().view(np.uint16), sv.view(np.uint16))
+
+
+@pytest.mark.parametrize("B,Lq,Hq,Hkv,lens", [(1, 1, 32, 8, [1]), (2, 1, 32, 8, [2048, 77]),
+                                             (3, 1, 16, 8, [16, 500, 33]), (2, 6, 32, 8, [300, 64]),
+                                             (1, 1, 32, 4, [4096])])
+def test_paged_attention_tq4(B, Lq, Hq, Hkv, lens):
+    rng = np.random.default_rng(B + Lq + Hq + sum(lens))
+    signs = np.where(rng.random(128) < 0.5, -1, 1).astype(np.int8)
+    maxb = max((l + 15) // 16 for l in lens)
+    P = B * maxb + 2
+    kx = orc.f32_to_bf16(rng.normal(size=(P * Hkv * 16, 128)))
+    vx = orc.f32_to_bf16(rng.normal(size=(P * Hkv * 16, 128)))
+    kcode, ksc = orc.tq4_encode(kx, signs)
+    vcode, vsc = orc.tq4_encode(vx, signs)
+    kcode, vcode = kcode.reshape(P, Hkv, 16, 64), vcode.reshape(P, Hkv, 16, 64)
+    ksc, vsc = ksc.reshape(P, Hkv, 16), vsc.reshape(P, Hkv, 16)
+    bt = rng.permutation(P)[:B * maxb].reshape(B, maxb).astype(np.int32)
+    q = orc.f32_to_bf16(rng.normal(size=(B, Lq, Hq, 128)))
+    sl = np.array(lens, np.int32)
+    ref = orc.bf16_to_f32(orc.paged_attention_tq4(q, kcode, ksc, vcode, vsc, bt, sl, signs))
+    got = ops().paged_attention_tq4(bf(q), t(kcode), t(ksc), t(vcode), t(vsc), t(bt), t(sl),
+                                    max(lens), t(signs))
+    got = orc.bf16_to_f32(to_np_bf(got))
+    np.testing.assert_allclose(got, ref, atol=1.5e-2, rtol=1e-2)
+
+
+# ---- a10/a15 ----------------------------------------------------------------------------------
+
+def test_argmax(kat):
+    o = ops()
+    for case in kat["argmax"]:
+        got = o.argmax(t(np.array(case["logits"], np.float32))).cpu().numpy()
+        assert got.tolist() == case["expect"], case["src"]
+    rng = np.random.default_rng(41)
+    lg = rng.normal(size=(4, 151936)).astype(np.float32)
+    lg[2, 100] = lg[2, 5000] = lg[2].max() + 1.0  # tie -> first
+    assert np.array_equal(o.argmax(t(lg)).cpu().numpy(), orc.argmax(lg))
+
+
+def test_sample_bit_exact(golden):
+    g = golden
+    o = ops()
+    got = o.sample(t(g["sm_logits"]), 0.7, t(g["sm_u"])).cpu().numpy()
+    assert np.array_equal(got, g["sm_t07"])
+    assert np.array_equal(o.sample(t(g["sm_logits"]), 0.0).cpu().numpy(), g["sm_t0"])
+    rng = np.random.default_rng(42)
+    lg = rng.normal(0, 1, size=(8, 151936)).astype(np.float32)
+    u = rng.random(8).astype(np.float32)
+    u[0] = 0.0
+    u[1] = np.float32(0.99999994)
+    for T in (0.7, 1.0, 0.05):
+        assert np.array_equal(o.sample(t(lg), T, t(u)).cpu().numpy(), orc.sample(lg, T, u))
+
+
+@pytest.mark.parametrize("T", [0.7, 0.0, 1.3])
+def test_spec_accept_bit_exact(T, golden):
+    o = ops()
+    if T == 0.7:
+        g = golden
+        acc, toks = o.spec_accept(t(g["sa_tl"]), t(g["sa_dl"]), t(g["sa_dt"]), 0.7, t(g["sa_au"]),
+                                  t(g["sa_su"]))
+        assert np.array_equal(acc.cpu().numpy(), g["sa_acc"])
+        assert np.array_equal(toks.cpu().numpy(), g["sa_toks"])
+    rng = np.random.default_rng(int(T * 10) + 43)
+    B, k, V = 4, 5, 151936
+    tl = rng.normal(0, 1, size=(B, k + 1, V)).astype(np.float32)
+    dl = (tl[:, :k] + rng.normal(0, 0.5, size=(B, k, V))).astype(np.float32)
+    # drafts drawn from the draft distribution itself (the realistic case)
+    dt = np.stack([orc.sample(dl[:, i], max(T, 0.7), rng.random(B).astype(np.float32))
+                   for i in range(k)], axis=1).astype(np.int32)
+    if T == 0.0:
+        dt[:2] = np.argmax(tl[:2, :k], axis=-1)
+    au = rng.random((B, k)).astype(np.float32)
+    su = rng.random(B).astype(np.float32)
+    acc_ref, toks_ref = orc.spec_accept(tl, dl, dt, T, au, su)
+    acc, toks = o.spec_accept(t(tl), t(dl), t(dt), T, t(au), t(su))
+    assert np.array_equal(acc.cpu().numpy(), acc_ref)
+    assert np.array_equal(toks.cpu().numpy(), toks_ref)
+
+
+def test_penalties(kat):
+    o = ops()
+    for case in kat["penalties"]:
+        lg = t(np.array([case["logits"]], np.float32))
+        hist = t(np.array([case["history"]], np.int32))
+        lens = t(np.array([len(case["history"])], np.int32))
+        o.apply_penalties(lg, hist, lens, case["rep"], case["freq"], case["pres"])
+        np.testing.assert_allclose(lg.cpu().numpy()[0], case["expect"], atol=1e-5, err_msg=case["src"])
+    rng = np.random.default_rng(44)
+    V = 1000
+    lg = rng.normal(size=(2, V)).astype(np.float32)
+    hist = rng.integers(0, V, size=(2, 64)).astype(np.int32)
+    lens = np.array([64, 10], np.int32)
+    lt = t(lg.copy())
+    o.apply_penalties(lt, t(hist), t(lens), 1.3, 0.2, 0.5)
+    for bidx in range(2):
+        ref = orc.apply_penalties(lg[bidx], hist[bidx, :lens[bidx]], 1.3, 0.2, 0.5)
+        np.testing.assert_array_equal(lt.cpu().numpy()[bidx], ref)
