@@ -1,0 +1,458 @@
+"""Decode throughput of the B200 hot path (4-bit Qwen3-8B architecture).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One "step" = one greedy decode step (all 36 layers + LM head + argmax) for a
+batch of B sequences at a synthetic KV context (default 2048 tokens).  The
+headline `value` is decode tok/s at B=1 on one GPU with every input resident in
+HBM; B=8 and B=32 are reported under `by_batch`.  `e2e` is the same metric
+through the public engine API with per-step host->device inputs and a
+device->host read of the sampled tokens inside the timed region.
+
+Weights are random-init N(0, 0.02) quantized to MLX-affine W4 g64 (no
+checkpoint available offline); the KV context is synthetic random bf16 (decode
+cost does not depend on the values).  Weights (4.26 GB/step) exceed L2, so
+every step streams them from HBM.
+
+With N > 1 (torchrun), each rank runs an independent replica over its own
+sequences (weak scaling); `value` sums tokens over ranks / max time over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+MODEL = "qwen3-8b"
+CTX = 2048
+BATCHES = (1, 8, 32)
+METRIC = "decode tok/s at B=1/8/32 (4-bit Qwen3-8B arch) @1/2/4/8 GPU; % HBM roofline"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ctx", type=int, default=CTX)
+    ap.add_argument("--batches", default=",".join(map(str, BATCHES)))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--quick", action="store_true", help="headline B only, no kernel table (profiling)")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------------------------
+def dist_setup():
+    import torch
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return ws, rank, local
+
+
+def allmax(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+    if not (dist.is_available() and dist.is_initialized()):
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier():
+    import torch
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------------------------
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 8:
+                self.samples.append(parts)
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[4 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+def setup_model(args_m, batches, ctx, total_steps, device):
+    import torch
+
+    from higgs_b200.engine import Engine, Sequence
+    from higgs_b200.model import Model, synth_weights_device
+
+    weights = synth_weights_device(args_m, seed=0, device=device)
+    per_seq_pages = math.ceil((ctx + total_steps + 2) / 16)
+    num_pages = max(batches) * per_seq_pages + 16
+    model = Model(args_m, weights, num_pages=num_pages, device=device)
+    # synthetic KV context (random bf16; decode cost does not depend on the values)
+    g = torch.Generator(device=device)
+    g.manual_seed(2)
+    for pool in (model.k_pool, model.v_pool):
+        for li in range(pool.shape[0]):
+            pool[li].copy_(torch.randn(pool[li].shape, generator=g, device=device).to(torch.bfloat16))
+    eng = Engine(model, max_seq_len=ctx + total_steps + 2, prefix_entries=0)
+    return model, eng, Sequence
+
+
+def make_seqs(eng, Sequence, B, ctx, vocab, seed=1):
+    rng = np.random.default_rng(seed)
+    seqs = []
+    for _ in range(B):
+        s = Sequence(prompt=np.zeros(0, np.int32))
+        s.pages = eng.pool.alloc(math.ceil((ctx + 1) / 16)).tolist()
+        s.length = ctx
+        s.last_token = int(rng.integers(0, vocab))
+        seqs.append(s)
+    return seqs
+
+
+def time_device_resident(eng, seqs, steps, warmup):
+    """Graph replays with all per-step inputs pre-staged in HBM; CUDA events on the stream."""
+    import torch
+    B = len(seqs)
+    g = eng._graph_for(B)
+    total = warmup + steps
+    for s in seqs:  # pages for every position the replays will write
+        eng._ensure_pages(s, s.length + total + 1)
+    # stage step 0 through the public path, then precompute every step's vectors on device
+    eng.stage_step(seqs, g, first=True)
+    host = np.zeros((total, 4 * B), np.int32)
+    for k in range(total):
+        for i, s in enumerate(seqs):
+            L = s.length + k
+            host[k, i] = L
+            host[k, B + i] = L + 1
+        slots = np.array([s.pages[(s.length + k) // 16] * 16 + (s.length + k) % 16 for s in seqs], np.int64)
+        host[k, 2 * B:] = slots.view(np.int32)
+    staged = torch.from_numpy(host).to(g.step_dev.device)
+    stream = torch.cuda.current_stream()
+    for k in range(warmup):
+        g.step_dev.copy_(staged[k], non_blocking=True)
+        g.run()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for k in range(warmup, total):
+        g.step_dev.copy_(staged[k], non_blocking=True)
+        g.run()
+    e1.record(stream)
+    e1.synchronize()
+    barrier()
+    ms = e0.elapsed_time(e1)
+    for s in seqs:  # the replays wrote KV at these positions
+        s.length += total
+    return ms, g.graph.num_kernels if g.graph is not None else None
+
+
+def time_e2e(eng, seqs, steps, warmup):
+    """Public API: Engine.decode_steps stages inputs from the host each step and reads the tokens back."""
+    import torch
+    eng.decode_steps(seqs, warmup)
+    barrier()
+    t0 = time.perf_counter()
+    eng.decode_steps(seqs, steps)
+    torch.cuda.synchronize()
+    t1 = time.perf_counter()
+    barrier()
+    return (t1 - t0) * 1e3
+
+
+def gemv_table(model, steps=20):
+    """Each W4 GEMV shape of one decode step timed alone (CUDA events, L2 flushed between)."""
+    import torch
+
+    from higgs_b200 import ops
+    a = model.args
+    H, D = a.hidden_size, a.head_dim
+    w = model.weights
+    p = "model.layers.0."
+    shapes = [
+        ("qkv", [p + "self_attn.q_proj", p + "self_attn.k_proj", p + "self_attn.v_proj"], H, a.num_hidden_layers),
+        ("o_proj", [p + "self_attn.o_proj"], a.num_attention_heads * D, a.num_hidden_layers),
+        ("gate_up_swiglu", [p + "mlp.gate_proj", p + "mlp.up_proj"], H, a.num_hidden_layers),
+        ("down", [p + "mlp.down_proj"], a.intermediate_size, a.num_hidden_layers),
+        ("lm_head", ["model.embed_tokens" if a.tie_word_embeddings else "lm_head"], H, 1),
+    ]
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=model.device)  # 256 MB > L2
+    rows = []
+    for name, tensors, K, count in shapes:
+        ws = [(w[t + ".weight"], w[t + ".scales"], w[t + ".biases"]) for t in tensors]
+        x = torch.randn(1, K, device=model.device).to(torch.bfloat16)
+        nbytes = sum(q.numel() * 4 + s.numel() * 2 + b.numel() * 2 for q, s, b in ws) + K * 2
+        if name == "gate_up_swiglu":
+            fn = lambda: ops.gate_up_swiglu(x, *ws[0], *ws[1])  # noqa: E731
+            nbytes += ws[0][0].shape[0] * 2
+        elif name == "qkv":
+            wq = [torch.cat([t[i] for t in ws]) for i in range(3)]
+            fn = lambda: ops.quantized_matmul(x, *wq)  # noqa: E731
+            nbytes += wq[0].shape[0] * 2
+        else:
+            fn = lambda: ops.quantized_matmul(x, *ws[0], out_f32=(name == "lm_head"))  # noqa: E731
+            nbytes += ws[0][0].shape[0] * (4 if name == "lm_head" else 2)
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        us = statistics.median(ts) * 1e3
+        rows.append({"shape": name, "launches_per_step": count, "bytes": int(nbytes), "us": round(us, 2),
+                     "gbs": round(nbytes / us / 1e3, 1)})
+    return rows
+
+
+def oracle_step_time(model_args, ctx, budget_s=20.0):
+    """Seconds per B=1 decode step of the full model through the oracle port on the host.
+
+    Timed at true shapes on 2- and 6-layer slices (embedding, final norm, LM head and
+    KV context included) and extrapolated linearly to all layers, since every layer
+    costs the same.  Packed weights are random codes / scales: the oracle's cost does
+    not depend on the values.  Returns (seconds_per_step, sample description)."""
+    import dataclasses
+
+    from oracle import oracle as orc
+    from oracle.model_ref import RefModel
+    from higgs_b200.model import tensor_specs
+    rng = np.random.default_rng(5)
+
+    def packed(shape):
+        N, K = shape
+        return (rng.integers(0, 2**32, size=(N, K // 8), dtype=np.uint64).astype(np.uint32),
+                orc.f32_to_bf16(rng.uniform(1e-3, 3e-3, size=(N, K // 64))),
+                orc.f32_to_bf16(rng.uniform(-0.02, 0, size=(N, K // 64))))
+
+    def build(L):
+        a = dataclasses.replace(model_args, num_hidden_layers=L)
+        w = {}
+        for name, kind, shape in tensor_specs(a):
+            if kind == "norm":
+                w[name] = np.full(shape, 0x3F80, np.uint16)
+            else:
+                w[name + ".weight"], w[name + ".scales"], w[name + ".biases"] = packed(shape)
+        ref = RefModel(a, w)
+        cache = ref.new_cache()
+        Hkv, D = a.num_key_value_heads, a.head_dim
+        for li in range(L):
+            cache[li] = [orc.f32_to_bf16(rng.normal(size=(ctx, Hkv, D))),
+                         orc.f32_to_bf16(rng.normal(size=(ctx, Hkv, D)))]
+        return ref, cache
+
+    times = {}
+    reps = {}
+    for L in (2, 6):
+        ref, cache = build(L)
+        tok = np.array([[7]], np.int32)
+        ref.forward(tok, [cache])  # warm
+        n, t0 = 0, time.perf_counter()
+        while n < 3 and (n == 0 or time.perf_counter() - t0 < budget_s / 4):
+            lg = ref.forward(tok, [cache])
+            tok = orc.argmax(lg[:, -1]).reshape(1, 1).astype(np.int32)
+            n += 1
+        times[L] = (time.perf_counter() - t0) / n
+        reps[L] = n
+        del ref, cache
+    per_layer = max(0.0, (times[6] - times[2]) / 4)
+    full = times[2] + (model_args.num_hidden_layers - 2) * per_layer
+    desc = (f"oracle port, B=1 decode at ctx {ctx}: {reps[2]} steps of a 2-layer and {reps[6]} of a "
+            f"6-layer slice at true shapes, extrapolated to {model_args.num_hidden_layers} layers")
+    return full, desc
+
+
+def run_ours(opt):
+    import torch
+
+    from higgs_b200.model import PRESETS
+    ws, rank, local = dist_setup()
+    device = f"cuda:{local}"
+    torch.cuda.set_device(local)
+    a = PRESETS[MODEL]
+    batches = [int(b) for b in opt.batches.split(",")]
+    if opt.quick:
+        batches = batches[:1]
+    total_steps = 2 * (opt.steps + opt.warmup) + 4
+    model, eng, Sequence = setup_model(a, batches, opt.ctx, total_steps, device)
+    hbm, peak_kind = peaks()
+    w_bytes = a.weight_bytes_per_step()
+    by_batch = {}
+    gpu_launches = None
+    clocks = None
+    for B in batches:
+        seqs = make_seqs(eng, Sequence, B, opt.ctx, a.vocab_size, seed=1 + rank)
+        with ClockSampler(local) as cs:
+            ms, nk = time_device_resident(eng, seqs, opt.steps, opt.warmup)
+        ms = allmax(ms)
+        # KV bytes read per step: every sequence's context (average over the timed steps)
+        kv_bytes = B * (opt.ctx + opt.warmup + opt.steps // 2) * a.kv_bytes_per_token()
+        step_ms = ms / opt.steps
+        tok_s = ws * B * opt.steps / (ms / 1e3)
+        by_batch[str(B)] = {"tok_s": round(tok_s, 1), "ms_per_step": round(step_ms, 4),
+                            "step_bytes": int(w_bytes + kv_bytes),
+                            "step_hbm_frac": round((w_bytes + kv_bytes) / (step_ms / 1e3) / 1e9 / hbm, 4)}
+        if B == batches[0]:
+            clocks = cs.summary()
+            gpu_launches = nk * opt.steps if nk else None
+            head = (B, ms, step_ms, tok_s, seqs)
+        for s in seqs:
+            eng.release(s)
+    B, ms, step_ms, tok_s, _ = head
+    # e2e through the public API at the headline batch
+    seqs = make_seqs(eng, Sequence, B, opt.ctx, a.vocab_size, seed=11 + rank)
+    e2e_ms = allmax(time_e2e(eng, seqs, opt.steps, opt.warmup))
+    for s in seqs:
+        eng.release(s)
+    e2e_tok_s = ws * B * opt.steps / (e2e_ms / 1e3)
+    out = {
+        "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": ws,
+        "steps": opt.steps, "warmup": opt.warmup, "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "w4a16 (u4 weights, bf16 act, f32 acc)",
+        "data": "synthetic: random-init N(0,0.02) W4 g64 weights, random KV context, uniform token ids",
+        "config": {"workload": f"{MODEL} decode B={B} ctx={opt.ctx}", "model": MODEL, "global_batch": B * ws,
+                   "seq_len": opt.ctx, "parallelism": f"replicas x{ws}" if ws > 1 else "single GPU",
+                   "l2": "weights 4.26 GB/step > 126 MB L2 (no flush needed)"},
+        "by_batch": by_batch,
+        "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 16 * B,
+                "d2h_bytes_per_step": 4 * B},
+        "gpu_launches": gpu_launches, "clocks": clocks,
+    }
+    if rank == 0 and not opt.quick:
+        rows = gemv_table(model)
+        tot_bytes = sum(r["bytes"] * r["launches_per_step"] for r in rows)
+        tot_us = sum(r["us"] * r["launches_per_step"] for r in rows)
+        achieved = tot_bytes / tot_us / 1e3
+        out["roofline"] = {"kernel": "qlinear_w4_kernel (all W4 GEMV shapes of one B=1 step, byte-weighted)",
+                           "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                           "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                           "traffic": None, "per_shape": rows}
+        sb = by_batch[str(B)]["step_bytes"]
+        out["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": round(sb / (step_ms / 1e3) / 1e9, 1),
+                                "peak": hbm, "frac": by_batch[str(B)]["step_hbm_frac"]}
+    if rank == 0 and ws == 1 and not opt.no_cpu_baseline and not opt.quick:
+        sec, desc = oracle_step_time(a, opt.ctx)
+        out["cpu_baseline"] = {"value": round(1.0 / sec, 4), "unit": "tok/s", "cores": os.cpu_count(),
+                               "kind": "port", "sample": desc}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------------------------
+# reference arm: the reference path's arithmetic restated on the host (oracle port)
+# ---------------------------------------------------------------------------------------------
+def run_reference(opt):
+    """The reference path restated on the host (oracle port), all host threads, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from higgs_b200.model import PRESETS
+    a = PRESETS[MODEL]
+    sec, desc = oracle_step_time(a, opt.ctx)
+    v = 1.0 / sec
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": 0,
+           "steps": opt.steps, "warmup": opt.warmup, "ms_per_step": round(sec * 1e3, 2),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "w4a16 (u4 weights, bf16 act, f32 acc)",
+           "data": "synthetic packed W4 weights and random KV context",
+           "config": {"workload": f"{MODEL} decode B=1 ctx={opt.ctx}", "model": MODEL, "global_batch": 1,
+                      "seq_len": opt.ctx, "parallelism": "host cores"},
+           "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                            "sample": desc + "; the reference's own mlx-rs CPU backend cannot be built here "
+                                             "(no Rust toolchain, MLX not vendored)"},
+           "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    opt = parse()
+    if opt.impl == "reference":
+        run_reference(opt)
+    else:
+        run_ours(opt)
+
+
+if __name__ == "__main__":
+    main()

@@ -305,16 +305,22 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_bf16_kernel(AttnArgs 
         o[mt][dt][2] *= alpha[1];
         o[mt][dt][3] *= alpha[1];
       }
-      const uint32_t pa0 = pack_bf2(s[0][0], s[0][1]), pa1 = pack_bf2(s[0][2], s[0][3]);
-      const uint32_t pa2 = pack_bf2(s[1][0], s[1][1]), pa3 = pack_bf2(s[1][2], s[1][3]);
+      // P as hi + lo bf16 pairs: the two MMAs carry ~16 mantissa bits of P
+      uint32_t ph[4], pl[4];
+      split_bf2(s[0][0], s[0][1], ph[0], pl[0]);
+      split_bf2(s[0][2], s[0][3], ph[1], pl[1]);
+      split_bf2(s[1][0], s[1][1], ph[2], pl[2]);
+      split_bf2(s[1][2], s[1][3], ph[3], pl[3]);
 #pragma unroll
       for (int d2 = 0; d2 < D / 16; ++d2) {
         uint32_t vb[4];
         const int mi = lane >> 3;
         const int tok = (mi & 1) * 8 + (lane & 7);
         ldmatrix_x4_trans(vb, Vs + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
-        mma_bf16_16816(o[mt][2 * d2], pa0, pa1, pa2, pa3, vb[0], vb[1]);
-        mma_bf16_16816(o[mt][2 * d2 + 1], pa0, pa1, pa2, pa3, vb[2], vb[3]);
+        mma_bf16_16816(o[mt][2 * d2], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
+        mma_bf16_16816(o[mt][2 * d2], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
       }
     }
     __syncwarp();
@@ -431,13 +437,13 @@ template <int MT>
 __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a) {
   constexpr int D = 128;
   constexpr int RP = 16 * MT;
-  // smem: qfrag [MT][8 kt][32 lanes][4] u32 | qsum [RP] f32 |
+  // smem: qfrag [MT][8 kt][32 lanes][hi 4 | lo 4] u32 | qsum [RP] f32 |
   //       per warp 2 stages x {kcodes 1 KB, vcodes 1 KB, kscale 32 B, vscale 32 B, vtile bf16 4 KB}
   constexpr int STAGE_BYTES = 1024 + 1024 + 32 + 32;
   constexpr int WARP_BYTES = 2 * STAGE_BYTES + 16 * D * 2;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem_raw);
-  float* qsum = reinterpret_cast<float*>(qfrag + MT * 8 * 32 * 4);
+  float* qsum = reinterpret_cast<float*>(qfrag + MT * 8 * 32 * 8);
   float* qrot = qsum + RP;  // [RP][128] f32 scratch, reused as per-warp buffers later
   uint8_t* wbase = reinterpret_cast<uint8_t*>(qrot);
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -465,10 +471,12 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
       f[3] = bf2f(qp[65 + 2 * lane]);
       tq_rotate_lane(f, a.signs, lane);
     }
+    // q' goes to the MMA as hi + lo bf16; the offset correction uses their exact sum
     float sum = 0.0f;
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      f[e] = round_bf(f[e]);
+      const float hi = round_bf(f[e]);
+      f[e] = hi + round_bf(f[e] - hi);
       sum += f[e];
     }
     sum = warp_sum(sum);
@@ -488,11 +496,11 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
     const int lo = 32 * tt + 8 * (kt >> 1) + 2 * (kt & 1);
     const float* r0 = qrot + (mt * 16 + gg) * D;
     const float* r1 = qrot + (mt * 16 + gg + 8) * D;
-    uint32_t* dst = qfrag + (size_t)i * 4;
-    dst[0] = pack_bf2(r0[lo], r0[lo + 4]);
-    dst[1] = pack_bf2(r1[lo], r1[lo + 4]);
-    dst[2] = pack_bf2(r0[lo + 1], r0[lo + 5]);
-    dst[3] = pack_bf2(r1[lo + 1], r1[lo + 5]);
+    uint32_t* dst = qfrag + (size_t)i * 8;
+    split_bf2(r0[lo], r0[lo + 4], dst[0], dst[4]);
+    split_bf2(r1[lo], r1[lo + 4], dst[1], dst[5]);
+    split_bf2(r0[lo + 1], r0[lo + 5], dst[2], dst[6]);
+    split_bf2(r1[lo + 1], r1[lo + 5], dst[3], dst[7]);
   }
   __syncthreads();
 
@@ -608,11 +616,13 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
         const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
         for (int kt = 0; kt < 8; ++kt) {
-          const uint4 qa = *reinterpret_cast<const uint4*>(qfrag + ((mt * 8 + kt) * 32 + lane) * 4);
+          const uint4* qp = reinterpret_cast<const uint4*>(qfrag + ((mt * 8 + kt) * 32 + lane) * 8);
+          const uint4 qa = qp[0], ql = qp[1];
           const uint32_t w = kws[kt >> 1];
           const uint32_t b0 = (kt & 1) ? nib_pair_bf16<8>(w) : nib_pair_bf16<0>(w);
           const uint32_t b1 = (kt & 1) ? nib_pair_bf16<12>(w) : nib_pair_bf16<4>(w);
           mma_bf16_16816(s[nt], qa.x, qa.y, qa.z, qa.w, b0, b1);
+          mma_bf16_16816(s[nt], ql.x, ql.y, ql.z, ql.w, b0, b1);
         }
       }
 #pragma unroll
@@ -636,18 +646,21 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
         o[mt][dt][3] *= alpha[1];
       }
       // P scaled by the per-token V scale
-      const uint32_t pa0 = pack_bf2(s[0][0] * vsc[0][0], s[0][1] * vsc[0][1]);
-      const uint32_t pa1 = pack_bf2(s[0][2] * vsc[0][0], s[0][3] * vsc[0][1]);
-      const uint32_t pa2 = pack_bf2(s[1][0] * vsc[1][0], s[1][1] * vsc[1][1]);
-      const uint32_t pa3 = pack_bf2(s[1][2] * vsc[1][0], s[1][3] * vsc[1][1]);
+      uint32_t ph[4], pl[4];
+      split_bf2(s[0][0] * vsc[0][0], s[0][1] * vsc[0][1], ph[0], pl[0]);
+      split_bf2(s[0][2] * vsc[0][0], s[0][3] * vsc[0][1], ph[1], pl[1]);
+      split_bf2(s[1][0] * vsc[1][0], s[1][1] * vsc[1][1], ph[2], pl[2]);
+      split_bf2(s[1][2] * vsc[1][0], s[1][3] * vsc[1][1], ph[3], pl[3]);
 #pragma unroll
       for (int d2 = 0; d2 < D / 16; ++d2) {
         uint32_t vb[4];
         const int mi = lane >> 3;
         const int tok = (mi & 1) * 8 + (lane & 7);
         ldmatrix_x4_trans(vb, vtile + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
-        mma_bf16_16816(o[mt][2 * d2], pa0, pa1, pa2, pa3, vb[0], vb[1]);
-        mma_bf16_16816(o[mt][2 * d2 + 1], pa0, pa1, pa2, pa3, vb[2], vb[3]);
+        mma_bf16_16816(o[mt][2 * d2], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
+        mma_bf16_16816(o[mt][2 * d2], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
       }
     }
     __syncwarp();
@@ -699,7 +712,7 @@ static size_t smem_bf16(int D, int MT) {
 }
 
 static size_t smem_tq4(int MT) {
-  const size_t head = (size_t)MT * 8 * 32 * 4 * 4 + 16 * MT * 4;
+  const size_t head = (size_t)MT * 8 * 32 * 8 * 4 + 16 * MT * 4;
   const size_t warps = (size_t)4 * (2 * (1024 + 1024 + 32 + 32) + 16 * 128 * 2);
   const size_t qrot = (size_t)16 * MT * 128 * 4;
   const size_t merge = (size_t)(9 * 16 * MT + 4 * 16 * MT * 128) * 4;

@@ -80,6 +80,13 @@ __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) {
   return (uint32_t)f2bf(lo) | ((uint32_t)f2bf(hi) << 16);
 }
 
+// (x0, x1) as bf16 pairs hi = bf16(x), lo = bf16(x - hi): hi + lo carries ~16
+// mantissa bits, so two bf16 MMAs reproduce an f32 operand closely.
+__device__ __forceinline__ void split_bf2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  hi = pack_bf2(x0, x1);
+  lo = pack_bf2(x0 - bf_lo(hi), x1 - bf_hi(hi));
+}
+
 // (a & b) | c in one LOP3
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;

@@ -33,4 +33,28 @@ struct QLinArgs {
 // M may exceed 32 (processed in 32-row passes); K % 256 == 0, N % 16 == 0.
 cudaError_t launch_qlinear(const QLinArgs& a, int epi, cudaStream_t st);
 
+// Stream-K GEMV (M <= 8), optional fused RMSNorm of x with norm_w.
+struct SkArgs {
+  const uint16_t* x;
+  const uint16_t* norm_w;
+  float eps;
+  int M, K, N;
+  int n_tiles;  // 16-row weight tiles (SwiGLU: gate/up interleaved, 2 per output tile)
+  int swiglu;
+  int nseg;
+  int seg_end[3];
+  const uint32_t* wseg[3];
+  const uint16_t* sseg[3];
+  const uint16_t* bseg[3];
+  uint16_t* y;
+  float* y_f32;
+  const uint16_t* residual;
+  // filled by the launcher from the workspace
+  int max_slots;
+  int* counters;
+  float* partials;
+};
+size_t qgemv_sk_workspace(int M, int K, int n_tiles);
+cudaError_t launch_qgemv_sk(SkArgs a, void* workspace, cudaStream_t st);
+
 }  // namespace higgs

@@ -14,6 +14,7 @@
 //
 // Weights are caller-owned device tensors registered under their MLX
 // safetensors names (lib.rs:604-723 loads the same keys); nothing is copied.
+#include <algorithm>
 #include <cmath>
 #include <string>
 #include <unordered_map>
@@ -71,6 +72,7 @@ struct higgs_model {
 
 struct higgs_graph {
   cudaGraphExec_t exec = nullptr;
+  int kernel_nodes = 0;
 };
 
 namespace {
@@ -80,8 +82,11 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
-  size_t h, x, qkv, q, attn, act, xl, logits, attn_ws, total;
+  size_t h, x, qkv, q, attn, act, xl, logits, sk, sk_bytes, attn_ws, total;
 };
+
+// Decode batches of <= 8 rows use the stream-K GEMV with the RMSNorms fused.
+bool use_sk(int T) { return T <= 8; }
 
 WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, bool last_only) {
   const size_t T = (size_t)B * Lq;
@@ -102,6 +107,18 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
   L.act = take(T * (size_t)c.intermediate * 2);
   L.xl = take(rows_lm * c.hidden * 2);
   L.logits = take(rows_lm * (size_t)c.vocab * 4);
+  L.sk_bytes = 0;
+  if (use_sk((int)T)) {
+    const int M = (int)T;
+    const int qkv_tiles = (c.heads + 2 * c.kv_heads) * D / 16;
+    size_t m = qgemv_sk_workspace(M, c.hidden, qkv_tiles);
+    m = std::max(m, qgemv_sk_workspace(M, c.heads * D, c.hidden / 16));
+    m = std::max(m, qgemv_sk_workspace(M, c.hidden, 2 * c.intermediate / 16));
+    m = std::max(m, qgemv_sk_workspace(M, c.intermediate, c.hidden / 16));
+    m = std::max(m, qgemv_sk_workspace(M, c.hidden, c.vocab / 16));
+    L.sk_bytes = m;
+  }
+  L.sk = take(L.sk_bytes);
   const size_t aws = higgs_paged_attention_workspace_size(B, Lq, c.heads, c.kv_heads, D, max_seq_len);
   L.attn_ws = take(aws);
   L.total = off;
@@ -189,11 +206,58 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   const int64_t tq_layer_bytes = m->num_pages * c.kv_heads * HIGGS_PAGE_SIZE * 64;
   const int64_t tq_layer_scales = m->num_pages * c.kv_heads * HIGGS_PAGE_SIZE;
 
+  const bool sk = use_sk(T);
+  void* skws = ws + L.sk;
+  auto sk_lin = [&](const QW& w, const uint16_t* xin, const uint16_t* norm, uint16_t* y, float* yf,
+                    const uint16_t* res) {
+    SkArgs a{};
+    a.x = xin;
+    a.norm_w = norm;
+    a.eps = c.rms_eps;
+    a.M = T;
+    a.K = w.K;
+    a.N = w.N;
+    a.n_tiles = w.N / 16;
+    a.nseg = 1;
+    a.seg_end[0] = w.N;
+    a.wseg[0] = w.w;
+    a.sseg[0] = w.s;
+    a.bseg[0] = w.b;
+    a.y = y;
+    a.y_f32 = yf;
+    a.residual = res;
+    return launch_qgemv_sk(a, skws, st);
+  };
   int rc = higgs_embed_gather_w4(m->ctx, f->tokens, T, m->embed.w, m->embed.s, m->embed.b, c.vocab,
                                  H, h, st);
   if (rc) return rc;
   for (int li = 0; li < n_layers; ++li) {
     const LayerW& Lw = m->layers[li];
+    if (sk) {
+      SkArgs a{};
+      a.x = h;
+      a.norm_w = Lw.ln_in;
+      a.eps = c.rms_eps;
+      a.M = T;
+      a.K = H;
+      a.N = Lw.q.N + Lw.k.N + Lw.v.N;
+      a.n_tiles = a.N / 16;
+      a.nseg = 3;
+      a.seg_end[0] = Lw.q.N;
+      a.seg_end[1] = Lw.q.N + Lw.k.N;
+      a.seg_end[2] = a.N;
+      a.wseg[0] = Lw.q.w;
+      a.sseg[0] = Lw.q.s;
+      a.bseg[0] = Lw.q.b;
+      a.wseg[1] = Lw.k.w;
+      a.sseg[1] = Lw.k.s;
+      a.bseg[1] = Lw.k.b;
+      a.wseg[2] = Lw.v.w;
+      a.sseg[2] = Lw.v.s;
+      a.bseg[2] = Lw.v.b;
+      a.y = qkv;
+      HG_CUDA(launch_qgemv_sk(a, skws, st));
+    } else {
     rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_in, c.rms_eps, x, nullptr, st);
     if (rc) return rc;
     {
@@ -220,6 +284,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.bseg[2] = Lw.v.b;
       a.y = qkv;
       HG_CUDA(launch_qlinear(a, EPI_STORE, st));
+    }
     }
     if (tq) {
       rc = higgs_qknorm_rope_kv_write_tq4(
@@ -252,6 +317,29 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       if (rc) return rc;
     }
     // h = h + o_proj(attn)   (in place: each element read then written by one thread)
+    if (sk) {
+      HG_CUDA(sk_lin(Lw.o, attn, nullptr, h, nullptr, h));
+      SkArgs a{};
+      a.x = h;
+      a.norm_w = Lw.ln_post;
+      a.eps = c.rms_eps;
+      a.M = T;
+      a.K = H;
+      a.N = c.intermediate;
+      a.n_tiles = 2 * c.intermediate / 16;
+      a.swiglu = 1;
+      a.nseg = 2;
+      a.wseg[0] = Lw.gate.w;
+      a.sseg[0] = Lw.gate.s;
+      a.bseg[0] = Lw.gate.b;
+      a.wseg[1] = Lw.up.w;
+      a.sseg[1] = Lw.up.s;
+      a.bseg[1] = Lw.up.b;
+      a.y = act;
+      HG_CUDA(launch_qgemv_sk(a, skws, st));
+      HG_CUDA(sk_lin(Lw.down, act, nullptr, h, nullptr, h));
+      continue;
+    }
     HG_CUDA(qlin(Lw.o, attn, T, h, nullptr, h, st));
     rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_post, c.rms_eps, x, nullptr, st);
     if (rc) return rc;
@@ -275,6 +363,14 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   }
   // final norm (+ last-token selection) and LM head
   const int rows_lm = f->last_only ? B : T;
+  if (sk && (Lq == 1 || !f->last_only) && !f->hidden_out) {
+    if (f->logits || f->argmax) HG_CUDA(sk_lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
+    if (f->argmax) {
+      rc = higgs_argmax(m->ctx, logits, rows_lm, c.vocab, f->argmax, st);
+      if (rc) return rc;
+    }
+    return HIGGS_OK;
+  }
   if (f->last_only) {
     rc = higgs_rmsnorm_strided(m->ctx, h + (size_t)(Lq - 1) * H, (int64_t)Lq * H, B, H,
                                m->final_norm, c.rms_eps, xl, st);
@@ -450,12 +546,23 @@ extern "C" int higgs_model_capture(higgs_model* m, const higgs_forward_args* f, 
     return rc;
   }
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  size_t n_nodes = 0;
+  int kernels = 0;
+  if (cudaGraphGetNodes(graph, nullptr, &n_nodes) == cudaSuccess && n_nodes > 0) {
+    std::vector<cudaGraphNode_t> nodes(n_nodes);
+    if (cudaGraphGetNodes(graph, nodes.data(), &n_nodes) == cudaSuccess)
+      for (size_t i = 0; i < n_nodes; ++i) {
+        cudaGraphNodeType ty;
+        if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++kernels;
+      }
+  }
   cudaGraphExec_t exec = nullptr;
   e = cudaGraphInstantiate(&exec, graph, 0);
   cudaGraphDestroy(graph);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
   higgs_graph* g = new higgs_graph;
   g->exec = exec;
+  g->kernel_nodes = kernels;
   *out = g;
   return HIGGS_OK;
 }
@@ -465,6 +572,8 @@ extern "C" int higgs_graph_launch(higgs_graph* g, void* stream) {
   HG_CUDA(cudaGraphLaunch(g->exec, (cudaStream_t)stream));
   return HIGGS_OK;
 }
+
+extern "C" int higgs_graph_num_kernels(const higgs_graph* g) { return g ? g->kernel_nodes : -1; }
 
 extern "C" int higgs_graph_destroy(higgs_graph* g) {
   if (!g) return HIGGS_OK;

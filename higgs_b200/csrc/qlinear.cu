@@ -339,9 +339,69 @@ __global__ void dequant_kernel(const uint32_t* w, const uint16_t* s, const uint1
   }
 }
 
+// One thread per (row, 64-group); the rounding sequence is the oracle's:
+// scale = bf16((hi - lo) / 15) (1 if that is 0), bias = bf16(lo),
+// q = clamp(rint((w - bias) / scale), 0, 15).
+__global__ void quantize_kernel(const float* w, int64_t N, int K, uint32_t* q, uint16_t* s,
+                                uint16_t* b) {
+  const int G = K / 64;
+  const int64_t total = N * G;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = idx / G, g = idx % G;
+    const float* src = w + n * K + g * 64;
+    float v[64];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(src)[i];
+      v[4 * i] = f.x;
+      v[4 * i + 1] = f.y;
+      v[4 * i + 2] = f.z;
+      v[4 * i + 3] = f.w;
+    }
+    float lo = v[0], hi = v[0];
+#pragma unroll
+    for (int i = 1; i < 64; ++i) {
+      lo = v[i] < lo ? v[i] : lo;
+      hi = v[i] > hi ? v[i] : hi;
+    }
+    uint16_t sb = f2bf(__fdiv_rn(__fsub_rn(hi, lo), 15.0f));
+    if (bf2f(sb) == 0.0f) sb = f2bf(1.0f);
+    const uint16_t bb = f2bf(lo);
+    const float sc = bf2f(sb), bi = bf2f(bb);
+    s[idx] = sb;
+    b[idx] = bb;
+#pragma unroll
+    for (int w8 = 0; w8 < 8; ++w8) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float c = rintf(__fdiv_rn(__fsub_rn(v[w8 * 8 + j], bi), sc));
+        c = fminf(fmaxf(c, 0.0f), 15.0f);
+        word |= ((uint32_t)c) << (4 * j);
+      }
+      q[n * (K / 8) + g * 8 + w8] = word;
+    }
+  }
+}
+
 }  // namespace higgs
 
 using namespace higgs;
+
+extern "C" int higgs_w4_quantize(higgs_ctx* ctx, const float* w, int64_t N, int K, uint32_t* q,
+                                 void* scales, void* biases, void* stream) {
+  HG_CHECK_ARG(ctx && w && q && scales && biases, "higgs_w4_quantize: null argument");
+  HG_CHECK_ARG(N >= 0 && K > 0 && K % 64 == 0, "higgs_w4_quantize: need K % 64 == 0");
+  if (N == 0) return HIGGS_OK;
+  const int64_t total = N * (K / 64);
+  const int64_t want = (total + 127) / 128;
+  const int blocks = (int)(want < 64 * sm_count() ? want : 64 * sm_count());
+  quantize_kernel<<<blocks, 128, 0, (cudaStream_t)stream>>>(w, N, K, q, (uint16_t*)scales,
+                                                             (uint16_t*)biases);
+  HG_CUDA(cudaGetLastError());
+  return HIGGS_OK;
+}
 
 extern "C" int higgs_w4_dequantize(higgs_ctx* ctx, const uint32_t* w, const void* scales,
                                    const void* biases, int N, int K, void* out, void* stream) {

@@ -25,9 +25,13 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_last_error": (ctypes.c_char_p, []),
     "higgs_version": (I, []),
     "higgs_w4_dequantize": (I, [P, P, P, P, I, I, P, P]),
+    "higgs_w4_quantize": (I, [P, P, I64, I, P, P, P, P]),
     "higgs_embed_gather_w4": (I, [P, P, I, P, P, P, I, I, P, P]),
     "higgs_qlinear_w4g64": (I, [P, P, I, I, P, P, P, I, P, P, P, P]),
     "higgs_qlinear_gate_up_swiglu": (I, [P, P, I, I, P, P, P, P, P, P, I, P, P]),
+    "higgs_qlinear_sk_workspace_size": (SZ, [I, I, I]),
+    "higgs_rmsnorm_qlinear_w4g64": (I, [P, P, I, I, P, F, P, P, P, I, P, P, P, P, SZ, P]),
+    "higgs_rmsnorm_gate_up_swiglu": (I, [P, P, I, I, P, F, P, P, P, P, P, P, I, P, P, SZ, P]),
     "higgs_rmsnorm": (I, [P, P, P, I, I, P, F, P, P, P]),
     "higgs_rope": (I, [P, P, I, I, I, P, P, P, P]),
     "higgs_qknorm_rope_kv_write": (I, [P, P, I, I, I, I, P, P, F, P, P, P, P, P, I64, I64, P, P]),
@@ -53,6 +57,20 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_model_capture": (I, [P, P, P, ctypes.POINTER(P)]),
     "higgs_graph_launch": (I, [P, P]),
     "higgs_graph_destroy": (I, [P]),
+    "higgs_graph_num_kernels": (I, [P]),
+    "higgs_block_pool_create": (I, [I64, ctypes.POINTER(P)]),
+    "higgs_block_pool_destroy": (I, [P]),
+    "higgs_block_pool_num_free": (I64, [P]),
+    "higgs_block_pool_alloc": (I, [P, I, P]),
+    "higgs_block_pool_retain": (I, [P, P, I]),
+    "higgs_block_pool_release": (I, [P, P, I]),
+    "higgs_block_pool_refcount": (I, [P, ctypes.c_int32]),
+    "higgs_prefix_cache_create": (I, [P, I, ctypes.POINTER(P)]),
+    "higgs_prefix_cache_destroy": (I, [P]),
+    "higgs_prefix_cache_len": (I, [P]),
+    "higgs_prefix_cache_clear": (I, [P]),
+    "higgs_prefix_cache_lookup": (I, [P, P, I, P, I, ctypes.POINTER(I)]),
+    "higgs_prefix_cache_store": (I, [P, P, I, P, I]),
 }
 
 

@@ -74,6 +74,43 @@ def gate_up_swiglu(x, wg, sg, bg, wu, su, bu):
     return y
 
 
+def sk_workspace(M: int, K: int, rows: int, device) -> torch.Tensor:
+    n = ffi.load().higgs_qlinear_sk_workspace_size(M, K, rows)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def rmsnorm_quantized_matmul(h, norm_w, eps, w, scales, biases, *, residual=None,
+                             out_f32: bool = False, workspace=None):
+    """nn::RmsNorm (norm_w, or none when norm_w is None) then quantized_matmul, for M <= 8."""
+    _chk(h, torch.bfloat16, "h")
+    K = h.shape[-1]
+    M = h.numel() // K
+    N = w.shape[0]
+    if workspace is None:
+        workspace = sk_workspace(M, K, N, h.device)
+    y = torch.empty(*h.shape[:-1], N, dtype=torch.float32 if out_f32 else torch.bfloat16,
+                    device=h.device)
+    ffi.call("higgs_rmsnorm_qlinear_w4g64", _ctx(h), _p(h), M, K, _p(norm_w), float(eps), _p(w),
+             _p(scales), _p(biases), N, None if out_f32 else _p(y), _p(y) if out_f32 else None,
+             _p(residual), _p(workspace), workspace.numel(), _st(h.device))
+    return y
+
+
+def rmsnorm_gate_up_swiglu(h, norm_w, eps, wg, sg, bg, wu, su, bu, workspace=None):
+    """nn::RmsNorm then swiglu(gate_proj, up_proj), for M <= 8."""
+    _chk(h, torch.bfloat16, "h")
+    K = h.shape[-1]
+    M = h.numel() // K
+    N = wg.shape[0]
+    if workspace is None:
+        workspace = sk_workspace(M, K, 2 * N, h.device)
+    y = torch.empty(*h.shape[:-1], N, dtype=torch.bfloat16, device=h.device)
+    ffi.call("higgs_rmsnorm_gate_up_swiglu", _ctx(h), _p(h), M, K, _p(norm_w), float(eps), _p(wg),
+             _p(sg), _p(bg), _p(wu), _p(su), _p(bu), N, _p(y), _p(workspace), workspace.numel(),
+             _st(h.device))
+    return y
+
+
 def dequantize(w, scales, biases, group_size: int = 64, bits: int = 4):
     """ops::dequantize (qwen3_next.rs:249-256): bf16 [N, K]."""
     if group_size != 64 or bits != 4:
@@ -83,6 +120,19 @@ def dequantize(w, scales, biases, group_size: int = 64, bits: int = 4):
     ffi.call("higgs_w4_dequantize", _ctx(w), _p(w), _p(scales), _p(biases), N, K, _p(out),
              _st(w.device))
     return out
+
+
+def quantize(w, group_size: int = 64, bits: int = 4):
+    """ops::quantize with this library's rounding: f32 [N, K] -> (u32-as-int32 [N, K/8], bf16 s, b)."""
+    if group_size != 64 or bits != 4:
+        raise NotImplementedError("only group_size=64, bits=4")
+    _chk(w, torch.float32, "w")
+    N, K = w.shape
+    q = torch.empty(N, K // 8, dtype=torch.int32, device=w.device)
+    s = torch.empty(N, K // 64, dtype=torch.bfloat16, device=w.device)
+    b = torch.empty(N, K // 64, dtype=torch.bfloat16, device=w.device)
+    ffi.call("higgs_w4_quantize", _ctx(w), _p(w), N, K, _p(q), _p(s), _p(b), _st(w.device))
+    return q, s, b
 
 
 def embed_gather(ids, w, scales, biases):

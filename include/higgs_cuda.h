@@ -41,6 +41,7 @@ extern "C" {
 #define HIGGS_ERR_WORKSPACE -4
 #define HIGGS_ERR_TIMEOUT -5
 #define HIGGS_ERR_STATE -6
+#define HIGGS_ERR_OUT_OF_PAGES -7
 
 #define HIGGS_PAGE_SIZE 16 /* tokens per KV page */
 
@@ -54,6 +55,8 @@ extern "C" {
 typedef struct higgs_ctx higgs_ctx;
 typedef struct higgs_model higgs_model;
 typedef struct higgs_graph higgs_graph;
+typedef struct higgs_block_pool higgs_block_pool;
+typedef struct higgs_prefix_cache higgs_prefix_cache;
 
 /* ---- context and errors ------------------------------------------------ */
 
@@ -73,6 +76,15 @@ int higgs_version(void);
  * out bf16 [N, K] = bf16(scale * q + bias). */
 int higgs_w4_dequantize(higgs_ctx* ctx, const uint32_t* w, const void* scales, const void* biases,
                         int N, int K, void* out, void* stream);
+
+/* ops::quantize(w, 64, 4) as used to build weights in the reference's tests
+ * (crates/higgs-models/src/qwen3_next.rs:2113-2116), with this library's
+ * documented rounding (MLX's own is not pinned by any reference test):
+ * per 64-group scale = bf16((max - min) / 15) (1 if that rounds to 0),
+ * bias = bf16(min), q = clamp(rint((w - bias) / scale), 0, 15).
+ * w f32 [N, K] -> q u32 [N, K/8], scales / biases bf16 [N, K/64]. */
+int higgs_w4_quantize(higgs_ctx* ctx, const float* w, int64_t N, int K, uint32_t* q, void* scales,
+                      void* biases, void* stream);
 
 /* QEmbedding::forward (crates/higgs-models/src/qwen3_next.rs:248-257):
  * out bf16 [n_ids, H] = dequantized rows ids[i] of the [V, H] table.  Ids
@@ -94,6 +106,30 @@ int higgs_embed_gather_w4(higgs_ctx* ctx, const int32_t* ids, int n_ids, const u
 int higgs_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, const uint32_t* w,
                         const void* scales, const void* biases, int N, void* y, float* y_f32,
                         const void* residual, void* stream);
+
+/* Decode-batch variants (M <= 8) of the two linear ops above with the
+ * preceding nn::RmsNorm fused in (transformer.rs:407-416: input_layernorm
+ * before q/k/v, post_attention_layernorm before the MLP): when norm_w != NULL,
+ * x is the residual stream h and the op consumes bf16(h * rsqrt(mean(h^2) +
+ * eps) * norm_w) (K <= 8192); with norm_w == NULL they equal
+ * higgs_qlinear_w4g64 / higgs_qlinear_gate_up_swiglu.  They balance the
+ * weight stream over every SM (stream-K) and need a workspace of
+ * higgs_qlinear_sk_workspace_size(M, K, rows) bytes (rows = N, or 2N for the
+ * SwiGLU pair, at most 262144) whose first 65536 bytes (tile counters) must be
+ * zero before the first call; each call leaves them zero, so one workspace of
+ * the largest size serves every shape back to back on a stream.  Results are
+ * deterministic (partial sums are combined in a fixed order). */
+size_t higgs_qlinear_sk_workspace_size(int M, int K, int N_rows);
+int higgs_rmsnorm_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, const void* norm_w,
+                                float eps, const uint32_t* w, const void* scales,
+                                const void* biases, int N, void* y, float* y_f32,
+                                const void* residual, void* workspace, size_t workspace_bytes,
+                                void* stream);
+int higgs_rmsnorm_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M, int K, const void* norm_w,
+                                 float eps, const uint32_t* w_gate, const void* s_gate,
+                                 const void* b_gate, const uint32_t* w_up, const void* s_up,
+                                 const void* b_up, int N, void* y, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 
 /* Mlp::forward gate/up half (crates/higgs-models/src/transformer.rs:349-353,
  * swiglu qwen3_next.rs:275-277): y bf16 [M, N] = silu(x Wg^T) * (x Wu^T),
@@ -305,7 +341,41 @@ int higgs_model_forward(higgs_model* m, const higgs_forward_args* args, void* st
 int higgs_model_capture(higgs_model* m, const higgs_forward_args* args, void* stream,
                         higgs_graph** out);
 int higgs_graph_launch(higgs_graph* g, void* stream);
+/* Kernel launches one replay of the captured graph performs. */
+int higgs_graph_num_kernels(const higgs_graph* g);
 int higgs_graph_destroy(higgs_graph* g);
+
+/* ---- a12/a13: KV page pool and radix prefix cache (host side) ----------- */
+
+/* Refcounted pool of KV page ids [0, num_pages).  Replaces per-request cache
+ * growth (crates/higgs-models/src/cache.rs:245-277): a sequence owns the pages
+ * of its block-table row; shared prefix pages carry one reference per owner.
+ * alloc is all-or-nothing (HIGGS_ERR_OUT_OF_PAGES); release frees a page when
+ * its count reaches zero.  Host memory only; not thread-safe. */
+int higgs_block_pool_create(int64_t num_pages, higgs_block_pool** out);
+int higgs_block_pool_destroy(higgs_block_pool* pool);
+int64_t higgs_block_pool_num_free(const higgs_block_pool* pool);
+int higgs_block_pool_alloc(higgs_block_pool* pool, int n, int32_t* pages);
+int higgs_block_pool_retain(higgs_block_pool* pool, const int32_t* pages, int n);
+int higgs_block_pool_release(higgs_block_pool* pool, const int32_t* pages, int n);
+int higgs_block_pool_refcount(const higgs_block_pool* pool, int32_t page);
+
+/* PrefixCache (crates/higgs-engine/src/prompt_cache.rs:41-311) over pages:
+ * a compressed radix trie of token ids whose entries hold page ids.  Only the
+ * whole 16-token pages of a stored prefix are kept (never the partly filled
+ * last page), matches need >= 16 tokens (prompt_cache.rs:8), the deepest
+ * match wins, and entries beyond max_entries are evicted least recently used.
+ * lookup copies the matched pages to pages_out, sets *matched_tokens (0 = no
+ * hit) and retains those pages for the caller, who releases them with the
+ * sequence.  store retains the pages it keeps. */
+int higgs_prefix_cache_create(higgs_block_pool* pool, int max_entries, higgs_prefix_cache** out);
+int higgs_prefix_cache_destroy(higgs_prefix_cache* pc);
+int higgs_prefix_cache_len(const higgs_prefix_cache* pc);
+int higgs_prefix_cache_clear(higgs_prefix_cache* pc);
+int higgs_prefix_cache_lookup(higgs_prefix_cache* pc, const int32_t* tokens, int n,
+                              int32_t* pages_out, int max_pages, int* matched_tokens);
+int higgs_prefix_cache_store(higgs_prefix_cache* pc, const int32_t* tokens, int n,
+                             const int32_t* pages, int n_pages);
 
 #ifdef __cplusplus
 }

@@ -430,3 +430,51 @@ def test_penalties(kat):
     for bidx in range(2):
         ref = orc.apply_penalties(lg[bidx], hist[bidx, :lens[bidx]], 1.3, 0.2, 0.5)
         np.testing.assert_array_equal(lt.cpu().numpy()[bidx], ref)
+
+
+# ---- stream-K GEMV with fused RMSNorm (decode batches) -----------------------------------
+
+@pytest.mark.parametrize("M,K,N,norm", [(1, 256, 16, False), (1, 4096, 6144, True), (3, 2048, 512, True),
+                                        (8, 4096, 1024, True), (5, 12288, 256, False),
+                                        (2, 1024, 4096 + 16, False), (1, 4096, 151936, True)])
+def test_rmsnorm_qlinear_sk(M, K, N, norm):
+    rng = np.random.default_rng(M + K + N)
+    q, s, b = qweights(rng, N, K)
+    h = orc.f32_to_bf16(rng.normal(0, 1, size=(M, K)))
+    nw = orc.f32_to_bf16(rng.uniform(0.5, 1.5, size=K))
+    x = orc.rmsnorm(h, nw, 1e-6)[0] if norm else h
+    yb_ref, yf_ref = orc.qmatmul(x, q, s, b, want_f32=True)
+    o = ops()
+    ws = o.sk_workspace(M, K, N, DEV)
+    yf = o.rmsnorm_quantized_matmul(bf(h), bf(nw) if norm else None, 1e-6, t(q.view(np.int32)), bf(s),
+                                    bf(b), out_f32=True, workspace=ws).cpu().numpy()
+    scale = np.abs(yf_ref).max()
+    # the fused norm may round an input element 1 ulp differently from the oracle's norm
+    tol = 3e-3 if norm else 1e-3
+    np.testing.assert_allclose(yf, yf_ref, rtol=tol, atol=tol * 0.1 * scale + 1e-6)
+    # deterministic, and the workspace is left reusable
+    y1 = o.rmsnorm_quantized_matmul(bf(h), bf(nw) if norm else None, 1e-6, t(q.view(np.int32)), bf(s),
+                                    bf(b), workspace=ws)
+    y2 = o.rmsnorm_quantized_matmul(bf(h), bf(nw) if norm else None, 1e-6, t(q.view(np.int32)), bf(s),
+                                    bf(b), workspace=ws)
+    assert torch.equal(y1, y2)
+    # bf16 output: within one bf16 rounding of the f32 reference, plus the f32 noise near zero
+    np.testing.assert_allclose(orc.bf16_to_f32(to_np_bf(y1)), yf_ref, rtol=2 ** -7,
+                               atol=tol * 0.1 * scale + 1e-6)
+
+
+@pytest.mark.parametrize("M,norm", [(1, True), (4, False), (8, True)])
+def test_rmsnorm_gate_up_swiglu_sk(M, norm):
+    rng = np.random.default_rng(70 + M)
+    K, N = 2048, 768
+    qg, sg, bg = qweights(rng, N, K)
+    qu, su, bu = qweights(rng, N, K)
+    h = orc.f32_to_bf16(rng.normal(size=(M, K)))
+    nw = orc.f32_to_bf16(rng.uniform(0.5, 1.5, size=K))
+    x = orc.rmsnorm(h, nw, 1e-6)[0] if norm else h
+    ref = orc.silu_mul(orc.qmatmul(x, qg, sg, bg), orc.qmatmul(x, qu, su, bu))
+    got = to_np_bf(ops().rmsnorm_gate_up_swiglu(bf(h), bf(nw) if norm else None, 1e-6,
+                                                t(qg.view(np.int32)), bf(sg), bf(bg),
+                                                t(qu.view(np.int32)), bf(su), bf(bu)))
+    np.testing.assert_allclose(orc.bf16_to_f32(got), orc.bf16_to_f32(ref), atol=3e-3, rtol=3e-2)
+    assert np.percentile(bf_ulps(got, ref), 99) <= 3
