@@ -22,6 +22,8 @@
 //    expanded to exact bf16 (c - 8) in shared memory with the per-token scale
 //    folded into P, and the merged output is rotated back with the inverse
 //    Hadamard transform.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace higgs {
@@ -882,4 +884,75 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
                           : launch_attn(paged_attn_tq4_kernel<2>, smem_tq4(2), a, p, st);
   HG_CUDA(e);
   return HIGGS_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of higgs_paged_attention.
+//
+// Some callers cannot allocate device memory at all on their serving path:
+// hosts that hand this library a fixed device-memory arena sized at start-up
+// and account for every byte themselves, or real-time decode loops that must
+// never block in the driver's allocator.  They cannot provide the split-K
+// workspace that higgs_paged_attention takes.  This entry point keeps that
+// scratch in a file-scope device array instead: kNoAllocScratchBytes on every
+// GPU that loads the library, for the life of the process.
+//
+// The array's host-side name is only a stand-in for the device symbol, so its
+// device address is looked up once per device with cudaGetSymbolAddress, with
+// that device current, on the first call made on that device.
+// ---------------------------------------------------------------------------
+namespace higgs {
+
+constexpr size_t kNoAllocScratchBytes = 8u << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static void* noalloc_scratch_ptr(int device, cudaError_t* err) {
+  static std::mutex mu;
+  static void* ptrs[128] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  *err = cudaSuccess;
+  if (device < 0 || device >= 128) {
+    *err = cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  if (!ptrs[device]) {
+    void* p = nullptr;
+    *err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (*err != cudaSuccess) return nullptr;
+    ptrs[device] = p;
+  }
+  return ptrs[device];
+}
+
+}  // namespace higgs
+
+extern "C" int higgs_paged_attention_noalloc(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq,
+                                             int Hkv, int D, const void* k_cache,
+                                             const void* v_cache, int64_t page_stride,
+                                             int64_t head_stride, const int32_t* block_table,
+                                             int max_blocks, const int32_t* seq_lens,
+                                             int max_seq_len, float scale, void* out,
+                                             void* stream) {
+  HG_CHECK_ARG(ctx && q && k_cache && v_cache && block_table && seq_lens && out,
+               "higgs_paged_attention_noalloc: null argument");
+  HG_CHECK_ARG(D == 64 || D == 128, "higgs_paged_attention_noalloc: D must be 64 or 128");
+  HG_CHECK_ARG(B > 0 && Lq > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
+               "higgs_paged_attention_noalloc: bad batch / head shape");
+  const size_t need = attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len), B, Hkv, D);
+  if (need > kNoAllocScratchBytes)
+    return fail(HIGGS_ERR_WORKSPACE,
+                "higgs_paged_attention_noalloc: this shape needs " + std::to_string(need) +
+                    " bytes of scratch, more than the built-in " +
+                    std::to_string(kNoAllocScratchBytes) +
+                    " bytes; use higgs_paged_attention with a caller-provided workspace");
+  int device = 0;
+  HG_CUDA(cudaGetDevice(&device));
+  cudaError_t err;
+  void* scratch = noalloc_scratch_ptr(device, &err);
+  if (!scratch) return cuda_fail(err, "cudaGetSymbolAddress(g_noalloc_scratch)");
+  // the split counters must start at zero whatever an earlier call left behind
+  HG_CUDA(cudaMemsetAsync(scratch, 0, kCounterBytes, (cudaStream_t)stream));
+  return higgs_paged_attention(ctx, q, B, Lq, Hq, Hkv, D, k_cache, v_cache, page_stride,
+                               head_stride, block_table, max_blocks, seq_lens, max_seq_len, scale,
+                               out, scratch, kNoAllocScratchBytes, stream);
 }

@@ -37,6 +37,7 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_qknorm_rope_kv_write": (I, [P, P, I, I, I, I, P, P, F, P, P, P, P, P, I64, I64, P, P]),
     "higgs_paged_attention_workspace_size": (SZ, [I, I, I, I, I, I]),
     "higgs_paged_attention": (I, [P, P, I, I, I, I, I, P, P, I64, I64, P, I, P, I, F, P, P, SZ, P]),
+    "higgs_paged_attention_noalloc": (I, [P, P, I, I, I, I, I, P, P, I64, I64, P, I, P, I, F, P, P]),
     "higgs_tq4_encode": (I, [P, P, I64, P, P, P, P]),
     "higgs_qknorm_rope_kv_write_tq4": (I, [P, P, I, I, I, P, P, F, P, P, P, P, P, P, P, P, I64, I64, P, P]),
     "higgs_paged_attention_tq4_workspace_size": (SZ, [I, I, I, I, I]),

@@ -201,6 +201,24 @@ int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq, 
                           const int32_t* seq_lens, int max_seq_len, float scale, void* out,
                           void* workspace, size_t workspace_bytes, void* stream);
 
+/* higgs_paged_attention without a workspace argument, for callers that cannot
+ * allocate device memory on their serving path (a host that owns a fixed
+ * device arena and budgets every byte itself, or a real-time decode loop that
+ * must never block in the driver's allocator).  No counterpart in the
+ * reference.  The split-K scratch is an 8 MiB array built into the library
+ * (held on every GPU that loads it until the process exits); shapes needing
+ * more are rejected with HIGGS_ERR_WORKSPACE.  The first call on a device looks
+ * up that array's device address, so make that first call before any stream
+ * capture.  Every call shares the one array: calls that overlap on the GPU
+ * (concurrent streams, several host threads) race and must be serialised by
+ * the caller.  Each call clears the split counters itself before launching. */
+int higgs_paged_attention_noalloc(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq, int Hkv,
+                                  int D, const void* k_cache, const void* v_cache,
+                                  int64_t page_stride, int64_t head_stride,
+                                  const int32_t* block_table, int max_blocks,
+                                  const int32_t* seq_lens, int max_seq_len, float scale, void* out,
+                                  void* stream);
+
 /* ---- a14: TurboQuant-style 4-bit KV (no reference counterpart; the
  * KeyValueCache trait only reserves is_quantized/group_size/bits hooks,
  * crates/higgs-models/src/cache.rs:4-18) ------------------------------------ */

@@ -1,0 +1,72 @@
+"""GPU: the allocation-free attention entry point agrees with the workspace one.
+
+higgs_paged_attention_noalloc serves callers that cannot allocate device
+memory on their serving path (a host that owns a fixed device arena, or a
+real-time decode loop that must never block in the driver's allocator): its
+split-K scratch is a fixed array inside the library instead of a
+caller-provided workspace.  This file is collected last, so a failure here
+never hides another test; it also passes when run alone in a fresh process.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _case(rng, B, Lq, Hq, Hkv, D, lens):
+    maxb = max((n + 15) // 16 for n in lens)
+    P = B * maxb + 2
+    kc = torch.randn(P, Hkv, 16, D, device=DEV).to(torch.bfloat16)
+    vc = torch.randn(P, Hkv, 16, D, device=DEV).to(torch.bfloat16)
+    bt = torch.from_numpy(rng.permutation(P)[:B * maxb].reshape(B, maxb).astype(np.int32)).to(DEV)
+    q = torch.randn(B, Lq, Hq, D, device=DEV).to(torch.bfloat16)
+    sl = torch.tensor(lens, dtype=torch.int32, device=DEV)
+    return q, kc, vc, bt, sl
+
+
+def _noalloc(q, kc, vc, bt, sl, max_seq_len):
+    from higgs_b200 import ffi
+    B, Lq, Hq, D = q.shape
+    Hkv = kc.shape[1]
+    out = torch.empty_like(q)
+    ffi.call("higgs_paged_attention_noalloc", ffi.ctx(0), q.data_ptr(), B, Lq, Hq, Hkv, D,
+             kc.data_ptr(), vc.data_ptr(), Hkv * 16 * D, 16 * D, bt.data_ptr(), bt.shape[1],
+             sl.data_ptr(), max_seq_len, float(1.0 / np.sqrt(D)), out.data_ptr(),
+             torch.cuda.current_stream().cuda_stream)
+    return out
+
+
+@pytest.mark.parametrize("B,Lq,Hq,Hkv,D,lens", [(1, 1, 32, 8, 128, [2048]),
+                                                 (3, 1, 16, 8, 128, [700, 33, 1500]),
+                                                 (2, 6, 32, 8, 64, [300, 90])])
+def test_noalloc_matches_workspace_entry_point(B, Lq, Hq, Hkv, D, lens):
+    from higgs_b200 import ops
+    rng = np.random.default_rng(sum(lens) + Lq)
+    for call in range(2):  # two calls in a row share the built-in scratch
+        q, kc, vc, bt, sl = _case(rng, B, Lq, Hq, Hkv, D, lens)
+        ref = ops.paged_attention(q, kc, vc, bt, sl, max(lens))
+        got = _noalloc(q, kc, vc, bt, sl, max(lens))
+        torch.cuda.synchronize()
+        np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(),
+                                   atol=1e-2, rtol=1e-2, err_msg=f"call {call}")
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch():
+    from higgs_b200 import ffi
+    lib = ffi.load()
+    q = torch.zeros(1, dtype=torch.bfloat16, device=DEV)
+    bt = torch.zeros(1, dtype=torch.int32, device=DEV)
+    # 295 sequences x 1 kv head x 32 query heads split twice: 9.75 MB of partials > 8 MiB.
+    # Rejected on the host before anything is launched or read.
+    rc = lib.higgs_paged_attention_noalloc(ffi.ctx(0), q.data_ptr(), 295, 1, 32, 1, 128,
+                                           q.data_ptr(), q.data_ptr(), 2048, 2048, bt.data_ptr(),
+                                           256, bt.data_ptr(), 4096, ctypes.c_float(0.1),
+                                           q.data_ptr(), None)
+    assert rc == -4
+    assert b"built-in" in lib.higgs_last_error()
