@@ -53,6 +53,17 @@ struct AttnArgs {
   float* ws_o;
   float* ws_lse;
   int* counters;
+  // fused front half (higgs_fused_attention): q/k/v come from the q|k|v
+  // projection output and the new K/V are appended by the kernel itself
+  const uint16_t* qkv;
+  const uint16_t* qn;
+  const uint16_t* kn;
+  float eps;
+  const int32_t* pos;
+  const float* inv_freq;
+  const int64_t* slots;
+  uint16_t* kc_w;
+  uint16_t* vc_w;
 };
 
 __device__ __forceinline__ int swz(int row, int chunk) { return chunk ^ (row & 7); }
@@ -172,18 +183,39 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
   __threadfence();
   const float* base_o = a.ws_o + (size_t)bh * a.splits * RP * D;
   const float* base_l = a.ws_lse + (size_t)bh * a.splits * RP;
+  // split weights w[s][row] = exp2(lse - max) / sum, staged in shared memory
+  // (sm_m / sm_l are free now; splits * R <= 4 * RP * D floats of sm_o's slots 1-3)
+  float* sw = sm_o + RP * D;  // [splits][R]
+  for (int i = threadIdx.x; i < a.splits * R; i += kAttnThreads)
+    sw[i] = __ldcg(base_l + (i / R) * RP + (i % R));
+  __syncthreads();
+  if (threadIdx.x < R) {
+    const int row = threadIdx.x;
+    float M = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, sw[s * R + row]);
+    float W = 0.0f;
+    for (int s = 0; s < a.splits; ++s) {
+      const float ls = sw[s * R + row];
+      const float w = (ls == -INFINITY) ? 0.0f : exp2f(ls - M);
+      sw[s * R + row] = w;
+      W += w;
+    }
+    sm_lse[row] = W > 0.0f ? 1.0f / W : 0.0f;
+  }
+  __syncthreads();
+  // every (row, d) sums its splits with independent loads, 4 in flight
   for (int i = threadIdx.x; i < R * D; i += kAttnThreads) {
     const int row = i / D;
-    float M = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, __ldcg(base_l + s * RP + row));
-    float W = 0.0f, O = 0.0f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ls = __ldcg(base_l + s * RP + row);
-      const float w = (ls == -INFINITY) ? 0.0f : exp2f(ls - M);
-      W += w;
-      O += w * __ldcg(base_o + (size_t)s * RP * D + i);
+    float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
+    int s = 0;
+    for (; s + 4 <= a.splits; s += 4) {
+      O0 += sw[(s + 0) * R + row] * __ldcg(base_o + (size_t)(s + 0) * RP * D + i);
+      O1 += sw[(s + 1) * R + row] * __ldcg(base_o + (size_t)(s + 1) * RP * D + i);
+      O2 += sw[(s + 2) * R + row] * __ldcg(base_o + (size_t)(s + 2) * RP * D + i);
+      O3 += sw[(s + 3) * R + row] * __ldcg(base_o + (size_t)(s + 3) * RP * D + i);
     }
-    sm_o[i] = W > 0.0f ? O / W : 0.0f;
+    for (; s < a.splits; ++s) O0 += sw[s * R + row] * __ldcg(base_o + (size_t)s * RP * D + i);
+    sm_o[i] = ((O0 + O1) + (O2 + O3)) * sm_lse[row];
   }
   __syncthreads();
   if (threadIdx.x == 0) a.counters[bh] = 0;
@@ -333,6 +365,257 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_bf16_kernel(AttnArgs 
 
   float* smem_f = reinterpret_cast<float*>(KV);
   FinishBf16<D> fin{&a};
+  attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
+}
+
+// ---------------------------------------------------------------------------
+// Fused decode attention (bf16 pages): q/k RMSNorm + RoPE + KV append + SDPA.
+//
+// The context pages of a split do not depend on the kernel that produced q|k|v,
+// so each warp starts streaming its first pages into shared memory BEFORE
+// griddepcontrol.wait; their DRAM latency overlaps the previous kernel's tail.
+// After the wait the CTA builds its normalised, rotated query rows, computes
+// the new tokens' K/V that fall in its page range, stores them to the cache
+// and patches them into the prefetched page tiles (a split is the only reader
+// of its own pages in this launch).  Requires G * Lq <= 32 (one row tile).
+// ---------------------------------------------------------------------------
+template <int D>
+__device__ __forceinline__ void fa_load_head(const uint16_t* src, int lane, float (&lo)[D / 64],
+                                             float (&hi)[D / 64]) {
+  constexpr int E = D / 64;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    lo[e] = bf2f(src[lane * E + e]);
+    hi[e] = bf2f(src[D / 2 + lane * E + e]);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void fa_norm(float (&lo)[D / 64], float (&hi)[D / 64], const uint16_t* w,
+                                        float eps, int lane) {
+  constexpr int E = D / 64;
+  float ss = 0.0f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) ss += lo[e] * lo[e] + hi[e] * hi[e];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    lo[e] = round_bf(lo[e] * inv * bf2f(w[lane * E + e]));
+    hi[e] = round_bf(hi[e] * inv * bf2f(w[D / 2 + lane * E + e]));
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void fa_rope(float (&lo)[D / 64], float (&hi)[D / 64], int pos,
+                                        const float* inv_freq, int lane) {
+  constexpr int E = D / 64;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float th = (float)pos * inv_freq[lane * E + e];
+    float sn, cs;
+    sincosf(th, &sn, &cs);
+    const float x0 = lo[e], x1 = hi[e];
+    lo[e] = round_bf(x0 * cs - x1 * sn);
+    hi[e] = round_bf(x1 * cs + x0 * sn);
+  }
+}
+
+// write a head (lane layout of fa_load_head) to a swizzled smem row
+template <int D>
+__device__ __forceinline__ void fa_store_row(uint16_t* tile, int row, int lane,
+                                             const float (&lo)[D / 64], const float (&hi)[D / 64]) {
+  constexpr int E = D / 64;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int i0 = lane * E + e, i1 = D / 2 + lane * E + e;
+    tile[row * D + swz(row, i0 / 8) * 8 + (i0 & 7)] = f2bf(lo[e]);
+    tile[row * D + swz(row, i1 / 8) * 8 + (i1 & 7)] = f2bf(hi[e]);
+  }
+}
+
+template <int D>
+__device__ __forceinline__ void fa_store_gmem(uint16_t* dst, int lane, const float (&lo)[D / 64],
+                                              const float (&hi)[D / 64]) {
+  constexpr int E = D / 64;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    dst[lane * E + e] = f2bf(lo[e]);
+    dst[D / 2 + lane * E + e] = f2bf(hi[e]);
+  }
+}
+
+template <int D, int MT, int S>
+__global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs a) {
+  constexpr int RP = 16 * MT;
+  constexpr int PAGE_ELEMS = 16 * D;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint16_t* Qs = reinterpret_cast<uint16_t*>(smem_raw);    // [RP][D]
+  uint16_t* NK = Qs + RP * D;                              // [Lq][2][D] new K / V (natural order)
+  uint16_t* KV = NK + ((2 * a.Lq * D + 63) / 64) * 64;    // [4 warps][S stages][K | V]
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int G = a.Hq / a.Hkv;
+  const int Lq = a.Lq;
+  const int R = G * Lq;
+  const int nh = a.Hq + 2 * a.Hkv;
+
+  // block table and lengths are host inputs of the step: safe before the wait
+  const int L = a.seq_lens[b];
+  const int n_pages = min((L + 15) / 16, a.max_blocks);
+  const int pg0 = split * a.pages_per_split;
+  const int pg1 = min(n_pages, pg0 + a.pages_per_split);
+  uint16_t* my = KV + warp * S * 2 * PAGE_ELEMS;
+  auto kbuf = [&](int st) { return my + st * 2 * PAGE_ELEMS; };
+  auto vbuf = [&](int st) { return my + st * 2 * PAGE_ELEMS + PAGE_ELEMS; };
+  auto issue = [&](int pg, int st) {
+    const int pid = a.bt[(size_t)b * a.max_blocks + pg];
+    const size_t off = (size_t)pid * a.page_stride + (size_t)h * a.head_stride;
+    const int valid = min(16, L - pg * 16);
+    load_page_bf16<D>(kbuf(st), a.kc + off, valid, lane);
+    load_page_bf16<D>(vbuf(st), a.vc + off, valid, lane);
+  };
+#pragma unroll
+  for (int s = 0; s < S - 1; ++s) {
+    const int pg = pg0 + warp + 4 * s;
+    if (pg < pg1) issue(pg, s);
+    cp_async_commit();
+  }
+
+  pdl_wait();
+  pdl_launch();
+
+  // query rows: RMSNorm (Qwen3) + RoPE, straight into the swizzled Q tile
+  for (int r = warp; r < RP; r += 4) {
+    if (r < R) {
+      const int tq = r / G, hq = h * G + r % G;
+      const int tok = b * Lq + tq;
+      float lo[D / 64], hi[D / 64];
+      fa_load_head<D>(a.qkv + ((size_t)tok * nh + hq) * D, lane, lo, hi);
+      if (a.qn) fa_norm<D>(lo, hi, a.qn, a.eps, lane);
+      fa_rope<D>(lo, hi, a.pos[tok], a.inv_freq, lane);
+      fa_store_row<D>(Qs, r, lane, lo, hi);
+    } else {
+      for (int i = lane; i < D; i += 32) Qs[r * D + i] = 0;
+    }
+  }
+  // the new tokens whose slots fall in this split: K (norm + RoPE) and V, to the
+  // cache and to shared memory for patching the prefetched tiles
+  for (int tq = warp; tq < Lq; tq += 4) {
+    const int p = L - Lq + tq;
+    const int pgi = p / 16;
+    if (p < 0 || pgi < pg0 || pgi >= pg1) continue;
+    const int tok = b * Lq + tq;
+    float klo[D / 64], khi[D / 64], vlo[D / 64], vhi[D / 64];
+    fa_load_head<D>(a.qkv + ((size_t)tok * nh + a.Hq + h) * D, lane, klo, khi);
+    if (a.kn) fa_norm<D>(klo, khi, a.kn, a.eps, lane);
+    fa_rope<D>(klo, khi, a.pos[tok], a.inv_freq, lane);
+    fa_load_head<D>(a.qkv + ((size_t)tok * nh + a.Hq + a.Hkv + h) * D, lane, vlo, vhi);
+    fa_store_gmem<D>(NK + (tq * 2) * D, lane, klo, khi);
+    fa_store_gmem<D>(NK + (tq * 2 + 1) * D, lane, vlo, vhi);
+    const int64_t slot = a.slots ? a.slots[tok] : -1;
+    if (slot >= 0) {
+      const int64_t page = slot / HIGGS_PAGE_SIZE;
+      const int sl = (int)(slot % HIGGS_PAGE_SIZE);
+      const size_t off = (size_t)page * a.page_stride + (size_t)h * a.head_stride + (size_t)sl * D;
+      fa_store_gmem<D>(a.kc_w + off, lane, klo, khi);
+      fa_store_gmem<D>(a.vc_w + off, lane, vlo, vhi);
+    }
+  }
+  __syncthreads();
+
+  float m[MT][2], l[MT][2], o[MT][D / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    m[mt][0] = m[mt][1] = -INFINITY;
+    l[mt][0] = l[mt][1] = 0.0f;
+#pragma unroll
+    for (int dt = 0; dt < D / 8; ++dt)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o[mt][dt][c] = 0.0f;
+  }
+
+  int i = 0;
+  for (int pg = pg0 + warp; pg < pg1; pg += 4, ++i) {
+    const int nxt = pg + 4 * (S - 1);
+    if (nxt < pg1) issue(nxt, (i + S - 1) % S);
+    cp_async_commit();
+    cp_async_wait<S - 1>();
+    __syncwarp();
+    uint16_t* Ks = kbuf(i % S);
+    uint16_t* Vs = vbuf(i % S);
+    // patch this launch's new tokens into the tile (the prefetch may predate them)
+    for (int tq = 0; tq < Lq; ++tq) {
+      const int p = L - Lq + tq;
+      if (p < 0 || p / 16 != pg) continue;
+      const int row = p % 16;
+      for (int c = lane; c < 2 * (D / 8); c += 32) {
+        const int kv = c / (D / 8), ch = c % (D / 8);
+        const uint4 v = *reinterpret_cast<const uint4*>(NK + (tq * 2 + kv) * D + ch * 8);
+        uint16_t* dst = (kv ? Vs : Ks) + row * D + swz(row, ch) * 8;
+        *reinterpret_cast<uint4*>(dst) = v;
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int kt = 0; kt < D / 16; ++kt) {
+        uint32_t qa[4], kb[4];
+        const int mi = lane >> 3;
+        const int row = mt * 16 + (mi & 1) * 8 + (lane & 7);
+        ldmatrix_x4(qa, Qs + row * D + swz(row, 2 * kt + (mi >> 1)) * 8);
+        const int tok = (mi >> 1) * 8 + (lane & 7);
+        ldmatrix_x4(kb, Ks + tok * D + swz(tok, 2 * kt + (mi & 1)) * 8);
+        mma_bf16_16816(sc[0], qa[0], qa[1], qa[2], qa[3], kb[0], kb[1]);
+        mma_bf16_16816(sc[1], qa[0], qa[1], qa[2], qa[3], kb[2], kb[3]);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = pg * 16 + nt * 8 + 2 * t + (c & 1);
+          const int row = mt * 16 + g + 8 * (c >> 1);
+          const int qpos = L - Lq + row / G;
+          const bool ok = row < R && j <= qpos;
+          sc[nt][c] = ok ? sc[nt][c] * a.scale_log2 : -INFINITY;
+        }
+      float alpha[2];
+      row_stats_update(m[mt], l[mt], sc, alpha);
+#pragma unroll
+      for (int dt = 0; dt < D / 8; ++dt) {
+        o[mt][dt][0] *= alpha[0];
+        o[mt][dt][1] *= alpha[0];
+        o[mt][dt][2] *= alpha[1];
+        o[mt][dt][3] *= alpha[1];
+      }
+      uint32_t ph[4], pl[4];
+      split_bf2(sc[0][0], sc[0][1], ph[0], pl[0]);
+      split_bf2(sc[0][2], sc[0][3], ph[1], pl[1]);
+      split_bf2(sc[1][0], sc[1][1], ph[2], pl[2]);
+      split_bf2(sc[1][2], sc[1][3], ph[3], pl[3]);
+#pragma unroll
+      for (int d2 = 0; d2 < D / 16; ++d2) {
+        uint32_t vb[4];
+        const int mi = lane >> 3;
+        const int tok = (mi & 1) * 8 + (lane & 7);
+        ldmatrix_x4_trans(vb, Vs + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
+        mma_bf16_16816(o[mt][2 * d2], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
+        mma_bf16_16816(o[mt][2 * d2], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
+        mma_bf16_16816(o[mt][2 * d2 + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+
+  float* smem_f = reinterpret_cast<float*>(KV);
+  AttnArgs ao = a;
+  ao.tq0 = 0;
+  FinishBf16<D> fin{&ao};
   attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
 }
 
@@ -683,7 +966,7 @@ struct SplitPlan {
   int splits, pps, rows_pad, lq_chunk, chunks;
 };
 
-static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len) {
+static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len, int min_pps = 4) {
   SplitPlan p;
   const int G = Hq / Hkv;
   // query tokens per launch so that G * chunk <= 32 rows
@@ -693,9 +976,11 @@ static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len) {
   const int max_pages = (max_seq_len + 15) / 16 > 0 ? (max_seq_len + 15) / 16 : 1;
   int want = (kTargetCtas + B * Hkv - 1) / (B * Hkv);
   if (want < 1) want = 1;
+  // the final merge stages splits x rows weights in 3 * RP * D floats of shared memory
+  if (want > 128) want = 128;
   // at least 4 pages (one per warp) per split
   int pps = (max_pages + want - 1) / want;
-  if (pps < 4) pps = 4;
+  if (pps < min_pps) pps = min_pps;
   p.pps = pps;
   p.splits = (max_pages + pps - 1) / pps;
   return p;
@@ -724,6 +1009,17 @@ static size_t smem_tq4(int MT) {
   return head + body;
 }
 
+constexpr int kFusedStages = 3;
+constexpr int kFusedMinPages = 8;  // two pages per warp: the prefetch covers a whole split
+
+static size_t smem_fused(int D, int MT, int Lq) {
+  const size_t q = (size_t)16 * MT * D * 2;
+  const size_t nk = (size_t)((2 * Lq * D + 63) / 64) * 64 * 2;
+  const size_t kv = (size_t)4 * kFusedStages * 2 * 16 * D * 2;
+  const size_t merge = (size_t)(9 * 16 * MT + 4 * 16 * MT * D) * 4;
+  return q + nk + (kv > merge ? kv : merge);
+}
+
 static cudaError_t g_prepare_status = cudaSuccess;
 
 // Raise the dynamic shared-memory limit of every attention instantiation once,
@@ -743,6 +1039,10 @@ void attention_prepare() {
   set(paged_attn_bf16_kernel<128, 2>, smem_bf16(128, 2));
   set(paged_attn_tq4_kernel<1>, smem_tq4(1));
   set(paged_attn_tq4_kernel<2>, smem_tq4(2));
+  set(fused_attn_bf16_kernel<64, 1, kFusedStages>, smem_fused(64, 1, 32));
+  set(fused_attn_bf16_kernel<64, 2, kFusedStages>, smem_fused(64, 2, 32));
+  set(fused_attn_bf16_kernel<128, 1, kFusedStages>, smem_fused(128, 1, 32));
+  set(fused_attn_bf16_kernel<128, 2, kFusedStages>, smem_fused(128, 2, 32));
   g_prepare_status = e;
 }
 
@@ -882,6 +1182,79 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
   const int MT = p.rows_pad / 16;
   cudaError_t e = MT == 1 ? launch_attn(paged_attn_tq4_kernel<1>, smem_tq4(1), a, p, st)
                           : launch_attn(paged_attn_tq4_kernel<2>, smem_tq4(2), a, p, st);
+  HG_CUDA(e);
+  return HIGGS_OK;
+}
+
+extern "C" size_t higgs_fused_attention_workspace_size(int B, int Lq, int Hq, int Hkv, int D,
+                                                       int max_seq_len) {
+  if (B <= 0 || Lq <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
+  return attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len, kFusedMinPages), B, Hkv, D);
+}
+
+extern "C" int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq,
+                                     int Hkv, int D, const void* q_norm_w, const void* k_norm_w,
+                                     float eps, const int32_t* positions, const float* inv_freq,
+                                     const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                                     int64_t page_stride, int64_t head_stride,
+                                     const int32_t* block_table, int max_blocks,
+                                     const int32_t* seq_lens, int max_seq_len, float scale,
+                                     void* out, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  HG_CHECK_ARG(ctx && qkv && positions && inv_freq && k_cache && v_cache && block_table &&
+                   seq_lens && out && workspace,
+               "higgs_fused_attention: null argument");
+  HG_CHECK_ARG(D == 64 || D == 128, "higgs_fused_attention: D must be 64 or 128");
+  HG_CHECK_ARG((q_norm_w == nullptr) == (k_norm_w == nullptr),
+               "higgs_fused_attention: give both q and k norm weights or neither");
+  HG_CHECK_ARG(Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) * Lq <= 32,
+               "higgs_fused_attention: needs (Hq / Hkv) * Lq <= 32");
+  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len, kFusedMinPages);
+  int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
+                         attn_ws_bytes(p, B, Hkv, D));
+  if (rc) return rc;
+  AttnArgs a = {};
+  a.B = B;
+  a.Lq = Lq;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.lq_chunk = Lq;
+  a.kc = (const uint16_t*)k_cache;
+  a.vc = (const uint16_t*)v_cache;
+  a.kc_w = (uint16_t*)k_cache;
+  a.vc_w = (uint16_t*)v_cache;
+  a.page_stride = page_stride;
+  a.head_stride = head_stride;
+  a.bt = block_table;
+  a.max_blocks = max_blocks;
+  a.seq_lens = seq_lens;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.out = (uint16_t*)out;
+  a.splits = p.splits;
+  a.pages_per_split = p.pps;
+  a.counters = (int*)workspace;
+  a.ws_lse = (float*)((char*)workspace + kCounterBytes);
+  a.ws_o = a.ws_lse + (size_t)B * Hkv * p.splits * p.rows_pad;
+  a.qkv = (const uint16_t*)qkv;
+  a.qn = (const uint16_t*)q_norm_w;
+  a.kn = (const uint16_t*)k_norm_w;
+  a.eps = eps;
+  a.pos = positions;
+  a.inv_freq = inv_freq;
+  a.slots = slot_mapping;
+  attention_prepare();
+  HG_CUDA(g_prepare_status);
+  const int MT = p.rows_pad / 16;
+  const size_t smem = smem_fused(D, MT, Lq);
+  cudaStream_t st = (cudaStream_t)stream;
+  const dim3 grid(p.splits, Hkv, B);
+  cudaError_t e;
+  if (D == 64)
+    e = MT == 1 ? launch_pdl(fused_attn_bf16_kernel<64, 1, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a)
+                : launch_pdl(fused_attn_bf16_kernel<64, 2, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a);
+  else
+    e = MT == 1 ? launch_pdl(fused_attn_bf16_kernel<128, 1, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a)
+                : launch_pdl(fused_attn_bf16_kernel<128, 2, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a);
   HG_CUDA(e);
   return HIGGS_OK;
 }

@@ -24,9 +24,21 @@ int cuda_fail(cudaError_t e, const char* what) {
   return HIGGS_ERR_CUDA;
 }
 
+void qgemv_set_f16(bool on);
+
 }  // namespace higgs
 
 using namespace higgs;
+
+extern "C" int higgs_set_option(const char* name, int value) {
+  HG_CHECK_ARG(name, "higgs_set_option: null name");
+  const std::string n(name);
+  if (n == "gemv_f16") {
+    qgemv_set_f16(value != 0);
+    return HIGGS_OK;
+  }
+  return fail(HIGGS_ERR_INVALID_ARG, "higgs_set_option: unknown option '" + n + "'");
+}
 
 extern "C" int higgs_version(void) { return 1; }
 

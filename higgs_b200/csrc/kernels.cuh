@@ -28,7 +28,15 @@ struct QLinArgs {
   uint16_t* y;
   float* y_f32;
   const uint16_t* residual;
+  // optional fused RMSNorm of x (ring GEMV only): x is the residual stream h
+  const uint16_t* norm_w;
+  float eps;
 };
+
+// W4 GEMV with per-warp cp.async rings (any M, 32 rows per pass; norm_w needs
+// qgemv_ring_can_fuse_norm(M, K)).
+cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st);
+bool qgemv_ring_can_fuse_norm(int M, int K);
 
 // M may exceed 32 (processed in 32-row passes); K % 256 == 0, N % 16 == 0.
 cudaError_t launch_qlinear(const QLinArgs& a, int epi, cudaStream_t st);

@@ -82,11 +82,10 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
-  size_t h, x, qkv, q, attn, act, xl, logits, sk, sk_bytes, attn_ws, total;
+  size_t h, x, qkv, q, attn, act, xl, logits, attn_ws, total;
 };
 
-// Decode batches of <= 8 rows use the stream-K GEMV with the RMSNorms fused.
-bool use_sk(int T) { return T <= 8; }
+
 
 WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, bool last_only) {
   const size_t T = (size_t)B * Lq;
@@ -107,18 +106,6 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
   L.act = take(T * (size_t)c.intermediate * 2);
   L.xl = take(rows_lm * c.hidden * 2);
   L.logits = take(rows_lm * (size_t)c.vocab * 4);
-  L.sk_bytes = 0;
-  if (use_sk((int)T)) {
-    const int M = (int)T;
-    const int qkv_tiles = (c.heads + 2 * c.kv_heads) * D / 16;
-    size_t m = qgemv_sk_workspace(M, c.hidden, qkv_tiles);
-    m = std::max(m, qgemv_sk_workspace(M, c.heads * D, c.hidden / 16));
-    m = std::max(m, qgemv_sk_workspace(M, c.hidden, 2 * c.intermediate / 16));
-    m = std::max(m, qgemv_sk_workspace(M, c.intermediate, c.hidden / 16));
-    m = std::max(m, qgemv_sk_workspace(M, c.hidden, c.vocab / 16));
-    L.sk_bytes = m;
-  }
-  L.sk = take(L.sk_bytes);
   const size_t aws = higgs_paged_attention_workspace_size(B, Lq, c.heads, c.kv_heads, D, max_seq_len);
   L.attn_ws = take(aws);
   L.total = off;
@@ -162,23 +149,6 @@ int get_vec(higgs_model* m, const std::string& name, int n, const uint16_t*& out
   return HIGGS_OK;
 }
 
-cudaError_t qlin(const QW& w, const uint16_t* x, int M, uint16_t* y, float* yf,
-                 const uint16_t* residual, cudaStream_t st) {
-  QLinArgs a{};
-  a.x = x;
-  a.M = M;
-  a.K = w.K;
-  a.N = w.N;
-  a.w = w.w;
-  a.s = w.s;
-  a.b = w.b;
-  a.nseg = 1;
-  a.y = y;
-  a.y_f32 = yf;
-  a.residual = residual;
-  return launch_qlinear(a, EPI_STORE, st);
-}
-
 int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   const higgs_model_config& c = m->cfg;
   const int B = f->B, Lq = f->Lq;
@@ -206,63 +176,40 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   const int64_t tq_layer_bytes = m->num_pages * c.kv_heads * HIGGS_PAGE_SIZE * 64;
   const int64_t tq_layer_scales = m->num_pages * c.kv_heads * HIGGS_PAGE_SIZE;
 
-  const bool sk = use_sk(T);
-  void* skws = ws + L.sk;
-  auto sk_lin = [&](const QW& w, const uint16_t* xin, const uint16_t* norm, uint16_t* y, float* yf,
-                    const uint16_t* res) {
-    SkArgs a{};
+  // decode batches fuse each RMSNorm into the GEMV that consumes it
+  const bool fuse = qgemv_ring_can_fuse_norm(T, H);
+  auto lin = [&](const QW& w, const uint16_t* xin, const uint16_t* norm, uint16_t* y, float* yf,
+                 const uint16_t* res) {
+    QLinArgs a{};
     a.x = xin;
     a.norm_w = norm;
     a.eps = c.rms_eps;
     a.M = T;
     a.K = w.K;
     a.N = w.N;
-    a.n_tiles = w.N / 16;
+    a.w = w.w;
+    a.s = w.s;
+    a.b = w.b;
     a.nseg = 1;
-    a.seg_end[0] = w.N;
-    a.wseg[0] = w.w;
-    a.sseg[0] = w.s;
-    a.bseg[0] = w.b;
     a.y = y;
     a.y_f32 = yf;
     a.residual = res;
-    return launch_qgemv_sk(a, skws, st);
+    return launch_qgemv_ring(a, EPI_STORE, st);
   };
   int rc = higgs_embed_gather_w4(m->ctx, f->tokens, T, m->embed.w, m->embed.s, m->embed.b, c.vocab,
                                  H, h, st);
   if (rc) return rc;
   for (int li = 0; li < n_layers; ++li) {
     const LayerW& Lw = m->layers[li];
-    if (sk) {
-      SkArgs a{};
-      a.x = h;
-      a.norm_w = Lw.ln_in;
-      a.eps = c.rms_eps;
-      a.M = T;
-      a.K = H;
-      a.N = Lw.q.N + Lw.k.N + Lw.v.N;
-      a.n_tiles = a.N / 16;
-      a.nseg = 3;
-      a.seg_end[0] = Lw.q.N;
-      a.seg_end[1] = Lw.q.N + Lw.k.N;
-      a.seg_end[2] = a.N;
-      a.wseg[0] = Lw.q.w;
-      a.sseg[0] = Lw.q.s;
-      a.bseg[0] = Lw.q.b;
-      a.wseg[1] = Lw.k.w;
-      a.sseg[1] = Lw.k.s;
-      a.bseg[1] = Lw.k.b;
-      a.wseg[2] = Lw.v.w;
-      a.sseg[2] = Lw.v.s;
-      a.bseg[2] = Lw.v.b;
-      a.y = qkv;
-      HG_CUDA(launch_qgemv_sk(a, skws, st));
-    } else {
-    rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_in, c.rms_eps, x, nullptr, st);
-    if (rc) return rc;
     {
+      if (!fuse) {
+        rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_in, c.rms_eps, x, nullptr, st);
+        if (rc) return rc;
+      }
       QLinArgs a{};
-      a.x = x;
+      a.x = fuse ? h : x;
+      a.norm_w = fuse ? Lw.ln_in : nullptr;
+      a.eps = c.rms_eps;
       a.M = T;
       a.K = H;
       a.N = Lw.q.N + Lw.k.N + Lw.v.N;
@@ -283,8 +230,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.sseg[2] = Lw.v.s;
       a.bseg[2] = Lw.v.b;
       a.y = qkv;
-      HG_CUDA(launch_qlinear(a, EPI_STORE, st));
-    }
+      HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
     }
     if (tq) {
       rc = higgs_qknorm_rope_kv_write_tq4(
@@ -302,6 +248,16 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
           HIGGS_PAGE_SIZE * 64, f->block_table, f->max_blocks, f->seq_lens, f->max_seq_len,
           m->signs, scale, attn, aws, aws_bytes, st);
       if (rc) return rc;
+    } else if ((c.heads / c.kv_heads) * Lq <= 32) {
+      // decode / verify: norm + RoPE + append + attention in one kernel
+      uint16_t* kc = (uint16_t*)m->k_pool + li * kv_layer_elems;
+      uint16_t* vc = (uint16_t*)m->v_pool + li * kv_layer_elems;
+      rc = higgs_fused_attention(m->ctx, qkv, B, Lq, c.heads, c.kv_heads, D, Lw.qn, Lw.kn,
+                                 c.rms_eps, f->positions, m->inv_freq, f->slot_mapping, kc, vc,
+                                 (int64_t)c.kv_heads * HIGGS_PAGE_SIZE * D,
+                                 (int64_t)HIGGS_PAGE_SIZE * D, f->block_table, f->max_blocks,
+                                 f->seq_lens, f->max_seq_len, scale, attn, aws, aws_bytes, st);
+      if (rc) return rc;
     } else {
       uint16_t* kc = (uint16_t*)m->k_pool + li * kv_layer_elems;
       uint16_t* vc = (uint16_t*)m->v_pool + li * kv_layer_elems;
@@ -317,35 +273,16 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       if (rc) return rc;
     }
     // h = h + o_proj(attn)   (in place: each element read then written by one thread)
-    if (sk) {
-      HG_CUDA(sk_lin(Lw.o, attn, nullptr, h, nullptr, h));
-      SkArgs a{};
-      a.x = h;
-      a.norm_w = Lw.ln_post;
-      a.eps = c.rms_eps;
-      a.M = T;
-      a.K = H;
-      a.N = c.intermediate;
-      a.n_tiles = 2 * c.intermediate / 16;
-      a.swiglu = 1;
-      a.nseg = 2;
-      a.wseg[0] = Lw.gate.w;
-      a.sseg[0] = Lw.gate.s;
-      a.bseg[0] = Lw.gate.b;
-      a.wseg[1] = Lw.up.w;
-      a.sseg[1] = Lw.up.s;
-      a.bseg[1] = Lw.up.b;
-      a.y = act;
-      HG_CUDA(launch_qgemv_sk(a, skws, st));
-      HG_CUDA(sk_lin(Lw.down, act, nullptr, h, nullptr, h));
-      continue;
-    }
-    HG_CUDA(qlin(Lw.o, attn, T, h, nullptr, h, st));
-    rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_post, c.rms_eps, x, nullptr, st);
-    if (rc) return rc;
+    HG_CUDA(lin(Lw.o, attn, nullptr, h, nullptr, h));
     {
+      if (!fuse) {
+        rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_post, c.rms_eps, x, nullptr, st);
+        if (rc) return rc;
+      }
       QLinArgs a{};
-      a.x = x;
+      a.x = fuse ? h : x;
+      a.norm_w = fuse ? Lw.ln_post : nullptr;
+      a.eps = c.rms_eps;
       a.M = T;
       a.K = H;
       a.N = c.intermediate;
@@ -357,14 +294,14 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.b2 = Lw.up.b;
       a.nseg = 1;
       a.y = act;
-      HG_CUDA(launch_qlinear(a, EPI_SWIGLU, st));
+      HG_CUDA(launch_qgemv_ring(a, EPI_SWIGLU, st));
     }
-    HG_CUDA(qlin(Lw.down, act, T, h, nullptr, h, st));
+    HG_CUDA(lin(Lw.down, act, nullptr, h, nullptr, h));
   }
   // final norm (+ last-token selection) and LM head
   const int rows_lm = f->last_only ? B : T;
-  if (sk && (Lq == 1 || !f->last_only) && !f->hidden_out) {
-    if (f->logits || f->argmax) HG_CUDA(sk_lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
+  if (fuse && (Lq == 1 || !f->last_only) && !f->hidden_out) {
+    if (f->logits || f->argmax) HG_CUDA(lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
     if (f->argmax) {
       rc = higgs_argmax(m->ctx, logits, rows_lm, c.vocab, f->argmax, st);
       if (rc) return rc;
@@ -379,7 +316,17 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   }
   if (rc) return rc;
   if (f->logits || f->argmax) {
-    HG_CUDA(qlin(m->head, xl, rows_lm, nullptr, logits, nullptr, st));
+    QLinArgs a{};
+    a.x = xl;
+    a.M = rows_lm;
+    a.K = H;
+    a.N = m->head.N;
+    a.w = m->head.w;
+    a.s = m->head.s;
+    a.b = m->head.b;
+    a.nseg = 1;
+    a.y_f32 = logits;
+    HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
   }
   if (f->argmax) {
     rc = higgs_argmax(m->ctx, logits, rows_lm, c.vocab, f->argmax, st);

@@ -448,7 +448,7 @@ extern "C" int higgs_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, 
   a.y = (uint16_t*)y;
   a.y_f32 = y_f32;
   a.residual = (const uint16_t*)residual;
-  HG_CUDA(launch_qlinear_epi<EPI_STORE>(a, (cudaStream_t)stream));
+  HG_CUDA(launch_qgemv_ring(a, EPI_STORE, (cudaStream_t)stream));
   return HIGGS_OK;
 }
 
@@ -475,6 +475,6 @@ extern "C" int higgs_qlinear_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M
   a.s2 = (const uint16_t*)s_up;
   a.b2 = (const uint16_t*)b_up;
   a.y = (uint16_t*)y;
-  HG_CUDA(launch_qlinear_epi<EPI_SWIGLU>(a, (cudaStream_t)stream));
+  HG_CUDA(launch_qgemv_ring(a, EPI_SWIGLU, (cudaStream_t)stream));
   return HIGGS_OK;
 }

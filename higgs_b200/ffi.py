@@ -24,6 +24,7 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_destroy": (I, [P]),
     "higgs_last_error": (ctypes.c_char_p, []),
     "higgs_version": (I, []),
+    "higgs_set_option": (I, [ctypes.c_char_p, I]),
     "higgs_w4_dequantize": (I, [P, P, P, P, I, I, P, P]),
     "higgs_w4_quantize": (I, [P, P, I64, I, P, P, P, P]),
     "higgs_embed_gather_w4": (I, [P, P, I, P, P, P, I, I, P, P]),
@@ -37,6 +38,8 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_qknorm_rope_kv_write": (I, [P, P, I, I, I, I, P, P, F, P, P, P, P, P, I64, I64, P, P]),
     "higgs_paged_attention_workspace_size": (SZ, [I, I, I, I, I, I]),
     "higgs_paged_attention": (I, [P, P, I, I, I, I, I, P, P, I64, I64, P, I, P, I, F, P, P, SZ, P]),
+    "higgs_fused_attention_workspace_size": (SZ, [I, I, I, I, I, I]),
+    "higgs_fused_attention": (I, [P, P, I, I, I, I, I, P, P, F, P, P, P, P, P, I64, I64, P, I, P, I, F, P, P, SZ, P]),
     "higgs_paged_attention_noalloc": (I, [P, P, I, I, I, I, I, P, P, I64, I64, P, I, P, I, F, P, P]),
     "higgs_tq4_encode": (I, [P, P, I64, P, P, P, P]),
     "higgs_qknorm_rope_kv_write_tq4": (I, [P, P, I, I, I, P, P, F, P, P, P, P, P, P, P, P, I64, I64, P, P]),

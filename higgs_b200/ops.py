@@ -228,6 +228,27 @@ def paged_attention(q, k_cache, v_cache, block_table, seq_lens, max_seq_len: int
     return out
 
 
+def fused_attention(qkv, Hq: int, Hkv: int, D: int, q_norm_w, k_norm_w, eps: float, positions,
+                    inv_freq, slot_mapping, k_cache, v_cache, block_table, seq_lens,
+                    max_seq_len: int, Lq: int = 1, scale=None, workspace=None):
+    """Attention::forward from q|k|v to the output (transformer.rs:246-294) in one kernel:
+    q/k norm, RoPE, cache append at slot_mapping, paged SDPA.  qkv bf16 [B*Lq, (Hq+2Hkv)*D]."""
+    T = qkv.shape[0]
+    B = T // Lq
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if workspace is None:
+        n = ffi.load().higgs_fused_attention_workspace_size(B, Lq, Hq, Hkv, D, max_seq_len)
+        workspace = torch.zeros(max(n, 4096), dtype=torch.uint8, device=qkv.device)
+    out = torch.empty(B, Lq, Hq, D, dtype=torch.bfloat16, device=qkv.device)
+    ffi.call("higgs_fused_attention", _ctx(qkv), _p(qkv), B, Lq, Hq, Hkv, D, _p(q_norm_w),
+             _p(k_norm_w), float(eps), _p(positions), _p(inv_freq), _p(slot_mapping), _p(k_cache),
+             _p(v_cache), Hkv * PAGE * D, PAGE * D, _p(block_table), block_table.shape[1],
+             _p(seq_lens), int(max_seq_len), float(scale), _p(out), _p(workspace),
+             workspace.numel(), _st(qkv.device))
+    return out
+
+
 def tq4_encode(x, signs):
     """TurboQuant encode of bf16 [n, 128] -> (codes u8 [n, 64], scales fp16 [n])."""
     n = x.numel() // 128

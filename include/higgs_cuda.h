@@ -70,6 +70,12 @@ int higgs_destroy(higgs_ctx* ctx);
 const char* higgs_last_error(void);
 int higgs_version(void);
 
+/* Process-wide tuning switches (no reference counterpart).  "gemv_f16" (0/1,
+ * default 0): decode GEMVs with x staged in shared memory feed the tensor cores
+ * fp16 operands (x scaled per token by a power of two, exact for bf16 inputs)
+ * instead of bf16 ones.  Unknown names return HIGGS_ERR_INVALID_ARG. */
+int higgs_set_option(const char* name, int value);
+
 /* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
 
 /* ops::dequantize (crates/higgs-models/src/qwen3_next.rs:249-256):
@@ -200,6 +206,24 @@ int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int Lq, int Hq, 
                           int64_t head_stride, const int32_t* block_table, int max_blocks,
                           const int32_t* seq_lens, int max_seq_len, float scale, void* out,
                           void* workspace, size_t workspace_bytes, void* stream);
+
+/* Attention::forward from the q|k|v projection to the attention output
+ * (crates/higgs-models/src/transformer.rs:246-294) in one kernel: q/k head
+ * RMSNorm (when the weights are given), RoPE at positions[t], the cache append
+ * of the new tokens at slot_mapping[t] (cache.rs:236-311), and the paged SDPA
+ * of higgs_paged_attention over the updated cache.  qkv bf16
+ * [B * Lq, (Hq + 2 Hkv) * D]; out bf16 [B, Lq, Hq, D]; needs (Hq / Hkv) * Lq <= 32
+ * (decode and speculative verify).  Workspace rules as higgs_paged_attention,
+ * sized by higgs_fused_attention_workspace_size. */
+size_t higgs_fused_attention_workspace_size(int B, int Lq, int Hq, int Hkv, int D,
+                                            int max_seq_len);
+int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq, int Hkv, int D,
+                          const void* q_norm_w, const void* k_norm_w, float eps,
+                          const int32_t* positions, const float* inv_freq,
+                          const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                          int64_t page_stride, int64_t head_stride, const int32_t* block_table,
+                          int max_blocks, const int32_t* seq_lens, int max_seq_len, float scale,
+                          void* out, void* workspace, size_t workspace_bytes, void* stream);
 
 /* higgs_paged_attention without a workspace argument, for callers that cannot
  * allocate device memory on their serving path (a host that owns a fixed

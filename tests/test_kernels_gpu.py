@@ -478,3 +478,48 @@ def test_rmsnorm_gate_up_swiglu_sk(M, norm):
                                                 t(qu.view(np.int32)), bf(su), bf(bu)))
     np.testing.assert_allclose(orc.bf16_to_f32(got), orc.bf16_to_f32(ref), atol=3e-3, rtol=3e-2)
     assert np.percentile(bf_ulps(got, ref), 99) <= 3
+
+
+# ---- fused decode attention (norm + RoPE + append + SDPA) --------------------------------
+
+@pytest.mark.parametrize("B,Lq,Hq,Hkv,D,qknorm,lens", [
+    (1, 1, 32, 8, 128, True, [2048]),
+    (1, 1, 32, 8, 128, True, [17]),
+    (3, 1, 16, 8, 128, True, [1, 16, 300]),
+    (2, 1, 32, 8, 64, False, [129, 4000]),
+    (2, 6, 32, 8, 128, True, [700, 6]),
+    (1, 2, 32, 4, 128, True, [33]),
+])
+def test_fused_attention_equals_unfused(B, Lq, Hq, Hkv, D, qknorm, lens):
+    rng = np.random.default_rng(B * 100 + Lq + D + sum(lens))
+    T = B * Lq
+    nh = Hq + 2 * Hkv
+    qkv = orc.f32_to_bf16(rng.normal(size=(T, nh * D)))
+    qn = orc.f32_to_bf16(rng.uniform(0.5, 1.5, size=D)) if qknorm else None
+    kn = orc.f32_to_bf16(rng.uniform(0.5, 1.5, size=D)) if qknorm else None
+    inv = orc.rope_inv_freq(D, 1000000.0)
+    maxb = max((n + 15) // 16 for n in lens)
+    P = B * maxb + 2
+    bt = rng.permutation(P)[:B * maxb].reshape(B, maxb).astype(np.int32)
+    pos = np.array([[n - Lq + tq for tq in range(Lq)] for n in lens], np.int32).reshape(-1)
+    slots = np.array([bt[b, p // 16] * 16 + p % 16 for b in range(B) for p in pos[b * Lq:(b + 1) * Lq]],
+                     np.int64)
+    kc0 = orc.f32_to_bf16(rng.normal(size=(P, Hkv, 16, D)))
+    vc0 = orc.f32_to_bf16(rng.normal(size=(P, Hkv, 16, D)))
+    sl = np.array(lens, np.int32)
+    o = ops()
+    # unfused: kv write then attention
+    kc1, vc1 = bf(kc0), bf(vc0)
+    q = o.qknorm_rope_kv_write(bf(qkv), Hq, Hkv, D, None if qn is None else bf(qn),
+                               None if kn is None else bf(kn), 1e-6, t(pos), t(inv), t(slots), kc1, vc1)
+    ref = o.paged_attention(q.view(B, Lq, Hq, D), kc1, vc1, t(bt), t(sl), max(lens))
+    # fused
+    kc2, vc2 = bf(kc0), bf(vc0)
+    got = o.fused_attention(bf(qkv), Hq, Hkv, D, None if qn is None else bf(qn),
+                            None if kn is None else bf(kn), 1e-6, t(pos), t(inv), t(slots), kc2, vc2,
+                            t(bt), t(sl), max(lens), Lq=Lq)
+    assert torch.equal(kc1, kc2) and torch.equal(vc1, vc2)  # identical cache append
+    np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), atol=1e-2, rtol=1e-2)
+    # and against the oracle on the updated cache
+    ref_o = orc.paged_attention(to_np_bf(q).reshape(B, Lq, Hq, D), to_np_bf(kc2), to_np_bf(vc2), bt, sl)
+    np.testing.assert_allclose(got.float().cpu().numpy(), orc.bf16_to_f32(ref_o), atol=1e-2, rtol=1e-2)
