@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--batches", default=",".join(map(str, BATCHES)))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--quick", action="store_true", help="headline B only, no kernel table (profiling)")
+    ap.add_argument("--configs", default="c1,c2,c3,c4,c5",
+                    help="other BASELINE configs to run at N=1 (comma list, '' for none)")
+    ap.add_argument("--kernel-case", default=None,
+                    help="run one small kernel case for ncu: qkv|o_proj|gate_up_swiglu|down|lm_head|attention|argmax")
     return ap.parse_args()
 
 
@@ -160,7 +164,7 @@ def setup_model(args_m, batches, ctx, total_steps, device):
 
     weights = synth_weights_device(args_m, seed=0, device=device)
     per_seq_pages = math.ceil((ctx + total_steps + 2) / 16)
-    num_pages = max(batches) * per_seq_pages + 16
+    num_pages = max(max(batches), 4) * per_seq_pages + 16  # >= the 4 sequences of C3
     model = Model(args_m, weights, num_pages=num_pages, device=device)
     # synthetic KV context (random bf16; decode cost does not depend on the values)
     g = torch.Generator(device=device)
@@ -235,53 +239,134 @@ def time_e2e(eng, seqs, steps, warmup):
     return (t1 - t0) * 1e3
 
 
-def gemv_table(model, steps=20):
-    """Each W4 GEMV shape of one decode step timed alone (CUDA events, L2 flushed between)."""
+def graph_time(fns, reps=10):
+    """Seconds per replay of a CUDA graph holding fns() back to back (PDL edges kept)."""
+    import torch
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for f in fns:
+            f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for f in fns:
+            f()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    e0.record(cur)
+    for _ in range(reps):
+        g.replay()
+    e1.record(cur)
+    e1.synchronize()
+    return e0.elapsed_time(e1) / reps * 1e-3
+
+
+def gemv_shapes(model):
+    """(name, per-layer weight triples, K, launches per step) of every W4 GEMV of a decode step."""
+    import torch
+    a = model.args
+    w = model.weights
+    L = a.num_hidden_layers
+    H, D = a.hidden_size, a.head_dim
+
+    def trip(name):
+        return (w[name + ".weight"], w[name + ".scales"], w[name + ".biases"])
+
+    lay = [f"model.layers.{i}." for i in range(L)]
+    qkv = [tuple(torch.cat([trip(p + "self_attn." + n)[k] for n in ("q_proj", "k_proj", "v_proj")])
+                 for k in range(3)) for p in lay]
+    head = "model.embed_tokens" if a.tie_word_embeddings else "lm_head"
+    return [("qkv", qkv, H, L),
+            ("o_proj", [trip(p + "self_attn.o_proj") for p in lay], a.num_attention_heads * D, L),
+            ("gate_up_swiglu", [trip(p + "mlp.gate_proj") + trip(p + "mlp.up_proj") for p in lay], H, L),
+            ("down", [trip(p + "mlp.down_proj") for p in lay], a.intermediate_size, L),
+            ("lm_head", [trip(head)] * 4, H, 1)]
+
+
+def gemv_roofline(model, M=1):
+    """Each W4 GEMV shape of one decode step timed inside a CUDA graph of back-to-back
+    launches over every layer's own weights (so no launch finds its weights in L2),
+    exactly as the step runs them; per-launch time = graph time / launches."""
     import torch
 
     from higgs_b200 import ops
-    a = model.args
-    H, D = a.hidden_size, a.head_dim
-    w = model.weights
-    p = "model.layers.0."
-    shapes = [
-        ("qkv", [p + "self_attn.q_proj", p + "self_attn.k_proj", p + "self_attn.v_proj"], H, a.num_hidden_layers),
-        ("o_proj", [p + "self_attn.o_proj"], a.num_attention_heads * D, a.num_hidden_layers),
-        ("gate_up_swiglu", [p + "mlp.gate_proj", p + "mlp.up_proj"], H, a.num_hidden_layers),
-        ("down", [p + "mlp.down_proj"], a.intermediate_size, a.num_hidden_layers),
-        ("lm_head", ["model.embed_tokens" if a.tie_word_embeddings else "lm_head"], H, 1),
-    ]
-    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=model.device)  # 256 MB > L2
     rows = []
-    for name, tensors, K, count in shapes:
-        ws = [(w[t + ".weight"], w[t + ".scales"], w[t + ".biases"]) for t in tensors]
-        x = torch.randn(1, K, device=model.device).to(torch.bfloat16)
-        nbytes = sum(q.numel() * 4 + s.numel() * 2 + b.numel() * 2 for q, s, b in ws) + K * 2
+    for name, ws, K, count in gemv_shapes(model):
+        x = torch.randn(M, K, device=model.device).to(torch.bfloat16)
+        N = ws[0][0].shape[0]
+        wbytes = sum(t.numel() * t.element_size() for t in ws[0])
         if name == "gate_up_swiglu":
-            fn = lambda: ops.gate_up_swiglu(x, *ws[0], *ws[1])  # noqa: E731
-            nbytes += ws[0][0].shape[0] * 2
-        elif name == "qkv":
-            wq = [torch.cat([t[i] for t in ws]) for i in range(3)]
-            fn = lambda: ops.quantized_matmul(x, *wq)  # noqa: E731
-            nbytes += wq[0].shape[0] * 2
+            fns = [lambda w=w: ops.gate_up_swiglu(x, *w) for w in ws]
+            nbytes = wbytes + M * K * 2 + M * N * 2
         else:
-            fn = lambda: ops.quantized_matmul(x, *ws[0], out_f32=(name == "lm_head"))  # noqa: E731
-            nbytes += ws[0][0].shape[0] * (4 if name == "lm_head" else 2)
-        for _ in range(3):
-            fn()
-        ts = []
-        for _ in range(steps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            fn()
-            e1.record()
-            e1.synchronize()
-            ts.append(e0.elapsed_time(e1))
-        us = statistics.median(ts) * 1e3
+            f32 = name == "lm_head"
+            fns = [lambda w=w, f=f32: ops.quantized_matmul(x, *w, out_f32=f) for w in ws]
+            nbytes = wbytes + M * K * 2 + M * N * (4 if f32 else 2)
+        us = graph_time(fns) / len(fns) * 1e6
         rows.append({"shape": name, "launches_per_step": count, "bytes": int(nbytes), "us": round(us, 2),
                      "gbs": round(nbytes / us / 1e3, 1)})
+        del fns
     return rows
+
+
+def kernel_case(opt):
+    """Small standalone launches of one hot kernel, for ncu captures (-k / -c)."""
+    import torch
+
+    from higgs_b200 import ops
+    from higgs_b200.model import PRESETS
+    dev = "cuda:0"
+    a = PRESETS[MODEL]
+    H = a.hidden_size
+    torch.manual_seed(0)
+
+    def mk(N, K):
+        return (torch.randint(-2**31, 2**31 - 1, (N, K // 8), dtype=torch.int32, device=dev),
+                (torch.rand(N, K // 64, device=dev) * 0.01).to(torch.bfloat16),
+                (torch.randn(N, K // 64, device=dev) * 0.01).to(torch.bfloat16))
+    case = opt.kernel_case
+    if case in ("qkv", "o_proj", "down", "lm_head", "gate_up_swiglu"):
+        K, N = {"qkv": (H, (a.num_attention_heads + 2 * a.num_key_value_heads) * a.head_dim),
+                "o_proj": (a.num_attention_heads * a.head_dim, H), "down": (a.intermediate_size, H),
+                "lm_head": (H, a.vocab_size), "gate_up_swiglu": (H, a.intermediate_size)}[case]
+        reps = 2 if case == "lm_head" else 8  # > 126 MB of distinct weights in flight
+        ws = [mk(N, K) + (mk(N, K) if case == "gate_up_swiglu" else ()) for _ in range(reps)]
+        x = torch.randn(1, K, device=dev).to(torch.bfloat16)
+        for it in range(3):
+            for w in ws:
+                if case == "gate_up_swiglu":
+                    ops.gate_up_swiglu(x, *w)
+                else:
+                    ops.quantized_matmul(x, *w, out_f32=case == "lm_head")
+    elif case == "attention":
+        B, Hq, Hkv, D, L = 1, a.num_attention_heads, a.num_key_value_heads, a.head_dim, opt.ctx
+        P = L // 16 + 1
+        nh = Hq + 2 * Hkv
+        caches = [(torch.randn(P, Hkv, 16, D, device=dev).to(torch.bfloat16),
+                   torch.randn(P, Hkv, 16, D, device=dev).to(torch.bfloat16)) for _ in range(8)]
+        qkv = torch.randn(1, nh * D, device=dev).to(torch.bfloat16)
+        qn = torch.ones(D, device=dev).to(torch.bfloat16)
+        inv = ops.rope_inv_freq(D, a.rope_theta, dev)
+        pos = torch.tensor([L - 1], dtype=torch.int32, device=dev)
+        slots = torch.tensor([L - 1], dtype=torch.int64, device=dev)
+        bt = torch.arange(P, dtype=torch.int32, device=dev).view(1, P)
+        sl = torch.tensor([L], dtype=torch.int32, device=dev)
+        for it in range(3):
+            for kc, vc in caches:
+                ops.fused_attention(qkv, Hq, Hkv, D, qn, qn, a.rms_norm_eps, pos, inv, slots, kc, vc, bt,
+                                    sl, L)
+    elif case == "argmax":
+        lg = torch.randn(1, a.vocab_size, device=dev)
+        for it in range(3):
+            ops.argmax(lg)
+    else:
+        raise SystemExit(f"unknown --kernel-case {case}")
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel_case": case, "ok": True}))
 
 
 def oracle_step_time(model_args, ctx, budget_s=20.0):
@@ -341,6 +426,174 @@ def oracle_step_time(model_args, ctx, budget_s=20.0):
     return full, desc
 
 
+# ---------------------------------------------------------------------------------------------
+# the other BASELINE configurations (reported under "by_config"; the headline is C-headline)
+# ---------------------------------------------------------------------------------------------
+def _synth_model(args_m, device, num_pages, kv_mode="bf16", weights=None):
+    from higgs_b200.model import Model, synth_weights_device
+    w = weights if weights is not None else synth_weights_device(args_m, seed=0, device=device)
+    return Model(args_m, w, num_pages=num_pages, kv_mode=kv_mode, device=device), w
+
+
+def _fill_kv(model, seed=2):
+    import torch
+    g = torch.Generator(device=model.device)
+    g.manual_seed(seed)
+    if model.kv_mode == "tq4":
+        for pool in (model.k_pool, model.v_pool):
+            for li in range(pool.shape[0]):
+                pool[li].copy_(torch.randint(0, 256, pool[li].shape, generator=g, device=model.device,
+                                             dtype=torch.int32).to(torch.uint8))
+        for sc in (model.k_scales, model.v_scales):
+            sc.fill_(0.05)
+    else:
+        for pool in (model.k_pool, model.v_pool):
+            for li in range(pool.shape[0]):
+                pool[li].copy_(torch.randn(pool[li].shape, generator=g, device=model.device).to(torch.bfloat16))
+
+
+def _entry(args_m, B, ctx, ms_step, hbm, kv_mode="bf16", experts_touched=0.0, extra=None):
+    w_bytes = args_m.weight_bytes_per_step(experts_touched)
+    kv = B * ctx * args_m.kv_bytes_per_token(kv_mode)
+    e = {"tok_s": round(B * 1e3 / ms_step, 1), "ms_per_step": round(ms_step, 4),
+         "step_bytes": int(w_bytes + kv),
+         "step_hbm_frac": round((w_bytes + kv) / (ms_step / 1e3) / 1e9 / hbm, 4)}
+    if extra:
+        e.update(extra)
+    return e
+
+
+def config_c1(device, hbm, steps):
+    """C1: Llama-3.2-1B arch, B=1, 128-token prompt, greedy decode (device-resident replays)."""
+    from higgs_b200.engine import Engine, Sequence
+    from higgs_b200.model import PRESETS
+    a = PRESETS["llama-3.2-1b"]
+    model, _ = _synth_model(a, device, num_pages=64)
+    eng = Engine(model, max_seq_len=512, prefix_entries=0)
+    rng = np.random.default_rng(1)
+    seq = eng.prefill(rng.integers(0, a.vocab_size, 128).astype(np.int32), use_prefix=False)
+    ms, _ = time_device_resident(eng, [seq], steps, 4)
+    return _entry(a, 1, 128 + steps // 2, ms / steps, hbm,
+                  extra={"workload": "llama-3.2-1b B=1 prompt 128, greedy"})
+
+
+def config_c2(device, hbm, steps):
+    """C2: Qwen3-1.7B arch, 8 sequences of 512-token prompts sharing a 256-token prefix (radix
+    cache), then greedy decode of all 8 together through the public engine API."""
+    import torch
+
+    from higgs_b200.engine import Engine
+    from higgs_b200.model import PRESETS
+    a = PRESETS["qwen3-1.7b"]
+    model, _ = _synth_model(a, device, num_pages=8 * 48 + 64)
+    eng = Engine(model, max_seq_len=768, prefix_entries=16)
+    rng = np.random.default_rng(2)
+    shared = rng.integers(0, a.vocab_size, 256).astype(np.int32)
+    prompts = [np.concatenate([shared, rng.integers(0, a.vocab_size, 256).astype(np.int32)])
+               for _ in range(8)]
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    seqs = [eng.prefill(p_, use_prefix=True) for p_ in prompts]
+    torch.cuda.synchronize()
+    t_pre = time.perf_counter() - t0
+    hits = [s.prefix_hit for s in seqs]
+    eng.decode_steps(seqs, 4)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    eng.decode_steps(seqs, steps)
+    torch.cuda.synchronize()
+    ms = (time.perf_counter() - t0) * 1e3
+    return _entry(a, 8, 512 + steps // 2, ms / steps, hbm,
+                  extra={"workload": "qwen3-1.7b 8 seqs, 512-token prompts (256 shared), greedy; "
+                                     "e2e through Engine.decode_steps",
+                         "prefill_s": round(t_pre, 3), "prefix_hit_tokens": hits})
+
+
+def config_c3(model, eng, Sequence, device, hbm, steps, ctx):
+    """C3: self-speculative decoding on the Qwen3-8B model: draft = first 9 layers + the shared
+    head, k=5, one batched verify of 6 tokens, rejection sampling at T=0.7 (uniforms seed 3)."""
+    import torch
+
+    from higgs_b200.engine import SpecDecoder
+    B, k = 4, 5
+    seqs = make_seqs(eng, Sequence, B, ctx, model.args.vocab_size, seed=21)
+    sd = SpecDecoder(eng, B, k=k, draft_layers=9, temperature=0.7)
+    rng = np.random.default_rng(3)
+    sd.steps(seqs, 3, rng)
+    n0 = sum(len(s.generated) for s in seqs)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    acc = sd.steps(seqs, steps, rng)
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    toks = sum(len(s.generated) for s in seqs) - n0
+    for s in seqs:
+        eng.release(s)
+    del sd
+    return {"workload": "qwen3-8b self-spec B=4 ctx 2048, draft 9 layers, k=5, T=0.7; e2e",
+            "tok_s": round(toks / dt, 1), "ms_per_spec_step": round(dt * 1e3 / steps, 3),
+            "accepted_per_step_mean": round(float(acc.mean()), 3),
+            "tokens_per_step_mean": round(float(acc.mean()) + 1.0, 3)}
+
+
+def config_c4(device, hbm, steps):
+    """C4: Qwen3-30B-A3B arch (128 experts, top-8), B=32 decode at ctx 4096, one GPU."""
+    import torch
+
+    from higgs_b200.engine import Engine, Sequence
+    from higgs_b200.model import PRESETS
+    a = PRESETS["qwen3-30b-a3b"]
+    B, ctx = 32, 4096
+    pages = B * math.ceil((ctx + steps + 16) / 16) + 16
+    model, w = _synth_model(a, device, num_pages=pages)
+    _fill_kv(model)
+    eng = Engine(model, max_seq_len=ctx + steps + 16, prefix_entries=0)
+    seqs = make_seqs(eng, Sequence, B, ctx, a.vocab_size, seed=31)
+    ms, _ = time_device_resident(eng, seqs, steps, 4)
+    touched = 128 * (1 - (1 - 8 / 128) ** B)  # expected distinct experts per layer
+    out = _entry(a, B, ctx + steps // 2, ms / steps, hbm, experts_touched=touched,
+                 extra={"workload": "qwen3-30b-a3b B=32 ctx 4096 greedy (router logits N(0,1))",
+                        "experts_touched_per_layer": round(touched, 1)})
+    del eng, model, w
+    torch.cuda.empty_cache()
+    return out
+
+
+def config_c5(weights, device, hbm, steps):
+    """C5: Qwen3-8B with TurboQuant 4-bit KV pages, B=16 at ctx 32768."""
+    import torch
+
+    from higgs_b200.engine import Engine, Sequence
+    from higgs_b200.model import PRESETS
+    a = PRESETS[MODEL]
+    B, ctx = 16, 32768
+    pages = B * math.ceil((ctx + steps + 16) / 16) + 16
+    model, _ = _synth_model(a, device, num_pages=pages, kv_mode="tq4", weights=weights)
+    _fill_kv(model)
+    eng = Engine(model, max_seq_len=ctx + steps + 16, prefix_entries=0)
+    seqs = make_seqs(eng, Sequence, B, ctx, a.vocab_size, seed=51)
+    ms, _ = time_device_resident(eng, seqs, steps, 4)
+    out = _entry(a, B, ctx + steps // 2, ms / steps, hbm, kv_mode="tq4",
+                 extra={"workload": "qwen3-8b TurboQuant KV B=16 ctx 32768 greedy"})
+    del eng, model
+    torch.cuda.empty_cache()
+    return out
+
+
+def ncu_traffic(rows):
+    """Per-launch DRAM bytes (read + write) of the W4 GEMV launches of one step, from the
+    committed ncu summary (profiles/qgemv_ring_dram_traffic.json: dram__bytes_read.sum +
+    dram__bytes_write.sum per shape, captured on the --kernel-case runs); null if absent."""
+    path = os.path.join(ROOT, "profiles", "qgemv_ring_dram_traffic.json")
+    try:
+        with open(path) as f:
+            per = json.load(f)["dram_bytes_per_launch"]
+        tot = sum(per[r["shape"]] * r["launches_per_step"] for r in rows)
+        return int(tot / sum(r["launches_per_step"] for r in rows))
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def run_ours(opt):
     import torch
 
@@ -398,17 +651,40 @@ def run_ours(opt):
         "gpu_launches": gpu_launches, "clocks": clocks,
     }
     if rank == 0 and not opt.quick:
-        rows = gemv_table(model)
+        rows = gemv_roofline(model)
         tot_bytes = sum(r["bytes"] * r["launches_per_step"] for r in rows)
         tot_us = sum(r["us"] * r["launches_per_step"] for r in rows)
         achieved = tot_bytes / tot_us / 1e3
-        out["roofline"] = {"kernel": "qlinear_w4_kernel (all W4 GEMV shapes of one B=1 step, byte-weighted)",
+        n_launch = sum(r["launches_per_step"] for r in rows)
+        out["roofline"] = {"kernel": "qgemv_ring_kernel (every W4 GEMV launch of one B=1 step; per-launch "
+                                     "averages, byte-weighted over shapes)",
                            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                           "traffic": None, "per_shape": rows}
+                           "algorithmic_bytes": int(tot_bytes / n_launch),
+                           "traffic": ncu_traffic(rows), "per_shape": rows}
         sb = by_batch[str(B)]["step_bytes"]
         out["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": round(sb / (step_ms / 1e3) / 1e9, 1),
                                 "peak": hbm, "frac": by_batch[str(B)]["step_hbm_frac"]}
+    if rank == 0 and ws == 1 and not opt.quick and opt.configs:
+        cfgs = {}
+        n = 16
+        want = opt.configs.split(",")
+        if "c3" in want:
+            cfgs["C3"] = config_c3(model, eng, Sequence, device, hbm, n, opt.ctx)
+        weights = model.weights
+        if "c5" in want:
+            cfgs["C5"] = config_c5(weights, device, hbm, n)
+        if "c1" in want:
+            cfgs["C1"] = config_c1(device, hbm, 64)
+        if "c2" in want:
+            cfgs["C2"] = config_c2(device, hbm, 64)
+        if "c4" in want:
+            del eng, model, weights
+            import gc
+            gc.collect()
+            torch.cuda.empty_cache()
+            cfgs["C4"] = config_c4(device, hbm, n)
+        out["by_config"] = cfgs
     if rank == 0 and ws == 1 and not opt.no_cpu_baseline and not opt.quick:
         sec, desc = oracle_step_time(a, opt.ctx)
         out["cpu_baseline"] = {"value": round(1.0 / sec, 4), "unit": "tok/s", "cores": os.cpu_count(),
@@ -448,7 +724,9 @@ def run_reference(opt):
 
 def main():
     opt = parse()
-    if opt.impl == "reference":
+    if opt.kernel_case:
+        kernel_case(opt)
+    elif opt.impl == "reference":
         run_reference(opt)
     else:
         run_ours(opt)

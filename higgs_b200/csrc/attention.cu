@@ -203,19 +203,33 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
     sm_lse[row] = W > 0.0f ? 1.0f / W : 0.0f;
   }
   __syncthreads();
-  // every (row, d) sums its splits with independent loads, 4 in flight
-  for (int i = threadIdx.x; i < R * D; i += kAttnThreads) {
-    const int row = i / D;
-    float O0 = 0.f, O1 = 0.f, O2 = 0.f, O3 = 0.f;
+  // every thread owns 4 consecutive d of one row; the float4 loads of 8 splits
+  // are issued together, so the merge costs ~splits/8 L2 round trips
+  for (int i4 = threadIdx.x; i4 < R * D / 4; i4 += kAttnThreads) {
+    const int row = (i4 * 4) / D;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     int s = 0;
-    for (; s + 4 <= a.splits; s += 4) {
-      O0 += sw[(s + 0) * R + row] * __ldcg(base_o + (size_t)(s + 0) * RP * D + i);
-      O1 += sw[(s + 1) * R + row] * __ldcg(base_o + (size_t)(s + 1) * RP * D + i);
-      O2 += sw[(s + 2) * R + row] * __ldcg(base_o + (size_t)(s + 2) * RP * D + i);
-      O3 += sw[(s + 3) * R + row] * __ldcg(base_o + (size_t)(s + 3) * RP * D + i);
+    for (; s < a.splits; s += 8) {
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[u] = s + u < a.splits
+                   ? __ldcg(reinterpret_cast<const float4*>(base_o + (size_t)(s + u) * RP * D) + i4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float w = s + u < a.splits ? sw[(s + u) * R + row] : 0.f;
+        acc.x = fmaf(w, v[u].x, acc.x);
+        acc.y = fmaf(w, v[u].y, acc.y);
+        acc.z = fmaf(w, v[u].z, acc.z);
+        acc.w = fmaf(w, v[u].w, acc.w);
+      }
     }
-    for (; s < a.splits; ++s) O0 += sw[s * R + row] * __ldcg(base_o + (size_t)s * RP * D + i);
-    sm_o[i] = ((O0 + O1) + (O2 + O3)) * sm_lse[row];
+    const float inv = sm_lse[row];
+    sm_o[i4 * 4 + 0] = acc.x * inv;
+    sm_o[i4 * 4 + 1] = acc.y * inv;
+    sm_o[i4 * 4 + 2] = acc.z * inv;
+    sm_o[i4 * 4 + 3] = acc.w * inv;
   }
   __syncthreads();
   if (threadIdx.x == 0) a.counters[bh] = 0;
@@ -1010,7 +1024,11 @@ static size_t smem_tq4(int MT) {
 }
 
 constexpr int kFusedStages = 3;
-constexpr int kFusedMinPages = 8;  // two pages per warp: the prefetch covers a whole split
+// pages per split of the fused kernel: two per warp by default, so the prefetch
+// issued before the grid dependency wait covers a whole split (tunable through
+// higgs_set_option("attn_min_pages", n), n >= 4; the workspace is sized for 4)
+static int g_fused_min_pages = 8;
+void attention_set_min_pages(int n) { g_fused_min_pages = n < 4 ? 4 : (n > 64 ? 64 : n); }
 
 static size_t smem_fused(int D, int MT, int Lq) {
   const size_t q = (size_t)16 * MT * D * 2;
@@ -1079,7 +1097,8 @@ extern "C" size_t higgs_paged_attention_tq4_workspace_size(int B, int Lq, int Hq
 }
 
 static int validate_attn(int B, int Lq, int Hq, int Hkv, int max_blocks, int max_seq_len,
-                         size_t ws_bytes, size_t need) {
+                         size_t ws_bytes, size_t need, const void* ws) {
+  HG_CHECK_ARG(((uintptr_t)ws & 15) == 0, "paged attention: workspace must be 16-byte aligned");
   HG_CHECK_ARG(B > 0 && Lq > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
                "paged attention: bad batch / head shape");
   HG_CHECK_ARG(B * Hkv * 1 <= kCounterBytes / 4, "paged attention: B * Hkv exceeds 1024");
@@ -1103,7 +1122,7 @@ extern "C" int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int L
   HG_CHECK_ARG(D == 64 || D == 128, "higgs_paged_attention: D must be 64 or 128");
   const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
-                         attn_ws_bytes(p, B, Hkv, D));
+                         attn_ws_bytes(p, B, Hkv, D), workspace);
   if (rc) return rc;
   AttnArgs a = {};
   a.q = (const uint16_t*)q;
@@ -1153,7 +1172,7 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
                "higgs_paged_attention_tq4: strides must be multiples of 64 bytes");
   const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
-                         attn_ws_bytes(p, B, Hkv, 128));
+                         attn_ws_bytes(p, B, Hkv, 128), workspace);
   if (rc) return rc;
   AttnArgs a = {};
   a.q = (const uint16_t*)q;
@@ -1189,7 +1208,7 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
 extern "C" size_t higgs_fused_attention_workspace_size(int B, int Lq, int Hq, int Hkv, int D,
                                                        int max_seq_len) {
   if (B <= 0 || Lq <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
-  return attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len, kFusedMinPages), B, Hkv, D);
+  return attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len, g_fused_min_pages), B, Hkv, D);
 }
 
 extern "C" int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq,
@@ -1209,9 +1228,9 @@ extern "C" int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int
                "higgs_fused_attention: give both q and k norm weights or neither");
   HG_CHECK_ARG(Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) * Lq <= 32,
                "higgs_fused_attention: needs (Hq / Hkv) * Lq <= 32");
-  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len, kFusedMinPages);
+  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len, g_fused_min_pages);
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
-                         attn_ws_bytes(p, B, Hkv, D));
+                         attn_ws_bytes(p, B, Hkv, D), workspace);
   if (rc) return rc;
   AttnArgs a = {};
   a.B = B;

@@ -25,6 +25,8 @@ int cuda_fail(cudaError_t e, const char* what) {
 }
 
 void qgemv_set_f16(bool on);
+void attention_set_min_pages(int n);
+void set_l2_prefetch(int mode);
 
 }  // namespace higgs
 
@@ -35,6 +37,14 @@ extern "C" int higgs_set_option(const char* name, int value) {
   const std::string n(name);
   if (n == "gemv_f16") {
     qgemv_set_f16(value != 0);
+    return HIGGS_OK;
+  }
+  if (n == "l2_prefetch") {
+    set_l2_prefetch(value);
+    return HIGGS_OK;
+  }
+  if (n == "attn_min_pages") {
+    attention_set_min_pages(value);
     return HIGGS_OK;
   }
   return fail(HIGGS_ERR_INVALID_ARG, "higgs_set_option: unknown option '" + n + "'");

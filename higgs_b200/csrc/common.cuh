@@ -162,6 +162,86 @@ __device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void* 
                : "r"(smem_u32(p)));
 }
 
+// exp(x) from correctly rounded f32 operations only (Cody-Waite reduction by
+// ln 2, degree-7 Taylor polynomial, exponent scaling), so host code performing
+// the same operations gets the same bits.
+__device__ __forceinline__ float det_exp(float x) {
+  if (!(x >= -87.0f)) return 0.0f;
+  if (x > 88.0f) x = 88.0f;
+  const float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
+  float r = __fmaf_rn(-kf, 0.693145751953125f, x);
+  r = __fmaf_rn(-kf, 1.42860682030941723e-6f, r);
+  float p = 1.98412698412698413e-4f;
+  p = __fmaf_rn(p, r, 1.38888888888888889e-3f);
+  p = __fmaf_rn(p, r, 8.33333333333333333e-3f);
+  p = __fmaf_rn(p, r, 4.16666666666666667e-2f);
+  p = __fmaf_rn(p, r, 1.66666666666666667e-1f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const int k = (int)kf;
+  return __fmul_rn(p, __uint_as_float((uint32_t)(k + 127) << 23));
+}
+
+// Orderable u64 key for argmax-style reductions: (ordered value bits << 32) |
+// (~index), so the u64 maximum is the largest value and, among equal values,
+// the lowest index.  NaN maps to the smallest key; -0 is folded onto +0.
+__device__ __forceinline__ unsigned long long argmax_key(float v, int j) {
+  uint32_t u = __float_as_uint(v);
+  if (v == 0.0f) u = 0u;
+  const uint32_t o = (v != v) ? 0u : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+  return ((unsigned long long)o << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)j);
+}
+
+// ---------------------------------------------------------------------------
+// L2 prefetch of read-only ranges (weights) by the TMA unit
+// ---------------------------------------------------------------------------
+// Ranges a later kernel of the step will stream: every CTA of the current
+// kernel asks for its share of their union with cp.async.bulk.prefetch.L2
+// before it waits on its predecessor, so HBM keeps streaming weights while the
+// step's dependency chain runs.  A prefetch is only a hint: it changes no data.
+// Ranges start on 16-byte boundaries and are whole multiples of 16 bytes.
+struct L2Prefetch {
+  static constexpr int kMax = 12;
+  const void* ptr[kMax];
+  unsigned long long bytes[kMax];
+  int n;
+};
+
+__device__ __forceinline__ void l2_prefetch_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// one lane walks [p, p + bytes) in 32 KB requests
+__device__ __forceinline__ void l2_prefetch_range(const void* p, unsigned long long bytes) {
+  if ((reinterpret_cast<uintptr_t>(p) & 15) != 0) return;  // the bulk unit needs 16-byte alignment
+  bytes &= ~15ull;
+  const char* c = static_cast<const char*>(p);
+  for (unsigned long long o = 0; o < bytes; o += 32768)
+    l2_prefetch_bulk(c + o, (uint32_t)(bytes - o < 32768 ? bytes - o : 32768));
+}
+
+// Share `cta` of `ncta` of the union of the ranges, issued by the lanes of warp 0.
+__device__ __forceinline__ void issue_l2_prefetch(const L2Prefetch& pf, int cta, int ncta) {
+  if (pf.n <= 0 || threadIdx.x >= 32) return;
+  unsigned long long total = 0;
+  for (int i = 0; i < pf.n; ++i) total += pf.bytes[i];
+  const unsigned long long per = ((total + ncta - 1) / ncta + 15) & ~15ull;
+  const unsigned long long lo = (unsigned long long)cta * per;
+  const unsigned long long hi = lo + per < total ? lo + per : total;
+  unsigned long long base = 0;
+  for (int i = 0; i < pf.n; ++i) {
+    const unsigned long long b0 = base, b1 = base + pf.bytes[i];
+    base = b1;
+    const unsigned long long s = lo > b0 ? lo : b0, e = hi < b1 ? hi : b1;
+    if (s >= e || ((reinterpret_cast<uintptr_t>(pf.ptr[i]) | pf.bytes[i]) & 15) != 0) continue;
+    const char* c = static_cast<const char*>(pf.ptr[i]) + (s - b0);
+    const unsigned long long len = e - s;
+    for (unsigned long long o = (unsigned long long)threadIdx.x * 32768; o < len; o += 32 * 32768ull)
+      l2_prefetch_bulk(c + o, (uint32_t)(len - o < 32768 ? len - o : 32768));
+  }
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

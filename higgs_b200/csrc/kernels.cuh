@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace higgs {
 
 enum { EPI_STORE = 0, EPI_SWIGLU = 1 };
@@ -31,12 +33,51 @@ struct QLinArgs {
   // optional fused RMSNorm of x (ring GEMV only): x is the residual stream h
   const uint16_t* norm_w;
   float eps;
+  // grouped experts (MoE, ring GEMV only): blockIdx.y picks a work item
+  // {expert, first slot in moe_sorted, pairs} of the routing plan; x row of pair
+  // p = p / moe_xdiv, output row = p; w/s/b (and w2/s2/b2) advance by
+  // expert * moe_ew u32 words / expert * moe_es bf16 elements.
+  const int4* moe_items;
+  const int* moe_n_items;
+  const int* moe_sorted;
+  int moe_max_items;
+  int moe_xdiv;
+  long long moe_ew, moe_es;
+  // weights of a later launch to pull into L2 (the next GEMV of the step)
+  L2Prefetch pf;
+  // also prefetch this CTA's own weight tiles to L2 at its start
+  int self_prefetch;
 };
+
+// Routing plan of the MoE router (moe.cu), in one buffer:
+//   int  header[4]  {n_items, n_pairs, E, k}
+//   int4 items[max_items]   {expert, first slot, pairs (<= 8), 0}
+//   int  sorted[T*k]        pairs grouped by expert, ascending within an expert
+//   int  counts[E]
+inline int moe_max_items(int P, int E) { return P / 8 + (E < P ? E : P) + 1; }
+size_t moe_plan_bytes(int T, int E, int k);
+cudaError_t launch_moe_route(const void* logits, bool bf16_in, int T, int E, int k, int norm,
+                             int32_t* idx, float* scores, void* plan, cudaStream_t st);
+cudaError_t launch_moe_grouped(const uint16_t* x, int T, int K, int k, bool x_per_pair,
+                               const void* plan, int E, int N, const uint32_t* w, const uint16_t* s,
+                               const uint16_t* b, const uint32_t* w2, const uint16_t* s2,
+                               const uint16_t* b2, uint16_t* y, cudaStream_t st);
+cudaError_t launch_moe_router(const uint16_t* x, int T, int K, const uint32_t* w,
+                              const uint16_t* s, const uint16_t* b, int E, uint16_t* out,
+                              cudaStream_t st);
+cudaError_t launch_moe_combine(const uint16_t* y, const float* scores, int T, int k, int H,
+                               uint16_t* h, cudaStream_t st);
 
 // W4 GEMV with per-warp cp.async rings (any M, 32 rows per pass; norm_w needs
 // qgemv_ring_can_fuse_norm(M, K)).
 cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st);
+// process-wide switches for the L2 prefetch fields (QLinArgs::pf, self_prefetch)
+bool l2_prefetch_next();
+bool l2_prefetch_self();
 bool qgemv_ring_can_fuse_norm(int M, int K);
+// Grouped-expert variant (the a.moe_* fields set): K * 8 tokens must fit the staged-x tile.
+cudaError_t launch_qgemv_grouped(const QLinArgs& a, int epi, cudaStream_t st);
+bool qgemv_grouped_supported(int K);
 
 // M may exceed 32 (processed in 32-row passes); K % 256 == 0, N % 16 == 0.
 cudaError_t launch_qlinear(const QLinArgs& a, int epi, cudaStream_t st);

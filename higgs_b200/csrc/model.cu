@@ -44,6 +44,9 @@ struct LayerW {
   QW q, k, v, o, gate, up, down;
   const uint16_t* qn = nullptr;
   const uint16_t* kn = nullptr;
+  // sparse block (Qwen3MoeMlpBlock): router [E, H] and stacked experts [E, N, K]
+  bool moe = false;
+  QW router, egate, eup, edown;  // e*: w/s/b point at expert 0, N/K per expert
 };
 
 void attention_prepare();
@@ -82,7 +85,8 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
-  size_t h, x, qkv, q, attn, act, xl, logits, attn_ws, total;
+  size_t h, x, qkv, q, attn, act, xl, logits, moe_rl, moe_idx, moe_sc, moe_plan, moe_act, moe_y,
+      attn_ws, total;
 };
 
 
@@ -106,6 +110,15 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
   L.act = take(T * (size_t)c.intermediate * 2);
   L.xl = take(rows_lm * c.hidden * 2);
   L.logits = take(rows_lm * (size_t)c.vocab * 4);
+  if (c.num_experts > 0) {
+    const size_t P = T * c.experts_per_tok;
+    L.moe_rl = take(T * (size_t)c.num_experts * 2);
+    L.moe_idx = take(P * 4);
+    L.moe_sc = take(P * 4);
+    L.moe_plan = take(moe_plan_bytes((int)T, c.num_experts, c.experts_per_tok));
+    L.moe_act = take(P * (size_t)c.moe_intermediate * 2);
+    L.moe_y = take(P * (size_t)c.hidden * 2);
+  }
   const size_t aws = higgs_paged_attention_workspace_size(B, Lq, c.heads, c.kv_heads, D, max_seq_len);
   L.attn_ws = take(aws);
   L.total = off;
@@ -134,6 +147,32 @@ int get_q(higgs_model* m, const std::string& base, int N, int K, QW& out) {
   out.w = (const uint32_t*)w.ptr;
   out.s = (const uint16_t*)s.ptr;
   out.b = (const uint16_t*)b.ptr;
+  out.N = N;
+  out.K = K;
+  return HIGGS_OK;
+}
+
+// stacked expert tensor [E, N, K/8] u32 + [E, N, K/64] bf16 scales / biases
+int get_q3(higgs_model* m, const std::string& base, int E, int N, int K, QW& out) {
+  auto it_w = m->tensors.find(base + ".weight");
+  auto it_s = m->tensors.find(base + ".scales");
+  auto it_b = m->tensors.find(base + ".biases");
+  if (it_w == m->tensors.end() || it_s == m->tensors.end() || it_b == m->tensors.end())
+    return fail(HIGGS_ERR_STATE, "model: missing quantized tensor " + base + ".{weight,scales,biases}");
+  auto shape_is = [](const TensorRef& t, int64_t a, int64_t b, int64_t c) {
+    return t.shape.size() == 3 && t.shape[0] == a && t.shape[1] == b && t.shape[2] == c;
+  };
+  const std::string dims = "[" + std::to_string(E) + ", " + std::to_string(N) + ", ";
+  if (it_w->second.dtype != HIGGS_DTYPE_U32 || !shape_is(it_w->second, E, N, K / 8))
+    return fail(HIGGS_ERR_INVALID_ARG, "model: " + base + ".weight must be u32 " + dims +
+                                           std::to_string(K / 8) + "]");
+  for (auto* t : {&it_s->second, &it_b->second})
+    if (t->dtype != HIGGS_DTYPE_BF16 || !shape_is(*t, E, N, K / 64))
+      return fail(HIGGS_ERR_INVALID_ARG, "model: " + base + ".{scales,biases} must be bf16 " + dims +
+                                             std::to_string(K / 64) + "]");
+  out.w = (const uint32_t*)it_w->second.ptr;
+  out.s = (const uint16_t*)it_s->second.ptr;
+  out.b = (const uint16_t*)it_b->second.ptr;
   out.N = N;
   out.K = K;
   return HIGGS_OK;
@@ -178,9 +217,26 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
 
   // decode batches fuse each RMSNorm into the GEMV that consumes it
   const bool fuse = qgemv_ring_can_fuse_norm(T, H);
+  // L2 prefetch lists: each GEMV asks for the weights of a later GEMV of the step
+  const bool pfon = l2_prefetch_next(), pfself = l2_prefetch_self();
+  auto add_q = [&](L2Prefetch& pf, const QW& w, size_t max_bytes = ~(size_t)0) {
+    if (!pfon || !w.w || pf.n + 3 > L2Prefetch::kMax) return;
+    const size_t wb = (size_t)w.N * w.K / 2, sb = (size_t)w.N * (w.K / 64) * 2;
+    const double f = max_bytes < wb ? (double)max_bytes / wb : 1.0;  // leading rows only
+    const size_t rows = (size_t)(w.N * f) / 16 * 16;
+    pf.ptr[pf.n] = w.w;
+    pf.bytes[pf.n++] = rows * (w.K / 2);
+    pf.ptr[pf.n] = w.s;
+    pf.bytes[pf.n++] = rows * (w.K / 64) * 2;
+    pf.ptr[pf.n] = w.b;
+    pf.bytes[pf.n++] = rows * (w.K / 64) * 2;
+    (void)sb;
+  };
   auto lin = [&](const QW& w, const uint16_t* xin, const uint16_t* norm, uint16_t* y, float* yf,
-                 const uint16_t* res) {
+                 const uint16_t* res, const L2Prefetch* pf = nullptr) {
     QLinArgs a{};
+    a.self_prefetch = pfself;
+    if (pf) a.pf = *pf;
     a.x = xin;
     a.norm_w = norm;
     a.eps = c.rms_eps;
@@ -230,6 +286,14 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.sseg[2] = Lw.v.s;
       a.bseg[2] = Lw.v.b;
       a.y = qkv;
+      a.self_prefetch = pfself;
+      add_q(a.pf, Lw.o);
+      if (Lw.moe) {
+        add_q(a.pf, Lw.router);
+      } else {
+        add_q(a.pf, Lw.gate);
+        add_q(a.pf, Lw.up);
+      }
       HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
     }
     if (tq) {
@@ -273,7 +337,41 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       if (rc) return rc;
     }
     // h = h + o_proj(attn)   (in place: each element read then written by one thread)
-    HG_CUDA(lin(Lw.o, attn, nullptr, h, nullptr, h));
+    {
+      L2Prefetch pf{};
+      if (!Lw.moe) add_q(pf, Lw.down);
+      HG_CUDA(lin(Lw.o, attn, nullptr, h, nullptr, h, &pf));
+    }
+    if (Lw.moe) {
+      // Qwen3MoeMlpBlock::forward_moe: router -> top-k plan -> grouped gate/up SwiGLU ->
+      // grouped down -> weighted sum + residual
+      const int E = c.num_experts, kk = c.experts_per_tok, F = c.moe_intermediate;
+      uint16_t* rl = (uint16_t*)(ws + L.moe_rl);
+      int32_t* idx = (int32_t*)(ws + L.moe_idx);
+      float* sc = (float*)(ws + L.moe_sc);
+      void* plan = ws + L.moe_plan;
+      uint16_t* pact = (uint16_t*)(ws + L.moe_act);
+      uint16_t* py = (uint16_t*)(ws + L.moe_y);
+      rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_post, c.rms_eps, x, nullptr, st);
+      if (rc) return rc;
+      {
+        L2Prefetch pf{};
+        if (li + 1 < n_layers) {
+          add_q(pf, m->layers[li + 1].q);
+          add_q(pf, m->layers[li + 1].k);
+          add_q(pf, m->layers[li + 1].v);
+        }
+        (void)pf;
+        HG_CUDA(launch_moe_router(x, T, H, Lw.router.w, Lw.router.s, Lw.router.b, E, rl, st));
+      }
+      HG_CUDA(launch_moe_route(rl, true, T, E, kk, c.norm_topk_prob, idx, sc, plan, st));
+      HG_CUDA(launch_moe_grouped(x, T, H, kk, false, plan, E, F, Lw.egate.w, Lw.egate.s, Lw.egate.b,
+                                 Lw.eup.w, Lw.eup.s, Lw.eup.b, pact, st));
+      HG_CUDA(launch_moe_grouped(pact, T, F, kk, true, plan, E, H, Lw.edown.w, Lw.edown.s,
+                                 Lw.edown.b, nullptr, nullptr, nullptr, py, st));
+      HG_CUDA(launch_moe_combine(py, sc, T, kk, H, h, st));
+      continue;
+    }
     {
       if (!fuse) {
         rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_post, c.rms_eps, x, nullptr, st);
@@ -294,6 +392,15 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.b2 = Lw.up.b;
       a.nseg = 1;
       a.y = act;
+      a.self_prefetch = pfself;
+      if (li + 1 < n_layers) {
+        const LayerW& Ln = m->layers[li + 1];
+        add_q(a.pf, Ln.q);
+        add_q(a.pf, Ln.k);
+        add_q(a.pf, Ln.v);
+      } else {
+        add_q(a.pf, m->head, (size_t)48 << 20);  // the head's leading 48 MB
+      }
       HG_CUDA(launch_qgemv_ring(a, EPI_SWIGLU, st));
     }
     HG_CUDA(lin(Lw.down, act, nullptr, h, nullptr, h));
@@ -326,6 +433,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
     a.b = m->head.b;
     a.nseg = 1;
     a.y_f32 = logits;
+    a.self_prefetch = pfself;
     HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
   }
   if (f->argmax) {
@@ -349,6 +457,8 @@ int validate_forward(higgs_model* m, const higgs_forward_args* f) {
   HG_CHECK_ARG(f->max_seq_len >= f->Lq && (int64_t)f->max_blocks * HIGGS_PAGE_SIZE >= f->max_seq_len,
                "higgs_model_forward: max_seq_len / max_blocks inconsistent");
   HG_CHECK_ARG(f->workspace, "higgs_model_forward: null workspace");
+  HG_CHECK_ARG(m->cfg.num_experts == 0 || (int64_t)f->B * f->Lq * m->cfg.experts_per_tok <= 65536,
+               "higgs_model_forward: MoE routes at most 65536 (token, expert) pairs per call");
   return HIGGS_OK;
 }
 
@@ -368,6 +478,18 @@ extern "C" int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg,
   HG_CHECK_ARG((c.heads * c.head_dim) % 256 == 0, "higgs_model_create: heads*head_dim must be a multiple of 256");
   HG_CHECK_ARG(c.kv_mode == HIGGS_KV_BF16 || (c.kv_mode == HIGGS_KV_TQ4 && c.head_dim == 128),
                "higgs_model_create: TurboQuant KV needs head_dim 128");
+  if (c.num_experts > 0) {
+    HG_CHECK_ARG(c.num_experts <= 1024 && c.num_experts % 16 == 0,
+                 "higgs_model_create: num_experts must be a multiple of 16, at most 1024");
+    HG_CHECK_ARG(c.experts_per_tok > 0 && c.experts_per_tok <= 32 && c.experts_per_tok <= c.num_experts,
+                 "higgs_model_create: experts_per_tok must be in [1, min(32, num_experts)]");
+    HG_CHECK_ARG(c.moe_intermediate > 0 && c.moe_intermediate % 256 == 0,
+                 "higgs_model_create: moe_intermediate must be a multiple of 256");
+    HG_CHECK_ARG(qgemv_grouped_supported(c.hidden) && qgemv_grouped_supported(c.moe_intermediate),
+                 "higgs_model_create: hidden / moe_intermediate too large for the grouped experts");
+  } else {
+    HG_CHECK_ARG(c.num_experts == 0, "higgs_model_create: negative num_experts");
+  }
   higgs_model* m = new higgs_model;
   m->ctx = ctx;
   m->cfg = c;
@@ -424,6 +546,16 @@ extern "C" int higgs_model_finalize(higgs_model* m) {
     if (c.qk_norm) {
       if ((rc = get_vec(m, p + "self_attn.q_norm.weight", D, L.qn))) return rc;
       if ((rc = get_vec(m, p + "self_attn.k_norm.weight", D, L.kn))) return rc;
+    }
+    L.moe = c.num_experts > 0 && m->tensors.count(p + "mlp.gate.weight");
+    if (L.moe) {
+      const int E = c.num_experts, F = c.moe_intermediate;
+      const std::string sw = p + "mlp.switch_mlp.";
+      if ((rc = get_q(m, p + "mlp.gate", E, H, L.router))) return rc;
+      if ((rc = get_q3(m, sw + "gate_proj", E, F, H, L.egate))) return rc;
+      if ((rc = get_q3(m, sw + "up_proj", E, F, H, L.eup))) return rc;
+      if ((rc = get_q3(m, sw + "down_proj", E, H, F, L.edown))) return rc;
+      continue;
     }
     if ((rc = get_q(m, p + "mlp.gate_proj", c.intermediate, H, L.gate))) return rc;
     if ((rc = get_q(m, p + "mlp.up_proj", c.intermediate, H, L.up))) return rc;

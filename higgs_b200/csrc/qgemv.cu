@@ -36,6 +36,7 @@ constexpr int kUnitW = 16 * 128;      // packed weight bytes of a unit
 constexpr int kUnitS = 16 * 4 * 2;    // scale bytes of a unit
 constexpr int kStage = kUnitW + 2 * kUnitS;  // + biases
 constexpr size_t kXsmemMax = 32 * 1024;        // x staged in shared memory up to this size
+constexpr size_t kXsmemGroupedMax = 72 * 1024; // grouped experts always stage 8 pairs
 
 // bytes of the fragment-ordered x tile: per token G groups x 4 lane slots x 32 B, padded
 inline size_t xfrag_bytes(int M, int K) { return (size_t)M * ((K / 64) * 128 + 16); }
@@ -93,8 +94,9 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16>
+template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER>
 __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
+  static_assert(!GATHER || (XSMEM && NT8 == 1), "grouped experts use the staged-x path");
   constexpr int RT = 8 / WK;
   constexpr int ROT = (EPI == EPI_SWIGLU) ? RT / 2 : RT;
   constexpr int MT = 8 * NT8;  // token slots
@@ -102,7 +104,12 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int rt = warp / WK, kw = warp % WK;
-  const int K = a.K, N = a.N, M = a.M;
+  const int K = a.K, N = a.N;
+  int M = a.M;
+  // token m reads x row xrow(m) and writes output row orow(m) (identity unless GATHER)
+  __shared__ int s_xrow[GATHER ? MT : 1], s_orow[GATHER ? MT : 1];
+  auto xrow = [&](int m) { return GATHER ? s_xrow[m] : m; };
+  auto orow = [&](int m) { return GATHER ? s_orow[m] : m; };
   const int KW = K / 8, G = K / 64;
   const int units = G / 4;
 
@@ -139,15 +146,50 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
   const int ub = tile_ok ? (units * kw) / WK : 0;
   const int ue = tile_ok ? (units * (kw + 1)) / WK : 0;
 
-  // prefetch the first S-1 units (weights never depend on the previous kernel)
+  // weights of the step's next GEMV -> L2, while this kernel's chain runs
+  issue_l2_prefetch(a.pf, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
+  if constexpr (!GATHER) {
+    if (a.self_prefetch && tile_ok && kw == 0 && lane == 0) {
+      // this tile's whole weight rows -> L2 (the ring below keeps only S-1 units in flight)
+      l2_prefetch_range(sg.W + (size_t)sg.row0 * KW, (size_t)16 * KW * 4);
+      l2_prefetch_range(sg.S + (size_t)sg.row0 * G, (size_t)16 * G * 2);
+      l2_prefetch_range(sg.B + (size_t)sg.row0 * G, (size_t)16 * G * 2);
+    }
+    // prefetch the first S-1 units (weights never depend on the previous kernel)
 #pragma unroll
-  for (int s = 0; s < S - 1; ++s) {
-    if (ub + s < ue) issue_unit(ring + s * kStage, sg, KW, G, ub + s, lane);
-    cp_async_commit();
+    for (int s = 0; s < S - 1; ++s) {
+      if (ub + s < ue) issue_unit(ring + s * kStage, sg, KW, G, ub + s, lane);
+      cp_async_commit();
+    }
+    pdl_wait();
+    pdl_launch();
+  } else {
+    // the expert and its pairs come from the router's plan: read it first
+    pdl_wait();
+    pdl_launch();
+    if ((int)blockIdx.y >= *a.moe_n_items) return;  // uniform over the CTA
+    const int4 it = a.moe_items[blockIdx.y];
+    M = it.z;
+    sg.W += (long long)it.x * a.moe_ew;
+    sg.S += (long long)it.x * a.moe_es;
+    sg.B += (long long)it.x * a.moe_es;
+    if (a.self_prefetch && tile_ok && kw == 0 && lane == 0) {
+      l2_prefetch_range(sg.W + (size_t)sg.row0 * KW, (size_t)16 * KW * 4);
+      l2_prefetch_range(sg.S + (size_t)sg.row0 * G, (size_t)16 * G * 2);
+      l2_prefetch_range(sg.B + (size_t)sg.row0 * G, (size_t)16 * G * 2);
+    }
+    if (threadIdx.x < MT) {
+      const int pr = threadIdx.x < M ? a.moe_sorted[it.y + threadIdx.x] : 0;
+      s_xrow[threadIdx.x] = pr / a.moe_xdiv;
+      s_orow[threadIdx.x] = pr;
+    }
+#pragma unroll
+    for (int s = 0; s < S - 1; ++s) {
+      if (ub + s < ue) issue_unit(ring + s * kStage, sg, KW, G, ub + s, lane);
+      cp_async_commit();
+    }
+    __syncthreads();
   }
-
-  pdl_wait();
-  pdl_launch();
 
   // XSMEM path: x in fp16 fragments, scaled per token by 2^e (exact for bf16
   // inputs) into fp16 range; X1 = sum(x), X2 = 1024 * (sum_even(x) + sum_odd(x) / 16)
@@ -160,7 +202,15 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
     __shared__ float inv_rms[MT];
     __shared__ float red[8][MT];
     __shared__ float redm[8][MT];
-    {
+    if constexpr (!NORM && !F16) {
+      // plain bf16 staging: no statistics needed
+      if (threadIdx.x < MT) {
+        inv_rms[threadIdx.x] = 1.0f;
+        unscale[threadIdx.x] = threadIdx.x < M ? 1.0f : 0.0f;
+        red[0][threadIdx.x] = 1.0f;
+      }
+      __syncthreads();
+    } else {
       float ss[MT], mx[MT];
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
@@ -169,17 +219,18 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
       }
       for (int vi = threadIdx.x; vi < M * (K / 8); vi += 256) {
         const int m = vi / (K / 8), k8 = vi % (K / 8);
-        const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)vi * 8);
+        const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)xrow(m) * K + k8 * 8);
         const uint32_t* vp = &v.x;
         uint4 wv = make_uint4(0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u);
-        if constexpr (NORM) wv = *reinterpret_cast<const uint4*>(a.norm_w + k8 * 8);
+        if constexpr (NORM && F16) wv = *reinterpret_cast<const uint4*>(a.norm_w + k8 * 8);
         const uint32_t* wp = &wv.x;
         float acc = 0.f, am = 0.f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float lo = bf_lo(vp[j]), hi = bf_hi(vp[j]);
           acc += lo * lo + hi * hi;
-          am = fmaxf(am, fmaxf(fabsf(lo * bf_lo(wp[j])), fabsf(hi * bf_hi(wp[j]))));
+          if constexpr (F16)  // the fp16 operand scale needs the largest |x * w|
+            am = fmaxf(am, fmaxf(fabsf(lo * bf_lo(wp[j])), fabsf(hi * bf_hi(wp[j]))));
         }
 #pragma unroll
         for (int mm = 0; mm < MT; ++mm)
@@ -190,8 +241,9 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
       }
 #pragma unroll
       for (int m = 0; m < MT; ++m) {
+        if (m >= M) break;  // M is uniform over the CTA
         const float r = warp_sum(ss[m]);
-        const float q = warp_max(mx[m]);
+        const float q = F16 ? warp_max(mx[m]) : 0.f;
         if (lane == 0) {
           red[warp][m] = r;
           redm[warp][m] = q;
@@ -230,7 +282,7 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
       const int task = base + lane;
       const bool valid = task < n_tasks;
       const int m = valid ? task / (G * 4) : 0, j = valid ? (task / 4) % G : 0, tt = task % 4;
-      const uint16_t* src = a.x + (size_t)m * K + j * 64 + 16 * tt;
+      const uint16_t* src = a.x + (size_t)xrow(m) * K + j * 64 + 16 * tt;
       uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
       if (valid) {
         v0 = *reinterpret_cast<const uint4*>(src);
@@ -478,7 +530,7 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
       const int row = n0 + g + 8 * (c >> 1);
       const int tok = 8 * j + 2 * t + (c & 1);
       if (tok >= M) continue;
-      const size_t o = (size_t)tok * N + row;
+      const size_t o = (size_t)orow(tok) * N + row;
       if (EPI == EPI_SWIGLU) {
         const float gv = round_bf(v), uv = round_bf(v2);
         a.y[o] = f2bf(gv / (1.0f + expf(-gv)) * uv);
@@ -493,23 +545,24 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
     }
 }
 
-template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16>
+template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER>
 cudaError_t launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
-  auto k = qgemv_ring_kernel<NT8, WK, EPI, S, XSMEM, NORM, F16>;
+  auto k = qgemv_ring_kernel<NT8, WK, EPI, S, XSMEM, NORM, F16, GATHER>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  return launch_pdl(k, dim3(ctas), dim3(256), smem, st, a);
+  return launch_pdl(k, dim3(ctas, GATHER ? a.moe_max_items : 1), dim3(256), smem, st, a);
 }
 
-template <int NT8, int EPI, int S, bool XSMEM, bool NORM, bool F16>
+template <int NT8, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER = false>
 cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
   const int nrt = a.N / 16;
   const int units = a.K / 256;
-  const size_t xs_bytes = XSMEM ? xfrag_bytes(a.M, a.K) + 2 * (size_t)(a.K / 64) * 8 * NT8 * 4 : 0;
+  const int mt = GATHER ? 8 : a.M;  // a grouped item holds up to 8 pairs
+  const size_t xs_bytes = XSMEM ? xfrag_bytes(mt, a.K) + 2 * (size_t)(a.K / 64) * 8 * NT8 * 4 : 0;
   const size_t ring = (size_t)8 * S * kStage;
   const size_t red = (size_t)8 * NT8 * 4 * 32 * 4;
   const size_t smem = (ring + xs_bytes) > red ? ring + xs_bytes : red;
@@ -517,32 +570,34 @@ cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
   if (per_sm > 3) per_sm = 3;
   if (per_sm < 1) per_sm = 1;
   const int slots = per_sm * sm_count();
+  // row tiles competing for the slots (grouped experts: every work item's tiles)
+  const long long work = (long long)nrt * (GATHER ? a.moe_max_items : 1);
   // largest row-tile count per CTA that still fills the slots; every warp keeps >= 1 unit
   int wk;
   if (EPI == EPI_SWIGLU) {
     wk = 4;  // 2 warp tiles (one gate/up pair) per CTA
-    if ((nrt + 1) / 2 >= slots && units >= 2) wk = 2;
-    if ((nrt + 3) / 4 >= slots) wk = 1;
+    if ((work + 1) / 2 >= slots && units >= 2) wk = 2;
+    if ((work + 3) / 4 >= slots) wk = 1;
     while (wk > 1 && units < wk) wk >>= 1;
     if (wk > 4) wk = 4;
     const int rot = (8 / wk) / 2;
     const int ctas = (nrt + rot - 1) / rot;
-    if (wk == 4) return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16>(a, ctas, smem, st);
-    if (wk == 2) return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16>(a, ctas, smem, st);
-    return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16>(a, ctas, smem, st);
+    if (wk == 4) return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
+    if (wk == 2) return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
+    return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
   }
   wk = 8;
-  if (nrt / 2 >= slots) wk = 4;
-  if (nrt / 4 >= slots) wk = 2;
-  if (nrt / 8 >= slots) wk = 1;
+  if (work / 2 >= slots) wk = 4;
+  if (work / 4 >= slots) wk = 2;
+  if (work / 8 >= slots) wk = 1;
   while (wk > 1 && units < wk) wk >>= 1;
   const int rot = 8 / wk;
   const int ctas = (nrt + rot - 1) / rot;
   switch (wk) {
-    case 8: return launch_cfg<NT8, 8, EPI, S, XSMEM, NORM, F16>(a, ctas, smem, st);
-    case 4: return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16>(a, ctas, smem, st);
-    case 2: return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16>(a, ctas, smem, st);
-    default: return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16>(a, ctas, smem, st);
+    case 8: return launch_cfg<NT8, 8, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
+    case 4: return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
+    case 2: return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
+    default: return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
   }
 }
 
@@ -588,6 +643,23 @@ cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st) {
 
 bool qgemv_ring_can_fuse_norm(int M, int K) { return M <= 8 && xfrag_bytes(M, K) <= kXsmemMax; }
 
+// Grouped-expert GEMV over a routing plan (a.moe_* set, a.M ignored): one
+// grid row per potential work item, items past the plan's count exit at once.
+bool qgemv_grouped_supported(int K) { return xfrag_bytes(8, K) <= kXsmemGroupedMax; }
+cudaError_t launch_qgemv_grouped(const QLinArgs& a, int epi, cudaStream_t st) {
+  if (!qgemv_grouped_supported(a.K) || a.moe_max_items <= 0 || a.moe_max_items > 65535)
+    return cudaErrorInvalidValue;
+  return epi == EPI_SWIGLU ? launch_wk<1, EPI_SWIGLU, 3, true, false, false, true>(a, st)
+                           : launch_wk<1, EPI_STORE, 3, true, false, false, true>(a, st);
+}
+
 void qgemv_set_f16(bool on) { g_gemv_f16 = on; }
+
+// L2 prefetch of GEMV weights: bit 0 = the step's next GEMV, bit 1 = each CTA's
+// own tiles.  Off by default: measured on B200 it lengthened the decode step.
+static int g_l2_prefetch = 0;
+void set_l2_prefetch(int mode) { g_l2_prefetch = mode & 3; }
+bool l2_prefetch_next() { return (g_l2_prefetch & 1) != 0; }
+bool l2_prefetch_self() { return (g_l2_prefetch & 2) != 0; }
 
 }  // namespace higgs

@@ -448,6 +448,7 @@ extern "C" int higgs_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, 
   a.y = (uint16_t*)y;
   a.y_f32 = y_f32;
   a.residual = (const uint16_t*)residual;
+  a.self_prefetch = l2_prefetch_self();
   HG_CUDA(launch_qgemv_ring(a, EPI_STORE, (cudaStream_t)stream));
   return HIGGS_OK;
 }
@@ -475,6 +476,7 @@ extern "C" int higgs_qlinear_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M
   a.s2 = (const uint16_t*)s_up;
   a.b2 = (const uint16_t*)b_up;
   a.y = (uint16_t*)y;
+  a.self_prefetch = l2_prefetch_self();
   HG_CUDA(launch_qgemv_ring(a, EPI_SWIGLU, (cudaStream_t)stream));
   return HIGGS_OK;
 }

@@ -10,29 +10,16 @@
 // draw is a deterministic function of (logits, T, u) whatever the reduction
 // order.  det_exp is a Cody-Waite + degree-7 Taylor exp built from correctly
 // rounded f32 operations only, so the CPU checker computes the same bits.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace higgs {
 
 constexpr int kSampThreads = 1024;
 
-__device__ __forceinline__ float det_exp(float x) {
-  if (!(x >= -87.0f)) return 0.0f;
-  if (x > 88.0f) x = 88.0f;
-  const float kf = rintf(__fmul_rn(x, 1.44269504088896341f));
-  float r = __fmaf_rn(-kf, 0.693145751953125f, x);
-  r = __fmaf_rn(-kf, 1.42860682030941723e-6f, r);
-  float p = 1.98412698412698413e-4f;
-  p = __fmaf_rn(p, r, 1.38888888888888889e-3f);
-  p = __fmaf_rn(p, r, 8.33333333333333333e-3f);
-  p = __fmaf_rn(p, r, 4.16666666666666667e-2f);
-  p = __fmaf_rn(p, r, 1.66666666666666667e-1f);
-  p = __fmaf_rn(p, r, 0.5f);
-  p = __fmaf_rn(p, r, 1.0f);
-  p = __fmaf_rn(p, r, 1.0f);
-  const int k = (int)kf;
-  return __fmul_rn(p, __uint_as_float((uint32_t)(k + 127) << 23));
-}
 
 __device__ __forceinline__ uint64_t fixed_mass(float l, float inv_t, float mxs) {
   const float e = det_exp(__fsub_rn(__fmul_rn(l, inv_t), mxs));
@@ -185,14 +172,84 @@ __device__ int block_argmax(const float* x, int V, float* shf, int* shi) {
   return ri == 0x7fffffff ? 0 : ri;
 }
 
-__global__ void __launch_bounds__(kSampThreads) argmax_kernel(const float* logits, int V,
-                                                              int32_t* out) {
+// Greedy argmax of one row split across a cluster of kArgmaxCluster CTAs: each
+// CTA reduces a slice to a single u64 key, then CTA 0 reads the others' keys
+// through distributed shared memory.  key = (ordered value bits << 32) |
+// (~index), so the u64 maximum is the largest value and, among equal values,
+// the lowest index; NaN maps to the smallest key (it wins only when the whole
+// row is NaN, giving index 0) and -0 is folded onto +0 so they compare equal.
+constexpr int kArgmaxCluster = 8;
+constexpr int kArgmaxThreads = 512;
+
+
+__global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmaxThreads)
+    argmax_cluster_kernel(const float* logits, int V, int32_t* out) {
+  __shared__ unsigned long long warp_best[kArgmaxThreads / 32];
+  __shared__ unsigned long long cta_best;
+  const int rank = blockIdx.x;  // cluster spans the whole x dimension
+  const float* row = logits + (size_t)blockIdx.y * V;
+  // slice bounds on 4-float boundaries so vector loads stay aligned
+  const int nv4 = V / 4;
+  const int per = (nv4 + kArgmaxCluster - 1) / kArgmaxCluster;
+  const int v0 = rank * per, v1 = min(nv4, v0 + per);
+  const bool vec = ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
   pdl_wait();
-  __shared__ float shf[32];
-  __shared__ int shi[32];
-  const int r = block_argmax(logits + (size_t)blockIdx.x * V, V, shf, shi);
-  if (threadIdx.x == 0) out[blockIdx.x] = r;
+  unsigned long long best = 0ull;
+  if (vec) {
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    int i = v0 + threadIdx.x;
+    for (; i + 3 * kArgmaxThreads < v1; i += 4 * kArgmaxThreads) {
+      float4 q[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) q[u] = __ldg(r4 + i + u * kArgmaxThreads);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int j = 4 * (i + u * kArgmaxThreads);
+        best = max(best, argmax_key(q[u].x, j));
+        best = max(best, argmax_key(q[u].y, j + 1));
+        best = max(best, argmax_key(q[u].z, j + 2));
+        best = max(best, argmax_key(q[u].w, j + 3));
+      }
+    }
+    for (; i < v1; i += kArgmaxThreads) {
+      const float4 q = __ldg(r4 + i);
+      const int j = 4 * i;
+      best = max(best, argmax_key(q.x, j));
+      best = max(best, argmax_key(q.y, j + 1));
+      best = max(best, argmax_key(q.z, j + 2));
+      best = max(best, argmax_key(q.w, j + 3));
+    }
+    // the V % 4 tail belongs to the last CTA
+    if (rank == kArgmaxCluster - 1)
+      for (int j = 4 * nv4 + threadIdx.x; j < V; j += kArgmaxThreads)
+        best = max(best, argmax_key(row[j], j));
+  } else {
+    const int per1 = (V + kArgmaxCluster - 1) / kArgmaxCluster;
+    const int e = min(V, (rank + 1) * per1);
+    for (int j = rank * per1 + threadIdx.x; j < e; j += kArgmaxThreads)
+      best = max(best, argmax_key(row[j], j));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  if ((threadIdx.x & 31) == 0) warp_best[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    unsigned long long b = threadIdx.x < kArgmaxThreads / 32 ? warp_best[threadIdx.x] : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+    if (threadIdx.x == 0) cta_best = b;
+  }
   pdl_launch();
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  if (rank == 0 && threadIdx.x < 32) {
+    unsigned long long b = 0ull;
+    if (threadIdx.x < kArgmaxCluster) b = *cluster.map_shared_rank(&cta_best, threadIdx.x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+    if (threadIdx.x == 0) out[blockIdx.y] = (int32_t)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
+  }
+  cluster.sync();  // peers keep their shared memory until CTA 0 has read it
 }
 
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(const float* logits, int V,
@@ -325,8 +382,9 @@ extern "C" int higgs_argmax(higgs_ctx* ctx, const float* logits, int B, int V, i
   HG_CHECK_ARG(ctx && logits && out, "higgs_argmax: null argument");
   HG_CHECK_ARG(B >= 0 && V > 0, "higgs_argmax: bad shape");
   if (B == 0) return HIGGS_OK;
-  HG_CUDA(launch_pdl(argmax_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream, logits,
-                     V, out));
+  HG_CHECK_ARG(B <= 65535, "higgs_argmax: B > 65535");
+  HG_CUDA(launch_pdl(argmax_cluster_kernel, dim3(kArgmaxCluster, B), dim3(kArgmaxThreads), 0,
+                     (cudaStream_t)stream, logits, V, out));
   return HIGGS_OK;
 }
 

@@ -194,3 +194,175 @@ class Engine:
         for s in seqs:
             self.release(s)
         return np.concatenate([first, rest], axis=1)
+
+
+class SpecDecoder:
+    """Self-speculative decoding with a layer-skip draft for a fixed batch of sequences.
+
+    Per step: k draft forwards through the first `draft_layers` layers plus the shared
+    LM head (each sampled at `temperature` with explicit uniforms), one verify forward of
+    the k+1 tokens [last, d1..dk] through every layer, then higgs_spec_accept keeps the
+    accepted drafts and draws the corrected (or bonus) token.  Rollback is only a length:
+    cache entries past the accepted prefix are overwritten by later steps.  The whole
+    step is one CUDA graph; per step the host copies in one packed vector (positions,
+    slots, lengths, uniforms) and copies out the accepted counts and tokens.
+
+    The reference engine has no speculative path (one token per forward,
+    crates/higgs-engine/src/simple.rs:880-971); the draft is Model::forward truncated
+    to its first layers (the n_layers field of higgs_forward_args)."""
+
+    def __init__(self, engine: "Engine", B: int, k: int = 5, draft_layers: int = 9,
+                 temperature: float = 0.7, use_graph: bool = True):
+        from . import ffi, ops  # noqa: F401
+        m = engine.model
+        dev = m.device
+        V = m.args.vocab_size
+        self.engine, self.B, self.k, self.T = engine, B, k, float(temperature)
+        self.draft_layers = draft_layers
+        k1 = k + 1
+        self.tok = torch.zeros(k1, B, dtype=torch.int32, device=dev)  # row 0 last, row i+1 draft i
+        self.vtok = torch.zeros(B, k1, dtype=torch.int32, device=dev)
+        self.dtok = torch.zeros(B, k, dtype=torch.int32, device=dev)
+        # packed step vector (int32 words; the i64 slot arrays first, on 8-byte boundaries):
+        # draft slots [k,B] i64 | verify slots [B,k1] i64 | draft pos [k,B] | draft lens [k,B]
+        # | verify pos [B,k1] | verify lens [B] | uniforms f32 [2kB + B]
+        n_words = 4 * k * B + 3 * B * k1 + B + 2 * k * B + B
+        self.step_host = torch.zeros(n_words, dtype=torch.int32, pin_memory=True)
+        self.step_dev = torch.zeros(n_words, dtype=torch.int32, device=dev)
+        o = 0
+
+        def take(n):
+            nonlocal o
+            v = self.step_dev[o:o + n]
+            o += n
+            return v
+        self.d_slots = take(2 * k * B).view(torch.int64).view(k, B)
+        self.v_slots = take(2 * B * k1).view(torch.int64).view(B, k1)
+        self.d_pos = take(k * B).view(k, B)
+        self.d_lens = take(k * B).view(k, B)
+        self.v_pos = take(B * k1).view(B, k1)
+        self.v_lens = take(B)
+        u = take(2 * k * B + B).view(torch.float32)
+        self.u_draft = u[:k * B].view(k, B)
+        self.u_accept = u[k * B:2 * k * B].view(B, k)
+        self.u_final = u[2 * k * B:]
+        self.block_table = torch.zeros(B, engine.max_blocks, dtype=torch.int32, device=dev)
+        self.bt_host = np.zeros((B, engine.max_blocks), np.int32)
+        self.draft_logits = torch.empty(k, B, V, dtype=torch.float32, device=dev)
+        self.draft_bkv = torch.empty(B, k, V, dtype=torch.float32, device=dev)
+        self.target_logits = torch.empty(B, k1, V, dtype=torch.float32, device=dev)
+        self.accepted = torch.zeros(B, dtype=torch.int32, device=dev)
+        self.out_tokens = torch.zeros(B, k1, dtype=torch.int32, device=dev)
+        self.out_host = torch.zeros(B * (k1 + 1), dtype=torch.int32, pin_memory=True)
+        msl = engine.max_seq_len
+        self.fa_draft = [m.forward_args(self.tok[i].view(B, 1), self.d_pos[i].view(B, 1),
+                                        self.d_slots[i].view(B, 1), self.block_table, self.d_lens[i],
+                                        msl, n_layers=draft_layers, logits=self.draft_logits[i])
+                         for i in range(k)]
+        self.fa_verify = m.forward_args(self.vtok, self.v_pos, self.v_slots, self.block_table,
+                                        self.v_lens, msl, last_only=False,
+                                        logits=self.target_logits.view(B * k1, V))
+        self.graph = None
+        if use_graph:
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                self._launch()  # warm-up outside capture (first-call attributes, workspaces)
+            torch.cuda.synchronize(dev)
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph, stream=s):
+                self._launch()
+        self.launches_per_step = None
+
+    def _launch(self):
+        import ctypes
+
+        from . import ffi
+        m = self.engine.model
+        st = torch.cuda.current_stream(m.device).cuda_stream
+        ctx = ffi.ctx(m.device.index or 0)
+        B, k, V = self.B, self.k, m.args.vocab_size
+        for i in range(k):
+            ffi.call("higgs_model_forward", m.handle, ctypes.byref(self.fa_draft[i]), st)
+            ffi.call("higgs_sample", ctx, self.draft_logits[i].data_ptr(), B, V, self.T,
+                     self.u_draft[i].data_ptr(), self.tok[i + 1].data_ptr(), st)
+        self.vtok.copy_(self.tok.t())
+        self.dtok.copy_(self.tok[1:].t())
+        ffi.call("higgs_model_forward", m.handle, ctypes.byref(self.fa_verify), st)
+        self.draft_bkv.copy_(self.draft_logits.transpose(0, 1))
+        ffi.call("higgs_spec_accept", ctx, self.target_logits.data_ptr(), self.draft_bkv.data_ptr(),
+                 self.dtok.data_ptr(), B, k, V, self.T, self.u_accept.data_ptr(),
+                 self.u_final.data_ptr(), self.accepted.data_ptr(), self.out_tokens.data_ptr(), st)
+
+    def stage(self, seqs: list[Sequence], uniforms: np.ndarray, first: bool):
+        """uniforms f32 [2kB + B]: draft draws [k, B], accept tests [B, k], final draws [B]."""
+        eng, B, k = self.engine, self.B, self.k
+        k1 = k + 1
+        sh = self.step_host.numpy()
+        bt_dirty = first
+        d_pos = np.zeros((k, B), np.int32)
+        d_slots = np.zeros((k, B), np.int64)
+        v_pos = np.zeros((B, k1), np.int32)
+        v_slots = np.zeros((B, k1), np.int64)
+        for b, s in enumerate(seqs):
+            before = len(s.pages)
+            eng._ensure_pages(s, s.length + k1)
+            if len(s.pages) != before or first:
+                self.bt_host[b, :len(s.pages)] = s.pages
+                bt_dirty = True
+            pos = s.length + np.arange(k1)
+            pg = np.array(s.pages, np.int64)
+            sl = pg[pos // PAGE] * PAGE + pos % PAGE
+            v_pos[b], v_slots[b] = pos, sl
+            d_pos[:, b], d_slots[:, b] = pos[:k], sl[:k]
+        o = 0
+        sh[o:o + 2 * k * B] = d_slots.reshape(-1).view(np.int32)
+        o += 2 * k * B
+        sh[o:o + 2 * B * k1] = v_slots.reshape(-1).view(np.int32)
+        o += 2 * B * k1
+        sh[o:o + k * B] = d_pos.reshape(-1)
+        o += k * B
+        sh[o:o + k * B] = (d_pos + 1).reshape(-1)
+        o += k * B
+        sh[o:o + B * k1] = v_pos.reshape(-1)
+        o += B * k1
+        sh[o:o + B] = v_pos[:, -1] + 1
+        o += B
+        sh[o:] = np.ascontiguousarray(uniforms, dtype=np.float32).view(np.int32)
+        self.step_dev.copy_(self.step_host, non_blocking=True)
+        if bt_dirty:
+            self.block_table.copy_(torch.from_numpy(self.bt_host), non_blocking=False)
+        if first:
+            self.tok[0].copy_(torch.tensor([s.last_token for s in seqs], dtype=torch.int32))
+
+    def steps(self, seqs: list[Sequence], n_steps: int, rng: np.random.Generator):
+        """Run n_steps speculative steps; returns (tokens generated per sequence, accepted counts
+        [n_steps, B])."""
+        B, k = self.B, self.k
+        assert len(seqs) == B
+        dev = self.engine.model.device
+        acc_hist = np.zeros((n_steps, B), np.int32)
+        for it in range(n_steps):
+            u = rng.random(2 * k * B + B, dtype=np.float32)
+            self.stage(seqs, u, first=(it == 0))
+            if self.graph is not None:
+                self.graph.replay()
+            else:
+                self._launch()
+            oh = self.out_host
+            oh[:B].copy_(self.accepted, non_blocking=True)
+            oh[B:].copy_(self.out_tokens.view(-1), non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+            acc = oh[:B].numpy().copy()
+            toks = oh[B:].numpy().reshape(B, k + 1)
+            acc_hist[it] = acc
+            last = np.empty(B, np.int32)
+            for b, s in enumerate(seqs):
+                n = int(acc[b])
+                new = toks[b, :n + 1]
+                s.generated.extend(int(x) for x in new)
+                s.length += n + 1
+                s.last_token = int(new[-1])
+                last[b] = s.last_token
+            self.tok[0].copy_(torch.from_numpy(last), non_blocking=True)
+        return acc_hist

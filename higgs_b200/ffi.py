@@ -50,6 +50,11 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_spec_accept": (I, [P, P, P, P, I, I, I, F, P, P, P, P, P]),
     "higgs_apply_penalties": (I, [P, P, I, I, P, P, I, F, F, F, P]),
     "higgs_rmsnorm_strided": (I, [P, P, I64, I, I, P, F, P, P]),
+    "higgs_moe_plan_size": (SZ, [I, I, I]),
+    "higgs_moe_route_topk": (I, [P, P, I, I, I, I, I, P, P, P, SZ, P]),
+    "higgs_moe_grouped_w4": (I, [P, P, I, I, I, I, P, P, P, P, P, P, P, I, I, P, P]),
+    "higgs_moe_combine": (I, [P, P, P, I, I, I, P, P]),
+    "higgs_moe_router": (I, [P, P, I, I, P, P, P, I, P, P]),
     "higgs_model_create": (I, [P, P, ctypes.POINTER(P)]),
     "higgs_model_set_tensor": (I, [P, ctypes.c_char_p, P, I, ctypes.POINTER(I64), I]),
     "higgs_model_finalize": (I, [P]),
@@ -82,7 +87,8 @@ class ModelConfig(ctypes.Structure):
     """higgs_model_config (include/higgs_cuda.h)."""
     _fields_ = [("hidden", I), ("layers", I), ("intermediate", I), ("heads", I), ("kv_heads", I),
                 ("head_dim", I), ("vocab", I), ("rms_eps", F), ("rope_theta", F),
-                ("tie_word_embeddings", I), ("qk_norm", I), ("kv_mode", I)]
+                ("tie_word_embeddings", I), ("qk_norm", I), ("kv_mode", I), ("num_experts", I),
+                ("experts_per_tok", I), ("moe_intermediate", I), ("norm_topk_prob", I)]
 
 
 class ForwardArgs(ctypes.Structure):

@@ -33,21 +33,41 @@ class ModelArgs:
     rms_norm_eps: float
     rope_theta: float
     tie_word_embeddings: bool
+    # Qwen3-MoE (Qwen3MoeModelArgs, crates/higgs-models/src/qwen3_moe.rs:37-97)
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    norm_topk_prob: bool = False
+    decoder_sparse_step: int = 1
+    mlp_only_layers: tuple = ()
 
     @property
     def qk_norm(self) -> bool:
         # Attention::new enables q/k RMSNorm for model_type "qwen3" (transformer.rs:193)
         return self.model_type in ("qwen3", "qwen3_moe")
 
+    def is_moe_layer(self, i: int) -> bool:
+        """Qwen3MoeModelArgs::is_moe_layer (qwen3_moe.rs:88-96)."""
+        if self.num_experts <= 0 or self.decoder_sparse_step <= 0:
+            return False
+        if i in self.mlp_only_layers:
+            return False
+        return (i + 1) % self.decoder_sparse_step == 0
+
     def with_layers(self, n: int) -> "ModelArgs":
         return dataclasses.replace(self, num_hidden_layers=n)
 
-    def weight_bytes_per_step(self) -> int:
-        """Bytes of packed weights one decode step streams (embedding: one row)."""
+    def weight_bytes_per_step(self, experts_touched: float = 0.0) -> int:
+        """Bytes of packed weights one decode step streams (embedding: one row).  MoE layers
+        count the router plus `experts_touched` distinct experts per layer."""
         H, D = self.hidden_size, self.head_dim
-        per_layer = (self.num_attention_heads * D * H * 2 + 2 * self.num_key_value_heads * D * H
-                     + 3 * self.intermediate_size * H)
-        params = self.num_hidden_layers * per_layer + self.vocab_size * H
+        attn = self.num_attention_heads * D * H * 2 + 2 * self.num_key_value_heads * D * H
+        params = self.vocab_size * H
+        for i in range(self.num_hidden_layers):
+            if self.is_moe_layer(i):
+                params += attn + self.num_experts * H + experts_touched * 3 * self.moe_intermediate_size * H
+            else:
+                params += attn + 3 * self.intermediate_size * H
         return int(params * 0.5625) + self.num_hidden_layers * 2 * H * 2 + H * 2
 
     def kv_bytes_per_token(self, kv_mode: str = "bf16") -> int:
@@ -62,6 +82,10 @@ PRESETS = {
     "qwen3-1.7b": ModelArgs("qwen3", 2048, 28, 6144, 16, 8, 128, 151936, 1e-6, 1000000.0, True),
     # Qwen3-8B: 36 layers, hidden 4096, 32/8 heads, head_dim 128, FFN 12288, vocab 151936, untied
     "qwen3-8b": ModelArgs("qwen3", 4096, 36, 12288, 32, 8, 128, 151936, 1e-6, 1000000.0, False),
+    # Qwen3-30B-A3B: 48 layers, hidden 2048, 32/4 heads, head_dim 128, 128 experts top-8 of FFN 768
+    "qwen3-30b-a3b": ModelArgs("qwen3_moe", 2048, 48, 6144, 32, 4, 128, 151936, 1e-6, 1000000.0, False,
+                               num_experts=128, num_experts_per_tok=8, moe_intermediate_size=768,
+                               norm_topk_prob=True),
 }
 
 
@@ -69,11 +93,18 @@ def tiny_args(model_type: str = "qwen3", layers: int = 2, vocab: int = 4096) -> 
     """Small shapes for parity tests (same structure, CPU-oracle friendly)."""
     if model_type == "llama":
         return ModelArgs("llama", 512, layers, 1024, 8, 2, 64, vocab, 1e-5, 500000.0, True)
+    if model_type == "qwen3_moe":
+        # layer 1 dense (mlp_only_layers), the others sparse: 32 experts, top-4 of FFN 256
+        return ModelArgs("qwen3_moe", 512, layers, 768, 4, 2, 128, vocab, 1e-6, 1000000.0, False,
+                         num_experts=32, num_experts_per_tok=4, moe_intermediate_size=256,
+                         norm_topk_prob=True, mlp_only_layers=(1,))
     return ModelArgs("qwen3", 512, layers, 768, 4, 2, 128, vocab, 1e-6, 1000000.0, False)
 
 
 def tensor_specs(args: ModelArgs) -> list[tuple[str, str, tuple[int, ...]]]:
-    """(name, kind, shape) of every tensor, kind in {"q4": [N, K] quantized, "norm": [n]}."""
+    """(name, kind, shape) of every tensor, kind in {"q4": [N, K] quantized, "q4router": [E, K]
+    quantized router (N(0, 1/K) init: N(0, 1) logits), "q4e": [E, N, K] stacked experts,
+    "norm": [n]}."""
     H, D = args.hidden_size, args.head_dim
     specs = [("model.embed_tokens", "q4", (args.vocab_size, H)), ("model.norm.weight", "norm", (H,))]
     if not args.tie_word_embeddings:
@@ -87,10 +118,21 @@ def tensor_specs(args: ModelArgs) -> list[tuple[str, str, tuple[int, ...]]]:
             (p + "self_attn.k_proj", "q4", (args.num_key_value_heads * D, H)),
             (p + "self_attn.v_proj", "q4", (args.num_key_value_heads * D, H)),
             (p + "self_attn.o_proj", "q4", (H, args.num_attention_heads * D)),
-            (p + "mlp.gate_proj", "q4", (args.intermediate_size, H)),
-            (p + "mlp.up_proj", "q4", (args.intermediate_size, H)),
-            (p + "mlp.down_proj", "q4", (H, args.intermediate_size)),
         ]
+        if args.is_moe_layer(i):
+            E, F = args.num_experts, args.moe_intermediate_size
+            specs += [
+                (p + "mlp.gate", "q4router", (E, H)),
+                (p + "mlp.switch_mlp.gate_proj", "q4e", (E, F, H)),
+                (p + "mlp.switch_mlp.up_proj", "q4e", (E, F, H)),
+                (p + "mlp.switch_mlp.down_proj", "q4e", (E, H, F)),
+            ]
+        else:
+            specs += [
+                (p + "mlp.gate_proj", "q4", (args.intermediate_size, H)),
+                (p + "mlp.up_proj", "q4", (args.intermediate_size, H)),
+                (p + "mlp.down_proj", "q4", (H, args.intermediate_size)),
+            ]
         if args.qk_norm:
             specs += [(p + "self_attn.q_norm.weight", "norm", (D,)),
                       (p + "self_attn.k_norm.weight", "norm", (D,))]
@@ -124,16 +166,21 @@ def synth_weights_device(args: ModelArgs, seed: int = 0, device="cuda:0", std: f
         if kind == "norm":
             out[name] = torch.ones(shape, dtype=torch.bfloat16, device=device)
             continue
-        N, K = shape
+        lead, K = shape[:-1], shape[-1]
+        N = math.prod(lead)
+        # router: N(0, 1/H) weights give N(0, 1) logits for unit-RMS inputs
+        sd = 1.0 / math.sqrt(K) if kind == "q4router" else std
         g.manual_seed(_seed(seed, name))
         q = torch.empty(N, K // 8, dtype=torch.int32, device=device)
         s = torch.empty(N, K // 64, dtype=torch.bfloat16, device=device)
         b = torch.empty(N, K // 64, dtype=torch.bfloat16, device=device)
         for r0 in range(0, N, chunk_rows):
             r1 = min(N, r0 + chunk_rows)
-            w = torch.randn(r1 - r0, K, generator=g, device=device, dtype=torch.float32) * std
+            w = torch.randn(r1 - r0, K, generator=g, device=device, dtype=torch.float32) * sd
             q[r0:r1], s[r0:r1], b[r0:r1] = ops.quantize(w)
-        out[name + ".weight"], out[name + ".scales"], out[name + ".biases"] = q, s, b
+        out[name + ".weight"] = q.view(*lead, K // 8)
+        out[name + ".scales"] = s.view(*lead, K // 64)
+        out[name + ".biases"] = b.view(*lead, K // 64)
     return out
 
 
@@ -180,7 +227,9 @@ class Model:
                               args.num_attention_heads, args.num_key_value_heads, args.head_dim,
                               args.vocab_size, args.rms_norm_eps, args.rope_theta,
                               int(args.tie_word_embeddings), int(args.qk_norm),
-                              ffi.KV_TQ4 if kv_mode == "tq4" else ffi.KV_BF16)
+                              ffi.KV_TQ4 if kv_mode == "tq4" else ffi.KV_BF16, args.num_experts,
+                              args.num_experts_per_tok, args.moe_intermediate_size,
+                              int(args.norm_topk_prob))
         h = ffi.P()
         ctx = ffi.ctx(self.device.index or 0)
         ffi.call("higgs_model_create", ctx, ctypes.byref(cfg), ctypes.byref(h))

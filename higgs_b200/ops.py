@@ -330,3 +330,69 @@ def apply_penalties(logits, history, hist_lens, rep: float = 1.0, freq: float = 
     ffi.call("higgs_apply_penalties", _ctx(logits), _p(logits), B, V, _p(history), _p(hist_lens),
              history.shape[1], float(rep), float(freq), float(pres), _st(logits.device))
     return logits
+
+
+# ---- a9: mixture of experts ------------------------------------------------------------------
+
+def moe_plan(T: int, E: int, k: int, device) -> torch.Tensor:
+    """Buffer for the routing plan of T tokens, E experts, top-k (higgs_moe_plan_size)."""
+    n = ffi.load().higgs_moe_plan_size(T, E, k)
+    return torch.zeros(max(n, 16), dtype=torch.uint8, device=device)
+
+
+def moe_router(x, w, scales, biases):
+    """Router QLinear of Qwen3MoeMlpBlock (qwen3_moe.rs:301-303) in the fixed summation order
+    of the quantized-matmul restatement: bf16 logits [T, E], bit-reproducible."""
+    _chk(x, torch.bfloat16, "x")
+    T, K = x.shape
+    E = w.shape[0]
+    out = torch.empty(T, E, dtype=torch.bfloat16, device=x.device)
+    ffi.call("higgs_moe_router", _ctx(x), _p(x), T, K, _p(w), _p(scales), _p(biases), E, _p(out),
+             _st(x.device))
+    return out
+
+
+def moe_route_topk(logits, k: int, norm_topk_prob: bool, plan=None):
+    """Router of Qwen3MoeMlpBlock::forward_moe (qwen3_moe.rs:303-316): softmax gates, top-k
+    experts (ties -> lower index), optional renormalisation.  logits bf16 or f32 [T, E].
+    Returns (idx int32 [T, k], scores f32 [T, k]); fills ``plan`` (from moe_plan) if given."""
+    if logits.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError("logits must be bf16 or f32")
+    _chk(logits, logits.dtype, "logits")
+    T, E = logits.shape
+    idx = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    sc = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    dt = ffi.DTYPE_BF16 if logits.dtype == torch.bfloat16 else ffi.DTYPE_F32
+    ffi.call("higgs_moe_route_topk", _ctx(logits), _p(logits), dt, T, E, k, int(norm_topk_prob),
+             _p(idx), _p(sc), _p(plan), 0 if plan is None else plan.numel(), _st(logits.device))
+    return idx, sc
+
+
+def moe_grouped_w4(x, k: int, plan, w, scales, biases, w_up=None, scales_up=None, biases_up=None,
+                   x_per_pair: bool = False):
+    """gather_qmm (qwen3_next.rs:294-363) over the routing plan: one output row per (token,
+    slot) pair.  w u32 [E, N, K/8]; scales/biases bf16 [E, N, K/64].  x bf16 [T, K] (pair p
+    reads row p // k) or, with x_per_pair, [T*k, K].  With w_up: swiglu(gate, up) fused.
+    Returns bf16 [T*k, N]."""
+    _chk(x, torch.bfloat16, "x")
+    E, N, K8 = w.shape
+    K = K8 * 8
+    P = x.shape[0] if x_per_pair else x.shape[0] * k
+    T = P // k
+    y = torch.empty(P, N, dtype=torch.bfloat16, device=x.device)
+    ffi.call("higgs_moe_grouped_w4", _ctx(x), _p(x), T, K, k, int(x_per_pair), _p(plan), _p(w),
+             _p(scales), _p(biases), _p(w_up), _p(scales_up), _p(biases_up), E, N, _p(y),
+             _st(x.device))
+    return y
+
+
+def moe_combine(y, scores, h):
+    """sum_j bf16(score_j) * y[t*k+j] added to the residual h in place (qwen3_moe.rs:319-320,
+    384-385).  y bf16 [T*k, H]; scores f32 [T, k]; h bf16 [T, H]."""
+    _chk(y, torch.bfloat16, "y")
+    _chk(scores, torch.float32, "scores")
+    _chk(h, torch.bfloat16, "h")
+    T, k = scores.shape
+    H = h.shape[-1]
+    ffi.call("higgs_moe_combine", _ctx(h), _p(y), _p(scores), T, k, H, _p(h), _st(h.device))
+    return h

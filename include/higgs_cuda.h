@@ -73,7 +73,12 @@ int higgs_version(void);
 /* Process-wide tuning switches (no reference counterpart).  "gemv_f16" (0/1,
  * default 0): decode GEMVs with x staged in shared memory feed the tensor cores
  * fp16 operands (x scaled per token by a power of two, exact for bf16 inputs)
- * instead of bf16 ones.  Unknown names return HIGGS_ERR_INVALID_ARG. */
+ * instead of bf16 ones.  "attn_min_pages" (4..64, default 8): KV pages per split
+ * of higgs_fused_attention; change it only between captures, since workspace
+ * sizes depend on it.  "l2_prefetch" (bit mask, default 0): bit 0 makes every
+ * GEMV of the decode step ask the TMA unit to pull the next GEMV's weights into
+ * L2, bit 1 makes each GEMV CTA pull its own weight tiles (a hint; results are
+ * unchanged).  Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
 /* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
@@ -310,16 +315,70 @@ int higgs_apply_penalties(higgs_ctx* ctx, float* logits, int B, int V, const int
                           const int32_t* hist_lens, int max_hist, float rep, float freq,
                           float pres, void* stream);
 
+/* ---- a9: mixture of experts (qwen3_moe.rs Qwen3MoeMlpBlock) ------------- */
+
+/* Bytes of the routing plan higgs_moe_route_topk writes for T tokens, E
+ * experts and top-k: the (token, slot) pairs p = t*k + j grouped by expert
+ * and cut into work items of at most 8 pairs of one expert, which
+ * higgs_moe_grouped_w4 consumes. */
+size_t higgs_moe_plan_size(int T, int E, int k);
+
+/* Router of Qwen3MoeMlpBlock::forward_moe (crates/higgs-models/src/
+ * qwen3_moe.rs:303-316): gates = softmax(logits) in f32, the k experts with
+ * the largest logits (ties -> lower expert index; softmax is monotonic, so
+ * this is MLX's argpartition(-k) over the gates with the tie order fixed),
+ * scores = their gates, renormalised to sum 1 when norm_topk_prob.
+ * logits [T, E] (dtype HIGGS_DTYPE_BF16 -- the router QLinear's output -- or
+ * HIGGS_DTYPE_F32); idx int32 [T, k] and scores f32 [T, k] in descending
+ * order.  plan (nullable) receives the routing plan.  E <= 1024, k <= 32,
+ * T*k <= 65536. */
+int higgs_moe_route_topk(higgs_ctx* ctx, const void* logits, int dtype, int T, int E, int k,
+                         int norm_topk_prob, int32_t* idx, float* scores, void* plan,
+                         size_t plan_bytes, void* stream);
+
+/* The router QLinear of Qwen3MoeMlpBlock (qwen3_moe.rs:301-303, `gate`):
+ * logits bf16 [T, E] = x bf16 [T, K] . dequant(w [E, K/8])^T, summed in a
+ * fixed order -- per (row, group of 64) the products x*q and the x values in
+ * k order, then s*sum(xq) + b*sum(x) added in group order -- so the expert
+ * choice downstream (a discontinuous function of these logits) is
+ * reproducible bit for bit.  K % 64 == 0, K <= 16384. */
+int higgs_moe_router(higgs_ctx* ctx, const void* x, int T, int K, const uint32_t* w,
+                     const void* scales, const void* biases, int E, void* logits, void* stream);
+
+/* gather_qmm (crates/higgs-models/src/qwen3_next.rs:294-363) as used by
+ * SwitchMlpWeights::forward_gather (qwen3_next.rs:844-904): for every pair p
+ * of the plan, y[p] = x[row(p)] . dequant(w[expert(p)])^T, row(p) = p / k when
+ * x_per_pair = 0 (x has T rows: the gate / up projections) or p when 1 (x has
+ * T*k rows: the down projection).  w u32 [E, N, K/8], scales / biases bf16
+ * [E, N, K/64] (MLX SwitchLinear layout).  With w_up set the call is the fused
+ * gate / up pair and y[p] = silu(gate) * up (swiglu, qwen3_next.rs:275-277).
+ * y bf16 [T*k, N]. */
+int higgs_moe_grouped_w4(higgs_ctx* ctx, const void* x, int T, int K, int k, int x_per_pair,
+                         const void* plan, const uint32_t* w, const void* scales,
+                         const void* biases, const uint32_t* w_up, const void* scales_up,
+                         const void* biases_up, int E, int N, void* y, void* stream);
+
+/* The weighted sum over the k expert outputs and the residual add of the
+ * decoder layer (qwen3_moe.rs:319-320, 384-385): h[t] = bf16(h[t] +
+ * bf16(sum_j bf16(scores[t,j]) * y[t*k+j])), f32 accumulation in j order.
+ * y bf16 [T*k, H]; h bf16 [T, H] in place. */
+int higgs_moe_combine(higgs_ctx* ctx, const void* y, const float* scores, int T, int k, int H,
+                      void* h, void* stream);
+
 /* ---- a7/a11: native decode step (transformer.rs Model) ------------------ */
 
 /* ModelArgs (crates/higgs-models/src/transformer.rs:69-97) reduced to what the
- * step needs.  qk_norm = 1 for model_type "qwen3" (transformer.rs:193). */
+ * step needs.  qk_norm = 1 for model_type "qwen3" (transformer.rs:193).
+ * Qwen3-MoE (Qwen3MoeModelArgs, qwen3_moe.rs:37-97): num_experts > 0 enables
+ * the sparse block on every layer that registers "mlp.gate" (router) and
+ * "mlp.switch_mlp.{gate,up,down}_proj"; the others stay dense. */
 typedef struct {
   int hidden, layers, intermediate, heads, kv_heads, head_dim, vocab;
   float rms_eps, rope_theta;
   int tie_word_embeddings;
   int qk_norm;
   int kv_mode; /* HIGGS_KV_BF16 or HIGGS_KV_TQ4 */
+  int num_experts, experts_per_tok, moe_intermediate, norm_topk_prob;
 } higgs_model_config;
 
 /* One forward over B sequences x Lq new tokens (Lq = 1 decode, k+1 verify,

@@ -664,38 +664,64 @@ void orc_apply_penalties(float* logits, int64_t V, const int32_t* history, int64
 
 /*
  * Qwen3MoeMlpBlock::forward_moe router (qwen3_moe.rs:303-316):
- * gates = softmax(logits) (f32, "precise"), top-k experts by gate value,
- * ties -> lower expert index, listed in descending gate order; scores
- * renormalised to sum 1 when norm_topk_prob.  logits [T, E] f32.
+ * gates = softmax(logits) in f32 (orc_exp, the deterministic exp), the k
+ * experts with the largest logits -- softmax is monotonic, so these are the
+ * top-k gates of MLX's argpartition(-k) -- with ties to the lower expert index
+ * and NaN never preferred, listed in descending order; scores = their gates,
+ * renormalised to sum 1 (summed in selection order) when norm_topk_prob.
+ * logits [T, E] f32.
  */
+static int moe_better(float a, int64_t ia, float b, int64_t ib) {
+  /* a strictly preferred over b: larger, NaN lowest, -0 == +0, ties -> lower index */
+  if (a != a) return (b != b) && ia < ib;
+  if (b != b) return 1;
+  if (a != b) return a > b;
+  return ia < ib;
+}
+
 void orc_moe_route_topk(const float* logits, int64_t T, int64_t E, int64_t k, int norm,
                         int32_t* idx, float* scores) {
-  float* g = (float*)malloc(sizeof(float) * (size_t)E);
+  char* taken = (char*)malloc((size_t)E);
   for (int64_t t = 0; t < T; ++t) {
     const float* l = logits + t * E;
-    float mx = l[0];
-    for (int64_t e = 1; e < E; ++e) mx = l[e] > mx ? l[e] : mx;
+    float mx = -INFINITY;
+    for (int64_t e = 0; e < E; ++e)
+      if (l[e] > mx) mx = l[e];
     float den = 0.0f;
-    for (int64_t e = 0; e < E; ++e) {
-      g[e] = expf(l[e] - mx);
-      den += g[e];
-    }
-    for (int64_t e = 0; e < E; ++e) g[e] /= den;
+    for (int64_t e = 0; e < E; ++e) den += orc_exp(l[e] - mx);
+    memset(taken, 0, (size_t)E);
     float ssum = 0.0f;
     for (int64_t i = 0; i < k; ++i) {
       int64_t best = -1;
-      for (int64_t e = 0; e < E; ++e) {
-        int taken = 0;
-        for (int64_t j = 0; j < i; ++j) taken |= (idx[t * k + j] == e);
-        if (taken) continue;
-        if (best < 0 || g[e] > g[best]) best = e;
-      }
+      for (int64_t e = 0; e < E; ++e)
+        if (!taken[e] && (best < 0 || moe_better(l[e], e, l[best], best))) best = e;
+      taken[best] = 1;
+      const float g = orc_exp(l[best] - mx) / den;
       idx[t * k + i] = (int32_t)best;
-      scores[t * k + i] = g[best];
-      ssum += g[best];
+      scores[t * k + i] = g;
+      ssum += g;
     }
     if (norm)
       for (int64_t i = 0; i < k; ++i) scores[t * k + i] /= ssum;
   }
-  free(g);
+  free(taken);
+}
+
+/*
+ * The weighted sum over the k expert outputs and the residual add
+ * (qwen3_moe.rs:319-320, 384-385) with MLX's bf16 rounding points:
+ * h[t] = bf16(h[t] + bf16(sum_j bf16(s_j) * y[t*k+j])), f32 in j order.
+ * y bf16 [T*k, H], scores f32 [T, k], h bf16 [T, H] in place.
+ */
+void orc_moe_combine(const uint16_t* y, const float* scores, int64_t T, int64_t k, int64_t H,
+                     uint16_t* h) {
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t c = 0; c < H; ++c) {
+      float acc = 0.0f;
+      for (int64_t j = 0; j < k; ++j) {
+        const float sc = bf2f(f2bf(scores[t * k + j]));
+        acc = acc + sc * bf2f(y[(t * k + j) * H + c]);
+      }
+      h[t * H + c] = f2bf(bf2f(h[t * H + c]) + bf2f(f2bf(acc)));
+    }
 }

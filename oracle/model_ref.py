@@ -30,8 +30,13 @@ def synth_weights_numpy(args, seed: int = 0, std: float = 0.02) -> dict:
             out[name] = np.full(shape, 0x3F80, np.uint16)
             continue
         rng = np.random.default_rng(_seed(seed, name))
-        q, s, b = orc.w4_quantize(rng.normal(0, std, size=shape).astype(np.float32))
-        out[name + ".weight"], out[name + ".scales"], out[name + ".biases"] = q, s, b
+        lead, K = shape[:-1], shape[-1]
+        sd = 1.0 / np.sqrt(K) if kind == "q4router" else std  # router logits N(0, 1)
+        w = rng.normal(0, sd, size=(int(np.prod(lead)), K)).astype(np.float32)
+        q, s, b = orc.w4_quantize(w)
+        out[name + ".weight"] = q.reshape(*lead, K // 8)
+        out[name + ".scales"] = s.reshape(*lead, K // 64)
+        out[name + ".biases"] = b.reshape(*lead, K // 64)
     return out
 
 
@@ -47,6 +52,17 @@ class RefModel:
         self.signs = signs
         self.inv = np.array([args.rope_theta ** (-(2.0 * i) / args.head_dim)
                              for i in range(args.head_dim // 2)], dtype=np.float32)
+
+    def _note_route_margin(self, lf, k, B, Lq):
+        """Flag sequences whose k-th and (k+1)-th router logits lie within one bf16 ulp: there a
+        last-bit difference in the router's input may legitimately swap an expert."""
+        srt = -np.sort(-lf, axis=1)
+        if srt.shape[1] <= k:
+            return
+        top, nxt = srt[:, k - 1], srt[:, k]
+        ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(top), 1e-30))) - 7)
+        near = (top - nxt) <= ulp
+        self.route_near |= near.reshape(B, Lq).any(axis=1)
 
     def q(self, name):
         return self.w[name + ".weight"], self.w[name + ".scales"], self.w[name + ".biases"]
@@ -64,6 +80,7 @@ class RefModel:
         B, Lq = tokens.shape
         H, D, Hq, Hkv = a.hidden_size, a.head_dim, a.num_attention_heads, a.num_key_value_heads
         nl = n_layers or a.num_hidden_layers
+        self.route_near = np.zeros(B, bool)
         h = orc.embed_gather(tokens.reshape(-1), *self.q("model.embed_tokens"))  # [T, H]
         offs = [c[0][0].shape[0] for c in caches]
         for li in range(nl):
@@ -106,6 +123,17 @@ class RefModel:
             o = orc.qmatmul(attn.reshape(B * Lq, Hq * D), *self.q(p + "self_attn.o_proj"))
             h = _add_bf(h, o)
             x = orc.rmsnorm(h, self.w[p + "post_attention_layernorm.weight"], a.rms_norm_eps)[0]
+            if a.is_moe_layer(li):
+                # Qwen3MoeMlpBlock::forward_moe (qwen3_moe.rs:293-322): bf16 router logits
+                rl = orc.qmatmul(x, *self.q(p + "mlp.gate"))
+                lf = orc.bf16_to_f32(rl)
+                idx, sc = orc.moe_route_topk(lf, a.num_experts_per_tok, a.norm_topk_prob)
+                self._note_route_margin(lf, a.num_experts_per_tok, B, Lq)
+                sw = p + "mlp.switch_mlp."
+                y = orc.moe_experts(x, idx, self.q(sw + "gate_proj"), self.q(sw + "up_proj"),
+                                    self.q(sw + "down_proj"))
+                h = orc.moe_combine(y, sc, h)
+                continue
             g = orc.qmatmul(x, *self.q(p + "mlp.gate_proj"))
             u = orc.qmatmul(x, *self.q(p + "mlp.up_proj"))
             d = orc.qmatmul(orc.silu_mul(g, u), *self.q(p + "mlp.down_proj"))
@@ -121,10 +149,14 @@ class RefModel:
         B = prompts.shape[0]
         caches = [self.new_cache() for _ in range(B)]
         lg = self.forward(prompts, caches)[:, -1]
-        toks, all_lg = [], []
+        toks, all_lg, near = [], [], []
         for _ in range(steps):
             nxt = orc.argmax(lg)
             toks.append(nxt)
             all_lg.append(lg)
+            near.append(self.route_near.copy())
             lg = self.forward(nxt.reshape(B, 1).astype(np.int32), caches)[:, -1]
+        # [steps, B]: the MoE routing of that step's logits had a near-tie (always False
+        # for dense models)
+        self.step_route_near = np.stack(near)
         return np.stack(toks, 1), np.stack(all_lg)

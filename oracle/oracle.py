@@ -266,7 +266,8 @@ def apply_penalties(logits, history, rep=1.0, freq=0.0, pres=0.0) -> np.ndarray:
 
 
 def moe_route_topk(logits, k: int, norm: bool):
-    """Qwen3MoeMlpBlock router (qwen3_moe.rs:303-316): (idx int32 [T,k], scores f32 [T,k])."""
+    """Qwen3MoeMlpBlock router (qwen3_moe.rs:303-316): (idx int32 [T,k], scores f32 [T,k]).
+    Top-k by logit, ties to the lower expert index; gates softmax in f32."""
     lg = np.ascontiguousarray(logits, dtype=np.float32)
     T, E = lg.shape
     idx = np.empty((T, k), np.int32)
@@ -274,3 +275,32 @@ def moe_route_topk(logits, k: int, norm: bool):
     lib().orc_moe_route_topk(_ptr(lg), I64(T), I64(E), I64(k), ctypes.c_int(int(norm)), _ptr(idx),
                              _ptr(sc))
     return idx, sc
+
+
+def moe_combine(y, scores, h):
+    """sum_j score_j * y_j + residual (qwen3_moe.rs:319-320, 384-385) with MLX's bf16
+    rounding points; y bf16 [T*k, H], scores f32 [T, k], h bf16 [T, H] -> new h."""
+    sc = np.ascontiguousarray(scores, dtype=np.float32)
+    T, k = sc.shape
+    yy = np.ascontiguousarray(y, dtype=np.uint16)
+    out = np.array(h, dtype=np.uint16, copy=True)
+    H = out.shape[-1]
+    lib().orc_moe_combine(_ptr(yy), _ptr(sc), I64(T), I64(k), I64(H), _ptr(out))
+    return out
+
+
+def moe_experts(x, idx, w_gate, w_up, w_down):
+    """SwitchMlpWeights::forward_gather (qwen3_next.rs:844-904) for each (token, slot) pair,
+    evaluated one expert at a time with qmatmul (gather_qmm == per-expert quantized_matmul,
+    qwen3_next.rs:2151-2206).  x bf16 [T, H]; idx int32 [T, k]; w_* = (q [E,N,K/8], s, b).
+    Returns bf16 [T*k, H]."""
+    T, k = idx.shape
+    Hd = w_down[0].shape[1]
+    out = np.zeros((T * k, Hd), np.uint16)
+    for e in np.unique(idx):
+        pairs = np.nonzero(idx.reshape(-1) == e)[0]
+        xe = np.ascontiguousarray(x[pairs // k])
+        g = qmatmul(xe, w_gate[0][e], w_gate[1][e], w_gate[2][e])
+        u = qmatmul(xe, w_up[0][e], w_up[1][e], w_up[2][e])
+        out[pairs] = qmatmul(silu_mul(g, u), w_down[0][e], w_down[1][e], w_down[2][e])
+    return out

@@ -368,6 +368,24 @@ def test_argmax(kat):
     rng = np.random.default_rng(41)
     lg = rng.normal(size=(4, 151936)).astype(np.float32)
     lg[2, 100] = lg[2, 5000] = lg[2].max() + 1.0  # tie -> first
+    lg[3, 150000] = lg[3, 7] = lg[3].max() + 1.0  # tie across cluster slices -> first
+    assert np.array_equal(o.argmax(t(lg)).cpu().numpy(), orc.argmax(lg))
+
+
+@pytest.mark.parametrize("V", [1, 3, 7, 31, 4099, 32001, 151937])
+def test_argmax_edges(V):
+    """Ragged rows (V % 4 != 0 leaves odd rows unaligned), NaN, -0/+0, all -inf."""
+    o = ops()
+    rng = np.random.default_rng(V)
+    lg = rng.normal(size=(5, V)).astype(np.float32)
+    lg[0, :] = np.nan                      # all NaN -> 0
+    lg[1, :] = -np.inf                     # all -inf -> 0
+    lg[1, V // 2] = np.nan                 # NaN never beats -inf
+    lg[2, :] = -1.0
+    lg[2, V - 1] = 0.0
+    lg[2, V // 3] = -0.0                   # -0 == +0 -> the lower index
+    lg[3, V - 1] = 1e30                    # winner in the ragged tail
+    lg[4, rng.integers(0, V, size=max(1, V // 7))] = np.nan
     assert np.array_equal(o.argmax(t(lg)).cpu().numpy(), orc.argmax(lg))
 
 

@@ -243,3 +243,42 @@ def test_moe_route_topk():
     p = np.exp(lg[0] - lg[0].max())
     p /= p.sum()
     np.testing.assert_allclose(sc2[0], p[[1, 3]], rtol=1e-6)
+
+
+def test_moe_route_nan_signed_zero_and_ties():
+    """NaN is never preferred, -0 == +0 (lower index first), exact ties -> lower index."""
+    lg = np.array([[np.nan, 0.0, -0.0, 1.0, 1.0, -np.inf]], np.float32)
+    idx, _ = orc.moe_route_topk(lg, 5, False)
+    assert idx.tolist() == [[3, 4, 1, 2, 5]]
+    lg2 = np.array([[-0.0, 0.0]], np.float32)
+    assert orc.moe_route_topk(lg2, 1, True)[0].tolist() == [[0]]
+
+
+def test_moe_combine_rounding_points():
+    """h + bf16(sum_j bf16(s_j) y_j): scores rounded to bf16 before the product."""
+    y = orc.f32_to_bf16(np.array([[1.0], [1.0]], np.float32))
+    sc = np.array([[0.3, 0.7]], np.float32)
+    h = orc.f32_to_bf16(np.array([[256.0]], np.float32))
+    out = orc.bf16_to_f32(orc.moe_combine(y, sc, h))
+    s_bf = orc.bf16_to_f32(orc.f32_to_bf16(sc))[0]
+    acc = orc.bf16_to_f32(orc.f32_to_bf16(np.float32(s_bf[0] + s_bf[1])))
+    assert out[0, 0] == orc.bf16_to_f32(orc.f32_to_bf16(np.float32(256.0) + acc))
+
+
+def test_moe_experts_equal_dense_per_expert():
+    """gather over experts == quantized_matmul on each expert's slice (qwen3_next.rs:2151-2206)."""
+    rng = np.random.default_rng(8)
+    E, F, H, T, k = 4, 256, 256, 3, 2
+    mk = lambda N, K: [a.reshape(E, N, -1) for a in orc.w4_quantize(
+        rng.normal(0, 0.02, size=(E * N, K)).astype(np.float32))]
+    wg, wu, wd = mk(F, H), mk(F, H), mk(H, F)
+    x = orc.f32_to_bf16(rng.normal(0, 1, size=(T, H)))
+    idx = np.array([[2, 0], [1, 2], [3, 3]], np.int32)
+    y = orc.moe_experts(x, idx, wg, wu, wd)
+    for t_ in range(T):
+        for j in range(k):
+            e = idx[t_, j]
+            g = orc.qmatmul(x[t_:t_ + 1], wg[0][e], wg[1][e], wg[2][e])
+            u = orc.qmatmul(x[t_:t_ + 1], wu[0][e], wu[1][e], wu[2][e])
+            d = orc.qmatmul(orc.silu_mul(g, u), wd[0][e], wd[1][e], wd[2][e])
+            assert np.array_equal(y[t_ * k + j], d[0])
