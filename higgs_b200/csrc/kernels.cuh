@@ -11,6 +11,18 @@ namespace higgs {
 
 enum { EPI_STORE = 0, EPI_SWIGLU = 1 };
 
+constexpr int kMaxRanks = 8;  // tensor-parallel ranks per communicator
+
+// tensor-parallel collectives (comm.cu)
+cudaError_t comm_step(higgs_comm* c, cudaStream_t st);
+cudaError_t comm_allreduce_residual(higgs_comm* c, int call, const float* partial, int n, uint16_t* h,
+                                    cudaStream_t st);
+cudaError_t comm_allreduce_argmax(higgs_comm* c, int call, const unsigned long long* keys, int n,
+                                  int32_t* out, cudaStream_t st);
+// greedy argmax keys of rows of f32 logits whose column j is vocabulary id j + offset
+cudaError_t launch_argmax_keys(const float* logits, int B, int V, int offset, unsigned long long* keys,
+                               cudaStream_t st);
+
 struct QLinArgs {
   const uint16_t* x;
   int M, K, N;

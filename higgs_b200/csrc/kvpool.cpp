@@ -9,7 +9,8 @@
 // full 16-token pages are ever stored, a page in the cache is immutable --
 // appending to a sequence always writes a page that sequence owns alone.
 // Trie semantics follow prompt_cache.rs: MIN_PREFIX_LEN = 16 (line 8), the
-// deepest cached node at depth >= 16 wins (find_deepest_match 68-98), edges
+// deepest match at depth >= 16 wins (find_deepest_match 68-98; here extended to
+// prefixes that end inside an edge, served from a cached descendant's pages), edges
 // split on partial matches (insert 224-270), least-recently-used eviction
 // beyond max entries (evict_lru 280-287) followed by pruning / compression
 // (prune 139-158).  Access time is a logical clock, not wall time.
@@ -69,24 +70,59 @@ void pool_retain(higgs_block_pool* p, const std::vector<int32_t>& pages) {
   for (int32_t pg : pages) p->refcount[pg]++;
 }
 
+// any cached node in n's subtree (its pages begin with the pages of every prefix of it)
+const Node* any_cached(const Node& n) {
+  if (n.cached) return &n;
+  for (const auto& kv : n.children)
+    if (const Node* c = any_cached(*kv.second)) return c;
+  return nullptr;
+}
+
+// Longest reusable prefix of the query, in whole pages.  The reference matches only
+// cached nodes whose whole token sequence prefixes the query (find_deepest_match);
+// with immutable pages any matched prefix -- ending inside an edge or at an internal
+// node -- can also be served from the leading pages of a cached descendant.  Returns
+// the node whose pages to use; *best_depth = tokens matched (a multiple of 16).
 const Node* find_deepest(const Node& n, const int32_t* tok, int len, int depth, int* best_depth) {
-  const Node* best = (n.cached && depth >= kMinPrefix) ? &n : nullptr;
-  if (best) *best_depth = depth;
-  if (depth >= len) return best;
-  auto it = n.children.find(tok[depth]);
-  if (it == n.children.end()) return best;
-  const Node& c = *it->second;
-  int common = 0;
-  while (common < (int)c.edge.size() && depth + common < len && c.edge[common] == tok[depth + common])
-    ++common;
-  if (common == (int)c.edge.size()) {
-    int d = 0;
-    const Node* deeper = find_deepest(c, tok, len, depth + common, &d);
-    if (deeper) {
-      *best_depth = d;
-      return deeper;
+  const Node* best = nullptr;
+  int bd = 0;
+  if (depth >= kMinPrefix) {
+    const int m = depth / kPage * kPage;
+    if (n.cached && m == depth) {
+      best = &n;
+      bd = depth;
+    } else if (m >= kMinPrefix) {
+      best = any_cached(n);
+      bd = best ? m : 0;
     }
   }
+  if (depth < len) {
+    auto it = n.children.find(tok[depth]);
+    if (it != n.children.end()) {
+      const Node& c = *it->second;
+      int common = 0;
+      while (common < (int)c.edge.size() && depth + common < len &&
+             c.edge[common] == tok[depth + common])
+        ++common;
+      if (common == (int)c.edge.size()) {
+        int d = 0;
+        const Node* deeper = find_deepest(c, tok, len, depth + common, &d);
+        if (deeper && d > bd) {
+          best = deeper;
+          bd = d;
+        }
+      } else {
+        const int m = (depth + common) / kPage * kPage;
+        if (m >= kMinPrefix && m > bd) {
+          if (const Node* src = any_cached(c)) {
+            best = src;
+            bd = m;
+          }
+        }
+      }
+    }
+  }
+  *best_depth = bd;
   return best;
 }
 
@@ -304,14 +340,15 @@ extern "C" int higgs_prefix_cache_lookup(higgs_prefix_cache* pc, const int32_t* 
   *matched_tokens = 0;
   int depth = 0;
   const Node* hit = find_deepest(pc->root, tokens, n, 0, &depth);
-  if (!hit) return HIGGS_OK;
-  const int np = (int)hit->pages.size();
+  if (!hit || depth < kMinPrefix) return HIGGS_OK;
+  const int np = depth / kPage;
   if (np > max_pages)
     return fail(HIGGS_ERR_INVALID_ARG, "higgs_prefix_cache_lookup: pages_out holds " +
                                            std::to_string(max_pages) + ", match needs " + std::to_string(np));
   const_cast<Node*>(hit)->last_access = ++pc->clock;
-  for (int i = 0; i < np; ++i) pages_out[i] = hit->pages[i];
-  pool_retain(pc->pool, hit->pages);  // the caller's reference
+  std::vector<int32_t> used(hit->pages.begin(), hit->pages.begin() + np);
+  for (int i = 0; i < np; ++i) pages_out[i] = used[i];
+  pool_retain(pc->pool, used);  // the caller's reference
   *matched_tokens = depth;
   return HIGGS_OK;
 }

@@ -71,6 +71,7 @@ struct higgs_model {
   void* v_scales = nullptr;
   const int8_t* signs = nullptr;
   int64_t num_pages = 0;
+  higgs_comm* comm = nullptr;  // tensor-parallel shard: sums / argmax over ranks
 };
 
 struct higgs_graph {
@@ -86,8 +87,10 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
   size_t h, x, qkv, q, attn, act, xl, logits, moe_rl, moe_idx, moe_sc, moe_plan, moe_act, moe_y,
-      attn_ws, total;
+      tp_part, tp_keys, attn_ws, total;
 };
+
+int head_rows(const higgs_model_config& c) { return c.tp_world > 1 ? c.head_rows : c.vocab; }
 
 
 
@@ -109,7 +112,11 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
   L.attn = take(T * (size_t)c.heads * D * 2);
   L.act = take(T * (size_t)c.intermediate * 2);
   L.xl = take(rows_lm * c.hidden * 2);
-  L.logits = take(rows_lm * (size_t)c.vocab * 4);
+  L.logits = take(rows_lm * (size_t)head_rows(c) * 4);
+  if (c.tp_world > 1) {
+    L.tp_part = take(T * c.hidden * 4);
+    L.tp_keys = take(rows_lm * 8);
+  }
   if (c.num_experts > 0) {
     const size_t P = T * c.experts_per_tok;
     L.moe_rl = take(T * (size_t)c.num_experts * 2);
@@ -252,6 +259,28 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
     a.residual = res;
     return launch_qgemv_ring(a, EPI_STORE, st);
   };
+  const bool tp = c.tp_world > 1;
+  float* part = tp ? (float*)(ws + L.tp_part) : nullptr;
+  if (tp) HG_CUDA(comm_step(m->comm, st));
+  // row-parallel GEMV (o_proj / down_proj): this rank's K slice, then the sum over
+  // ranks added to the residual stream, or the residual epilogue on one GPU
+  auto row_parallel = [&](const QW& w, const uint16_t* xin, int call, const L2Prefetch* pf) -> int {
+    if (!tp) {
+      HG_CUDA(lin(w, xin, nullptr, h, nullptr, h, pf));
+      return HIGGS_OK;
+    }
+    HG_CUDA(lin(w, xin, nullptr, nullptr, part, nullptr, pf));
+    HG_CUDA(comm_allreduce_residual(m->comm, call, part, T * H, h, st));
+    return HIGGS_OK;
+  };
+  // greedy tokens from this rank's logits (vocabulary shard under tensor parallelism)
+  auto emit_argmax = [&](const float* lg, int rows) -> int {
+    if (!tp) return higgs_argmax(m->ctx, lg, rows, c.vocab, f->argmax, st);
+    unsigned long long* keys = (unsigned long long*)(ws + L.tp_keys);
+    HG_CUDA(launch_argmax_keys(lg, rows, c.head_rows, c.tp_rank * c.head_rows, keys, st));
+    HG_CUDA(comm_allreduce_argmax(m->comm, 2 * c.layers, keys, rows, f->argmax, st));
+    return HIGGS_OK;
+  };
   int rc = higgs_embed_gather_w4(m->ctx, f->tokens, T, m->embed.w, m->embed.s, m->embed.b, c.vocab,
                                  H, h, st);
   if (rc) return rc;
@@ -340,7 +369,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
     {
       L2Prefetch pf{};
       if (!Lw.moe) add_q(pf, Lw.down);
-      HG_CUDA(lin(Lw.o, attn, nullptr, h, nullptr, h, &pf));
+      if ((rc = row_parallel(Lw.o, attn, 2 * li, &pf))) return rc;
     }
     if (Lw.moe) {
       // Qwen3MoeMlpBlock::forward_moe: router -> top-k plan -> grouped gate/up SwiGLU ->
@@ -403,14 +432,14 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       }
       HG_CUDA(launch_qgemv_ring(a, EPI_SWIGLU, st));
     }
-    HG_CUDA(lin(Lw.down, act, nullptr, h, nullptr, h));
+    if ((rc = row_parallel(Lw.down, act, 2 * li + 1, nullptr))) return rc;
   }
   // final norm (+ last-token selection) and LM head
   const int rows_lm = f->last_only ? B : T;
   if (fuse && (Lq == 1 || !f->last_only) && !f->hidden_out) {
     if (f->logits || f->argmax) HG_CUDA(lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
     if (f->argmax) {
-      rc = higgs_argmax(m->ctx, logits, rows_lm, c.vocab, f->argmax, st);
+      rc = emit_argmax(logits, rows_lm);
       if (rc) return rc;
     }
     return HIGGS_OK;
@@ -437,7 +466,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
     HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
   }
   if (f->argmax) {
-    rc = higgs_argmax(m->ctx, logits, rows_lm, c.vocab, f->argmax, st);
+    rc = emit_argmax(logits, rows_lm);
     if (rc) return rc;
   }
   if (f->hidden_out) {
@@ -457,6 +486,8 @@ int validate_forward(higgs_model* m, const higgs_forward_args* f) {
   HG_CHECK_ARG(f->max_seq_len >= f->Lq && (int64_t)f->max_blocks * HIGGS_PAGE_SIZE >= f->max_seq_len,
                "higgs_model_forward: max_seq_len / max_blocks inconsistent");
   HG_CHECK_ARG(f->workspace, "higgs_model_forward: null workspace");
+  if (m->cfg.tp_world > 1 && !m->comm)
+    return fail(HIGGS_ERR_STATE, "higgs_model_forward: tensor-parallel shard without a communicator");
   HG_CHECK_ARG(m->cfg.num_experts == 0 || (int64_t)f->B * f->Lq * m->cfg.experts_per_tok <= 65536,
                "higgs_model_forward: MoE routes at most 65536 (token, expert) pairs per call");
   return HIGGS_OK;
@@ -478,6 +509,13 @@ extern "C" int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg,
   HG_CHECK_ARG((c.heads * c.head_dim) % 256 == 0, "higgs_model_create: heads*head_dim must be a multiple of 256");
   HG_CHECK_ARG(c.kv_mode == HIGGS_KV_BF16 || (c.kv_mode == HIGGS_KV_TQ4 && c.head_dim == 128),
                "higgs_model_create: TurboQuant KV needs head_dim 128");
+  if (c.tp_world > 1) {
+    HG_CHECK_ARG(c.tp_world <= kMaxRanks && c.tp_rank >= 0 && c.tp_rank < c.tp_world,
+                 "higgs_model_create: bad tp_rank / tp_world (tp_world <= 8)");
+    HG_CHECK_ARG(c.head_rows > 0 && c.head_rows % 16 == 0 && (int64_t)c.head_rows * c.tp_world == c.vocab,
+                 "higgs_model_create: head_rows * tp_world must equal vocab (head_rows % 16 == 0)");
+    HG_CHECK_ARG(c.num_experts == 0, "higgs_model_create: tensor parallelism covers dense models");
+  }
   if (c.num_experts > 0) {
     HG_CHECK_ARG(c.num_experts <= 1024 && c.num_experts % 16 == 0,
                  "higgs_model_create: num_experts must be a multiple of 16, at most 1024");
@@ -527,8 +565,15 @@ extern "C" int higgs_model_finalize(higgs_model* m) {
   if (rc) return rc;
   if (c.tie_word_embeddings) {
     m->head = m->embed;
+    if (c.tp_world > 1) {  // this rank's rows of the tied table
+      const size_t r0 = (size_t)c.tp_rank * c.head_rows;
+      m->head.w += r0 * (H / 8);
+      m->head.s += r0 * (H / 64);
+      m->head.b += r0 * (H / 64);
+      m->head.N = c.head_rows;
+    }
   } else {
-    rc = get_q(m, "lm_head", c.vocab, H, m->head);
+    rc = get_q(m, "lm_head", head_rows(c), H, m->head);
     if (rc) return rc;
   }
   rc = get_vec(m, "model.norm.weight", H, m->final_norm);
@@ -569,6 +614,13 @@ extern "C" int higgs_model_finalize(higgs_model* m) {
   }
   attention_prepare();
   m->finalized = true;
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_model_set_comm(higgs_model* m, higgs_comm* comm) {
+  HG_CHECK_ARG(m && comm, "higgs_model_set_comm: null argument");
+  HG_CHECK_ARG(m->cfg.tp_world > 1, "higgs_model_set_comm: the model is not a tensor-parallel shard");
+  m->comm = comm;
   return HIGGS_OK;
 }
 

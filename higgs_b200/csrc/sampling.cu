@@ -183,7 +183,8 @@ constexpr int kArgmaxThreads = 512;
 
 
 __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmaxThreads)
-    argmax_cluster_kernel(const float* logits, int V, int32_t* out) {
+    argmax_cluster_kernel(const float* logits, int V, int offset, int32_t* out,
+                          unsigned long long* key_out) {
   __shared__ unsigned long long warp_best[kArgmaxThreads / 32];
   __shared__ unsigned long long cta_best;
   const int rank = blockIdx.x;  // cluster spans the whole x dimension
@@ -205,15 +206,15 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int j = 4 * (i + u * kArgmaxThreads);
-        best = max(best, argmax_key(q[u].x, j));
-        best = max(best, argmax_key(q[u].y, j + 1));
-        best = max(best, argmax_key(q[u].z, j + 2));
-        best = max(best, argmax_key(q[u].w, j + 3));
+        best = max(best, argmax_key(q[u].x, offset + j));
+        best = max(best, argmax_key(q[u].y, offset + j + 1));
+        best = max(best, argmax_key(q[u].z, offset + j + 2));
+        best = max(best, argmax_key(q[u].w, offset + j + 3));
       }
     }
     for (; i < v1; i += kArgmaxThreads) {
       const float4 q = __ldg(r4 + i);
-      const int j = 4 * i;
+      const int j = offset + 4 * i;
       best = max(best, argmax_key(q.x, j));
       best = max(best, argmax_key(q.y, j + 1));
       best = max(best, argmax_key(q.z, j + 2));
@@ -222,12 +223,12 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
     // the V % 4 tail belongs to the last CTA
     if (rank == kArgmaxCluster - 1)
       for (int j = 4 * nv4 + threadIdx.x; j < V; j += kArgmaxThreads)
-        best = max(best, argmax_key(row[j], j));
+        best = max(best, argmax_key(row[j], offset + j));
   } else {
     const int per1 = (V + kArgmaxCluster - 1) / kArgmaxCluster;
     const int e = min(V, (rank + 1) * per1);
     for (int j = rank * per1 + threadIdx.x; j < e; j += kArgmaxThreads)
-      best = max(best, argmax_key(row[j], j));
+      best = max(best, argmax_key(row[j], offset + j));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
@@ -247,7 +248,10 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
     if (threadIdx.x < kArgmaxCluster) b = *cluster.map_shared_rank(&cta_best, threadIdx.x);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
-    if (threadIdx.x == 0) out[blockIdx.y] = (int32_t)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
+    if (threadIdx.x == 0) {
+      if (key_out) key_out[blockIdx.y] = b;
+      else out[blockIdx.y] = (int32_t)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
+    }
   }
   cluster.sync();  // peers keep their shared memory until CTA 0 has read it
 }
@@ -373,6 +377,12 @@ __global__ void penalties_kernel(float* logits, int V, const int32_t* hist, cons
   pdl_launch();
 }
 
+cudaError_t launch_argmax_keys(const float* logits, int B, int V, int offset, unsigned long long* keys,
+                               cudaStream_t st) {
+  return launch_pdl(argmax_cluster_kernel, dim3(kArgmaxCluster, B), dim3(kArgmaxThreads), 0, st,
+                    logits, V, offset, (int32_t*)nullptr, keys);
+}
+
 }  // namespace higgs
 
 using namespace higgs;
@@ -384,7 +394,7 @@ extern "C" int higgs_argmax(higgs_ctx* ctx, const float* logits, int B, int V, i
   if (B == 0) return HIGGS_OK;
   HG_CHECK_ARG(B <= 65535, "higgs_argmax: B > 65535");
   HG_CUDA(launch_pdl(argmax_cluster_kernel, dim3(kArgmaxCluster, B), dim3(kArgmaxThreads), 0,
-                     (cudaStream_t)stream, logits, V, out));
+                     (cudaStream_t)stream, logits, V, 0, out, (unsigned long long*)nullptr));
   return HIGGS_OK;
 }
 

@@ -55,6 +55,15 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_moe_grouped_w4": (I, [P, P, I, I, I, I, P, P, P, P, P, P, P, I, I, P, P]),
     "higgs_moe_combine": (I, [P, P, P, I, I, I, P, P]),
     "higgs_moe_router": (I, [P, P, I, I, P, P, P, I, P, P]),
+    "higgs_comm_handle_size": (SZ, []),
+    "higgs_comm_create": (I, [P, I, I, SZ, I, ctypes.POINTER(P), P]),
+    "higgs_comm_connect": (I, [P, P]),
+    "higgs_comm_destroy": (I, [P]),
+    "higgs_comm_error": (I, [P, ctypes.POINTER(I)]),
+    "higgs_comm_step": (I, [P, P]),
+    "higgs_allreduce_residual": (I, [P, I, P, I, P, P]),
+    "higgs_allreduce_argmax": (I, [P, I, P, I, P, P]),
+    "higgs_model_set_comm": (I, [P, P]),
     "higgs_model_create": (I, [P, P, ctypes.POINTER(P)]),
     "higgs_model_set_tensor": (I, [P, ctypes.c_char_p, P, I, ctypes.POINTER(I64), I]),
     "higgs_model_finalize": (I, [P]),
@@ -88,7 +97,8 @@ class ModelConfig(ctypes.Structure):
     _fields_ = [("hidden", I), ("layers", I), ("intermediate", I), ("heads", I), ("kv_heads", I),
                 ("head_dim", I), ("vocab", I), ("rms_eps", F), ("rope_theta", F),
                 ("tie_word_embeddings", I), ("qk_norm", I), ("kv_mode", I), ("num_experts", I),
-                ("experts_per_tok", I), ("moe_intermediate", I), ("norm_topk_prob", I)]
+                ("experts_per_tok", I), ("moe_intermediate", I), ("norm_topk_prob", I),
+                ("tp_world", I), ("tp_rank", I), ("head_rows", I)]
 
 
 class ForwardArgs(ctypes.Structure):

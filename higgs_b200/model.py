@@ -190,6 +190,77 @@ def hadamard_signs(seed: int = 4) -> np.ndarray:
     return np.where(rng.random(128) < 0.5, -1, 1).astype(np.int8)
 
 
+# ---- tensor parallelism ----------------------------------------------------------------------
+
+# column-parallel (output rows split) and row-parallel (input columns split) projections
+_COL = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "mlp.gate_proj", "mlp.up_proj")
+_ROW = ("self_attn.o_proj", "mlp.down_proj")
+
+
+def check_tp(args: ModelArgs, world: int):
+    """The shapes a `world`-way split needs: whole heads and kv heads per rank, K slices of the
+    row-parallel projections in whole 256-column units, 16-row vocabulary shards."""
+    D = args.head_dim
+    ok = (args.num_experts == 0 and args.num_attention_heads % world == 0
+          and args.num_key_value_heads % world == 0
+          and (args.num_attention_heads // world * D) % 256 == 0
+          and args.intermediate_size % (256 * world) == 0 and args.vocab_size % (16 * world) == 0)
+    if not ok:
+        raise ValueError(f"{args.model_type} cannot be split {world} ways")
+
+
+def shard_weights(args: ModelArgs, weights: dict, rank: int, world: int) -> dict:
+    """This rank's slices of MLX-layout weights (numpy arrays or torch tensors): rows of the
+    column-parallel projections and of the LM head, K columns (in 64-wide groups) of the
+    row-parallel ones; norms and the embedding whole (a tied head is sliced by the runner)."""
+    check_tp(args, world)
+
+    def cont(a):
+        return a.contiguous() if isinstance(a, torch.Tensor) else np.ascontiguousarray(a)
+    out = {}
+    for name, t in weights.items():
+        base, _, leaf = name.rpartition(".")
+        mod = base.split(".", 3)[-1] if base.startswith("model.layers.") else base
+        if mod in _COL or base == "lm_head":
+            n = t.shape[0] // world
+            out[name] = t[rank * n:(rank + 1) * n]
+        elif mod in _ROW:
+            n = t.shape[1] // world  # words (weight) or groups (scales / biases)
+            out[name] = cont(t[:, rank * n:(rank + 1) * n])
+        else:
+            out[name] = t
+    return out
+
+
+class TPGroup:
+    """This rank's communicator (higgs_comm_*): IPC handles exchanged with `all_gather`, a
+    callable taking this rank's handle bytes and returning every rank's, in rank order
+    (torch.distributed.all_gather_object in the bench and tests)."""
+
+    def __init__(self, rank: int, world: int, words_per_call: int, n_calls: int, all_gather,
+                 device=None):
+        self.rank, self.world = rank, world
+        n = int(ffi.load().higgs_comm_handle_size())
+        hdl = ctypes.create_string_buffer(n)
+        h = ffi.P()
+        ctx = ffi.ctx(torch.device(device).index if device is not None else torch.cuda.current_device())
+        ffi.call("higgs_comm_create", ctx, rank, world, words_per_call, n_calls, ctypes.byref(h), hdl)
+        self.handle = h.value
+        allh = all_gather(bytes(hdl.raw))
+        buf = ctypes.create_string_buffer(b"".join(allh), n * world)
+        ffi.call("higgs_comm_connect", self.handle, buf)
+
+    def error(self) -> int:
+        v = ctypes.c_int(0)
+        ffi.call("higgs_comm_error", self.handle, ctypes.byref(v))
+        return v.value
+
+    def close(self):
+        if getattr(self, "handle", None):
+            ffi.load().higgs_comm_destroy(self.handle)
+            self.handle = None
+
+
 class Graph:
     """A captured forward; relaunch after updating the argument vectors in place."""
 
@@ -217,19 +288,27 @@ class Model:
     """The native runner plus its paged KV pools (AnyModel::forward on the device)."""
 
     def __init__(self, args: ModelArgs, weights: dict[str, torch.Tensor], num_pages: int,
-                 kv_mode: str = "bf16", device="cuda:0", signs: np.ndarray | None = None):
+                 kv_mode: str = "bf16", device="cuda:0", signs: np.ndarray | None = None,
+                 tp: TPGroup | None = None):
+        """With `tp`, `weights` are this rank's shard (shard_weights) and the model is one
+        rank of a tensor-parallel group: greedy tokens are identical on every rank."""
         self.args = args
         self.device = torch.device(device)
         self.weights = weights
         self.kv_mode = kv_mode
         self.num_pages = num_pages
-        cfg = ffi.ModelConfig(args.hidden_size, args.num_hidden_layers, args.intermediate_size,
-                              args.num_attention_heads, args.num_key_value_heads, args.head_dim,
-                              args.vocab_size, args.rms_norm_eps, args.rope_theta,
+        self.tp = tp
+        w = tp.world if tp else 1
+        if tp:
+            check_tp(args, w)
+        cfg = ffi.ModelConfig(args.hidden_size, args.num_hidden_layers, args.intermediate_size // w,
+                              args.num_attention_heads // w, args.num_key_value_heads // w,
+                              args.head_dim, args.vocab_size, args.rms_norm_eps, args.rope_theta,
                               int(args.tie_word_embeddings), int(args.qk_norm),
                               ffi.KV_TQ4 if kv_mode == "tq4" else ffi.KV_BF16, args.num_experts,
                               args.num_experts_per_tok, args.moe_intermediate_size,
-                              int(args.norm_topk_prob))
+                              int(args.norm_topk_prob), w, tp.rank if tp else 0,
+                              args.vocab_size // w)
         h = ffi.P()
         ctx = ffi.ctx(self.device.index or 0)
         ffi.call("higgs_model_create", ctx, ctypes.byref(cfg), ctypes.byref(h))
@@ -241,7 +320,9 @@ class Model:
             ffi.call("higgs_model_set_tensor", self.handle, name.encode(), t.data_ptr(), dt, shape,
                      t.dim())
         ffi.call("higgs_model_finalize", self.handle)
-        L, Hkv, D = args.num_hidden_layers, args.num_key_value_heads, args.head_dim
+        if tp:
+            ffi.call("higgs_model_set_comm", self.handle, tp.handle)
+        L, Hkv, D = args.num_hidden_layers, args.num_key_value_heads // w, args.head_dim
         if kv_mode == "tq4":
             self.signs = torch.from_numpy(hadamard_signs() if signs is None else signs).to(self.device)
             self.k_pool = torch.zeros(L, num_pages, Hkv, PAGE, 64, dtype=torch.uint8, device=self.device)
@@ -291,7 +372,8 @@ class Model:
         [B, max_blocks], seq_lens int32 [B] (all CUDA).  Returns (logits f32, argmax int32)."""
         B, Lq = tokens.shape
         rows = B if last_only else B * Lq
-        logits = (torch.empty(rows, self.args.vocab_size, dtype=torch.float32, device=self.device)
+        vocab_out = self.args.vocab_size // (self.tp.world if self.tp else 1)  # this rank's shard
+        logits = (torch.empty(rows, vocab_out, dtype=torch.float32, device=self.device)
                   if want_logits else None)
         am = torch.empty(rows, dtype=torch.int32, device=self.device)
         fa = self.forward_args(tokens, positions, slot_mapping, block_table, seq_lens, max_seq_len,

@@ -57,6 +57,7 @@ typedef struct higgs_model higgs_model;
 typedef struct higgs_graph higgs_graph;
 typedef struct higgs_block_pool higgs_block_pool;
 typedef struct higgs_prefix_cache higgs_prefix_cache;
+typedef struct higgs_comm higgs_comm;
 
 /* ---- context and errors ------------------------------------------------ */
 
@@ -365,6 +366,32 @@ int higgs_moe_grouped_w4(higgs_ctx* ctx, const void* x, int T, int K, int k, int
 int higgs_moe_combine(higgs_ctx* ctx, const void* y, const float* scores, int T, int k, int H,
                       void* h, void* stream);
 
+/* ---- (e): tensor-parallel collectives over NVLink peer memory ------------ */
+
+/* A communicator of `world` ranks (one process per GPU).  Each rank allocates
+ * a buffer of n_calls call regions (one per collective call site of a decode
+ * step, 2 x layers + 1 for the decode runner) of words_per_call u32 words per
+ * rank, and gets its CUDA IPC handle (higgs_comm_handle_size() bytes) in
+ * ipc_handle_out; the host exchanges the handles (any side channel) and passes
+ * all `world` of them, in rank order, to higgs_comm_connect.  Collectives are
+ * one-shot pushes into every rank's buffer with per-CTA flags; every rank must
+ * issue the same calls in the same order, and higgs_comm_step once per step
+ * before them.  A wait that sees no progress for about a second gives up and
+ * sets the flag that higgs_comm_error returns (and clears). */
+size_t higgs_comm_handle_size(void);
+int higgs_comm_create(higgs_ctx* ctx, int rank, int world, size_t words_per_call, int n_calls,
+                      higgs_comm** out, void* ipc_handle_out);
+int higgs_comm_connect(higgs_comm* comm, const void* handles);
+int higgs_comm_destroy(higgs_comm* comm);
+int higgs_comm_error(higgs_comm* comm, int* out);
+int higgs_comm_step(higgs_comm* comm, void* stream);
+/* h bf16 [n] += bf16(sum over ranks of partial f32 [n]), summed in rank order. */
+int higgs_allreduce_residual(higgs_comm* comm, int call, const float* partial, int n, void* h,
+                             void* stream);
+/* out int32 [n] = index of the max over ranks of keys u64 [n] (argmax keys). */
+int higgs_allreduce_argmax(higgs_comm* comm, int call, const uint64_t* keys, int n, int32_t* out,
+                           void* stream);
+
 /* ---- a7/a11: native decode step (transformer.rs Model) ------------------ */
 
 /* ModelArgs (crates/higgs-models/src/transformer.rs:69-97) reduced to what the
@@ -379,6 +406,15 @@ typedef struct {
   int qk_norm;
   int kv_mode; /* HIGGS_KV_BF16 or HIGGS_KV_TQ4 */
   int num_experts, experts_per_tok, moe_intermediate, norm_topk_prob;
+  /* Tensor parallelism (no reference counterpart): with tp_world > 1 the model
+   * is this rank's shard -- heads, kv_heads and intermediate are the per-rank
+   * counts (column-parallel q|k|v and gate|up, row-parallel o_proj / down_proj
+   * over K), the LM head holds rows [tp_rank*head_rows, (tp_rank+1)*head_rows)
+   * of the vocabulary (the embedding stays whole), and a communicator from
+   * higgs_comm_create / higgs_model_set_comm sums the row-parallel partials
+   * and reduces the greedy argmax over the shards.  head_rows = vocab when
+   * tp_world <= 1. */
+  int tp_world, tp_rank, head_rows;
 } higgs_model_config;
 
 /* One forward over B sequences x Lq new tokens (Lq = 1 decode, k+1 verify,
@@ -416,6 +452,9 @@ int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg, higgs_mode
 int higgs_model_set_tensor(higgs_model* m, const char* name, const void* ptr, int dtype,
                            const int64_t* shape, int ndim);
 int higgs_model_finalize(higgs_model* m);
+/* Attach the communicator of a tensor-parallel shard (cfg.tp_world > 1); it
+ * must hold at least 2 x layers + 1 call regions of B*Lq*hidden words. */
+int higgs_model_set_comm(higgs_model* m, higgs_comm* comm);
 int higgs_model_destroy(higgs_model* m);
 
 /* Paged KV pools for all layers: bf16 [layers, pages, Hkv, 16, D] each; or
@@ -466,6 +505,9 @@ int higgs_block_pool_refcount(const higgs_block_pool* pool, int32_t page);
  * whole 16-token pages of a stored prefix are kept (never the partly filled
  * last page), matches need >= 16 tokens (prompt_cache.rs:8), the deepest
  * match wins, and entries beyond max_entries are evicted least recently used.
+ * Unlike the reference, which reuses a stored prompt only when all of it
+ * prefixes the query, any shared prefix is reused in whole pages (pages are
+ * immutable, so a stored prompt's leading pages serve every prefix of it). 
  * lookup copies the matched pages to pages_out, sets *matched_tokens (0 = no
  * hit) and retains those pages for the caller, who releases them with the
  * sequence.  store retains the pages it keeps. */

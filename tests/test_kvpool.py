@@ -173,3 +173,30 @@ def test_edge_split_preserves_existing_entry():
     assert len(pc) == 2
     m, got = pc.lookup(np.concatenate([toks(0, 50), [999]]))
     assert m == 48 and got.tolist() == long_pages[:3].tolist()
+
+
+def test_partial_prefix_served_from_descendant_pages():
+    """Beyond the reference (which matches only whole stored prompts): a query sharing the
+    first 256 tokens of a stored 512-token prompt reuses its first 16 pages."""
+    pool = BlockPool(128)
+    pc = PrefixCache(pool, 10)
+    rng = np.random.default_rng(2)
+    shared = rng.integers(0, 1000, 256).astype(np.int32)
+    p1 = np.concatenate([shared, rng.integers(1000, 2000, 256).astype(np.int32)])
+    p2 = np.concatenate([shared, rng.integers(2000, 3000, 256).astype(np.int32)])
+    pages = store(pc, pool, p1)
+    m, got = pc.lookup(p2[:-1])
+    assert m == 256 and got.tolist() == pages[:16].tolist()
+    assert pool.refcount(int(pages[0])) == 2 and pool.refcount(int(pages[20])) == 1
+    pool.release(got)
+    # a match ending mid-page is floored to whole pages; under 16 tokens nothing
+    q = np.concatenate([p1[:40], [5000]])
+    assert pc.lookup(q)[0] == 32
+    pool.release(pc.lookup(q)[1])
+    assert pc.lookup(np.concatenate([p1[:10], [5000]]))[0] == 0
+    # after storing p2 the split node serves p3 as well
+    store(pc, pool, p2)
+    p3 = np.concatenate([shared, [7, 8, 9]])
+    m3, g3 = pc.lookup(p3)
+    assert m3 == 256
+    pool.release(g3)
