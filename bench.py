@@ -53,7 +53,8 @@ def parse():
     ap.add_argument("--configs", default="c1,c2,c3,c4,c5",
                     help="other BASELINE configs to run at N=1 (comma list, '' for none)")
     ap.add_argument("--kernel-case", default=None,
-                    help="run one small kernel case for ncu: qkv|o_proj|gate_up_swiglu|down|lm_head|attention|argmax")
+                    help="run one small kernel case for ncu: qkv|o_proj|gate_up_swiglu|down|lm_head[:tokens]"
+                         "|attention|argmax")
     return ap.parse_args()
 
 
@@ -156,6 +157,21 @@ def peaks():
 # ---------------------------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------------------------
+def make_tp_group(args_m, rank, world, max_tokens, device):
+    """This rank's peer-memory communicator; IPC handles exchanged over a gloo group."""
+    import torch.distributed as dist
+
+    from higgs_b200.model import TPGroup
+    gloo = dist.new_group(backend="gloo")
+
+    def gather(b):
+        out = [None] * world
+        dist.all_gather_object(out, b, group=gloo)
+        return out
+    return TPGroup(rank, world, words_per_call=max_tokens * args_m.hidden_size,
+                   n_calls=2 * args_m.num_hidden_layers + 1, all_gather=gather, device=device)
+
+
 def setup_model(args_m, batches, ctx, total_steps, device, world=1, rank=0):
     """The model on one GPU, or (world > 1) this rank's tensor-parallel shard with its
     peer-memory communicator."""
@@ -169,16 +185,8 @@ def setup_model(args_m, batches, ctx, total_steps, device, world=1, rank=0):
     num_pages = max(max(batches), 4) * per_seq_pages + 16  # >= the 4 sequences of C3
     tp = None
     if world > 1:
-        import torch.distributed as dist
-        gloo = dist.new_group(backend="gloo")
-
-        def gather(b):
-            out = [None] * world
-            dist.all_gather_object(out, b, group=gloo)
-            return out
         weights = shard_weights(args_m, weights, rank, world)
-        tp = TPGroup(rank, world, words_per_call=max(batches) * args_m.hidden_size,
-                     n_calls=2 * args_m.num_hidden_layers + 1, all_gather=gather, device=device)
+        tp = make_tp_group(args_m, rank, world, max(batches), device)
     model = Model(args_m, weights, num_pages=num_pages, device=device, tp=tp)
     # synthetic KV context (random bf16; decode cost does not depend on the values)
     g = torch.Generator(device=device)
@@ -345,14 +353,15 @@ def kernel_case(opt):
         return (torch.randint(-2**31, 2**31 - 1, (N, K // 8), dtype=torch.int32, device=dev),
                 (torch.rand(N, K // 64, device=dev) * 0.01).to(torch.bfloat16),
                 (torch.randn(N, K // 64, device=dev) * 0.01).to(torch.bfloat16))
-    case = opt.kernel_case
+    case, _, mrows = opt.kernel_case.partition(":")  # "<shape>[:<tokens>]", default 1 token
+    M = int(mrows) if mrows else 1
     if case in ("qkv", "o_proj", "down", "lm_head", "gate_up_swiglu"):
         K, N = {"qkv": (H, (a.num_attention_heads + 2 * a.num_key_value_heads) * a.head_dim),
                 "o_proj": (a.num_attention_heads * a.head_dim, H), "down": (a.intermediate_size, H),
                 "lm_head": (H, a.vocab_size), "gate_up_swiglu": (H, a.intermediate_size)}[case]
         reps = 2 if case == "lm_head" else 8  # > 126 MB of distinct weights in flight
         ws = [mk(N, K) + (mk(N, K) if case == "gate_up_swiglu" else ()) for _ in range(reps)]
-        x = torch.randn(1, K, device=dev).to(torch.bfloat16)
+        x = torch.randn(M, K, device=dev).to(torch.bfloat16)
         for it in range(3):
             for w in ws:
                 if case == "gate_up_swiglu":
@@ -553,24 +562,37 @@ def config_c3(model, eng, Sequence, device, hbm, steps, ctx):
             "tokens_per_step_mean": round(float(acc.mean()) + 1.0, 3)}
 
 
-def config_c4(device, hbm, steps):
-    """C4: Qwen3-30B-A3B arch (128 experts, top-8), B=32 decode at ctx 4096, one GPU."""
+def config_c4(device, hbm, steps, world=1, rank=0):
+    """C4: Qwen3-30B-A3B arch (128 experts, top-8), B=32 decode at ctx 4096; on N GPUs
+    attention is tensor parallel and the experts are split over the ranks (expert
+    parallelism), both reduced by the peer-memory all-reduce."""
     import torch
 
     from higgs_b200.engine import Engine, Sequence
-    from higgs_b200.model import PRESETS
+    from higgs_b200.model import PRESETS, Model, shard_weights, synth_weights_device
     a = PRESETS["qwen3-30b-a3b"]
     B, ctx = 32, 4096
     pages = B * math.ceil((ctx + steps + 16) / 16) + 16
-    model, w = _synth_model(a, device, num_pages=pages)
+    w = synth_weights_device(a, seed=0, device=device)
+    tp = None
+    if world > 1:
+        w = shard_weights(a, w, rank, world)
+        tp = make_tp_group(a, rank, world, B, device)
+    model = Model(a, w, num_pages=pages, device=device, tp=tp)
     _fill_kv(model)
     eng = Engine(model, max_seq_len=ctx + steps + 16, prefix_entries=0)
     seqs = make_seqs(eng, Sequence, B, ctx, a.vocab_size, seed=31)
     ms, _ = time_device_resident(eng, seqs, steps, 4)
+    ms = allmax(ms)
     touched = 128 * (1 - (1 - 8 / 128) ** B)  # expected distinct experts per layer
     out = _entry(a, B, ctx + steps // 2, ms / steps, hbm, experts_touched=touched,
                  extra={"workload": "qwen3-30b-a3b B=32 ctx 4096 greedy (router logits N(0,1))",
-                        "experts_touched_per_layer": round(touched, 1)})
+                        "experts_touched_per_layer": round(touched, 1),
+                        "parallelism": f"tp{world} attention + ep{world} experts" if world > 1 else "single GPU"})
+    if world > 1:
+        out["step_hbm_frac"] = round(out["step_hbm_frac"] / world, 4)  # per-GPU bytes
+    for s_ in seqs:
+        eng.release(s_)
     del eng, model, w
     torch.cuda.empty_cache()
     return out
@@ -704,6 +726,10 @@ def run_ours(opt):
             torch.cuda.empty_cache()
             cfgs["C4"] = config_c4(device, hbm, n)
         out["by_config"] = cfgs
+    elif ws > 1 and not opt.quick and "c4" in opt.configs.split(","):
+        c4 = config_c4(device, hbm, 16, ws, rank)  # every rank takes part
+        if rank == 0:
+            out["by_config"] = {"C4": c4}
     if rank == 0 and ws == 1 and not opt.no_cpu_baseline and not opt.quick:
         sec, desc = oracle_step_time(a, opt.ctx)
         out["cpu_baseline"] = {"value": round(1.0 / sec, 4), "unit": "tok/s", "cores": os.cpu_count(),

@@ -990,11 +990,14 @@ static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len, int
   const int max_pages = (max_seq_len + 15) / 16 > 0 ? (max_seq_len + 15) / 16 : 1;
   int want = (kTargetCtas + B * Hkv - 1) / (B * Hkv);
   if (want < 1) want = 1;
-  // the final merge stages splits x rows weights in 3 * RP * D floats of shared memory
   if (want > 128) want = 128;
-  // at least 4 pages (one per warp) per split
+  // at least min_pps pages (one per warp) per split (measured: capping the pages per
+  // split to raise the CTA count for long contexts was slower on B200)
   int pps = (max_pages + want - 1) / want;
   if (pps < min_pps) pps = min_pps;
+  // the final merge stages splits x rows weights in 3 * RP * D (>= 3 * 16 * 64) floats
+  // of shared memory: keep splits * rows_pad <= 3072
+  while ((max_pages + pps - 1) / pps * p.rows_pad > 3072) pps *= 2;
   p.pps = pps;
   p.splits = (max_pages + pps - 1) / pps;
   return p;

@@ -27,6 +27,10 @@ int cuda_fail(cudaError_t e, const char* what) {
 void qgemv_set_f16(bool on);
 void attention_set_min_pages(int n);
 void set_l2_prefetch(int mode);
+void set_gemm_tc(bool on);
+void set_gemm_tc_rows(int m);
+void qgemv_set_wk(int wk);
+void qgemm_tc_prepare();
 
 }  // namespace higgs
 
@@ -37,6 +41,18 @@ extern "C" int higgs_set_option(const char* name, int value) {
   const std::string n(name);
   if (n == "gemv_f16") {
     qgemv_set_f16(value != 0);
+    return HIGGS_OK;
+  }
+  if (n == "gemv_wk") {
+    qgemv_set_wk(value);
+    return HIGGS_OK;
+  }
+  if (n == "gemm_tc_rows") {
+    set_gemm_tc_rows(value);
+    return HIGGS_OK;
+  }
+  if (n == "gemm_tc") {
+    set_gemm_tc(value != 0);
     return HIGGS_OK;
   }
   if (n == "l2_prefetch") {
@@ -68,6 +84,7 @@ extern "C" int higgs_init(int device, higgs_ctx** out) {
   if (major != 10 || minor != 0)
     return fail(HIGGS_ERR_UNSUPPORTED, "higgs_init: device is sm_" + std::to_string(major) +
                                            std::to_string(minor) + ", this build targets sm_100a");
+  qgemm_tc_prepare();
   higgs_ctx* c = new higgs_ctx;
   c->device = device;
   c->sms = sms;

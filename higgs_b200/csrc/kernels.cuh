@@ -55,6 +55,11 @@ struct QLinArgs {
   int moe_max_items;
   int moe_xdiv;
   long long moe_ew, moe_es;
+  // expert parallelism: only experts [moe_e_lo, moe_e_lo + moe_e_n) live here (0 = all)
+  int moe_e_lo, moe_e_n;
+  // scratch for the tensor-core path's split-K partials (M >= 16; may be null)
+  void* tc_ws;
+  size_t tc_ws_bytes;
   // weights of a later launch to pull into L2 (the next GEMV of the step)
   L2Prefetch pf;
   // also prefetch this CTA's own weight tiles to L2 at its start
@@ -73,7 +78,13 @@ cudaError_t launch_moe_route(const void* logits, bool bf16_in, int T, int E, int
 cudaError_t launch_moe_grouped(const uint16_t* x, int T, int K, int k, bool x_per_pair,
                                const void* plan, int E, int N, const uint32_t* w, const uint16_t* s,
                                const uint16_t* b, const uint32_t* w2, const uint16_t* s2,
-                               const uint16_t* b2, uint16_t* y, cudaStream_t st);
+                               const uint16_t* b2, uint16_t* y, cudaStream_t st, int e_lo = 0,
+                               int e_n = 0);
+// expert parallelism: this rank's share of the weighted sum, f32 [T, H], pairs whose expert
+// lies outside [e_lo, e_lo + e_n) contribute nothing
+cudaError_t launch_moe_combine_partial(const uint16_t* y, const float* scores, const int32_t* idx,
+                                       int T, int k, int H, int e_lo, int e_n, float* part,
+                                       cudaStream_t st);
 cudaError_t launch_moe_router(const uint16_t* x, int T, int K, const uint32_t* w,
                               const uint16_t* s, const uint16_t* b, int E, uint16_t* out,
                               cudaStream_t st);
@@ -87,6 +98,11 @@ cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st);
 bool l2_prefetch_next();
 bool l2_prefetch_self();
 bool qgemv_ring_can_fuse_norm(int M, int K);
+// M >= 16: the tcgen05 matrix path (qgemm_tc.cu); launch_qgemv_ring routes there itself.
+bool qgemm_tc_supported(const QLinArgs& a);
+size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu);
+cudaError_t launch_qgemm_tc(const QLinArgs& a, int epi, void* ws, size_t ws_bytes, cudaStream_t st);
+void qgemm_tc_prepare();
 // Grouped-expert variant (the a.moe_* fields set): K * 8 tokens must fit the staged-x tile.
 cudaError_t launch_qgemv_grouped(const QLinArgs& a, int epi, cudaStream_t st);
 bool qgemv_grouped_supported(int K);

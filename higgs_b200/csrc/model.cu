@@ -87,7 +87,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
   size_t h, x, qkv, q, attn, act, xl, logits, moe_rl, moe_idx, moe_sc, moe_plan, moe_act, moe_y,
-      tp_part, tp_keys, attn_ws, total;
+      tp_part, tp_keys, tc_ws, tc_ws_bytes, attn_ws, total;
 };
 
 int head_rows(const higgs_model_config& c) { return c.tp_world > 1 ? c.head_rows : c.vocab; }
@@ -116,6 +116,16 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
   if (c.tp_world > 1) {
     L.tp_part = take(T * c.hidden * 4);
     L.tp_keys = take(rows_lm * 8);
+  }
+  {  // split-K partials of the tensor-core path (a few MB; used from 16 rows by default)
+    const int H = c.hidden, Hd = c.heads * D, Nqkv = (c.heads + 2 * c.kv_heads) * D;
+    size_t need = qgemm_tc_workspace((int)T, H, Nqkv, false);
+    need = std::max(need, qgemm_tc_workspace((int)T, Hd, H, false));
+    need = std::max(need, qgemm_tc_workspace((int)T, H, c.intermediate, true));
+    need = std::max(need, qgemm_tc_workspace((int)T, c.intermediate, H, false));
+    need = std::max(need, qgemm_tc_workspace((int)rows_lm, H, head_rows(c), false));
+    L.tc_ws_bytes = need;
+    L.tc_ws = take(need);
   }
   if (c.num_experts > 0) {
     const size_t P = T * c.experts_per_tok;
@@ -224,6 +234,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
 
   // decode batches fuse each RMSNorm into the GEMV that consumes it
   const bool fuse = qgemv_ring_can_fuse_norm(T, H);
+  void* tc_ws = L.tc_ws_bytes ? (void*)(ws + L.tc_ws) : nullptr;
   // L2 prefetch lists: each GEMV asks for the weights of a later GEMV of the step
   const bool pfon = l2_prefetch_next(), pfself = l2_prefetch_self();
   auto add_q = [&](L2Prefetch& pf, const QW& w, size_t max_bytes = ~(size_t)0) {
@@ -243,6 +254,8 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
                  const uint16_t* res, const L2Prefetch* pf = nullptr) {
     QLinArgs a{};
     a.self_prefetch = pfself;
+    a.tc_ws = tc_ws;
+    a.tc_ws_bytes = L.tc_ws_bytes;
     if (pf) a.pf = *pf;
     a.x = xin;
     a.norm_w = norm;
@@ -316,6 +329,8 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.bseg[2] = Lw.v.b;
       a.y = qkv;
       a.self_prefetch = pfself;
+      a.tc_ws = tc_ws;
+      a.tc_ws_bytes = L.tc_ws_bytes;
       add_q(a.pf, Lw.o);
       if (Lw.moe) {
         add_q(a.pf, Lw.router);
@@ -394,11 +409,18 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
         HG_CUDA(launch_moe_router(x, T, H, Lw.router.w, Lw.router.s, Lw.router.b, E, rl, st));
       }
       HG_CUDA(launch_moe_route(rl, true, T, E, kk, c.norm_topk_prob, idx, sc, plan, st));
+      // expert parallelism: this rank holds experts [e_lo, e_lo + e_n)
+      const int e_n = tp ? E / c.tp_world : 0, e_lo = tp ? c.tp_rank * e_n : 0;
       HG_CUDA(launch_moe_grouped(x, T, H, kk, false, plan, E, F, Lw.egate.w, Lw.egate.s, Lw.egate.b,
-                                 Lw.eup.w, Lw.eup.s, Lw.eup.b, pact, st));
+                                 Lw.eup.w, Lw.eup.s, Lw.eup.b, pact, st, e_lo, e_n));
       HG_CUDA(launch_moe_grouped(pact, T, F, kk, true, plan, E, H, Lw.edown.w, Lw.edown.s,
-                                 Lw.edown.b, nullptr, nullptr, nullptr, py, st));
-      HG_CUDA(launch_moe_combine(py, sc, T, kk, H, h, st));
+                                 Lw.edown.b, nullptr, nullptr, nullptr, py, st, e_lo, e_n));
+      if (tp) {
+        HG_CUDA(launch_moe_combine_partial(py, sc, idx, T, kk, H, e_lo, e_n, part, st));
+        HG_CUDA(comm_allreduce_residual(m->comm, 2 * li + 1, part, T * H, h, st));
+      } else {
+        HG_CUDA(launch_moe_combine(py, sc, T, kk, H, h, st));
+      }
       continue;
     }
     {
@@ -422,6 +444,8 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.nseg = 1;
       a.y = act;
       a.self_prefetch = pfself;
+      a.tc_ws = tc_ws;
+      a.tc_ws_bytes = L.tc_ws_bytes;
       if (li + 1 < n_layers) {
         const LayerW& Ln = m->layers[li + 1];
         add_q(a.pf, Ln.q);
@@ -463,6 +487,8 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
     a.nseg = 1;
     a.y_f32 = logits;
     a.self_prefetch = pfself;
+    a.tc_ws = tc_ws;
+    a.tc_ws_bytes = L.tc_ws_bytes;
     HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
   }
   if (f->argmax) {
@@ -514,7 +540,8 @@ extern "C" int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg,
                  "higgs_model_create: bad tp_rank / tp_world (tp_world <= 8)");
     HG_CHECK_ARG(c.head_rows > 0 && c.head_rows % 16 == 0 && (int64_t)c.head_rows * c.tp_world == c.vocab,
                  "higgs_model_create: head_rows * tp_world must equal vocab (head_rows % 16 == 0)");
-    HG_CHECK_ARG(c.num_experts == 0, "higgs_model_create: tensor parallelism covers dense models");
+    HG_CHECK_ARG(c.num_experts % c.tp_world == 0,
+                 "higgs_model_create: expert parallelism needs num_experts % tp_world == 0");
   }
   if (c.num_experts > 0) {
     HG_CHECK_ARG(c.num_experts <= 1024 && c.num_experts % 16 == 0,
@@ -595,11 +622,12 @@ extern "C" int higgs_model_finalize(higgs_model* m) {
     L.moe = c.num_experts > 0 && m->tensors.count(p + "mlp.gate.weight");
     if (L.moe) {
       const int E = c.num_experts, F = c.moe_intermediate;
+      const int El = c.tp_world > 1 ? E / c.tp_world : E;  // experts held by this rank
       const std::string sw = p + "mlp.switch_mlp.";
       if ((rc = get_q(m, p + "mlp.gate", E, H, L.router))) return rc;
-      if ((rc = get_q3(m, sw + "gate_proj", E, F, H, L.egate))) return rc;
-      if ((rc = get_q3(m, sw + "up_proj", E, F, H, L.eup))) return rc;
-      if ((rc = get_q3(m, sw + "down_proj", E, H, F, L.edown))) return rc;
+      if ((rc = get_q3(m, sw + "gate_proj", El, F, H, L.egate))) return rc;
+      if ((rc = get_q3(m, sw + "up_proj", El, F, H, L.eup))) return rc;
+      if ((rc = get_q3(m, sw + "down_proj", El, H, F, L.edown))) return rc;
       continue;
     }
     if ((rc = get_q(m, p + "mlp.gate_proj", c.intermediate, H, L.gate))) return rc;

@@ -238,6 +238,38 @@ __global__ void __launch_bounds__(128) moe_combine_kernel(const uint16_t* y, con
   pdl_launch();
 }
 
+// Expert parallelism: part[t] = sum over this rank's pairs j of bf16(s_j) * y[t*k+j], f32 in
+// j order (the all-reduce then adds the ranks' shares and the residual, rounding once).
+__global__ void __launch_bounds__(128) moe_combine_partial_kernel(const uint16_t* y, const float* scores,
+                                                                  const int32_t* idx, int T, int k,
+                                                                  int H, int e_lo, int e_n,
+                                                                  float* part) {
+  pdl_wait();
+  const int t = blockIdx.y;
+  const int c8 = blockIdx.x * 128 + threadIdx.x;
+  if (c8 * 8 < H) {
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int e = idx[(size_t)t * k + j];
+      if (e < e_lo || e >= e_lo + e_n) continue;
+      const float sc = round_bf(scores[(size_t)t * k + j]);
+      const uint4 v = ldg_u4(y + ((size_t)t * k + j) * H + c8 * 8);
+      const uint32_t* vp = &v.x;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = __fadd_rn(acc[2 * i], __fmul_rn(sc, bf_lo(vp[i])));
+        acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __fmul_rn(sc, bf_hi(vp[i])));
+      }
+    }
+    float4* pp = reinterpret_cast<float4*>(part + (size_t)t * H + c8 * 8);
+    pp[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    pp[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+  }
+  pdl_launch();
+}
+
 template <bool BF16IN>
 cudaError_t launch_route_nv(const void* logits, int T, int E, int k, int norm, int32_t* idx,
                             float* scores, int* plan, cudaStream_t st) {
@@ -267,7 +299,7 @@ cudaError_t launch_moe_route(const void* logits, bool bf16_in, int T, int E, int
 cudaError_t launch_moe_grouped(const uint16_t* x, int T, int K, int k, bool x_per_pair,
                                const void* plan, int E, int N, const uint32_t* w, const uint16_t* s,
                                const uint16_t* b, const uint32_t* w2, const uint16_t* s2,
-                               const uint16_t* b2, uint16_t* y, cudaStream_t st) {
+                               const uint16_t* b2, uint16_t* y, cudaStream_t st, int e_lo, int e_n) {
   QLinArgs a{};
   a.x = x;
   a.M = 8;
@@ -289,6 +321,8 @@ cudaError_t launch_moe_grouped(const uint16_t* x, int T, int K, int k, bool x_pe
   a.moe_xdiv = x_per_pair ? 1 : k;
   a.moe_ew = (long long)N * (K / 8);
   a.moe_es = (long long)N * (K / 64);
+  a.moe_e_lo = e_lo;
+  a.moe_e_n = e_n;
   a.self_prefetch = l2_prefetch_self();
   return launch_qgemv_grouped(a, w2 ? EPI_SWIGLU : EPI_STORE, st);
 }
@@ -300,6 +334,14 @@ cudaError_t launch_moe_router(const uint16_t* x, int T, int K, const uint32_t* w
   const int R = 256 / G;
   return launch_pdl(moe_router_kernel, dim3((E + R - 1) / R, T), dim3(256), 0, st, x, K, w, s, b, E,
                     R, out);
+}
+
+cudaError_t launch_moe_combine_partial(const uint16_t* y, const float* scores, const int32_t* idx,
+                                       int T, int k, int H, int e_lo, int e_n, float* part,
+                                       cudaStream_t st) {
+  const dim3 grid((H / 8 + 127) / 128, T);
+  return launch_pdl(moe_combine_partial_kernel, grid, dim3(128), 0, st, y, scores, idx, T, k, H, e_lo, e_n,
+                    part);
 }
 
 cudaError_t launch_moe_combine(const uint16_t* y, const float* scores, int T, int k, int H,

@@ -1,0 +1,558 @@
+// qgemm_tc.cu -- W4 g64 quantized matmul for M >= 16 tokens on the tcgen05
+// tensor cores (batched decode, speculative verify, prefill).
+//
+// Reference op replaced: ops::quantized_matmul (qwen3_next.rs:174-183) in its
+// matrix form.  MLX evaluates many-token quantized matmuls by dequantizing the
+// weights to the activation type first (qmm); so does this kernel:
+// w = bf16(s*q + b) with one rounding (a bf16x2 fused multiply-add of the exact
+// nibble value), then bf16 x bf16 -> f32 on the tensor cores.
+//
+// One CTA computes a 128-row x BN-token tile over a slice of K (split-K when the
+// tile count alone cannot fill the GPU):
+//   * 8 producer warps: thread (row, half) streams 16 bytes of packed weights per
+//     64-wide k group (a register ring 8 groups deep), dequantizes them with
+//     LOP3 / bf16x2 FMA / PRMT and stores the bf16 row slice into shared memory
+//     in the 128-byte-swizzled K-major layout the MMA reads;
+//   * 1 MMA warp: TMA brings the x tile (BN tokens x 64 k, same swizzle), one
+//     elected lane issues tcgen05.mma (M=128, N=BN, K=16) x 4 per group into a
+//     TMEM accumulator and tcgen05.commit releases the stage;
+//   * the producers then read TMEM (tcgen05.ld, 32 lanes per warp quarter) and
+//     run the epilogue: bf16 / f32 store, residual add, SwiGLU (gate and up tiles
+//     share the CTA), or a split-K partial reduced in split order by the last CTA.
+// TMEM is allocated only after griddepcontrol.wait, so a kernel launched early
+// never holds tensor memory that its predecessor still needs.  Every mbarrier
+// wait is bounded (about 2 s): on timeout the kernel records an error that
+// higgs_tc_error reports, and finishes.
+#include <cuda.h>
+
+#include <map>
+#include <mutex>
+#include <tuple>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace higgs {
+
+namespace {
+
+constexpr int kTcRows = 128;       // weight rows per tile (UMMA M)
+constexpr int kTcStages = 4;       // shared-memory stages (k groups)
+constexpr int kTcProducers = 256;  // 8 warps, thread = (row, half of 64 k)
+constexpr int kTcThreads = kTcProducers + 32;
+constexpr int kTileA = kTcRows * 128;  // 128 rows x 64 bf16 = 16 KB
+constexpr int kRing = 8;               // k groups in flight per producer thread
+
+struct TcArgs {
+  int M, K, N;
+  int nseg;
+  int seg_end[3];
+  const uint32_t* w[3];
+  const uint16_t* s[3];
+  const uint16_t* b[3];
+  const uint32_t* w2;  // up projection (SwiGLU)
+  const uint16_t* s2;
+  const uint16_t* b2;
+  uint16_t* y;
+  float* y_f32;
+  const uint16_t* residual;
+  int splits, groups_per_split;
+  float* part;    // split-K partials
+  int* counters;  // one per (n tile, m tile), self-resetting
+  int* err;
+};
+
+// ---- mbarrier / TMA / tcgen05 primitives -----------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned bytes) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                   smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Bounded wait for the completion of phase `parity`; false (and *err set) on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* err) {
+  const uint32_t a = smem_u32(bar);
+  const long long t0 = clock64();
+  while (true) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (ok) return true;
+    if (clock64() - t0 > (1ll << 32)) break;  // ~2 s at 2 GHz
+  }
+  if (err) atomicExch(err, 1);
+  return false;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_alloc(uint32_t* dst, int cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tc_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc_dealloc(uint32_t taddr, int cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+// 16 consecutive f32 columns of this thread's TMEM lane
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void producers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTcProducers) : "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused by swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset
+  d |= (uint64_t)1 << 46;            // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// 8 weights of one packed word -> 16 bytes of bf16 in k order: w = bf16(s*q + b)
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+  const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
+  uint32_t p[4] = {lop3_and_or(w, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u),
+                   lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u)};
+  uint32_t q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // (128 + q) - 128 = q exactly; then one rounding of s*q + b
+    const __nv_bfloat162 qq = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&p[i]), c128);
+    const __nv_bfloat162 r = __hfma2(s2, qq, b2);
+    q[i] = *reinterpret_cast<const uint32_t*>(&r);
+  }
+  // q[i] = (w_i, w_{i+4}) -> k order (0,1) (2,3) (4,5) (6,7)
+  return make_uint4(prmt(q[0], q[1], 0x5410), prmt(q[2], q[3], 0x5410), prmt(q[0], q[1], 0x7632),
+                    prmt(q[2], q[3], 0x7632));
+}
+
+template <int BN, bool SWIGLU>
+__global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+  constexpr int NA = SWIGLU ? 2 : 1;
+  constexpr int kTileB = BN * 128;
+  constexpr int kStage = NA * kTileA + kTileB;
+  constexpr int TCOLS = (NA * BN <= 32) ? 32 : (NA * BN <= 64) ? 64 : (NA * BN <= 128) ? 128 : 256;
+  constexpr int HC = BN / 2;  // accumulator columns read per producer warp
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[kTcStages];
+  __shared__ __align__(8) uint64_t empty_bar[kTcStages];
+  __shared__ __align__(8) uint64_t done_bar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int is_last;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
+  const int n0 = n_tile * kTcRows, m0 = m_tile * BN;
+  const int G = a.K / 64;
+  const int g0 = split * a.groups_per_split;
+  const int g1 = min(G, g0 + a.groups_per_split);
+  const int nst = g1 - g0;
+
+  int seg = 0;
+  for (int i = 1; i < a.nseg; ++i)
+    if (n0 >= a.seg_end[i - 1]) seg = i;
+  const int row0 = n0 - (seg ? a.seg_end[seg - 1] : 0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(&full_bar[i], kTcProducers + 1);
+      mbar_init(&empty_bar[i], 1);
+    }
+    mbar_init(&done_bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  // weights never depend on the previous kernel: the producers start their
+  // register rings before the grid dependency wait
+  const int pid = threadIdx.x;
+  const int r = pid >> 1, hf = pid & 1;
+  const bool producer = pid < kTcProducers;
+  const size_t KW = (size_t)(a.K / 8);
+  const uint32_t* W = a.w[seg] + (size_t)(row0 + r) * KW + hf * 4;
+  const uint16_t* S = a.s[seg] + (size_t)(row0 + r) * G;
+  const uint16_t* Bb = a.b[seg] + (size_t)(row0 + r) * G;
+  const uint32_t* W2 = SWIGLU ? a.w2 + (size_t)(row0 + r) * KW + hf * 4 : nullptr;
+  const uint16_t* S2 = SWIGLU ? a.s2 + (size_t)(row0 + r) * G : nullptr;
+  const uint16_t* B2 = SWIGLU ? a.b2 + (size_t)(row0 + r) * G : nullptr;
+  uint4 ring[kRing][NA];
+  uint32_t sb[kRing][NA];  // scale | bias << 16
+  auto fetch = [&](int i, int d) {
+    const int g = g0 + i;
+    ring[d][0] = ldg_stream_u4(W + (size_t)g * 8);
+    sb[d][0] = (uint32_t)S[g] | ((uint32_t)Bb[g] << 16);
+    if constexpr (SWIGLU) {
+      ring[d][1] = ldg_stream_u4(W2 + (size_t)g * 8);
+      sb[d][1] = (uint32_t)S2[g] | ((uint32_t)B2[g] << 16);
+    }
+  };
+  if (producer) {
+#pragma unroll
+    for (int d = 0; d < kRing; ++d)
+      if (d < nst) fetch(d, d);
+  }
+
+  pdl_wait();  // x and the residual come from the previous kernel
+  if (warp == kTcProducers / 32) {
+    tc_alloc(&tmem_base, TCOLS);
+    tc_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base;
+  pdl_launch();
+
+  if (!producer) {
+    // ---------------- TMA + MMA warp ----------------
+    if (lane == 0) {
+      const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                             ((uint32_t)(kTcRows >> 4) << 24);
+      for (int i = 0; i < kTcStages && i < nst; ++i) {
+        uint8_t* st = smem + i * kStage;
+        mbar_arrive_expect_tx(&full_bar[i], kTileB);
+        tma_load_2d(st + NA * kTileA, &xmap, (g0 + i) * 64, m0, &full_bar[i]);
+      }
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % kTcStages;
+        mbar_wait(&full_bar[slot], (i / kTcStages) & 1, a.err);
+        tc_fence_after();
+        uint8_t* st = smem + slot * kStage;
+        const uint32_t sbx = smem_u32(st + NA * kTileA);
+#pragma unroll
+        for (int t = 0; t < NA; ++t) {
+          const uint32_t sa = smem_u32(st + t * kTileA);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma(tbase + t * BN, sw128_desc(sa + kk * 32), sw128_desc(sbx + kk * 32), idesc,
+                   (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(&empty_bar[slot]);
+        if (i + kTcStages < nst) {
+          // reuse this slot for group i + stages once its MMAs have read it
+          mbar_wait(&empty_bar[slot], (i / kTcStages) & 1, a.err);
+          mbar_arrive_expect_tx(&full_bar[slot], kTileB);
+          tma_load_2d(st + NA * kTileA, &xmap, (g0 + i + kTcStages) * 64, m0, &full_bar[slot]);
+        }
+      }
+      tc_commit(&done_bar);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- producers: dequantize into the swizzled A tiles ----------------
+    for (int i0 = 0; i0 < nst; i0 += kRing) {
+#pragma unroll
+      for (int d = 0; d < kRing; ++d) {
+        const int i = i0 + d;
+        if (i >= nst) break;
+        const int slot = i % kTcStages;
+        if (i >= kTcStages) mbar_wait(&empty_bar[slot], ((i / kTcStages) - 1) & 1, a.err);
+        uint8_t* st = smem + slot * kStage;
+#pragma unroll
+        for (int t = 0; t < NA; ++t) {
+          const uint32_t sbv = sb[d][t];
+          const __nv_bfloat162 s2 = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)(sbv & 0xFFFF)),
+                                                        __ushort_as_bfloat16((uint16_t)(sbv & 0xFFFF)));
+          const __nv_bfloat162 b2 = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)(sbv >> 16)),
+                                                        __ushort_as_bfloat16((uint16_t)(sbv >> 16)));
+          const uint32_t* wv = &ring[d][t].x;
+          uint8_t* rowp = st + t * kTileA + r * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int c = hf * 4 + j;  // 16-byte chunk of the 128-byte row
+            *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = dequant8(wv[j], s2, b2);
+          }
+        }
+        fence_proxy_async();
+        mbar_arrive(&full_bar[slot]);
+        if (i + kRing < nst) fetch(i + kRing, d);
+      }
+    }
+
+    // ---------------- epilogue ----------------
+    mbar_wait(&done_bar, 0, a.err);
+    tc_fence_after();
+    const int sub = warp & 3, chalf = warp >> 2;
+    const int row = sub * 32 + lane;
+    float acc[NA][HC];
+#pragma unroll
+    for (int t = 0; t < NA; ++t)
+#pragma unroll
+      for (int c = 0; c < HC; c += 16)
+        tc_ld16(tbase + ((uint32_t)(sub * 32) << 16) + t * BN + chalf * HC + c, &acc[t][c]);
+    tc_wait_ld();
+    tc_fence_before();
+
+    const int tile = m_tile * gridDim.x + n_tile;
+    bool final_cta = true;
+    if (a.splits > 1) {
+      float* mine = a.part + ((size_t)tile * a.splits + split) * NA * kTcRows * BN;
+#pragma unroll
+      for (int t = 0; t < NA; ++t)
+#pragma unroll
+        for (int jj = 0; jj < HC; ++jj) mine[(t * BN + chalf * HC + jj) * kTcRows + row] = acc[t][jj];
+      __threadfence();
+      producers_sync();
+      if (pid == 0) is_last = atomicAdd(a.counters + tile, 1) == a.splits - 1;
+      producers_sync();
+      final_cta = is_last;
+      if (final_cta) {
+        __threadfence();
+        // sum every split in split order (the same bits whichever CTA finishes last)
+#pragma unroll
+        for (int t = 0; t < NA; ++t)
+#pragma unroll
+          for (int jj = 0; jj < HC; ++jj) acc[t][jj] = 0.f;
+        for (int sp = 0; sp < a.splits; ++sp) {
+          const float* p = a.part + ((size_t)tile * a.splits + sp) * NA * kTcRows * BN;
+#pragma unroll
+          for (int t = 0; t < NA; ++t)
+#pragma unroll
+            for (int jj = 0; jj < HC; ++jj) acc[t][jj] += __ldcg(p + (t * BN + chalf * HC + jj) * kTcRows + row);
+        }
+        if (pid == 0) a.counters[tile] = 0;
+      }
+    }
+    if (final_cta) {
+      const int n = n0 + row;
+#pragma unroll
+      for (int jj = 0; jj < HC; ++jj) {
+        const int tok = m0 + chalf * HC + jj;
+        if (tok >= a.M) break;
+        const size_t o = (size_t)tok * a.N + n;
+        if constexpr (SWIGLU) {
+          const float gv = round_bf(acc[0][jj]), uv = round_bf(acc[1][jj]);
+          a.y[o] = f2bf(gv / (1.0f + expf(-gv)) * uv);
+        } else {
+          const float v = acc[0][jj];
+          if (a.y_f32) a.y_f32[o] = v;
+          if (a.y) {
+            uint16_t rv = f2bf(v);
+            if (a.residual) rv = f2bf(bf2f(rv) + bf2f(a.residual[o]));
+            a.y[o] = rv;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == kTcProducers / 32) {
+    tc_fence_after();
+    tc_dealloc(tbase, TCOLS);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// x [M, K] bf16 as TMA tiles of 64 k x BN tokens, 128-byte swizzle (cached per buffer)
+bool x_tensor_map(const void* x, int M, int K, int BN, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int, int>, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_tuple(x, M, K, BN);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return true;
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)BN};
+  const cuuint32_t estr[2] = {1, 1};
+  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  if (cache.size() > 4096) cache.clear();
+  cache[key] = m;
+  *out = m;
+  return true;
+}
+
+int* tc_err_ptr() {
+  static int* p = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    if (cudaMalloc(&p, sizeof(int)) == cudaSuccess) cudaMemset(p, 0, sizeof(int));
+  });
+  return p;
+}
+
+template <int BN, bool SWIGLU>
+cudaError_t launch_bn(const CUtensorMap& map, const TcArgs& a, dim3 grid, cudaStream_t st) {
+  constexpr int NA = SWIGLU ? 2 : 1;
+  constexpr size_t smem = (size_t)kTcStages * (NA * kTileA + BN * 128) + 1024;
+  auto k = qgemm_tc_kernel<BN, SWIGLU>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  return launch_pdl(k, grid, dim3(kTcThreads), smem, st, map, a);
+}
+
+int tc_splits(int M, int K, int N) {
+  const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
+  const int G = K / 64;
+  int splits = (int)((2 * 148 + tiles - 1) / tiles);
+  if (splits > G / 4) splits = G / 4;
+  if (splits < 1 || tiles > 1024) splits = 1;  // the counter region holds 1024 tiles
+  return splits;
+}
+
+}  // namespace
+
+// K % 256 == 0, N (and every row segment) % 128 == 0, x 16-byte aligned, no fused norm.
+bool qgemm_tc_supported(const QLinArgs& a) {
+  if (a.M < 1 || a.K % 256 || a.N % kTcRows || ((uintptr_t)a.x & 15) || a.norm_w || a.moe_items) return false;
+  if (a.nseg > 1)
+    for (int i = 0; i < a.nseg; ++i)
+      if (a.seg_end[i] % kTcRows) return false;
+  return encode_fn() != nullptr;
+}
+
+size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu) {
+  const int splits = tc_splits(M, K, N);
+  if (splits == 1) return 0;
+  const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
+  return 4096 + tiles * splits * (swiglu ? 2 : 1) * kTcRows * BN * sizeof(float);
+}
+
+cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (!qgemm_tc_supported(q)) return cudaErrorInvalidValue;
+  const bool swiglu = epi == EPI_SWIGLU;
+  const int BN = q.M <= 32 ? 32 : (q.M <= 64 ? 64 : 128);
+  CUtensorMap map;
+  if (!x_tensor_map(q.x, q.M, q.K, BN, &map)) return cudaErrorInvalidValue;
+  TcArgs a{};
+  a.M = q.M;
+  a.K = q.K;
+  a.N = q.N;
+  a.nseg = q.nseg > 1 ? q.nseg : 1;
+  if (q.nseg > 1) {
+    for (int i = 0; i < 3; ++i) {
+      a.seg_end[i] = q.seg_end[i];
+      a.w[i] = q.wseg[i];
+      a.s[i] = q.sseg[i];
+      a.b[i] = q.bseg[i];
+    }
+  } else {
+    a.w[0] = q.w;
+    a.s[0] = q.s;
+    a.b[0] = q.b;
+  }
+  a.w2 = q.w2;
+  a.s2 = q.s2;
+  a.b2 = q.b2;
+  a.y = q.y;
+  a.y_f32 = q.y_f32;
+  a.residual = q.residual;
+  a.err = tc_err_ptr();
+  const int n_tiles = q.N / kTcRows, m_tiles = (q.M + BN - 1) / BN;
+  const int G = q.K / 64;
+  int splits = 1;
+  const size_t need = qgemm_tc_workspace(q.M, q.K, q.N, swiglu);
+  if (need && ws && ws_bytes >= need && ((uintptr_t)ws & 255) == 0) {
+    splits = tc_splits(q.M, q.K, q.N);
+    a.counters = static_cast<int*>(ws);
+    a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + 4096);
+  }
+  a.groups_per_split = (G + splits - 1) / splits;
+  a.splits = (G + a.groups_per_split - 1) / a.groups_per_split;  // every split holds >= 1 group
+  const dim3 grid(n_tiles, m_tiles, a.splits);
+  if (swiglu) {
+    if (BN == 32) return launch_bn<32, true>(map, a, grid, st);
+    if (BN == 64) return launch_bn<64, true>(map, a, grid, st);
+    return launch_bn<128, true>(map, a, grid, st);
+  }
+  if (BN == 32) return launch_bn<32, false>(map, a, grid, st);
+  if (BN == 64) return launch_bn<64, false>(map, a, grid, st);
+  return launch_bn<128, false>(map, a, grid, st);
+}
+
+// one-time host state (error flag, driver entry point): call before any stream capture
+void qgemm_tc_prepare() {
+  tc_err_ptr();
+  encode_fn();
+}
+
+int qgemm_tc_error_and_clear() {
+  int* p = tc_err_ptr();
+  if (!p) return 0;
+  int v = 0;
+  cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost);
+  if (v) cudaMemset(p, 0, sizeof(int));
+  return v;
+}
+
+}  // namespace higgs
+
+extern "C" int higgs_tc_error(int* out) {
+  HG_CHECK_ARG(out, "higgs_tc_error: null argument");
+  *out = higgs::qgemm_tc_error_and_clear();
+  return HIGGS_OK;
+}

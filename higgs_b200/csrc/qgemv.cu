@@ -169,10 +169,12 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
     pdl_launch();
     if ((int)blockIdx.y >= *a.moe_n_items) return;  // uniform over the CTA
     const int4 it = a.moe_items[blockIdx.y];
+    if (a.moe_e_n && (it.x < a.moe_e_lo || it.x >= a.moe_e_lo + a.moe_e_n)) return;  // another rank's
     M = it.z;
-    sg.W += (long long)it.x * a.moe_ew;
-    sg.S += (long long)it.x * a.moe_es;
-    sg.B += (long long)it.x * a.moe_es;
+    const long long el = it.x - a.moe_e_lo;  // index among the experts held here
+    sg.W += el * a.moe_ew;
+    sg.S += el * a.moe_es;
+    sg.B += el * a.moe_es;
     if (a.self_prefetch && tile_ok && kw == 0 && lane == 0) {
       l2_prefetch_range(sg.W + (size_t)sg.row0 * KW, (size_t)16 * KW * 4);
       l2_prefetch_range(sg.S + (size_t)sg.row0 * G, (size_t)16 * G * 2);
@@ -545,6 +547,9 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
     }
 }
 
+// K-split ways per row tile forced through higgs_set_option("gemv_wk", 1|2|4|8); 0 = heuristic
+int g_force_wk = 0;
+
 template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER>
 cudaError_t launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
   auto k = qgemv_ring_kernel<NT8, WK, EPI, S, XSMEM, NORM, F16, GATHER>;
@@ -578,6 +583,7 @@ cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
     wk = 4;  // 2 warp tiles (one gate/up pair) per CTA
     if ((work + 1) / 2 >= slots && units >= 2) wk = 2;
     if ((work + 3) / 4 >= slots) wk = 1;
+    if (g_force_wk == 1 || g_force_wk == 2 || g_force_wk == 4) wk = g_force_wk;
     while (wk > 1 && units < wk) wk >>= 1;
     if (wk > 4) wk = 4;
     const int rot = (8 / wk) / 2;
@@ -586,10 +592,10 @@ cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
     if (wk == 2) return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
     return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
   }
-  wk = 8;
-  if (work / 2 >= slots) wk = 4;
-  if (work / 4 >= slots) wk = 2;
-  if (work / 8 >= slots) wk = 1;
+  // measured on B200 (M=1): K split 8 ways while the tiles alone cannot fill the
+  // slots, else 4 ways -- more CTAs beat fewer fatter ones even for the LM head
+  wk = (work / 2 >= slots) ? 4 : 8;
+  if (g_force_wk > 0) wk = g_force_wk;
   while (wk > 1 && units < wk) wk >>= 1;
   const int rot = 8 / wk;
   const int ctas = (nrt + rot - 1) / rot;
@@ -626,8 +632,15 @@ cudaError_t launch_epi(const QLinArgs& a, cudaStream_t st) {
 
 // M rows per pass: <= 32 (a fused norm needs M <= 8 and the x tile in shared memory).
 bool qgemv_ring_can_fuse_norm(int M, int K);
+static bool g_gemm_tc = true;  // route M >= g_gemm_tc_rows to the tensor-core path
+static int g_gemm_tc_rows = 16;
+void set_gemm_tc(bool on) { g_gemm_tc = on; }
+void set_gemm_tc_rows(int m) { g_gemm_tc_rows = m < 1 ? 1 : m; }
+
 cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st) {
   if (a.norm_w && !qgemv_ring_can_fuse_norm(a.M, a.K)) return cudaErrorInvalidValue;
+  if (g_gemm_tc && a.M >= g_gemm_tc_rows && qgemm_tc_supported(a))
+    return launch_qgemm_tc(a, epi, a.tc_ws, a.tc_ws_bytes, st);
   QLinArgs c = a;
   for (int m0 = 0; m0 < a.M; m0 += 32) {
     c.M = (a.M - m0) < 32 ? (a.M - m0) : 32;
@@ -654,6 +667,7 @@ cudaError_t launch_qgemv_grouped(const QLinArgs& a, int epi, cudaStream_t st) {
 }
 
 void qgemv_set_f16(bool on) { g_gemv_f16 = on; }
+void qgemv_set_wk(int wk) { g_force_wk = (wk == 1 || wk == 2 || wk == 4 || wk == 8) ? wk : 0; }
 
 // L2 prefetch of GEMV weights: bit 0 = the step's next GEMV, bit 1 = each CTA's
 // own tiles.  Off by default: measured on B200 it lengthened the decode step.

@@ -197,14 +197,23 @@ _COL = ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "mlp.gate_pr
 _ROW = ("self_attn.o_proj", "mlp.down_proj")
 
 
+def kv_heads_per_rank(args: ModelArgs, world: int) -> int:
+    """kv heads a rank holds: an even share, or one head replicated over world / Hkv ranks
+    when there are fewer kv heads than ranks (each rank's query heads then belong to it)."""
+    return max(1, args.num_key_value_heads // world)
+
+
 def check_tp(args: ModelArgs, world: int):
-    """The shapes a `world`-way split needs: whole heads and kv heads per rank, K slices of the
-    row-parallel projections in whole 256-column units, 16-row vocabulary shards."""
-    D = args.head_dim
-    ok = (args.num_experts == 0 and args.num_attention_heads % world == 0
-          and args.num_key_value_heads % world == 0
-          and (args.num_attention_heads // world * D) % 256 == 0
-          and args.intermediate_size % (256 * world) == 0 and args.vocab_size % (16 * world) == 0)
+    """The shapes a `world`-way split needs: whole query heads per rank and kv heads either
+    split evenly or replicated, K slices of the row-parallel projections in whole 256-column
+    units, 16-row vocabulary shards, and (MoE) whole experts per rank."""
+    D, Hq, Hkv = args.head_dim, args.num_attention_heads, args.num_key_value_heads
+    kv_ok = Hkv % world == 0 or (world % Hkv == 0 and Hq // world <= Hq // Hkv)
+    dense = any(not args.is_moe_layer(i) for i in range(args.num_hidden_layers))
+    ok = (Hq % world == 0 and kv_ok and (Hq // world * D) % 256 == 0
+          and (not dense or args.intermediate_size % (256 * world) == 0)
+          and args.vocab_size % (16 * world) == 0
+          and (args.num_experts == 0 or args.num_experts % world == 0))
     if not ok:
         raise ValueError(f"{args.model_type} cannot be split {world} ways")
 
@@ -212,8 +221,13 @@ def check_tp(args: ModelArgs, world: int):
 def shard_weights(args: ModelArgs, weights: dict, rank: int, world: int) -> dict:
     """This rank's slices of MLX-layout weights (numpy arrays or torch tensors): rows of the
     column-parallel projections and of the LM head, K columns (in 64-wide groups) of the
-    row-parallel ones; norms and the embedding whole (a tied head is sliced by the runner)."""
+    row-parallel ones, its kv head(s), its experts (expert parallelism: experts
+    [rank*E/world, (rank+1)*E/world)); norms, the router and the embedding whole (a tied
+    head is sliced by the runner)."""
     check_tp(args, world)
+    D, Hkv = args.head_dim, args.num_key_value_heads
+    kvr = kv_heads_per_rank(args, world)
+    kv0 = (rank * Hkv) // world if Hkv < world else rank * kvr  # first kv head of this rank
 
     def cont(a):
         return a.contiguous() if isinstance(a, torch.Tensor) else np.ascontiguousarray(a)
@@ -221,12 +235,17 @@ def shard_weights(args: ModelArgs, weights: dict, rank: int, world: int) -> dict
     for name, t in weights.items():
         base, _, leaf = name.rpartition(".")
         mod = base.split(".", 3)[-1] if base.startswith("model.layers.") else base
-        if mod in _COL or base == "lm_head":
+        if mod in ("self_attn.k_proj", "self_attn.v_proj"):
+            out[name] = t[kv0 * D:(kv0 + kvr) * D]
+        elif mod in _COL or base == "lm_head":
             n = t.shape[0] // world
             out[name] = t[rank * n:(rank + 1) * n]
         elif mod in _ROW:
             n = t.shape[1] // world  # words (weight) or groups (scales / biases)
             out[name] = cont(t[:, rank * n:(rank + 1) * n])
+        elif mod.startswith("mlp.switch_mlp."):
+            n = t.shape[0] // world
+            out[name] = t[rank * n:(rank + 1) * n]
         else:
             out[name] = t
     return out
@@ -302,7 +321,7 @@ class Model:
         if tp:
             check_tp(args, w)
         cfg = ffi.ModelConfig(args.hidden_size, args.num_hidden_layers, args.intermediate_size // w,
-                              args.num_attention_heads // w, args.num_key_value_heads // w,
+                              args.num_attention_heads // w, kv_heads_per_rank(args, w),
                               args.head_dim, args.vocab_size, args.rms_norm_eps, args.rope_theta,
                               int(args.tie_word_embeddings), int(args.qk_norm),
                               ffi.KV_TQ4 if kv_mode == "tq4" else ffi.KV_BF16, args.num_experts,
@@ -322,7 +341,7 @@ class Model:
         ffi.call("higgs_model_finalize", self.handle)
         if tp:
             ffi.call("higgs_model_set_comm", self.handle, tp.handle)
-        L, Hkv, D = args.num_hidden_layers, args.num_key_value_heads // w, args.head_dim
+        L, Hkv, D = args.num_hidden_layers, kv_heads_per_rank(args, w), args.head_dim
         if kv_mode == "tq4":
             self.signs = torch.from_numpy(hadamard_signs() if signs is None else signs).to(self.device)
             self.k_pool = torch.zeros(L, num_pages, Hkv, PAGE, 64, dtype=torch.uint8, device=self.device)

@@ -79,8 +79,17 @@ int higgs_version(void);
  * sizes depend on it.  "l2_prefetch" (bit mask, default 0): bit 0 makes every
  * GEMV of the decode step ask the TMA unit to pull the next GEMV's weights into
  * L2, bit 1 makes each GEMV CTA pull its own weight tiles (a hint; results are
- * unchanged).  Unknown names return HIGGS_ERR_INVALID_ARG. */
+ * unchanged).  "gemm_tc" (0/1, default 1): quantized linears over 16 or more
+ * rows use the tcgen05 tensor-core kernel (weights dequantized to bf16 first,
+ * MLX's qmm form) instead of the decode GEMV; "gemm_tc_rows" (default 16) moves
+ * that threshold (fused-RMSNorm decode launches always stay on the GEMV).  "gemv_wk" (0, 1, 2, 4, 8; default
+ * 0 = heuristic): ways each 16-row tile of the decode GEMV splits K over warps.
+ * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
+
+/* Nonzero when a bounded wait of the tensor-core quantized matmul gave up since
+ * the last call (the error flag is then cleared).  Synchronising. */
+int higgs_tc_error(int* out);
 
 /* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
 

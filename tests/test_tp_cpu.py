@@ -148,3 +148,87 @@ def test_shard_weights_slices():
         np.testing.assert_allclose(tot, full, rtol=1e-4, atol=1e-5)
     with pytest.raises(ValueError):
         shard_weights(args, w, 0, 3)  # 8 heads do not split 3 ways
+
+
+def _ep_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    try:
+        import torch
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from higgs_b200.model import shard_weights, tiny_args
+        args = tiny_args("qwen3_moe", layers=1)
+        w = synth_weights_numpy(args, seed=0)
+        sw = shard_weights(args, w, rank, world)
+        p = "model.layers.0.mlp."
+        rng = np.random.default_rng(6)
+        T, k, H = 5, args.num_experts_per_tok, args.hidden_size
+        x = orc.f32_to_bf16(rng.normal(0, 1, size=(T, H)))
+        rl = orc.qmatmul(x, sw[p + "gate.weight"], sw[p + "gate.scales"], sw[p + "gate.biases"])
+        idx, sc = orc.moe_route_topk(orc.bf16_to_f32(rl), k, args.norm_topk_prob)
+        El = args.num_experts // world
+        e_lo = rank * El
+        trip = lambda n: tuple(sw[p + "switch_mlp." + n + "." + l] for l in ("weight", "scales", "biases"))  # noqa: E731
+        g, u, d = trip("gate_proj"), trip("up_proj"), trip("down_proj")
+        part = np.zeros((T, H), np.float32)
+        for t_ in range(T):
+            for j in range(k):
+                e = int(idx[t_, j])
+                if not e_lo <= e < e_lo + El:
+                    continue
+                el = e - e_lo
+                xe = x[t_:t_ + 1]
+                a = orc.silu_mul(orc.qmatmul(xe, g[0][el], g[1][el], g[2][el]),
+                                 orc.qmatmul(xe, u[0][el], u[1][el], u[2][el]))
+                y = orc.qmatmul(a, d[0][el], d[1][el], d[2][el])
+                part[t_] += orc.bf16_to_f32(orc.f32_to_bf16(sc[t_, j])) * orc.bf16_to_f32(y[0])
+        tt = torch.from_numpy(part)
+        dist.all_reduce(tt)
+        q.put((rank, tt.numpy(), x, idx, sc))
+    except Exception:
+        import traceback
+        q.put((rank, None, traceback.format_exc(), None, None))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_ep_moe_decomposition_matches_oracle():
+    """Expert parallelism: each rank runs only its experts' pairs and the f32 shares summed
+    over ranks equal the whole block (oracle moe_experts + combine) before the final rounding."""
+    from higgs_b200.model import tiny_args
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29650 + os.getpid() % 1000
+    ps = [ctx.Process(target=_ep_worker, args=(r, world, port, q)) for r in range(world)]
+    for p_ in ps:
+        p_.start()
+    res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
+    for p_ in ps:
+        p_.join(timeout=60)
+    for r in res:
+        assert r[1] is not None, r[2]
+    args = tiny_args("qwen3_moe", layers=1)
+    w = synth_weights_numpy(args, seed=0)
+    p = "model.layers.0.mlp.switch_mlp."
+    trip = lambda n: tuple(w[p + n + "." + l] for l in ("weight", "scales", "biases"))  # noqa: E731
+    _, _, x, idx, sc = res[0]
+    y = orc.moe_experts(x, idx, trip("gate_proj"), trip("up_proj"), trip("down_proj"))
+    h0 = np.zeros(x.shape, np.uint16)
+    full = orc.bf16_to_f32(orc.moe_combine(y, sc, h0))  # bf16(sum) on a zero residual
+    ep = orc.bf16_to_f32(orc.f32_to_bf16(res[0][1]))
+    np.testing.assert_array_equal(res[0][1], res[1][1])
+    np.testing.assert_allclose(ep, full, atol=1e-3 * np.abs(full).max(), rtol=1e-2)
+
+
+def test_shard_weights_replicates_kv_heads_when_fewer_than_ranks():
+    from higgs_b200.model import ModelArgs, kv_heads_per_rank, shard_weights
+    args = ModelArgs("qwen3", 512, 1, 1024, 8, 2, 128, 4096, 1e-6, 1000000.0, False)
+    w = synth_weights_numpy(args, seed=0)
+    assert kv_heads_per_rank(args, 4) == 1
+    k = "model.layers.0.self_attn.k_proj.weight"
+    parts = [shard_weights(args, w, r, 4)[k] for r in range(4)]
+    D = args.head_dim
+    for r in range(4):  # ranks 0,1 hold kv head 0 (query heads 0-3), ranks 2,3 kv head 1
+        assert np.array_equal(parts[r], w[k][(r // 2) * D:(r // 2 + 1) * D])

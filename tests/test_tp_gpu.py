@@ -19,7 +19,14 @@ pytestmark = [pytest.mark.gpu,
 STEPS = 32
 
 
-def _worker(rank, world, port, q):
+def moe_tp_args():
+    """Tiny Qwen3-MoE (layer 1 dense) whose dense FFN splits two ways."""
+    import dataclasses
+    from higgs_b200.model import tiny_args
+    return dataclasses.replace(tiny_args("qwen3_moe", layers=3), intermediate_size=1024)
+
+
+def _worker(rank, world, port, q, kind="dense"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     try:
@@ -31,7 +38,7 @@ def _worker(rank, world, port, q):
         from higgs_b200.engine import Engine
         from higgs_b200.model import Model, TPGroup, shard_weights, weights_to_device
         from tests.test_tp_cpu import tp_args
-        args = tp_args()
+        args = tp_args() if kind == "dense" else moe_tp_args()
         w = synth_weights_numpy(args, seed=0)
         dev = f"cuda:{rank}"
         wd = weights_to_device(shard_weights(args, w, rank, world), dev)
@@ -57,15 +64,17 @@ def _worker(rank, world, port, q):
             dist.destroy_process_group()
 
 
-def test_tp2_greedy_matches_oracle():
-    from oracle import oracle as orc
+@pytest.mark.parametrize("kind", ["dense", "moe"])
+def test_tp2_greedy_matches_oracle(kind):
+    """Dense: tensor parallel.  MoE: attention tensor parallel, experts split over the two
+    ranks (expert parallelism) with the expert outputs summed by the same all-reduce."""
     from oracle.model_ref import RefModel, synth_weights_numpy
     from tests.test_tp_cpu import tp_args
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + os.getpid() % 1000
-    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    port = 29700 + os.getpid() % 1000 + (7 if kind == "moe" else 0)
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q, kind)) for r in range(world)]
     for p_ in ps:
         p_.start()
     res = sorted((q.get(timeout=600) for _ in range(world)), key=lambda r: r[0])
@@ -75,14 +84,17 @@ def test_tp2_greedy_matches_oracle():
         assert r[1] is not None, r[2]
         assert r[2] == 0, "a collective timed out"
     assert np.array_equal(res[0][1], res[1][1])
-    args = tp_args()
+    args = tp_args() if kind == "dense" else moe_tp_args()
     w = synth_weights_numpy(args, seed=0)
     pr = np.random.default_rng(1).integers(0, args.vocab_size, size=(2, 20)).astype(np.int32)
-    ref_tok, ref_lg = RefModel(args, w).greedy(pr, STEPS)
+    ref = RefModel(args, w)
+    ref_tok, ref_lg = ref.greedy(pr, STEPS)
     top2 = np.sort(ref_lg, axis=-1)[..., -2:]
     margin = top2[..., 1] - top2[..., 0]  # [steps, B]
+    near = ref.step_route_near  # MoE routings within one bf16 ulp of a swap
     for b in range(2):
         d = np.nonzero(res[0][1][b] != ref_tok[b])[0]
         if d.size:
             k = int(d[0])
-            assert margin[k, b] < 4e-2, f"seq {b} diverges at step {k} with margin {margin[k, b]:.3f}"
+            assert margin[k, b] < 4e-2 or near[:k + 1, b].any(), (
+                f"seq {b} diverges at step {k} with margin {margin[k, b]:.3f}")

@@ -62,7 +62,8 @@ def test_noalloc_rejects_shapes_beyond_its_scratch():
     lib = ffi.load()
     q = torch.zeros(1, dtype=torch.bfloat16, device=DEV)
     bt = torch.zeros(1, dtype=torch.int32, device=DEV)
-    # 295 sequences x 1 kv head x 32 query heads split twice: 9.75 MB of partials > 8 MiB.
+    # 295 sequences x 1 kv head x 32 query heads at 4096 tokens: tens of MB of split
+    # partials, far beyond the 8 MiB built-in scratch.
     # Rejected on the host before anything is launched or read.
     rc = lib.higgs_paged_attention_noalloc(ffi.ctx(0), q.data_ptr(), 295, 1, 32, 1, 128,
                                            q.data_ptr(), q.data_ptr(), 2048, 2048, bt.data_ptr(),
