@@ -68,6 +68,7 @@ def dist_setup():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if ws > 1:
         import datetime
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # stdout carries only the JSON line
 
         import torch.distributed as dist
         torch.cuda.set_device(local)

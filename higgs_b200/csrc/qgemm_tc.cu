@@ -9,9 +9,11 @@
 //
 // One CTA computes a 128-row x BN-token tile over a slice of K (split-K when the
 // tile count alone cannot fill the GPU):
-//   * 8 producer warps: thread (row, half) streams 16 bytes of packed weights per
-//     64-wide k group (a register ring 8 groups deep), dequantizes them with
-//     LOP3 / bf16x2 FMA / PRMT and stores the bf16 row slice into shared memory
+//   * 1 loader warp: TMA streams the packed weight tile (128 rows x 32 bytes per
+//     64-wide k group) into an 8-stage shared-memory ring, starting before the
+//     grid dependency wait (weights never depend on the previous kernel);
+//   * 8 producer warps: thread (row, half) takes 16 packed bytes from the ring,
+//     dequantizes them with LOP3 / bf16x2 FMA / PRMT and stores the bf16 row slice
 //     in the 128-byte-swizzled K-major layout the MMA reads;
 //   * 1 MMA warp: TMA brings the x tile (BN tokens x 64 k, same swizzle), one
 //     elected lane issues tcgen05.mma (M=128, N=BN, K=16) x 4 per group into a
@@ -25,6 +27,7 @@
 // higgs_tc_error reports, and finishes.
 #include <cuda.h>
 
+#include <cstring>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -37,11 +40,12 @@ namespace higgs {
 namespace {
 
 constexpr int kTcRows = 128;       // weight rows per tile (UMMA M)
-constexpr int kTcStages = 4;       // shared-memory stages (k groups)
-constexpr int kTcProducers = 256;  // 8 warps, thread = (row, half of 64 k)
-constexpr int kTcThreads = kTcProducers + 32;
+constexpr int kTcProducers = 256;      // 8 warps, thread = (row, half of 64 k)
+constexpr int kTcThreads = kTcProducers + 64;  // + MMA warp + weight-loader warp
 constexpr int kTileA = kTcRows * 128;  // 128 rows x 64 bf16 = 16 KB
-constexpr int kRing = 8;               // k groups in flight per producer thread
+constexpr int kPkTile = kTcRows * 32;  // 128 rows x 64 packed nibbles = 4 KB
+constexpr int kPkStages = 8;           // packed weight stages in flight (TMA)
+constexpr int kRing = 8;               // scale / bias groups prefetched per producer thread
 
 struct TcArgs {
   int M, K, N;
@@ -167,17 +171,29 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bf
                     prmt(q[2], q[3], 0x7632));
 }
 
+// Weight tiles of a CTA: the packed rows [row0, row0 + 128) of one tensor, 64 k per stage.
+struct WMaps {
+  CUtensorMap w[3];  // q | k | v segments (or the single tensor)
+  CUtensorMap up;    // SwiGLU up projection
+};
+
 template <int BN, bool SWIGLU>
-__global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+__global__ void __launch_bounds__(kTcThreads, 1)
+    qgemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ WMaps wm, TcArgs a) {
   constexpr int NA = SWIGLU ? 2 : 1;
+  constexpr int AS = SWIGLU ? 3 : 4;  // bf16 operand stages
   constexpr int kTileB = BN * 128;
   constexpr int kStage = NA * kTileA + kTileB;
+  constexpr int kPk = NA * kPkTile;  // packed bytes per stage
   constexpr int TCOLS = (NA * BN <= 32) ? 32 : (NA * BN <= 64) ? 64 : (NA * BN <= 128) ? 128 : 256;
   constexpr int HC = BN / 2;  // accumulator columns read per producer warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t full_bar[kTcStages];
-  __shared__ __align__(8) uint64_t empty_bar[kTcStages];
+  uint8_t* pk = smem + AS * kStage;  // packed ring (1024-aligned: kStage is a multiple of 1024)
+  __shared__ __align__(8) uint64_t full_bar[AS];
+  __shared__ __align__(8) uint64_t empty_bar[AS];
+  __shared__ __align__(8) uint64_t pk_full[kPkStages];
+  __shared__ __align__(8) uint64_t pk_empty[kPkStages];
   __shared__ __align__(8) uint64_t done_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int is_last;
@@ -196,46 +212,56 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const __grid_co
   const int row0 = n0 - (seg ? a.seg_end[seg - 1] : 0);
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcStages; ++i) {
+    for (int i = 0; i < AS; ++i) {
       mbar_init(&full_bar[i], kTcProducers + 1);
       mbar_init(&empty_bar[i], 1);
+    }
+    for (int i = 0; i < kPkStages; ++i) {
+      mbar_init(&pk_full[i], 1);
+      mbar_init(&pk_empty[i], kTcProducers);
     }
     mbar_init(&done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  // weights never depend on the previous kernel: the producers start their
-  // register rings before the grid dependency wait
   const int pid = threadIdx.x;
   const int r = pid >> 1, hf = pid & 1;
   const bool producer = pid < kTcProducers;
-  const size_t KW = (size_t)(a.K / 8);
-  const uint32_t* W = a.w[seg] + (size_t)(row0 + r) * KW + hf * 4;
+  const int mma_warp = kTcProducers / 32, load_warp = mma_warp + 1;
+
+  // weights never depend on the previous kernel: the loader fills the whole packed
+  // ring before the grid dependency wait (no waits needed for the first pass)
+  const CUtensorMap* wmap = &wm.w[seg];
+  auto load_stage = [&](int i) {
+    const int slot = i % kPkStages;
+    mbar_arrive_expect_tx(&pk_full[slot], kPk);
+    uint8_t* dst = pk + slot * kPk;
+    tma_load_2d(dst, wmap, (g0 + i) * 32, row0, &pk_full[slot]);
+    if constexpr (SWIGLU) tma_load_2d(dst + kPkTile, &wm.up, (g0 + i) * 32, row0, &pk_full[slot]);
+  };
+  if (warp == load_warp && lane == 0)
+    for (int i = 0; i < kPkStages && i < nst; ++i) load_stage(i);
+
+  // scales / biases: a small register ring, also before the wait
   const uint16_t* S = a.s[seg] + (size_t)(row0 + r) * G;
   const uint16_t* Bb = a.b[seg] + (size_t)(row0 + r) * G;
-  const uint32_t* W2 = SWIGLU ? a.w2 + (size_t)(row0 + r) * KW + hf * 4 : nullptr;
   const uint16_t* S2 = SWIGLU ? a.s2 + (size_t)(row0 + r) * G : nullptr;
   const uint16_t* B2 = SWIGLU ? a.b2 + (size_t)(row0 + r) * G : nullptr;
-  uint4 ring[kRing][NA];
   uint32_t sb[kRing][NA];  // scale | bias << 16
-  auto fetch = [&](int i, int d) {
+  auto fetch_sb = [&](int i, int d) {
     const int g = g0 + i;
-    ring[d][0] = ldg_stream_u4(W + (size_t)g * 8);
     sb[d][0] = (uint32_t)S[g] | ((uint32_t)Bb[g] << 16);
-    if constexpr (SWIGLU) {
-      ring[d][1] = ldg_stream_u4(W2 + (size_t)g * 8);
-      sb[d][1] = (uint32_t)S2[g] | ((uint32_t)B2[g] << 16);
-    }
+    if constexpr (SWIGLU) sb[d][1] = (uint32_t)S2[g] | ((uint32_t)B2[g] << 16);
   };
   if (producer) {
 #pragma unroll
     for (int d = 0; d < kRing; ++d)
-      if (d < nst) fetch(d, d);
+      if (d < nst) fetch_sb(d, d);
   }
 
   pdl_wait();  // x and the residual come from the previous kernel
-  if (warp == kTcProducers / 32) {
+  if (warp == mma_warp) {
     tc_alloc(&tmem_base, TCOLS);
     tc_relinquish();
   }
@@ -245,19 +271,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const __grid_co
   const uint32_t tbase = tmem_base;
   pdl_launch();
 
-  if (!producer) {
-    // ---------------- TMA + MMA warp ----------------
+  if (warp == load_warp) {
+    // ---------------- loaders: lane 0 refills each packed weight slot once the producers
+    // drained it; lane 1 brings each x tile once the MMAs of that stage slot are done
+    if (lane == 0) {
+      for (int i = kPkStages; i < nst; ++i) {
+        mbar_wait(&pk_empty[i % kPkStages], ((i / kPkStages) - 1) & 1, a.err);
+        load_stage(i);
+      }
+    } else if (lane == 1) {
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % AS;
+        if (i >= AS) mbar_wait(&empty_bar[slot], ((i / AS) - 1) & 1, a.err);
+        mbar_arrive_expect_tx(&full_bar[slot], kTileB);
+        tma_load_2d(smem + slot * kStage + NA * kTileA, &xmap, (g0 + i) * 64, m0, &full_bar[slot]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == mma_warp) {
+    // ---------------- MMA warp: one elected lane issues, commits release the stage ----------------
     if (lane == 0) {
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                              ((uint32_t)(kTcRows >> 4) << 24);
-      for (int i = 0; i < kTcStages && i < nst; ++i) {
-        uint8_t* st = smem + i * kStage;
-        mbar_arrive_expect_tx(&full_bar[i], kTileB);
-        tma_load_2d(st + NA * kTileA, &xmap, (g0 + i) * 64, m0, &full_bar[i]);
-      }
       for (int i = 0; i < nst; ++i) {
-        const int slot = i % kTcStages;
-        mbar_wait(&full_bar[slot], (i / kTcStages) & 1, a.err);
+        const int slot = i % AS;
+        mbar_wait(&full_bar[slot], (i / AS) & 1, a.err);
         tc_fence_after();
         uint8_t* st = smem + slot * kStage;
         const uint32_t sbx = smem_u32(st + NA * kTileA);
@@ -270,25 +308,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const __grid_co
                    (i > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(&empty_bar[slot]);
-        if (i + kTcStages < nst) {
-          // reuse this slot for group i + stages once its MMAs have read it
-          mbar_wait(&empty_bar[slot], (i / kTcStages) & 1, a.err);
-          mbar_arrive_expect_tx(&full_bar[slot], kTileB);
-          tma_load_2d(st + NA * kTileA, &xmap, (g0 + i + kTcStages) * 64, m0, &full_bar[slot]);
-        }
       }
       tc_commit(&done_bar);
     }
     __syncwarp();
-  } else {
-    // ---------------- producers: dequantize into the swizzled A tiles ----------------
+  } else if (producer) {
+    // ---------------- producers: packed smem -> bf16 swizzled A tiles ----------------
     for (int i0 = 0; i0 < nst; i0 += kRing) {
 #pragma unroll
       for (int d = 0; d < kRing; ++d) {
         const int i = i0 + d;
         if (i >= nst) break;
-        const int slot = i % kTcStages;
-        if (i >= kTcStages) mbar_wait(&empty_bar[slot], ((i / kTcStages) - 1) & 1, a.err);
+        const int ps = i % kPkStages, slot = i % AS;
+        mbar_wait(&pk_full[ps], (i / kPkStages) & 1, a.err);
+        uint4 wv[NA];
+#pragma unroll
+        for (int t = 0; t < NA; ++t)
+          wv[t] = *reinterpret_cast<const uint4*>(pk + ps * kPk + t * kPkTile + r * 32 + hf * 16);
+        mbar_arrive(&pk_empty[ps]);
+        if (i >= AS) mbar_wait(&empty_bar[slot], ((i / AS) - 1) & 1, a.err);
         uint8_t* st = smem + slot * kStage;
 #pragma unroll
         for (int t = 0; t < NA; ++t) {
@@ -297,17 +335,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const __grid_co
                                                         __ushort_as_bfloat16((uint16_t)(sbv & 0xFFFF)));
           const __nv_bfloat162 b2 = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)(sbv >> 16)),
                                                         __ushort_as_bfloat16((uint16_t)(sbv >> 16)));
-          const uint32_t* wv = &ring[d][t].x;
+          const uint32_t* w = &wv[t].x;
           uint8_t* rowp = st + t * kTileA + r * 128;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int c = hf * 4 + j;  // 16-byte chunk of the 128-byte row
-            *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = dequant8(wv[j], s2, b2);
+            *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = dequant8(w[j], s2, b2);
           }
         }
         fence_proxy_async();
         mbar_arrive(&full_bar[slot]);
-        if (i + kRing < nst) fetch(i + kRing, d);
+        if (i + kRing < nst) fetch_sb(i + kRing, d);
       }
     }
 
@@ -378,7 +416,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) qgemm_tc_kernel(const __grid_co
     }
   }
   __syncthreads();
-  if (warp == kTcProducers / 32) {
+  if (warp == mma_warp) {
     tc_fence_after();
     tc_dealloc(tbase, TCOLS);
   }
@@ -430,6 +468,34 @@ bool x_tensor_map(const void* x, int M, int K, int BN, CUtensorMap* out) {
   return true;
 }
 
+// packed weights [rows, K/2 bytes] as TMA tiles of 32 bytes (64 k) x 128 rows (cached)
+bool w_tensor_map(const void* w, int rows, int K, CUtensorMap* out) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int>, CUtensorMap> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  auto key = std::make_tuple(w, rows, K);
+  auto it = cache.find(key);
+  if (it != cache.end()) {
+    *out = it->second;
+    return true;
+  }
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || ((uintptr_t)w & 15)) return false;
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {(cuuint64_t)K / 2, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)K / 2};
+  const cuuint32_t box[2] = {32, (cuuint32_t)kTcRows};
+  const cuuint32_t estr[2] = {1, 1};
+  if (fn(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(w), dims, strides, box, estr,
+         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  if (cache.size() > 65536) cache.clear();
+  cache[key] = m;
+  *out = m;
+  return true;
+}
+
 int* tc_err_ptr() {
   static int* p = nullptr;
   static std::once_flag once;
@@ -440,9 +506,11 @@ int* tc_err_ptr() {
 }
 
 template <int BN, bool SWIGLU>
-cudaError_t launch_bn(const CUtensorMap& map, const TcArgs& a, dim3 grid, cudaStream_t st) {
+cudaError_t launch_bn(const CUtensorMap& map, const WMaps& wm, const TcArgs& a, dim3 grid, cudaStream_t st) {
   constexpr int NA = SWIGLU ? 2 : 1;
-  constexpr size_t smem = (size_t)kTcStages * (NA * kTileA + BN * 128) + 1024;
+  constexpr int AS = SWIGLU ? 3 : 4;
+  constexpr size_t smem = (size_t)AS * (NA * kTileA + BN * 128) + (size_t)kPkStages * NA * kPkTile + 1024;
+  static_assert(smem <= 227 * 1024, "shared memory budget");
   auto k = qgemm_tc_kernel<BN, SWIGLU>;
   static bool attr = false;
   if (!attr) {
@@ -450,7 +518,7 @@ cudaError_t launch_bn(const CUtensorMap& map, const TcArgs& a, dim3 grid, cudaSt
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  return launch_pdl(k, grid, dim3(kTcThreads), smem, st, map, a);
+  return launch_pdl(k, grid, dim3(kTcThreads), smem, st, map, wm, a);
 }
 
 int tc_splits(int M, int K, int N) {
@@ -512,6 +580,13 @@ cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_byte
   a.y_f32 = q.y_f32;
   a.residual = q.residual;
   a.err = tc_err_ptr();
+  WMaps wm;
+  memset(&wm, 0, sizeof(wm));
+  for (int i = 0; i < a.nseg; ++i) {
+    const int rows = a.nseg > 1 ? a.seg_end[i] - (i ? a.seg_end[i - 1] : 0) : q.N;
+    if (!w_tensor_map(a.w[i], rows, q.K, &wm.w[i])) return cudaErrorInvalidValue;
+  }
+  if (swiglu && !w_tensor_map(a.w2, q.N, q.K, &wm.up)) return cudaErrorInvalidValue;
   const int n_tiles = q.N / kTcRows, m_tiles = (q.M + BN - 1) / BN;
   const int G = q.K / 64;
   int splits = 1;
@@ -525,13 +600,13 @@ cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_byte
   a.splits = (G + a.groups_per_split - 1) / a.groups_per_split;  // every split holds >= 1 group
   const dim3 grid(n_tiles, m_tiles, a.splits);
   if (swiglu) {
-    if (BN == 32) return launch_bn<32, true>(map, a, grid, st);
-    if (BN == 64) return launch_bn<64, true>(map, a, grid, st);
-    return launch_bn<128, true>(map, a, grid, st);
+    if (BN == 32) return launch_bn<32, true>(map, wm, a, grid, st);
+    if (BN == 64) return launch_bn<64, true>(map, wm, a, grid, st);
+    return launch_bn<128, true>(map, wm, a, grid, st);
   }
-  if (BN == 32) return launch_bn<32, false>(map, a, grid, st);
-  if (BN == 64) return launch_bn<64, false>(map, a, grid, st);
-  return launch_bn<128, false>(map, a, grid, st);
+  if (BN == 32) return launch_bn<32, false>(map, wm, a, grid, st);
+  if (BN == 64) return launch_bn<64, false>(map, wm, a, grid, st);
+  return launch_bn<128, false>(map, wm, a, grid, st);
 }
 
 // one-time host state (error flag, driver entry point): call before any stream capture
