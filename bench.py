@@ -325,12 +325,21 @@ def gemv_roofline(model, M=1):
         x = torch.randn(M, K, device=model.device).to(torch.bfloat16)
         N = ws[0][0].shape[0]
         wbytes = sum(t.numel() * t.element_size() for t in ws[0])
+        # > 8 rows: the tensor-core matmul split over every SM, as the model step runs it
+        sk = ops.sk_workspace(M, K, 2 * N, model.device) if M > 8 else None
         if name == "gate_up_swiglu":
-            fns = [lambda w=w: ops.gate_up_swiglu(x, *w) for w in ws]
+            if sk is None:
+                fns = [lambda w=w: ops.gate_up_swiglu(x, *w) for w in ws]
+            else:
+                fns = [lambda w=w: ops.rmsnorm_gate_up_swiglu(x, None, 0.0, *w, workspace=sk) for w in ws]
             nbytes = wbytes + M * K * 2 + M * N * 2
         else:
             f32 = name == "lm_head"
-            fns = [lambda w=w, f=f32: ops.quantized_matmul(x, *w, out_f32=f) for w in ws]
+            if sk is None:
+                fns = [lambda w=w, f=f32: ops.quantized_matmul(x, *w, out_f32=f) for w in ws]
+            else:
+                fns = [lambda w=w, f=f32: ops.rmsnorm_quantized_matmul(x, None, 0.0, *w, out_f32=f, workspace=sk)
+                       for w in ws]
             nbytes = wbytes + M * K * 2 + M * N * (4 if f32 else 2)
         us = graph_time(fns) / len(fns) * 1e6
         rows.append({"shape": name, "launches_per_step": count, "bytes": int(nbytes), "us": round(us, 2),
@@ -363,12 +372,18 @@ def kernel_case(opt):
         reps = 2 if case == "lm_head" else 8  # > 126 MB of distinct weights in flight
         ws = [mk(N, K) + (mk(N, K) if case == "gate_up_swiglu" else ()) for _ in range(reps)]
         x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        sk = ops.sk_workspace(M, K, 2 * N, dev) if M > 8 else None  # stream-K tensor-core path
         for it in range(3):
             for w in ws:
                 if case == "gate_up_swiglu":
-                    ops.gate_up_swiglu(x, *w)
-                else:
+                    if sk is None:
+                        ops.gate_up_swiglu(x, *w)
+                    else:
+                        ops.rmsnorm_gate_up_swiglu(x, None, 0.0, *w, workspace=sk)
+                elif sk is None:
                     ops.quantized_matmul(x, *w, out_f32=case == "lm_head")
+                else:
+                    ops.rmsnorm_quantized_matmul(x, None, 0.0, *w, out_f32=case == "lm_head", workspace=sk)
     elif case == "attention":
         B, Hq, Hkv, D, L = 1, a.num_attention_heads, a.num_key_value_heads, a.head_dim, opt.ctx
         P = L // 16 + 1

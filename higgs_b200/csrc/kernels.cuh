@@ -57,7 +57,7 @@ struct QLinArgs {
   long long moe_ew, moe_es;
   // expert parallelism: only experts [moe_e_lo, moe_e_lo + moe_e_n) live here (0 = all)
   int moe_e_lo, moe_e_n;
-  // scratch for the tensor-core path's split-K partials (M >= 16; may be null)
+  // scratch for the tensor-core path's stream-K partials (M >= 17; may be null)
   void* tc_ws;
   size_t tc_ws_bytes;
   // weights of a later launch to pull into L2 (the next GEMV of the step)
@@ -98,7 +98,7 @@ cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st);
 bool l2_prefetch_next();
 bool l2_prefetch_self();
 bool qgemv_ring_can_fuse_norm(int M, int K);
-// M >= 16: the tcgen05 matrix path (qgemm_tc.cu); launch_qgemv_ring routes there itself.
+// M >= 17: the tcgen05 matrix path (qgemm_tc.cu); launch_qgemv_ring routes there itself.
 bool qgemm_tc_supported(const QLinArgs& a);
 size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu);
 cudaError_t launch_qgemm_tc(const QLinArgs& a, int epi, void* ws, size_t ws_bytes, cudaStream_t st);

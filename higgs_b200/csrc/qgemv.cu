@@ -633,7 +633,7 @@ cudaError_t launch_epi(const QLinArgs& a, cudaStream_t st) {
 // M rows per pass: <= 32 (a fused norm needs M <= 8 and the x tile in shared memory).
 bool qgemv_ring_can_fuse_norm(int M, int K);
 static bool g_gemm_tc = true;  // route M >= g_gemm_tc_rows to the tensor-core path
-static int g_gemm_tc_rows = 16;
+static int g_gemm_tc_rows = 17;
 void set_gemm_tc(bool on) { g_gemm_tc = on; }
 void set_gemm_tc_rows(int m) { g_gemm_tc_rows = m < 1 ? 1 : m; }
 

@@ -22,6 +22,9 @@
 // The first two units of a warp's range are fetched before griddepcontrol.wait,
 // and dependents are released right after it, so consecutive kernels overlap
 // their weight streams with the previous kernel's tail.
+#include <algorithm>
+#include <string>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -335,8 +338,25 @@ cudaError_t launch_qgemv_sk(SkArgs a, void* workspace, cudaStream_t st) {
 using namespace higgs;
 
 extern "C" size_t higgs_qlinear_sk_workspace_size(int M, int K, int N_rows) {
-  if (M <= 0 || M > 8 || K <= 0 || K % 256 || N_rows <= 0 || N_rows % 16) return 0;
+  if (M <= 0 || K <= 0 || K % 256 || N_rows <= 0 || N_rows % 16) return 0;
+  if (M > 8)  // the tensor-core path: the same counter region, then its partial tiles
+    return std::max({kSkCounterBytes, qgemm_tc_workspace(M, K, N_rows, false),
+                     qgemm_tc_workspace(M, K, N_rows / 2, true)});
   return qgemv_sk_workspace(M, K, N_rows / 16);
+}
+
+// M > 8 rows without a fused norm: the ring GEMV (< 17 rows) or the tensor-core
+// matmul, which balances its weight stream over every SM with this workspace.
+static int wide_qlinear(const char* fn, QLinArgs a, int epi, void* workspace, size_t workspace_bytes,
+                        void* stream) {
+  const size_t need = higgs_qlinear_sk_workspace_size(a.M, a.K, epi == EPI_SWIGLU ? 2 * a.N : a.N);
+  if (workspace_bytes < need)
+    return fail(HIGGS_ERR_WORKSPACE,
+                std::string(fn) + ": workspace too small (need " + std::to_string(need) + " bytes)");
+  a.tc_ws = workspace;
+  a.tc_ws_bytes = workspace_bytes;
+  HG_CUDA(launch_qgemv_ring(a, epi, (cudaStream_t)stream));
+  return HIGGS_OK;
 }
 
 extern "C" int higgs_rmsnorm_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K,
@@ -346,8 +366,23 @@ extern "C" int higgs_rmsnorm_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M,
                                            size_t workspace_bytes, void* stream) {
   HG_CHECK_ARG(ctx && x && w && scales && biases && workspace, "higgs_rmsnorm_qlinear_w4g64: null argument");
   HG_CHECK_ARG(y || y_f32, "higgs_rmsnorm_qlinear_w4g64: need y or y_f32");
-  HG_CHECK_ARG(M >= 1 && M <= 8, "higgs_rmsnorm_qlinear_w4g64: M must be in [1, 8]");
+  HG_CHECK_ARG(M >= 1 && (M <= 8 || !norm_w), "higgs_rmsnorm_qlinear_w4g64: fused norm needs M in [1, 8]");
   HG_CHECK_ARG(K % 256 == 0 && N % 16 == 0 && N > 0, "higgs_rmsnorm_qlinear_w4g64: need K % 256 == 0, N % 16 == 0");
+  HG_CHECK_ARG(!residual || y, "higgs_rmsnorm_qlinear_w4g64: residual needs a bf16 y");
+  if (M > 8) {
+    QLinArgs q = {};
+    q.x = (const uint16_t*)x;
+    q.M = M;
+    q.K = K;
+    q.N = N;
+    q.w = w;
+    q.s = (const uint16_t*)scales;
+    q.b = (const uint16_t*)biases;
+    q.y = (uint16_t*)y;
+    q.y_f32 = y_f32;
+    q.residual = (const uint16_t*)residual;
+    return wide_qlinear("higgs_rmsnorm_qlinear_w4g64", q, EPI_STORE, workspace, workspace_bytes, stream);
+  }
   HG_CHECK_ARG(!norm_w || K <= 8192, "higgs_rmsnorm_qlinear_w4g64: fused norm needs K <= 8192");
   HG_CHECK_ARG(N / 16 <= kSkMaxTiles, "higgs_rmsnorm_qlinear_w4g64: N must be <= 262144");
   const size_t need = qgemv_sk_workspace(M, K, N / 16);
@@ -382,8 +417,23 @@ extern "C" int higgs_rmsnorm_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M
                                             size_t workspace_bytes, void* stream) {
   HG_CHECK_ARG(ctx && x && w_gate && s_gate && b_gate && w_up && s_up && b_up && y && workspace,
                "higgs_rmsnorm_gate_up_swiglu: null argument");
-  HG_CHECK_ARG(M >= 1 && M <= 8, "higgs_rmsnorm_gate_up_swiglu: M must be in [1, 8]");
+  HG_CHECK_ARG(M >= 1 && (M <= 8 || !norm_w), "higgs_rmsnorm_gate_up_swiglu: fused norm needs M in [1, 8]");
   HG_CHECK_ARG(K % 256 == 0 && N % 16 == 0 && N > 0, "higgs_rmsnorm_gate_up_swiglu: need K % 256 == 0, N % 16 == 0");
+  if (M > 8) {
+    QLinArgs q = {};
+    q.x = (const uint16_t*)x;
+    q.M = M;
+    q.K = K;
+    q.N = N;
+    q.w = w_gate;
+    q.s = (const uint16_t*)s_gate;
+    q.b = (const uint16_t*)b_gate;
+    q.w2 = w_up;
+    q.s2 = (const uint16_t*)s_up;
+    q.b2 = (const uint16_t*)b_up;
+    q.y = (uint16_t*)y;
+    return wide_qlinear("higgs_rmsnorm_gate_up_swiglu", q, EPI_SWIGLU, workspace, workspace_bytes, stream);
+  }
   HG_CHECK_ARG(!norm_w || K <= 8192, "higgs_rmsnorm_gate_up_swiglu: fused norm needs K <= 8192");
   HG_CHECK_ARG(2 * N / 16 <= kSkMaxTiles, "higgs_rmsnorm_gate_up_swiglu: N must be <= 131072");
   const size_t need = qgemv_sk_workspace(M, K, 2 * N / 16);

@@ -81,7 +81,10 @@ def sk_workspace(M: int, K: int, rows: int, device) -> torch.Tensor:
 
 def rmsnorm_quantized_matmul(h, norm_w, eps, w, scales, biases, *, residual=None,
                              out_f32: bool = False, workspace=None):
-    """nn::RmsNorm (norm_w, or none when norm_w is None) then quantized_matmul, for M <= 8."""
+    """nn::RmsNorm (norm_w, or none when norm_w is None) then quantized_matmul.
+
+    M <= 8 with or without the norm (stream-K GEMV); any M without it (from 17 rows the
+    tensor-core matmul, spread over every SM with the workspace)."""
     _chk(h, torch.bfloat16, "h")
     K = h.shape[-1]
     M = h.numel() // K
@@ -97,7 +100,8 @@ def rmsnorm_quantized_matmul(h, norm_w, eps, w, scales, biases, *, residual=None
 
 
 def rmsnorm_gate_up_swiglu(h, norm_w, eps, wg, sg, bg, wu, su, bu, workspace=None):
-    """nn::RmsNorm then swiglu(gate_proj, up_proj), for M <= 8."""
+    """nn::RmsNorm (or none when norm_w is None) then swiglu(gate_proj, up_proj); M <= 8
+    with the norm, any M without it."""
     _chk(h, torch.bfloat16, "h")
     K = h.shape[-1]
     M = h.numel() // K

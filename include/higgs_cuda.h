@@ -79,9 +79,9 @@ int higgs_version(void);
  * sizes depend on it.  "l2_prefetch" (bit mask, default 0): bit 0 makes every
  * GEMV of the decode step ask the TMA unit to pull the next GEMV's weights into
  * L2, bit 1 makes each GEMV CTA pull its own weight tiles (a hint; results are
- * unchanged).  "gemm_tc" (0/1, default 1): quantized linears over 16 or more
+ * unchanged).  "gemm_tc" (0/1, default 1): quantized linears over 17 or more
  * rows use the tcgen05 tensor-core kernel (weights dequantized to bf16 first,
- * MLX's qmm form) instead of the decode GEMV; "gemm_tc_rows" (default 16) moves
+ * MLX's qmm form) instead of the decode GEMV; "gemm_tc_rows" (default 17) moves
  * that threshold (fused-RMSNorm decode launches always stay on the GEMV).  "gemv_wk" (0, 1, 2, 4, 8; default
  * 0 = heuristic): ways each 16-row tile of the decode GEMV splits K over warps.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */

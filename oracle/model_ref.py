@@ -66,11 +66,11 @@ class RefModel:
 
     def lin(self, x, name, want_f32=False):
         """quantized_matmul in the GPU path's form: MLX's matrix form (weights dequantized
-        to bf16 first) for >= 16 rows when the output width is a multiple of 128, the exact
+        to bf16 first) for >= 17 rows when the output width is a multiple of 128, the exact
         vector form otherwise."""
         q, s, b = self.q(name)
         rows = x.size // x.shape[-1]
-        if rows >= 16 and q.shape[0] % 128 == 0 and x.shape[-1] % 256 == 0:
+        if rows >= 17 and q.shape[0] % 128 == 0 and x.shape[-1] % 256 == 0:
             return orc.qmatmul_dq(x, q, s, b, want_f32=want_f32)
         return orc.qmatmul(x, q, s, b, want_f32=want_f32)
 

@@ -95,7 +95,7 @@ def test_gate_up_swiglu(M):
     qg, sg, bg = qweights(rng, N, K)
     qu, su, bu = qweights(rng, N, K)
     x = orc.f32_to_bf16(rng.normal(size=(M, K)))
-    qm = orc.qmatmul_dq if M >= 16 else orc.qmatmul  # the GPU's matrix form from 16 rows
+    qm = orc.qmatmul_dq if M >= 17 else orc.qmatmul  # the GPU's matrix form from 17 rows
     ref = orc.silu_mul(qm(x, qg, sg, bg), qm(x, qu, su, bu))
     got = to_np_bf(ops().gate_up_swiglu(bf(x), t(qg.view(np.int32)), bf(sg), bf(bg),
                                         t(qu.view(np.int32)), bf(su), bf(bu)))
@@ -546,21 +546,31 @@ def test_fused_attention_equals_unfused(B, Lq, Hq, Hkv, D, qknorm, lens):
     np.testing.assert_allclose(got.float().cpu().numpy(), orc.bf16_to_f32(ref_o), atol=1e-2, rtol=1e-2)
 
 
-# ---- a1 matrix form: tcgen05 path for M >= 16 ---------------------------------------------------
+# ---- a1 matrix form: tcgen05 path for M >= 17 ---------------------------------------------------
 
-@pytest.mark.parametrize("M,K,N", [(16, 256, 128), (20, 4096, 1024), (32, 4096, 4096), (33, 2048, 256),
-                                   (64, 12288, 512), (100, 1024, 384), (300, 512, 256)])
-def test_qgemm_tc_vs_oracle(M, K, N):
-    """M >= 16 rows run on the tensor cores with weights dequantized to bf16 (MLX's qmm form)."""
+def _tc_matmul(path, x, q, s, b, **kw):
+    """quantized_matmul through one CTA per tile ("tiles") or the stream-K split over every
+    SM with a workspace ("streamk")."""
+    o = ops()
+    if path == "tiles":
+        return o.quantized_matmul(x, q, s, b, **kw)
+    return o.rmsnorm_quantized_matmul(x, None, 0.0, q, s, b, **kw)
+
+
+@pytest.mark.parametrize("path", ["tiles", "streamk"])
+@pytest.mark.parametrize("M,K,N", [(17, 256, 128), (20, 4096, 1024), (32, 4096, 4096), (33, 2048, 256),
+                                   (64, 12288, 512), (100, 1024, 384), (300, 512, 256), (40, 768, 6144)])
+def test_qgemm_tc_vs_oracle(M, K, N, path):
+    """M >= 17 rows run on the tensor cores with weights dequantized to bf16 (MLX's qmm form)."""
     rng = np.random.default_rng(M * 7 + K + N)
     q, s, b = qweights(rng, N, K)
     x = orc.f32_to_bf16(rng.normal(0, 1, size=(M, K)))
     yb_ref, yf_ref = orc.qmatmul_dq(x, q, s, b, want_f32=True)
-    o = ops()
-    yf = o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b), out_f32=True).cpu().numpy()
+    qt, st_, bt_ = t(q.view(np.int32)), bf(s), bf(b)
+    yf = _tc_matmul(path, bf(x), qt, st_, bt_, out_f32=True).cpu().numpy()
     scale = np.abs(yf_ref).max()
     np.testing.assert_allclose(yf, yf_ref, rtol=1e-3, atol=1e-4 * scale + 1e-6)
-    yb = to_np_bf(o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b)))
+    yb = to_np_bf(_tc_matmul(path, bf(x), qt, st_, bt_))
     # outputs that are small next to the row scale come out of cancellation, where the f32
     # summation order (tensor core vs sequential) moves many of their low bits
     big = np.abs(yf_ref) >= 1e-2 * scale
@@ -569,24 +579,55 @@ def test_qgemm_tc_vs_oracle(M, K, N):
                   <= 2e-3 * scale + np.abs(yf_ref) * 2.0 ** -7)
     # residual epilogue: one ulp of y may survive the add, bounded by the operands' magnitude
     res = orc.f32_to_bf16(rng.normal(0, 1, size=(M, N)))
-    yr = to_np_bf(o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b), residual=bf(res)))
+    yr = to_np_bf(_tc_matmul(path, bf(x), qt, st_, bt_, residual=bf(res)))
     ref_r = orc.f32_to_bf16(orc.bf16_to_f32(yb_ref) + orc.bf16_to_f32(res))
     mag = np.maximum(np.abs(orc.bf16_to_f32(yb_ref)), np.abs(orc.bf16_to_f32(res)))
     assert np.all(np.abs(orc.bf16_to_f32(yr) - orc.bf16_to_f32(ref_r)) <= mag * 2.0 ** -6 + 2e-3 * scale)
 
 
-@pytest.mark.parametrize("M,K,N", [(16, 1024, 256), (48, 4096, 1536), (130, 512, 128)])
-def test_qgemm_tc_swiglu_vs_oracle(M, K, N):
+@pytest.mark.parametrize("path", ["tiles", "streamk"])
+@pytest.mark.parametrize("M,K,N", [(17, 1024, 256), (48, 4096, 1536), (130, 512, 128), (32, 4096, 3072)])
+def test_qgemm_tc_swiglu_vs_oracle(M, K, N, path):
     rng = np.random.default_rng(M + K + N)
     qg, sg, bg = qweights(rng, N, K)
     qu, su, bu = qweights(rng, N, K)
     x = orc.f32_to_bf16(rng.normal(0, 1, size=(M, K)))
     ref = orc.silu_mul(orc.qmatmul_dq(x, qg, sg, bg), orc.qmatmul_dq(x, qu, su, bu))
-    got = to_np_bf(ops().gate_up_swiglu(bf(x), t(qg.view(np.int32)), bf(sg), bf(bg),
-                                        t(qu.view(np.int32)), bf(su), bf(bu)))
+    args = (bf(x), t(qg.view(np.int32)), bf(sg), bf(bg), t(qu.view(np.int32)), bf(su), bf(bu))
+    if path == "tiles":
+        got = to_np_bf(ops().gate_up_swiglu(*args))
+    else:
+        got = to_np_bf(ops().rmsnorm_gate_up_swiglu(args[0], None, 0.0, *args[1:]))
     sa = np.abs(orc.bf16_to_f32(ref)).max()
     np.testing.assert_allclose(orc.bf16_to_f32(got), orc.bf16_to_f32(ref), atol=2e-3 * sa, rtol=2e-2)
     assert np.mean(bf_ulps(got, ref) <= 1) > 0.99
+
+
+def test_qgemm_tc_streamk_shared_workspace():
+    """One zeroed workspace serves matmuls of several shapes back to back (tile counters reset
+    themselves), and the split-tile sums are deterministic."""
+    import torch
+    o = ops()
+    rng = np.random.default_rng(5)
+    shapes = [(32, 4096, 6144), (17, 12288, 4096), (64, 4096, 1024), (24, 1024, 128)]
+    ws = o.sk_workspace(64, 12288, 2 * 6144, "cuda")
+    outs = []
+    for rep in range(2):
+        for M, K, N in shapes:
+            r2 = np.random.default_rng(M + K + N)
+            q, s, b = qweights(r2, N, K)
+            x = orc.f32_to_bf16(r2.normal(0, 1, size=(M, K)))
+            y = o.rmsnorm_quantized_matmul(bf(x), None, 0.0, t(q.view(np.int32)), bf(s), bf(b),
+                                           out_f32=True, workspace=ws)
+            if rep == 0:
+                outs.append(y)
+                yf_ref = orc.qmatmul_dq(x, q, s, b, want_f32=True)[1]
+                np.testing.assert_allclose(y.cpu().numpy(), yf_ref, rtol=1e-3,
+                                           atol=1e-4 * np.abs(yf_ref).max() + 1e-6)
+            else:
+                assert torch.equal(y, outs[shapes.index((M, K, N))])
+    torch.cuda.synchronize()
+    assert int(ws[:65536].count_nonzero()) == 0
 
 
 def test_qgemm_tc_no_timeouts():
