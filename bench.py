@@ -325,7 +325,7 @@ def gemv_roofline(model, M=1):
         x = torch.randn(M, K, device=model.device).to(torch.bfloat16)
         N = ws[0][0].shape[0]
         wbytes = sum(t.numel() * t.element_size() for t in ws[0])
-        # > 8 rows: the tensor-core matmul split over every SM, as the model step runs it
+        # > 8 rows: through the workspace entry (split-K tensor-core matmul), as the model step runs it
         sk = ops.sk_workspace(M, K, 2 * N, model.device) if M > 8 else None
         if name == "gate_up_swiglu":
             if sk is None:
@@ -372,7 +372,7 @@ def kernel_case(opt):
         reps = 2 if case == "lm_head" else 8  # > 126 MB of distinct weights in flight
         ws = [mk(N, K) + (mk(N, K) if case == "gate_up_swiglu" else ()) for _ in range(reps)]
         x = torch.randn(M, K, device=dev).to(torch.bfloat16)
-        sk = ops.sk_workspace(M, K, 2 * N, dev) if M > 8 else None  # stream-K tensor-core path
+        sk = ops.sk_workspace(M, K, 2 * N, dev) if M > 8 else None  # split-K tensor-core path
         for it in range(3):
             for w in ws:
                 if case == "gate_up_swiglu":

@@ -57,7 +57,7 @@ struct QLinArgs {
   long long moe_ew, moe_es;
   // expert parallelism: only experts [moe_e_lo, moe_e_lo + moe_e_n) live here (0 = all)
   int moe_e_lo, moe_e_n;
-  // scratch for the tensor-core path's stream-K partials (M >= 17; may be null)
+  // scratch for the tensor-core path's split-K partials (M >= 17; may be null)
   void* tc_ws;
   size_t tc_ws_bytes;
   // weights of a later launch to pull into L2 (the next GEMV of the step)

@@ -117,7 +117,7 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
     L.tp_part = take(T * c.hidden * 4);
     L.tp_keys = take(rows_lm * 8);
   }
-  {  // stream-K partials of the tensor-core path (a few MB; used from 17 rows by default)
+  {  // split-K partials of the tensor-core path (a few MB; used from 17 rows by default)
     const int H = c.hidden, Hd = c.heads * D, Nqkv = (c.heads + 2 * c.kv_heads) * D;
     size_t need = qgemm_tc_workspace((int)T, H, Nqkv, false);
     need = std::max(need, qgemm_tc_workspace((int)T, Hd, H, false));

@@ -7,34 +7,25 @@
 // w = bf16(s*q + b) with one rounding (a bf16x2 fused multiply-add of the exact
 // nibble value), then bf16 x bf16 -> f32 on the tensor cores.
 //
-// Work split (stream-K): the (tile, 64-wide k group) units of the whole matmul
-// -- a tile is 128 weight rows x BN tokens -- are cut into one contiguous range
-// per CTA, one CTA per SM, so every SM streams the same share of the weights
-// whatever the tile count.  A tile split between CTAs is finished by the last
-// of them, which adds the f32 partials in CTA order (the same bits whichever
-// CTA ends last).
-//
-// Per CTA (448 threads):
-//   * loader warp, lane 0: TMA streams the packed weight tile of each unit
-//     (128 rows x 32 bytes) into a deep shared-memory ring, starting before the
-//     grid dependency wait (weights never depend on the previous kernel);
-//     lane 1: TMA brings the x tile (BN tokens x 64 k, 128-byte swizzle) into
-//     its own ring, released by the MMA that read it;
-//   * 8 dequant warps: warp w owns TMEM lanes 32(w%4).. and k half w/4; each
-//     thread dequantizes 32 weights of its row (LOP3 / bf16x2 FMA / PRMT) and
-//     writes them with tcgen05.st straight into a TMEM A-operand stage, so the
-//     dequantized tile never passes through shared memory;
-//   * MMA warp: one lane issues tcgen05.mma (A from TMEM, x from shared memory,
-//     M=128, N=BN, K=16) x 4 per unit into one of two TMEM accumulators;
-//     tcgen05.commit releases the A stage, the x stage and, at the end of a
-//     tile, the accumulator;
-//   * 4 epilogue warps read a finished accumulator (tcgen05.ld) while the MMA
-//     already fills the other one: bf16 / f32 store, residual add, SwiGLU (gate
-//     and up tiles share the CTA), or the f32 partial of a split tile.
+// One CTA computes a 128-row x BN-token tile over a slice of K (split-K when the
+// tile count alone cannot fill the GPU):
+//   * loader warp, lane 0: TMA streams the packed weight tile (128 rows x 32
+//     bytes per 64-wide k group) into an 8-stage shared-memory ring, starting
+//     before the grid dependency wait (weights never depend on the previous
+//     kernel); lane 1: TMA brings the x tile (BN tokens x 64 k, 128-byte swizzle)
+//     into the operand stage once the MMAs that read the stage completed;
+//   * 8 producer warps: thread (row, half) takes 16 packed bytes from the ring,
+//     dequantizes them with LOP3 / bf16x2 FMA / PRMT and stores the bf16 row slice
+//     in the 128-byte-swizzled K-major layout the MMA reads;
+//   * 1 MMA warp: one lane issues tcgen05.mma (M=128, N=BN, K=16) x 4 per group
+//     into a TMEM accumulator and tcgen05.commit releases the stage;
+//   * the producers then read TMEM (tcgen05.ld, 32 lanes per warp quarter) and
+//     run the epilogue: bf16 / f32 store, residual add, SwiGLU (gate and up tiles
+//     share the CTA), or a split-K partial reduced in split order by the last CTA.
 // TMEM is allocated only after griddepcontrol.wait, so a kernel launched early
 // never holds tensor memory that its predecessor still needs.  Every mbarrier
-// wait is bounded (about 2 s, or at once after another CTA failed): on timeout
-// the kernel records an error that higgs_tc_error reports and finishes.
+// wait is bounded (about 2 s): on timeout the kernel records an error that
+// higgs_tc_error reports, and finishes.
 #include <cuda.h>
 
 #include <algorithm>
@@ -50,56 +41,32 @@ namespace higgs {
 
 namespace {
 
-constexpr int kTcRows = 128;               // weight rows per tile (UMMA M)
-constexpr int kTcDequant = 256;            // 8 dequant warps
-constexpr int kMmaWarp = kTcDequant / 32;  // 8, 9: MMA issuers (even / odd units)
-constexpr int kIssuers = 2;
-constexpr int kLoadWarp = kMmaWarp + kIssuers;  // 10
-constexpr int kEpiWarp0 = kLoadWarp + 1;        // 11..14
-constexpr int kTcEpilogue = 128;
-constexpr int kTcThreads = kTcDequant + 32 * (kIssuers + 1) + kTcEpilogue;
+constexpr int kTcRows = 128;       // weight rows per tile (UMMA M)
+constexpr int kTcProducers = 256;      // 8 warps, thread = (row, half of 64 k)
+constexpr int kTcThreads = kTcProducers + 64;  // + MMA warp + weight-loader warp
+constexpr int kTileA = kTcRows * 128;  // 128 rows x 64 bf16 = 16 KB
 constexpr int kPkTile = kTcRows * 32;  // 128 rows x 64 packed nibbles = 4 KB
-constexpr int kRing = 8;               // scale / bias units prefetched per dequant thread
-constexpr int kSmemBudget = 200 * 1024;
-constexpr int kTmemCols = 512;
-constexpr int kTcMaxTiles = 16384;  // stream-K tile counters in the workspace
+constexpr int kPkStages = 8;           // packed weight stages in flight (TMA)
+constexpr int kRing = 8;               // scale / bias groups prefetched per producer thread
+constexpr int kTcMaxTiles = 16384;     // split-K tile counters in the workspace
 constexpr size_t kTcCounterBytes = kTcMaxTiles * sizeof(int);
-
-// Per-instantiation pipeline shape.
-template <int BN, bool SWIGLU>
-struct TcCfg {
-  static constexpr int NA = SWIGLU ? 2 : 1;  // weight tiles per unit (gate, up)
-  static constexpr int kTileB = BN * 128;    // x tile: BN tokens x 64 bf16
-  static constexpr int XS = (49152 / kTileB) > 8 ? 8 : (49152 / kTileB);
-  static constexpr int kPk = NA * kPkTile;  // packed bytes per unit
-  static constexpr int PS0 = (kSmemBudget - XS * kTileB) / kPk;
-  static constexpr int PS = PS0 > 32 ? 32 : PS0;  // packed units in flight
-  static constexpr int ACC = NA * BN;             // TMEM columns of one accumulator
-  // accumulators: one per issuer, double-buffered across tiles when TMEM allows
-  static constexpr int NB = 2 * kIssuers * ACC <= 256 ? 2 : 1;
-  static constexpr int A0 = kIssuers * NB * ACC < 128 ? 128 : kIssuers * NB * ACC;  // first A column
-  static constexpr int AS = (kTmemCols - A0) / (NA * 32);  // A-operand stages
-  static constexpr size_t kSmem = (size_t)XS * kTileB + (size_t)PS * kPk + 1024;
-  static_assert(A0 <= 256, "accumulators leave half of TMEM to the A stages");
-  static_assert(AS >= 4 && XS >= 3 && PS >= 16, "pipeline depth");
-  // more than half the SM's shared memory: one CTA per SM, so all of TMEM is ours
-  static_assert(kSmem <= 227 * 1024 && kSmem > 114 * 1024, "one CTA per SM");
-};
 
 struct TcArgs {
   int M, K, N;
-  int m_tiles, tiles;  // tile t = n_tile * m_tiles + m_tile
   int nseg;
   int seg_end[3];
+  const uint32_t* w[3];
   const uint16_t* s[3];
   const uint16_t* b[3];
-  const uint16_t* s2;  // up projection (SwiGLU)
+  const uint32_t* w2;  // up projection (SwiGLU)
+  const uint16_t* s2;
   const uint16_t* b2;
   uint16_t* y;
   float* y_f32;
   const uint16_t* residual;
-  float* part;    // f32 partials of split tiles: 2 slots per CTA
-  int* counters;  // one per tile, self-resetting
+  int splits, groups_per_split;
+  float* part;    // split-K partials
+  int* counters;  // one per (n tile, m tile), self-resetting
   int* err;
 };
 
@@ -117,12 +84,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, unsigned by
                "r"(bytes)
                : "memory");
 }
-// Bounded wait for the completion of phase `parity`.  False (and *err set) on
-// timeout; false at once when any CTA has already failed.
+// Bounded wait for the completion of phase `parity`; false (and *err set) on timeout.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* err) {
   const uint32_t a = smem_u32(bar);
   const long long t0 = clock64();
-  for (unsigned it = 1;; ++it) {
+  while (true) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
@@ -130,12 +96,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity, int* e
         : "r"(a), "r"(parity)
         : "memory");
     if (ok) return true;
-    if ((it & 1023) == 0) {
-      if (*reinterpret_cast<volatile int*>(err)) return false;
-      if (clock64() - t0 > (1ll << 32)) break;  // ~2 s at 2 GHz
-    }
+    if (clock64() - t0 > (1ll << 32)) break;  // ~2 s at 2 GHz
   }
-  atomicExch(err, 1);
+  if (err) atomicExch(err, 1);
   return false;
 }
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
@@ -145,6 +108,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_alloc(uint32_t* dst, int cols) {
@@ -157,20 +121,19 @@ __device__ __forceinline__ void tc_relinquish() {
 __device__ __forceinline__ void tc_dealloc(uint32_t taddr, int cols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
 }
-// D[tmem] (+)= A[tmem] . B[smem]^T
-__device__ __forceinline__ void tc_mma_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accum) {
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accum) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::
-          "r"(tmem_d),
-      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accum)
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\ttcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum)
       : "memory");
 }
 __device__ __forceinline__ void tc_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-// 16 consecutive 32-bit columns of this thread's TMEM lane
+// 16 consecutive f32 columns of this thread's TMEM lane
 __device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(
@@ -181,27 +144,8 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
-__device__ __forceinline__ void tc_st16(uint32_t taddr, const uint32_t* v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
-      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-      : "memory");
-}
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTcEpilogue) : "memory"); }
-// true on every epilogue thread iff v is true on all of them
-__device__ __forceinline__ bool epilogue_all(bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "n"(kTcEpilogue)
-      : "memory");
-  return r != 0;
-}
+__device__ __forceinline__ void producers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTcProducers) : "memory"); }
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -213,8 +157,8 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return d;
 }
 
-// 8 weights of one packed word -> 4 bf16 pairs in k order: w = bf16(s*q + b)
-__device__ __forceinline__ void dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2, uint32_t* out) {
+// 8 weights of one packed word -> 16 bytes of bf16 in k order: w = bf16(s*q + b)
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
   const __nv_bfloat162 c128 = __floats2bfloat162_rn(128.f, 128.f);
   uint32_t p[4] = {lop3_and_or(w, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 4, 0x000F000Fu, 0x43004300u),
                    lop3_and_or(w >> 8, 0x000F000Fu, 0x43004300u), lop3_and_or(w >> 12, 0x000F000Fu, 0x43004300u)};
@@ -227,175 +171,108 @@ __device__ __forceinline__ void dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfl
     q[i] = *reinterpret_cast<const uint32_t*>(&r);
   }
   // q[i] = (w_i, w_{i+4}) -> k order (0,1) (2,3) (4,5) (6,7)
-  out[0] = prmt(q[0], q[1], 0x5410);
-  out[1] = prmt(q[2], q[3], 0x5410);
-  out[2] = prmt(q[0], q[1], 0x7632);
-  out[3] = prmt(q[2], q[3], 0x7632);
+  return make_uint4(prmt(q[0], q[1], 0x5410), prmt(q[2], q[3], 0x5410), prmt(q[0], q[1], 0x7632),
+                    prmt(q[2], q[3], 0x7632));
 }
 
-// Weight tiles of a unit: the packed rows [row0, row0 + 128) of one tensor, 64 k.
+// Weight tiles of a CTA: the packed rows [row0, row0 + 128) of one tensor, 64 k per stage.
 struct WMaps {
   CUtensorMap w[3];  // q | k | v segments (or the single tensor)
   CUtensorMap up;    // SwiGLU up projection
 };
 
-// Tile t -> row segment, its first row inside the segment, and the tile origin.
-struct TilePos {
-  int seg, row0, n0, m0;
-};
-template <int BN>
-__device__ __forceinline__ TilePos tile_pos(const TcArgs& a, int t) {
-  TilePos p;
-  const int n_tile = t / a.m_tiles;
-  p.m0 = (t - n_tile * a.m_tiles) * BN;
-  p.n0 = n_tile * kTcRows;
-  p.seg = 0;
-  for (int i = 1; i < a.nseg; ++i)
-    if (p.n0 >= a.seg_end[i - 1]) p.seg = i;
-  p.row0 = p.n0 - (p.seg ? a.seg_end[p.seg - 1] : 0);
-  return p;
-}
-
-// Units [begin(c), begin(c + 1)) belong to CTA c; owner(u) is the CTA holding unit u.
-__device__ __forceinline__ long long unit_begin(long long U, int P, int c) { return (long long)c * U / P; }
-__device__ __forceinline__ int unit_owner(long long U, int P, long long u) {
-  return (int)(((u + 1) * P + U - 1) / U) - 1;
-}
-
-// 16 tokens of output row n from f32 accumulators (gate / up for SwiGLU).
-template <bool SWIGLU>
-__device__ __forceinline__ void tc_emit(const TcArgs& a, int n, int tok0, const float* g, const float* u) {
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int tok = tok0 + j;
-    if (tok >= a.M) break;
-    const size_t o = (size_t)tok * a.N + n;
-    if constexpr (SWIGLU) {
-      const float gv = round_bf(g[j]), uv = round_bf(u[j]);
-      a.y[o] = f2bf(gv / (1.0f + expf(-gv)) * uv);
-    } else {
-      const float v = g[j];
-      if (a.y_f32) a.y_f32[o] = v;
-      if (a.y) {
-        uint16_t rv = f2bf(v);
-        if (a.residual) rv = f2bf(bf2f(rv) + bf2f(a.residual[o]));
-        a.y[o] = rv;
-      }
-    }
-  }
-}
-
 template <int BN, bool SWIGLU>
 __global__ void __launch_bounds__(kTcThreads, 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ WMaps wm, TcArgs a) {
-  using C = TcCfg<BN, SWIGLU>;
-  constexpr int NA = C::NA, AS = C::AS, XS = C::XS, PS = C::PS, kPk = C::kPk, kTileB = C::kTileB;
-  constexpr int ACC = C::ACC, A0 = C::A0, NB = C::NB;
+  constexpr int NA = SWIGLU ? 2 : 1;
+  constexpr int AS = SWIGLU ? 3 : 4;  // bf16 operand stages
+  constexpr int kTileB = BN * 128;
+  constexpr int kStage = NA * kTileA + kTileB;
+  constexpr int kPk = NA * kPkTile;  // packed bytes per stage
+  constexpr int TCOLS = (NA * BN <= 32) ? 32 : (NA * BN <= 64) ? 64 : (NA * BN <= 128) ? 128 : 256;
+  constexpr int HC = BN / 2;  // accumulator columns read per producer warp
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* xsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* pk = xsm + XS * kTileB;  // packed ring (1024-aligned)
-  __shared__ __align__(8) uint64_t a_full[AS];
-  __shared__ __align__(8) uint64_t a_empty[AS];
-  __shared__ __align__(8) uint64_t x_full[XS];
-  __shared__ __align__(8) uint64_t x_empty[XS];
-  __shared__ __align__(8) uint64_t pk_full[PS];
-  __shared__ __align__(8) uint64_t pk_empty[PS];
-  __shared__ __align__(8) uint64_t acc_full[NB];
-  __shared__ __align__(8) uint64_t acc_empty[NB];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint8_t* pk = smem + AS * kStage;  // packed ring (1024-aligned: kStage is a multiple of 1024)
+  __shared__ __align__(8) uint64_t full_bar[AS];
+  __shared__ __align__(8) uint64_t empty_bar[AS];
+  __shared__ __align__(8) uint64_t pk_full[kPkStages];
+  __shared__ __align__(8) uint64_t pk_empty[kPkStages];
   __shared__ __align__(8) uint64_t done_bar;
   __shared__ uint32_t tmem_base;
   __shared__ int is_last;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, m_tile = blockIdx.y, split = blockIdx.z;
+  const int n0 = n_tile * kTcRows, m0 = m_tile * BN;
   const int G = a.K / 64;
-  const int P = gridDim.x;
-  const long long U = (long long)a.tiles * G;
-  const long long ub = unit_begin(U, P, blockIdx.x), ue = unit_begin(U, P, blockIdx.x + 1);
-  const int nst = (int)(ue - ub);
-  const int t_first = (int)(ub / G), g_first = (int)(ub - (long long)t_first * G);
+  const int g0 = split * a.groups_per_split;
+  const int g1 = min(G, g0 + a.groups_per_split);
+  const int nst = g1 - g0;
+
+  int seg = 0;
+  for (int i = 1; i < a.nseg; ++i)
+    if (n0 >= a.seg_end[i - 1]) seg = i;
+  const int row0 = n0 - (seg ? a.seg_end[seg - 1] : 0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < AS; ++i) {
-      mbar_init(&a_full[i], kTcDequant);
-      mbar_init(&a_empty[i], 1);
+      mbar_init(&full_bar[i], kTcProducers + 1);
+      mbar_init(&empty_bar[i], 1);
     }
-    for (int i = 0; i < XS; ++i) {
-      mbar_init(&x_full[i], 1);
-      mbar_init(&x_empty[i], 1);
-    }
-    for (int i = 0; i < PS; ++i) {
+    for (int i = 0; i < kPkStages; ++i) {
       mbar_init(&pk_full[i], 1);
-      mbar_init(&pk_empty[i], kTcDequant);
+      mbar_init(&pk_empty[i], kTcProducers);
     }
-    for (int i = 0; i < NB; ++i) {
-      mbar_init(&acc_full[i], kIssuers);
-      mbar_init(&acc_empty[i], kTcEpilogue);
-    }
-    mbar_init(&done_bar, kIssuers);
+    mbar_init(&done_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
 
-  // ---- before the grid dependency wait: weights only ----
-  // loader lane 0 cursor (unit -> tile / group) and the first PS packed units
-  int lg = g_first, lt = t_first;
-  TilePos lp = tile_pos<BN>(a, lt);
-  auto load_pk = [&](int i) {
-    const int slot = i % PS;
+  const int pid = threadIdx.x;
+  const int r = pid >> 1, hf = pid & 1;
+  const bool producer = pid < kTcProducers;
+  const int mma_warp = kTcProducers / 32, load_warp = mma_warp + 1;
+
+  // weights never depend on the previous kernel: the loader fills the whole packed
+  // ring before the grid dependency wait (no waits needed for the first pass)
+  const CUtensorMap* wmap = &wm.w[seg];
+  auto load_stage = [&](int i) {
+    const int slot = i % kPkStages;
     mbar_arrive_expect_tx(&pk_full[slot], kPk);
     uint8_t* dst = pk + slot * kPk;
-    tma_load_2d(dst, &wm.w[lp.seg], lg * 32, lp.row0, &pk_full[slot]);
-    if constexpr (SWIGLU) tma_load_2d(dst + kPkTile, &wm.up, lg * 32, lp.row0, &pk_full[slot]);
-    if (++lg == G) {
-      lg = 0;
-      lp = tile_pos<BN>(a, ++lt);
-    }
+    tma_load_2d(dst, wmap, (g0 + i) * 32, row0, &pk_full[slot]);
+    if constexpr (SWIGLU) tma_load_2d(dst + kPkTile, &wm.up, (g0 + i) * 32, row0, &pk_full[slot]);
   };
-  if (warp == kLoadWarp && lane == 0)
-    for (int i = 0; i < PS && i < nst; ++i) load_pk(i);
+  if (warp == load_warp && lane == 0)
+    for (int i = 0; i < kPkStages && i < nst; ++i) load_stage(i);
 
-  // dequant threads: row r of the tile, k half hf; scale / bias register ring
-  const int q4 = warp & 3, hf = (warp >> 2) & 1, r = q4 * 32 + lane;
-  const bool dequant = warp < kMmaWarp;
-  const bool issuer = warp >= kMmaWarp && warp < kMmaWarp + kIssuers;
-  // raw bf16 loads, first used kRing units later: combining them at fetch time would
-  // stall the thread on each load's latency
+  // scales / biases: a small register ring, also before the wait
+  const uint16_t* S = a.s[seg] + (size_t)(row0 + r) * G;
+  const uint16_t* Bb = a.b[seg] + (size_t)(row0 + r) * G;
+  const uint16_t* S2 = SWIGLU ? a.s2 + (size_t)(row0 + r) * G : nullptr;
+  const uint16_t* B2 = SWIGLU ? a.b2 + (size_t)(row0 + r) * G : nullptr;
+  // raw bf16 loads, first used kRing groups later (combining them at fetch time would
+  // stall the thread on each load)
   __nv_bfloat16 sr[kRing][NA], br[kRing][NA];
-  int ft = t_first, fg = g_first;
-  const uint16_t *S = nullptr, *Bb = nullptr, *S2 = nullptr, *B2 = nullptr;
-  auto sb_rows = [&]() {
-    const TilePos p = tile_pos<BN>(a, ft);
-    const size_t off = (size_t)(p.row0 + r) * G;
-    S = a.s[p.seg] + off;
-    Bb = a.b[p.seg] + off;
+  auto fetch_sb = [&](int i, int d) {
+    const int g = g0 + i;
+    sr[d][0] = reinterpret_cast<const __nv_bfloat16*>(S)[g];
+    br[d][0] = reinterpret_cast<const __nv_bfloat16*>(Bb)[g];
     if constexpr (SWIGLU) {
-      S2 = a.s2 + (size_t)(p.n0 + r) * G;
-      B2 = a.b2 + (size_t)(p.n0 + r) * G;
+      sr[d][1] = reinterpret_cast<const __nv_bfloat16*>(S2)[g];
+      br[d][1] = reinterpret_cast<const __nv_bfloat16*>(B2)[g];
     }
   };
-  auto fetch_sb = [&](int d) {  // the cursor's unit into ring slot d, then advance
-    sr[d][0] = reinterpret_cast<const __nv_bfloat16*>(S)[fg];
-    br[d][0] = reinterpret_cast<const __nv_bfloat16*>(Bb)[fg];
-    if constexpr (SWIGLU) {
-      sr[d][1] = reinterpret_cast<const __nv_bfloat16*>(S2)[fg];
-      br[d][1] = reinterpret_cast<const __nv_bfloat16*>(B2)[fg];
-    }
-    if (++fg == G) {
-      fg = 0;
-      ++ft;
-      if (ft < a.tiles) sb_rows();
-    }
-  };
-  if (dequant) {
-    sb_rows();
+  if (producer) {
 #pragma unroll
     for (int d = 0; d < kRing; ++d)
-      if (d < nst) fetch_sb(d);
+      if (d < nst) fetch_sb(d, d);
   }
 
-  pdl_wait();  // x, the residual and the workspace come from earlier kernels
-  if (warp == kMmaWarp) {
-    tc_alloc(&tmem_base, kTmemCols);
+  pdl_wait();  // x and the residual come from the previous kernel
+  if (warp == mma_warp) {
+    tc_alloc(&tmem_base, TCOLS);
     tc_relinquish();
   }
   tc_fence_before();
@@ -404,207 +281,153 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tbase = tmem_base;
   pdl_launch();
 
-  if (warp == kLoadWarp) {
+  if (warp == load_warp) {
+    // ---------------- loaders: lane 0 refills each packed weight slot once the producers
+    // drained it; lane 1 brings each x tile once the MMAs of that stage slot are done
     if (lane == 0) {
-      // ---- packed weights: refill each slot once the dequant warps drained it ----
-      for (int i = PS; i < nst; ++i) {
-        if (!mbar_wait(&pk_empty[i % PS], ((i / PS) - 1) & 1, a.err)) break;
-        load_pk(i);
+      for (int i = kPkStages; i < nst; ++i) {
+        mbar_wait(&pk_empty[i % kPkStages], ((i / kPkStages) - 1) & 1, a.err);
+        load_stage(i);
       }
-      for (int p = 0; p < PS && p < nst; ++p)  // own copies in flight (no-op unless a wait failed)
-        mbar_wait(&pk_full[p], ((nst - 1 - p) / PS) & 1, a.err);
     } else if (lane == 1) {
-      // ---- x tiles: refill each slot once the MMAs that read it completed ----
-      int g = g_first, t = t_first;
-      int m0 = tile_pos<BN>(a, t).m0;
       for (int i = 0; i < nst; ++i) {
-        const int xs = i % XS;
-        if (i >= XS && !mbar_wait(&x_empty[xs], ((i / XS) - 1) & 1, a.err)) break;
-        mbar_arrive_expect_tx(&x_full[xs], kTileB);
-        tma_load_2d(xsm + xs * kTileB, &xmap, g * 64, m0, &x_full[xs]);
-        if (++g == G) {
-          g = 0;
-          m0 = tile_pos<BN>(a, ++t).m0;
-        }
+        const int slot = i % AS;
+        if (i >= AS) mbar_wait(&empty_bar[slot], ((i / AS) - 1) & 1, a.err);
+        mbar_arrive_expect_tx(&full_bar[slot], kTileB);
+        tma_load_2d(smem + slot * kStage + NA * kTileA, &xmap, (g0 + i) * 64, m0, &full_bar[slot]);
       }
-      for (int p = 0; p < XS && p < nst; ++p) mbar_wait(&x_full[p], ((nst - 1 - p) / XS) & 1, a.err);
     }
     __syncwarp();
-  } else if (issuer) {
-    // ---- MMA: issuer w takes the units of parity w into its own accumulator, so one
-    // issuer's barrier waits and commits overlap the other's MMAs; commits release the
-    // A / x stages and, at the end of a tile, the issuer's share of the accumulator ----
+  } else if (warp == mma_warp) {
+    // ---------------- MMA warp: one elected lane issues, commits release the stage ----------------
     if (lane == 0) {
-      const int w = warp - kMmaWarp;
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                              ((uint32_t)(kTcRows >> 4) << 24);
-      int g = g_first, s = 0;
-      bool ok = true, started = false;
-      for (int i = 0; i < nst && ok; ++i) {
-        const int b = NB == 2 ? (s & 1) : 0;
-        const bool last = i == nst - 1 || g == G - 1;
-        // before touching (or signalling) accumulator b again, its previous tile must be read
-        const bool need_empty = !started && s >= NB && ((i & 1) == w || last);
-        if (need_empty) ok = mbar_wait(&acc_empty[b], ((s / NB) - 1) & 1, a.err);
-        if (ok && (i & 1) == w) {
-          const int slot = i % AS, xs = i % XS;
-          ok = mbar_wait(&a_full[slot], (i / AS) & 1, a.err);
-          ok = ok && mbar_wait(&x_full[xs], (i / XS) & 1, a.err);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t sbx = smem_u32(xsm + xs * kTileB);
-          const uint32_t d = tbase + (w * NB + b) * ACC;
+      for (int i = 0; i < nst; ++i) {
+        const int slot = i % AS;
+        mbar_wait(&full_bar[slot], (i / AS) & 1, a.err);
+        tc_fence_after();
+        uint8_t* st = smem + slot * kStage;
+        const uint32_t sbx = smem_u32(st + NA * kTileA);
 #pragma unroll
-          for (int t = 0; t < NA; ++t)
+        for (int t = 0; t < NA; ++t) {
+          const uint32_t sa = smem_u32(st + t * kTileA);
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              tc_mma_ts(d + t * BN, tbase + A0 + slot * (NA * 32) + t * 32 + kk * 8, sw128_desc(sbx + kk * 32),
-                        idesc, (started || kk > 0) ? 1u : 0u);
-          tc_commit(&a_empty[slot]);
-          tc_commit(&x_empty[xs]);
-          started = true;
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma(tbase + t * BN, sw128_desc(sa + kk * 32), sw128_desc(sbx + kk * 32), idesc,
+                   (i > 0 || kk > 0) ? 1u : 0u);
         }
-        if (ok && last) {  // this issuer's share of the tile is complete (or empty)
-          if (started)
-            tc_commit(&acc_full[b]);
-          else
-            mbar_arrive(&acc_full[b]);
-          started = false;
-          ++s;
-        }
-        if (++g == G) g = 0;
+        tc_commit(&empty_bar[slot]);
       }
       tc_commit(&done_bar);
     }
     __syncwarp();
-  } else if (dequant) {
-    // ---- dequant: packed smem -> bf16 pairs -> TMEM A stage ----
-    const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16) + A0 + hf * 16;
-    bool ok = true;
-    for (int i0 = 0; i0 < nst && ok; i0 += kRing) {
+  } else if (producer) {
+    // ---------------- producers: packed smem -> bf16 swizzled A tiles ----------------
+    for (int i0 = 0; i0 < nst; i0 += kRing) {
 #pragma unroll
       for (int d = 0; d < kRing; ++d) {
         const int i = i0 + d;
         if (i >= nst) break;
-        const int ps = i % PS, slot = i % AS;
-        // warp-uniform outcome: the tcgen05 st / wait below need the whole warp
-        if (!(ok = __all_sync(0xffffffffu, mbar_wait(&pk_full[ps], (i / PS) & 1, a.err)))) break;
+        const int ps = i % kPkStages, slot = i % AS;
+        mbar_wait(&pk_full[ps], (i / kPkStages) & 1, a.err);
         uint4 wv[NA];
 #pragma unroll
         for (int t = 0; t < NA; ++t)
           wv[t] = *reinterpret_cast<const uint4*>(pk + ps * kPk + t * kPkTile + r * 32 + hf * 16);
-        if (i >= AS && !(ok = __all_sync(0xffffffffu, mbar_wait(&a_empty[slot], ((i / AS) - 1) & 1, a.err)))) break;
-        tc_fence_after();
+        if (i >= AS) mbar_wait(&empty_bar[slot], ((i / AS) - 1) & 1, a.err);
+        uint8_t* st = smem + slot * kStage;
 #pragma unroll
         for (int t = 0; t < NA; ++t) {
           const __nv_bfloat162 s2 = __bfloat162bfloat162(sr[d][t]);
           const __nv_bfloat162 b2 = __bfloat162bfloat162(br[d][t]);
           const uint32_t* w = &wv[t].x;
-          uint32_t v[16];
+          uint8_t* rowp = st + t * kTileA + r * 128;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) dequant8(w[j], s2, b2, v + 4 * j);
-          tc_st16(tl + slot * (NA * 32) + t * 32, v);
+          for (int j = 0; j < 4; ++j) {
+            const int c = hf * 4 + j;  // 16-byte chunk of the 128-byte row
+            *reinterpret_cast<uint4*>(rowp + ((c ^ (r & 7)) << 4)) = dequant8(w[j], s2, b2);
+          }
         }
         // release the packed slot only once its words have been consumed: the refill is an
         // async-proxy (TMA) write, which the barrier does not order behind a load in flight
         mbar_arrive(&pk_empty[ps]);
-        tc_wait_st();
-        tc_fence_before();
-        mbar_arrive(&a_full[slot]);
-        if (i + kRing < nst) fetch_sb(d);
+        fence_proxy_async();
+        mbar_arrive(&full_bar[slot]);
+        if (i + kRing < nst) fetch_sb(i + kRing, d);
       }
     }
-  } else {
-    // ---- epilogue: one finished tile at a time, TMEM lanes 32(warp % 4).. ----
-    const int ep = threadIdx.x - kEpiWarp0 * 32;
-    const uint32_t tl = tbase + ((uint32_t)(q4 * 32) << 16);
-    int s = 0;
-    // the tile's columns c0..c0+15 of gate (and up): the issuers' accumulators added
-    float gv[16], uv[16];
-    auto read_acc = [&](uint32_t tacc0, bool both, int c0) {
-      float g2[16], u2[16];
-      tc_ld16(tacc0 + c0, gv);
-      if constexpr (SWIGLU) tc_ld16(tacc0 + BN + c0, uv);
-      if (both) {
-        tc_ld16(tacc0 + NB * ACC + c0, g2);
-        if constexpr (SWIGLU) tc_ld16(tacc0 + NB * ACC + BN + c0, u2);
-      }
-      tc_wait_ld();
-      if (both) {
+
+    // ---------------- epilogue ----------------
+    mbar_wait(&done_bar, 0, a.err);
+    tc_fence_after();
+    const int sub = warp & 3, chalf = warp >> 2;
+    const int row = sub * 32 + lane;
+    float acc[NA][HC];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          gv[j] += g2[j];
-          if constexpr (SWIGLU) uv[j] += u2[j];
-        }
-      }
-    };
-    for (int t = t_first; (long long)t * G < ue; ++t, ++s) {
-      const int b = NB == 2 ? (s & 1) : 0;
-      if (!epilogue_all(mbar_wait(&acc_full[b], (s / NB) & 1, a.err))) break;
-      tc_fence_after();
-      const TilePos p = tile_pos<BN>(a, t);
-      const int n = p.n0 + r;
-      const long long tu = (long long)t * G;
-      const int c_lo = unit_owner(U, P, tu), c_hi = unit_owner(U, P, tu + G - 1);
-      // units of this tile held here: [i0, i1]; issuer w owns the ones of parity w
-      const int i0 = (int)std::max<long long>(0, tu - ub), i1 = (int)std::min<long long>(nst - 1, tu + G - 1 - ub);
-      const bool w0 = i1 > i0 || (i0 & 1) == 0, w1 = i1 > i0 || (i0 & 1) == 1;
-      const uint32_t tacc = tl + (w0 ? 0 : NB * ACC) + b * ACC;  // the first contributing issuer
-      const bool both = w0 && w1;
-      if (c_lo == c_hi) {  // the whole tile is ours
-        for (int c0 = 0; c0 < BN && p.m0 + c0 < a.M; c0 += 16) {
-          read_acc(tacc, both, c0);
-          tc_emit<SWIGLU>(a, n, p.m0 + c0, gv, uv);
-        }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[b]);
-        continue;
-      }
-      // split tile: publish this CTA's partial; the last contributor finishes it
-      constexpr size_t kPart = (size_t)NA * kTcRows * BN;
-      float* mine = a.part + ((size_t)blockIdx.x * 2 + (t == t_first ? 0 : 1)) * kPart;
-      for (int c0 = 0; c0 < BN && p.m0 + c0 < a.M; c0 += 16) {
-        read_acc(tacc, both, c0);
+    for (int t = 0; t < NA; ++t)
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          mine[(size_t)(c0 + j) * kTcRows + r] = gv[j];
-          if constexpr (SWIGLU) mine[(size_t)(BN + c0 + j) * kTcRows + r] = uv[j];
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&acc_empty[b]);
+      for (int c = 0; c < HC; c += 16)
+        tc_ld16(tbase + ((uint32_t)(sub * 32) << 16) + t * BN + chalf * HC + c, &acc[t][c]);
+    tc_wait_ld();
+    tc_fence_before();
+
+    const int tile = m_tile * gridDim.x + n_tile;
+    bool final_cta = true;
+    if (a.splits > 1) {
+      float* mine = a.part + ((size_t)tile * a.splits + split) * NA * kTcRows * BN;
+#pragma unroll
+      for (int t = 0; t < NA; ++t)
+#pragma unroll
+        for (int jj = 0; jj < HC; ++jj) mine[(t * BN + chalf * HC + jj) * kTcRows + row] = acc[t][jj];
       __threadfence();
-      epilogue_sync();
-      if (ep == 0) is_last = atomicAdd(a.counters + t, 1) == c_hi - c_lo;
-      epilogue_sync();
-      if (is_last) {
+      producers_sync();
+      if (pid == 0) is_last = atomicAdd(a.counters + tile, 1) == a.splits - 1;
+      producers_sync();
+      final_cta = is_last;
+      if (final_cta) {
         __threadfence();
-        for (int c0 = 0; c0 < BN && p.m0 + c0 < a.M; c0 += 16) {
-          float gv[16], uv[16];
+        // sum every split in split order (the same bits whichever CTA finishes last)
 #pragma unroll
-          for (int j = 0; j < 16; ++j) gv[j] = uv[j] = 0.f;
-          for (int c = c_lo; c <= c_hi; ++c) {  // CTA order
-            const int slot = unit_begin(U, P, c) >= tu ? 0 : 1;  // first tile of CTA c, or its last
-            const float* q = a.part + ((size_t)c * 2 + slot) * kPart;
+        for (int t = 0; t < NA; ++t)
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              gv[j] += __ldcg(q + (size_t)(c0 + j) * kTcRows + r);
-              if constexpr (SWIGLU) uv[j] += __ldcg(q + (size_t)(BN + c0 + j) * kTcRows + r);
-            }
-          }
-          tc_emit<SWIGLU>(a, n, p.m0 + c0, gv, uv);
+          for (int jj = 0; jj < HC; ++jj) acc[t][jj] = 0.f;
+        for (int sp = 0; sp < a.splits; ++sp) {
+          const float* p = a.part + ((size_t)tile * a.splits + sp) * NA * kTcRows * BN;
+#pragma unroll
+          for (int t = 0; t < NA; ++t)
+#pragma unroll
+            for (int jj = 0; jj < HC; ++jj) acc[t][jj] += __ldcg(p + (t * BN + chalf * HC + jj) * kTcRows + row);
         }
-        if (ep == 0) a.counters[t] = 0;
+        if (pid == 0) a.counters[tile] = 0;
       }
-      epilogue_sync();
+    }
+    if (final_cta) {
+      const int n = n0 + row;
+#pragma unroll
+      for (int jj = 0; jj < HC; ++jj) {
+        const int tok = m0 + chalf * HC + jj;
+        if (tok >= a.M) break;
+        const size_t o = (size_t)tok * a.N + n;
+        if constexpr (SWIGLU) {
+          const float gv = round_bf(acc[0][jj]), uv = round_bf(acc[1][jj]);
+          a.y[o] = f2bf(gv / (1.0f + expf(-gv)) * uv);
+        } else {
+          const float v = acc[0][jj];
+          if (a.y_f32) a.y_f32[o] = v;
+          if (a.y) {
+            uint16_t rv = f2bf(v);
+            if (a.residual) rv = f2bf(bf2f(rv) + bf2f(a.residual[o]));
+            a.y[o] = rv;
+          }
+        }
+      }
     }
   }
   __syncthreads();
-  if (warp == kMmaWarp) {
-    mbar_wait(&done_bar, 0, a.err);
-    __syncwarp();
+  if (warp == mma_warp) {
     tc_fence_after();
-    tc_dealloc(tbase, kTmemCols);
+    tc_dealloc(tbase, TCOLS);
   }
 }
 
@@ -691,6 +514,22 @@ int* tc_err_ptr() {
   return p;
 }
 
+template <int BN, bool SWIGLU>
+cudaError_t launch_bn(const CUtensorMap& map, const WMaps& wm, const TcArgs& a, dim3 grid, cudaStream_t st) {
+  constexpr int NA = SWIGLU ? 2 : 1;
+  constexpr int AS = SWIGLU ? 3 : 4;
+  constexpr size_t smem = (size_t)AS * (NA * kTileA + BN * 128) + (size_t)kPkStages * NA * kPkTile + 1024;
+  static_assert(smem <= 227 * 1024, "shared memory budget");
+  auto k = qgemm_tc_kernel<BN, SWIGLU>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  return launch_pdl(k, grid, dim3(kTcThreads), smem, st, map, wm, a);
+}
+
 int tc_sms() {
   static int n = 0;
   static std::once_flag once;
@@ -703,21 +542,16 @@ int tc_sms() {
   return n;
 }
 
-// tokens per tile: 32 / 64 / 128 (SwiGLU stops at 64: two double-buffered
-// accumulators of gate and up must leave TMEM room for the A stages)
-int tc_bn(int M, bool swiglu) { return M <= 32 ? 32 : (M <= 64 || swiglu ? 64 : 128); }
-
-template <int BN, bool SWIGLU>
-cudaError_t launch_bn(const CUtensorMap& map, const WMaps& wm, const TcArgs& a, int P, cudaStream_t st) {
-  constexpr size_t smem = TcCfg<BN, SWIGLU>::kSmem;
-  auto k = qgemm_tc_kernel<BN, SWIGLU>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
-  return launch_pdl(k, dim3(P), dim3(kTcThreads), smem, st, map, wm, a);
+// K splits: about two CTAs per SM in total, at least 4 groups of 64 per split
+int tc_splits(int M, int K, int N) {
+  const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
+  const int G = K / 64;
+  if (tiles == 0 || M < 1) return 1;  // no tile (N < 128): nothing to split
+  int splits = (int)((2 * tc_sms() + tiles - 1) / tiles);
+  if (splits > G / 4) splits = G / 4;
+  if (splits < 1 || tiles > (size_t)kTcMaxTiles) splits = 1;
+  return splits;
 }
 
 }  // namespace
@@ -732,75 +566,77 @@ bool qgemm_tc_supported(const QLinArgs& a) {
 }
 
 // A fixed counter region (one int per tile, up to kTcMaxTiles, zero between
-// calls), then two f32 partial tiles per CTA.  The fixed region lets matmuls of
-// every shape -- and the stream-K GEMV, whose counters sit in the same bytes --
-// share one workspace back to back on a stream.
+// calls), then the split-K partial tiles.  The fixed region lets matmuls of every
+// shape -- and the stream-K GEMV, whose counters sit in the same bytes -- share
+// one workspace back to back on a stream.
 size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu) {
-  (void)K;
-  (void)N;
-  const int BN = tc_bn(M, swiglu);
-  return kTcCounterBytes + (size_t)tc_sms() * 2 * (swiglu ? 2 : 1) * kTcRows * BN * sizeof(float);
+  const int splits = tc_splits(M, K, N);
+  if (splits == 1) return 0;
+  const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
+  return kTcCounterBytes + tiles * splits * (swiglu ? 2 : 1) * kTcRows * BN * sizeof(float);
 }
 
 cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!qgemm_tc_supported(q)) return cudaErrorInvalidValue;
   const bool swiglu = epi == EPI_SWIGLU;
-  const int BN = tc_bn(q.M, swiglu);
+  const int BN = q.M <= 32 ? 32 : (q.M <= 64 ? 64 : 128);
   CUtensorMap map;
   if (!x_tensor_map(q.x, q.M, q.K, BN, &map)) return cudaErrorInvalidValue;
   TcArgs a{};
   a.M = q.M;
   a.K = q.K;
   a.N = q.N;
-  a.m_tiles = (q.M + BN - 1) / BN;
-  a.tiles = (q.N / kTcRows) * a.m_tiles;
   a.nseg = q.nseg > 1 ? q.nseg : 1;
-  const uint32_t* w[3] = {q.w, nullptr, nullptr};
   if (q.nseg > 1) {
     for (int i = 0; i < 3; ++i) {
       a.seg_end[i] = q.seg_end[i];
-      w[i] = q.wseg[i];
+      a.w[i] = q.wseg[i];
       a.s[i] = q.sseg[i];
       a.b[i] = q.bseg[i];
     }
   } else {
+    a.w[0] = q.w;
     a.s[0] = q.s;
     a.b[0] = q.b;
   }
+  a.w2 = q.w2;
   a.s2 = q.s2;
   a.b2 = q.b2;
   a.y = q.y;
   a.y_f32 = q.y_f32;
   a.residual = q.residual;
   a.err = tc_err_ptr();
-  if (!a.err) return cudaErrorMemoryAllocation;
   WMaps wm;
   memset(&wm, 0, sizeof(wm));
   for (int i = 0; i < a.nseg; ++i) {
     const int rows = a.nseg > 1 ? a.seg_end[i] - (i ? a.seg_end[i - 1] : 0) : q.N;
-    if (!w_tensor_map(w[i], rows, q.K, &wm.w[i])) return cudaErrorInvalidValue;
+    if (!w_tensor_map(a.w[i], rows, q.K, &wm.w[i])) return cudaErrorInvalidValue;
   }
-  if (swiglu && !w_tensor_map(q.w2, q.N, q.K, &wm.up)) return cudaErrorInvalidValue;
-  // stream-K over every SM when the workspace allows it, else one CTA per tile
-  const long long U = (long long)a.tiles * (q.K / 64);
-  int P = a.tiles;
+  if (swiglu && !w_tensor_map(a.w2, q.N, q.K, &wm.up)) return cudaErrorInvalidValue;
+  const int n_tiles = q.N / kTcRows, m_tiles = (q.M + BN - 1) / BN;
+  const int G = q.K / 64;
+  int splits = 1;
   const size_t need = qgemm_tc_workspace(q.M, q.K, q.N, swiglu);
-  if (ws && ws_bytes >= need && ((uintptr_t)ws & 255) == 0 && a.tiles <= kTcMaxTiles) {
-    P = (int)std::min<long long>(tc_sms(), (U + 3) / 4);
+  if (need && ws && ws_bytes >= need && ((uintptr_t)ws & 255) == 0) {
+    splits = tc_splits(q.M, q.K, q.N);
     a.counters = static_cast<int*>(ws);
     a.part = reinterpret_cast<float*>(static_cast<char*>(ws) + kTcCounterBytes);
   }
-  if (P < 1) P = 1;
+  a.groups_per_split = (G + splits - 1) / splits;
+  a.splits = (G + a.groups_per_split - 1) / a.groups_per_split;  // every split holds >= 1 group
+  const dim3 grid(n_tiles, m_tiles, a.splits);
   if (swiglu) {
-    if (BN == 32) return launch_bn<32, true>(map, wm, a, P, st);
-    return launch_bn<64, true>(map, wm, a, P, st);
+    if (BN == 32) return launch_bn<32, true>(map, wm, a, grid, st);
+    if (BN == 64) return launch_bn<64, true>(map, wm, a, grid, st);
+    return launch_bn<128, true>(map, wm, a, grid, st);
   }
-  if (BN == 32) return launch_bn<32, false>(map, wm, a, P, st);
-  if (BN == 64) return launch_bn<64, false>(map, wm, a, P, st);
-  return launch_bn<128, false>(map, wm, a, P, st);
+  if (BN == 32) return launch_bn<32, false>(map, wm, a, grid, st);
+  if (BN == 64) return launch_bn<64, false>(map, wm, a, grid, st);
+  return launch_bn<128, false>(map, wm, a, grid, st);
 }
 
-// one-time host state (error flag, driver entry point, SM count): call before any stream capture
+// one-time host state (error flag, driver entry point): call before any stream capture
 void qgemm_tc_prepare() {
   tc_err_ptr();
   encode_fn();

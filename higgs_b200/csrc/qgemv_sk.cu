@@ -346,7 +346,7 @@ extern "C" size_t higgs_qlinear_sk_workspace_size(int M, int K, int N_rows) {
 }
 
 // M > 8 rows without a fused norm: the ring GEMV (< 17 rows) or the tensor-core
-// matmul, which balances its weight stream over every SM with this workspace.
+// matmul, which splits K over this workspace when its tiles alone cannot fill the GPU.
 static int wide_qlinear(const char* fn, QLinArgs a, int epi, void* workspace, size_t workspace_bytes,
                         void* stream) {
   const size_t need = higgs_qlinear_sk_workspace_size(a.M, a.K, epi == EPI_SWIGLU ? 2 * a.N : a.N);

@@ -84,7 +84,7 @@ def rmsnorm_quantized_matmul(h, norm_w, eps, w, scales, biases, *, residual=None
     """nn::RmsNorm (norm_w, or none when norm_w is None) then quantized_matmul.
 
     M <= 8 with or without the norm (stream-K GEMV); any M without it (from 17 rows the
-    tensor-core matmul, spread over every SM with the workspace)."""
+    tensor-core matmul, which splits K over the workspace when its tiles are few)."""
     _chk(h, torch.bfloat16, "h")
     K = h.shape[-1]
     M = h.numel() // K

@@ -128,18 +128,19 @@ int higgs_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, const uint3
                         const void* scales, const void* biases, int N, void* y, float* y_f32,
                         const void* residual, void* stream);
 
-/* Decode-batch variants (M <= 8) of the two linear ops above with the
- * preceding nn::RmsNorm fused in (transformer.rs:407-416: input_layernorm
- * before q/k/v, post_attention_layernorm before the MLP): when norm_w != NULL,
- * x is the residual stream h and the op consumes bf16(h * rsqrt(mean(h^2) +
- * eps) * norm_w) (K <= 8192); with norm_w == NULL they equal
- * higgs_qlinear_w4g64 / higgs_qlinear_gate_up_swiglu.  They balance the
- * weight stream over every SM (stream-K) and need a workspace of
- * higgs_qlinear_sk_workspace_size(M, K, rows) bytes (rows = N, or 2N for the
- * SwiGLU pair, at most 262144) whose first 65536 bytes (tile counters) must be
- * zero before the first call; each call leaves them zero, so one workspace of
- * the largest size serves every shape back to back on a stream.  Results are
- * deterministic (partial sums are combined in a fixed order). */
+/* Workspace variants of the two linear ops above.  For M <= 8 the preceding
+ * nn::RmsNorm can be fused in (transformer.rs:407-416: input_layernorm before
+ * q/k/v, post_attention_layernorm before the MLP): when norm_w != NULL, x is
+ * the residual stream h and the op consumes bf16(h * rsqrt(mean(h^2) + eps) *
+ * norm_w) (K <= 8192); with norm_w == NULL they equal higgs_qlinear_w4g64 /
+ * higgs_qlinear_gate_up_swiglu, for any M >= 1.  M <= 8 balances the weight
+ * stream over every SM (stream-K GEMV); from 17 rows the tensor-core matmul
+ * splits K over the workspace when its tiles alone cannot fill the GPU.  They
+ * need higgs_qlinear_sk_workspace_size(M, K, rows) bytes (rows = N, or 2N for
+ * the SwiGLU pair, at most 262144) whose first 65536 bytes (tile counters) must
+ * be zero before the first call; each call leaves them zero, so one workspace
+ * of the largest size serves every shape back to back on a stream.  Results
+ * are deterministic (partial sums are combined in a fixed order). */
 size_t higgs_qlinear_sk_workspace_size(int M, int K, int N_rows);
 int higgs_rmsnorm_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, const void* norm_w,
                                 float eps, const uint32_t* w, const void* scales,

@@ -70,3 +70,20 @@ def test_argument_validation_without_device(lib):
     # null context
     rc = lib.higgs_qlinear_w4g64(None, fake, 1, 256, fake, fake, fake, 16, fake, None, None, None)
     assert rc == -1
+
+
+def test_workspace_size_queries_without_device(lib):
+    """Workspace size queries are host arithmetic: they answer without a GPU, cover the
+    fixed 64 KB counter region, and return 0 for shapes the ops reject."""
+    f = lib.higgs_qlinear_sk_workspace_size
+    f.restype = ctypes.c_size_t
+    f.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    # decode GEMV (M <= 8) and the wide tensor-core path, including outputs below one
+    # 128-row tile and the SwiGLU reading of the row count
+    for M, K, rows in [(1, 4096, 4096), (8, 12288, 4096), (9, 1024, 128), (17, 256, 128),
+                       (17, 256, 64), (32, 4096, 6144), (64, 12288, 24576), (300, 512, 256)]:
+        assert f(M, K, rows) >= 65536, (M, K, rows)
+    # larger problems need at least as much
+    assert f(32, 4096, 12288) >= f(32, 4096, 6144)
+    for M, K, rows in [(0, 4096, 4096), (1, 100, 4096), (1, 4096, 10), (-1, 256, 16)]:
+        assert f(M, K, rows) == 0, (M, K, rows)

@@ -549,15 +549,15 @@ def test_fused_attention_equals_unfused(B, Lq, Hq, Hkv, D, qknorm, lens):
 # ---- a1 matrix form: tcgen05 path for M >= 17 ---------------------------------------------------
 
 def _tc_matmul(path, x, q, s, b, **kw):
-    """quantized_matmul through one CTA per tile ("tiles") or the stream-K split over every
-    SM with a workspace ("streamk")."""
+    """quantized_matmul without a workspace (one CTA per tile, "tiles") or through the
+    workspace entry, which splits K over the CTAs of small tile counts ("ws")."""
     o = ops()
     if path == "tiles":
         return o.quantized_matmul(x, q, s, b, **kw)
     return o.rmsnorm_quantized_matmul(x, None, 0.0, q, s, b, **kw)
 
 
-@pytest.mark.parametrize("path", ["tiles", "streamk"])
+@pytest.mark.parametrize("path", ["tiles", "ws"])
 @pytest.mark.parametrize("M,K,N", [(17, 256, 128), (20, 4096, 1024), (32, 4096, 4096), (33, 2048, 256),
                                    (64, 12288, 512), (100, 1024, 384), (300, 512, 256), (40, 768, 6144)])
 def test_qgemm_tc_vs_oracle(M, K, N, path):
@@ -585,7 +585,7 @@ def test_qgemm_tc_vs_oracle(M, K, N, path):
     assert np.all(np.abs(orc.bf16_to_f32(yr) - orc.bf16_to_f32(ref_r)) <= mag * 2.0 ** -6 + 2e-3 * scale)
 
 
-@pytest.mark.parametrize("path", ["tiles", "streamk"])
+@pytest.mark.parametrize("path", ["tiles", "ws"])
 @pytest.mark.parametrize("M,K,N", [(17, 1024, 256), (48, 4096, 1536), (130, 512, 128), (32, 4096, 3072)])
 def test_qgemm_tc_swiglu_vs_oracle(M, K, N, path):
     rng = np.random.default_rng(M + K + N)
@@ -603,7 +603,7 @@ def test_qgemm_tc_swiglu_vs_oracle(M, K, N, path):
     assert np.mean(bf_ulps(got, ref) <= 1) > 0.99
 
 
-def test_qgemm_tc_streamk_shared_workspace():
+def test_qgemm_tc_shared_workspace():
     """One zeroed workspace serves matmuls of several shapes back to back (tile counters reset
     themselves), and the split-tile sums are deterministic."""
     import torch
