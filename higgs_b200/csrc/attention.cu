@@ -1031,7 +1031,7 @@ constexpr int kFusedStages = 3;
 // issued before the grid dependency wait covers a whole split (tunable through
 // higgs_set_option("attn_min_pages", n), n >= 4; the workspace is sized for 4)
 static int g_fused_min_pages = 8;
-void attention_set_min_pages(int n) { g_fused_min_pages = n < 4 ? 4 : (n > 64 ? 64 : n); }
+void attention_set_min_pages(int n) { g_fused_min_pages = n < 4 ? 4 : (n > 4096 ? 4096 : n); }
 
 static size_t smem_fused(int D, int MT, int Lq) {
   const size_t q = (size_t)16 * MT * D * 2;

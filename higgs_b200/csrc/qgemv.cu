@@ -94,9 +94,11 @@ __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER>
+// ONE: a single token (M == 1); only its outputs are folded.
+template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER, bool ONE = false>
 __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
   static_assert(!GATHER || (XSMEM && NT8 == 1), "grouped experts use the staged-x path");
+  static_assert(!ONE || (XSMEM && NT8 == 1 && !GATHER && !F16), "single-token fold: staged bf16 x");
   constexpr int RT = 8 / WK;
   constexpr int ROT = (EPI == EPI_SWIGLU) ? RT / 2 : RT;
   constexpr int MT = 8 * NT8;  // token slots
@@ -421,13 +423,19 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
           mma_bf16_16816(acc, A[1][0], A[1][1], A[1][2], A[1][3], X0.z, X0.w);
           mma_bf16_16816(acc, A[2][0], A[2][1], A[2][2], A[2][3], X1.x, X1.y);
           mma_bf16_16816(acc, A[3][0], A[3][1], A[3][2], A[3][3], X1.z, X1.w);
-          const float2 x1 = *reinterpret_cast<const float2*>(x1s + grp * MT + 8 * j + 2 * t);
-          const float2 x2 = *reinterpret_cast<const float2*>(x2s + grp * MT + 8 * j + 2 * t);
-          // y += s * acc - s * 128 sum(x) + b * sum(x)
-          y[j][0] = fmaf(sgv[gi], acc[0], fmaf(bgv[gi], x1.x, fmaf(-sgv[gi], x2.x, y[j][0])));
-          y[j][1] = fmaf(sgv[gi], acc[1], fmaf(bgv[gi], x1.y, fmaf(-sgv[gi], x2.y, y[j][1])));
-          y[j][2] = fmaf(sg8[gi], acc[2], fmaf(bg8[gi], x1.x, fmaf(-sg8[gi], x2.x, y[j][2])));
-          y[j][3] = fmaf(sg8[gi], acc[3], fmaf(bg8[gi], x1.y, fmaf(-sg8[gi], x2.y, y[j][3])));
+          // y += s * acc + (b - 128 s) * sum(x): the MMA saw 128 + q
+          const float bb0 = fmaf(-128.0f, sgv[gi], bgv[gi]), bb1 = fmaf(-128.0f, sg8[gi], bg8[gi]);
+          if constexpr (ONE) {  // token 0 sits in lanes t == 0, outputs 0 and 2
+            const float x1 = x1s[grp * MT + 2 * t];
+            y[j][0] = fmaf(sgv[gi], acc[0], fmaf(bb0, x1, y[j][0]));
+            y[j][2] = fmaf(sg8[gi], acc[2], fmaf(bb1, x1, y[j][2]));
+          } else {
+            const float2 x1 = *reinterpret_cast<const float2*>(x1s + grp * MT + 8 * j + 2 * t);
+            y[j][0] = fmaf(sgv[gi], acc[0], fmaf(bb0, x1.x, y[j][0]));
+            y[j][1] = fmaf(sgv[gi], acc[1], fmaf(bb0, x1.y, y[j][1]));
+            y[j][2] = fmaf(sg8[gi], acc[2], fmaf(bb1, x1.x, y[j][2]));
+            y[j][3] = fmaf(sg8[gi], acc[3], fmaf(bb1, x1.y, y[j][3]));
+          }
         }
       } else if constexpr (XSMEM && F16) {
         const uint32_t wA8 = wA >> 8, wB8 = wB >> 8, wC8 = wC >> 8, wD8 = wD >> 8;
@@ -550,9 +558,9 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
 // K-split ways per row tile forced through higgs_set_option("gemv_wk", 1|2|4|8); 0 = heuristic
 int g_force_wk = 0;
 
-template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER>
+template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER, bool ONE>
 cudaError_t launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
-  auto k = qgemv_ring_kernel<NT8, WK, EPI, S, XSMEM, NORM, F16, GATHER>;
+  auto k = qgemv_ring_kernel<NT8, WK, EPI, S, XSMEM, NORM, F16, GATHER, ONE>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
@@ -562,7 +570,7 @@ cudaError_t launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st
   return launch_pdl(k, dim3(ctas, GATHER ? a.moe_max_items : 1), dim3(256), smem, st, a);
 }
 
-template <int NT8, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER = false>
+template <int NT8, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER = false, bool ONE = false>
 cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
   const int nrt = a.N / 16;
   const int units = a.K / 256;
@@ -588,9 +596,9 @@ cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
     if (wk > 4) wk = 4;
     const int rot = (8 / wk) / 2;
     const int ctas = (nrt + rot - 1) / rot;
-    if (wk == 4) return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
-    if (wk == 2) return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
-    return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
+    if (wk == 4) return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16, GATHER, ONE>(a, ctas, smem, st);
+    if (wk == 2) return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16, GATHER, ONE>(a, ctas, smem, st);
+    return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16, GATHER, ONE>(a, ctas, smem, st);
   }
   // measured on B200 (M=1): K split 8 ways while the tiles alone cannot fill the
   // slots, else 4 ways -- more CTAs beat fewer fatter ones even for the LM head
@@ -600,10 +608,10 @@ cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
   const int rot = 8 / wk;
   const int ctas = (nrt + rot - 1) / rot;
   switch (wk) {
-    case 8: return launch_cfg<NT8, 8, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
-    case 4: return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
-    case 2: return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
-    default: return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16, GATHER>(a, ctas, smem, st);
+    case 8: return launch_cfg<NT8, 8, EPI, S, XSMEM, NORM, F16, GATHER, ONE>(a, ctas, smem, st);
+    case 4: return launch_cfg<NT8, 4, EPI, S, XSMEM, NORM, F16, GATHER, ONE>(a, ctas, smem, st);
+    case 2: return launch_cfg<NT8, 2, EPI, S, XSMEM, NORM, F16, GATHER, ONE>(a, ctas, smem, st);
+    default: return launch_cfg<NT8, 1, EPI, S, XSMEM, NORM, F16, GATHER, ONE>(a, ctas, smem, st);
   }
 }
 
@@ -619,6 +627,10 @@ cudaError_t launch_epi(const QLinArgs& a, cudaStream_t st) {
       if (a.norm_w) return launch_wk<1, EPI, 3, true, true, true>(a, st);
       if (xsmem) return launch_wk<1, EPI, 3, true, false, true>(a, st);
     } else {
+      if (a.M == 1) {  // one token: fold only its outputs
+        if (a.norm_w) return launch_wk<1, EPI, 3, true, true, false, false, true>(a, st);
+        if (xsmem) return launch_wk<1, EPI, 3, true, false, false, false, true>(a, st);
+      }
       if (a.norm_w) return launch_wk<1, EPI, 3, true, true, false>(a, st);
       if (xsmem) return launch_wk<1, EPI, 3, true, false, false>(a, st);
     }

@@ -74,7 +74,7 @@ int higgs_version(void);
 /* Process-wide tuning switches (no reference counterpart).  "gemv_f16" (0/1,
  * default 0): decode GEMVs with x staged in shared memory feed the tensor cores
  * fp16 operands (x scaled per token by a power of two, exact for bf16 inputs)
- * instead of bf16 ones.  "attn_min_pages" (4..64, default 8): KV pages per split
+ * instead of bf16 ones.  "attn_min_pages" (4..4096, default 8): KV pages per split
  * of higgs_fused_attention; change it only between captures, since workspace
  * sizes depend on it.  "l2_prefetch" (bit mask, default 0): bit 0 makes every
  * GEMV of the decode step ask the TMA unit to pull the next GEMV's weights into
