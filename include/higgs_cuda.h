@@ -246,8 +246,10 @@ int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq
  * device arena and budgets every byte itself, or a real-time decode loop that
  * must never block in the driver's allocator).  No counterpart in the
  * reference.  The split-K scratch is an 8 MiB array built into the library
- * (held on every GPU that loads it until the process exits); shapes needing
- * more are rejected with HIGGS_ERR_WORKSPACE.  The first call on a device looks
+ * (held on every GPU that loads it until the process exits).  The split plan
+ * keeps a launch within one resident wave of CTAs, so every shape the call
+ * accepts (B * Hkv <= 1024, D 64 or 128) fits; a shape needing more would be
+ * rejected with HIGGS_ERR_WORKSPACE before any launch.  The first call on a device looks
  * up that array's device address, so make that first call before any stream
  * capture.  Every call shares the one array: calls that overlap on the GPU
  * (concurrent streams, several host threads) race and must be serialised by

@@ -87,3 +87,24 @@ def test_workspace_size_queries_without_device(lib):
     assert f(32, 4096, 12288) >= f(32, 4096, 6144)
     for M, K, rows in [(0, 4096, 4096), (1, 100, 4096), (1, 4096, 10), (-1, 256, 16)]:
         assert f(M, K, rows) == 0, (M, K, rows)
+
+
+def test_noalloc_attention_scratch_covers_every_shape(lib):
+    """The allocation-free attention entry point keeps its split partials in a fixed 8 MiB
+    array.  The split plan caps the CTAs of a launch at one resident wave, so every shape
+    the entry accepts (B * Hkv <= 1024, D <= 128) fits; checked here on the host with the
+    workspace query the entry point uses."""
+    f = lib.higgs_paged_attention_workspace_size
+    f.restype = ctypes.c_size_t
+    f.argtypes = [ctypes.c_int] * 6
+    worst = 0
+    for B in (1, 2, 3, 8, 17, 32, 37, 64, 100, 148, 256, 295, 296, 297, 512, 1024):
+        for Hkv in (1, 2, 4, 8):
+            if B * Hkv > 1024:
+                continue
+            for G in (1, 4, 8, 16, 32):
+                for Lq in (1, 2, 5, 8, 33):
+                    for D in (64, 128):
+                        for L in (16, 2048, 32768, 131072):
+                            worst = max(worst, f(B, Lq, G * Hkv, Hkv, D, max(L, Lq)))
+    assert 0 < worst <= 8 << 20, worst
