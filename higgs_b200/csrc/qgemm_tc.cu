@@ -542,13 +542,14 @@ int tc_sms() {
   return n;
 }
 
-// K splits: about two CTAs per SM in total, at least 4 groups of 64 per split
+// K splits: as many as keep the launch within two waves of one CTA per SM (a partial
+// third wave costs more than longer splits), at least 4 groups of 64 per split
 int tc_splits(int M, int K, int N) {
   const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
   const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
   const int G = K / 64;
   if (tiles == 0 || M < 1) return 1;  // no tile (N < 128): nothing to split
-  int splits = (int)((2 * tc_sms() + tiles - 1) / tiles);
+  int splits = (int)((2 * (size_t)tc_sms()) / tiles);
   if (splits > G / 4) splits = G / 4;
   if (splits < 1 || tiles > (size_t)kTcMaxTiles) splits = 1;
   return splits;

@@ -413,7 +413,12 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
         for (int j = 0; j < NT8; ++j) {
           const int tok = 8 * j + g;
           uint4 X0 = make_uint4(0, 0, 0, 0), X1 = make_uint4(0, 0, 0, 0);
-          if (tok < M) {
+          if constexpr (ONE) {
+            // every lane takes token 0's fragment: the other MMA columns are never stored
+            const uint4* xp = reinterpret_cast<const uint4*>(xf + (grp * 4 + t) * 32);
+            X0 = xp[0];
+            X1 = xp[1];
+          } else if (tok < M) {
             const uint4* xp = reinterpret_cast<const uint4*>(xf + tok * xtok_bytes + (grp * 4 + t) * 32);
             X0 = xp[0];
             X1 = xp[1];
