@@ -608,6 +608,9 @@ cudaError_t launch_wk(const QLinArgs& a, cudaStream_t st) {
   // measured on B200 (M=1): K split 8 ways while the tiles alone cannot fill the
   // slots, else 4 ways -- more CTAs beat fewer fatter ones even for the LM head
   wk = (work / 2 >= slots) ? 4 : 8;
+  // very wide outputs (the LM head: ~9.5k row tiles): fewer K splits, fatter warps
+  // (measured, N = 151936: M=1 wk 2 103.7 vs 106.7 us; M=8 wk 1 129.6 vs 146.6 us)
+  if (!GATHER && work >= 16LL * slots) wk = a.M >= 4 ? 1 : 2;
   if (g_force_wk > 0) wk = g_force_wk;
   while (wk > 1 && units < wk) wk >>= 1;
   const int rot = 8 / wk;
