@@ -134,6 +134,7 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
       lv += __shfl_xor_sync(0xffffffffu, lv, 1);
       lv += __shfl_xor_sync(0xffffffffu, lv, 2);
       const int row = mt * 16 + g + 8 * hlf;
+      if (row >= R) continue;  // padding rows of the MMA tile are never read
       if (t == 0) {
         sm_m[warp * RP + row] = m[mt][hlf];
         sm_l[warp * RP + row] = lv;
@@ -183,49 +184,46 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
   __threadfence();
   const float* base_o = a.ws_o + (size_t)bh * a.splits * RP * D;
   const float* base_l = a.ws_lse + (size_t)bh * a.splits * RP;
-  // split weights w[s][row] = exp2(lse - max) / sum, staged in shared memory
-  // (sm_m / sm_l are free now; splits * R <= 4 * RP * D floats of sm_o's slots 1-3)
-  float* sw = sm_o + RP * D;  // [splits][R]
-  for (int i = threadIdx.x; i < a.splits * R; i += kAttnThreads)
-    sw[i] = __ldcg(base_l + (i / R) * RP + (i % R));
-  __syncthreads();
-  if (threadIdx.x < R) {
-    const int row = threadIdx.x;
-    float M = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) M = fmaxf(M, sw[s * R + row]);
-    float W = 0.0f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float ls = sw[s * R + row];
-      const float w = (ls == -INFINITY) ? 0.0f : exp2f(ls - M);
-      sw[s * R + row] = w;
-      W += w;
-    }
-    sm_lse[row] = W > 0.0f ? 1.0f / W : 0.0f;
-  }
-  __syncthreads();
-  // every thread owns 4 consecutive d of one row; the float4 loads of 8 splits
-  // are issued together, so the merge costs ~splits/8 L2 round trips
+  // every thread owns 4 consecutive d of one row; the lse and the float4 partials of up
+  // to 16 splits are loaded together and folded with a running maximum, so the merge
+  // costs one L2 round trip per 16 splits
+  constexpr int CH = 16;
   for (int i4 = threadIdx.x; i4 < R * D / 4; i4 += kAttnThreads) {
     const int row = (i4 * 4) / D;
+    float M = -INFINITY, W = 0.0f;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    int s = 0;
-    for (; s < a.splits; s += 8) {
-      float4 v[8];
+    for (int s0 = 0; s0 < a.splits; s0 += CH) {
+      float ls[CH];
+      float4 v[CH];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        v[u] = s + u < a.splits
-                   ? __ldcg(reinterpret_cast<const float4*>(base_o + (size_t)(s + u) * RP * D) + i4)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u = 0; u < CH; ++u) {
+        const bool in = s0 + u < a.splits;
+        ls[u] = in ? __ldcg(base_l + (size_t)(s0 + u) * RP + row) : -INFINITY;
+        v[u] = in ? __ldcg(reinterpret_cast<const float4*>(base_o + (size_t)(s0 + u) * RP * D) + i4)
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float Mc = M;
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const float w = s + u < a.splits ? sw[(s + u) * R + row] : 0.f;
+      for (int u = 0; u < CH; ++u) Mc = fmaxf(Mc, ls[u]);
+      if (Mc == -INFINITY) continue;  // no key of this row in these splits
+      const float r = (M == -INFINITY) ? 0.0f : exp2f(M - Mc);
+      W *= r;
+      acc.x *= r;
+      acc.y *= r;
+      acc.z *= r;
+      acc.w *= r;
+#pragma unroll
+      for (int u = 0; u < CH; ++u) {
+        const float w = (ls[u] == -INFINITY) ? 0.0f : exp2f(ls[u] - Mc);
+        W += w;
         acc.x = fmaf(w, v[u].x, acc.x);
         acc.y = fmaf(w, v[u].y, acc.y);
         acc.z = fmaf(w, v[u].z, acc.z);
         acc.w = fmaf(w, v[u].w, acc.w);
       }
+      M = Mc;
     }
-    const float inv = sm_lse[row];
+    const float inv = W > 0.0f ? 1.0f / W : 0.0f;
     sm_o[i4 * 4 + 0] = acc.x * inv;
     sm_o[i4 * 4 + 1] = acc.y * inv;
     sm_o[i4 * 4 + 2] = acc.z * inv;
@@ -435,6 +433,37 @@ __device__ __forceinline__ void fa_rope(float (&lo)[D / 64], float (&hi)[D / 64]
   }
 }
 
+// fa_norm / fa_rope with the weight and frequency operands already in registers
+template <int D>
+__device__ __forceinline__ void fa_norm_r(float (&lo)[D / 64], float (&hi)[D / 64], const float (&wlo)[D / 64],
+                                          const float (&whi)[D / 64], float eps) {
+  constexpr int E = D / 64;
+  float ss = 0.0f;
+#pragma unroll
+  for (int e = 0; e < E; ++e) ss += lo[e] * lo[e] + hi[e] * hi[e];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    lo[e] = round_bf(lo[e] * inv * wlo[e]);
+    hi[e] = round_bf(hi[e] * inv * whi[e]);
+  }
+}
+template <int D>
+__device__ __forceinline__ void fa_rope_r(float (&lo)[D / 64], float (&hi)[D / 64], int pos,
+                                          const float (&ifq)[D / 64]) {
+  constexpr int E = D / 64;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float th = (float)pos * ifq[e];
+    float sn, cs;
+    sincosf(th, &sn, &cs);
+    const float x0 = lo[e], x1 = hi[e];
+    lo[e] = round_bf(x0 * cs - x1 * sn);
+    hi[e] = round_bf(x1 * cs + x0 * sn);
+  }
+}
+
 // write a head (lane layout of fa_load_head) to a swizzled smem row
 template <int D>
 __device__ __forceinline__ void fa_store_row(uint16_t* tile, int row, int lane,
@@ -497,6 +526,19 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
     cp_async_commit();
   }
 
+  // norm weights and RoPE frequencies are constants of the model: into registers before
+  // the wait, so the query / key preparation after it waits on one load only
+  constexpr int E = D / 64;
+  float qwl[E], qwh[E], kwl[E], kwh[E], ifq[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    qwl[e] = a.qn ? bf2f(a.qn[lane * E + e]) : 1.0f;
+    qwh[e] = a.qn ? bf2f(a.qn[D / 2 + lane * E + e]) : 1.0f;
+    kwl[e] = a.kn ? bf2f(a.kn[lane * E + e]) : 1.0f;
+    kwh[e] = a.kn ? bf2f(a.kn[D / 2 + lane * E + e]) : 1.0f;
+    ifq[e] = a.inv_freq[lane * E + e];
+  }
+
   pdl_wait();
   pdl_launch();
 
@@ -507,8 +549,9 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
       const int tok = b * Lq + tq;
       float lo[D / 64], hi[D / 64];
       fa_load_head<D>(a.qkv + ((size_t)tok * nh + hq) * D, lane, lo, hi);
-      if (a.qn) fa_norm<D>(lo, hi, a.qn, a.eps, lane);
-      fa_rope<D>(lo, hi, a.pos[tok], a.inv_freq, lane);
+      const int ptok = a.pos[tok];
+      if (a.qn) fa_norm_r<D>(lo, hi, qwl, qwh, a.eps);
+      fa_rope_r<D>(lo, hi, ptok, ifq);
       fa_store_row<D>(Qs, r, lane, lo, hi);
     } else {
       for (int i = lane; i < D; i += 32) Qs[r * D + i] = 0;
@@ -523,8 +566,9 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
     const int tok = b * Lq + tq;
     float klo[D / 64], khi[D / 64], vlo[D / 64], vhi[D / 64];
     fa_load_head<D>(a.qkv + ((size_t)tok * nh + a.Hq + h) * D, lane, klo, khi);
-    if (a.kn) fa_norm<D>(klo, khi, a.kn, a.eps, lane);
-    fa_rope<D>(klo, khi, a.pos[tok], a.inv_freq, lane);
+    const int ptok = a.pos[tok];
+    if (a.kn) fa_norm_r<D>(klo, khi, kwl, kwh, a.eps);
+    fa_rope_r<D>(klo, khi, ptok, ifq);
     fa_load_head<D>(a.qkv + ((size_t)tok * nh + a.Hq + a.Hkv + h) * D, lane, vlo, vhi);
     fa_store_gmem<D>(NK + (tq * 2) * D, lane, klo, khi);
     fa_store_gmem<D>(NK + (tq * 2 + 1) * D, lane, vlo, vhi);
