@@ -29,6 +29,7 @@ void attention_set_min_pages(int n);
 void set_l2_prefetch(int mode);
 void set_gemm_tc(bool on);
 void set_gemm_tc_rows(int m);
+void set_gemm_tc_waves(int w);
 void qgemv_set_wk(int wk);
 void qgemm_tc_prepare();
 
@@ -49,6 +50,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemm_tc_rows") {
     set_gemm_tc_rows(value);
+    return HIGGS_OK;
+  }
+  if (n == "gemm_tc_waves") {
+    set_gemm_tc_waves(value);
     return HIGGS_OK;
   }
   if (n == "gemm_tc") {

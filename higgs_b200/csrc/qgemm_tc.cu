@@ -542,14 +542,19 @@ int tc_sms() {
   return n;
 }
 
-// K splits: as many as keep the launch within two waves of one CTA per SM (a partial
-// third wave costs more than longer splits), at least 4 groups of 64 per split
+// waves of one CTA per SM that the K splits of a launch may fill (higgs_set_option
+// "gemm_tc_waves"; change it only between captures, since workspace sizes depend on it)
+int g_tc_waves = 1;
+
+// K splits: as many as keep the launch within g_tc_waves waves of one CTA per SM (a
+// partial extra wave costs more than longer splits; measured at B=32 decode, Qwen3-8B:
+// 1 wave 6.84, 2 waves 7.16, 3 waves 7.97 ms per step), at least 4 groups of 64 per split
 int tc_splits(int M, int K, int N) {
   const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
   const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
   const int G = K / 64;
   if (tiles == 0 || M < 1) return 1;  // no tile (N < 128): nothing to split
-  int splits = (int)((2 * (size_t)tc_sms()) / tiles);
+  int splits = (int)(((size_t)g_tc_waves * tc_sms()) / tiles);
   if (splits > G / 4) splits = G / 4;
   if (splits < 1 || tiles > (size_t)kTcMaxTiles) splits = 1;
   return splits;
@@ -637,7 +642,9 @@ cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_byte
   return launch_bn<128, false>(map, wm, a, grid, st);
 }
 
-// one-time host state (error flag, driver entry point): call before any stream capture
+void set_gemm_tc_waves(int w) { g_tc_waves = w < 1 ? 1 : (w > 8 ? 8 : w); }
+
+// one-time host state (error flag, driver entry point, SM count): call before any stream capture
 void qgemm_tc_prepare() {
   tc_err_ptr();
   encode_fn();

@@ -206,6 +206,19 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
     __shared__ float inv_rms[MT];
     __shared__ float red[8][MT];
     __shared__ float redm[8][MT];
+    // one pass over x when every staging task below fits one thread (fused norm, bf16
+    // operands): the values loaded for the RMS statistics stay in registers for the staging
+    const bool one_pass = NORM && !F16 && M * G * 4 <= 256;
+    uint4 pv0 = make_uint4(0, 0, 0, 0), pv1 = make_uint4(0, 0, 0, 0), pw0 = pv0, pw1 = pv0;
+    if (one_pass && (int)threadIdx.x < M * G * 4) {
+      const int task = threadIdx.x;
+      const int k0 = ((task / 4) % G) * 64 + 16 * (task % 4);
+      const uint16_t* src = a.x + (size_t)xrow(task / (G * 4)) * K + k0;
+      pv0 = *reinterpret_cast<const uint4*>(src);
+      pv1 = *reinterpret_cast<const uint4*>(src + 8);
+      pw0 = *reinterpret_cast<const uint4*>(a.norm_w + k0);  // with the same round trip
+      pw1 = *reinterpret_cast<const uint4*>(a.norm_w + k0 + 8);
+    }
     if constexpr (!NORM && !F16) {
       // plain bf16 staging: no statistics needed
       if (threadIdx.x < MT) {
@@ -221,7 +234,21 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
         ss[m] = 0.f;
         mx[m] = 0.f;
       }
-      for (int vi = threadIdx.x; vi < M * (K / 8); vi += 256) {
+      if (one_pass && (int)threadIdx.x < M * G * 4) {
+        const int m = threadIdx.x / (G * 4);
+        const uint32_t* p0 = &pv0.x;
+        const uint32_t* p1 = &pv1.x;
+        float acc = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float a0 = bf_lo(p0[e]), a1 = bf_hi(p0[e]), b0 = bf_lo(p1[e]), b1 = bf_hi(p1[e]);
+          acc += a0 * a0 + a1 * a1 + b0 * b0 + b1 * b1;
+        }
+#pragma unroll
+        for (int mm = 0; mm < MT; ++mm)
+          if (mm == m) ss[mm] += acc;
+      }
+      for (int vi = one_pass ? M * (K / 8) : (int)threadIdx.x; vi < M * (K / 8); vi += 256) {
         const int m = vi / (K / 8), k8 = vi % (K / 8);
         const uint4 v = *reinterpret_cast<const uint4*>(a.x + (size_t)xrow(m) * K + k8 * 8);
         const uint32_t* vp = &v.x;
@@ -288,7 +315,10 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
       const int m = valid ? task / (G * 4) : 0, j = valid ? (task / 4) % G : 0, tt = task % 4;
       const uint16_t* src = a.x + (size_t)xrow(m) * K + j * 64 + 16 * tt;
       uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
-      if (valid) {
+      if (one_pass) {  // this thread's only task, loaded above
+        v0 = pv0;
+        v1 = pv1;
+      } else if (valid) {
         v0 = *reinterpret_cast<const uint4*>(src);
         v1 = *reinterpret_cast<const uint4*>(src + 8);
       }
@@ -306,8 +336,8 @@ __global__ void __launch_bounds__(256) qgemv_ring_kernel(QLinArgs a) {
       }
       if constexpr (NORM) {
         const float inv = inv_rms[m];
-        const uint4 w0 = *reinterpret_cast<const uint4*>(a.norm_w + j * 64 + 16 * tt);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(a.norm_w + j * 64 + 16 * tt + 8);
+        const uint4 w0 = one_pass ? pw0 : *reinterpret_cast<const uint4*>(a.norm_w + j * 64 + 16 * tt);
+        const uint4 w1 = one_pass ? pw1 : *reinterpret_cast<const uint4*>(a.norm_w + j * 64 + 16 * tt + 8);
         const uint32_t* q0 = &w0.x;
         const uint32_t* q1 = &w1.x;
 #pragma unroll
