@@ -30,6 +30,7 @@ void set_l2_prefetch(int mode);
 void set_gemm_tc(bool on);
 void set_gemm_tc_rows(int m);
 void set_gemm_tc_waves(int w);
+void set_gemm_tc_wave_cost(int c);
 void qgemv_set_wk(int wk);
 void qgemm_tc_prepare();
 
@@ -54,6 +55,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemm_tc_waves") {
     set_gemm_tc_waves(value);
+    return HIGGS_OK;
+  }
+  if (n == "gemm_tc_wave_cost") {
+    set_gemm_tc_wave_cost(value);
     return HIGGS_OK;
   }
   if (n == "gemm_tc") {

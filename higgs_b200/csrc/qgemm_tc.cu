@@ -542,22 +542,33 @@ int tc_sms() {
   return n;
 }
 
-// waves of one CTA per SM that the K splits of a launch may fill (higgs_set_option
-// "gemm_tc_waves"; change it only between captures, since workspace sizes depend on it)
-int g_tc_waves = 1;
+// K splits of a launch: the count that minimises waves x (k groups per split + a fixed
+// cost per wave, in k-group units), at most g_tc_waves waves of one CTA per SM and at
+// least 4 groups of 64 per split.  A wave the tiles fill only partly costs a whole wave.
+// Measured at B=32 decode (Qwen3-8B): one wave for every shape 6.84 ms per step, two
+// 7.16 ms, three 7.97 ms; this choice (wave cost 8) 6.70 ms.  Both knobs are higgs_set_option values ("gemm_tc_waves",
+// "gemm_tc_wave_cost"); change them only between captures (workspace sizes follow).
+int g_tc_waves = 2;
+int g_tc_wave_cost = 8;
 
-// K splits: as many as keep the launch within g_tc_waves waves of one CTA per SM (a
-// partial extra wave costs more than longer splits; measured at B=32 decode, Qwen3-8B:
-// 1 wave 6.84, 2 waves 7.16, 3 waves 7.97 ms per step), at least 4 groups of 64 per split
 int tc_splits(int M, int K, int N) {
   const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
-  const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
+  const long long tiles = (long long)(N / kTcRows) * ((M + BN - 1) / BN);
   const int G = K / 64;
-  if (tiles == 0 || M < 1) return 1;  // no tile (N < 128): nothing to split
-  int splits = (int)(((size_t)g_tc_waves * tc_sms()) / tiles);
-  if (splits > G / 4) splits = G / 4;
-  if (splits < 1 || tiles > (size_t)kTcMaxTiles) splits = 1;
-  return splits;
+  if (tiles == 0 || M < 1 || tiles > kTcMaxTiles) return 1;  // no tile, or beyond the counters
+  const long long sms = tc_sms();
+  int best = 1;
+  long long best_cost = -1;
+  for (int s = 1; s <= G / 4 && s <= 64; ++s) {
+    const long long waves = (tiles * s + sms - 1) / sms;
+    if (s > 1 && waves > g_tc_waves) break;
+    const long long cost = waves * ((G + s - 1) / s + g_tc_wave_cost);
+    if (best_cost < 0 || cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
 }
 
 }  // namespace
@@ -643,6 +654,7 @@ cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_byte
 }
 
 void set_gemm_tc_waves(int w) { g_tc_waves = w < 1 ? 1 : (w > 8 ? 8 : w); }
+void set_gemm_tc_wave_cost(int c) { g_tc_wave_cost = c < 0 ? 0 : (c > 1000 ? 1000 : c); }
 
 // one-time host state (error flag, driver entry point, SM count): call before any stream capture
 void qgemm_tc_prepare() {

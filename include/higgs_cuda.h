@@ -81,9 +81,10 @@ int higgs_version(void);
  * L2, bit 1 makes each GEMV CTA pull its own weight tiles (a hint; results are
  * unchanged).  "gemm_tc" (0/1, default 1): quantized linears over 17 or more
  * rows use the tcgen05 tensor-core kernel (weights dequantized to bf16 first,
- * MLX's qmm form) instead of the decode GEMV; "gemm_tc_waves" (1..8, default 1): waves of one CTA per SM
- * that the tensor-core kernel's K splits may fill (change it only between
- * captures: workspace sizes depend on it).  "gemm_tc_rows" (default 17) moves
+ * MLX's qmm form) instead of the decode GEMV; "gemm_tc_waves" (1..8, default 2) and "gemm_tc_wave_cost"
+ * (default 8): the tensor-core kernel picks the K-split count that minimises
+ * waves x (k groups per split + wave cost) within that many waves of one CTA
+ * per SM (change them only between captures: workspace sizes depend on them).  "gemm_tc_rows" (default 17) moves
  * that threshold (fused-RMSNorm decode launches always stay on the GEMV).  "gemv_wk" (0, 1, 2, 4, 8; default
  * 0 = heuristic): ways each 16-row tile of the decode GEMV splits K over warps.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
