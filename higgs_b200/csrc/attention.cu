@@ -31,6 +31,7 @@ namespace higgs {
 constexpr int kAttnThreads = 128;
 constexpr int kCounterBytes = 4096;
 constexpr int kTargetCtas = 2 * 148;
+constexpr int kTq4Stages = 4;  // per-warp page ring of the TurboQuant kernel
 
 struct AttnArgs {
   const uint16_t* q;
@@ -781,25 +782,72 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
   constexpr int D = 128;
   constexpr int RP = 16 * MT;
   // smem: qfrag [MT][8 kt][32 lanes][hi 4 | lo 4] u32 | qsum [RP] f32 |
-  //       per warp 2 stages x {kcodes 1 KB, vcodes 1 KB, kscale 32 B, vscale 32 B, vtile bf16 4 KB}
+  //       per warp: kTq4Stages stages x {kcodes 1 KB, vcodes 1 KB, kscale 32 B, vscale 32 B},
+  //       vtile bf16 4 KB | qrot [RP][128] f32 query scratch
+  // (the rings fill before the query rotation, so the scratch cannot share their bytes)
+  constexpr int S = kTq4Stages;
   constexpr int STAGE_BYTES = 1024 + 1024 + 32 + 32;
-  constexpr int WARP_BYTES = 2 * STAGE_BYTES + 16 * D * 2;
+  constexpr int WARP_BYTES = S * STAGE_BYTES + 16 * D * 2;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem_raw);
   float* qsum = reinterpret_cast<float*>(qfrag + MT * 8 * 32 * 8);
-  float* qrot = qsum + RP;  // [RP][128] f32 scratch, reused as per-warp buffers later
-  uint8_t* wbase = reinterpret_cast<uint8_t*>(qrot);
+  uint8_t* wbase = reinterpret_cast<uint8_t*>(qsum + RP);
+  float* qrot = reinterpret_cast<float*>(wbase + 4 * WARP_BYTES);
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int G = a.Hq / a.Hkv;
   const int R = G * a.lq_chunk;
 
-  pdl_wait();
+  // block table and lengths are inputs of the step (not written by the previous kernel)
   const int L = a.seq_lens[b];
   const int n_pages = min((L + 15) / 16, a.max_blocks);
   const int pg0 = split * a.pages_per_split;
   const int pg1 = min(n_pages, pg0 + a.pages_per_split);
+  uint8_t* my = wbase + warp * WARP_BYTES;
+  auto kcb = [&](int st) { return my + st * STAGE_BYTES; };
+  auto vcb = [&](int st) { return my + st * STAGE_BYTES + 1024; };
+  auto ksb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2048); };
+  auto vsb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2080); };
+  auto issue = [&](int pg, int st) {
+    const int pid = a.bt[(size_t)b * a.max_blocks + pg];
+    const size_t off = (size_t)pid * a.page_stride + (size_t)h * a.head_stride;
+    const size_t soff = (size_t)pid * (a.page_stride / 64) + (size_t)h * (a.head_stride / 64);
+    const int valid = min(16, L - pg * 16);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int qd = lane + 32 * i;  // 64 chunks of 16 B = 16 rows x 64 B
+      const int r = qd >> 2;
+      const int bytes = r < valid ? 16 : 0;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(kcb(st) + qd * 16)),
+                   "l"(a.kcode + off + qd * 16), "r"(bytes));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vcb(st) + qd * 16)),
+                   "l"(a.vcode + off + qd * 16), "r"(bytes));
+    }
+    if (lane < 2) {
+      const int bytes = (lane * 8 < valid) ? 16 : 0;  // each 16 B chunk = 8 scales
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(ksb(st) + lane * 8)),
+                   "l"(a.kscale + soff + lane * 8), "r"(bytes));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vsb(st) + lane * 8)),
+                   "l"(a.vscale + soff + lane * 8), "r"(bytes));
+    }
+  };
+  // the first S-1 pages of this warp into the ring; pages holding only tokens of earlier
+  // steps (the previous kernel appends this step's) are fetched before the dependency wait
+  int pre = 0;
+  const int old_end = L - a.Lq;  // positions below this were written by earlier steps
+  for (; pre < S - 1; ++pre) {
+    const int pgs = pg0 + warp + 4 * pre;
+    if (pgs >= pg1 || (pgs + 1) * 16 > old_end) break;
+    issue(pgs, pre);
+    cp_async_commit();
+  }
+  pdl_wait();
+  for (; pre < S - 1; ++pre) {
+    const int pgs = pg0 + warp + 4 * pre;
+    if (pgs < pg1) issue(pgs, pre);
+    cp_async_commit();
+  }
 
   // rotate the query rows: q' = R q, rounded to bf16 (the MMA operand), and
   // the per-row sum of the rounded q' (removes the +136 code offset)
@@ -863,45 +911,26 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
     qs[mt][0] = qsum[mt * 16 + g];
     qs[mt][1] = qsum[mt * 16 + g + 8];
   }
-
-  uint8_t* my = wbase + warp * WARP_BYTES;
-  uint16_t* vtile = reinterpret_cast<uint16_t*>(my + 2 * STAGE_BYTES);
-  auto kcb = [&](int st) { return my + st * STAGE_BYTES; };
-  auto vcb = [&](int st) { return my + st * STAGE_BYTES + 1024; };
-  auto ksb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2048); };
-  auto vsb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2080); };
-  auto issue = [&](int pg, int st) {
-    const int pid = a.bt[(size_t)b * a.max_blocks + pg];
-    const size_t off = (size_t)pid * a.page_stride + (size_t)h * a.head_stride;
-    const size_t soff = (size_t)pid * (a.page_stride / 64) + (size_t)h * (a.head_stride / 64);
-    const int valid = min(16, L - pg * 16);
+  // one 16-row tile: its query fragments stay in registers for the whole page loop
+  // instead of being re-read from shared memory for every page
+  uint4 qreg[MT == 1 ? 8 : 1][2];
+  if constexpr (MT == 1) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
-      const int qd = lane + 32 * i;  // 64 chunks of 16 B = 16 rows x 64 B
-      const int r = qd >> 2;
-      const int bytes = r < valid ? 16 : 0;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(kcb(st) + qd * 16)),
-                   "l"(a.kcode + off + qd * 16), "r"(bytes));
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vcb(st) + qd * 16)),
-                   "l"(a.vcode + off + qd * 16), "r"(bytes));
+    for (int kt = 0; kt < 8; ++kt) {
+      const uint4* qp = reinterpret_cast<const uint4*>(qfrag + (kt * 32 + lane) * 8);
+      qreg[kt][0] = qp[0];
+      qreg[kt][1] = qp[1];
     }
-    if (lane < 2) {
-      const int bytes = (lane * 8 < valid) ? 16 : 0;  // each 16 B chunk = 8 scales
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(ksb(st) + lane * 8)),
-                   "l"(a.kscale + soff + lane * 8), "r"(bytes));
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vsb(st) + lane * 8)),
-                   "l"(a.vscale + soff + lane * 8), "r"(bytes));
-    }
-  };
+  }
 
-  int stage = 0;
-  int pg = pg0 + warp;
-  if (pg < pg1) issue(pg, 0);
-  cp_async_commit();
-  for (; pg < pg1; pg += 4) {
-    if (pg + 4 < pg1) issue(pg + 4, stage ^ 1);
+  uint16_t* vtile = reinterpret_cast<uint16_t*>(my + S * STAGE_BYTES);
+  int i = 0;
+  for (int pg = pg0 + warp; pg < pg1; pg += 4, ++i) {
+    const int stage = i % S;
+    const int nxt = pg + 4 * (S - 1);
+    if (nxt < pg1) issue(nxt, (i + S - 1) % S);
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<S - 1>();
     __syncwarp();
     const uint8_t* kc = kcb(stage);
     const uint8_t* vcc = vcb(stage);
@@ -952,22 +981,36 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
       }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
+      // the hi and lo halves of q' accumulate separately: two short MMA chains per
+      // 8-key block instead of one of 16
       float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      float sl[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
         const uint4 kw = *reinterpret_cast<const uint4*>(kc + (nt * 8 + g) * 64 + 16 * t);
         const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
         for (int kt = 0; kt < 8; ++kt) {
-          const uint4* qp = reinterpret_cast<const uint4*>(qfrag + ((mt * 8 + kt) * 32 + lane) * 8);
-          const uint4 qa = qp[0], ql = qp[1];
+          uint4 qa, ql;
+          if constexpr (MT == 1) {
+            qa = qreg[kt][0];
+            ql = qreg[kt][1];
+          } else {
+            const uint4* qp = reinterpret_cast<const uint4*>(qfrag + ((mt * 8 + kt) * 32 + lane) * 8);
+            qa = qp[0];
+            ql = qp[1];
+          }
           const uint32_t w = kws[kt >> 1];
           const uint32_t b0 = (kt & 1) ? nib_pair_bf16<8>(w) : nib_pair_bf16<0>(w);
           const uint32_t b1 = (kt & 1) ? nib_pair_bf16<12>(w) : nib_pair_bf16<4>(w);
           mma_bf16_16816(s[nt], qa.x, qa.y, qa.z, qa.w, b0, b1);
-          mma_bf16_16816(s[nt], ql.x, ql.y, ql.z, ql.w, b0, b1);
+          mma_bf16_16816(sl[nt], ql.x, ql.y, ql.z, ql.w, b0, b1);
         }
       }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[nt][c] += sl[nt][c];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -1007,12 +1050,11 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
       }
     }
     __syncwarp();
-    stage ^= 1;
   }
   cp_async_wait<0>();
   pdl_launch();
 
-  float* smem_f = reinterpret_cast<float*>(qrot);
+  float* smem_f = reinterpret_cast<float*>(wbase);  // rings and query scratch are dead now
   FinishTq4 fin{&a};
   attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
 }
@@ -1064,11 +1106,10 @@ static size_t smem_bf16(int D, int MT) {
 
 static size_t smem_tq4(int MT) {
   const size_t head = (size_t)MT * 8 * 32 * 8 * 4 + 16 * MT * 4;
-  const size_t warps = (size_t)4 * (2 * (1024 + 1024 + 32 + 32) + 16 * 128 * 2);
+  const size_t warps = (size_t)4 * (kTq4Stages * (1024 + 1024 + 32 + 32) + 16 * 128 * 2);
   const size_t qrot = (size_t)16 * MT * 128 * 4;
   const size_t merge = (size_t)(9 * 16 * MT + 4 * 16 * MT * 128) * 4;
-  size_t body = warps;
-  if (qrot > body) body = qrot;
+  size_t body = warps + qrot;  // the query scratch follows the rings
   if (merge > body) body = merge;
   return head + body;
 }

@@ -583,15 +583,17 @@ bool qgemm_tc_supported(const QLinArgs& a) {
 }
 
 // A fixed counter region (one int per tile, up to kTcMaxTiles, zero between
-// calls), then the split-K partial tiles.  The fixed region lets matmuls of every
-// shape -- and the stream-K GEMV, whose counters sit in the same bytes -- share
-// one workspace back to back on a stream.
+// calls), then the split-K partial tiles.  Split launches fill at most g_tc_waves
+// waves of CTAs, so the partials never exceed that many CTAs' tiles whatever N and
+// K are: the size depends on M (the tile width) and the options only, and one
+// workspace sized for the largest M serves every shape back to back on a stream --
+// the stream-K GEMV's counters sit in the same first bytes.
 size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu) {
-  const int splits = tc_splits(M, K, N);
-  if (splits == 1) return 0;
+  (void)K;
+  (void)N;
   const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
-  const size_t tiles = (size_t)(N / kTcRows) * ((M + BN - 1) / BN);
-  return kTcCounterBytes + tiles * splits * (swiglu ? 2 : 1) * kTcRows * BN * sizeof(float);
+  return kTcCounterBytes +
+         (size_t)g_tc_waves * tc_sms() * (swiglu ? 2 : 1) * kTcRows * BN * sizeof(float);
 }
 
 cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_bytes, cudaStream_t st) {

@@ -20,6 +20,12 @@
  *     *_workspace_size() query returns.
  *   - A context may be used by one host thread at a time; distinct contexts
  *     are independent.
+ *   - Kernels start early behind the previous kernel on the stream
+ *     (programmatic dependent launch) and fetch what cannot depend on it
+ *     first: weights, and for the attention calls the block table, the
+ *     sequence lengths and the KV pages of earlier steps.  Those inputs must
+ *     therefore not be written by the kernel enqueued immediately before the
+ *     call (host copies, or any earlier kernel, are fine).
  *   - Quantized weights use the MLX affine layout: weight u32 [N, K/8] with
  *     element k of a row in word k/8 at bits 4*(k%8); scales and biases bf16
  *     [N, K/64]; w = scale * q + bias (group size 64, 4 bits).

@@ -108,3 +108,17 @@ def test_noalloc_attention_scratch_covers_every_shape(lib):
                         for L in (16, 2048, 32768, 131072):
                             worst = max(worst, f(B, Lq, G * Hkv, Hkv, D, max(L, Lq)))
     assert 0 < worst <= 8 << 20, worst
+
+
+def test_one_workspace_serves_every_shape(lib):
+    """The workspace contract: a workspace sized for the largest shape of a given row
+    count serves every smaller shape (the split choice may differ per shape)."""
+    f = lib.higgs_qlinear_sk_workspace_size
+    f.restype = ctypes.c_size_t
+    f.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    shapes = [(4096, 6144), (4096, 4096), (4096, 24576), (12288, 4096), (4096, 151936),
+              (768, 2048), (2048, 768 * 2), (256, 128)]
+    for M in (1, 8, 17, 32, 33, 64, 100, 300):
+        big = f(M, 12288, 151936 * 2)
+        for K, rows in shapes:
+            assert 0 < f(M, K, rows) <= big, (M, K, rows)
