@@ -31,7 +31,7 @@ namespace higgs {
 constexpr int kAttnThreads = 128;
 constexpr int kCounterBytes = 4096;
 constexpr int kTargetCtas = 2 * 148;
-constexpr int kTq4Stages = 4;  // per-warp page ring of the TurboQuant kernel
+constexpr int kTq4Stages = 6;  // per-warp page ring of the TurboQuant kernel (a pair + 4 in flight)
 
 struct AttnArgs {
   const uint16_t* q;
@@ -87,11 +87,14 @@ __device__ __forceinline__ void load_page_bf16(uint16_t* dst, const uint16_t* sr
   }
 }
 
-__device__ __forceinline__ void row_stats_update(float (&m)[2], float (&l)[2], float (&s)[2][4],
+template <int NT>
+__device__ __forceinline__ void row_stats_update(float (&m)[2], float (&l)[2], float (&s)[NT][4],
                                                  float (&alpha)[2]) {
 #pragma unroll
   for (int hlf = 0; hlf < 2; ++hlf) {
-    float mx = fmaxf(fmaxf(s[0][2 * hlf], s[0][2 * hlf + 1]), fmaxf(s[1][2 * hlf], s[1][2 * hlf + 1]));
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) mx = fmaxf(mx, fmaxf(s[nt][2 * hlf], s[nt][2 * hlf + 1]));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float mn = fmaxf(m[hlf], mx);
@@ -99,7 +102,7 @@ __device__ __forceinline__ void row_stats_update(float (&m)[2], float (&l)[2], f
     m[hlf] = mn;
     float rs = 0.0f;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         float& v = s[nt][2 * hlf + e];
@@ -783,11 +786,11 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
   constexpr int RP = 16 * MT;
   // smem: qfrag [MT][8 kt][32 lanes][hi 4 | lo 4] u32 | qsum [RP] f32 |
   //       per warp: kTq4Stages stages x {kcodes 1 KB, vcodes 1 KB, kscale 32 B, vscale 32 B},
-  //       vtile bf16 4 KB | qrot [RP][128] f32 query scratch
+  //       two V tiles bf16 4 KB each | qrot [RP][128] f32 query scratch
   // (the rings fill before the query rotation, so the scratch cannot share their bytes)
   constexpr int S = kTq4Stages;
   constexpr int STAGE_BYTES = 1024 + 1024 + 32 + 32;
-  constexpr int WARP_BYTES = S * STAGE_BYTES + 16 * D * 2;
+  constexpr int WARP_BYTES = S * STAGE_BYTES + 2 * 16 * D * 2;  // + two V tiles
   extern __shared__ __align__(128) uint8_t smem_raw[];
   uint32_t* qfrag = reinterpret_cast<uint32_t*>(smem_raw);
   float* qsum = reinterpret_cast<float*>(qfrag + MT * 8 * 32 * 8);
@@ -832,18 +835,19 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
                    "l"(a.vscale + soff + lane * 8), "r"(bytes));
     }
   };
-  // the first S-1 pages of this warp into the ring; pages holding only tokens of earlier
+  // the first PRO pages of this warp into the ring; pages holding only tokens of earlier
   // steps (the previous kernel appends this step's) are fetched before the dependency wait
+  constexpr int PRO = S - 2;  // pages in flight beyond the pair being processed
   int pre = 0;
   const int old_end = L - a.Lq;  // positions below this were written by earlier steps
-  for (; pre < S - 1; ++pre) {
+  for (; pre < PRO; ++pre) {
     const int pgs = pg0 + warp + 4 * pre;
     if (pgs >= pg1 || (pgs + 1) * 16 > old_end) break;
     issue(pgs, pre);
     cp_async_commit();
   }
   pdl_wait();
-  for (; pre < S - 1; ++pre) {
+  for (; pre < PRO; ++pre) {
     const int pgs = pg0 + warp + 4 * pre;
     if (pgs < pg1) issue(pgs, pre);
     cp_async_commit();
@@ -923,71 +927,80 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
     }
   }
 
-  uint16_t* vtile = reinterpret_cast<uint16_t*>(my + S * STAGE_BYTES);
-  int i = 0;
-  for (int pg = pg0 + warp; pg < pg1; pg += 4, ++i) {
-    const int stage = i % S;
-    const int nxt = pg + 4 * (S - 1);
-    if (nxt < pg1) issue(nxt, (i + S - 1) % S);
-    cp_async_commit();
-    cp_async_wait<S - 1>();
-    __syncwarp();
-    const uint8_t* kc = kcb(stage);
-    const uint8_t* vcc = vcb(stage);
-    const __half* ks = ksb(stage);
-    const __half* vs = vsb(stage);
-    const int valid = min(16, L - pg * 16);
-    // expand V codes to exact bf16 (c - 8): lane -> token lane/2, half lane&1
-    {
-      const int r = lane >> 1, hlf = lane & 1;
-      const uint4* src = reinterpret_cast<const uint4*>(vcc + r * 64 + hlf * 32);
+  // two pages per iteration: their score chains interleave and one online-softmax update
+  // covers both (32 keys); a page past the split is empty (its keys are masked)
+  uint16_t* vtile0 = reinterpret_cast<uint16_t*>(my + S * STAGE_BYTES);
+  uint16_t* vtile1 = vtile0 + 16 * D;
+  auto expand_v = [&](int st, uint16_t* vtile) {
+    // V codes to exact bf16 (c - 8): lane -> token lane/2, half lane&1
+    const int r = lane >> 1, hlf = lane & 1;
+    const uint4* src = reinterpret_cast<const uint4*>(vcb(st) + r * 64 + hlf * 32);
 #pragma unroll
-      for (int v4 = 0; v4 < 2; ++v4) {
-        const uint4 w4 = src[v4];
-        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+    for (int v4 = 0; v4 < 2; ++v4) {
+      const uint4 w4 = src[v4];
+      const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-        for (int wi = 0; wi < 4; ++wi) {
-          const int chunk = hlf * 8 + v4 * 4 + wi;
-          const uint32_t off136 = 0x43084308u;  // bf16 pair (136, 136)
-          uint4 outv;
-          uint32_t p0 = nib_pair_bf16<0>(ws[wi]), p1 = nib_pair_bf16<4>(ws[wi]);
-          uint32_t p2 = nib_pair_bf16<8>(ws[wi]), p3 = nib_pair_bf16<12>(ws[wi]);
-          __nv_bfloat162 o0 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p0),
-                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
-          __nv_bfloat162 o1 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p1),
-                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
-          __nv_bfloat162 o2 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p2),
-                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
-          __nv_bfloat162 o3 = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p3),
-                                      *reinterpret_cast<const __nv_bfloat162*>(&off136));
-          outv.x = *reinterpret_cast<uint32_t*>(&o0);
-          outv.y = *reinterpret_cast<uint32_t*>(&o1);
-          outv.z = *reinterpret_cast<uint32_t*>(&o2);
-          outv.w = *reinterpret_cast<uint32_t*>(&o3);
-          *reinterpret_cast<uint4*>(vtile + r * D + swz(r, chunk) * 8) = outv;
+      for (int wi = 0; wi < 4; ++wi) {
+        const int chunk = hlf * 8 + v4 * 4 + wi;
+        const uint32_t off136 = 0x43084308u;  // bf16 pair (136, 136)
+        const __nv_bfloat162 o136 = *reinterpret_cast<const __nv_bfloat162*>(&off136);
+        uint32_t p[4] = {nib_pair_bf16<0>(ws[wi]), nib_pair_bf16<4>(ws[wi]), nib_pair_bf16<8>(ws[wi]),
+                         nib_pair_bf16<12>(ws[wi])};
+        uint32_t q[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __nv_bfloat162 d = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&p[e]), o136);
+          q[e] = *reinterpret_cast<const uint32_t*>(&d);
         }
+        *reinterpret_cast<uint4*>(vtile + r * D + swz(r, chunk) * 8) = make_uint4(q[0], q[1], q[2], q[3]);
       }
     }
+  };
+
+  int j = 0;  // this warp's local page index (the pair j, j + 1)
+  for (int pg = pg0 + warp; pg < pg1; pg += 8, j += 2) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {  // refill the slots the previous pair released
+      const int p2 = pg + 4 * (PRO + u);
+      if (p2 < pg1) issue(p2, (j + PRO + u) % S);
+      cp_async_commit();
+    }
+    cp_async_wait<PRO>();  // pages j and j + 1 have landed
     __syncwarp();
-    // per-token scales for the S columns this lane owns
-    float ksc[2][2], vsc[2][2];
+    const int st0 = j % S, st1 = (j + 1) % S;
+    const int pgp[2] = {pg, pg + 4};
+    expand_v(st0, vtile0);
+    expand_v(st1, vtile1);
+    __syncwarp();
+    // per-token scales of the key columns this lane owns (n-tiles 0-1 page a, 2-3 page b)
+    float ksc[4][2], vsc[4][2];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int pp = 0; pp < 2; ++pp) {
+      // a second page past this split's range (it may still be in the sequence) is empty
+      const int valid = pgp[pp] < pg1 ? min(16, L - pgp[pp] * 16) : 0;
+      const __half* ks = ksb(pp ? st1 : st0);
+      const __half* vs = vsb(pp ? st1 : st0);
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int j = nt * 8 + 2 * t + e;
-        ksc[nt][e] = j < valid ? __half2float(ks[j]) : 0.0f;
-        vsc[nt][e] = j < valid ? __half2float(vs[j]) : 0.0f;
-      }
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int jj = nt * 8 + 2 * t + e;
+          ksc[2 * pp + nt][e] = jj < valid ? __half2float(ks[jj]) : 0.0f;
+          vsc[2 * pp + nt][e] = jj < valid ? __half2float(vs[jj]) : 0.0f;
+        }
+    }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      // the hi and lo halves of q' accumulate separately: two short MMA chains per
-      // 8-key block instead of one of 16
-      float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      float sl[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      // the hi and lo halves of q' accumulate separately: short, independent MMA chains
+      float s[4][4], sl[4][4];
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const uint4 kw = *reinterpret_cast<const uint4*>(kc + (nt * 8 + g) * 64 + 16 * t);
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) s[nt][c] = sl[nt][c] = 0.0f;
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt) {
+        const uint8_t* kc = kcb((nt >> 1) ? st1 : st0);
+        const uint4 kw = *reinterpret_cast<const uint4*>(kc + ((nt & 1) * 8 + g) * 64 + 16 * t);
         const uint32_t kws[4] = {kw.x, kw.y, kw.z, kw.w};
 #pragma unroll
         for (int kt = 0; kt < 8; ++kt) {
@@ -1008,18 +1021,14 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
         }
       }
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int c = 0; c < 4; ++c) s[nt][c] += sl[nt][c];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
+      for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const int j = pg * 16 + nt * 8 + 2 * t + (c & 1);
+          const int jk = pgp[nt >> 1] * 16 + (nt & 1) * 8 + 2 * t + (c & 1);
           const int row = mt * 16 + g + 8 * (c >> 1);
           const int qpos = L - a.Lq + a.tq0 + row / G;
-          const bool ok = row < R && j <= qpos;
-          const float raw = s[nt][c] - 136.0f * qs[mt][c >> 1];
+          const bool ok = row < R && jk <= qpos && pgp[nt >> 1] < pg1;
+          const float raw = (s[nt][c] + sl[nt][c]) - 136.0f * qs[mt][c >> 1];
           s[nt][c] = ok ? raw * ksc[nt][c & 1] * a.scale_log2 : -INFINITY;
         }
       float alpha[2];
@@ -1031,22 +1040,29 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
         o[mt][dt][2] *= alpha[1];
         o[mt][dt][3] *= alpha[1];
       }
-      // P scaled by the per-token V scale
-      uint32_t ph[4], pl[4];
-      split_bf2(s[0][0] * vsc[0][0], s[0][1] * vsc[0][1], ph[0], pl[0]);
-      split_bf2(s[0][2] * vsc[0][0], s[0][3] * vsc[0][1], ph[1], pl[1]);
-      split_bf2(s[1][0] * vsc[1][0], s[1][1] * vsc[1][1], ph[2], pl[2]);
-      split_bf2(s[1][2] * vsc[1][0], s[1][3] * vsc[1][1], ph[3], pl[3]);
+      // P scaled by the per-token V scale; page a's keys are the first k-step, page b's the second
+      uint32_t ph[2][4], pl[2][4];
+#pragma unroll
+      for (int pp = 0; pp < 2; ++pp) {
+        const int n0 = 2 * pp;
+        split_bf2(s[n0][0] * vsc[n0][0], s[n0][1] * vsc[n0][1], ph[pp][0], pl[pp][0]);
+        split_bf2(s[n0][2] * vsc[n0][0], s[n0][3] * vsc[n0][1], ph[pp][1], pl[pp][1]);
+        split_bf2(s[n0 + 1][0] * vsc[n0 + 1][0], s[n0 + 1][1] * vsc[n0 + 1][1], ph[pp][2], pl[pp][2]);
+        split_bf2(s[n0 + 1][2] * vsc[n0 + 1][0], s[n0 + 1][3] * vsc[n0 + 1][1], ph[pp][3], pl[pp][3]);
+      }
 #pragma unroll
       for (int d2 = 0; d2 < D / 16; ++d2) {
-        uint32_t vb[4];
         const int mi = lane >> 3;
         const int tok = (mi & 1) * 8 + (lane & 7);
-        ldmatrix_x4_trans(vb, vtile + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
-        mma_bf16_16816(o[mt][2 * d2], ph[0], ph[1], ph[2], ph[3], vb[0], vb[1]);
-        mma_bf16_16816(o[mt][2 * d2 + 1], ph[0], ph[1], ph[2], ph[3], vb[2], vb[3]);
-        mma_bf16_16816(o[mt][2 * d2], pl[0], pl[1], pl[2], pl[3], vb[0], vb[1]);
-        mma_bf16_16816(o[mt][2 * d2 + 1], pl[0], pl[1], pl[2], pl[3], vb[2], vb[3]);
+#pragma unroll
+        for (int pp = 0; pp < 2; ++pp) {
+          uint32_t vb[4];
+          ldmatrix_x4_trans(vb, (pp ? vtile1 : vtile0) + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
+          mma_bf16_16816(o[mt][2 * d2], ph[pp][0], ph[pp][1], ph[pp][2], ph[pp][3], vb[0], vb[1]);
+          mma_bf16_16816(o[mt][2 * d2 + 1], ph[pp][0], ph[pp][1], ph[pp][2], ph[pp][3], vb[2], vb[3]);
+          mma_bf16_16816(o[mt][2 * d2], pl[pp][0], pl[pp][1], pl[pp][2], pl[pp][3], vb[0], vb[1]);
+          mma_bf16_16816(o[mt][2 * d2 + 1], pl[pp][0], pl[pp][1], pl[pp][2], pl[pp][3], vb[2], vb[3]);
+        }
       }
     }
     __syncwarp();
@@ -1106,7 +1122,7 @@ static size_t smem_bf16(int D, int MT) {
 
 static size_t smem_tq4(int MT) {
   const size_t head = (size_t)MT * 8 * 32 * 8 * 4 + 16 * MT * 4;
-  const size_t warps = (size_t)4 * (kTq4Stages * (1024 + 1024 + 32 + 32) + 16 * 128 * 2);
+  const size_t warps = (size_t)4 * (kTq4Stages * (1024 + 1024 + 32 + 32) + 2 * 16 * 128 * 2);
   const size_t qrot = (size_t)16 * MT * 128 * 4;
   const size_t merge = (size_t)(9 * 16 * MT + 4 * 16 * MT * 128) * 4;
   size_t body = warps + qrot;  // the query scratch follows the rings
