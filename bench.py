@@ -401,6 +401,24 @@ def kernel_case(opt):
             for kc, vc in caches:
                 ops.fused_attention(qkv, Hq, Hkv, D, qn, qn, a.rms_norm_eps, pos, inv, slots, kc, vc, bt,
                                     sl, L)
+    elif case == "attention_tq4":  # C5 shapes: B=16, ctx 32768, TurboQuant pages
+        B, Hq, Hkv, L = 16, a.num_attention_heads, a.num_key_value_heads, 32768
+        maxb = L // 16
+        P = B * maxb
+        caches = []
+        for _ in range(2):  # 2 x 1.1 GB of codes: no launch finds its pages in L2
+            caches.append((torch.randint(0, 256, (P, Hkv, 16, 64), dtype=torch.uint8, device=dev),
+                           (torch.rand(P, Hkv, 16, device=dev) * 0.1).to(torch.float16),
+                           torch.randint(0, 256, (P, Hkv, 16, 64), dtype=torch.uint8, device=dev),
+                           (torch.rand(P, Hkv, 16, device=dev) * 0.1).to(torch.float16)))
+        q = torch.randn(B, 1, Hq, 128, device=dev).to(torch.bfloat16)
+        bt = torch.arange(P, dtype=torch.int32, device=dev).view(B, maxb)
+        sl = torch.full((B,), L, dtype=torch.int32, device=dev)
+        signs = torch.where(torch.rand(128, device=dev) < 0.5, -1, 1).to(torch.int8)
+        ws = ops.attention_workspace(B, 1, Hq, Hkv, 128, L, dev)
+        for it in range(3):
+            for kc, ks, vc, vs in caches:
+                ops.paged_attention_tq4(q, kc, ks, vc, vs, bt, sl, L, signs, workspace=ws)
     elif case == "argmax":
         lg = torch.randn(1, a.vocab_size, device=dev)
         for it in range(3):
