@@ -83,9 +83,11 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_kernel(CommArgs c, int
       }
     }
   }
-  __threadfence_system();
+  // the barrier orders every thread's pushes before the flag writers; one system-scope
+  // fence per flag writer then publishes them (measured: per-thread fences cost ~3 us a call)
   __syncthreads();
   if (threadIdx.x < c.world) {
+    __threadfence_system();
     unsigned* f = reinterpret_cast<unsigned*>(c.peer[threadIdx.x]) +
                   ((size_t)call * c.world + c.rank) * c.max_ctas + blockIdx.x;
     st_release_sys(f, s);
@@ -107,11 +109,39 @@ __global__ void __launch_bounds__(kCommThreads) allreduce_kernel(CommArgs c, int
   const uint32_t* mine = reinterpret_cast<const uint32_t*>(c.peer[c.rank] + c.flag_bytes) +
                          (size_t)call * c.world * c.words;
   if (MODE == AR_SUM_RESIDUAL) {
+    // 4 words per thread: every rank's partial and the residual are loaded together (one
+    // round trip), then summed in rank order -- the same bits as one element at a time
+    // (the residual is read 8 bytes at a time only when it is 8-byte aligned; slots always are)
     uint16_t* h = static_cast<uint16_t*>(out);
-    for (int i = w0 + threadIdx.x; i < w1; i += kCommThreads) {
-      float y = 0.f;
-      for (int q = 0; q < c.world; ++q) y += __uint_as_float(__ldcg(mine + (size_t)q * c.words + i));
-      h[i] = f2bf(bf2f(h[i]) + round_bf(y));
+    const bool h8 = (reinterpret_cast<uintptr_t>(h) & 7) == 0;
+    for (int i = w0 + 4 * threadIdx.x; i < w1; i += 4 * kCommThreads) {
+      if (h8 && i + 4 <= w1) {
+        float4 v[kMaxRanks];
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+          if (q < c.world) v[q] = __ldcg(reinterpret_cast<const float4*>(mine + (size_t)q * c.words + i));
+        const uint2 hv = *reinterpret_cast<const uint2*>(h + i);
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int q = 0; q < kMaxRanks; ++q)
+          if (q < c.world) {
+            y[0] += v[q].x;
+            y[1] += v[q].y;
+            y[2] += v[q].z;
+            y[3] += v[q].w;
+          }
+        const uint32_t w0v = ((uint32_t)f2bf(bf2f((uint16_t)(hv.x & 0xFFFF)) + round_bf(y[0]))) |
+                             ((uint32_t)f2bf(bf2f((uint16_t)(hv.x >> 16)) + round_bf(y[1])) << 16);
+        const uint32_t w1v = ((uint32_t)f2bf(bf2f((uint16_t)(hv.y & 0xFFFF)) + round_bf(y[2]))) |
+                             ((uint32_t)f2bf(bf2f((uint16_t)(hv.y >> 16)) + round_bf(y[3])) << 16);
+        *reinterpret_cast<uint2*>(h + i) = make_uint2(w0v, w1v);
+      } else {
+        for (int e = i; e < min(i + 4, w1); ++e) {
+          float y = 0.f;
+          for (int q = 0; q < c.world; ++q) y += __uint_as_float(__ldcg(mine + (size_t)q * c.words + e));
+          h[e] = f2bf(bf2f(h[e]) + round_bf(y));
+        }
+      }
     }
   } else {
     int32_t* o = static_cast<int32_t*>(out);
