@@ -98,6 +98,10 @@ cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st);
 bool l2_prefetch_next();
 bool l2_prefetch_self();
 bool qgemv_ring_can_fuse_norm(int M, int K);
+// M == 1 (decode at batch 1): the register-fed GEMV of qgemv_m1.cu; launch_qgemv_ring routes there itself.
+bool qgemv_m1_supported(const QLinArgs& a);
+cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st);
+void qgemv_m1_set(int on, int wk, int depth, int l2, int persist);  // -1 leaves a setting as it is
 // M >= 17: the tcgen05 matrix path (qgemm_tc.cu); launch_qgemv_ring routes there itself.
 bool qgemm_tc_supported(const QLinArgs& a);
 size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu);

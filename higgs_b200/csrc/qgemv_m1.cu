@@ -1,0 +1,497 @@
+// qgemv_m1.cu -- W4 g64 GEMV for a single token (decode at batch 1): packed
+// weights loaded straight into registers, the quantization groups carried in
+// the MMA's output columns.
+//
+// Reference op replaced: ops::quantized_matmul (qwen3_next.rs:174-183) at one
+// token, with the preceding nn::RmsNorm (transformer.rs:407, 415) optionally fused.
+//
+// One token leaves seven of the eight MMA columns of m16n8k16 idle; this kernel
+// uses them to keep groups apart instead.  A warp owns 16 rows (fragment rows g
+// and g+8) and a K range in units of 256 (4 groups of 64).  Per unit and row,
+// the four quad lanes t load 64 contiguous bytes twice (LDG.128 at bytes
+// 64h + 16t, h = 0, 1), so in the MMAs of half h lanes t = 0, 1 carry group 2h
+// and lanes 2, 3 group 2h + 1.  The B operand routes group j of an even unit
+// into output column j and of an odd unit into column 4 + j (the B fragment of
+// column c is zero except in the two lanes (c, t) whose data is group c % 4), so
+// the 32 MMAs of a unit pair build the 8 (row x group) dot products of each row
+// pair in one accumulator, and the per-group fold
+//     y += s * acc + (b - 128 s) * sum(x)
+// runs once per unit pair over fully used accumulators.  Weights enter the MMA
+// as the exact bf16 values 128 + q (one shift and one LOP3 per pair of codes);
+// x enters as bf16 itself, so staging it is a permutation (plus the fused
+// RMSNorm): one pass, no scaling.  Per unit a warp issues 4 LDG.128, 112 ALU
+// unpack ops, 16 mma.sync and 8 LDS.128 (x fragments; lanes whose column is
+// unused read a zero block); the next D units of weights stay in flight in
+// registers, and the first D are requested before the kernel waits on its
+// predecessor.  Before the wait each CTA also asks L2 for every weight byte it
+// will stream (cp.async.bulk.prefetch), so HBM streams the CTA's whole slice from
+// its start while the register ring reads L2.  CTAs walk tile groups round-robin
+// (one group each by default; optionally a grid capped at the resident slots).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace higgs {
+
+namespace {
+
+constexpr int kM1Threads = 256;
+constexpr int kM1MaxK = 32768;  // staged x: K / 256 * 512 B + sums + 1 KB
+constexpr int kM1RegChunks = 4;   // fused norm: x chunks held in registers between the passes (K <= 8192)
+constexpr int kM1NormChunks = 2;  // fused norm: norm-weight chunks loaded before the wait (K <= 4096)
+
+struct M1Seg {
+  const uint32_t* W;
+  const uint16_t* S;
+  const uint16_t* B;
+  int row0;
+};
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D (f32); no side effects, so the
+// compiler may schedule it freely among the unpack ops
+__device__ __forceinline__ void m1_mma(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                       uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 m1_lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(addr));
+  return v;
+}
+
+__host__ __device__ inline size_t m1_xf_bytes(int K) { return (size_t)(K / 256) * 512; }
+// x fragments | 64 pad | 512 B of zeros (at 64 mod 128) | 64 pad | sum(x) per group | reduction [8][16]
+inline size_t m1_smem_bytes(int K) { return m1_xf_bytes(K) + 640 + (size_t)(K / 64) * 4 + 8 * 16 * 4; }
+
+// B fragments of chunk x[8c .. 8c+7]: (x0, x4) (x1, x5) (x2, x6) (x3, x7), the pairs the
+// A side forms from one word of codes (nibbles i and i + 4 of each word)
+__device__ __forceinline__ uint4 m1_frag(uint4 v) {
+  return make_uint4(prmt(v.x, v.z, 0x5410), prmt(v.x, v.z, 0x7632), prmt(v.y, v.w, 0x5410),
+                    prmt(v.y, v.w, 0x7632));
+}
+
+// WK warps split the K range of each 16-row tile; RT = 8 / WK tiles per CTA (SwiGLU: RT / 2
+// gate/up pairs).  D units of weights in flight per warp (even).
+template <int WK, int EPI, bool NORM, int D>
+__global__ void __launch_bounds__(kM1Threads, 2) qgemv_m1_kernel(QLinArgs a) {
+  static_assert(D % 2 == 0, "units are folded in pairs");
+  constexpr int RT = 8 / WK;
+  constexpr int ROT = (EPI == EPI_SWIGLU) ? RT / 2 : RT;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int rt = warp / WK, kw = warp % WK;
+  const int K = a.K, N = a.N, KW = K / 8, G = K / 64;
+  const int units = K / 256;
+
+  uint8_t* xf = smem;
+  uint8_t* zero = smem + m1_xf_bytes(K) + 64;
+  float* xs = reinterpret_cast<float*>(zero + 576);  // sum(x) per group
+  float* red = xs + G;                               // [8 warps][16 rows]
+
+  // tile groups (ROT output tiles each) are dealt round-robin to the resident CTAs
+  const int n_groups = (N / 16 + ROT - 1) / ROT;
+  // this warp's 16-row tile of group grp and its K range [ub, ue) (empty past N)
+  struct Tile {
+    M1Seg sg;
+    int ub, ue;
+  };
+  auto tile_of = [&](int grp) {
+    Tile tl;
+    int out_tile, which = 0;
+    if (EPI == EPI_SWIGLU) {
+      out_tile = grp * ROT + rt / 2;
+      which = rt & 1;
+    } else {
+      out_tile = grp * ROT + rt;
+    }
+    const int n0 = out_tile * 16;
+    const bool ok = n0 < N;
+    tl.sg.W = which ? a.w2 : a.w;
+    tl.sg.S = which ? a.s2 : a.s;
+    tl.sg.B = which ? a.b2 : a.b;
+    tl.sg.row0 = ok ? n0 : 0;
+    if (EPI != EPI_SWIGLU && a.nseg > 1) {
+#pragma unroll
+      for (int i = 1; i < 3; ++i)
+        if (i < a.nseg && ok && n0 >= a.seg_end[i - 1]) {
+          tl.sg.W = a.wseg[i];
+          tl.sg.S = a.sseg[i];
+          tl.sg.B = a.bseg[i];
+          tl.sg.row0 = n0 - a.seg_end[i - 1];
+        }
+    }
+    tl.ub = ok ? (units * kw) / WK : 0;
+    tl.ue = ok ? (units * (kw + 1)) / WK : 0;
+    return tl;
+  };
+
+  issue_l2_prefetch(a.pf, blockIdx.x, gridDim.x);
+  if (a.self_prefetch && lane < 16) {
+    // every K range this warp will stream, of all its groups -> L2 now: the register ring
+    // below (D units deep) then reads L2 instead of waiting on HBM round trips
+    for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
+      const Tile tl = tile_of(grp);
+      if (tl.ub >= tl.ue) continue;
+      const char* row = reinterpret_cast<const char*>(tl.sg.W + (size_t)(tl.sg.row0 + lane) * KW);
+      l2_prefetch_range(row + (size_t)tl.ub * 128, (size_t)(tl.ue - tl.ub) * 128);
+      if (lane < 2 && kw == 0) {  // the tile's scales / biases, once per tile
+        const uint16_t* sbp = lane ? tl.sg.B : tl.sg.S;
+        l2_prefetch_range(sbp + (size_t)tl.sg.row0 * G, (size_t)16 * G * 2);
+      }
+    }
+  }
+
+  // lane (g, t): rows g and g+8; per unit the 16-byte chunks t and 4 + t of the row's 128 B;
+  // scales / biases of groups (4 u0 + 2t, +1) of a unit pair starting at u0, as bf16 pairs
+  const uint4 *wg, *w8;
+  const uint32_t *sgp, *sg8, *bgp, *bg8;
+  int ub, ue;
+  auto bind = [&](const Tile& tl) {
+    ub = tl.ub;
+    ue = tl.ue;
+    wg = reinterpret_cast<const uint4*>(tl.sg.W + (size_t)(tl.sg.row0 + g) * KW) + t;
+    w8 = wg + (size_t)2 * KW;  // 8 rows further (K / 32 uint4 per row)
+    sgp = reinterpret_cast<const uint32_t*>(tl.sg.S + (size_t)(tl.sg.row0 + g) * G) + t;
+    sg8 = sgp + (size_t)4 * G;  // (8 rows * G bf16) / 2
+    bgp = reinterpret_cast<const uint32_t*>(tl.sg.B + (size_t)(tl.sg.row0 + g) * G) + t;
+    bg8 = bgp + (size_t)4 * G;
+  };
+
+  uint4 buf[D][4];
+  uint32_t sb[D / 2][4];
+  auto load_unit = [&](uint4 (&b)[4], int u) {
+    b[0] = ldg_stream_u4(wg + 8 * u);
+    b[1] = ldg_stream_u4(wg + 8 * u + 4);
+    b[2] = ldg_stream_u4(w8 + 8 * u);
+    b[3] = ldg_stream_u4(w8 + 8 * u + 4);
+  };
+  auto load_scales = [&](uint32_t (&q)[4], int u0) {
+    // this lane folds unit u0 + t/2; past the range it folds nothing (scales 0)
+    const bool ok = u0 + (t >> 1) < ue;
+    q[0] = ok ? __ldg(sgp + 2 * u0) : 0u;
+    q[1] = ok ? __ldg(sg8 + 2 * u0) : 0u;
+    q[2] = ok ? __ldg(bgp + 2 * u0) : 0u;
+    q[3] = ok ? __ldg(bg8 + 2 * u0) : 0u;
+  };
+  auto prologue = [&]() {
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      if (ub + d < ue) load_unit(buf[d], ub + d);
+      if ((d & 1) == 0) load_scales(sb[d / 2], ub + d);
+    }
+  };
+
+  // the first group's first D units and scales, and the norm weights of this thread's
+  // first chunks: none of them depends on the previous kernel
+  bind(tile_of(blockIdx.x));
+  prologue();
+  uint4 nwr[NORM ? kM1NormChunks : 1];
+  if constexpr (NORM) {
+#pragma unroll
+    for (int r = 0; r < kM1NormChunks; ++r) {
+      const int c = threadIdx.x + r * kM1Threads;
+      nwr[r] = c < K / 8 ? *reinterpret_cast<const uint4*>(a.norm_w + 8 * c) : make_uint4(0, 0, 0, 0);
+    }
+  }
+  pdl_wait();
+  pdl_launch();
+
+  if (threadIdx.x < 32) reinterpret_cast<uint4*>(zero)[threadIdx.x] = make_uint4(0, 0, 0, 0);
+  const uint16_t* x = a.x;
+  // ---- fused RMSNorm: the token's sum of squares (its chunks kept for the staging) ----
+  __shared__ float s_ss[8];
+  uint4 xr[NORM ? kM1RegChunks : 1];
+  float inv = 1.0f;
+  if constexpr (NORM) {
+    float ss = 0.f;
+#pragma unroll
+    for (int r = 0; r < kM1RegChunks; ++r) xr[r] = make_uint4(0, 0, 0, 0);
+    for (int c = threadIdx.x, r = 0; c < K / 8; c += kM1Threads, ++r) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + 8 * c);
+#pragma unroll
+      for (int j = 0; j < kM1RegChunks; ++j)
+        if (j == r) xr[j] = v;
+      const uint32_t* vp = &v.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float lo = bf_lo(vp[j]), hi = bf_hi(vp[j]);
+        ss += lo * lo + hi * hi;
+      }
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) s_ss[warp] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) tot += s_ss[w];
+    inv = 1.0f / sqrtf(tot / (float)K + a.eps);
+  }
+
+  // ---- x fragments: chunk c = 32u + 16h + 4t + e (x[8c .. 8c+7]) at
+  // xf + ((u * 8 + h * 4 + e) * 4 + t) * 16; sum(x) per group (8 consecutive chunks).
+  // Whole warps iterate (K / 8 is a multiple of 32).
+  for (int base = warp * 32, r = 0; base < K / 8; base += kM1Threads, ++r) {
+    const int c = base + lane;
+    uint4 v;
+    if constexpr (NORM) {
+      v = xr[0];
+#pragma unroll
+      for (int j = 1; j < kM1RegChunks; ++j)
+        if (j == r) v = xr[j];
+      if (r >= kM1RegChunks) v = *reinterpret_cast<const uint4*>(x + 8 * c);
+      uint4 wv = nwr[0];
+#pragma unroll
+      for (int j = 1; j < kM1NormChunks; ++j)
+        if (j == r) wv = nwr[j];
+      if (r >= kM1NormChunks) wv = *reinterpret_cast<const uint4*>(a.norm_w + 8 * c);
+      uint32_t* vp = &v.x;
+      const uint32_t* wp = &wv.x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        vp[j] = pack_bf2(bf_lo(vp[j]) * inv * bf_lo(wp[j]), bf_hi(vp[j]) * inv * bf_hi(wp[j]));
+    } else {
+      v = *reinterpret_cast<const uint4*>(x + 8 * c);
+    }
+    const int u = c >> 5, h = (c >> 4) & 1, tt = (c >> 2) & 3, e = c & 3;
+    *reinterpret_cast<uint4*>(xf + ((u * 8 + h * 4 + e) * 4 + tt) * 16) = m1_frag(v);
+    const uint32_t* vp = &v.x;
+    float x1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x1 += bf_lo(vp[j]) + bf_hi(vp[j]);
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) x1 += __shfl_xor_sync(0xffffffffu, x1, o);
+    if ((lane & 7) == 0) xs[c >> 3] = x1;
+  }
+  __syncthreads();
+
+  // lane (g, t) supplies B column g: in half h of a unit of parity p it carries data iff
+  // g == 4p + 2h + t/2, else it reads the zero block
+  const uint32_t xreal = smem_u32(xf) + t * 16;
+  const uint32_t xzero = smem_u32(zero);
+  const float2* xs2 = reinterpret_cast<const float2*>(xs);
+
+  for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
+    if (grp != (int)blockIdx.x) {
+      bind(tile_of(grp));
+      prologue();
+    }
+    float acc[2][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[h][c] = 0.f;
+    float yg = 0.f, yg8 = 0.f;
+
+    // ---- main loop over this warp's units ----
+    for (int base = ub; base < ue; base += D) {
+#pragma unroll
+      for (int d = 0; d < D; ++d) {
+        const int u = base + d;
+        if (u >= ue) break;  // uniform over the warp
+        const int p = d & 1;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const bool act = g == 4 * p + 2 * h + (t >> 1);
+          const uint32_t xb = (act ? xreal + u * 512 : xzero) + h * 256;
+          uint4 xv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) xv[e] = m1_lds128(xb + e * 64);
+          const uint32_t* wa = &buf[d][h].x;
+          const uint32_t* wb = &buf[d][2 + h].x;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t A = wa[e], B = wb[e];
+            m1_mma(acc[h], nib_pair_bf16<0>(A), nib_pair_bf16<0>(B), nib_pair_bf16<4>(A),
+                   nib_pair_bf16<4>(B), xv[e].x, xv[e].y);
+            m1_mma(acc[h], nib_pair_bf16<8>(A), nib_pair_bf16<8>(B), nib_pair_bf16<12>(A),
+                   nib_pair_bf16<12>(B), xv[e].z, xv[e].w);
+          }
+        }
+        // buffer d is consumed: request unit u + D into it
+        if (u + D < ue) load_unit(buf[d], u + D);
+        if (p == 1 || u + 1 == ue) {
+          // fold the pair (u0, u0 + 1): lane t holds columns 2t, 2t+1 = groups 4 u0 + 2t, +1;
+          // the MMA saw 128 + q, so y += s * acc + (b - 128 s) * sum(x)
+          const int u0 = u - p;
+          const bool ok = u0 + (t >> 1) < ue;
+          const float2 X = xs2[ok ? 2 * u0 + t : 0];
+          const uint32_t* q = sb[d / 2];
+          const float sa = bf_lo(q[0]), sb_ = bf_hi(q[0]), s8a = bf_lo(q[1]), s8b = bf_hi(q[1]);
+          const float ba = fmaf(-128.0f, sa, bf_lo(q[2])), bb = fmaf(-128.0f, sb_, bf_hi(q[2]));
+          const float b8a = fmaf(-128.0f, s8a, bf_lo(q[3])), b8b = fmaf(-128.0f, s8b, bf_hi(q[3]));
+          yg = fmaf(sa, acc[0][0] + acc[1][0], fmaf(ba, X.x, yg));
+          yg = fmaf(sb_, acc[0][1] + acc[1][1], fmaf(bb, X.y, yg));
+          yg8 = fmaf(s8a, acc[0][2] + acc[1][2], fmaf(b8a, X.x, yg8));
+          yg8 = fmaf(s8b, acc[0][3] + acc[1][3], fmaf(b8b, X.y, yg8));
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) acc[h][c] = 0.f;
+          if (u0 + D < ue) load_scales(sb[d / 2], u0 + D);
+        }
+      }
+    }
+
+    // ---- reduction over the quad, then over the K-split warps ----
+    yg += __shfl_xor_sync(0xffffffffu, yg, 1);
+    yg += __shfl_xor_sync(0xffffffffu, yg, 2);
+    yg8 += __shfl_xor_sync(0xffffffffu, yg8, 1);
+    yg8 += __shfl_xor_sync(0xffffffffu, yg8, 2);
+    if (t == 0) {
+      red[warp * 16 + g] = yg;
+      red[warp * 16 + g + 8] = yg8;
+    }
+    __syncthreads();
+    if ((int)threadIdx.x < ROT * 16) {
+      const int r = threadIdx.x >> 4, j = threadIdx.x & 15;
+      const int tile = grp * ROT + r;
+      const int row = tile * 16 + j;
+      if (tile * 16 < N) {
+        if (EPI == EPI_SWIGLU) {
+          float vg = 0.f, vu = 0.f;
+#pragma unroll
+          for (int w = 0; w < WK; ++w) {
+            vg += red[((2 * r) * WK + w) * 16 + j];
+            vu += red[((2 * r + 1) * WK + w) * 16 + j];
+          }
+          const float gv = round_bf(vg), uv = round_bf(vu);
+          a.y[row] = f2bf(gv / (1.0f + expf(-gv)) * uv);
+        } else {
+          float v = 0.f;
+#pragma unroll
+          for (int w = 0; w < WK; ++w) v += red[(r * WK + w) * 16 + j];
+          if (a.y_f32) a.y_f32[row] = v;
+          if (a.y) {
+            uint16_t o = f2bf(v);
+            if (a.residual) o = f2bf(bf2f(o) + bf2f(a.residual[row]));
+            a.y[row] = o;
+          }
+        }
+      }
+    }
+    __syncthreads();  // red is rewritten by the next group
+  }
+}
+
+bool g_m1_on = true;
+bool g_m1_l2 = true;  // each CTA prefetches its whole weight slice to L2 before the wait
+int g_m1_wk = 0;      // forced K split (1, 2, 4, 8), 0 = cost model
+int g_m1_depth = 2;   // units in flight per warp (2 or 4)
+// grid capped at the resident slots, CTAs looping over tile groups; off = one CTA per group.
+// Measured on B200 (B=1 Qwen3-8B step, same box): one CTA per group with the L2 prefetch
+// 2.278 ms, capped grid 2.326 (no prefetch) / 2.369 (prefetch), one CTA per group without
+// the prefetch 2.426, the multi-token ring kernel 2.415
+bool g_m1_persist = false;
+
+template <int WK, int EPI, bool NORM, int D>
+cudaError_t m1_launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
+  auto k = qgemv_m1_kernel<WK, EPI, NORM, D>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  return launch_pdl(k, dim3(ctas), dim3(kM1Threads), smem, st, a);
+}
+
+template <int EPI, bool NORM, int D>
+cudaError_t m1_launch_d(const QLinArgs& a_in, cudaStream_t st) {
+  QLinArgs a = a_in;
+  if (g_m1_l2) a.self_prefetch = 1;
+  const int nrt = a.N / 16;
+  const int units = a.K / 256;
+  const size_t smem = m1_smem_bytes(a.K);
+  const int slots = 2 * sm_count();  // two CTAs per SM (register bound); the grid never exceeds it
+  // Cost of a K split: the resident CTAs' iterations over tile groups x (units per warp + 1,
+  // the per-group reduction); ties go to more splits (more warps streaming).  It picks the
+  // split measured fastest on B200 for each Qwen3-8B shape (qkv 4, o_proj / down 8,
+  // gate/up 4, LM head 2).
+  const int max_wk = EPI == EPI_SWIGLU ? 4 : 8;
+  int wk = 1;
+  long long best = -1;
+  for (int c = 1; c <= max_wk && c <= units; c *= 2) {
+    const int rot = EPI == EPI_SWIGLU ? (8 / c) / 2 : 8 / c;
+    const long long groups = (nrt + rot - 1) / rot;
+    const long long cost = (groups + slots - 1) / slots * ((units + c - 1) / c + 1);
+    if (best < 0 || cost <= best) {
+      best = cost;
+      wk = c;
+    }
+  }
+  if (!g_m1_persist) {
+    // One CTA per group.  Single matrices: the most K splits whose CTAs fit one wave, so
+    // every CTA is resident (and has asked L2 for its whole slice) from the start; wider
+    // outputs take wk = 1.  Gate/up (twice the bytes per row tile): the fewest splits that
+    // fill every slot -- at wk = 1 its 57 MB is not in L2 by the time its input is.
+    // Per-launch times inside the B=1 Qwen3-8B step on B200 (us, by wk 1/2/4/8): qkv
+    // 12.6/9.5/6.0/8.7, o_proj 14.8/9.6/6.0/4.7, down 32.1/24.4/18.8/12.0, LM head
+    // 89/96/120/178; gate/up wk 2 20.7, wk 1 25.7 (18.9 only behind a slow o_proj)
+    if (EPI == EPI_SWIGLU) {
+      wk = max_wk;
+      for (int c = 1; c <= max_wk; c *= 2) {
+        const int rot = (8 / c) / 2;
+        if ((nrt + rot - 1) / rot >= slots) {
+          wk = c;
+          break;
+        }
+      }
+    } else {
+      wk = 1;
+      for (int c = max_wk; c >= 1; c /= 2)
+        if ((nrt + 8 / c - 1) / (8 / c) <= slots) {
+          wk = c;
+          break;
+        }
+    }
+  }
+  if (g_m1_wk > 0) wk = g_m1_wk > max_wk ? max_wk : g_m1_wk;
+  while (wk > 1 && units < wk) wk >>= 1;
+  const int rot = EPI == EPI_SWIGLU ? (8 / wk) / 2 : 8 / wk;
+  const int groups = (nrt + rot - 1) / rot;
+  const int ctas = (g_m1_persist && groups > slots) ? slots : groups;
+  switch (wk) {
+    case 8:
+      if constexpr (EPI != EPI_SWIGLU) return m1_launch_cfg<8, EPI, NORM, D>(a, ctas, smem, st);
+      return cudaErrorInvalidValue;
+    case 4: return m1_launch_cfg<4, EPI, NORM, D>(a, ctas, smem, st);
+    case 2: return m1_launch_cfg<2, EPI, NORM, D>(a, ctas, smem, st);
+    default: return m1_launch_cfg<1, EPI, NORM, D>(a, ctas, smem, st);
+  }
+}
+
+template <int EPI, bool NORM>
+cudaError_t m1_launch_norm(const QLinArgs& a, cudaStream_t st) {
+  return g_m1_depth == 4 ? m1_launch_d<EPI, NORM, 4>(a, st) : m1_launch_d<EPI, NORM, 2>(a, st);
+}
+
+}  // namespace
+
+// One token, not a grouped-expert launch, K within the staged-x limit.
+bool qgemv_m1_supported(const QLinArgs& a) {
+  return g_m1_on && a.M == 1 && a.moe_items == nullptr && a.K % 256 == 0 && a.K <= kM1MaxK &&
+         a.N % 16 == 0;
+}
+
+cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st) {
+  if (!qgemv_m1_supported(a)) return cudaErrorInvalidValue;
+  if (epi == EPI_SWIGLU)
+    return a.norm_w ? m1_launch_norm<EPI_SWIGLU, true>(a, st) : m1_launch_norm<EPI_SWIGLU, false>(a, st);
+  return a.norm_w ? m1_launch_norm<EPI_STORE, true>(a, st) : m1_launch_norm<EPI_STORE, false>(a, st);
+}
+
+void qgemv_m1_set(int on, int wk, int depth, int l2, int persist) {
+  if (persist >= 0) g_m1_persist = persist != 0;
+  if (l2 >= 0) g_m1_l2 = l2 != 0;
+  if (on >= 0) g_m1_on = on != 0;
+  if (wk >= 0) g_m1_wk = (wk == 1 || wk == 2 || wk == 4 || wk == 8) ? wk : 0;
+  if (depth >= 0) g_m1_depth = depth == 4 ? 4 : 2;
+}
+
+}  // namespace higgs

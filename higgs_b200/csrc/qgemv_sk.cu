@@ -389,6 +389,25 @@ extern "C" int higgs_rmsnorm_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M,
   if (workspace_bytes < need)
     return fail(HIGGS_ERR_WORKSPACE, "higgs_rmsnorm_qlinear_w4g64: workspace too small (need " +
                                          std::to_string(need) + " bytes)");
+  if (M == 1) {  // one token: the register-fed GEMV (no workspace use)
+    QLinArgs q = {};
+    q.x = (const uint16_t*)x;
+    q.M = 1;
+    q.K = K;
+    q.N = N;
+    q.w = w;
+    q.s = (const uint16_t*)scales;
+    q.b = (const uint16_t*)biases;
+    q.y = (uint16_t*)y;
+    q.y_f32 = y_f32;
+    q.residual = (const uint16_t*)residual;
+    q.norm_w = (const uint16_t*)norm_w;
+    q.eps = eps;
+    if (qgemv_m1_supported(q)) {
+      HG_CUDA(launch_qgemv_m1(q, EPI_STORE, (cudaStream_t)stream));
+      return HIGGS_OK;
+    }
+  }
   SkArgs a{};
   a.x = (const uint16_t*)x;
   a.norm_w = (const uint16_t*)norm_w;
@@ -440,6 +459,26 @@ extern "C" int higgs_rmsnorm_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M
   if (workspace_bytes < need)
     return fail(HIGGS_ERR_WORKSPACE, "higgs_rmsnorm_gate_up_swiglu: workspace too small (need " +
                                          std::to_string(need) + " bytes)");
+  if (M == 1) {  // one token: the register-fed GEMV (no workspace use)
+    QLinArgs q = {};
+    q.x = (const uint16_t*)x;
+    q.M = 1;
+    q.K = K;
+    q.N = N;
+    q.w = w_gate;
+    q.s = (const uint16_t*)s_gate;
+    q.b = (const uint16_t*)b_gate;
+    q.w2 = w_up;
+    q.s2 = (const uint16_t*)s_up;
+    q.b2 = (const uint16_t*)b_up;
+    q.y = (uint16_t*)y;
+    q.norm_w = (const uint16_t*)norm_w;
+    q.eps = eps;
+    if (qgemv_m1_supported(q)) {
+      HG_CUDA(launch_qgemv_m1(q, EPI_SWIGLU, (cudaStream_t)stream));
+      return HIGGS_OK;
+    }
+  }
   SkArgs a{};
   a.x = (const uint16_t*)x;
   a.norm_w = (const uint16_t*)norm_w;

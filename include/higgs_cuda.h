@@ -93,6 +93,14 @@ int higgs_version(void);
  * per SM (change them only between captures: workspace sizes depend on them).  "gemm_tc_rows" (default 17) moves
  * that threshold (fused-RMSNorm decode launches always stay on the GEMV).  "gemv_wk" (0, 1, 2, 4, 8; default
  * 0 = heuristic): ways each 16-row tile of the decode GEMV splits K over warps.
+ * One-token linears (M == 1, every entry above including the fused-RMSNorm ones)
+ * run the register-fed single-token GEMV: "gemv_m1" (0/1, default 1) switches it
+ * off (back to the multi-token GEMV); "gemv_m1_wk" (0, 1, 2, 4, 8; default 0 =
+ * heuristic) forces its K split; "gemv_m1_depth" (2 or 4, default 2) sets the
+ * weight units each warp keeps in flight; "gemv_m1_l2" (0/1, default 1) makes each
+ * of its CTAs ask L2 for its whole weight slice before waiting on the previous
+ * kernel (a hint); "gemv_m1_persist" (0/1, default 0) caps its grid at the
+ * resident CTA slots with CTAs looping over row-tile groups.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
