@@ -655,9 +655,9 @@ def config_c5(weights, device, hbm, steps):
 
 def ncu_traffic(rows):
     """Per-launch DRAM bytes (read + write) of the W4 GEMV launches of one step, from the
-    committed ncu summary (profiles/qgemv_ring_dram_traffic.json: dram__bytes_read.sum +
+    committed ncu summary (profiles/qgemv_m1_dram_traffic.json: dram__bytes_read.sum +
     dram__bytes_write.sum per shape, captured on the --kernel-case runs); null if absent."""
-    path = os.path.join(ROOT, "profiles", "qgemv_ring_dram_traffic.json")
+    path = os.path.join(ROOT, "profiles", "qgemv_m1_dram_traffic.json")
     try:
         with open(path) as f:
             per = json.load(f)["dram_bytes_per_launch"]
@@ -731,7 +731,7 @@ def run_ours(opt):
         tot_us = sum(r["us"] * r["launches_per_step"] for r in rows)
         achieved = tot_bytes / tot_us / 1e3
         n_launch = sum(r["launches_per_step"] for r in rows)
-        out["roofline"] = {"kernel": "qgemv_ring_kernel (every W4 GEMV launch of one B=1 step; per-launch "
+        out["roofline"] = {"kernel": "qgemv_m1_kernel (every W4 GEMV launch of one B=1 step; per-launch "
                                      "averages, byte-weighted over shapes)",
                            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),

@@ -65,6 +65,9 @@ struct AttnArgs {
   const int64_t* slots;
   uint16_t* kc_w;
   uint16_t* vc_w;
+  // weights of a later launch to pull into L2 (the decode step's next GEMVs): this
+  // kernel is latency-bound at small batches and leaves HBM idle
+  L2Prefetch pf;
 };
 
 __device__ __forceinline__ int swz(int row, int chunk) { return chunk ^ (row & 7); }
@@ -529,6 +532,8 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
     if (pg < pg1) issue(pg, s);
     cp_async_commit();
   }
+  issue_l2_prefetch(a.pf, (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x,
+                    gridDim.x * gridDim.y * gridDim.z);
 
   // norm weights and RoPE frequencies are constants of the model: into registers before
   // the wait, so the query / key preparation after it waits on one load only
@@ -1318,15 +1323,15 @@ extern "C" size_t higgs_fused_attention_workspace_size(int B, int Lq, int Hq, in
   return attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len, g_fused_min_pages), B, Hkv, D);
 }
 
-extern "C" int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq,
-                                     int Hkv, int D, const void* q_norm_w, const void* k_norm_w,
-                                     float eps, const int32_t* positions, const float* inv_freq,
-                                     const int64_t* slot_mapping, void* k_cache, void* v_cache,
-                                     int64_t page_stride, int64_t head_stride,
-                                     const int32_t* block_table, int max_blocks,
-                                     const int32_t* seq_lens, int max_seq_len, float scale,
-                                     void* out, void* workspace, size_t workspace_bytes,
-                                     void* stream) {
+namespace higgs {
+int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq, int Hkv, int D,
+                           const void* q_norm_w, const void* k_norm_w, float eps,
+                           const int32_t* positions, const float* inv_freq,
+                           const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                           int64_t page_stride, int64_t head_stride, const int32_t* block_table,
+                           int max_blocks, const int32_t* seq_lens, int max_seq_len, float scale,
+                           void* out, void* workspace, size_t workspace_bytes, void* stream,
+                           const L2Prefetch* pf) {
   HG_CHECK_ARG(ctx && qkv && positions && inv_freq && k_cache && v_cache && block_table &&
                    seq_lens && out && workspace,
                "higgs_fused_attention: null argument");
@@ -1368,6 +1373,7 @@ extern "C" int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int
   a.pos = positions;
   a.inv_freq = inv_freq;
   a.slots = slot_mapping;
+  if (pf) a.pf = *pf;
   attention_prepare();
   HG_CUDA(g_prepare_status);
   const int MT = p.rows_pad / 16;
@@ -1383,6 +1389,22 @@ extern "C" int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int
                 : launch_pdl(fused_attn_bf16_kernel<128, 2, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a);
   HG_CUDA(e);
   return HIGGS_OK;
+}
+}  // namespace higgs
+
+extern "C" int higgs_fused_attention(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq,
+                                     int Hkv, int D, const void* q_norm_w, const void* k_norm_w,
+                                     float eps, const int32_t* positions, const float* inv_freq,
+                                     const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                                     int64_t page_stride, int64_t head_stride,
+                                     const int32_t* block_table, int max_blocks,
+                                     const int32_t* seq_lens, int max_seq_len, float scale,
+                                     void* out, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  return fused_attention_launch(ctx, qkv, B, Lq, Hq, Hkv, D, q_norm_w, k_norm_w, eps, positions,
+                                inv_freq, slot_mapping, k_cache, v_cache, page_stride, head_stride,
+                                block_table, max_blocks, seq_lens, max_seq_len, scale, out, workspace,
+                                workspace_bytes, stream, nullptr);
 }
 
 // ---------------------------------------------------------------------------

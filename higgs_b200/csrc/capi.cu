@@ -32,7 +32,7 @@ void set_gemm_tc_rows(int m);
 void set_gemm_tc_waves(int w);
 void set_gemm_tc_wave_cost(int c);
 void qgemv_set_wk(int wk);
-void qgemv_m1_set(int on, int wk, int depth, int l2, int persist);
+void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);
 void qgemm_tc_prepare();
 
 }  // namespace higgs
@@ -51,23 +51,27 @@ extern "C" int higgs_set_option(const char* name, int value) {
     return HIGGS_OK;
   }
   if (n == "gemv_m1") {
-    qgemv_m1_set(value != 0, -1, -1, -1, -1);
+    qgemv_m1_set(value != 0, -1, -1, -1, -1, -1);
     return HIGGS_OK;
   }
   if (n == "gemv_m1_wk") {
-    qgemv_m1_set(-1, value, -1, -1, -1);
+    qgemv_m1_set(-1, value, -1, -1, -1, -1);
     return HIGGS_OK;
   }
   if (n == "gemv_m1_depth") {
-    qgemv_m1_set(-1, -1, value, -1, -1);
+    qgemv_m1_set(-1, -1, value, -1, -1, -1);
     return HIGGS_OK;
   }
   if (n == "gemv_m1_persist") {
-    qgemv_m1_set(-1, -1, -1, -1, value);
+    qgemv_m1_set(-1, -1, -1, -1, value, -1);
+    return HIGGS_OK;
+  }
+  if (n == "gemv_m1_l1") {
+    qgemv_m1_set(-1, -1, -1, -1, -1, value);
     return HIGGS_OK;
   }
   if (n == "gemv_m1_l2") {
-    qgemv_m1_set(-1, -1, -1, value, -1);
+    qgemv_m1_set(-1, -1, -1, value, -1, -1);
     return HIGGS_OK;
   }
   if (n == "gemm_tc_rows") {

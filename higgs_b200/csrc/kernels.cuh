@@ -64,6 +64,8 @@ struct QLinArgs {
   L2Prefetch pf;
   // also prefetch this CTA's own weight tiles to L2 at its start
   int self_prefetch;
+  // single-token GEMV: weight units prefetched into L1 ahead of its register ring (0 = off)
+  int m1_l1_ahead;
 };
 
 // Routing plan of the MoE router (moe.cu), in one buffer:
@@ -98,10 +100,19 @@ cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st);
 bool l2_prefetch_next();
 bool l2_prefetch_self();
 bool qgemv_ring_can_fuse_norm(int M, int K);
+// higgs_fused_attention with an L2 prefetch list for the decode step's later GEMVs
+int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int Hq, int Hkv, int D,
+                           const void* q_norm_w, const void* k_norm_w, float eps,
+                           const int32_t* positions, const float* inv_freq,
+                           const int64_t* slot_mapping, void* k_cache, void* v_cache,
+                           int64_t page_stride, int64_t head_stride, const int32_t* block_table,
+                           int max_blocks, const int32_t* seq_lens, int max_seq_len, float scale,
+                           void* out, void* workspace, size_t workspace_bytes, void* stream,
+                           const L2Prefetch* pf);
 // M == 1 (decode at batch 1): the register-fed GEMV of qgemv_m1.cu; launch_qgemv_ring routes there itself.
 bool qgemv_m1_supported(const QLinArgs& a);
 cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st);
-void qgemv_m1_set(int on, int wk, int depth, int l2, int persist);  // -1 leaves a setting as it is
+void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);  // -1 leaves a setting as it is
 // M >= 17: the tcgen05 matrix path (qgemm_tc.cu); launch_qgemv_ring routes there itself.
 bool qgemm_tc_supported(const QLinArgs& a);
 size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu);

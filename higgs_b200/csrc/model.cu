@@ -299,6 +299,8 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   if (rc) return rc;
   for (int li = 0; li < n_layers; ++li) {
     const LayerW& Lw = m->layers[li];
+    L2Prefetch next_pf{};
+    const bool attn_fused = !tq && (c.heads / c.kv_heads) * Lq <= 32;
     {
       if (!fuse) {
         rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_in, c.rms_eps, x, nullptr, st);
@@ -331,13 +333,16 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       a.self_prefetch = pfself;
       a.tc_ws = tc_ws;
       a.tc_ws_bytes = L.tc_ws_bytes;
-      add_q(a.pf, Lw.o);
+      // the next GEMVs' weights: requested by the fused attention kernel when it runs
+      // (latency-bound, HBM idle), else by this launch
+      add_q(next_pf, Lw.o);
       if (Lw.moe) {
-        add_q(a.pf, Lw.router);
+        add_q(next_pf, Lw.router);
       } else {
-        add_q(a.pf, Lw.gate);
-        add_q(a.pf, Lw.up);
+        add_q(next_pf, Lw.gate);
+        add_q(next_pf, Lw.up);
       }
+      if (!attn_fused) a.pf = next_pf;
       HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
     }
     if (tq) {
@@ -360,11 +365,12 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       // decode / verify: norm + RoPE + append + attention in one kernel
       uint16_t* kc = (uint16_t*)m->k_pool + li * kv_layer_elems;
       uint16_t* vc = (uint16_t*)m->v_pool + li * kv_layer_elems;
-      rc = higgs_fused_attention(m->ctx, qkv, B, Lq, c.heads, c.kv_heads, D, Lw.qn, Lw.kn,
-                                 c.rms_eps, f->positions, m->inv_freq, f->slot_mapping, kc, vc,
-                                 (int64_t)c.kv_heads * HIGGS_PAGE_SIZE * D,
-                                 (int64_t)HIGGS_PAGE_SIZE * D, f->block_table, f->max_blocks,
-                                 f->seq_lens, f->max_seq_len, scale, attn, aws, aws_bytes, st);
+      rc = fused_attention_launch(m->ctx, qkv, B, Lq, c.heads, c.kv_heads, D, Lw.qn, Lw.kn,
+                                  c.rms_eps, f->positions, m->inv_freq, f->slot_mapping, kc, vc,
+                                  (int64_t)c.kv_heads * HIGGS_PAGE_SIZE * D,
+                                  (int64_t)HIGGS_PAGE_SIZE * D, f->block_table, f->max_blocks,
+                                  f->seq_lens, f->max_seq_len, scale, attn, aws, aws_bytes, st,
+                                  &next_pf);
       if (rc) return rc;
     } else {
       uint16_t* kc = (uint16_t*)m->k_pool + li * kv_layer_elems;

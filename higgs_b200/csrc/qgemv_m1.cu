@@ -35,6 +35,7 @@ namespace higgs {
 namespace {
 
 constexpr int kM1Threads = 256;
+constexpr int kM1CtasPerSm = 2;  // register bound: 128 registers a thread
 constexpr int kM1MaxK = 32768;  // staged x: K / 256 * 512 B + sums + 1 KB
 constexpr int kM1RegChunks = 4;   // fused norm: x chunks held in registers between the passes (K <= 8192)
 constexpr int kM1NormChunks = 2;  // fused norm: norm-weight chunks loaded before the wait (K <= 4096)
@@ -54,6 +55,18 @@ __device__ __forceinline__ void m1_mma(float (&d)[4], uint32_t a0, uint32_t a1, 
       "{%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// weights: L1-allocating loads, so lines pulled in by m1_prefetch_l1 are hit there
+__device__ __forceinline__ uint4 m1_ldg128(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void m1_prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
 
 __device__ __forceinline__ uint4 m1_lds128(uint32_t addr) {
@@ -78,7 +91,7 @@ __device__ __forceinline__ uint4 m1_frag(uint4 v) {
 // WK warps split the K range of each 16-row tile; RT = 8 / WK tiles per CTA (SwiGLU: RT / 2
 // gate/up pairs).  D units of weights in flight per warp (even).
 template <int WK, int EPI, bool NORM, int D>
-__global__ void __launch_bounds__(kM1Threads, 2) qgemv_m1_kernel(QLinArgs a) {
+__global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLinArgs a) {
   static_assert(D % 2 == 0, "units are folded in pairs");
   constexpr int RT = 8 / WK;
   constexpr int ROT = (EPI == EPI_SWIGLU) ? RT / 2 : RT;
@@ -132,18 +145,17 @@ __global__ void __launch_bounds__(kM1Threads, 2) qgemv_m1_kernel(QLinArgs a) {
   };
 
   issue_l2_prefetch(a.pf, blockIdx.x, gridDim.x);
-  if (a.self_prefetch && lane < 16) {
-    // every K range this warp will stream, of all its groups -> L2 now: the register ring
-    // below (D units deep) then reads L2 instead of waiting on HBM round trips
+  if (a.self_prefetch && kw == 0 && lane < 3) {
+    // every tile this CTA will stream -> L2 now, one contiguous request per tile (its 16
+    // rows are adjacent: 16 x K/2 bytes; lanes 1, 2 take the scales and biases), so the
+    // register ring below (D units deep) reads L2 instead of waiting on HBM round trips
     for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
       const Tile tl = tile_of(grp);
       if (tl.ub >= tl.ue) continue;
-      const char* row = reinterpret_cast<const char*>(tl.sg.W + (size_t)(tl.sg.row0 + lane) * KW);
-      l2_prefetch_range(row + (size_t)tl.ub * 128, (size_t)(tl.ue - tl.ub) * 128);
-      if (lane < 2 && kw == 0) {  // the tile's scales / biases, once per tile
-        const uint16_t* sbp = lane ? tl.sg.B : tl.sg.S;
-        l2_prefetch_range(sbp + (size_t)tl.sg.row0 * G, (size_t)16 * G * 2);
-      }
+      if (lane == 0)
+        l2_prefetch_range(tl.sg.W + (size_t)tl.sg.row0 * KW, (size_t)16 * KW * 4);
+      else
+        l2_prefetch_range((lane == 1 ? tl.sg.S : tl.sg.B) + (size_t)tl.sg.row0 * G, (size_t)16 * G * 2);
     }
   }
 
@@ -166,10 +178,10 @@ __global__ void __launch_bounds__(kM1Threads, 2) qgemv_m1_kernel(QLinArgs a) {
   uint4 buf[D][4];
   uint32_t sb[D / 2][4];
   auto load_unit = [&](uint4 (&b)[4], int u) {
-    b[0] = ldg_stream_u4(wg + 8 * u);
-    b[1] = ldg_stream_u4(wg + 8 * u + 4);
-    b[2] = ldg_stream_u4(w8 + 8 * u);
-    b[3] = ldg_stream_u4(w8 + 8 * u + 4);
+    b[0] = m1_ldg128(wg + 8 * u);
+    b[1] = m1_ldg128(wg + 8 * u + 4);
+    b[2] = m1_ldg128(w8 + 8 * u);
+    b[3] = m1_ldg128(w8 + 8 * u + 4);
   };
   auto load_scales = [&](uint32_t (&q)[4], int u0) {
     // this lane folds unit u0 + t/2; past the range it folds nothing (scales 0)
@@ -275,6 +287,7 @@ __global__ void __launch_bounds__(kM1Threads, 2) qgemv_m1_kernel(QLinArgs a) {
   const uint32_t xreal = smem_u32(xf) + t * 16;
   const uint32_t xzero = smem_u32(zero);
   const float2* xs2 = reinterpret_cast<const float2*>(xs);
+  const int l1d = a.m1_l1_ahead;
 
   for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
     if (grp != (int)blockIdx.x) {
@@ -313,8 +326,13 @@ __global__ void __launch_bounds__(kM1Threads, 2) qgemv_m1_kernel(QLinArgs a) {
                    nib_pair_bf16<12>(B), xv[e].z, xv[e].w);
           }
         }
-        // buffer d is consumed: request unit u + D into it
+        // buffer d is consumed: request unit u + D into it, and unit u + D + l1d into L1
+        // (lane t == 0 of each row pair: the rows' 128-byte lines)
         if (u + D < ue) load_unit(buf[d], u + D);
+        if (l1d > 0 && t == 0 && u + D + l1d < ue) {
+          m1_prefetch_l1(wg + 8 * (u + D + l1d));
+          m1_prefetch_l1(w8 + 8 * (u + D + l1d));
+        }
         if (p == 1 || u + 1 == ue) {
           // fold the pair (u0, u0 + 1): lane t holds columns 2t, 2t+1 = groups 4 u0 + 2t, +1;
           // the MMA saw 128 + q, so y += s * acc + (b - 128 s) * sum(x)
@@ -388,6 +406,7 @@ int g_m1_depth = 2;   // units in flight per warp (2 or 4)
 // 2.278 ms, capped grid 2.326 (no prefetch) / 2.369 (prefetch), one CTA per group without
 // the prefetch 2.426, the multi-token ring kernel 2.415
 bool g_m1_persist = false;
+int g_m1_l1 = 0;  // units ahead of the register ring that are prefetched into L1 (0 = off)
 
 template <int WK, int EPI, bool NORM, int D>
 cudaError_t m1_launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
@@ -405,10 +424,11 @@ template <int EPI, bool NORM, int D>
 cudaError_t m1_launch_d(const QLinArgs& a_in, cudaStream_t st) {
   QLinArgs a = a_in;
   if (g_m1_l2) a.self_prefetch = 1;
+  a.m1_l1_ahead = g_m1_l1;
   const int nrt = a.N / 16;
   const int units = a.K / 256;
   const size_t smem = m1_smem_bytes(a.K);
-  const int slots = 2 * sm_count();  // two CTAs per SM (register bound); the grid never exceeds it
+  const int slots = kM1CtasPerSm * sm_count();
   // Cost of a K split: the resident CTAs' iterations over tile groups x (units per warp + 1,
   // the per-group reduction); ties go to more splits (more warps streaming).  It picks the
   // split measured fastest on B200 for each Qwen3-8B shape (qkv 4, o_proj / down 8,
@@ -486,7 +506,8 @@ cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st) {
   return a.norm_w ? m1_launch_norm<EPI_STORE, true>(a, st) : m1_launch_norm<EPI_STORE, false>(a, st);
 }
 
-void qgemv_m1_set(int on, int wk, int depth, int l2, int persist) {
+void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1) {
+  if (l1 >= 0) g_m1_l1 = l1 > 16 ? 16 : l1;
   if (persist >= 0) g_m1_persist = persist != 0;
   if (l2 >= 0) g_m1_l2 = l2 != 0;
   if (on >= 0) g_m1_on = on != 0;
