@@ -736,7 +736,8 @@ def run_ours(opt):
                            "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                            "algorithmic_bytes": int(tot_bytes / n_launch),
-                           "traffic": ncu_traffic(rows), "per_shape": rows}
+                           # the committed capture is of one-GPU shapes: no figure for a TP shard
+                           "traffic": ncu_traffic(rows) if ws == 1 else None, "per_shape": rows}
         sb = by_batch[str(B)]["step_bytes"]
         out["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": round(sb / (step_ms / 1e3) / 1e9, 1),
                                 "peak": hbm, "frac": by_batch[str(B)]["step_hbm_frac"]}
