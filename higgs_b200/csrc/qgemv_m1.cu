@@ -404,8 +404,9 @@ int g_m1_depth = 2;   // units in flight per warp (2 or 4)
 // grid capped at the resident slots, CTAs looping over tile groups; off = one CTA per group.
 // Measured on B200 (B=1 Qwen3-8B step, same box): one CTA per group with the L2 prefetch
 // 2.278 ms, capped grid 2.326 (no prefetch) / 2.369 (prefetch), one CTA per group without
-// the prefetch 2.426, the multi-token ring kernel 2.415
-bool g_m1_persist = false;
+// the prefetch 2.426, the multi-token ring kernel 2.415; capping gate/up alone (its
+// late second wave folded into resident CTAs) 2.232 vs 2.146 on another box
+int g_m1_persist = 0;  // 1: every launch; 2: gate/up only, at its one-CTA-per-group split
 int g_m1_l1 = 0;  // units ahead of the register ring that are prefetched into L1 (0 = off)
 
 template <int WK, int EPI, bool NORM, int D>
@@ -445,7 +446,8 @@ cudaError_t m1_launch_d(const QLinArgs& a_in, cudaStream_t st) {
       wk = c;
     }
   }
-  if (!g_m1_persist) {
+  const bool persist = g_m1_persist == 1 || (g_m1_persist == 2 && EPI == EPI_SWIGLU);
+  if (g_m1_persist != 1) {
     // One CTA per group.  Single matrices: the most K splits whose CTAs fit one wave, so
     // every CTA is resident (and has asked L2 for its whole slice) from the start; wider
     // outputs take wk = 1.  Gate/up (twice the bytes per row tile): the fewest splits that
@@ -475,7 +477,7 @@ cudaError_t m1_launch_d(const QLinArgs& a_in, cudaStream_t st) {
   while (wk > 1 && units < wk) wk >>= 1;
   const int rot = EPI == EPI_SWIGLU ? (8 / wk) / 2 : 8 / wk;
   const int groups = (nrt + rot - 1) / rot;
-  const int ctas = (g_m1_persist && groups > slots) ? slots : groups;
+  const int ctas = (persist && groups > slots) ? slots : groups;
   switch (wk) {
     case 8:
       if constexpr (EPI != EPI_SWIGLU) return m1_launch_cfg<8, EPI, NORM, D>(a, ctas, smem, st);
@@ -508,7 +510,7 @@ cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st) {
 
 void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1) {
   if (l1 >= 0) g_m1_l1 = l1 > 16 ? 16 : l1;
-  if (persist >= 0) g_m1_persist = persist != 0;
+  if (persist >= 0) g_m1_persist = persist > 2 ? 2 : persist;
   if (l2 >= 0) g_m1_l2 = l2 != 0;
   if (on >= 0) g_m1_on = on != 0;
   if (wk >= 0) g_m1_wk = (wk == 1 || wk == 2 || wk == 4 || wk == 8) ? wk : 0;

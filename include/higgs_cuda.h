@@ -99,8 +99,10 @@ int higgs_version(void);
  * heuristic) forces its K split; "gemv_m1_depth" (2 or 4, default 2) sets the
  * weight units each warp keeps in flight; "gemv_m1_l2" (0/1, default 1) makes each
  * of its CTAs ask L2 for its whole weight slice before waiting on the previous
- * kernel (a hint); "gemv_m1_persist" (0/1, default 0) caps its grid at the
- * resident CTA slots with CTAs looping over row-tile groups.
+ * kernel (a hint); "gemv_m1_persist" (0, 1, 2; default 0) caps its grid at the
+ * resident CTA slots with CTAs looping over row-tile groups (1: every launch, 2:
+ * gate/up launches only); "gemv_m1_l1" (0..16, default 0) prefetches that many
+ * weight units into L1 ahead of each warp's register ring.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
