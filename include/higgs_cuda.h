@@ -82,10 +82,12 @@ int higgs_version(void);
  * fp16 operands (x scaled per token by a power of two, exact for bf16 inputs)
  * instead of bf16 ones.  "attn_min_pages" (4..4096, default 8): KV pages per split
  * of higgs_fused_attention; change it only between captures, since workspace
- * sizes depend on it.  "l2_prefetch" (bit mask, default 0): bit 0 makes every
- * GEMV of the decode step ask the TMA unit to pull the next GEMV's weights into
- * L2, bit 1 makes each GEMV CTA pull its own weight tiles (a hint; results are
- * unchanged).  "gemm_tc" (0/1, default 1): quantized linears over 17 or more
+ * sizes depend on it.  "l2_prefetch" (bit mask, default 0): bit 0 makes the
+ * decode step ask the TMA unit to pull later GEMVs' weights into L2 ahead of them
+ * (the fused attention kernel requests o_proj's and the MLP's, o_proj down_proj's,
+ * gate/up the next layer's q|k|v), bit 1 makes each multi-token GEMV CTA pull its
+ * own weight tiles (hints; results are unchanged; measured on B200, both lengthen
+ * the Qwen3-8B decode step at B=1 and B=8).  "gemm_tc" (0/1, default 1): quantized linears over 17 or more
  * rows use the tcgen05 tensor-core kernel (weights dequantized to bf16 first,
  * MLX's qmm form) instead of the decode GEMV; "gemm_tc_waves" (1..8, default 2) and "gemm_tc_wave_cost"
  * (default 8): the tensor-core kernel picks the K-split count that minimises
