@@ -430,10 +430,10 @@ cudaError_t m1_launch_d(const QLinArgs& a_in, cudaStream_t st) {
   const int units = a.K / 256;
   const size_t smem = m1_smem_bytes(a.K);
   const int slots = kM1CtasPerSm * sm_count();
-  // Cost of a K split: the resident CTAs' iterations over tile groups x (units per warp + 1,
-  // the per-group reduction); ties go to more splits (more warps streaming).  It picks the
-  // split measured fastest on B200 for each Qwen3-8B shape (qkv 4, o_proj / down 8,
-  // gate/up 4, LM head 2).
+  // Capped grid (persist mode 1): cost of a K split = the resident CTAs' iterations over
+  // tile groups x (units per warp + 1, the per-group reduction); ties go to more splits
+  // (more warps streaming).  It picks the split that is fastest for each Qwen3-8B shape
+  // when timed alone on B200 (qkv 4, o_proj / down 8, gate/up 4, LM head 2).
   const int max_wk = EPI == EPI_SWIGLU ? 4 : 8;
   int wk = 1;
   long long best = -1;
