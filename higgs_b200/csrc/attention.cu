@@ -25,6 +25,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "timeline.cuh"
 
 namespace higgs {
 
@@ -175,6 +176,7 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
   const int bh = b * a.Hkv + h;
   if (a.splits == 1) {
     finish(sm_o, R, b, h);
+    HG_TL_END(3001);
     return;
   }
   // write the split partial (valid rows only)
@@ -187,7 +189,11 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
   __shared__ int is_last;
   if (threadIdx.x == 0) is_last = (atomicAdd(a.counters + bh, 1) == a.splits - 1);
   __syncthreads();
-  if (!is_last) return;
+  HG_TL_MARK(6);
+  if (!is_last) {
+    HG_TL_END(3002);
+    return;
+  }
   __threadfence();
   const float* base_o = a.ws_o + (size_t)bh * a.splits * RP * D;
   const float* base_l = a.ws_lse + (size_t)bh * a.splits * RP;
@@ -240,6 +246,7 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
   __syncthreads();
   if (threadIdx.x == 0) a.counters[bh] = 0;
   finish(sm_o, R, b, h);
+  HG_TL_END(3003);
 }
 
 template <int D>
@@ -505,6 +512,7 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
   uint16_t* NK = Qs + RP * D;                              // [Lq][2][D] new K / V (natural order)
   uint16_t* KV = NK + ((2 * a.Lq * D + 63) / 64) * 64;    // [4 warps][S stages][K | V]
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  HG_TL_MARK(0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int G = a.Hq / a.Hkv;
@@ -550,6 +558,7 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
   }
 
   pdl_wait();
+  HG_TL_MARK(1);
   pdl_launch();
 
   // query rows: RMSNorm (Qwen3) + RoPE, straight into the swizzled Q tile
@@ -592,6 +601,7 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
     }
   }
   __syncthreads();
+  HG_TL_MARK(4);
 
   float m[MT][2], l[MT][2], o[MT][D / 8][4];
 #pragma unroll
@@ -684,6 +694,7 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
   AttnArgs ao = a;
   ao.tq0 = 0;
   FinishBf16<D> fin{&ao};
+  HG_TL_MARK(5);
   attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
 }
 
@@ -1478,3 +1489,5 @@ extern "C" int higgs_paged_attention_noalloc(higgs_ctx* ctx, const void* q, int 
                                head_stride, block_table, max_blocks, seq_lens, max_seq_len, scale,
                                out, scratch, kNoAllocScratchBytes, stream);
 }
+
+HG_TL_FETCH_FN(higgs_timeline_fetch_attn)

@@ -29,6 +29,7 @@
 // (one group each by default; optionally a grid capped at the resident slots).
 #include "common.cuh"
 #include "kernels.cuh"
+#include "timeline.cuh"
 
 namespace higgs {
 
@@ -96,6 +97,7 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
   constexpr int RT = 8 / WK;
   constexpr int ROT = (EPI == EPI_SWIGLU) ? RT / 2 : RT;
   extern __shared__ __align__(128) uint8_t smem[];
+  HG_TL_MARK(0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int rt = warp / WK, kw = warp % WK;
@@ -212,6 +214,7 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
     }
   }
   pdl_wait();
+  HG_TL_MARK(1);
   pdl_launch();
 
   if (threadIdx.x < 32) reinterpret_cast<uint4*>(zero)[threadIdx.x] = make_uint4(0, 0, 0, 0);
@@ -395,6 +398,7 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
     }
     __syncthreads();  // red is rewritten by the next group
   }
+  HG_TL_END(1000 + EPI * 100 + NORM * 10 + WK);
 }
 
 bool g_m1_on = true;
@@ -518,3 +522,5 @@ void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1) {
 }
 
 }  // namespace higgs
+
+HG_TL_FETCH_FN(higgs_timeline_fetch_gemv)
