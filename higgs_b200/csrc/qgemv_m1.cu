@@ -220,6 +220,8 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
   if (threadIdx.x < 32) reinterpret_cast<uint4*>(zero)[threadIdx.x] = make_uint4(0, 0, 0, 0);
   const uint16_t* x = a.x;
   // ---- fused RMSNorm: the token's sum of squares (its chunks kept for the staging) ----
+  // (measured on B200: every warp summing the whole token itself, to drop the barrier below,
+  // lengthened the B=1 decode step 2.15 -> 2.39 ms: 16 dependent L2 loads per lane)
   __shared__ float s_ss[8];
   uint4 xr[NORM ? kM1RegChunks : 1];
   float inv = 1.0f;
