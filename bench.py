@@ -14,8 +14,14 @@ checkpoint available offline); the KV context is synthetic random bf16 (decode
 cost does not depend on the values).  Weights (4.26 GB/step) exceed L2, so
 every step streams them from HBM.
 
-With N > 1 (torchrun), each rank runs an independent replica over its own
-sequences (weak scaling); `value` sums tokens over ranks / max time over ranks.
+With N > 1 (torchrun), the same model and batch run tensor-parallel over the N
+GPUs (strong scaling): each rank holds a column / row shard of every projection
+and a vocabulary shard of the LM head, and the ranks sum their partials with a
+peer-memory all-reduce after attention and after the MLP of every layer.
+`value` is the batch's tokens over the maximum time over ranks.  `tp_parity`
+checks the tensor-parallel model's greedy stream and logits against the same
+weights on one GPU; `comm_errors` counts collectives whose bounded wait gave up
+(the run fails if any did).
 """
 from __future__ import annotations
 
@@ -175,7 +181,7 @@ def make_tp_group(args_m, rank, world, max_tokens, device):
 
 def setup_model(args_m, batches, ctx, total_steps, device, world=1, rank=0):
     """The model on one GPU, or (world > 1) this rank's tensor-parallel shard with its
-    peer-memory communicator."""
+    peer-memory communicator (the unsharded weights are kept for the parity check)."""
     import torch
 
     from higgs_b200.engine import Engine, Sequence
@@ -185,7 +191,9 @@ def setup_model(args_m, batches, ctx, total_steps, device, world=1, rank=0):
     per_seq_pages = math.ceil((ctx + total_steps + 2) / 16)
     num_pages = max(max(batches), 4) * per_seq_pages + 16  # >= the 4 sequences of C3
     tp = None
+    full = None
     if world > 1:
+        full = weights
         weights = shard_weights(args_m, weights, rank, world)
         tp = make_tp_group(args_m, rank, world, max(batches), device)
     model = Model(args_m, weights, num_pages=num_pages, device=device, tp=tp)
@@ -196,7 +204,7 @@ def setup_model(args_m, batches, ctx, total_steps, device, world=1, rank=0):
         for li in range(pool.shape[0]):
             pool[li].copy_(torch.randn(pool[li].shape, generator=g, device=device).to(torch.bfloat16))
     eng = Engine(model, max_seq_len=ctx + total_steps + 2, prefix_entries=0)
-    return model, eng, Sequence
+    return model, eng, Sequence, full
 
 
 def make_seqs(eng, Sequence, B, ctx, vocab, seed=1):
@@ -429,8 +437,80 @@ def kernel_case(opt):
     print(json.dumps({"kernel_case": case, "ok": True}))
 
 
+def tp_parity(args_m, full_w, tp_model, device, steps=64, prompt_len=32, seed=7):
+    """Greedy decode of `steps` tokens from one seeded prompt on this rank's tensor-parallel
+    model (every rank takes part) and on an unsharded copy of the same weights on this rank's
+    GPU alone.  Tokens: the free-running TP stream against the one-GPU stream.  Logits: the
+    TP model teacher-forced on the one-GPU stream, this rank's vocabulary shard against the
+    same slice of the one-GPU logits.  Maxima are taken over ranks."""
+    import torch
+
+    from higgs_b200.engine import Engine
+    from higgs_b200.model import Model
+    world, rank = tp_model.tp.world, tp_model.tp.rank
+    pr = np.random.default_rng(seed).integers(0, args_m.vocab_size, size=(1, prompt_len)).astype(np.int32)
+    msl = prompt_len + steps + 16
+    # the tensor-parallel model: free-running stream (collectives on every rank, same order)
+    tp_free = Engine(tp_model, max_seq_len=msl, prefix_entries=0).generate_greedy(list(pr), steps,
+                                                                                   use_prefix=False)
+    # the same weights on this GPU alone
+    one = Model(args_m, full_w, num_pages=math.ceil(msl / 16) + 4, device=device)
+    e1 = Engine(one, max_seq_len=msl, prefix_entries=0, keep_logits=True)
+    s1 = e1.prefill(pr[0], use_prefix=False)
+    first = s1.last_token
+    one_rest = e1.decode_steps([s1], steps - 1)
+    one_tok = np.concatenate([[first], one_rest[0]]).astype(np.int32)
+    one_lg = np.stack(e1.step_logits)[:, 0]  # [steps-1, V]
+    del e1, s1, one
+    torch.cuda.empty_cache()
+    # the TP model teacher-forced on the one-GPU stream
+    et = Engine(tp_model, max_seq_len=msl, prefix_entries=0, keep_logits=True)
+    st = et.prefill(pr[0], use_prefix=False)
+    st.last_token = int(one_tok[0])
+    et.decode_steps([st], steps - 1, force=one_tok[None, :steps - 1])
+    shard = args_m.vocab_size // world
+    tp_lg = np.stack(et.step_logits)[:, 0, :shard]
+    ref = one_lg[:, rank * shard:(rank + 1) * shard]
+    err = float(np.max(np.abs(tp_lg - ref)))
+    rel = float(np.max(np.abs(tp_lg - ref) / (np.abs(ref) + 1e-6)))
+    et.release(st)
+    diff = np.nonzero(tp_free[0] != one_tok)[0]
+    first_diff = int(diff[0]) if diff.size else None
+    top2 = np.sort(one_lg, axis=-1)[:, -2:]
+    margin_at = (float(top2[first_diff - 1, 1] - top2[first_diff - 1, 0])
+                 if first_diff is not None and first_diff >= 1 else None)
+    return {"tokens": steps, "tokens_equal": bool(allmax(float(first_diff is not None)) == 0.0),
+            "first_diff": first_diff, "margin_at_first_diff": margin_at,
+            "max_logit_abs": round(allmax(err), 6), "max_logit_rel": round(allmax(rel), 6),
+            "prompt": f"{prompt_len} uniform ids (seed {seed}), B=1, one GPU vs tp{world}"}
+
+
+def comm_errors(model) -> int:
+    """Collectives of this rank's communicator whose bounded wait gave up, plus tensor-core
+    matmul timeouts on this GPU (both flags are cleared by the read)."""
+    import ctypes
+
+    from higgs_b200 import ffi
+    n = 0
+    if model.tp is not None:
+        n += model.tp.error()
+    v = ctypes.c_int(0)
+    ffi.call("higgs_tc_error", ffi.ctx(model.device.index or 0), ctypes.byref(v))
+    return n + v.value
+
+
+def host_threads() -> int:
+    """Host cores this process may run on; the oracle's OpenMP team is set to this many
+    explicitly, since torchrun exports OMP_NUM_THREADS=1 to every rank."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):
+        return os.cpu_count() or 1
+
+
 def oracle_step_time(model_args, ctx, budget_s=20.0):
-    """Seconds per B=1 decode step of the full model through the oracle port on the host.
+    """Seconds per B=1 decode step of the full model through the oracle port on the host,
+    with every host core (returns seconds, sample description, threads used).
 
     Timed at true shapes on 2- and 6-layer slices (embedding, final norm, LM head and
     KV context included) and extrapolated linearly to all layers, since every layer
@@ -441,6 +521,7 @@ def oracle_step_time(model_args, ctx, budget_s=20.0):
     from oracle import oracle as orc
     from oracle.model_ref import RefModel
     from higgs_b200.model import tensor_specs
+    threads = orc.set_threads(host_threads())
     rng = np.random.default_rng(5)
 
     def packed(shape):
@@ -481,9 +562,10 @@ def oracle_step_time(model_args, ctx, budget_s=20.0):
         del ref, cache
     per_layer = max(0.0, (times[6] - times[2]) / 4)
     full = times[2] + (model_args.num_hidden_layers - 2) * per_layer
-    desc = (f"oracle port, B=1 decode at ctx {ctx}: {reps[2]} steps of a 2-layer and {reps[6]} of a "
-            f"6-layer slice at true shapes, extrapolated to {model_args.num_hidden_layers} layers")
-    return full, desc
+    desc = (f"oracle port on {threads} OpenMP threads, B=1 decode at ctx {ctx}: {reps[2]} steps of a "
+            f"2-layer and {reps[6]} of a 6-layer slice at true shapes, extrapolated to "
+            f"{model_args.num_hidden_layers} layers")
+    return full, desc, threads
 
 
 # ---------------------------------------------------------------------------------------------
@@ -599,7 +681,9 @@ def config_c3(model, eng, Sequence, device, hbm, steps, ctx):
 def config_c4(device, hbm, steps, world=1, rank=0):
     """C4: Qwen3-30B-A3B arch (128 experts, top-8), B=32 decode at ctx 4096; on N GPUs
     attention is tensor parallel and the experts are split over the ranks (expert
-    parallelism), both reduced by the peer-memory all-reduce."""
+    parallelism), both reduced by the peer-memory all-reduce.  Returns (entry, parity,
+    errors): on N GPUs, the greedy parity of the sharded model against the unsharded
+    weights on one GPU and the count of collectives that timed out; (entry, None, 0) on one."""
     import torch
 
     from higgs_b200.engine import Engine, Sequence
@@ -609,7 +693,9 @@ def config_c4(device, hbm, steps, world=1, rank=0):
     pages = B * math.ceil((ctx + steps + 16) / 16) + 16
     w = synth_weights_device(a, seed=0, device=device)
     tp = None
+    full = None
     if world > 1:
+        full = w
         w = shard_weights(a, w, rank, world)
         tp = make_tp_group(a, rank, world, B, device)
     model = Model(a, w, num_pages=pages, device=device, tp=tp)
@@ -627,9 +713,16 @@ def config_c4(device, hbm, steps, world=1, rank=0):
         out["step_hbm_frac"] = round(out["step_hbm_frac"] / world, 4)  # per-GPU bytes
     for s_ in seqs:
         eng.release(s_)
-    del eng, model, w
+    parity, errors = None, 0
+    if world > 1:
+        errors = int(allmax(float(comm_errors(model))))
+        del eng
+        torch.cuda.empty_cache()
+        parity = tp_parity(a, full, model, device)
+        errors += int(allmax(float(comm_errors(model))))
+    del model, w, full
     torch.cuda.empty_cache()
-    return out
+    return out, parity, errors
 
 
 def config_c5(weights, device, hbm, steps):
@@ -667,6 +760,13 @@ def ncu_traffic(rows):
         return None
 
 
+def bench_config(ws: int, B: int, ctx: int) -> dict:
+    """The headline workload (shared by both arms)."""
+    return {"workload": f"{MODEL} decode B={B} ctx={ctx}", "model": MODEL, "global_batch": B,
+            "seq_len": ctx, "parallelism": f"tp{ws} (peer-memory all-reduce)" if ws > 1 else "single GPU",
+            "l2": "weights 4.26 GB/step > 126 MB L2 (no flush needed)"}
+
+
 def run_ours(opt):
     import torch
 
@@ -679,7 +779,7 @@ def run_ours(opt):
     if opt.quick:
         batches = batches[:1]
     total_steps = 2 * (opt.steps + opt.warmup) + 4
-    model, eng, Sequence = setup_model(a, batches, opt.ctx, total_steps, device, ws, rank)
+    model, eng, Sequence, full_weights = setup_model(a, batches, opt.ctx, total_steps, device, ws, rank)
     hbm, peak_kind = peaks()
     w_bytes = a.weight_bytes_per_step()
     by_batch = {}
@@ -711,20 +811,24 @@ def run_ours(opt):
     for s in seqs:
         eng.release(s)
     e2e_tok_s = B * opt.steps / (e2e_ms / 1e3)
+    n_comm_err = int(allmax(float(comm_errors(model))))
     out = {
         "metric": METRIC, "value": round(tok_s, 1), "unit": "tok/s", "n_gpus": ws,
         "steps": opt.steps, "warmup": opt.warmup, "ms_per_step": round(step_ms, 4),
         "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None,
         "dtype": "w4a16 (u4 weights, bf16 act, f32 acc)",
         "data": "synthetic: random-init N(0,0.02) W4 g64 weights, random KV context, uniform token ids",
-        "config": {"workload": f"{MODEL} decode B={B} ctx={opt.ctx}", "model": MODEL, "global_batch": B,
-                   "seq_len": opt.ctx, "parallelism": f"tp{ws} (peer-memory all-reduce)" if ws > 1 else "single GPU",
-                   "l2": "weights 4.26 GB/step > 126 MB L2 (no flush needed)"},
+        "config": bench_config(ws, B, opt.ctx),
         "by_batch": by_batch,
         "e2e": {"value": round(e2e_tok_s, 1), "unit": "tok/s", "h2d_bytes_per_step": 16 * B,
                 "d2h_bytes_per_step": 4 * B},
-        "gpu_launches": gpu_launches, "clocks": clocks,
+        "gpu_launches": gpu_launches, "clocks": clocks, "comm_errors": n_comm_err,
     }
+    if ws > 1:
+        parity = {"dense_b1": tp_parity(a, full_weights, model, device)}
+        del full_weights
+        torch.cuda.empty_cache()
+        parity_err = int(allmax(float(comm_errors(model))))
     if rank == 0 and not opt.quick:
         rows = gemv_roofline(model)
         tot_bytes = sum(r["bytes"] * r["launches_per_step"] for r in rows)
@@ -759,15 +863,24 @@ def run_ours(opt):
             import gc
             gc.collect()
             torch.cuda.empty_cache()
-            cfgs["C4"] = config_c4(device, hbm, n)
+            cfgs["C4"] = config_c4(device, hbm, n)[0]
         out["by_config"] = cfgs
     elif ws > 1 and not opt.quick and "c4" in opt.configs.split(","):
-        c4 = config_c4(device, hbm, 16, ws, rank)  # every rank takes part
+        del eng, model
+        import gc
+        gc.collect()
+        torch.cuda.empty_cache()
+        c4, c4_parity, c4_err = config_c4(device, hbm, 16, ws, rank)  # every rank takes part
+        parity["c4_ep"] = c4_parity
+        parity_err += c4_err
         if rank == 0:
             out["by_config"] = {"C4": c4}
+    if ws > 1:
+        out["tp_parity"] = parity
+        out["comm_errors"] += parity_err
     if rank == 0 and ws == 1 and not opt.no_cpu_baseline and not opt.quick:
-        sec, desc = oracle_step_time(a, opt.ctx)
-        out["cpu_baseline"] = {"value": round(1.0 / sec, 4), "unit": "tok/s", "cores": os.cpu_count(),
+        sec, desc, threads = oracle_step_time(a, opt.ctx)
+        out["cpu_baseline"] = {"value": round(1.0 / sec, 4), "unit": "tok/s", "cores": threads,
                                "kind": "port", "sample": desc}
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -786,16 +899,17 @@ def run_reference(opt):
         return
     from higgs_b200.model import PRESETS
     a = PRESETS[MODEL]
-    sec, desc = oracle_step_time(a, opt.ctx)
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    B = int(opt.batches.split(",")[0])
+    sec, desc, threads = oracle_step_time(a, opt.ctx)
     v = 1.0 / sec
-    out = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": 0,
+    out = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": ws,
            "steps": opt.steps, "warmup": opt.warmup, "ms_per_step": round(sec * 1e3, 2),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "higher_is_better": True, "scaling": "strong" if ws > 1 else "weak", "vs_baseline": None,
            "dtype": "w4a16 (u4 weights, bf16 act, f32 acc)",
            "data": "synthetic packed W4 weights and random KV context",
-           "config": {"workload": f"{MODEL} decode B=1 ctx={opt.ctx}", "model": MODEL, "global_batch": 1,
-                      "seq_len": opt.ctx, "parallelism": "host cores"},
-           "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+           "config": bench_config(ws, B, opt.ctx),
+           "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "port",
                             "sample": desc + "; the reference's own mlx-rs CPU backend cannot be built here "
                                              "(no Rust toolchain, MLX not vendored)"},
            "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}

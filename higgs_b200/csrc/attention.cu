@@ -1162,14 +1162,9 @@ static size_t smem_fused(int D, int MT, int Lq) {
   return q + nk + (kv > merge ? kv : merge);
 }
 
-static cudaError_t g_prepare_status = cudaSuccess;
-
-// Raise the dynamic shared-memory limit of every attention instantiation once,
-// outside any stream capture.
-void attention_prepare() {
-  static bool done = false;
-  if (done) return;
-  done = true;
+// Raise the dynamic shared-memory limit of every attention instantiation, once
+// per device (the limit is a per-device setting), outside any stream capture.
+static cudaError_t attention_prepare_device() {
   cudaError_t e = cudaSuccess;
   auto set = [&](void (*k)(AttnArgs), size_t smem) {
     cudaError_t r = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1185,15 +1180,18 @@ void attention_prepare() {
   set(fused_attn_bf16_kernel<64, 2, kFusedStages>, smem_fused(64, 2, 32));
   set(fused_attn_bf16_kernel<128, 1, kFusedStages>, smem_fused(128, 1, 32));
   set(fused_attn_bf16_kernel<128, 2, kFusedStages>, smem_fused(128, 2, 32));
-  g_prepare_status = e;
+  return e;
 }
+
+static PerDeviceOnce g_attn_prepared;
+
+cudaError_t attention_prepare() { return g_attn_prepared.run(attention_prepare_device); }
 
 template <typename K>
 static cudaError_t launch_attn(K kernel, size_t smem, const AttnArgs& a, const SplitPlan& p,
                                cudaStream_t st) {
-  attention_prepare();
-  if (g_prepare_status != cudaSuccess) return g_prepare_status;
-  cudaError_t e = cudaSuccess;
+  cudaError_t e = attention_prepare();
+  if (e != cudaSuccess) return e;
   for (int c = 0; c < p.chunks; ++c) {
     AttnArgs ac = a;
     ac.tq0 = c * p.lq_chunk;
@@ -1244,6 +1242,7 @@ extern "C" int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int L
   HG_CHECK_ARG(ctx && q && k_cache && v_cache && block_table && seq_lens && out && workspace,
                "higgs_paged_attention: null argument");
   HG_CHECK_ARG(D == 64 || D == 128, "higgs_paged_attention: D must be 64 or 128");
+  HG_DEVICE(ctx);
   const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
                          attn_ws_bytes(p, B, Hkv, D), workspace);
@@ -1294,6 +1293,7 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
                "higgs_paged_attention_tq4: null argument");
   HG_CHECK_ARG(page_stride % 64 == 0 && head_stride % 64 == 0,
                "higgs_paged_attention_tq4: strides must be multiples of 64 bytes");
+  HG_DEVICE(ctx);
   const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
                          attn_ws_bytes(p, B, Hkv, 128), workspace);
@@ -1352,6 +1352,7 @@ int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int H
                "higgs_fused_attention: give both q and k norm weights or neither");
   HG_CHECK_ARG(Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) * Lq <= 32,
                "higgs_fused_attention: needs (Hq / Hkv) * Lq <= 32");
+  HG_DEVICE(ctx);
   const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len, g_fused_min_pages);
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
                          attn_ws_bytes(p, B, Hkv, D), workspace);
@@ -1386,8 +1387,7 @@ int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int H
   a.inv_freq = inv_freq;
   a.slots = slot_mapping;
   if (pf) a.pf = *pf;
-  attention_prepare();
-  HG_CUDA(g_prepare_status);
+  HG_CUDA(attention_prepare());
   const int MT = p.rows_pad / 16;
   const size_t smem = smem_fused(D, MT, Lq);
   cudaStream_t st = (cudaStream_t)stream;
@@ -1471,6 +1471,7 @@ extern "C" int higgs_paged_attention_noalloc(higgs_ctx* ctx, const void* q, int 
   HG_CHECK_ARG(D == 64 || D == 128, "higgs_paged_attention_noalloc: D must be 64 or 128");
   HG_CHECK_ARG(B > 0 && Lq > 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0,
                "higgs_paged_attention_noalloc: bad batch / head shape");
+  HG_DEVICE(ctx);
   const size_t need = attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len), B, Hkv, D);
   if (need > kNoAllocScratchBytes)
     return fail(HIGGS_ERR_WORKSPACE,
@@ -1478,10 +1479,8 @@ extern "C" int higgs_paged_attention_noalloc(higgs_ctx* ctx, const void* q, int 
                     " bytes of scratch, more than the built-in " +
                     std::to_string(kNoAllocScratchBytes) +
                     " bytes; use higgs_paged_attention with a caller-provided workspace");
-  int device = 0;
-  HG_CUDA(cudaGetDevice(&device));
   cudaError_t err;
-  void* scratch = noalloc_scratch_ptr(device, &err);
+  void* scratch = noalloc_scratch_ptr(ctx->device, &err);
   if (!scratch) return cuda_fail(err, "cudaGetSymbolAddress(g_noalloc_scratch)");
   // the split counters must start at zero whatever an earlier call left behind
   HG_CUDA(cudaMemsetAsync(scratch, 0, kCounterBytes, (cudaStream_t)stream));

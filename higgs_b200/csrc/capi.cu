@@ -1,14 +1,36 @@
 // capi.cu -- context lifetime and the thread-local error channel of the C ABI.
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
 
-struct higgs_ctx {
-  int device;
-  int sms;
-};
-
 namespace higgs {
+
+DeviceState& device_state(int dev) {
+  static DeviceState states[kMaxDevices];
+  return states[(dev >= 0 && dev < kMaxDevices) ? dev : 0];
+}
+
+// Per-device set-up done by the first higgs_init on each device, with that
+// device current: the multiprocessor count and the tensor-core matmul's
+// timeout flag (the only device memory the library holds per device).
+static int device_setup(int dev, int sms) {
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  DeviceState& st = device_state(dev);
+  st.sms = sms;
+  if (!st.tc_err) {
+    int* p = nullptr;
+    HG_CUDA(cudaMalloc(&p, sizeof(int)));
+    const cudaError_t e = cudaMemset(p, 0, sizeof(int));
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      return cuda_fail(e, "cudaMemset(tensor-core error flag)");
+    }
+    st.tc_err = p;
+  }
+  return HIGGS_OK;
+}
 
 static thread_local std::string g_last_error;
 
@@ -111,7 +133,9 @@ extern "C" int higgs_init(int device, higgs_ctx** out) {
   int n = 0;
   HG_CUDA(cudaGetDeviceCount(&n));
   HG_CHECK_ARG(device >= 0 && device < n, "higgs_init: no such device");
-  HG_CUDA(cudaSetDevice(device));
+  HG_CHECK_ARG(device < kMaxDevices, "higgs_init: device ordinal above 63");
+  DeviceGuard guard;  // set-up runs on `device`; the caller's current device is restored
+  if (int e = guard.enter(device)) return e;
   int major = 0, minor = 0, sms = 0;
   HG_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
   HG_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
@@ -119,6 +143,7 @@ extern "C" int higgs_init(int device, higgs_ctx** out) {
   if (major != 10 || minor != 0)
     return fail(HIGGS_ERR_UNSUPPORTED, "higgs_init: device is sm_" + std::to_string(major) +
                                            std::to_string(minor) + ", this build targets sm_100a");
+  if (int e = device_setup(device, sms)) return e;
   qgemm_tc_prepare();
   higgs_ctx* c = new higgs_ctx;
   c->device = device;

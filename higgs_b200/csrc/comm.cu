@@ -211,12 +211,13 @@ using namespace higgs;
 extern "C" int higgs_comm_create(higgs_ctx* ctx, int rank, int world, size_t words_per_call,
                                  int n_calls, higgs_comm** out, void* ipc_handle_out) {
   HG_CHECK_ARG(ctx && out && ipc_handle_out, "higgs_comm_create: null argument");
+  HG_DEVICE(ctx);
   *out = nullptr;
   HG_CHECK_ARG(world >= 1 && world <= kMaxRanks && rank >= 0 && rank < world,
                "higgs_comm_create: bad rank / world (world <= 8)");
   HG_CHECK_ARG(words_per_call > 0 && n_calls > 0, "higgs_comm_create: empty communicator");
   higgs_comm* c = new higgs_comm;
-  cudaGetDevice(&c->device);
+  c->device = ctx->device;
   c->rank = rank;
   c->world = world;
   c->n_calls = n_calls;
@@ -245,6 +246,7 @@ extern "C" int higgs_comm_create(higgs_ctx* ctx, int rank, int world, size_t wor
 
 extern "C" int higgs_comm_connect(higgs_comm* c, const void* handles) {
   HG_CHECK_ARG(c && handles, "higgs_comm_connect: null argument");
+  HG_DEVICE(c);
   const char* hs = static_cast<const char*>(handles);
   for (int q = 0; q < c->world; ++q) {
     if (q == c->rank) continue;
@@ -259,6 +261,8 @@ extern "C" int higgs_comm_connect(higgs_comm* c, const void* handles) {
 
 extern "C" int higgs_comm_destroy(higgs_comm* c) {
   if (!c) return HIGGS_OK;
+  DeviceGuard guard;
+  guard.enter(c->device);
   for (int q = 0; q < c->world; ++q)
     if (q != c->rank && c->peer[q]) cudaIpcCloseMemHandle(c->peer[q]);
   if (c->buf) cudaFree(c->buf);
@@ -271,6 +275,7 @@ extern "C" size_t higgs_comm_handle_size(void) { return sizeof(cudaIpcMemHandle_
 
 extern "C" int higgs_comm_error(higgs_comm* c, int* out) {
   HG_CHECK_ARG(c && out, "higgs_comm_error: null argument");
+  HG_DEVICE(c);
   int v = 0;
   HG_CUDA(cudaMemcpy(&v, c->err, sizeof(int), cudaMemcpyDeviceToHost));
   *out = v;
@@ -280,6 +285,7 @@ extern "C" int higgs_comm_error(higgs_comm* c, int* out) {
 
 extern "C" int higgs_comm_step(higgs_comm* c, void* stream) {
   HG_CHECK_ARG(c, "higgs_comm_step: null communicator");
+  HG_DEVICE(c);
   HG_CUDA(comm_step(c, (cudaStream_t)stream));
   return HIGGS_OK;
 }
@@ -290,6 +296,7 @@ extern "C" int higgs_allreduce_residual(higgs_comm* c, int call, const float* pa
   HG_CHECK_ARG(call >= 0 && call < c->n_calls && (size_t)n <= c->words,
                "higgs_allreduce_residual: call index or size outside the communicator");
   HG_CHECK_ARG(((uintptr_t)partial & 15) == 0, "higgs_allreduce_residual: partial must be 16-byte aligned");
+  HG_DEVICE(c);
   if (n == 0) return HIGGS_OK;
   HG_CUDA(comm_allreduce_residual(c, call, partial, n, (uint16_t*)h, (cudaStream_t)stream));
   return HIGGS_OK;
@@ -301,6 +308,7 @@ extern "C" int higgs_allreduce_argmax(higgs_comm* c, int call, const uint64_t* k
   HG_CHECK_ARG(call >= 0 && call < c->n_calls && (size_t)2 * n <= c->words,
                "higgs_allreduce_argmax: call index or size outside the communicator");
   HG_CHECK_ARG(((uintptr_t)keys & 15) == 0, "higgs_allreduce_argmax: keys must be 16-byte aligned");
+  HG_DEVICE(c);
   if (n == 0) return HIGGS_OK;
   HG_CUDA(comm_allreduce_argmax(c, call, (const unsigned long long*)keys, n, out,
                                 (cudaStream_t)stream));

@@ -50,16 +50,92 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
-inline int sm_count() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
+// ---------------------------------------------------------------------------
+// per-device state
+// ---------------------------------------------------------------------------
+// A process may hold contexts on several GPUs.  Every entry point that takes a
+// context (or a model / communicator built on one) makes that context's
+// device current for the duration of the call (DeviceGuard), so helpers below
+// it can key their state on the current device.  Device-side state (the
+// tensor-core matmul's timeout flag) is allocated by higgs_init, once per
+// device; nothing allocates lazily inside a compute call.
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  int sms = 0;            // multiprocessor count
+  int* tc_err = nullptr;  // tensor-core matmul timeout flag (device int)
+};
+
+// State of device `dev` (0 <= dev < kMaxDevices); filled by higgs_init.
+DeviceState& device_state(int dev);
+
+inline int current_device() {
+  int d = 0;
+  if (cudaGetDevice(&d) != cudaSuccess || d < 0 || d >= kMaxDevices) d = 0;
+  return d;
 }
+
+inline int sm_count() {
+  const int n = device_state(current_device()).sms;
+  return n > 0 ? n : 148;
+}
+
+// A one-time host action (a kernel attribute) done once per device: a kernel's
+// dynamic shared-memory limit is a per-device setting.  Two threads may both
+// run the action the first time; it is idempotent.
+struct PerDeviceOnce {
+  unsigned long long done = 0;
+  template <typename Fn>
+  cudaError_t run(Fn fn) {
+    const unsigned long long bit = 1ull << current_device();
+    if (__atomic_load_n(&done, __ATOMIC_ACQUIRE) & bit) return cudaSuccess;
+    const cudaError_t e = fn();
+    if (e == cudaSuccess) __atomic_fetch_or(&done, bit, __ATOMIC_ACQ_REL);
+    return e;
+  }
+};
+
+// Makes `dev` current for one entry-point call and restores the caller's
+// device on return.
+class DeviceGuard {
+ public:
+  DeviceGuard() = default;
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+  int enter(int dev) {
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (cur == dev) return 0;
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice(context device)");
+    prev_ = cur;
+    return 0;
+  }
+  ~DeviceGuard() {
+    if (prev_ >= 0) cudaSetDevice(prev_);
+  }
+
+ private:
+  int prev_ = -1;
+};
+
+}  // namespace higgs
+
+struct higgs_ctx {
+  int device;
+  int sms;
+};
+
+namespace higgs {
+
+// First statement of an entry point after its null checks: run on ctx's device.
+#define HG_DEVICE(ctx_)                                               \
+  ::higgs::DeviceGuard hg_device_guard_;                              \
+  do {                                                                \
+    const int hg_e_ = hg_device_guard_.enter((ctx_)->device);         \
+    if (hg_e_ != 0) return hg_e_;                                     \
+  } while (0)
 
 // ---------------------------------------------------------------------------
 // device helpers

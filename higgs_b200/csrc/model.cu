@@ -49,7 +49,7 @@ struct LayerW {
   QW router, egate, eup, edown;  // e*: w/s/b point at expert 0, N/K per expert
 };
 
-void attention_prepare();
+cudaError_t attention_prepare();
 
 }  // namespace higgs
 
@@ -75,6 +75,7 @@ struct higgs_model {
 };
 
 struct higgs_graph {
+  int device = 0;  // the capturing model's device
   cudaGraphExec_t exec = nullptr;
   int kernel_nodes = 0;
 };
@@ -529,6 +530,7 @@ int validate_forward(higgs_model* m, const higgs_forward_args* f) {
 
 extern "C" int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg, higgs_model** out) {
   HG_CHECK_ARG(ctx && cfg && out, "higgs_model_create: null argument");
+  HG_DEVICE(ctx);
   *out = nullptr;
   const higgs_model_config& c = *cfg;
   HG_CHECK_ARG(c.hidden > 0 && c.hidden % 256 == 0, "higgs_model_create: hidden must be a multiple of 256");
@@ -570,6 +572,8 @@ extern "C" int higgs_model_create(higgs_ctx* ctx, const higgs_model_config* cfg,
 
 extern "C" int higgs_model_destroy(higgs_model* m) {
   if (!m) return HIGGS_OK;
+  DeviceGuard guard;
+  guard.enter(m->ctx->device);
   if (m->inv_freq) cudaFree(m->inv_freq);
   delete m;
   return HIGGS_OK;
@@ -581,6 +585,7 @@ extern "C" int higgs_model_set_tensor(higgs_model* m, const char* name, const vo
                "higgs_model_set_tensor: bad argument");
   HG_CHECK_ARG(dtype == HIGGS_DTYPE_U32 || dtype == HIGGS_DTYPE_BF16 || dtype == HIGGS_DTYPE_F32,
                "higgs_model_set_tensor: unknown dtype");
+  HG_DEVICE(m->ctx);
   TensorRef t;
   t.ptr = ptr;
   t.dtype = dtype;
@@ -592,6 +597,7 @@ extern "C" int higgs_model_set_tensor(higgs_model* m, const char* name, const vo
 
 extern "C" int higgs_model_finalize(higgs_model* m) {
   HG_CHECK_ARG(m, "higgs_model_finalize: null model");
+  HG_DEVICE(m->ctx);
   const higgs_model_config& c = m->cfg;
   const int H = c.hidden, D = c.head_dim;
   int rc = get_q(m, "model.embed_tokens", c.vocab, H, m->embed);
@@ -646,7 +652,7 @@ extern "C" int higgs_model_finalize(higgs_model* m) {
     HG_CUDA(cudaMalloc(&m->inv_freq, f.size() * sizeof(float)));
     HG_CUDA(cudaMemcpy(m->inv_freq, f.data(), f.size() * sizeof(float), cudaMemcpyHostToDevice));
   }
-  attention_prepare();
+  HG_CUDA(attention_prepare());
   m->finalized = true;
   return HIGGS_OK;
 }
@@ -654,6 +660,7 @@ extern "C" int higgs_model_finalize(higgs_model* m) {
 extern "C" int higgs_model_set_comm(higgs_model* m, higgs_comm* comm) {
   HG_CHECK_ARG(m && comm, "higgs_model_set_comm: null argument");
   HG_CHECK_ARG(m->cfg.tp_world > 1, "higgs_model_set_comm: the model is not a tensor-parallel shard");
+  HG_DEVICE(m->ctx);
   m->comm = comm;
   return HIGGS_OK;
 }
@@ -662,6 +669,7 @@ extern "C" int higgs_model_set_kv_cache(higgs_model* m, void* k_pool, void* v_po
                                         int64_t num_pages) {
   HG_CHECK_ARG(m && k_pool && v_pool && num_pages > 0, "higgs_model_set_kv_cache: bad argument");
   HG_CHECK_ARG(m->cfg.kv_mode == HIGGS_KV_BF16, "higgs_model_set_kv_cache: model uses TurboQuant KV");
+  HG_DEVICE(m->ctx);
   m->k_pool = k_pool;
   m->v_pool = v_pool;
   m->num_pages = num_pages;
@@ -674,6 +682,7 @@ extern "C" int higgs_model_set_kv_cache_tq4(higgs_model* m, uint8_t* k_codes, vo
   HG_CHECK_ARG(m && k_codes && k_scales && v_codes && v_scales && signs && num_pages > 0,
                "higgs_model_set_kv_cache_tq4: bad argument");
   HG_CHECK_ARG(m->cfg.kv_mode == HIGGS_KV_TQ4, "higgs_model_set_kv_cache_tq4: model uses bf16 KV");
+  HG_DEVICE(m->ctx);
   m->k_pool = k_codes;
   m->v_pool = v_codes;
   m->k_scales = k_scales;
@@ -692,12 +701,14 @@ extern "C" size_t higgs_model_workspace_size(const higgs_model* m, int B, int Lq
 extern "C" int higgs_model_forward(higgs_model* m, const higgs_forward_args* f, void* stream) {
   int rc = validate_forward(m, f);
   if (rc) return rc;
+  HG_DEVICE(m->ctx);
   return forward_impl(m, f, (cudaStream_t)stream);
 }
 
 extern "C" int higgs_model_capture(higgs_model* m, const higgs_forward_args* f, void* stream,
                                    higgs_graph** out) {
-  HG_CHECK_ARG(out && stream, "higgs_model_capture: needs a non-default stream and an out pointer");
+  HG_CHECK_ARG(m && out && stream, "higgs_model_capture: needs a model, a non-default stream and an out pointer");
+  HG_DEVICE(m->ctx);
   *out = nullptr;
   int rc = validate_forward(m, f);
   if (rc) return rc;
@@ -726,6 +737,7 @@ extern "C" int higgs_model_capture(higgs_model* m, const higgs_forward_args* f, 
   cudaGraphDestroy(graph);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGraphInstantiate");
   higgs_graph* g = new higgs_graph;
+  g->device = m->ctx->device;
   g->exec = exec;
   g->kernel_nodes = kernels;
   *out = g;
@@ -734,6 +746,7 @@ extern "C" int higgs_model_capture(higgs_model* m, const higgs_forward_args* f, 
 
 extern "C" int higgs_graph_launch(higgs_graph* g, void* stream) {
   HG_CHECK_ARG(g && g->exec, "higgs_graph_launch: null graph");
+  HG_DEVICE(g);
   HG_CUDA(cudaGraphLaunch(g->exec, (cudaStream_t)stream));
   return HIGGS_OK;
 }
@@ -742,6 +755,8 @@ extern "C" int higgs_graph_num_kernels(const higgs_graph* g) { return g ? g->ker
 
 extern "C" int higgs_graph_destroy(higgs_graph* g) {
   if (!g) return HIGGS_OK;
+  DeviceGuard guard;
+  guard.enter(g->device);
   if (g->exec) cudaGraphExecDestroy(g->exec);
   delete g;
   return HIGGS_OK;

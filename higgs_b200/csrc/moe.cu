@@ -368,6 +368,7 @@ extern "C" int higgs_moe_route_topk(higgs_ctx* ctx, const void* logits, int dtyp
   HG_CHECK_ARG(E > 0 && E <= 1024, "higgs_moe_route_topk: E must be in [1, 1024]");
   HG_CHECK_ARG(k > 0 && k <= 32 && k <= E, "higgs_moe_route_topk: k must be in [1, min(E, 32)]");
   HG_CHECK_ARG(T >= 0 && (int64_t)T * k <= 65536, "higgs_moe_route_topk: T * k must be <= 65536");
+  HG_DEVICE(ctx);
   if (T == 0) return HIGGS_OK;
   if (plan)
     HG_CHECK_ARG(plan_bytes >= moe_plan_bytes(T, E, k) && ((uintptr_t)plan & 15) == 0,
@@ -391,6 +392,7 @@ extern "C" int higgs_moe_grouped_w4(higgs_ctx* ctx, const void* x, int T, int K,
   HG_CHECK_ARG(E > 0 && k > 0 && T >= 0 && moe_max_items(T * k, E) <= 65535,
                "higgs_moe_grouped_w4: bad T / k / E");
   HG_CHECK_ARG(((uintptr_t)plan & 15) == 0, "higgs_moe_grouped_w4: plan must be 16-byte aligned");
+  HG_DEVICE(ctx);
   if (T == 0) return HIGGS_OK;
   HG_CUDA(launch_moe_grouped((const uint16_t*)x, T, K, k, x_per_pair != 0, plan, E, N, w,
                              (const uint16_t*)scales, (const uint16_t*)biases, w_up,
@@ -405,6 +407,7 @@ extern "C" int higgs_moe_router(higgs_ctx* ctx, const void* x, int T, int K, con
   HG_CHECK_ARG(ctx && x && w && scales && biases && logits, "higgs_moe_router: null argument");
   HG_CHECK_ARG(T >= 0 && T <= 65535 && E > 0 && K > 0 && K % 64 == 0 && K / 64 <= 256,
                "higgs_moe_router: bad shape (K % 64 == 0, K <= 16384, T <= 65535)");
+  HG_DEVICE(ctx);
   if (T == 0) return HIGGS_OK;
   HG_CUDA(launch_moe_router((const uint16_t*)x, T, K, w, (const uint16_t*)scales,
                             (const uint16_t*)biases, E, (uint16_t*)logits, (cudaStream_t)stream));
@@ -416,6 +419,7 @@ extern "C" int higgs_moe_combine(higgs_ctx* ctx, const void* y, const float* sco
   HG_CHECK_ARG(ctx && y && scores && h, "higgs_moe_combine: null argument");
   HG_CHECK_ARG(T >= 0 && k > 0 && H > 0 && H % 8 == 0 && T <= 65535,
                "higgs_moe_combine: bad shape (H % 8 == 0, T <= 65535)");
+  HG_DEVICE(ctx);
   if (T == 0) return HIGGS_OK;
   HG_CUDA(launch_moe_combine((const uint16_t*)y, scores, T, k, H, (uint16_t*)h, (cudaStream_t)stream));
   return HIGGS_OK;

@@ -306,6 +306,7 @@ extern "C" int higgs_rmsnorm(higgs_ctx* ctx, const void* x, const void* residual
   HG_CHECK_ARG(ctx && x && weight && y, "higgs_rmsnorm: null argument");
   HG_CHECK_ARG(rows >= 0 && H > 0 && H % 8 == 0 && H <= 8192,
                "higgs_rmsnorm: need H % 8 == 0 and H <= 8192");
+  HG_DEVICE(ctx);
   if (rows == 0) return HIGGS_OK;
   HG_CUDA(launch_pdl(rmsnorm_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream,
                      (const uint16_t*)x, (const uint16_t*)residual, H, (const uint16_t*)weight, eps,
@@ -318,6 +319,7 @@ extern "C" int higgs_rmsnorm_strided(higgs_ctx* ctx, const void* x, int64_t in_s
   HG_CHECK_ARG(ctx && x && weight && y, "higgs_rmsnorm_strided: null argument");
   HG_CHECK_ARG(rows >= 0 && H > 0 && H % 8 == 0 && H <= 8192 && in_stride >= H && in_stride % 8 == 0,
                "higgs_rmsnorm_strided: need H % 8 == 0, H <= 8192, in_stride >= H, in_stride % 8 == 0");
+  HG_DEVICE(ctx);
   if (rows == 0) return HIGGS_OK;
   HG_CUDA(launch_pdl(rmsnorm_kernel, dim3(rows), dim3(256), 0, (cudaStream_t)stream,
                      (const uint16_t*)x, (const uint16_t*)nullptr, H, (const uint16_t*)weight, eps,
@@ -330,6 +332,7 @@ extern "C" int higgs_rope(higgs_ctx* ctx, const void* x, int rows, int heads, in
   HG_CHECK_ARG(ctx && x && positions && inv_freq && y, "higgs_rope: null argument");
   HG_CHECK_ARG(D == 64 || D == 128, "higgs_rope: D must be 64 or 128");
   HG_CHECK_ARG(rows >= 0 && heads > 0, "higgs_rope: bad shape");
+  HG_DEVICE(ctx);
   if (rows == 0) return HIGGS_OK;
   const int items = rows * heads;
   dim3 grid((items + 3) / 4);
@@ -355,6 +358,7 @@ extern "C" int higgs_qknorm_rope_kv_write(higgs_ctx* ctx, const void* qkv, int T
   HG_CHECK_ARG(T >= 0 && Hq > 0 && Hkv > 0 && Hq % Hkv == 0, "higgs_qknorm_rope_kv_write: bad heads");
   HG_CHECK_ARG((q_norm_w == nullptr) == (k_norm_w == nullptr),
                "higgs_qknorm_rope_kv_write: give both q and k norm weights or neither");
+  HG_DEVICE(ctx);
   if (T == 0) return HIGGS_OK;
   KvWriteArgs a = {};
   a.qkv = (const uint16_t*)qkv;
@@ -398,6 +402,7 @@ extern "C" int higgs_qknorm_rope_kv_write_tq4(
                "higgs_qknorm_rope_kv_write_tq4: strides must be multiples of 64 bytes");
   HG_CHECK_ARG((q_norm_w == nullptr) == (k_norm_w == nullptr),
                "higgs_qknorm_rope_kv_write_tq4: give both q and k norm weights or neither");
+  HG_DEVICE(ctx);
   if (T == 0) return HIGGS_OK;
   KvWriteArgs a = {};
   a.qkv = (const uint16_t*)qkv;
@@ -428,6 +433,7 @@ extern "C" int higgs_tq4_encode(higgs_ctx* ctx, const void* x, int64_t n, const 
                                 uint8_t* codes, void* scales, void* stream) {
   HG_CHECK_ARG(ctx && x && signs && codes && scales, "higgs_tq4_encode: null argument");
   HG_CHECK_ARG(n >= 0, "higgs_tq4_encode: bad count");
+  HG_DEVICE(ctx);
   if (n == 0) return HIGGS_OK;
   HG_CUDA(launch_pdl(tq4_encode_kernel, dim3((unsigned)((n + 3) / 4)), dim3(128), 0,
                      (cudaStream_t)stream, (const uint16_t*)x, n, signs, codes, (__half*)scales));

@@ -505,14 +505,8 @@ bool w_tensor_map(const void* w, int rows, int K, CUtensorMap* out) {
   return true;
 }
 
-int* tc_err_ptr() {
-  static int* p = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    if (cudaMalloc(&p, sizeof(int)) == cudaSuccess) cudaMemset(p, 0, sizeof(int));
-  });
-  return p;
-}
+// the current device's timeout flag, allocated by higgs_init
+int* tc_err_ptr() { return device_state(current_device()).tc_err; }
 
 template <int BN, bool SWIGLU>
 cudaError_t launch_bn(const CUtensorMap& map, const WMaps& wm, const TcArgs& a, dim3 grid, cudaStream_t st) {
@@ -521,26 +515,14 @@ cudaError_t launch_bn(const CUtensorMap& map, const WMaps& wm, const TcArgs& a, 
   constexpr size_t smem = (size_t)AS * (NA * kTileA + BN * 128) + (size_t)kPkStages * NA * kPkTile + 1024;
   static_assert(smem <= 227 * 1024, "shared memory budget");
   auto k = qgemm_tc_kernel<BN, SWIGLU>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  cudaError_t e = attr.run(
+      [&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
+  if (e != cudaSuccess) return e;
   return launch_pdl(k, grid, dim3(kTcThreads), smem, st, map, wm, a);
 }
 
-int tc_sms() {
-  static int n = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess ||
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
-      n = 148;
-  });
-  return n;
-}
+int tc_sms() { return sm_count(); }
 
 // K splits of a launch: the count that minimises waves x (k groups per split + a fixed
 // cost per wave, in k-group units), at most g_tc_waves waves of one CTA per SM and at
@@ -658,12 +640,8 @@ cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_byte
 void set_gemm_tc_waves(int w) { g_tc_waves = w < 1 ? 1 : (w > 8 ? 8 : w); }
 void set_gemm_tc_wave_cost(int c) { g_tc_wave_cost = c < 0 ? 0 : (c > 1000 ? 1000 : c); }
 
-// one-time host state (error flag, driver entry point, SM count): call before any stream capture
-void qgemm_tc_prepare() {
-  tc_err_ptr();
-  encode_fn();
-  tc_sms();
-}
+// one-time host state (the driver's tensor-map encoder): call before any stream capture
+void qgemm_tc_prepare() { encode_fn(); }
 
 int qgemm_tc_error_and_clear() {
   int* p = tc_err_ptr();
@@ -676,8 +654,9 @@ int qgemm_tc_error_and_clear() {
 
 }  // namespace higgs
 
-extern "C" int higgs_tc_error(int* out) {
-  HG_CHECK_ARG(out, "higgs_tc_error: null argument");
+extern "C" int higgs_tc_error(higgs_ctx* ctx, int* out) {
+  HG_CHECK_ARG(ctx && out, "higgs_tc_error: null argument");
+  HG_DEVICE(ctx);
   *out = higgs::qgemm_tc_error_and_clear();
   return HIGGS_OK;
 }

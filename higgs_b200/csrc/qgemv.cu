@@ -596,12 +596,10 @@ int g_force_wk = 0;
 template <int NT8, int WK, int EPI, int S, bool XSMEM, bool NORM, bool F16, bool GATHER, bool ONE>
 cudaError_t launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
   auto k = qgemv_ring_kernel<NT8, WK, EPI, S, XSMEM, NORM, F16, GATHER, ONE>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  const cudaError_t e =
+      attr.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); });
+  if (e != cudaSuccess) return e;
   return launch_pdl(k, dim3(ctas, GATHER ? a.moe_max_items : 1), dim3(256), smem, st, a);
 }
 

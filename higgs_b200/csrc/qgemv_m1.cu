@@ -418,12 +418,10 @@ int g_m1_l1 = 0;  // units ahead of the register ring that are prefetched into L
 template <int WK, int EPI, bool NORM, int D>
 cudaError_t m1_launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
   auto k = qgemv_m1_kernel<WK, EPI, NORM, D>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  static PerDeviceOnce attr;
+  const cudaError_t e =
+      attr.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024); });
+  if (e != cudaSuccess) return e;
   return launch_pdl(k, dim3(ctas), dim3(kM1Threads), smem, st, a);
 }
 

@@ -322,12 +322,12 @@ cudaError_t launch_qgemv_sk(SkArgs a, void* workspace, cudaStream_t st) {
   a.partials = (float*)(ws + kSkCounterBytes);
   if (a.norm_w) {
     const size_t smem = (size_t)a.M * (a.K + 8) * 2;
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(qgemv_sk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           8 * (8192 + 8) * 2);
-      attr = true;
-    }
+    static PerDeviceOnce attr;
+    const cudaError_t e = attr.run([] {
+      return cudaFuncSetAttribute(qgemv_sk_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  8 * (8192 + 8) * 2);
+    });
+    if (e != cudaSuccess) return e;
     return launch_pdl(qgemv_sk_kernel<true>, dim3(grid), dim3(256), smem, st, a);
   }
   return launch_pdl(qgemv_sk_kernel<false>, dim3(grid), dim3(256), 0, st, a);
@@ -369,6 +369,7 @@ extern "C" int higgs_rmsnorm_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M,
   HG_CHECK_ARG(M >= 1 && (M <= 8 || !norm_w), "higgs_rmsnorm_qlinear_w4g64: fused norm needs M in [1, 8]");
   HG_CHECK_ARG(K % 256 == 0 && N % 16 == 0 && N > 0, "higgs_rmsnorm_qlinear_w4g64: need K % 256 == 0, N % 16 == 0");
   HG_CHECK_ARG(!residual || y, "higgs_rmsnorm_qlinear_w4g64: residual needs a bf16 y");
+  HG_DEVICE(ctx);
   if (M > 8) {
     QLinArgs q = {};
     q.x = (const uint16_t*)x;
@@ -438,6 +439,7 @@ extern "C" int higgs_rmsnorm_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M
                "higgs_rmsnorm_gate_up_swiglu: null argument");
   HG_CHECK_ARG(M >= 1 && (M <= 8 || !norm_w), "higgs_rmsnorm_gate_up_swiglu: fused norm needs M in [1, 8]");
   HG_CHECK_ARG(K % 256 == 0 && N % 16 == 0 && N > 0, "higgs_rmsnorm_gate_up_swiglu: need K % 256 == 0, N % 16 == 0");
+  HG_DEVICE(ctx);
   if (M > 8) {
     QLinArgs q = {};
     q.x = (const uint16_t*)x;

@@ -393,6 +393,7 @@ extern "C" int higgs_w4_quantize(higgs_ctx* ctx, const float* w, int64_t N, int 
                                  void* scales, void* biases, void* stream) {
   HG_CHECK_ARG(ctx && w && q && scales && biases, "higgs_w4_quantize: null argument");
   HG_CHECK_ARG(N >= 0 && K > 0 && K % 64 == 0, "higgs_w4_quantize: need K % 64 == 0");
+  HG_DEVICE(ctx);
   if (N == 0) return HIGGS_OK;
   const int64_t total = N * (K / 64);
   const int64_t want = (total + 127) / 128;
@@ -407,6 +408,7 @@ extern "C" int higgs_w4_dequantize(higgs_ctx* ctx, const uint32_t* w, const void
                                    const void* biases, int N, int K, void* out, void* stream) {
   HG_CHECK_ARG(ctx && w && scales && biases && out, "higgs_w4_dequantize: null argument");
   HG_CHECK_ARG(N > 0 && K > 0 && K % 64 == 0, "higgs_w4_dequantize: need N > 0, K % 64 == 0");
+  HG_DEVICE(ctx);
   const int64_t total = (int64_t)N * (K / 8);
   const int blocks = (int)((total + 255) / 256 < 8 * sm_count() ? (total + 255) / 256 : 8 * sm_count());
   dequant_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(
@@ -421,6 +423,7 @@ extern "C" int higgs_embed_gather_w4(higgs_ctx* ctx, const int32_t* ids, int n_i
   HG_CHECK_ARG(ctx && ids && w && scales && biases && out, "higgs_embed_gather_w4: null argument");
   HG_CHECK_ARG(n_ids >= 0 && V > 0 && H > 0 && H % 64 == 0,
                "higgs_embed_gather_w4: need H % 64 == 0");
+  HG_DEVICE(ctx);
   if (n_ids == 0) return HIGGS_OK;
   HG_CUDA(launch_pdl(embed_gather_kernel, dim3(n_ids), dim3(128), 0, (cudaStream_t)stream, ids, w,
                      (const uint16_t*)scales, (const uint16_t*)biases, V, H, (uint16_t*)out));
@@ -436,6 +439,7 @@ extern "C" int higgs_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M, int K, 
   HG_CHECK_ARG(M >= 0 && K > 0 && N > 0, "higgs_qlinear_w4g64: bad shape");
   HG_CHECK_ARG(K % 256 == 0, "higgs_qlinear_w4g64: K must be a multiple of 256");
   HG_CHECK_ARG(N % 16 == 0, "higgs_qlinear_w4g64: N must be a multiple of 16");
+  HG_DEVICE(ctx);
   if (M == 0) return HIGGS_OK;
   QLinArgs a = {};
   a.x = (const uint16_t*)x;
@@ -463,6 +467,7 @@ extern "C" int higgs_qlinear_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M
   HG_CHECK_ARG(M >= 0 && K > 0 && N > 0, "higgs_qlinear_gate_up_swiglu: bad shape");
   HG_CHECK_ARG(K % 256 == 0, "higgs_qlinear_gate_up_swiglu: K must be a multiple of 256");
   HG_CHECK_ARG(N % 16 == 0, "higgs_qlinear_gate_up_swiglu: N must be a multiple of 16");
+  HG_DEVICE(ctx);
   if (M == 0) return HIGGS_OK;
   QLinArgs a = {};
   a.x = (const uint16_t*)x;

@@ -391,6 +391,7 @@ extern "C" int higgs_argmax(higgs_ctx* ctx, const float* logits, int B, int V, i
                             void* stream) {
   HG_CHECK_ARG(ctx && logits && out, "higgs_argmax: null argument");
   HG_CHECK_ARG(B >= 0 && V > 0, "higgs_argmax: bad shape");
+  HG_DEVICE(ctx);
   if (B == 0) return HIGGS_OK;
   HG_CHECK_ARG(B <= 65535, "higgs_argmax: B > 65535");
   HG_CUDA(launch_pdl(argmax_cluster_kernel, dim3(kArgmaxCluster, B), dim3(kArgmaxThreads), 0,
@@ -404,6 +405,7 @@ extern "C" int higgs_sample(higgs_ctx* ctx, const float* logits, int B, int V, f
   HG_CHECK_ARG(B >= 0 && V > 0, "higgs_sample: bad shape");
   HG_CHECK_ARG(temperature >= 0.0f, "higgs_sample: negative temperature");
   HG_CHECK_ARG(temperature == 0.0f || uniforms, "higgs_sample: uniforms required when T > 0");
+  HG_DEVICE(ctx);
   if (B == 0) return HIGGS_OK;
   const int greedy = temperature == 0.0f;
   const float inv_t = greedy ? 1.0f : 1.0f / temperature;
@@ -423,6 +425,7 @@ extern "C" int higgs_spec_accept(higgs_ctx* ctx, const float* target_logits,
   HG_CHECK_ARG(temperature >= 0.0f, "higgs_spec_accept: negative temperature");
   HG_CHECK_ARG(temperature == 0.0f || (draft_logits && accept_uniforms && sample_uniforms),
                "higgs_spec_accept: draft logits and uniforms required when T > 0");
+  HG_DEVICE(ctx);
   if (B == 0) return HIGGS_OK;
   const int greedy = temperature == 0.0f;
   const float inv_t = greedy ? 1.0f : 1.0f / temperature;
@@ -440,6 +443,7 @@ extern "C" int higgs_apply_penalties(higgs_ctx* ctx, float* logits, int B, int V
   HG_CHECK_ARG(B >= 0 && V > 0 && max_hist >= 0, "higgs_apply_penalties: bad shape");
   HG_CHECK_ARG(max_hist == 0 || (history && hist_lens), "higgs_apply_penalties: null history");
   HG_CHECK_ARG(rep > 0.0f, "higgs_apply_penalties: repetition penalty must be > 0");
+  HG_DEVICE(ctx);
   if (B == 0 || max_hist == 0) return HIGGS_OK;
   HG_CUDA(launch_pdl(penalties_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, logits, V,
                      history, hist_lens, max_hist, rep, freq, pres));

@@ -25,7 +25,7 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_last_error": (ctypes.c_char_p, []),
     "higgs_version": (I, []),
     "higgs_set_option": (I, [ctypes.c_char_p, I]),
-    "higgs_tc_error": (I, [ctypes.POINTER(I)]),
+    "higgs_tc_error": (I, [P, ctypes.POINTER(I)]),
     "higgs_w4_dequantize": (I, [P, P, P, P, I, I, P, P]),
     "higgs_w4_quantize": (I, [P, P, I64, I, P, P, P, P]),
     "higgs_embed_gather_w4": (I, [P, P, I, P, P, P, I, I, P, P]),

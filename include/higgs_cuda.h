@@ -12,12 +12,21 @@
  *     for the most recent failure.
  *   - All tensor arguments are caller-owned DEVICE pointers on the context's
  *     device, row-major and densely packed unless a stride says otherwise.
- *     "bf16" / "fp16" buffers are passed as void*.
+ *     "bf16" / "fp16" buffers are passed as void*.  Every call that takes a
+ *     context (or a model / communicator / graph built on one) runs on that
+ *     context's device whatever device is current, and restores the caller's
+ *     current device before it returns; one process may hold contexts on
+ *     several GPUs (device ordinals 0..63).
  *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Calls only
  *     enqueue work; they do not synchronise.  Device memory is allocated only
- *     by higgs_init() and higgs_model_finalize() (a RoPE table); every other
- *     call takes its scratch from caller-provided workspace whose size a
+ *     by higgs_init() (one int per device, the first time a device is
+ *     initialised), higgs_model_finalize() (a RoPE table) and
+ *     higgs_comm_create() (the peer-exchange buffers); every other call takes
+ *     its scratch from caller-provided workspace whose size a
  *     *_workspace_size() query returns.
+ *   - Per-device state lives until the process exits and does not survive a
+ *     device reset (cudaDeviceReset, or the primary context being destroyed):
+ *     after one, the library must not be used again in that process.
  *   - A context may be used by one host thread at a time; distinct contexts
  *     are independent.
  *   - Kernels start early behind the previous kernel on the stream
@@ -108,9 +117,10 @@ int higgs_version(void);
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
-/* Nonzero when a bounded wait of the tensor-core quantized matmul gave up since
- * the last call (the error flag is then cleared).  Synchronising. */
-int higgs_tc_error(int* out);
+/* Nonzero when a bounded wait of the tensor-core quantized matmul gave up on
+ * the context's device since the last call (the device's flag is then
+ * cleared).  Synchronising. */
+int higgs_tc_error(higgs_ctx* ctx, int* out);
 
 /* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
 
@@ -410,7 +420,10 @@ int higgs_moe_combine(higgs_ctx* ctx, const void* y, const float* scores, int T,
  * one-shot pushes into every rank's buffer with per-CTA flags; every rank must
  * issue the same calls in the same order, and higgs_comm_step once per step
  * before them.  A wait that sees no progress for about a second gives up and
- * sets the flag that higgs_comm_error returns (and clears). */
+ * sets the flag that higgs_comm_error returns (and clears); the results of that
+ * step are then undefined.  After a nonzero higgs_comm_error the ranks may no
+ * longer agree on the step number, so every rank must destroy its communicator
+ * and create and connect a new one before the next collective. */
 size_t higgs_comm_handle_size(void);
 int higgs_comm_create(higgs_ctx* ctx, int rank, int world, size_t words_per_call, int n_calls,
                       higgs_comm** out, void* ipc_handle_out);

@@ -60,6 +60,14 @@ static inline float h2f(uint16_t h) {
   return (float)v;
 }
 
+/* OpenMP team size for every parallel loop below; returns the size in force.
+ * A launcher may have set OMP_NUM_THREADS=1 in the environment (torchrun does),
+ * so the CPU baselines set it explicitly. */
+int orc_set_threads(int n) {
+  if (n > 0) omp_set_num_threads(n);
+  return omp_get_max_threads();
+}
+
 static inline uint16_t f2h(float f) {
   _Float16 v = (_Float16)f; /* IEEE round to nearest even */
   uint16_t h;
@@ -225,35 +233,71 @@ void orc_qmatmul(const uint16_t* x, int64_t M, int64_t K, const uint32_t* q,
 /*
  * The matrix (many-token) form of quantized_matmul: MLX's qmm dequantizes each
  * weight to the activation type before the dot products, so here
- * w = bf16(s*q + b) (one rounding of the exact value) and y = sum_k x_k w_k in
- * f32, k ascending.  The decode form above (qmv) keeps q exact.
+ * w = bf16(s*q + b) (one rounding of the exact value) and each output is an
+ * f32 dot product in a fixed order: eight lane sums s_j = sum over k = j mod 8
+ * (k ascending) of x_k*w_k, then y = ((s0+s1)+(s2+s3)) + ((s4+s5)+(s6+s7)).
+ * (MLX's tiled kernels fix no order either; the GPU tests bound the
+ * difference.)  The decode form above (qmv) keeps q exact.
+ *
+ * Blocked for speed only: rows of W are dequantized 16 at a time into an f32
+ * panel, and four outputs share each load of x.  The lane structure lets the
+ * compiler use 8-wide vectors (an AVX2 clone is picked at run time where the
+ * host has it) without reassociating any sum.
  */
+#define DQ_ROWS 16
+__attribute__((target_clones("avx2", "default")))
+static void dq_panel(const float* xf, int64_t M, int64_t K, const float* wp, int nrows,
+                     int64_t n0, int64_t N, float* y_f32, uint16_t* y_bf16) {
+  for (int64_t m = 0; m < M; ++m) {
+    const float* xr = xf + m * K;
+    for (int r = 0; r < nrows; r += 4) {
+      float acc[4][8];
+      for (int i = 0; i < 4; ++i)
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0f;
+      const int nr = nrows - r < 4 ? nrows - r : 4;
+      for (int64_t k = 0; k < K; k += 8) {
+        for (int i = 0; i < 4; ++i) {
+          const float* wr = wp + (int64_t)(r + (i < nr ? i : 0)) * K + k;
+          for (int j = 0; j < 8; ++j) acc[i][j] += xr[k + j] * wr[j];
+        }
+      }
+      for (int i = 0; i < nr; ++i) {
+        const float* a = acc[i];
+        const float v = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+        const int64_t n = n0 + r + i;
+        if (y_f32) y_f32[m * N + n] = v;
+        if (y_bf16) y_bf16[m * N + n] = f2bf(v);
+      }
+    }
+  }
+}
+
 void orc_qmatmul_dq(const uint16_t* x, int64_t M, int64_t K, const uint32_t* q,
                     const uint16_t* scales, const uint16_t* biases, int64_t N, float* y_f32,
                     uint16_t* y_bf16) {
   const int64_t G = K / 64;
   float* xf = (float*)malloc(sizeof(float) * (size_t)(M * K));
   for (int64_t i = 0; i < M * K; ++i) xf[i] = bf2f(x[i]);
+  const int64_t panels = (N + DQ_ROWS - 1) / DQ_ROWS;
 #pragma omp parallel
   {
-    float* wr = (float*)malloc(sizeof(float) * (size_t)K);
-#pragma omp for schedule(static)
-    for (int64_t n = 0; n < N; ++n) {
-      const uint32_t* row = q + n * (K / 8);
-      for (int64_t k = 0; k < K; ++k) {
-        const float sv = bf2f(scales[n * G + k / 64]), bv = bf2f(biases[n * G + k / 64]);
-        const float qv = (float)((row[k / 8] >> (4 * (k % 8))) & 0xF);
-        wr[k] = bf2f(f2bf(sv * qv + bv));
+    float* wp = (float*)malloc(sizeof(float) * (size_t)(DQ_ROWS * K));
+#pragma omp for schedule(dynamic)
+    for (int64_t pi = 0; pi < panels; ++pi) {
+      const int64_t n0 = pi * DQ_ROWS;
+      const int nrows = (int)(N - n0 < DQ_ROWS ? N - n0 : DQ_ROWS);
+      for (int r = 0; r < nrows; ++r) {
+        const int64_t n = n0 + r;
+        const uint32_t* row = q + n * (K / 8);
+        for (int64_t k = 0; k < K; ++k) {
+          const float sv = bf2f(scales[n * G + k / 64]), bv = bf2f(biases[n * G + k / 64]);
+          const float qv = (float)((row[k / 8] >> (4 * (k % 8))) & 0xF);
+          wp[r * K + k] = bf2f(f2bf(sv * qv + bv));
+        }
       }
-      for (int64_t m = 0; m < M; ++m) {
-        const float* xr = xf + m * K;
-        float acc = 0.0f;
-        for (int64_t k = 0; k < K; ++k) acc += xr[k] * wr[k];
-        if (y_f32) y_f32[m * N + n] = acc;
-        if (y_bf16) y_bf16[m * N + n] = f2bf(acc);
-      }
+      dq_panel(xf, M, K, wp, nrows, n0, N, y_f32, y_bf16);
     }
-    free(wr);
+    free(wp);
   }
   free(xf);
 }

@@ -83,9 +83,9 @@ class RefModel:
                  np.zeros((0, self.a.num_key_value_heads, self.a.head_dim), np.uint16)]
                 for _ in range(L)]
 
-    def forward(self, tokens, caches, n_layers: int = 0):
+    def forward(self, tokens, caches, n_layers: int = 0, last_only: bool = False):
         """tokens int [B, Lq]; caches: one new_cache() per sequence (appended in place).
-        Returns f32 logits [B, Lq, V]."""
+        Returns f32 logits [B, Lq, V] ([B, 1, V] for the last position with last_only)."""
         a = self.a
         B, Lq = tokens.shape
         H, D, Hq, Hkv = a.hidden_size, a.head_dim, a.num_attention_heads, a.num_key_value_heads
@@ -148,6 +148,9 @@ class RefModel:
             u = self.lin(x, p + "mlp.up_proj")
             d = self.lin(orc.silu_mul(g, u), p + "mlp.down_proj")
             h = _add_bf(h, d)
+        if last_only:
+            h = np.ascontiguousarray(h.reshape(B, Lq, -1)[:, -1])
+            Lq = 1
         x = orc.rmsnorm(h, self.w["model.norm.weight"], a.rms_norm_eps)[0]
         head = "model.embed_tokens" if a.tie_word_embeddings else "lm_head"
         _, logits = self.lin(x, head, want_f32=True)
@@ -158,7 +161,7 @@ class RefModel:
         logits of each step [steps, B, V])."""
         B = prompts.shape[0]
         caches = [self.new_cache() for _ in range(B)]
-        lg = self.forward(prompts, caches)[:, -1]
+        lg = self.forward(prompts, caches, last_only=True)[:, -1]
         toks, all_lg, near = [], [], []
         for _ in range(steps):
             nxt = orc.argmax(lg)

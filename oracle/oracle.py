@@ -37,6 +37,12 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+def set_threads(n: int) -> int:
+    """OpenMP threads for the oracle's parallel loops (n <= 0: unchanged); returns the count
+    in force."""
+    return int(lib().orc_set_threads(int(n)))
+
+
 def _ptr(a):
     return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
 

@@ -675,5 +675,5 @@ def test_qgemm_tc_no_timeouts():
     """No bounded mbarrier wait of the tensor-core kernel gave up in the tests above."""
     from higgs_b200 import ffi
     v = ctypes.c_int(-1)
-    ffi.call("higgs_tc_error", ctypes.byref(v))
+    ffi.call("higgs_tc_error", ffi.ctx(0), ctypes.byref(v))
     assert v.value == 0

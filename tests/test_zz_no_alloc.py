@@ -1,4 +1,5 @@
-"""GPU: the allocation-free attention entry point agrees with the workspace one.
+"""GPU: the allocation-free attention entry point agrees with the workspace one and
+with the CPU oracle.
 
 higgs_paged_attention_noalloc serves callers that cannot allocate device
 memory on their serving path (a host that owns a fixed device arena, or a
@@ -42,19 +43,36 @@ def _noalloc(q, kc, vc, bt, sl, max_seq_len):
     return out
 
 
+def _bits(t):
+    return t.view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+# (2, 12, 32, 8, 128): 48 query rows per kv head, so one call runs several query chunks that
+# reuse the shared split counters, with the largest scratch of these cases (4.5 MiB);
+# (37, 1, 32, 8, 128): B * Hkv = 296 split counters, long contexts.
 @pytest.mark.parametrize("B,Lq,Hq,Hkv,D,lens", [(1, 1, 32, 8, 128, [2048]),
                                                  (3, 1, 16, 8, 128, [700, 33, 1500]),
-                                                 (2, 6, 32, 8, 64, [300, 90])])
+                                                 (2, 6, 32, 8, 64, [300, 90]),
+                                                 (2, 12, 32, 8, 128, [2000, 1500]),
+                                                 (37, 1, 32, 8, 128, [4096 - 97 * i for i in range(37)])])
 def test_noalloc_matches_workspace_entry_point(B, Lq, Hq, Hkv, D, lens):
+    """Two calls in a row (they share the built-in scratch) against the workspace entry
+    point and against orc.paged_attention on the same inputs; tolerance abs / rel 1e-2, the
+    attention tests' bound."""
     from higgs_b200 import ops
     rng = np.random.default_rng(sum(lens) + Lq)
-    for call in range(2):  # two calls in a row share the built-in scratch
+    for call in range(2):
         q, kc, vc, bt, sl = _case(rng, B, Lq, Hq, Hkv, D, lens)
         ref = ops.paged_attention(q, kc, vc, bt, sl, max(lens))
         got = _noalloc(q, kc, vc, bt, sl, max(lens))
         torch.cuda.synchronize()
-        np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(),
-                                   atol=1e-2, rtol=1e-2, err_msg=f"call {call}")
+        g = got.float().cpu().numpy()
+        np.testing.assert_allclose(g, ref.float().cpu().numpy(), atol=1e-2, rtol=1e-2,
+                                   err_msg=f"call {call}: vs workspace entry point")
+        orc_out = orc.paged_attention(_bits(q), _bits(kc), _bits(vc), bt.cpu().numpy(),
+                                      sl.cpu().numpy())
+        np.testing.assert_allclose(g, orc.bf16_to_f32(orc_out), atol=1e-2, rtol=1e-2,
+                                   err_msg=f"call {call}: vs oracle")
 
 
 def test_noalloc_rejects_bad_arguments_on_the_host():
