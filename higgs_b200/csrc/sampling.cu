@@ -383,6 +383,336 @@ cudaError_t launch_argmax_keys(const float* logits, int B, int V, int offset, un
                     logits, V, offset, (int32_t*)nullptr, keys);
 }
 
+// ---------------------------------------------------------------------------
+// Filtered sampling: top-k / top-p / min-p (sample_filtered, lib.rs:392-460).
+//
+// One row per cluster of kFiltCtas CTAs; CTA r owns a contiguous slice of the
+// vocabulary and keeps its fixed-point masses E_j in shared memory.  Tokens are
+// ranked by the 57-bit key (E_j << 24) | (2^24 - 1 - j): mass descending, ties
+// to the lower index.  Every filter keeps a prefix of that order, so the kept
+// set is {j : key_j >= theta}; theta comes from radix selections over the keys
+// (8-bit digits, top down): by count for the top-k boundary (the key of rank
+// k - 1), by mass for the top-p boundary (the first key whose inclusive mass
+// prefix exceeds top_p * S); min-p is a bound on E alone.  Per digit pass each
+// warp histograms its keys (shared atomics), the CTA folds its warps, and every
+// CTA of the cluster reads the kFiltCtas CTA histograms through distributed
+// shared memory and takes the same decision.  The draw is the inverse CDF of
+// the kept masses in index order (the rule of sample_kernel).
+// ---------------------------------------------------------------------------
+constexpr int kFiltCtas = 8;
+constexpr int kFiltThreads = 512;
+constexpr int kFiltWarps = kFiltThreads / 32;
+constexpr int kFiltSlice = 20480;  // vocabulary entries per CTA: V <= 163840
+constexpr size_t kFiltSmem = (size_t)kFiltSlice * 8 + (size_t)kFiltWarps * 256 * 8 + 256 * 8 * 2;
+
+__device__ __forceinline__ uint64_t filt_key(uint64_t E, int j) {
+  return (E << 24) | (uint64_t)(0xFFFFFF - j);
+}
+
+// Returns the largest bucket d whose cumulative value (strictly-above total
+// `above` plus the buckets > d plus bucket d) exceeds `target` (count mode:
+// an integer rank; mass mode: a double bound), and the cumulative strictly
+// above d; d = -1 when no bucket does.  Warp 0 only.
+__device__ __forceinline__ int filt_bucket(const uint64_t* h, uint64_t above, double target,
+                                           uint64_t* above_out) {
+  const int lane = threadIdx.x & 31;
+  uint64_t v[8], tot = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    v[i] = h[lane * 8 + i];
+    tot += v[i];
+  }
+  // exclusive suffix sum over lanes above this one
+  uint64_t suf = tot;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t lo = __shfl_down_sync(0xffffffffu, (uint32_t)suf, o);
+    const uint32_t hi = __shfl_down_sync(0xffffffffu, (uint32_t)(suf >> 32), o);
+    if (lane + o < 32) suf += ((uint64_t)hi << 32) | lo;
+  }
+  uint64_t c = above + (suf - tot);  // everything in higher lanes
+  int found = -1;
+  uint64_t found_above = 0;
+#pragma unroll
+  for (int i = 7; i >= 0; --i) {
+    if (found < 0 && (double)(c + v[i]) > target) {
+      found = lane * 8 + i;
+      found_above = c;
+    }
+    c += v[i];
+  }
+  const unsigned m = __ballot_sync(0xffffffffu, found >= 0);
+  if (m == 0) return -1;
+  const int src = 31 - __clz(m);
+  const int d = __shfl_sync(0xffffffffu, found, src);
+  const uint64_t fa = ((uint64_t)__shfl_sync(0xffffffffu, (uint32_t)(found_above >> 32), src) << 32) |
+                      __shfl_sync(0xffffffffu, (uint32_t)found_above, src);
+  *above_out = fa;
+  return d;
+}
+
+struct FiltArgs {
+  const float* logits;
+  int V;
+  float inv_t;
+  int top_k;     // 1..V-1 to filter, else off
+  float top_p;   // < 1 to filter
+  float min_p;   // > 0 to filter (clamped to 1)
+  const float* uniforms;
+  int32_t* out;
+};
+
+__global__ void __cluster_dims__(kFiltCtas, 1, 1) __launch_bounds__(kFiltThreads)
+    sample_filtered_kernel(FiltArgs a) {
+  extern __shared__ __align__(16) unsigned char filt_smem[];
+  uint64_t* E = reinterpret_cast<uint64_t*>(filt_smem);
+  uint64_t* whist = E + kFiltSlice;                // [warps][256]
+  uint64_t* cta_hist = whist + kFiltWarps * 256;   // [256], read by the cluster
+  uint64_t* comb = cta_hist + 256;                 // [256], this CTA's copy of the cluster sum
+  __shared__ float red_f[32];
+  __shared__ uint64_t red_u[32];
+  __shared__ float cta_max;
+  __shared__ uint64_t cta_sum, cta_top, cta_kept;
+  __shared__ int sel_d;
+  __shared__ uint64_t sel_above;
+
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int V = a.V;
+  const float* row = a.logits + (size_t)blockIdx.y * V;
+  const int per = (V + kFiltCtas - 1) / kFiltCtas;
+  const int v0 = rank * per;
+  const int n = max(0, min(V - v0, per));
+  const int C = (n + kFiltThreads - 1) / kFiltThreads;  // contiguous chunk per thread
+  const int i0 = min(n, (int)threadIdx.x * C), i1 = min(n, i0 + C);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+
+  // 1. row maximum
+  float mx = -INFINITY;
+  for (int i = i0; i < i1; ++i) mx = fmaxf(mx, row[v0 + i]);
+  mx = block_max(mx, red_f);
+  if (threadIdx.x == 0) cta_max = mx;
+  cluster.sync();
+  mx = -INFINITY;
+  for (int r = 0; r < kFiltCtas; ++r) mx = fmaxf(mx, *cluster.map_shared_rank(&cta_max, r));
+  const float mxs = __fmul_rn(mx, a.inv_t);
+
+  // 2. fixed-point masses, their sum and the top key
+  uint64_t s = 0, top = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint64_t e = fixed_mass(row[v0 + i], a.inv_t, mxs);
+    E[i] = e;
+    s += e;
+    top = max(top, filt_key(e, v0 + i));
+  }
+  uint64_t tot;
+  block_exscan_u64(s, red_u, &tot);
+  __syncthreads();
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)top, o);
+    const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(top >> 32), o);
+    top = max(top, ((uint64_t)hi << 32) | lo);
+  }
+  if (lane == 0) red_u[warp] = top;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint64_t t = 0;
+    for (int w = 0; w < kFiltWarps; ++w) t = max(t, red_u[w]);
+    cta_top = t;
+    cta_sum = tot;
+  }
+  cluster.sync();
+  uint64_t S = 0;
+  top = 0;
+  for (int r = 0; r < kFiltCtas; ++r) {
+    S += *cluster.map_shared_rank(&cta_sum, r);
+    top = max(top, *cluster.map_shared_rank(&cta_top, r));
+  }
+
+  // 3. the kept-set threshold
+  uint64_t theta = 0;
+  if (a.min_p > 0.0f) {
+    const double t = __dmul_rn((double)fminf(a.min_p, 1.0f), (double)(top >> 24));
+    theta = max(theta, (uint64_t)ceil(t) << 24);
+  }
+  for (int mode = 0; mode < 2; ++mode) {
+    // mode 0: top-k (count), mode 1: top-p (mass)
+    if (mode == 0 && !(a.top_k >= 1 && a.top_k < V)) continue;
+    if (mode == 1 && !(a.top_p < 1.0f)) continue;
+    const double target = mode == 0 ? (double)(a.top_k - 1) : __dmul_rn((double)a.top_p, (double)S);
+    uint64_t prefix = 0, above = 0;
+    bool all = false;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < kFiltWarps * 256; i += kFiltThreads) whist[i] = 0;
+      __syncthreads();
+      uint64_t* wh = whist + warp * 256;
+      for (int i = i0; i < i1; ++i) {
+        const uint64_t key = filt_key(E[i], v0 + i);
+        if (shift < 56 && (key >> (shift + 8)) != (prefix >> (shift + 8))) continue;
+        const int d = (int)((key >> shift) & 255);
+        atomicAdd((unsigned long long*)&wh[d], mode == 0 ? 1ull : (unsigned long long)E[i]);
+      }
+      __syncthreads();
+      if (threadIdx.x < 256) {
+        uint64_t h = 0;
+        for (int w = 0; w < kFiltWarps; ++w) h += whist[w * 256 + threadIdx.x];
+        cta_hist[threadIdx.x] = h;
+      }
+      cluster.sync();
+      if (threadIdx.x < 256) {
+        uint64_t h = 0;
+        for (int r = 0; r < kFiltCtas; ++r) h += cluster.map_shared_rank(cta_hist, r)[threadIdx.x];
+        comb[threadIdx.x] = h;
+      }
+      cluster.sync();  // every CTA has read the histograms before they are rebuilt
+      if (warp == 0) {
+        uint64_t ab = 0;
+        const int d = filt_bucket(comb, above, target, &ab);
+        if (lane == 0) {
+          sel_d = d;
+          sel_above = ab;
+        }
+      }
+      __syncthreads();
+      if (sel_d < 0) {  // mass mode: every remaining key stays within top_p
+        all = true;
+        break;
+      }
+      prefix |= (uint64_t)sel_d << shift;
+      above = sel_above;
+      __syncthreads();
+    }
+    if (mode == 0) {
+      theta = max(theta, prefix);  // the key of rank k - 1
+    } else if (!all) {
+      theta = max(theta, prefix == top ? top : prefix + 1);  // rank 0 always stays
+    }
+  }
+
+  // 4. inverse CDF of the kept masses in index order
+  uint64_t w = 0;
+  for (int i = i0; i < i1; ++i)
+    if (filt_key(E[i], v0 + i) >= theta) w += E[i];
+  uint64_t kept;
+  const uint64_t before = block_exscan_u64(w, red_u, &kept);
+  if (threadIdx.x == 0) cta_kept = kept;
+  cluster.sync();
+  uint64_t off = 0, total = 0;
+  for (int r = 0; r < kFiltCtas; ++r) {
+    const uint64_t t = *cluster.map_shared_rank(&cta_kept, r);
+    if (r < rank) off += t;
+    total += t;
+  }
+  if (total == 0) {
+    if (rank == 0 && threadIdx.x == 0) a.out[blockIdx.y] = 0xFFFFFF - (int)(top & 0xFFFFFF);
+  } else {
+    uint64_t target = (uint64_t)__dmul_rn((double)a.uniforms[blockIdx.y], (double)total);
+    if (target >= total) target = total - 1;
+    if (target >= off && target < off + kept) {
+      const uint64_t t = target - off;
+      if (w > 0 && before <= t && t < before + w) {
+        uint64_t c = before;
+        for (int i = i0; i < i1; ++i) {
+          if (filt_key(E[i], v0 + i) < theta) continue;
+          c += E[i];
+          if (c > t) {
+            a.out[blockIdx.y] = v0 + i;
+            break;
+          }
+        }
+      }
+    }
+  }
+  pdl_launch();
+  cluster.sync();  // peers keep their shared memory until every CTA has read it
+}
+
+// ---------------------------------------------------------------------------
+// LogprobArrays::compute (lib.rs:495-533): log-softmax of the scaled logits,
+// the chosen token's value and the top_n largest.  Z = sum of
+// floor(det_exp(s_j - m) * 2^44) is an exact integer; lp_j = f32((double)
+// (s_j - m) - log(Z * 2^-44)).  The top_n come from top_n block maxima over
+// the ordered (value, lower index first) keys.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kSampThreads) logprobs_kernel(const float* logits, int V, float inv_t,
+                                                                const int32_t* tokens, int top_n,
+                                                                float* token_lp, int32_t* top_ids,
+                                                                float* top_lp) {
+  pdl_wait();
+  __shared__ float shf[32];
+  __shared__ uint64_t shu[32];
+  __shared__ unsigned long long shk[32];
+  const int b = blockIdx.x;
+  const float* row = logits + (size_t)b * V;
+  float m = -INFINITY;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) m = fmaxf(m, __fmul_rn(row[j], inv_t));
+  m = block_max(m, shf);
+  uint64_t z = 0;
+  for (int j = threadIdx.x; j < V; j += blockDim.x)
+    z += (uint64_t)__dmul_rn((double)det_exp(__fsub_rn(__fmul_rn(row[j], inv_t), m)), 17592186044416.0);
+  uint64_t Z;
+  block_exscan_u64(z, shu, &Z);
+  const double L = log(__dmul_rn((double)Z, 5.684341886080801486968994140625e-14));
+  if (threadIdx.x == 0) {
+    const int t = tokens[b];
+    token_lp[b] = (t >= 0 && t < V)
+                      ? (float)__dsub_rn((double)__fsub_rn(__fmul_rn(row[t], inv_t), m), L)
+                      : -INFINITY;
+  }
+  unsigned long long prev = ~0ull;
+  for (int i = 0; i < top_n; ++i) {
+    unsigned long long best = 0ull;
+    bool any = false;
+    for (int j = threadIdx.x; j < V; j += blockDim.x) {
+      const unsigned long long k = argmax_key(__fmul_rn(row[j], inv_t), j);
+      if (k < prev && (!any || k > best)) {
+        best = k;
+        any = true;
+      }
+    }
+    // keys are unique per index, so 0 doubles as "none" only for an exhausted row
+    best = any ? best + 1 : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) shk[threadIdx.x >> 5] = best;
+    __syncthreads();
+    best = 0ull;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) best = max(best, shk[w]);
+    if (best == 0ull) {
+      if (threadIdx.x == 0) {
+        top_ids[(size_t)b * top_n + i] = -1;
+        top_lp[(size_t)b * top_n + i] = -INFINITY;
+      }
+      continue;
+    }
+    best -= 1;
+    prev = best;
+    const int j = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+    if (threadIdx.x == 0) {
+      top_ids[(size_t)b * top_n + i] = j;
+      top_lp[(size_t)b * top_n + i] =
+          (float)__dsub_rn((double)__fsub_rn(__fmul_rn(row[j], inv_t), m), L);
+    }
+  }
+  pdl_launch();
+}
+
+// Constraint::apply_mask (constrained.rs:79-110): logits += allowed ? 0 : -inf.
+__global__ void token_mask_kernel(float* logits, int V, const uint32_t* allowed, int words) {
+  pdl_wait();
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  const int b = blockIdx.y;
+  if (j < V) {
+    const uint32_t w = allowed[(size_t)b * words + (j >> 5)];
+    float* l = logits + (size_t)b * V + j;
+    *l = __fadd_rn(*l, ((w >> (j & 31)) & 1u) ? 0.0f : -INFINITY);
+  }
+  pdl_launch();
+}
+
 }  // namespace higgs
 
 using namespace higgs;
@@ -447,5 +777,79 @@ extern "C" int higgs_apply_penalties(higgs_ctx* ctx, float* logits, int B, int V
   if (B == 0 || max_hist == 0) return HIGGS_OK;
   HG_CUDA(launch_pdl(penalties_kernel, dim3(B), dim3(256), 0, (cudaStream_t)stream, logits, V,
                      history, hist_lens, max_hist, rep, freq, pres));
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_sample_filtered(higgs_ctx* ctx, const float* logits, int B, int V,
+                                     float temperature, int top_k, float top_p, float min_p,
+                                     const float* uniforms, int32_t* out, void* stream) {
+  HG_CHECK_ARG(ctx && logits && out, "higgs_sample_filtered: null argument");
+  HG_CHECK_ARG(B >= 0 && V > 0, "higgs_sample_filtered: bad shape");
+  HG_CHECK_ARG(B <= 65535, "higgs_sample_filtered: B > 65535");
+  HG_CHECK_ARG(temperature >= 0.0f, "higgs_sample_filtered: negative temperature");
+  HG_CHECK_ARG(temperature == 0.0f || uniforms, "higgs_sample_filtered: uniforms required when T > 0");
+  HG_CHECK_ARG(top_k >= 0, "higgs_sample_filtered: negative top_k");
+  HG_CHECK_ARG(top_p >= 0.0f, "higgs_sample_filtered: negative top_p");
+  HG_CHECK_ARG(V <= kFiltCtas * kFiltSlice,
+               "higgs_sample_filtered: V above 163840 (the per-row shared-memory capacity)");
+  HG_DEVICE(ctx);
+  if (B == 0) return HIGGS_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (temperature == 0.0f) {
+    HG_CUDA(launch_pdl(argmax_cluster_kernel, dim3(kArgmaxCluster, B), dim3(kArgmaxThreads), 0, st,
+                       logits, V, 0, out, (unsigned long long*)nullptr));
+    return HIGGS_OK;
+  }
+  const float inv_t = 1.0f / temperature;
+  const bool filt = (top_k >= 1 && top_k < V) || top_p < 1.0f || min_p > 0.0f;
+  if (!filt) {  // no filter keeps every token: the plain draw
+    HG_CUDA(launch_pdl(sample_kernel, dim3(B), dim3(kSampThreads), 0, st, logits, V, inv_t, 0,
+                       uniforms, out));
+    return HIGGS_OK;
+  }
+  static PerDeviceOnce attr;
+  HG_CUDA(attr.run([] {
+    return cudaFuncSetAttribute(sample_filtered_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                (int)kFiltSmem);
+  }));
+  FiltArgs a;
+  a.logits = logits;
+  a.V = V;
+  a.inv_t = inv_t;
+  a.top_k = top_k;
+  a.top_p = top_p;
+  a.min_p = min_p;
+  a.uniforms = uniforms;
+  a.out = out;
+  HG_CUDA(launch_pdl(sample_filtered_kernel, dim3(kFiltCtas, B), dim3(kFiltThreads), kFiltSmem, st, a));
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_logprobs(higgs_ctx* ctx, const float* logits, int B, int V, float temperature,
+                              const int32_t* tokens, int top_n, float* token_logprob,
+                              int32_t* top_ids, float* top_logprobs, void* stream) {
+  HG_CHECK_ARG(ctx && logits && tokens && token_logprob, "higgs_logprobs: null argument");
+  HG_CHECK_ARG(B >= 0 && V > 0 && top_n >= 0, "higgs_logprobs: bad shape");
+  HG_CHECK_ARG(top_n == 0 || (top_ids && top_logprobs), "higgs_logprobs: null top-n outputs");
+  HG_CHECK_ARG(temperature >= 0.0f, "higgs_logprobs: negative temperature");
+  HG_DEVICE(ctx);
+  if (B == 0) return HIGGS_OK;
+  // simple.rs:269-275: unscaled at T <= f32::EPSILON, else logits * (1 / T)
+  const float inv_t = temperature <= 1.1920928955078125e-7f ? 1.0f : 1.0f / temperature;
+  HG_CUDA(launch_pdl(logprobs_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream, logits, V,
+                     inv_t, tokens, top_n, token_logprob, top_ids, top_logprobs));
+  return HIGGS_OK;
+}
+
+extern "C" int higgs_apply_token_mask(higgs_ctx* ctx, float* logits, int B, int V,
+                                      const uint32_t* allowed, int words_per_row, void* stream) {
+  HG_CHECK_ARG(ctx && logits && allowed, "higgs_apply_token_mask: null argument");
+  HG_CHECK_ARG(B >= 0 && V > 0, "higgs_apply_token_mask: bad shape");
+  HG_CHECK_ARG(B <= 65535, "higgs_apply_token_mask: B > 65535");
+  HG_CHECK_ARG((int64_t)words_per_row * 32 >= V, "higgs_apply_token_mask: mask rows shorter than V bits");
+  HG_DEVICE(ctx);
+  if (B == 0) return HIGGS_OK;
+  HG_CUDA(launch_pdl(token_mask_kernel, dim3((V + 255) / 256, B), dim3(256), 0, (cudaStream_t)stream,
+                     logits, V, allowed, words_per_row));
   return HIGGS_OK;
 }

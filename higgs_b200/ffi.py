@@ -50,6 +50,9 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_sample": (I, [P, P, I, I, F, P, P, P]),
     "higgs_spec_accept": (I, [P, P, P, P, I, I, I, F, P, P, P, P, P]),
     "higgs_apply_penalties": (I, [P, P, I, I, P, P, I, F, F, F, P]),
+    "higgs_sample_filtered": (I, [P, P, I, I, F, I, F, F, P, P, P]),
+    "higgs_logprobs": (I, [P, P, I, I, F, P, I, P, P, P, P]),
+    "higgs_apply_token_mask": (I, [P, P, I, I, P, I, P]),
     "higgs_rmsnorm_strided": (I, [P, P, I64, I, I, P, F, P, P]),
     "higgs_moe_plan_size": (SZ, [I, I, I]),
     "higgs_moe_route_topk": (I, [P, P, I, I, I, I, I, P, P, P, SZ, P]),

@@ -314,6 +314,42 @@ def sample(logits, temperature: float, uniforms=None):
     return out
 
 
+def sample_filtered(logits, temperature: float, top_k: int = 0, top_p: float = 1.0,
+                    min_p: float = 0.0, uniforms=None):
+    """sample() with sample_filtered's top-k / top-p / min-p (lib.rs:373-460), explicit
+    uniforms [B] for T > 0; int32 [B]."""
+    _chk(logits, torch.float32, "logits")
+    B, V = logits.shape
+    out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    ffi.call("higgs_sample_filtered", _ctx(logits), _p(logits), B, V, float(temperature),
+             int(top_k), float(top_p), float(min_p), _p(uniforms), _p(out), _st(logits.device))
+    return out
+
+
+def logprobs(logits, temperature: float, tokens, top_n: int = 0):
+    """LogprobArrays::compute (lib.rs:495-533): (token logprob f32 [B], top ids int32 [B, n],
+    top logprobs f32 [B, n])."""
+    _chk(logits, torch.float32, "logits")
+    B, V = logits.shape
+    dev = logits.device
+    lp = torch.empty(B, dtype=torch.float32, device=dev)
+    ids = torch.empty(B, top_n, dtype=torch.int32, device=dev)
+    tl = torch.empty(B, top_n, dtype=torch.float32, device=dev)
+    ffi.call("higgs_logprobs", _ctx(logits), _p(logits), B, V, float(temperature), _p(tokens),
+             int(top_n), _p(lp), _p(ids) if top_n else None, _p(tl) if top_n else None, _st(dev))
+    return lp, ids, tl
+
+
+def apply_token_mask(logits, allowed_bits):
+    """Constraint::apply_mask (constrained.rs:79-110) in place: f32 [B, V] += 0 / -inf from an
+    int32 bitmask [B, ceil(V/32)] (bit j%32 of word j/32 = token j allowed)."""
+    _chk(logits, torch.float32, "logits")
+    B, V = logits.shape
+    ffi.call("higgs_apply_token_mask", _ctx(logits), _p(logits), B, V, _p(allowed_bits),
+             allowed_bits.shape[1], _st(logits.device))
+    return logits
+
+
 def spec_accept(target_logits, draft_logits, draft_tokens, temperature: float,
                 accept_uniforms=None, sample_uniforms=None):
     """Speculative acceptance: (accepted int32 [B], out_tokens int32 [B, k+1])."""

@@ -359,6 +359,38 @@ int higgs_apply_penalties(higgs_ctx* ctx, float* logits, int B, int V, const int
                           const int32_t* hist_lens, int max_hist, float rep, float freq,
                           float pres, void* stream);
 
+/* sample() with filtering (crates/higgs-models/src/lib.rs:373-385 calling
+ * sample_filtered lib.rs:392-460): out int32 [B] from logits f32 [B, V] at
+ * `temperature`, keeping the tokens that pass top_k (0 = off), top_p (>= 1 =
+ * off) and min_p (<= 0 = off, clamped to 1) before an inverse-CDF draw with
+ * uniforms[b].  Masses are the fixed-point E_j of higgs_sample; ranks order
+ * them by mass, ties to the lower index; rank r is kept iff r < top_k, and
+ * (r == 0 or its inclusive mass prefix <= top_p * sum E), and E_r >= min_p *
+ * max E (the products in IEEE double), so a draw is exact given the uniform.
+ * temperature 0 is the argmax; no active filter is higgs_sample.  V <= 163840.
+ * One cluster of 8 CTAs per row. */
+int higgs_sample_filtered(higgs_ctx* ctx, const float* logits, int B, int V, float temperature,
+                          int top_k, float top_p, float min_p, const float* uniforms,
+                          int32_t* out, void* stream);
+
+/* LogprobArrays::compute (crates/higgs-models/src/lib.rs:495-533) on the
+ * logits scaled as its callers do (crates/higgs-engine/src/simple.rs:269-277:
+ * unscaled when temperature <= FLT_EPSILON, else times 1/T): token_logprob f32
+ * [B] of tokens[b], and the top_n (ties to the lower index) as top_ids int32
+ * [B, top_n] and top_logprobs f32 [B, top_n] (-1 / -inf past the vocabulary).
+ * log Z is the log of an exact fixed-point sum (2^-44 units) in double. */
+int higgs_logprobs(higgs_ctx* ctx, const float* logits, int B, int V, float temperature,
+                   const int32_t* tokens, int top_n, float* token_logprob, int32_t* top_ids,
+                   float* top_logprobs, void* stream);
+
+/* Constraint::apply_mask (crates/higgs-engine/src/constrained.rs:79-110), in
+ * place: logits f32 [B, V] += 0 where the token is allowed, -inf elsewhere.
+ * allowed u32 [B, words_per_row]: bit (j % 32) of word j / 32 = token j
+ * allowed (words_per_row * 32 >= V).  The set itself comes from the host's
+ * FSM each step, as in the reference. */
+int higgs_apply_token_mask(higgs_ctx* ctx, float* logits, int B, int V, const uint32_t* allowed,
+                           int words_per_row, void* stream);
+
 /* ---- a9: mixture of experts (qwen3_moe.rs Qwen3MoeMlpBlock) ------------- */
 
 /* Bytes of the routing plan higgs_moe_route_topk writes for T tokens, E

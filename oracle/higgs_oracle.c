@@ -738,6 +738,136 @@ void orc_apply_penalties(float* logits, int64_t V, const int32_t* history, int64
   free(cnt);
 }
 
+/*
+ * Constraint::apply_mask (crates/higgs-engine/src/constrained.rs:79-110):
+ * logits + mask, mask 0 for allowed tokens and -inf for the others.  The
+ * allowed set of row b is a bitmask: bit (j % 32) of word j / 32 of
+ * allowed[b * words ...] set = token j allowed.  One f32 add per logit.
+ */
+void orc_apply_token_mask(float* logits, int64_t B, int64_t V, const uint32_t* allowed,
+                          int64_t words) {
+  for (int64_t b = 0; b < B; ++b)
+    for (int64_t j = 0; j < V; ++j) {
+      const int on = (allowed[b * words + j / 32] >> (j % 32)) & 1u;
+      logits[b * V + j] = logits[b * V + j] + (on ? 0.0f : -INFINITY);
+    }
+}
+
+/*
+ * sample() with top-k / top-p / min-p filtering (lib.rs:373-385 calling
+ * sample_filtered lib.rs:392-460), over the same fixed-point masses as
+ * orc_sample:
+ *   E_j = fixed_probs(logits / T), S = sum E_j;  rank order = E descending,
+ *   ties to the lower index (a stable descending sort);
+ *   keep rank r iff  r < k  (top_k; 0 = off, clamped to [1, V]),
+ *                and (r == 0 or cum_r <= top_p * S)  (cum_r = inclusive sum
+ *                    of E over ranks 0..r; off when top_p >= 1),
+ *                and E_r >= min_p * E_max  (min_p clamped to [0, 1]; off when
+ *                    min_p <= 0);
+ *   then an inverse-CDF draw (uniform u, index order, the rule of orc_sample)
+ *   over the kept masses.  The products top_p * S and min_p * E_max are IEEE
+ *   double; every other quantity is an exact integer.  Each filter keeps a
+ *   prefix of the rank order, so the kept set is {j : key_j >= theta} for the
+ *   key (E_j << 24) | (2^24 - 1 - j) (V < 2^24).  T == 0 is the argmax.
+ */
+static int cmp_u64_desc(const void* a, const void* b) {
+  const uint64_t x = *(const uint64_t*)a, y = *(const uint64_t*)b;
+  return x < y ? 1 : (x > y ? -1 : 0);
+}
+
+void orc_sample_filtered(const float* logits, int64_t B, int64_t V, float temperature,
+                         int64_t top_k, float top_p, float min_p, const float* uniforms,
+                         int32_t* out) {
+  if (temperature == 0.0f) {
+    orc_argmax(logits, B, V, out);
+    return;
+  }
+  const float inv_t = 1.0f / temperature;
+  uint64_t* E = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)V);
+  uint64_t* key = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)V);
+  for (int64_t b = 0; b < B; ++b) {
+    const uint64_t S = fixed_probs(logits + b * V, V, inv_t, E);
+    for (int64_t j = 0; j < V; ++j) key[j] = (E[j] << 24) | (uint64_t)(0xFFFFFF - j);
+    qsort(key, (size_t)V, sizeof(uint64_t), cmp_u64_desc);
+    const int64_t k = (top_k <= 0 || top_k > V) ? V : top_k;
+    const double pS = (double)top_p * (double)S;
+    const float mp = min_p > 1.0f ? 1.0f : min_p;
+    const double thr = (double)mp * (double)(key[0] >> 24);
+    int64_t n = 0;
+    uint64_t cum = 0;
+    for (; n < V; ++n) {
+      const uint64_t En = key[n] >> 24;
+      cum += En;
+      if (n >= k) break;
+      if (top_p < 1.0f && n > 0 && !((double)cum <= pS)) break;
+      if (min_p > 0.0f && !((double)En >= thr)) break;
+    }
+    const uint64_t theta = key[n - 1]; /* n >= 1: rank 0 always passes */
+    uint64_t tot = 0;
+    for (int64_t j = 0; j < V; ++j) {
+      const uint64_t kj = (E[j] << 24) | (uint64_t)(0xFFFFFF - j);
+      if (kj < theta) E[j] = 0;
+      tot += E[j];
+    }
+    out[b] = (int32_t)inverse_cdf(E, V, tot, uniforms[b]);
+  }
+  free(E);
+  free(key);
+}
+
+/*
+ * LogprobArrays::compute (lib.rs:495-533): log_softmax of the temperature-
+ * scaled logits (s_j = l_j * (1/T), unscaled when T <= FLT_EPSILON as at
+ * simple.rs:269-275), the chosen token's log-probability and the top_n
+ * largest (ties to the lower index) with their log-probabilities.
+ *   m = max s;  Z = sum floor(orc_exp(s_j - m) * 2^44) * 2^-44  (exact sum);
+ *   lp_j = f32((double)(s_j - m) - log(Z))   (s_j - m in f32).
+ */
+void orc_logprobs(const float* logits, int64_t B, int64_t V, float temperature,
+                  const int32_t* tokens, int64_t top_n, float* token_lp, int32_t* top_ids,
+                  float* top_lp) {
+  const float inv_t = temperature <= 1.1920928955078125e-7f ? 1.0f : 1.0f / temperature;
+  for (int64_t b = 0; b < B; ++b) {
+    const float* l = logits + b * V;
+    float m = l[0] * inv_t;
+    for (int64_t j = 1; j < V; ++j) {
+      const float s = l[j] * inv_t;
+      m = s > m ? s : m;
+    }
+    uint64_t z = 0;
+    for (int64_t j = 0; j < V; ++j)
+      z += (uint64_t)((double)orc_exp(l[j] * inv_t - m) * 17592186044416.0);
+    const double L = log((double)z * 5.684341886080801486968994140625e-14);
+    const int32_t t = tokens[b];
+    token_lp[b] = (t >= 0 && t < V) ? (float)((double)(l[t] * inv_t - m) - L) : -INFINITY;
+    /* top_n by (s_j, lower index first) */
+    int64_t prev = -1;
+    float prev_s = INFINITY;
+    for (int64_t i = 0; i < top_n; ++i) {
+      int64_t best = -1;
+      float bs = -INFINITY;
+      for (int64_t j = 0; j < V; ++j) {
+        const float s = l[j] * inv_t;
+        const int after = s < prev_s || (s == prev_s && j > prev);
+        if (!after) continue;
+        if (best < 0 || s > bs) {
+          best = j;
+          bs = s;
+        }
+      }
+      if (best < 0) {
+        top_ids[b * top_n + i] = -1;
+        top_lp[b * top_n + i] = -INFINITY;
+        continue;
+      }
+      top_ids[b * top_n + i] = (int32_t)best;
+      top_lp[b * top_n + i] = (float)((double)(bs - m) - L);
+      prev = best;
+      prev_s = bs;
+    }
+  }
+}
+
 /* ------------------------------------------------------------------------ */
 /* Mixture of experts                                                        */
 /* ------------------------------------------------------------------------ */

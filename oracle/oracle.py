@@ -277,6 +277,51 @@ def spec_accept(target_logits, draft_logits, draft_tokens, temperature, accept_u
     return acc, toks
 
 
+def apply_token_mask(logits, allowed_bits) -> np.ndarray:
+    """Constraint::apply_mask (constrained.rs:79-110): logits + (0 | -inf) from a per-row bitmask
+    u32 [B, ceil(V/32)] (bit j%32 of word j/32 = token j allowed); returns a new array."""
+    lg = np.array(logits, dtype=np.float32)
+    B, V = lg.shape
+    bits = np.ascontiguousarray(allowed_bits, dtype=np.uint32)
+    lib().orc_apply_token_mask(_ptr(lg), I64(B), I64(V), _ptr(bits), I64(bits.shape[1]))
+    return lg
+
+
+def allowed_bits(allowed_ids_per_row, V: int) -> np.ndarray:
+    """Bitmask u32 [B, ceil(V/32)] from per-row lists of allowed token ids."""
+    W = (V + 31) // 32
+    out = np.zeros((len(allowed_ids_per_row), W), np.uint32)
+    for b, ids in enumerate(allowed_ids_per_row):
+        ids = np.asarray([i for i in ids if 0 <= i < V], np.int64)
+        np.bitwise_or.at(out[b], ids // 32, (np.uint32(1) << (ids % 32).astype(np.uint32)))
+    return out
+
+
+def sample_filtered(logits, temperature, top_k=0, top_p=1.0, min_p=0.0, uniforms=None) -> np.ndarray:
+    """sample() with top-k / top-p / min-p (lib.rs:373-460) over the fixed-point masses."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    B, V = lg.shape
+    out = np.empty(B, np.int32)
+    u = None if uniforms is None else np.ascontiguousarray(uniforms, dtype=np.float32)
+    lib().orc_sample_filtered(_ptr(lg), I64(B), I64(V), F(temperature), I64(int(top_k)), F(top_p),
+                              F(min_p), _ptr(u), _ptr(out))
+    return out
+
+
+def logprobs(logits, temperature, tokens, top_n: int):
+    """LogprobArrays::compute (lib.rs:495-533): (token logprob f32 [B], top ids int32 [B, n],
+    top logprobs f32 [B, n])."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    B, V = lg.shape
+    lp = np.empty(B, np.float32)
+    ids = np.empty((B, max(top_n, 0)), np.int32)
+    tl = np.empty((B, max(top_n, 0)), np.float32)
+    lib().orc_logprobs(_ptr(lg), I64(B), I64(V), F(temperature),
+                       _ptr(np.ascontiguousarray(tokens, dtype=np.int32)), I64(top_n), _ptr(lp),
+                       _ptr(ids), _ptr(tl))
+    return lp, ids, tl
+
+
 def apply_penalties(logits, history, rep=1.0, freq=0.0, pres=0.0) -> np.ndarray:
     """apply_penalties (lib.rs:278-363) on one row; returns a new array."""
     lg = np.array(logits, dtype=np.float32).reshape(-1)

@@ -30,6 +30,32 @@ REFERENCE_KAT = {
         {"src": "crates/higgs-models/src/lib.rs:831-836 sample_single_element_logits",
          "logits": [[5.0]], "expect": [0]},
     ],
+    # "expect": the token every uniform must give (the other tokens carry no mass after the
+    # filter, or exp underflows), or null where the reference test checks only the shape and
+    # the draw is left to the uniform ("allowed" then lists the tokens the filter keeps)
+    "sample_filtered": [
+        {"src": "crates/higgs-models/src/lib.rs:1070-1085 sample_top_k_limits_to_k_tokens",
+         "logits": [[0.0, 0.0, 0.0, 100.0]], "temperature": 1.0, "top_k": 2, "top_p": 1.0,
+         "min_p": 0.0, "expect": 3},
+        {"src": "crates/higgs-models/src/lib.rs:1086-1098 sample_top_k_larger_than_vocab_is_no_op",
+         "logits": [[0.1, 100.0, 0.0]], "temperature": 1.0, "top_k": 100, "top_p": 1.0,
+         "min_p": 0.0, "expect": 1},
+        {"src": "crates/higgs-models/src/lib.rs:1100-1115 sample_min_p_filters_low_probability",
+         "logits": [[100.0, 0.0, 0.0, 0.0]], "temperature": 1.0, "top_k": 0, "top_p": 1.0,
+         "min_p": 0.5, "expect": 0},
+        {"src": "crates/higgs-models/src/lib.rs:826-829 sample_with_top_p",
+         "logits": [[0.0, 100.0, 0.0]], "temperature": 1.0, "top_k": 0, "top_p": 0.5,
+         "min_p": 0.0, "expect": 1},
+        {"src": "crates/higgs-models/src/lib.rs:821-824 sample_with_temperature",
+         "logits": [[0.1, 100.0, 0.0]], "temperature": 0.5, "top_k": 0, "top_p": 1.0,
+         "min_p": 0.0, "expect": 1},
+        {"src": "crates/higgs-models/src/lib.rs:850-853 sample_top_p_with_uniform_logits",
+         "logits": [[1.0, 1.0, 1.0, 1.0]], "temperature": 1.0, "top_k": 0, "top_p": 0.3,
+         "min_p": 0.0, "expect": None, "allowed": [0]},
+        {"src": "crates/higgs-models/src/lib.rs:845-848 sample_uniform_logits_with_temperature",
+         "logits": [[1.0, 1.0, 1.0, 1.0]], "temperature": 1.0, "top_k": 0, "top_p": 1.0,
+         "min_p": 0.0, "expect": None, "allowed": [0, 1, 2, 3]},
+    ],
     "penalties": [
         {"src": "crates/higgs-models/src/lib.rs:1137-1154 apply_repetition_penalty",
          "logits": [4.0, 2.0, 6.0], "history": [0, 2], "rep": 2.0, "freq": 0.0, "pres": 0.0,
@@ -129,6 +155,21 @@ def oracle_vectors() -> dict[str, np.ndarray]:
     su = rng.random(B).astype(np.float32)
     acc, toks = orc.spec_accept(tl, dl, dt, 0.7, au, su)
     v.update(sa_tl=tl, sa_dl=dl, sa_dt=dt, sa_au=au, sa_su=su, sa_acc=acc, sa_toks=toks)
+    # filtered sampling (top-k / top-p / min-p), logprobs, constraint mask
+    fl = (rng.normal(0, 3, size=(4, 2000))).astype(np.float32)
+    fl[1, 100:110] = fl[1, 5]  # ties across the top-k boundary
+    fu = rng.random(4).astype(np.float32)
+    v.update(sf_logits=fl, sf_u=fu,
+             sf_k40=orc.sample_filtered(fl, 0.8, top_k=40, uniforms=fu),
+             sf_p09=orc.sample_filtered(fl, 0.8, top_p=0.9, uniforms=fu),
+             sf_m01=orc.sample_filtered(fl, 0.8, min_p=0.1, uniforms=fu),
+             sf_all=orc.sample_filtered(fl, 1.3, top_k=100, top_p=0.8, min_p=0.02, uniforms=fu))
+    toks = rng.integers(0, 2000, size=4).astype(np.int32)
+    lp, ids, tlp = orc.logprobs(fl, 0.7, toks, 5)
+    v.update(lp_tokens=toks, lp_lp=lp, lp_ids=ids, lp_top=tlp)
+    allowed = [rng.choice(2000, size=n, replace=False) for n in (1, 7, 300, 2000)]
+    bits = orc.allowed_bits(allowed, 2000)
+    v.update(mk_bits=bits, mk_out=orc.apply_token_mask(fl, bits))
     return v
 
 

@@ -493,6 +493,86 @@ def test_penalties(kat):
         np.testing.assert_array_equal(lt.cpu().numpy()[bidx], ref)
 
 
+def test_sample_filtered_kat_and_golden(kat, golden):
+    """The reference's top-k / top-p / min-p tests (lib.rs:821-853, 1070-1115) and the golden
+    oracle draws, bit for bit."""
+    o = ops()
+    us = np.linspace(0, 1, 32, endpoint=False, dtype=np.float32)
+    for case in kat["sample_filtered"]:
+        lg = np.repeat(np.array(case["logits"], np.float32), len(us), 0)
+        got = set(o.sample_filtered(t(lg), case["temperature"], case["top_k"], case["top_p"],
+                                    case["min_p"], t(us)).cpu().numpy().tolist())
+        want = {case["expect"]} if case["expect"] is not None else set(case["allowed"])
+        assert got == want, (case["src"], got, want)
+    g = golden
+    fl, fu = t(g["sf_logits"]), t(g["sf_u"])
+    assert np.array_equal(o.sample_filtered(fl, 0.8, top_k=40, uniforms=fu).cpu().numpy(), g["sf_k40"])
+    assert np.array_equal(o.sample_filtered(fl, 0.8, top_p=0.9, uniforms=fu).cpu().numpy(), g["sf_p09"])
+    assert np.array_equal(o.sample_filtered(fl, 0.8, min_p=0.1, uniforms=fu).cpu().numpy(), g["sf_m01"])
+    assert np.array_equal(o.sample_filtered(fl, 1.3, 100, 0.8, 0.02, uniforms=fu).cpu().numpy(),
+                          g["sf_all"])
+
+
+@pytest.mark.parametrize("V,T,top_k,top_p,min_p", [
+    (151936, 0.7, 50, 1.0, 0.0), (151936, 0.7, 0, 0.9, 0.0), (151936, 1.0, 0, 1.0, 0.05),
+    (151936, 0.8, 40, 0.95, 0.02), (128256, 1.5, 1, 1.0, 0.0), (128256, 0.6, 0, 0.0, 0.0),
+    (4099, 2.0, 4098, 0.999, 0.0), (163840, 1.0, 1000, 0.5, 0.001), (7, 1.0, 3, 0.7, 0.2)])
+def test_sample_filtered_bit_exact(V, T, top_k, top_p, min_p):
+    """Tokens equal the oracle's for identical uniforms over many rows: vocabularies of the
+    benchmark models and the largest supported, ties at the filter boundaries, extreme
+    uniforms, flat rows (every token within top_p) and peaked ones."""
+    o = ops()
+    rng = np.random.default_rng(V + top_k)
+    B = 24
+    lg = rng.normal(0, 2, size=(B, V)).astype(np.float32)
+    lg[1] = 0.25                                    # flat row
+    lg[2, : min(V, 64)] = lg[2].max()               # a block of tied maxima
+    lg[3, rng.integers(0, V, size=max(1, V // 50))] = lg[3].max() - 0.5  # ties inside the set
+    lg[4, V - 1] = lg[4].max() + 30.0               # one dominant token at the end
+    u = rng.random(B).astype(np.float32)
+    u[0], u[5] = 0.0, np.float32(0.99999994)
+    got = o.sample_filtered(t(lg), T, top_k, top_p, min_p, t(u)).cpu().numpy()
+    ref = orc.sample_filtered(lg, T, top_k, top_p, min_p, u)
+    assert np.array_equal(got, ref), np.nonzero(got != ref)[0].tolist()
+
+
+def test_sample_filtered_rejects_oversized_vocab():
+    from higgs_b200 import ffi
+    o = ops()
+    lg = t(np.zeros((1, 163841), np.float32))
+    with pytest.raises(ffi.HiggsError, match="163840"):
+        o.sample_filtered(lg, 1.0, 5, uniforms=t(np.zeros(1, np.float32)))
+
+
+@pytest.mark.parametrize("V,T,top_n", [(151936, 0.7, 5), (128256, 0.0, 20), (1000, 1.3, 0),
+                                       (7, 1.0, 10)])
+def test_logprobs_match_oracle(V, T, top_n, golden):
+    o = ops()
+    g = golden
+    lp, ids, tl = o.logprobs(t(g["sf_logits"]), 0.7, t(g["lp_tokens"]), 5)
+    assert np.array_equal(ids.cpu().numpy(), g["lp_ids"])
+    np.testing.assert_allclose(lp.cpu().numpy(), g["lp_lp"], rtol=0, atol=1e-6)
+    np.testing.assert_allclose(tl.cpu().numpy(), g["lp_top"], rtol=0, atol=1e-6)
+    rng = np.random.default_rng(V)
+    lg = rng.normal(0, 3, size=(6, V)).astype(np.float32)
+    lg[1, : min(V, 30)] = lg[1].max()  # tied top values
+    toks = rng.integers(0, V, size=6).astype(np.int32)
+    toks[0] = V  # out of range -> -inf
+    lp, ids, tl = o.logprobs(t(lg), T, t(toks), top_n)
+    rlp, rids, rtl = orc.logprobs(lg, T, toks, top_n)
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    np.testing.assert_allclose(lp.cpu().numpy(), rlp, rtol=0, atol=1e-6)
+    np.testing.assert_allclose(tl.cpu().numpy(), rtl, rtol=0, atol=1e-6)
+
+
+def test_token_mask_bit_exact(golden):
+    o = ops()
+    g = golden
+    lg = t(g["sf_logits"].copy())
+    o.apply_token_mask(lg, t(g["mk_bits"].view(np.int32)))
+    assert np.array_equal(lg.cpu().numpy().view(np.uint32), g["mk_out"].view(np.uint32))
+
+
 # ---- stream-K GEMV with fused RMSNorm (decode batches) -----------------------------------
 
 @pytest.mark.parametrize("M,K,N,norm", [(1, 256, 16, False), (1, 4096, 6144, True), (3, 2048, 512, True),

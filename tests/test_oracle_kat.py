@@ -24,6 +24,18 @@ def test_kat_argmax(kat):
         assert got.tolist() == case["expect"], case["src"]
 
 
+def test_kat_sample_filtered(kat):
+    """The reference's top-k / top-p / min-p tests (lib.rs:821-853, 1070-1115): the kept tokens
+    and, where the filter leaves one token with mass, the token itself, for any uniform."""
+    us = np.linspace(0, 1, 64, endpoint=False, dtype=np.float32)
+    for case in kat["sample_filtered"]:
+        lg = np.array(case["logits"], np.float32)
+        got = {int(orc.sample_filtered(lg, case["temperature"], case["top_k"], case["top_p"],
+                                       case["min_p"], np.array([u], np.float32))[0]) for u in us}
+        want = {case["expect"]} if case["expect"] is not None else set(case["allowed"])
+        assert got == want, (case["src"], got, want)
+
+
 def test_kat_penalties(kat):
     for case in kat["penalties"]:
         got = orc.apply_penalties(np.array(case["logits"], np.float32), case["history"],
@@ -140,6 +152,82 @@ def test_golden_reproduced(golden):
     assert np.array_equal(orc.sample(g["sm_logits"], 0.0, None), g["sm_t0"])
     acc, toks = orc.spec_accept(g["sa_tl"], g["sa_dl"], g["sa_dt"], 0.7, g["sa_au"], g["sa_su"])
     assert np.array_equal(acc, g["sa_acc"]) and np.array_equal(toks, g["sa_toks"])
+    fl, fu = g["sf_logits"], g["sf_u"]
+    assert np.array_equal(orc.sample_filtered(fl, 0.8, top_k=40, uniforms=fu), g["sf_k40"])
+    assert np.array_equal(orc.sample_filtered(fl, 0.8, top_p=0.9, uniforms=fu), g["sf_p09"])
+    assert np.array_equal(orc.sample_filtered(fl, 0.8, min_p=0.1, uniforms=fu), g["sf_m01"])
+    assert np.array_equal(orc.sample_filtered(fl, 1.3, top_k=100, top_p=0.8, min_p=0.02, uniforms=fu),
+                          g["sf_all"])
+    lp, ids, tlp = orc.logprobs(fl, 0.7, g["lp_tokens"], 5)
+    assert np.array_equal(lp, g["lp_lp"]) and np.array_equal(ids, g["lp_ids"])
+    assert np.array_equal(tlp, g["lp_top"])
+    assert np.array_equal(orc.apply_token_mask(fl, g["mk_bits"]), g["mk_out"])
+
+
+def _filtered_reference(lg, T, top_k, top_p, min_p):
+    """A plain restatement of sample_filtered's masks (lib.rs:392-460) on the oracle's
+    fixed-point masses: a stable descending argsort, the three masks, their product."""
+    inv_t = np.float32(1.0) / np.float32(T)
+    s = (lg.astype(np.float32) * inv_t).astype(np.float32)
+    mxs = np.float32(lg.max()) * inv_t
+    E = np.array([np.uint64(np.float64(orc.det_exp(float(np.float32(v - mxs)))) * 4294967296.0)
+                  for v in s], np.uint64)
+    order = np.argsort(-E.astype(np.float64), kind="stable")
+    Es = E[order]
+    V = lg.size
+    k = V if top_k <= 0 or top_k > V else top_k
+    rank_ok = np.arange(V) < k
+    cum = np.cumsum(Es.astype(np.uint64))
+    p_ok = (cum.astype(np.float64) <= np.float64(np.float32(top_p)) * np.float64(E.sum())) \
+        if top_p < 1.0 else np.ones(V, bool)
+    p_ok[0] = True
+    m_ok = (Es.astype(np.float64) >= np.float64(np.float32(min(min_p, 1.0))) * np.float64(Es[0])) \
+        if min_p > 0 else np.ones(V, bool)
+    keep = np.zeros(V, bool)
+    keep[order] = rank_ok & p_ok & m_ok
+    return keep
+
+
+@pytest.mark.parametrize("top_k,top_p,min_p", [(5, 1.0, 0.0), (0, 0.6, 0.0), (0, 1.0, 0.05),
+                                               (30, 0.95, 0.01), (1, 1.0, 0.0), (0, 0.0, 0.0)])
+def test_sample_filtered_keeps_exactly_the_mask_product(top_k, top_p, min_p):
+    """Every draw lands in the kept set of the plain restatement, and with a dense grid of
+    uniforms every kept token is drawn with its renormalised mass."""
+    rng = np.random.default_rng(11)
+    lg = rng.normal(0, 1.5, size=(1, 64)).astype(np.float32)
+    lg[0, 10:14] = lg[0, 3]  # ties
+    T = 0.9
+    keep = _filtered_reference(lg[0], T, top_k, top_p, min_p)
+    us = np.linspace(0, 1, 20000, endpoint=False, dtype=np.float32)
+    toks = orc.sample_filtered(np.repeat(lg, len(us), 0), T, top_k, top_p, min_p, us)
+    assert keep[toks].all()
+    p = np.exp(lg[0].astype(np.float64) / T - lg[0].max() / T) * keep
+    p /= p.sum()
+    np.testing.assert_allclose(np.bincount(toks, minlength=64) / len(us), p, atol=2e-3)
+
+
+def test_logprobs_match_float64_log_softmax():
+    rng = np.random.default_rng(12)
+    lg = rng.normal(0, 4, size=(3, 5000)).astype(np.float32)
+    toks = np.array([0, 17, 4999], np.int32)
+    for T in (0.0, 0.7, 1.5):
+        lp, ids, tlp = orc.logprobs(lg, T, toks, 6)
+        inv = np.float32(1.0) if T <= 1.1920929e-07 else np.float32(1.0) / np.float32(T)
+        s = (lg * inv).astype(np.float64)
+        ref = s - s.max(1, keepdims=True)
+        ref = ref - np.log(np.exp(ref).sum(1, keepdims=True))
+        np.testing.assert_allclose(lp, ref[np.arange(3), toks], atol=2e-6)
+        order = np.argsort(-(lg * inv), axis=1, kind="stable")[:, :6]
+        assert np.array_equal(ids, order)
+        np.testing.assert_allclose(tlp, np.take_along_axis(ref, order, 1), atol=2e-6)
+
+
+def test_token_mask_adds_minus_inf():
+    lg = np.array([[1.0, -2.0, 0.5, 3.0, -0.0, 7.0]], np.float32)
+    bits = orc.allowed_bits([[1, 4]], 6)
+    out = orc.apply_token_mask(lg, bits)
+    assert out[0, 1] == -2.0 and out[0, 4] == 0.0 and not np.signbit(out[0, 4])
+    assert np.all(np.isneginf(out[0, [0, 2, 3, 5]]))
 
 
 # ---- oracle self-consistency ---------------------------------------------------------
