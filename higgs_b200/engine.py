@@ -21,6 +21,23 @@ from .model import Model
 
 
 @dataclasses.dataclass
+class SamplingParams:
+    """SamplingParams (crates/higgs-models/src/lib.rs:30-68).  top_k 0, top_p 1, min_p 0 and the
+    neutral penalty values (1, 0, 0) mean "off"; temperature 0 is greedy."""
+    temperature: float = 1.0
+    top_p: float = 1.0
+    top_k: int = 0
+    min_p: float = 0.0
+    repetition_penalty: float = 1.0
+    frequency_penalty: float = 0.0
+    presence_penalty: float = 0.0
+
+    def has_penalties(self) -> bool:
+        return (self.repetition_penalty != 1.0 or self.frequency_penalty != 0.0
+                or self.presence_penalty != 0.0)
+
+
+@dataclasses.dataclass
 class Sequence:
     prompt: np.ndarray
     pages: list = dataclasses.field(default_factory=list)
@@ -182,6 +199,82 @@ class Engine:
                 s.generated.append(s.last_token)
             out[:, k] = toks
         return out
+
+    def decode_steps_sampled(self, seqs: list[Sequence], steps: int, params: SamplingParams,
+                             uniforms: np.ndarray, top_logprobs: int | None = None,
+                             allowed=None):
+        """`steps` sampled decode steps: each step's logits go through the reference's logits
+        processors on the device, in its order (crates/higgs-engine/src/simple.rs:318-347):
+        penalties over the tokens generated so far, the constraint mask, sample() with the
+        top-k / top-p / min-p filters, and logprobs of the scaled, masked logits.
+
+        uniforms f32 [steps, B] drive the draws; allowed(step) -> list of B allowed-token-id
+        lists (or None for no constraint at that step) stands for the host-side FSM.  Returns
+        (tokens [B, steps], logprobs [B, steps] or None, top ids / top logprobs [B, steps, n]
+        or None)."""
+        from . import ops
+        B = len(seqs)
+        dev = self.model.device
+        V = self.model.args.vocab_size
+        g = self._graph_for_logits(B)
+        out = np.zeros((B, steps), np.int32)
+        lps = np.zeros((B, steps), np.float32) if top_logprobs is not None else None
+        n = top_logprobs or 0
+        tids = np.zeros((B, steps, n), np.int32)
+        tlps = np.zeros((B, steps, n), np.float32)
+        u_dev = torch.empty(B, dtype=torch.float32, device=dev)
+        tok_dev = torch.empty(B, dtype=torch.int32, device=dev)
+        for k in range(steps):
+            self.stage_step(seqs, g, first=(k == 0))
+            u_dev.copy_(torch.from_numpy(np.ascontiguousarray(uniforms[k], dtype=np.float32)))
+            g.run()
+            logits = g.logits[:, :V]
+            if self.keep_logits:  # the model's logits, before the processors
+                self.step_logits.append(logits.cpu().numpy())
+            if params.has_penalties():
+                hmax = max(1, max(len(s.generated) for s in seqs))
+                hist = np.zeros((B, hmax), np.int32)
+                lens = np.array([len(s.generated) for s in seqs], np.int32)
+                for i, s in enumerate(seqs):
+                    hist[i, :len(s.generated)] = s.generated
+                ops.apply_penalties(logits, torch.from_numpy(hist).to(dev), torch.from_numpy(lens).to(dev),
+                                    params.repetition_penalty, params.frequency_penalty,
+                                    params.presence_penalty)
+            sets = allowed(k) if allowed is not None else None
+            if sets is not None:
+                bits = np.zeros((B, (V + 31) // 32), np.uint32)
+                for i, ids in enumerate(sets):
+                    ids = np.asarray(ids, np.int64)
+                    ids = ids[(ids >= 0) & (ids < V)]
+                    np.bitwise_or.at(bits[i], ids // 32, np.uint32(1) << (ids % 32).astype(np.uint32))
+                ops.apply_token_mask(logits, torch.from_numpy(bits.view(np.int32)).to(dev))
+            tok = ops.sample_filtered(logits, params.temperature, params.top_k, params.top_p,
+                                      params.min_p, u_dev)
+            tok_dev.copy_(tok)
+            if top_logprobs is not None:
+                lp, ti, tl = ops.logprobs(logits, params.temperature, tok_dev, n)
+            g.tokens.view(B).copy_(tok_dev)  # the next step feeds the sampled token
+            toks = tok_dev.cpu().numpy()
+            if top_logprobs is not None:
+                lps[:, k] = lp.cpu().numpy()
+                tids[:, k] = ti.cpu().numpy()
+                tlps[:, k] = tl.cpu().numpy()
+            for i, s in enumerate(seqs):
+                s.length += 1
+                s.last_token = int(toks[i])
+                s.generated.append(s.last_token)
+            out[:, k] = toks
+        if top_logprobs is None:
+            return out, None, None, None
+        return out, lps, tids, tlps
+
+    def _graph_for_logits(self, B: int) -> _DecodeGraph:
+        """The decode graph of batch B with its logits kept on the device."""
+        key = ("logits", B)
+        if key not in self._graphs:
+            self._graphs[key] = _DecodeGraph(self.model, B, self.max_blocks, self.max_seq_len,
+                                             self.use_graph, True)
+        return self._graphs[key]
 
     def generate_greedy(self, prompts, max_new_tokens: int, use_prefix: bool = True) -> np.ndarray:
         """Prefill each prompt, then decode all of them together; tokens [B, max_new_tokens]

@@ -93,6 +93,13 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_prefix_cache_clear": (I, [P]),
     "higgs_prefix_cache_lookup": (I, [P, P, I, P, I, ctypes.POINTER(I)]),
     "higgs_prefix_cache_store": (I, [P, P, I, P, I]),
+    "higgs_safetensors_open": (I, [ctypes.c_char_p, ctypes.POINTER(P)]),
+    "higgs_safetensors_close": (I, [P]),
+    "higgs_safetensors_count": (I, [P]),
+    "higgs_safetensors_find": (I, [P, ctypes.c_char_p]),
+    "higgs_safetensors_info": (I, [P, I, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(I),
+                                   ctypes.POINTER(I), ctypes.POINTER(I64)]),
+    "higgs_safetensors_read": (I, [P, P, I, I64, I64, I64, I64, P, I, P]),
 }
 
 
@@ -113,7 +120,7 @@ class ForwardArgs(ctypes.Structure):
                 ("workspace", P), ("workspace_bytes", SZ)]
 
 
-DTYPE_U32, DTYPE_BF16, DTYPE_F32 = 0, 1, 2
+DTYPE_U32, DTYPE_BF16, DTYPE_F32, DTYPE_F16 = 0, 1, 2, 3
 KV_BF16, KV_TQ4 = 0, 1
 
 

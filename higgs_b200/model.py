@@ -218,36 +218,49 @@ def check_tp(args: ModelArgs, world: int):
         raise ValueError(f"{args.model_type} cannot be split {world} ways")
 
 
-def shard_weights(args: ModelArgs, weights: dict, rank: int, world: int) -> dict:
-    """This rank's slices of MLX-layout weights (numpy arrays or torch tensors): rows of the
-    column-parallel projections and of the LM head, K columns (in 64-wide groups) of the
-    row-parallel ones, its kv head(s), its experts (expert parallelism: experts
-    [rank*E/world, (rank+1)*E/world)); norms, the router and the embedding whole (a tied
-    head is sliced by the runner)."""
-    check_tp(args, world)
+def shard_plan(args: ModelArgs, name: str, rows: int, cols: int, rank: int, world: int):
+    """This rank's slice (row0, rows, col0, cols) of tensor `name` viewed as 2-D (leading dims
+    flattened into rows): rows of the column-parallel projections and of the LM head, K columns
+    (whole 64-wide groups) of the row-parallel ones, its kv head(s), its experts (expert
+    parallelism: experts [rank*E/world, (rank+1)*E/world), contiguous rows); everything else
+    (norms, the router, the embedding -- a tied head is sliced by the runner) whole."""
+    if world == 1:
+        return 0, rows, 0, cols
     D, Hkv = args.head_dim, args.num_key_value_heads
     kvr = kv_heads_per_rank(args, world)
     kv0 = (rank * Hkv) // world if Hkv < world else rank * kvr  # first kv head of this rank
+    base, _, _ = name.rpartition(".")
+    mod = base.split(".", 3)[-1] if base.startswith("model.layers.") else base
+    if mod in ("self_attn.k_proj", "self_attn.v_proj"):
+        return kv0 * D, kvr * D, 0, cols
+    if mod in _COL or base == "lm_head" or mod.startswith("mlp.switch_mlp."):
+        n = rows // world
+        return rank * n, n, 0, cols
+    if mod in _ROW:
+        n = cols // world  # words (weight) or groups (scales / biases)
+        return 0, rows, rank * n, n
+    return 0, rows, 0, cols
+
+
+def shard_weights(args: ModelArgs, weights: dict, rank: int, world: int) -> dict:
+    """This rank's slices (shard_plan) of MLX-layout weights (numpy arrays or torch tensors)."""
+    check_tp(args, world)
 
     def cont(a):
         return a.contiguous() if isinstance(a, torch.Tensor) else np.ascontiguousarray(a)
     out = {}
     for name, t in weights.items():
-        base, _, leaf = name.rpartition(".")
-        mod = base.split(".", 3)[-1] if base.startswith("model.layers.") else base
-        if mod in ("self_attn.k_proj", "self_attn.v_proj"):
-            out[name] = t[kv0 * D:(kv0 + kvr) * D]
-        elif mod in _COL or base == "lm_head":
-            n = t.shape[0] // world
-            out[name] = t[rank * n:(rank + 1) * n]
-        elif mod in _ROW:
-            n = t.shape[1] // world  # words (weight) or groups (scales / biases)
-            out[name] = cont(t[:, rank * n:(rank + 1) * n])
-        elif mod.startswith("mlp.switch_mlp."):
-            n = t.shape[0] // world
-            out[name] = t[rank * n:(rank + 1) * n]
-        else:
+        shape = tuple(t.shape)
+        rows = int(np.prod(shape[:-1])) if len(shape) > 1 else 1
+        r0, nr, c0, nc = shard_plan(args, name, rows, shape[-1], rank, world)
+        if (r0, nr, c0, nc) == (0, rows, 0, shape[-1]):
             out[name] = t
+            continue
+        per = rows // shape[0] if len(shape) > 1 else 1  # flattened rows per leading index
+        if c0 == 0 and nc == shape[-1]:  # a run of leading indices
+            out[name] = t[r0 // per:(r0 + nr) // per]
+        else:
+            out[name] = cont(t[..., c0:c0 + nc])
     return out
 
 

@@ -63,6 +63,7 @@ extern "C" {
 #define HIGGS_DTYPE_U32 0
 #define HIGGS_DTYPE_BF16 1
 #define HIGGS_DTYPE_F32 2
+#define HIGGS_DTYPE_F16 3
 
 #define HIGGS_KV_BF16 0 /* bf16 pages [pages, Hkv, 16, D] */
 #define HIGGS_KV_TQ4 1  /* TurboQuant pages: codes [pages, Hkv, 16, 64] + fp16 scales */
@@ -73,6 +74,7 @@ typedef struct higgs_graph higgs_graph;
 typedef struct higgs_block_pool higgs_block_pool;
 typedef struct higgs_prefix_cache higgs_prefix_cache;
 typedef struct higgs_comm higgs_comm;
+typedef struct higgs_safetensors higgs_safetensors;
 
 /* ---- context and errors ------------------------------------------------ */
 
@@ -597,6 +599,33 @@ int higgs_prefix_cache_lookup(higgs_prefix_cache* pc, const int32_t* tokens, int
                               int32_t* pages_out, int max_pages, int* matched_tokens);
 int higgs_prefix_cache_store(higgs_prefix_cache* pc, const int32_t* tokens, int n,
                              const int32_t* pages, int n_pages);
+
+/* ---- (f)2: MLX-format safetensors model directories --------------------- */
+
+/* collect_safetensors_files + Array::load_safetensors
+ * (crates/higgs-models/src/lib.rs:604-723): opens model_dir's
+ * model.safetensors.index.json (every file its weight_map names) or its single
+ * model.safetensors, and memory-maps the files.  Tensor names are looked up
+ * as stored or with ".inner" segments removed (the reverse of
+ * remap_quantized_key, lib.rs:709-723), so both naming styles load.
+ * dtypes: U32 / I32 (packed codes, HIGGS_DTYPE_U32), BF16, F32, F16. */
+int higgs_safetensors_open(const char* model_dir, higgs_safetensors** out);
+int higgs_safetensors_close(higgs_safetensors* st);
+int higgs_safetensors_count(const higgs_safetensors* st);
+/* Index of the tensor called `name`, or -1 (not an error). */
+int higgs_safetensors_find(const higgs_safetensors* st, const char* name);
+/* Tensor i: its name (the ".inner"-free form; valid until close), dtype,
+ * rank and shape (up to 8 dims, written to shape[0..ndim)). */
+int higgs_safetensors_info(const higgs_safetensors* st, int i, const char** name, int* dtype,
+                           int* ndim, int64_t* shape);
+/* Copies rows [row0, row0 + rows) x columns [col0, col0 + cols) of tensor i
+ * (leading dims flattened into rows, columns = elements of the last dim) to
+ * dst, densely packed (row pitch cols * element size): host memory, or (with
+ * dst_on_device and a context) device memory through `stream`, complete on
+ * return.  A tensor-parallel rank reads only its own shard this way. */
+int higgs_safetensors_read(higgs_ctx* ctx, const higgs_safetensors* st, int i, int64_t row0,
+                           int64_t rows, int64_t col0, int64_t cols, void* dst, int dst_on_device,
+                           void* stream);
 
 #ifdef __cplusplus
 }

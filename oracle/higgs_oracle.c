@@ -60,6 +60,24 @@ static inline float h2f(uint16_t h) {
   return (float)v;
 }
 
+/*
+ * Summation order of the floating-point reductions below that have no order
+ * fixed by the reference (MLX leaves them to its kernels): 0 = the order each
+ * function documents; 1 = a second, equally valid order (matrix-form lane sums
+ * folded in reverse, vector-form groups summed last to first, attention dot
+ * products over d in reverse).  Comparing the two measures the rounding noise
+ * that any change of summation order alone puts into a bf16 forward -- the
+ * floor against which a GPU kernel's different order is judged.  The exact
+ * paths (router logits, sampling, TurboQuant codes) are only defined, and
+ * only used, at order 0.
+ */
+static int g_order = 0;
+int orc_set_order(int mode) {
+  const int old = g_order;
+  g_order = mode ? 1 : 0;
+  return old;
+}
+
 /* OpenMP team size for every parallel loop below; returns the size in force.
  * A launcher may have set OMP_NUM_THREADS=1 in the environment (torchrun does),
  * so the CPU baselines set it explicitly. */
@@ -211,7 +229,8 @@ void orc_qmatmul(const uint16_t* x, int64_t M, int64_t K, const uint32_t* q,
     for (int64_t m = 0; m < M; ++m) {
       const float* xr = xf + m * K;
       float acc = 0.0f;
-      for (int64_t g = 0; g < G; ++g) {
+      for (int64_t gi = 0; gi < G; ++gi) {
+        const int64_t g = g_order == 0 ? gi : G - 1 - gi;
         float sxq = 0.0f, sx = 0.0f;
         for (int w8 = 0; w8 < 8; ++w8) {
           const uint32_t word = row[g * 8 + w8];
@@ -263,7 +282,9 @@ static void dq_panel(const float* xf, int64_t M, int64_t K, const float* wp, int
       }
       for (int i = 0; i < nr; ++i) {
         const float* a = acc[i];
-        const float v = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));
+        const float v = g_order == 0
+                            ? ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]))
+                            : ((a[7] + a[6]) + (a[5] + a[4])) + ((a[3] + a[2]) + (a[1] + a[0]));
         const int64_t n = n0 + r + i;
         if (y_f32) y_f32[m * N + n] = v;
         if (y_bf16) y_bf16[m * N + n] = f2bf(v);
@@ -401,7 +422,10 @@ void orc_paged_attention(const uint16_t* q, int64_t B, int64_t Lq, int64_t Hq, i
           const int64_t pg = block_table[b * max_blocks + j / page];
           const uint16_t* kv = kc + pg * page_stride + hk * head_stride + (j % page) * D;
           float s = 0.0f;
-          for (int64_t d = 0; d < D; ++d) s += bf2f(qv[d]) * bf2f(kv[d]);
+          for (int64_t di = 0; di < D; ++di) {
+            const int64_t d = g_order == 0 ? di : D - 1 - di;
+            s += bf2f(qv[d]) * bf2f(kv[d]);
+          }
           sc[j] = s * scale;
           mx = sc[j] > mx ? sc[j] : mx;
         }

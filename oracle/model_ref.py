@@ -156,6 +156,16 @@ class RefModel:
         _, logits = self.lin(x, head, want_f32=True)
         return logits.reshape(B, Lq, -1)
 
+    def teacher_forced(self, prompts: np.ndarray, tokens: np.ndarray):
+        """Logits [steps, B, V] of the prefill's last position and of decode steps fed
+        tokens[:, k] (k < steps - 1): the oracle on a given token stream."""
+        B, steps = tokens.shape
+        caches = [self.new_cache() for _ in range(B)]
+        out = [self.forward(prompts, caches, last_only=True)[:, -1]]
+        for k in range(steps - 1):
+            out.append(self.forward(tokens[:, k:k + 1].astype(np.int32), caches)[:, -1])
+        return np.stack(out)
+
     def greedy(self, prompts: np.ndarray, steps: int):
         """Prefill [B, P] prompts then `steps` greedy decode tokens; returns (tokens [B, steps],
         logits of each step [steps, B, V])."""

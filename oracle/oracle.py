@@ -43,6 +43,22 @@ def set_threads(n: int) -> int:
     return int(lib().orc_set_threads(int(n)))
 
 
+class summation_order:
+    """Context manager: run the oracle's unordered floating-point reductions in the second
+    valid order (orc_set_order(1)) -- two restatements of the same arithmetic whose difference
+    is the rounding noise of summation order alone."""
+
+    def __init__(self, mode: int = 1):
+        self.mode = mode
+
+    def __enter__(self):
+        self.old = lib().orc_set_order(self.mode)
+        return self
+
+    def __exit__(self, *exc):
+        lib().orc_set_order(self.old)
+
+
 def _ptr(a):
     return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
 

@@ -154,7 +154,9 @@ def test_moe_model_matches_oracle():
     Expert choice is a discontinuous function of the router logits: where the oracle's k-th
     and (k+1)-th logits of a step lie within one bf16 ulp, a last-bit difference upstream may
     swap an expert on one side only.  Those (step, sequence) rows are excluded from the
-    logits bound (and must stay a small minority); every other row meets the dense bar."""
+    logits bound (and must stay a small minority).  Every other row meets the dense bar, or --
+    where the oracle's own rounding noise reaches past it -- stays within 1.5x of the noise
+    the oracle shows under a second valid summation order (orc_set_order(1))."""
     args, w, m, _ = build("qwen3_moe", layers=3)
     assert [args.is_moe_layer(i) for i in range(3)] == [True, False, True]
     pr = prompts(args, 2, 20, seed=3)
@@ -163,7 +165,15 @@ def test_moe_model_matches_oracle():
     near = ref.step_route_near[1:]  # rows of gl
     assert near.mean() < 0.35, f"too many near-tie routings: {near.mean():.2f}"
     keep = ~near
-    np.testing.assert_allclose(gl[keep], ref_lg[1:][keep], atol=2e-2, rtol=1e-2)
+    with orc.summation_order(1):
+        alt = ref.teacher_forced(pr, ref_tok)
+    err = np.abs(gl[keep] - ref_lg[1:][keep])
+    floor = np.abs(alt[1:][keep] - ref_lg[1:][keep])
+    inside = err <= 2e-2 + 1e-2 * np.abs(ref_lg[1:][keep])
+    print(f"\nMoE logits: max {err.max():.3e} std {err.std():.3e} inside the bar {inside.mean():.4f}; "
+          f"reordered oracle max {floor.max():.3e} std {floor.std():.3e}")
+    assert inside.all() or (err.max() <= 1.5 * floor.max() + 1e-3
+                            and err.std() <= 1.5 * floor.std() + 1e-4)
     agree = forced.T == ref_tok[:, 1:].T
     top2 = np.sort(ref_lg[1:], axis=-1)[..., -2:]
     margin = top2[..., 1] - top2[..., 0]
@@ -242,3 +252,72 @@ def test_spec_decode_sampled_step_matches_oracle_accept():
         sd.tok[0].copy_(torch.from_numpy(last))
     for s in seqs:
         eng.release(s)
+
+
+def test_sampled_decode_processors_match_oracle():
+    """Sampled decode through Engine.decode_steps_sampled: every step's logits pass through the
+    penalties (over the generated tokens), the constraint mask, the top-k / top-p / min-p draw
+    and logprobs on the device, in the reference's order (simple.rs:318-347).  Each step is
+    checked bit for bit against the oracle's processors applied to the same raw logits with
+    the same uniforms (the draws, masked tokens and penalised values are integer / exact)."""
+    from higgs_b200.engine import Engine, SamplingParams
+    args, w, m, _ = build("qwen3")
+    pr = prompts(args, 2, 16, seed=21)
+    eng = Engine(m, max_seq_len=128, keep_logits=True)
+    seqs = [eng.prefill(p, use_prefix=False) for p in pr]
+    for s in seqs:
+        s.generated.append(s.last_token)
+    params = SamplingParams(temperature=0.8, top_p=0.9, top_k=50, min_p=0.01,
+                            repetition_penalty=1.3, frequency_penalty=0.2, presence_penalty=0.1)
+    steps = 12
+    rng = np.random.default_rng(5)
+    u = rng.random((steps, 2)).astype(np.float32)
+    allowed_sets = {k: [rng.choice(args.vocab_size, size=300, replace=False).tolist() for _ in range(2)]
+                    for k in range(0, steps, 2)}
+    hist0 = [list(s.generated) for s in seqs]
+    eng.step_logits.clear()
+    toks, lps, tids, tlps = eng.decode_steps_sampled(seqs, steps, params, u, top_logprobs=4,
+                                                     allowed=lambda k: allowed_sets.get(k))
+    hist = [list(h) for h in hist0]
+    for k in range(steps):
+        raw = eng.step_logits[k]
+        for b in range(2):
+            lg = orc.apply_penalties(raw[b], hist[b], params.repetition_penalty,
+                                     params.frequency_penalty, params.presence_penalty)[None]
+            if k in allowed_sets:
+                lg = orc.apply_token_mask(lg, orc.allowed_bits([allowed_sets[k][b]], args.vocab_size))
+                assert toks[b, k] in set(allowed_sets[k][b])
+            ref = orc.sample_filtered(lg, params.temperature, params.top_k, params.top_p,
+                                      params.min_p, u[k, b:b + 1])
+            assert toks[b, k] == ref[0], (k, b)
+            rlp, rids, rtl = orc.logprobs(lg, params.temperature, toks[b:b + 1, k], 4)
+            np.testing.assert_allclose(lps[b, k], rlp[0], atol=1e-6)
+            assert np.array_equal(tids[b, k], rids[0])
+            np.testing.assert_allclose(tlps[b, k], rtl[0], atol=1e-6)
+            hist[b].append(int(toks[b, k]))
+    for s in seqs:
+        eng.release(s)
+
+
+def test_model_loaded_from_mlx_checkpoint(tmp_path):
+    """An MLX-format directory (config.json + two safetensors files with an index) loaded by
+    higgs_b200.loader onto the GPU gives the same device tensors and the same greedy stream as
+    the weights it was written from."""
+    from higgs_b200.engine import Engine
+    from higgs_b200.loader import load_model_args, load_weights
+    from higgs_b200.model import Model
+    from tests.mlx_checkpoint import write_model_dir
+    args, w, m, _ = build("qwen3")
+    write_model_dir(str(tmp_path), args, w, shards=2, inner_names=True)
+    a2 = load_model_args(str(tmp_path))
+    assert a2 == args
+    wd = load_weights(str(tmp_path), a2, DEV)
+    for k, v in w.items():
+        t = wd[k].view(torch.int16) if wd[k].dtype == torch.bfloat16 else wd[k]
+        got = t.cpu().numpy().view(v.dtype)
+        assert got.shape == v.shape and np.array_equal(got, v), k
+    m2 = Model(a2, wd, num_pages=256, device=DEV)
+    pr = prompts(args, 2, 20, seed=13)
+    a = Engine(m, max_seq_len=128).generate_greedy(list(pr), 16, use_prefix=False)
+    b = Engine(m2, max_seq_len=128).generate_greedy(list(pr), 16, use_prefix=False)
+    assert np.array_equal(a, b)
