@@ -56,6 +56,7 @@ void set_gemm_tc_wave_cost(int c);
 void qgemv_set_wk(int wk);
 void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);
 void qgemm_tc_prepare();
+void decode_chain_set(int on, int l2_ahead);
 
 }  // namespace higgs
 
@@ -90,6 +91,14 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
+    return HIGGS_OK;
+  }
+  if (n == "decode_chain") {
+    decode_chain_set(value != 0, -1);
+    return HIGGS_OK;
+  }
+  if (n == "decode_chain_l2_ahead") {
+    decode_chain_set(-1, value != 0);
     return HIGGS_OK;
   }
   if (n == "gemv_m1_l2") {

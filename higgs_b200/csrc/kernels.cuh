@@ -112,6 +112,35 @@ int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int H
 // M == 1 (decode at batch 1): the register-fed GEMV of qgemv_m1.cu; launch_qgemv_ring routes there itself.
 bool qgemv_m1_supported(const QLinArgs& a);
 cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st);
+
+// One GEMV phase of a decode chain (qgemv_m1.cu): y = W x for one token, with an optional
+// fused RMSNorm of x, SwiGLU over gate (w) / up (w2), q|k|v row segments and a residual
+// epilogue; wk (the K split) is filled in by launch_decode_chain.
+constexpr int kChainMaxPhases = 4;
+struct ChainPhase {
+  const uint16_t* x;       // input [K] (bf16), written before the launch or by an earlier phase
+  const uint16_t* norm_w;  // fused RMSNorm of x (null: none)
+  int K, N, wk, swiglu;
+  int nseg;  // row segments (q|k|v); segment 0 is w[0]
+  int seg_end[3];
+  const uint32_t* w[3];
+  const uint16_t* s[3];
+  const uint16_t* b[3];
+  const uint32_t* w2;  // up projection (SwiGLU)
+  const uint16_t* s2;
+  const uint16_t* b2;
+  uint16_t* y;
+  float* y_f32;
+  const uint16_t* residual;
+};
+// Whether the persistent decode chain replaces the separate one-token GEMV launches
+// (higgs_set_option("decode_chain")) and whether a phase fits it.
+bool decode_chain_on();
+bool decode_chain_fits(const ChainPhase& p);
+// nph (<= kChainMaxPhases) phases in one launch; bar: nph zeroed u32 counters this launch
+// leaves zeroed again.  Bounded waits report through the per-device timeout flag.
+cudaError_t launch_decode_chain(ChainPhase* ph, int nph, float eps, unsigned* bar, cudaStream_t st);
+void decode_chain_set(int on, int l2_ahead);
 void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);  // -1 leaves a setting as it is
 // M >= 17: the tcgen05 matrix path (qgemm_tc.cu); launch_qgemv_ring routes there itself.
 bool qgemm_tc_supported(const QLinArgs& a);

@@ -88,7 +88,7 @@ size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
   size_t h, x, qkv, q, attn, act, xl, logits, moe_rl, moe_idx, moe_sc, moe_plan, moe_act, moe_y,
-      tp_part, tp_keys, tc_ws, tc_ws_bytes, attn_ws, total;
+      tp_part, tp_keys, tc_ws, tc_ws_bytes, chain_bar, attn_ws, total;
 };
 
 int head_rows(const higgs_model_config& c) { return c.tp_world > 1 ? c.head_rows : c.vocab; }
@@ -137,6 +137,8 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
     L.moe_act = take(P * (size_t)c.moe_intermediate * 2);
     L.moe_y = take(P * (size_t)c.hidden * 2);
   }
+  // decode-chain barrier counters, kChainMaxPhases per layer (zero between launches)
+  L.chain_bar = take((size_t)c.layers * kChainMaxPhases * 4);
   const size_t aws = higgs_paged_attention_workspace_size(B, Lq, c.heads, c.kv_heads, D, max_seq_len);
   L.attn_ws = take(aws);
   L.total = off;
@@ -298,11 +300,33 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   int rc = higgs_embed_gather_w4(m->ctx, f->tokens, T, m->embed.w, m->embed.s, m->embed.b, c.vocab,
                                  H, h, st);
   if (rc) return rc;
+  // One token on one GPU: the GEMVs between two attention launches run as one persistent
+  // decode-chain launch (o_proj, norm + gate/up, down, norm + the next q|k|v or the head).
+  const bool chain = !tp && T == 1 && fuse && !tq && decode_chain_on() &&
+                     (c.heads / c.kv_heads) * Lq <= 32;
+  unsigned* chain_bar = (unsigned*)(ws + L.chain_bar);
+  bool qkv_ready = false;   // the previous chain launch wrote this layer's q|k|v
+  bool head_done = false;   // the last chain launch wrote the logits
+  auto chain_qkv = [&](const LayerW& Ln, ChainPhase& P) {
+    P = ChainPhase{};
+    P.x = h;
+    P.norm_w = Ln.ln_in;
+    P.K = H;
+    P.N = Ln.q.N + Ln.k.N + Ln.v.N;
+    P.nseg = 3;
+    P.seg_end[0] = Ln.q.N;
+    P.seg_end[1] = Ln.q.N + Ln.k.N;
+    P.seg_end[2] = P.N;
+    P.w[0] = Ln.q.w, P.s[0] = Ln.q.s, P.b[0] = Ln.q.b;
+    P.w[1] = Ln.k.w, P.s[1] = Ln.k.s, P.b[1] = Ln.k.b;
+    P.w[2] = Ln.v.w, P.s[2] = Ln.v.s, P.b[2] = Ln.v.b;
+    P.y = qkv;
+  };
   for (int li = 0; li < n_layers; ++li) {
     const LayerW& Lw = m->layers[li];
     L2Prefetch next_pf{};
     const bool attn_fused = !tq && (c.heads / c.kv_heads) * Lq <= 32;
-    {
+    if (!qkv_ready) {
       if (!fuse) {
         rc = higgs_rmsnorm(m->ctx, h, nullptr, T, H, Lw.ln_in, c.rms_eps, x, nullptr, st);
         if (rc) return rc;
@@ -346,6 +370,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       if (!attn_fused) a.pf = next_pf;
       HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
     }
+    qkv_ready = false;
     if (tq) {
       rc = higgs_qknorm_rope_kv_write_tq4(
           m->ctx, qkv, T, c.heads, c.kv_heads, Lw.qn, Lw.kn, c.rms_eps, f->positions, m->inv_freq,
@@ -386,6 +411,45 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
                                  (int64_t)HIGGS_PAGE_SIZE * D, f->block_table, f->max_blocks,
                                  f->seq_lens, f->max_seq_len, scale, attn, aws, aws_bytes, st);
       if (rc) return rc;
+    }
+    if (chain && !Lw.moe) {
+      ChainPhase ph[kChainMaxPhases];
+      int n = 0;
+      ChainPhase& o = ph[n++];  // h = h + o_proj(attn)
+      o = ChainPhase{};
+      o.x = attn, o.K = Lw.o.K, o.N = Lw.o.N, o.nseg = 1;
+      o.w[0] = Lw.o.w, o.s[0] = Lw.o.s, o.b[0] = Lw.o.b;
+      o.y = h, o.residual = h;
+      ChainPhase& gu = ph[n++];  // act = swiglu(gate(norm(h)), up(norm(h)))
+      gu = ChainPhase{};
+      gu.x = h, gu.norm_w = Lw.ln_post, gu.K = H, gu.N = c.intermediate, gu.swiglu = 1, gu.nseg = 1;
+      gu.w[0] = Lw.gate.w, gu.s[0] = Lw.gate.s, gu.b[0] = Lw.gate.b;
+      gu.w2 = Lw.up.w, gu.s2 = Lw.up.s, gu.b2 = Lw.up.b;
+      gu.y = act;
+      ChainPhase& dn = ph[n++];  // h = h + down(act)
+      dn = ChainPhase{};
+      dn.x = act, dn.K = Lw.down.K, dn.N = Lw.down.N, dn.nseg = 1;
+      dn.w[0] = Lw.down.w, dn.s[0] = Lw.down.s, dn.b[0] = Lw.down.b;
+      dn.y = h, dn.residual = h;
+      if (li + 1 < n_layers && !m->layers[li + 1].moe) {
+        chain_qkv(m->layers[li + 1], ph[n]);
+        if (decode_chain_fits(ph[n])) {
+          ++n;
+          qkv_ready = true;
+        }
+      } else if (li + 1 == n_layers && (f->logits || f->argmax) && !f->hidden_out) {
+        ChainPhase& hd = ph[n];  // logits = head(norm(h))
+        hd = ChainPhase{};
+        hd.x = h, hd.norm_w = m->final_norm, hd.K = H, hd.N = m->head.N, hd.nseg = 1;
+        hd.w[0] = m->head.w, hd.s[0] = m->head.s, hd.b[0] = m->head.b;
+        hd.y_f32 = logits;
+        if (decode_chain_fits(hd)) {
+          ++n;
+          head_done = true;
+        }
+      }
+      HG_CUDA(launch_decode_chain(ph, n, c.rms_eps, chain_bar + (size_t)li * kChainMaxPhases, st));
+      continue;
     }
     // h = h + o_proj(attn)   (in place: each element read then written by one thread)
     {
@@ -468,7 +532,8 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   // final norm (+ last-token selection) and LM head
   const int rows_lm = f->last_only ? B : T;
   if (fuse && (Lq == 1 || !f->last_only) && !f->hidden_out) {
-    if (f->logits || f->argmax) HG_CUDA(lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
+    if ((f->logits || f->argmax) && !head_done)
+      HG_CUDA(lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
     if (f->argmax) {
       rc = emit_argmax(logits, rows_lm);
       if (rc) return rc;

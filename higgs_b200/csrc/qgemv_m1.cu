@@ -27,6 +27,9 @@
 // will stream (cp.async.bulk.prefetch), so HBM streams the CTA's whole slice from
 // its start while the register ring reads L2.  CTAs walk tile groups round-robin
 // (one group each by default; optionally a grid capped at the resident slots).
+#include <algorithm>
+#include <cstring>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "timeline.cuh"
@@ -403,6 +406,370 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
   HG_TL_END(1000 + EPI * 100 + NORM * 10 + WK);
 }
 
+// ---------------------------------------------------------------------------
+// Decode chain: the GEMVs between two attention launches of a one-token decode
+// step -- o_proj (+ residual), RMSNorm + gate/up + SwiGLU, down (+ residual),
+// RMSNorm + the next layer's q|k|v (or the final norm + LM head) -- as the
+// phases of one persistent launch of kChainCtasPerSm CTAs per SM.  Each phase
+// is the single-token GEMV above with its K split, tiles and summation order
+// (so its outputs equal the separate launches' bit for bit); phases are
+// separated by grid barriers (an arrival counter per phase, bounded waits).
+// What the separate launches cannot do: a CTA issues the next phase's weight
+// loads into its registers, and (l2_ahead) asks L2 for its next slice, before
+// it waits at the barrier, so HBM keeps streaming weights through the
+// dependency points instead of idling between launches.
+// ---------------------------------------------------------------------------
+struct ChainArgs {
+  ChainPhase ph[kChainMaxPhases];
+  int nph;
+  float eps;
+  unsigned* bar;  // nph arrival counters: zero at launch, zeroed again by the last CTA out
+  int* err;       // set when a barrier wait gives up
+  int l2_ahead;   // 1: a phase's L2 requests are issued while the previous phase runs
+};
+
+__device__ __forceinline__ unsigned chain_ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Arrival of this CTA at counter c (after every thread's writes of the phase).
+__device__ __forceinline__ unsigned chain_arrive(unsigned* c) {
+  __syncthreads();
+  unsigned old = 0;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    old = atomicAdd(c, 1u);
+  }
+  return old;
+}
+
+// Wait until every CTA has arrived at c; gives up (and sets *err) after ~2^24 polls.
+__device__ __forceinline__ void chain_wait(const unsigned* c, unsigned n, int* err) {
+  if (threadIdx.x == 0) {
+    unsigned it = 0;
+    while (chain_ld_acquire(c) < n) {
+      if (++it > (1u << 24)) {
+        if (err) atomicExch(err, 1);
+        break;
+      }
+      __nanosleep(32);
+    }
+  }
+  __syncthreads();
+}
+
+template <int D>
+__global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) chain_kernel(const __grid_constant__ ChainArgs a) {
+  static_assert(D % 2 == 0, "units are folded in pairs");
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float s_ss[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  struct Tile {
+    const uint32_t* W;
+    const uint16_t* S;
+    const uint16_t* B;
+    int row0, ub, ue;
+  };
+  // warp's tile of group grp in phase P (same mapping as qgemv_m1_kernel)
+  auto tile_of = [&](const ChainPhase& P, int grp) {
+    const int WK = P.wk, RT = 8 / WK, ROT = P.swiglu ? RT / 2 : RT;
+    const int rt = warp / WK, kw = warp % WK;
+    const int units = P.K / 256;
+    Tile tl;
+    int out_tile, which = 0;
+    if (P.swiglu) {
+      out_tile = grp * ROT + rt / 2;
+      which = rt & 1;
+    } else {
+      out_tile = grp * ROT + rt;
+    }
+    const int n0 = out_tile * 16;
+    const bool ok = n0 < P.N;
+    tl.W = which ? P.w2 : P.w[0];
+    tl.S = which ? P.s2 : P.s[0];
+    tl.B = which ? P.b2 : P.b[0];
+    tl.row0 = ok ? n0 : 0;
+    if (!P.swiglu && P.nseg > 1) {
+#pragma unroll
+      for (int i = 1; i < 3; ++i)
+        if (i < P.nseg && ok && n0 >= P.seg_end[i - 1]) {
+          tl.W = P.w[i];
+          tl.S = P.s[i];
+          tl.B = P.b[i];
+          tl.row0 = n0 - P.seg_end[i - 1];
+        }
+    }
+    tl.ub = ok ? (units * kw) / WK : 0;
+    tl.ue = ok ? (units * (kw + 1)) / WK : 0;
+    return tl;
+  };
+  auto n_groups_of = [&](const ChainPhase& P) {
+    const int RT = 8 / P.wk, ROT = P.swiglu ? RT / 2 : RT;
+    return (P.N / 16 + ROT - 1) / ROT;
+  };
+  // every tile this CTA streams in phase P -> L2, one request per tile (lanes 1, 2: scales,
+  // biases), issued by the warps that own a tile's first K range
+  auto l2_slice = [&](const ChainPhase& P) {
+    if (warp % P.wk != 0 || lane >= 3) return;
+    const int KW = P.K / 8, G = P.K / 64;
+    for (int grp = blockIdx.x; grp < n_groups_of(P); grp += gridDim.x) {
+      const Tile tl = tile_of(P, grp);
+      if (tl.ub >= tl.ue) continue;
+      if (lane == 0)
+        l2_prefetch_range(tl.W + (size_t)tl.row0 * KW, (size_t)16 * KW * 4);
+      else
+        l2_prefetch_range((lane == 1 ? tl.S : tl.B) + (size_t)tl.row0 * G, (size_t)16 * G * 2);
+    }
+  };
+
+  const uint4 *wg = nullptr, *w8 = nullptr;
+  const uint32_t *sgp = nullptr, *sg8 = nullptr, *bgp = nullptr, *bg8 = nullptr;
+  int ub = 0, ue = 0;
+  auto bind = [&](const ChainPhase& P, const Tile& tl) {
+    const int KW = P.K / 8, G = P.K / 64;
+    ub = tl.ub;
+    ue = tl.ue;
+    wg = reinterpret_cast<const uint4*>(tl.W + (size_t)(tl.row0 + g) * KW) + t;
+    w8 = wg + (size_t)2 * KW;
+    sgp = reinterpret_cast<const uint32_t*>(tl.S + (size_t)(tl.row0 + g) * G) + t;
+    sg8 = sgp + (size_t)4 * G;
+    bgp = reinterpret_cast<const uint32_t*>(tl.B + (size_t)(tl.row0 + g) * G) + t;
+    bg8 = bgp + (size_t)4 * G;
+  };
+  uint4 buf[D][4];
+  uint32_t sb[D / 2][4];
+  auto load_unit = [&](uint4 (&bb)[4], int u) {
+    bb[0] = m1_ldg128(wg + 8 * u);
+    bb[1] = m1_ldg128(wg + 8 * u + 4);
+    bb[2] = m1_ldg128(w8 + 8 * u);
+    bb[3] = m1_ldg128(w8 + 8 * u + 4);
+  };
+  auto load_scales = [&](uint32_t (&q)[4], int u0) {
+    const bool ok = u0 + (t >> 1) < ue;
+    q[0] = ok ? __ldg(sgp + 2 * u0) : 0u;
+    q[1] = ok ? __ldg(sg8 + 2 * u0) : 0u;
+    q[2] = ok ? __ldg(bgp + 2 * u0) : 0u;
+    q[3] = ok ? __ldg(bg8 + 2 * u0) : 0u;
+  };
+  auto prologue = [&]() {
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      if (ub + d < ue) load_unit(buf[d], ub + d);
+      if ((d & 1) == 0) load_scales(sb[d / 2], ub + d);
+    }
+  };
+
+  // phase 0's slice and first weights: none depends on the previous kernel
+  l2_slice(a.ph[0]);
+  if (a.l2_ahead && a.nph > 1) l2_slice(a.ph[1]);
+  bind(a.ph[0], tile_of(a.ph[0], blockIdx.x));
+  prologue();
+  const unsigned nct = gridDim.x;
+
+#pragma unroll 1
+  for (int p = 0; p < a.nph; ++p) {
+    const ChainPhase& P = a.ph[p];
+    const int K = P.K, N = P.N, WK = P.wk, G = K / 64;
+    const int RT = 8 / WK, ROT = P.swiglu ? RT / 2 : RT;
+    const bool norm = P.norm_w != nullptr;
+    uint4 nwr[kM1NormChunks];
+    if (norm) {
+#pragma unroll
+      for (int r = 0; r < kM1NormChunks; ++r) {
+        const int c = threadIdx.x + r * kM1Threads;
+        nwr[r] = c < K / 8 ? *reinterpret_cast<const uint4*>(P.norm_w + 8 * c) : make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (p == 0) {
+      pdl_wait();
+      pdl_launch();
+    } else {
+      chain_wait(a.bar + (p - 1), nct, a.err);
+    }
+    uint8_t* xf = smem;
+    uint8_t* zero = smem + m1_xf_bytes(K) + 64;
+    float* xs = reinterpret_cast<float*>(zero + 576);
+    float* red = xs + G;
+    if (threadIdx.x < 32) reinterpret_cast<uint4*>(zero)[threadIdx.x] = make_uint4(0, 0, 0, 0);
+    // activations were written by other CTAs of this launch: read them from L2 (ld.cg)
+    const uint16_t* x = P.x;
+    uint4 xr[kM1RegChunks];
+    float inv = 1.0f;
+    if (norm) {
+      float ss = 0.f;
+#pragma unroll
+      for (int r = 0; r < kM1RegChunks; ++r) xr[r] = make_uint4(0, 0, 0, 0);
+      for (int c = threadIdx.x, r = 0; c < K / 8; c += kM1Threads, ++r) {
+        const uint4 v = __ldcg(reinterpret_cast<const uint4*>(x + 8 * c));
+#pragma unroll
+        for (int j = 0; j < kM1RegChunks; ++j)
+          if (j == r) xr[j] = v;
+        const uint32_t* vp = &v.x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float lo = bf_lo(vp[j]), hi = bf_hi(vp[j]);
+          ss += lo * lo + hi * hi;
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) s_ss[warp] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) tot += s_ss[w];
+      inv = 1.0f / sqrtf(tot / (float)K + a.eps);
+    }
+    for (int base = warp * 32, r = 0; base < K / 8; base += kM1Threads, ++r) {
+      const int c = base + lane;
+      uint4 v;
+      if (norm) {
+        v = xr[0];
+#pragma unroll
+        for (int j = 1; j < kM1RegChunks; ++j)
+          if (j == r) v = xr[j];
+        if (r >= kM1RegChunks) v = __ldcg(reinterpret_cast<const uint4*>(x + 8 * c));
+        uint4 wv = nwr[0];
+#pragma unroll
+        for (int j = 1; j < kM1NormChunks; ++j)
+          if (j == r) wv = nwr[j];
+        if (r >= kM1NormChunks) wv = *reinterpret_cast<const uint4*>(P.norm_w + 8 * c);
+        uint32_t* vp = &v.x;
+        const uint32_t* wp = &wv.x;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          vp[j] = pack_bf2(bf_lo(vp[j]) * inv * bf_lo(wp[j]), bf_hi(vp[j]) * inv * bf_hi(wp[j]));
+      } else {
+        v = __ldcg(reinterpret_cast<const uint4*>(x + 8 * c));
+      }
+      const int u = c >> 5, h = (c >> 4) & 1, tt = (c >> 2) & 3, e = c & 3;
+      *reinterpret_cast<uint4*>(xf + ((u * 8 + h * 4 + e) * 4 + tt) * 16) = m1_frag(v);
+      const uint32_t* vp = &v.x;
+      float x1 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) x1 += bf_lo(vp[j]) + bf_hi(vp[j]);
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) x1 += __shfl_xor_sync(0xffffffffu, x1, o);
+      if ((lane & 7) == 0) xs[c >> 3] = x1;
+    }
+    __syncthreads();
+    if (a.l2_ahead && p + 2 < a.nph) l2_slice(a.ph[p + 2]);
+
+    const uint32_t xreal = smem_u32(xf) + t * 16;
+    const uint32_t xzero = smem_u32(zero);
+    const float2* xs2 = reinterpret_cast<const float2*>(xs);
+    const int n_groups = n_groups_of(P);
+    for (int grp = blockIdx.x; grp < n_groups; grp += gridDim.x) {
+      if (grp != (int)blockIdx.x) {
+        bind(P, tile_of(P, grp));
+        prologue();
+      }
+      float acc[2][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[h][c] = 0.f;
+      float yg = 0.f, yg8 = 0.f;
+      for (int base = ub; base < ue; base += D) {
+#pragma unroll
+        for (int d = 0; d < D; ++d) {
+          const int u = base + d;
+          if (u >= ue) break;
+          const int pp = d & 1;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const bool act = g == 4 * pp + 2 * h + (t >> 1);
+            const uint32_t xb = (act ? xreal + u * 512 : xzero) + h * 256;
+            uint4 xv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) xv[e] = m1_lds128(xb + e * 64);
+            const uint32_t* wa = &buf[d][h].x;
+            const uint32_t* wb = &buf[d][2 + h].x;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t A = wa[e], B = wb[e];
+              m1_mma(acc[h], nib_pair_bf16<0>(A), nib_pair_bf16<0>(B), nib_pair_bf16<4>(A),
+                     nib_pair_bf16<4>(B), xv[e].x, xv[e].y);
+              m1_mma(acc[h], nib_pair_bf16<8>(A), nib_pair_bf16<8>(B), nib_pair_bf16<12>(A),
+                     nib_pair_bf16<12>(B), xv[e].z, xv[e].w);
+            }
+          }
+          if (u + D < ue) load_unit(buf[d], u + D);
+          if (pp == 1 || u + 1 == ue) {
+            const int u0 = u - pp;
+            const bool ok = u0 + (t >> 1) < ue;
+            const float2 X = xs2[ok ? 2 * u0 + t : 0];
+            const uint32_t* q = sb[d / 2];
+            const float sa = bf_lo(q[0]), sb_ = bf_hi(q[0]), s8a = bf_lo(q[1]), s8b = bf_hi(q[1]);
+            const float ba = fmaf(-128.0f, sa, bf_lo(q[2])), bb = fmaf(-128.0f, sb_, bf_hi(q[2]));
+            const float b8a = fmaf(-128.0f, s8a, bf_lo(q[3])), b8b = fmaf(-128.0f, s8b, bf_hi(q[3]));
+            yg = fmaf(sa, acc[0][0] + acc[1][0], fmaf(ba, X.x, yg));
+            yg = fmaf(sb_, acc[0][1] + acc[1][1], fmaf(bb, X.y, yg));
+            yg8 = fmaf(s8a, acc[0][2] + acc[1][2], fmaf(b8a, X.x, yg8));
+            yg8 = fmaf(s8b, acc[0][3] + acc[1][3], fmaf(b8b, X.y, yg8));
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) acc[h][c] = 0.f;
+            if (u0 + D < ue) load_scales(sb[d / 2], u0 + D);
+          }
+        }
+      }
+      yg += __shfl_xor_sync(0xffffffffu, yg, 1);
+      yg += __shfl_xor_sync(0xffffffffu, yg, 2);
+      yg8 += __shfl_xor_sync(0xffffffffu, yg8, 1);
+      yg8 += __shfl_xor_sync(0xffffffffu, yg8, 2);
+      if (t == 0) {
+        red[warp * 16 + g] = yg;
+        red[warp * 16 + g + 8] = yg8;
+      }
+      __syncthreads();
+      if ((int)threadIdx.x < ROT * 16) {
+        const int r = threadIdx.x >> 4, j = threadIdx.x & 15;
+        const int tile = grp * ROT + r;
+        const int row = tile * 16 + j;
+        if (tile * 16 < N) {
+          if (P.swiglu) {
+            float vg = 0.f, vu = 0.f;
+            for (int w = 0; w < WK; ++w) {
+              vg += red[((2 * r) * WK + w) * 16 + j];
+              vu += red[((2 * r + 1) * WK + w) * 16 + j];
+            }
+            const float gv = round_bf(vg), uv = round_bf(vu);
+            P.y[row] = f2bf(gv / (1.0f + expf(-gv)) * uv);
+          } else {
+            float v = 0.f;
+            for (int w = 0; w < WK; ++w) v += red[(r * WK + w) * 16 + j];
+            if (P.y_f32) P.y_f32[row] = v;
+            if (P.y) {
+              uint16_t o = f2bf(v);
+              if (P.residual) o = f2bf(bf2f(o) + bf2f(__ldcg(P.residual + row)));
+              P.y[row] = o;
+            }
+          }
+        }
+      }
+      __syncthreads();
+    }
+    // the next phase's first weights go in flight before the barrier
+    if (p + 1 < a.nph) {
+      const ChainPhase& Q = a.ph[p + 1];
+      if (!a.l2_ahead) l2_slice(Q);
+      bind(Q, tile_of(Q, blockIdx.x));
+      prologue();
+    }
+    const unsigned old = chain_arrive(a.bar + p);
+    if (p + 1 == a.nph && threadIdx.x == 0 && old == nct - 1) {
+      // the last CTA out: every other CTA has passed every wait of this launch
+      for (int i = 0; i < a.nph; ++i) a.bar[i] = 0u;
+      __threadfence();
+    }
+  }
+}
+
 bool g_m1_on = true;
 bool g_m1_l2 = true;  // each CTA prefetches its whole weight slice to L2 before the wait
 int g_m1_wk = 0;      // forced K split (1, 2, 4, 8), 0 = cost model
@@ -424,6 +791,44 @@ cudaError_t m1_launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t
   if (e != cudaSuccess) return e;
   return launch_pdl(k, dim3(ctas), dim3(kM1Threads), smem, st, a);
 }
+
+}  // namespace
+
+// K split of a one-CTA-per-group launch (the default): single matrices take the most K splits
+// whose CTAs fit one wave, so every CTA is resident (and has asked L2 for its whole slice) from
+// the start; wider outputs take wk = 1.  Gate/up (twice the bytes per row tile) takes the
+// fewest splits that fill every slot -- at wk = 1 its 57 MB is not in L2 by the time its input
+// is.  Per-launch times inside the B=1 Qwen3-8B step on B200 (us, by wk 1/2/4/8): qkv
+// 12.6/9.5/6.0/8.7, o_proj 14.8/9.6/6.0/4.7, down 32.1/24.4/18.8/12.0, LM head 89/96/120/178;
+// gate/up wk 2 20.7, wk 1 25.7 (18.9 only behind a slow o_proj).  The decode-chain kernel
+// takes the same split, so its results equal these launches' bit for bit.
+int m1_default_wk(int N, int K, bool swiglu, int slots) {
+  const int nrt = N / 16, units = K / 256;
+  const int max_wk = swiglu ? 4 : 8;
+  int wk;
+  if (swiglu) {
+    wk = max_wk;
+    for (int c = 1; c <= max_wk; c *= 2) {
+      const int rot = (8 / c) / 2;
+      if ((nrt + rot - 1) / rot >= slots) {
+        wk = c;
+        break;
+      }
+    }
+  } else {
+    wk = 1;
+    for (int c = max_wk; c >= 1; c /= 2)
+      if ((nrt + 8 / c - 1) / (8 / c) <= slots) {
+        wk = c;
+        break;
+      }
+  }
+  if (g_m1_wk > 0) wk = g_m1_wk > max_wk ? max_wk : g_m1_wk;
+  while (wk > 1 && units < wk) wk >>= 1;
+  return wk;
+}
+
+namespace {
 
 template <int EPI, bool NORM, int D>
 cudaError_t m1_launch_d(const QLinArgs& a_in, cudaStream_t st) {
@@ -452,33 +857,11 @@ cudaError_t m1_launch_d(const QLinArgs& a_in, cudaStream_t st) {
   }
   const bool persist = g_m1_persist == 1 || (g_m1_persist == 2 && EPI == EPI_SWIGLU);
   if (g_m1_persist != 1) {
-    // One CTA per group.  Single matrices: the most K splits whose CTAs fit one wave, so
-    // every CTA is resident (and has asked L2 for its whole slice) from the start; wider
-    // outputs take wk = 1.  Gate/up (twice the bytes per row tile): the fewest splits that
-    // fill every slot -- at wk = 1 its 57 MB is not in L2 by the time its input is.
-    // Per-launch times inside the B=1 Qwen3-8B step on B200 (us, by wk 1/2/4/8): qkv
-    // 12.6/9.5/6.0/8.7, o_proj 14.8/9.6/6.0/4.7, down 32.1/24.4/18.8/12.0, LM head
-    // 89/96/120/178; gate/up wk 2 20.7, wk 1 25.7 (18.9 only behind a slow o_proj)
-    if (EPI == EPI_SWIGLU) {
-      wk = max_wk;
-      for (int c = 1; c <= max_wk; c *= 2) {
-        const int rot = (8 / c) / 2;
-        if ((nrt + rot - 1) / rot >= slots) {
-          wk = c;
-          break;
-        }
-      }
-    } else {
-      wk = 1;
-      for (int c = max_wk; c >= 1; c /= 2)
-        if ((nrt + 8 / c - 1) / (8 / c) <= slots) {
-          wk = c;
-          break;
-        }
-    }
+    wk = m1_default_wk(a.N, a.K, EPI == EPI_SWIGLU, slots);  // one CTA per group
+  } else {
+    if (g_m1_wk > 0) wk = g_m1_wk > max_wk ? max_wk : g_m1_wk;
+    while (wk > 1 && units < wk) wk >>= 1;
   }
-  if (g_m1_wk > 0) wk = g_m1_wk > max_wk ? max_wk : g_m1_wk;
-  while (wk > 1 && units < wk) wk >>= 1;
   const int rot = EPI == EPI_SWIGLU ? (8 / wk) / 2 : 8 / wk;
   const int groups = (nrt + rot - 1) / rot;
   const int ctas = (persist && groups > slots) ? slots : groups;
@@ -519,6 +902,49 @@ void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1) {
   if (on >= 0) g_m1_on = on != 0;
   if (wk >= 0) g_m1_wk = (wk == 1 || wk == 2 || wk == 4 || wk == 8) ? wk : 0;
   if (depth >= 0) g_m1_depth = depth == 4 ? 4 : 2;
+}
+
+// ---- decode chain host side ----
+static bool g_chain_on = true;
+static int g_chain_l2_ahead = 1;
+
+void decode_chain_set(int on, int l2_ahead) {
+  if (on >= 0) g_chain_on = on != 0;
+  if (l2_ahead >= 0) g_chain_l2_ahead = l2_ahead != 0;
+}
+
+bool decode_chain_on() { return g_chain_on && g_m1_on; }
+
+bool decode_chain_fits(const ChainPhase& p) {
+  return p.K % 256 == 0 && p.K <= kM1MaxK && p.N % 16 == 0 && p.N > 0 &&
+         (!p.norm_w || p.K <= 8 * kM1Threads * kM1RegChunks) && (!p.swiglu || p.N % 32 == 0);
+}
+
+cudaError_t launch_decode_chain(ChainPhase* ph, int nph, float eps, unsigned* bar, cudaStream_t st) {
+  if (nph < 1 || nph > kChainMaxPhases || !bar) return cudaErrorInvalidValue;
+  ChainArgs a;
+  memset(&a, 0, sizeof(a));
+  const int slots = kM1CtasPerSm * sm_count();
+  size_t smem = 0;
+  for (int i = 0; i < nph; ++i) {
+    if (!decode_chain_fits(ph[i])) return cudaErrorInvalidValue;
+    ph[i].wk = m1_default_wk(ph[i].N, ph[i].K, ph[i].swiglu != 0, slots);
+    a.ph[i] = ph[i];
+    smem = std::max(smem, m1_smem_bytes(ph[i].K));
+  }
+  a.nph = nph;
+  a.eps = eps;
+  a.bar = bar;
+  a.err = device_state(current_device()).tc_err;
+  a.l2_ahead = g_chain_l2_ahead;
+  auto k = chain_kernel<2>;
+  static PerDeviceOnce attr;
+  const cudaError_t e =
+      attr.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024); });
+  if (e != cudaSuccess) return e;
+  // one CTA per resident slot: every CTA of the grid is resident at once, which the
+  // barriers between phases rely on
+  return launch_pdl(k, dim3(slots), dim3(kM1Threads), smem, st, a);
 }
 
 }  // namespace higgs

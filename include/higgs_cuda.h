@@ -115,13 +115,20 @@ int higgs_version(void);
  * kernel (a hint); "gemv_m1_persist" (0, 1, 2; default 0) caps its grid at the
  * resident CTA slots with CTAs looping over row-tile groups (1: every launch, 2:
  * gate/up launches only); "gemv_m1_l1" (0..16, default 0) prefetches that many
- * weight units into L1 ahead of each warp's register ring.
+ * weight units into L1 ahead of each warp's register ring.  "decode_chain" (0/1,
+ * default 1): a one-token decode step on one GPU runs the GEMVs between two
+ * attention launches (o_proj, norm + gate/up, down, norm + the next q|k|v or the
+ * final norm + LM head) as one persistent launch with grid barriers, each phase
+ * the single-token GEMV with the same K split and summation order (the same
+ * bits); "decode_chain_l2_ahead" (0/1, default 1): its CTAs ask L2 for the next
+ * phase's weights while the current phase runs.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
-/* Nonzero when a bounded wait of the tensor-core quantized matmul gave up on
- * the context's device since the last call (the device's flag is then
- * cleared).  Synchronising. */
+/* Nonzero when a bounded wait of the tensor-core quantized matmul or of the
+ * decode-chain kernel's barriers gave up on the context's device since the
+ * last call (the device's flag is then cleared; the results of that call are
+ * undefined).  Synchronising. */
 int higgs_tc_error(higgs_ctx* ctx, int* out);
 
 /* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
@@ -546,7 +553,9 @@ int higgs_model_set_kv_cache_tq4(higgs_model* m, uint8_t* k_codes, void* k_scale
                                  uint8_t* v_codes, void* v_scales, int64_t num_pages,
                                  const int8_t* signs);
 
-/* Bytes of scratch higgs_model_forward needs for (B, Lq, max_seq_len, last_only). */
+/* Bytes of scratch higgs_model_forward needs for (B, Lq, max_seq_len, last_only).
+ * The workspace must be zero-filled before its first use; every forward leaves
+ * its counters (attention splits, decode-chain barriers) zeroed again. */
 size_t higgs_model_workspace_size(const higgs_model* m, int B, int Lq, int max_seq_len,
                                   int last_only);
 

@@ -91,6 +91,9 @@ def greedy_report(ref_tok, ref_lg, gpu_first, forced, gl, free, alt_lg, atol=2e-
     top2 = np.sort(ref_lg, axis=-1)[..., -2:]
     margin = top2[..., 1] - top2[..., 0]  # [steps, B]
     agree = np.concatenate([gpu_first[None], forced.T], 0) == ref_tok.T  # [steps, B]
+    alt_agree = np.argmax(alt_lg, axis=-1) == ref_tok.T  # the reordered oracle on the same stream
+    print(f"forced-argmax disagreements with the oracle: GPU {int((~agree).sum())}, reordered oracle "
+          f"{int((~alt_agree).sum())} (of {agree.size} steps)")
     near = margin <= 2 * noise
     bad = np.argwhere(~agree & ~near)
     print(f"greedy: max rel err {rel:.3e}; "
