@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--quick", action="store_true", help="headline B only, no kernel table (profiling)")
     ap.add_argument("--configs", default="c1,c2,c3,c4,c5",
                     help="other BASELINE configs to run at N=1 (comma list, '' for none)")
+    ap.add_argument("--option", action="append", default=[],
+                    help="library tuning switch name=value (higgs_set_option), repeatable")
     ap.add_argument("--kernel-case", default=None,
                     help="run one small kernel case for ncu: qkv|o_proj|gate_up_swiglu|down|lm_head[:tokens]"
                          "|attention|argmax")
@@ -354,6 +356,52 @@ def gemv_roofline(model, M=1):
                      "gbs": round(nbytes / us / 1e3, 1)})
         del fns
     return rows
+
+
+def chain_roofline(model, reps=10):
+    """The decode-chain kernel as the B=1 step runs it: one launch per layer (o_proj + residual,
+    norm + gate/up SwiGLU, down + residual, norm + the next layer's q|k|v) over that layer's
+    own weights, all layers back to back in one CUDA graph so no launch finds its weights in L2;
+    per-launch time = graph time / layers.  Returns (bytes per launch, us per launch)."""
+    import torch
+
+    from higgs_b200 import ops
+    a = model.args
+    w = model.weights
+    dev = model.device
+    L, H = a.num_hidden_layers, a.hidden_size
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    attn = torch.randn(a.num_attention_heads * a.head_dim, generator=g, device=dev).to(torch.bfloat16)
+    h = torch.randn(H, generator=g, device=dev).to(torch.bfloat16)
+    act = torch.zeros(a.intermediate_size, dtype=torch.bfloat16, device=dev)
+    qkv = torch.zeros((a.num_attention_heads + 2 * a.num_key_value_heads) * a.head_dim,
+                      dtype=torch.bfloat16, device=dev)
+    bars = torch.zeros(4 * L, dtype=torch.int32, device=dev)
+
+    def trip(n):
+        return w[n + ".weight"], w[n + ".scales"], w[n + ".biases"]
+    launches, nbytes = [], 0
+    for li in range(L):
+        p, pn = f"model.layers.{li}.", f"model.layers.{(li + 1) % L}."
+        ph = [ops.chain_gemv(attn, *trip(p + "self_attn.o_proj"), y=h, residual=h),
+              ops.chain_gemv(h, *trip(p + "mlp.gate_proj"), norm_w=w[p + "post_attention_layernorm.weight"],
+                             up=trip(p + "mlp.up_proj"), y=act),
+              ops.chain_gemv(act, *trip(p + "mlp.down_proj"), y=h, residual=h),
+              ops.chain_gemv(h, None, None, None, norm_w=w[pn + "input_layernorm.weight"],
+                             segments=[trip(pn + "self_attn." + n) for n in ("q_proj", "k_proj", "v_proj")],
+                             y=qkv)]
+        launches.append((ph, bars[4 * li:4 * li + 4]))
+        if li == 0:
+            for n in ("self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
+                nbytes += sum(t.numel() * t.element_size() for t in trip(p + n))
+            nbytes += sum(sum(t.numel() * t.element_size() for t in trip(pn + "self_attn." + n))
+                          for n in ("q_proj", "k_proj", "v_proj"))
+            # activations read and written once: attn, h (3 reads, 2 writes), act (w + r), qkv
+            nbytes += attn.numel() * 2 + 5 * H * 2 + 2 * act.numel() * 2 + qkv.numel() * 2
+    fns = [lambda ph=ph, b=b: ops.decode_chain(ph, a.rms_norm_eps, b, dev) for ph, b in launches]
+    us = graph_time(fns, reps) / L * 1e6
+    return int(nbytes), us
 
 
 def kernel_case(opt):
@@ -669,13 +717,22 @@ def config_c3(model, eng, Sequence, device, hbm, steps, ctx):
     torch.cuda.synchronize()
     dt = time.perf_counter() - t0
     toks = sum(len(s.generated) for s in seqs) - n0
+    parts = sd.time_parts()
     for s in seqs:
         eng.release(s)
     del sd
+    # plain greedy decode of the same batch on the same model, for comparison
+    plain = make_seqs(eng, Sequence, B, ctx, model.args.vocab_size, seed=22)
+    ms_plain, _ = time_device_resident(eng, plain, steps, 3)
+    for s in plain:
+        eng.release(s)
     return {"workload": "qwen3-8b self-spec B=4 ctx 2048, draft 9 layers, k=5, T=0.7; e2e",
             "tok_s": round(toks / dt, 1), "ms_per_spec_step": round(dt * 1e3 / steps, 3),
             "accepted_per_step_mean": round(float(acc.mean()), 3),
-            "tokens_per_step_mean": round(float(acc.mean()) + 1.0, 3)}
+            "tokens_per_step_mean": round(float(acc.mean()) + 1.0, 3),
+            "parts_device": parts,
+            "plain_greedy_b4": {"tok_s": round(B * steps / (ms_plain / 1e3), 1),
+                                "ms_per_step": round(ms_plain / steps, 4)}}
 
 
 def config_c4(device, hbm, steps, world=1, rank=0):
@@ -767,6 +824,17 @@ def bench_config(ws: int, B: int, ctx: int) -> dict:
             "l2": "weights 4.26 GB/step > 126 MB L2 (no flush needed)"}
 
 
+def chain_traffic():
+    """DRAM bytes (read + write) of one decode-chain launch from the committed ncu summary
+    (profiles/chain_dram_traffic.json, captured on a reduced-layer model at true widths); null
+    if absent."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "chain_dram_traffic.json")) as f:
+            return int(json.load(f)["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
 def run_ours(opt):
     import torch
 
@@ -833,15 +901,25 @@ def run_ours(opt):
         rows = gemv_roofline(model)
         tot_bytes = sum(r["bytes"] * r["launches_per_step"] for r in rows)
         tot_us = sum(r["us"] * r["launches_per_step"] for r in rows)
-        achieved = tot_bytes / tot_us / 1e3
-        n_launch = sum(r["launches_per_step"] for r in rows)
-        out["roofline"] = {"kernel": "qgemv_m1_kernel (every W4 GEMV launch of one B=1 step; per-launch "
-                                     "averages, byte-weighted over shapes)",
-                           "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
-                           "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                           "algorithmic_bytes": int(tot_bytes / n_launch),
-                           # the committed capture is of one-GPU shapes: no figure for a TP shard
-                           "traffic": ncu_traffic(rows) if ws == 1 else None, "per_shape": rows}
+        gemv_achieved = tot_bytes / tot_us / 1e3
+        gemv = {"kernel": "qgemv_m1_kernel (each W4 GEMV shape as a separate launch; per-launch "
+                          "averages, byte-weighted over shapes)", "achieved": round(gemv_achieved, 1),
+                "frac": round(gemv_achieved / hbm, 4), "per_shape": rows}
+        if ws == 1:
+            cb, cus = chain_roofline(model)
+            achieved = cb / cus / 1e3
+            out["roofline"] = {"kernel": "chain_kernel (one launch per layer: o_proj + gate/up + down + "
+                                         "next q|k|v, 108.6 MB of weights; CUDA events over a graph of "
+                                         "every layer's launch)",
+                               "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                               "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                               "algorithmic_bytes": cb, "us_per_launch": round(cus, 2),
+                               "traffic": chain_traffic(), "gemv_launches": gemv}
+        else:
+            out["roofline"] = dict(gemv, bound="hbm", peak=hbm, peak_kind=peak_kind, unit="GB/s",
+                                   algorithmic_bytes=int(tot_bytes / sum(r["launches_per_step"] for r in rows)),
+                                   # the committed capture is of one-GPU shapes: no figure for a shard
+                                   traffic=None)
         sb = by_batch[str(B)]["step_bytes"]
         out["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": round(sb / (step_ms / 1e3) / 1e9, 1),
                                 "peak": hbm, "frac": by_batch[str(B)]["step_hbm_frac"]}
@@ -918,6 +996,11 @@ def run_reference(opt):
 
 def main():
     opt = parse()
+    if opt.option and opt.impl != "reference":
+        from higgs_b200 import ffi
+        for o in opt.option:
+            name, _, val = o.partition("=")
+            ffi.call("higgs_set_option", name.encode(), int(val))
     if opt.kernel_case:
         kernel_case(opt)
     elif opt.impl == "reference":

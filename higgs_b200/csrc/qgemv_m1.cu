@@ -950,3 +950,50 @@ cudaError_t launch_decode_chain(ChainPhase* ph, int nph, float eps, unsigned* ba
 }  // namespace higgs
 
 HG_TL_FETCH_FN(higgs_timeline_fetch_gemv)
+
+extern "C" int higgs_decode_chain(higgs_ctx* ctx, const higgs_chain_gemv* phases, int n_phases,
+                                  float eps, uint32_t* barriers, void* stream) {
+  using namespace higgs;
+  HG_CHECK_ARG(ctx && phases && barriers, "higgs_decode_chain: null argument");
+  HG_CHECK_ARG(n_phases >= 1 && n_phases <= kChainMaxPhases, "higgs_decode_chain: 1..4 phases");
+  ChainPhase ph[kChainMaxPhases];
+  for (int i = 0; i < n_phases; ++i) {
+    const higgs_chain_gemv& q = phases[i];
+    HG_CHECK_ARG(q.x && q.w[0] && q.s[0] && q.b[0] && (q.y || q.y_f32),
+                 "higgs_decode_chain: phase without input, weights or output");
+    HG_CHECK_ARG(q.nseg >= 1 && q.nseg <= 3, "higgs_decode_chain: nseg must be 1..3");
+    HG_CHECK_ARG(!q.swiglu || (q.w2 && q.s2 && q.b2 && q.y && q.nseg == 1),
+                 "higgs_decode_chain: SwiGLU needs up weights, a bf16 y and one segment");
+    HG_CHECK_ARG(!q.residual || q.y, "higgs_decode_chain: residual needs a bf16 y");
+    ChainPhase& p = ph[i];
+    p = ChainPhase{};
+    p.x = (const uint16_t*)q.x;
+    p.norm_w = (const uint16_t*)q.norm_w;
+    p.K = q.K;
+    p.N = q.N;
+    p.swiglu = q.swiglu != 0;
+    p.nseg = q.nseg;
+    for (int j = 0; j < 3; ++j) {
+      p.seg_end[j] = q.seg_end[j];
+      p.w[j] = q.w[j];
+      p.s[j] = (const uint16_t*)q.s[j];
+      p.b[j] = (const uint16_t*)q.b[j];
+    }
+    if (q.nseg > 1)
+      for (int j = 0; j < q.nseg; ++j)
+        HG_CHECK_ARG(p.w[j] && p.s[j] && p.b[j] && p.seg_end[j] % 16 == 0 &&
+                         (j == 0 ? p.seg_end[0] > 0 : p.seg_end[j] > p.seg_end[j - 1]) &&
+                         (j + 1 < q.nseg || p.seg_end[j] == q.N),
+                     "higgs_decode_chain: bad row segments");
+    p.w2 = q.w2;
+    p.s2 = (const uint16_t*)q.s2;
+    p.b2 = (const uint16_t*)q.b2;
+    p.y = (uint16_t*)q.y;
+    p.y_f32 = q.y_f32;
+    p.residual = (const uint16_t*)q.residual;
+    HG_CHECK_ARG(decode_chain_fits(p), "higgs_decode_chain: shape outside the chain's limits");
+  }
+  HG_DEVICE(ctx);
+  HG_CUDA(launch_decode_chain(ph, n_phases, eps, barriers, (cudaStream_t)stream));
+  return HIGGS_OK;
+}

@@ -367,7 +367,7 @@ class SpecDecoder:
                 self._launch()
         self.launches_per_step = None
 
-    def _launch(self):
+    def _launch(self, parts=("draft", "verify", "accept")):
         import ctypes
 
         from . import ffi
@@ -375,17 +375,46 @@ class SpecDecoder:
         st = torch.cuda.current_stream(m.device).cuda_stream
         ctx = ffi.ctx(m.device.index or 0)
         B, k, V = self.B, self.k, m.args.vocab_size
-        for i in range(k):
-            ffi.call("higgs_model_forward", m.handle, ctypes.byref(self.fa_draft[i]), st)
-            ffi.call("higgs_sample", ctx, self.draft_logits[i].data_ptr(), B, V, self.T,
-                     self.u_draft[i].data_ptr(), self.tok[i + 1].data_ptr(), st)
-        self.vtok.copy_(self.tok.t())
-        self.dtok.copy_(self.tok[1:].t())
-        ffi.call("higgs_model_forward", m.handle, ctypes.byref(self.fa_verify), st)
-        self.draft_bkv.copy_(self.draft_logits.transpose(0, 1))
-        ffi.call("higgs_spec_accept", ctx, self.target_logits.data_ptr(), self.draft_bkv.data_ptr(),
-                 self.dtok.data_ptr(), B, k, V, self.T, self.u_accept.data_ptr(),
-                 self.u_final.data_ptr(), self.accepted.data_ptr(), self.out_tokens.data_ptr(), st)
+        if "draft" in parts:
+            for i in range(k):
+                ffi.call("higgs_model_forward", m.handle, ctypes.byref(self.fa_draft[i]), st)
+                ffi.call("higgs_sample", ctx, self.draft_logits[i].data_ptr(), B, V, self.T,
+                         self.u_draft[i].data_ptr(), self.tok[i + 1].data_ptr(), st)
+        if "verify" in parts:
+            self.vtok.copy_(self.tok.t())
+            self.dtok.copy_(self.tok[1:].t())
+            ffi.call("higgs_model_forward", m.handle, ctypes.byref(self.fa_verify), st)
+        if "accept" in parts:
+            self.draft_bkv.copy_(self.draft_logits.transpose(0, 1))
+            ffi.call("higgs_spec_accept", ctx, self.target_logits.data_ptr(), self.draft_bkv.data_ptr(),
+                     self.dtok.data_ptr(), B, k, V, self.T, self.u_accept.data_ptr(),
+                     self.u_final.data_ptr(), self.accepted.data_ptr(), self.out_tokens.data_ptr(), st)
+
+    def time_parts(self, reps: int = 10) -> dict:
+        """Device milliseconds of one speculative step's parts -- the k draft forwards with
+        their draws, the batched verify forward, the acceptance -- each captured as its own
+        CUDA graph over the currently staged inputs and timed with CUDA events.  (The parts
+        rewrite KV slots past the sequences' lengths, which later steps overwrite anyway.)"""
+        dev = self.engine.model.device
+        out = {}
+        for part in ("draft", "verify", "accept"):
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self._launch((part,))
+            for _ in range(2):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            cur = torch.cuda.current_stream(dev)
+            e0.record(cur)
+            for _ in range(reps):
+                g.replay()
+            e1.record(cur)
+            e1.synchronize()
+            out[part + "_ms"] = round(e0.elapsed_time(e1) / reps, 4)
+            del g
+        return out
 
     def stage(self, seqs: list[Sequence], uniforms: np.ndarray, first: bool):
         """uniforms f32 [2kB + B]: draft draws [k, B], accept tests [B, k], final draws [B]."""

@@ -35,6 +35,7 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_rmsnorm_qlinear_w4g64": (I, [P, P, I, I, P, F, P, P, P, I, P, P, P, P, SZ, P]),
     "higgs_rmsnorm_gate_up_swiglu": (I, [P, P, I, I, P, F, P, P, P, P, P, P, I, P, P, SZ, P]),
     "higgs_rmsnorm": (I, [P, P, P, I, I, P, F, P, P, P]),
+    "higgs_decode_chain": (I, [P, P, I, F, P, P]),
     "higgs_rope": (I, [P, P, I, I, I, P, P, P, P]),
     "higgs_qknorm_rope_kv_write": (I, [P, P, I, I, I, I, P, P, F, P, P, P, P, P, I64, I64, P, P]),
     "higgs_paged_attention_workspace_size": (SZ, [I, I, I, I, I, I]),
@@ -101,6 +102,13 @@ SIGNATURES: dict[str, tuple] = {
                                    ctypes.POINTER(I), ctypes.POINTER(I64)]),
     "higgs_safetensors_read": (I, [P, P, I, I64, I64, I64, I64, P, I, P]),
 }
+
+
+class ChainGemv(ctypes.Structure):
+    """higgs_chain_gemv (include/higgs_cuda.h)."""
+    _fields_ = [("x", P), ("norm_w", P), ("K", I), ("N", I), ("swiglu", I), ("nseg", I),
+                ("seg_end", I * 3), ("w", P * 3), ("s", P * 3), ("b", P * 3), ("w2", P), ("s2", P),
+                ("b2", P), ("y", P), ("y_f32", P), ("residual", P)]
 
 
 class ModelConfig(ctypes.Structure):

@@ -74,6 +74,35 @@ def gate_up_swiglu(x, wg, sg, bg, wu, su, bu):
     return y
 
 
+def chain_gemv(x, w, scales, biases, *, norm_w=None, up=None, segments=None, y=None, y_f32=None,
+               residual=None) -> "ffi.ChainGemv":
+    """One phase of decode_chain: y = quantized_matmul(norm(x), w) at one token.  up = (w2, s2,
+    b2) makes it a SwiGLU phase; segments = [(w, s, b), ...] (q|k|v) replaces w/scales/biases."""
+    c = ffi.ChainGemv()
+    segs = segments or [(w, scales, biases)]
+    c.x, c.norm_w = _p(x), _p(norm_w)
+    c.K = x.shape[-1]
+    c.N = sum(t[0].shape[0] for t in segs)
+    c.swiglu, c.nseg = int(up is not None), len(segs)
+    end = 0
+    for i, (wi, si, bi) in enumerate(segs):
+        end += wi.shape[0]
+        c.seg_end[i] = end
+        c.w[i], c.s[i], c.b[i] = _p(wi), _p(si), _p(bi)
+    if up is not None:
+        c.w2, c.s2, c.b2 = _p(up[0]), _p(up[1]), _p(up[2])
+    c.y, c.y_f32, c.residual = _p(y), _p(y_f32), _p(residual)
+    return c
+
+
+def decode_chain(phases, eps: float, barriers, device):
+    """higgs_decode_chain: the phases (chain_gemv) in one persistent launch; barriers is a zeroed
+    int32 tensor of at least len(phases) entries (left zeroed)."""
+    arr = (ffi.ChainGemv * len(phases))(*phases)
+    ffi.call("higgs_decode_chain", ffi.ctx(torch.device(device).index or 0), arr, len(phases),
+             float(eps), _p(barriers), _st(torch.device(device)))
+
+
 def sk_workspace(M: int, K: int, rows: int, device) -> torch.Tensor:
     n = ffi.load().higgs_qlinear_sk_workspace_size(M, K, rows)
     return torch.zeros(n, dtype=torch.uint8, device=device)

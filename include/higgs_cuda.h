@@ -201,6 +201,44 @@ int higgs_qlinear_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M, int K,
                                  const uint32_t* w_up, const void* s_up, const void* b_up, int N,
                                  void* y, void* stream);
 
+/* One GEMV of a one-token decode chain: y = W x (bf16 x [K]) with optional
+ * fused RMSNorm of x (norm_w), SwiGLU over gate w / up w2 (y = silu(g) * u),
+ * q|k|v-style row segments (nseg <= 3: rows [seg_end[i-1], seg_end[i]) from
+ * w[i]), and outputs bf16 y (optionally + residual) and / or f32 y_f32. */
+typedef struct higgs_chain_gemv {
+  const void* x;
+  const void* norm_w;
+  int K, N, swiglu, nseg;
+  int seg_end[3];
+  const uint32_t* w[3];
+  const void* s[3];
+  const void* b[3];
+  const uint32_t* w2;
+  const void* s2;
+  const void* b2;
+  void* y;
+  float* y_f32;
+  const void* residual;
+} higgs_chain_gemv;
+
+/* The GEMVs of a transformer block after its attention at one token, as one
+ * persistent launch: TransformerBlock::forward's residual adds and post-attention
+ * RMSNorm with Mlp::forward (crates/higgs-models/src/transformer.rs:404-418,
+ * 345-353) -- h += o_proj(attn); act = swiglu(gate(norm(h)), up(norm(h)));
+ * h += down(act); then the next block's norm + q|k|v (or the final norm + LM
+ * head) -- each phase an ops::quantized_matmul (qwen3_next.rs:174-183) with
+ * the single-token GEMV's K split and summation order (the same bits as
+ * separate higgs_qlinear_w4g64 / higgs_rmsnorm_* calls at M = 1), phases
+ * separated by grid barriers.  n_phases <= 4; K <= 32768 (8192 with a fused
+ * norm), multiples of 256; N multiple of 16 (32 with SwiGLU).  barriers:
+ * n_phases u32 counters, zero on entry and left zero.  A phase's input may be
+ * an earlier phase's output.  The launch's CTAs (two per SM) must all be
+ * resident at once, so the GPU must not be running a concurrent kernel that
+ * never finishes; a barrier wait that gives up sets the flag higgs_tc_error
+ * reports. */
+int higgs_decode_chain(higgs_ctx* ctx, const higgs_chain_gemv* phases, int n_phases, float eps,
+                       uint32_t* barriers, void* stream);
+
 /* ---- a3/a4: norms and RoPE ---------------------------------------------- */
 
 /* nn::RmsNorm / fast::rms_norm (crates/higgs-models/src/transformer.rs:375-377,

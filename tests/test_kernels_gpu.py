@@ -757,3 +757,66 @@ def test_qgemm_tc_no_timeouts():
     v = ctypes.c_int(-1)
     ffi.call("higgs_tc_error", ffi.ctx(0), ctypes.byref(v))
     assert v.value == 0
+
+
+# ---- decode chain (one-token GEMVs of a block in one persistent launch) ------------------------
+
+@pytest.mark.parametrize("H,Hd,F,Nq,Nkv", [(4096, 4096, 12288, 4096, 1024), (2048, 2048, 8192, 2048, 512),
+                                           (512, 512, 768, 512, 256)])
+def test_decode_chain_entry_equals_separate_ops(H, Hd, F, Nq, Nkv):
+    """higgs_decode_chain's four phases equal the separate one-token ops bit for bit (same K
+    split, same summation order): h += o_proj(attn); act = swiglu(gate/up(norm(h))); h +=
+    down(act); qkv = q|k|v(norm(h)) as three row segments vs one concatenated matrix."""
+    o = ops()
+    rng = np.random.default_rng(H + F)
+
+    def wq(N, K):
+        q, s, b = orc.w4_quantize(rng.normal(0, 0.02, size=(N, K)).astype(np.float32))
+        return t(q.view(np.int32)), bf(s), bf(b)
+    Wo, Wg, Wu, Wd = wq(H, Hd), wq(F, H), wq(F, H), wq(H, F)
+    Wq, Wk, Wv = wq(Nq, H), wq(Nkv, H), wq(Nkv, H)
+    ln_post = bf(orc.f32_to_bf16(rng.uniform(0.5, 1.5, H)))
+    ln_in = bf(orc.f32_to_bf16(rng.uniform(0.5, 1.5, H)))
+    attn = bf(orc.f32_to_bf16(rng.normal(0, 1, Hd)))
+    h0 = bf(orc.f32_to_bf16(rng.normal(0, 1, H)))
+    eps = 1e-6
+    # separate launches
+    h1 = o.quantized_matmul(attn[None], *Wo, residual=h0[None])
+    act = o.rmsnorm_gate_up_swiglu(h1, ln_post, eps, *Wg, *Wu)
+    h2 = o.quantized_matmul(act, *Wd, residual=h1)
+    cat = tuple(torch.cat([a, b_, c], 0) for a, b_, c in zip(Wq, Wk, Wv))
+    qkv_ref = o.rmsnorm_quantized_matmul(h2, ln_in, eps, *cat)
+    # one chain launch
+    h = h0.clone()
+    act_c = torch.zeros(F, dtype=torch.bfloat16, device=DEV)
+    qkv = torch.zeros(Nq + 2 * Nkv, dtype=torch.bfloat16, device=DEV)
+    bars = torch.zeros(4, dtype=torch.int32, device=DEV)
+    ph = [o.chain_gemv(attn, *Wo, y=h, residual=h),
+          o.chain_gemv(h, *Wg, norm_w=ln_post, up=Wu, y=act_c),
+          o.chain_gemv(act_c, *Wd, y=h, residual=h),
+          o.chain_gemv(h, None, None, None, norm_w=ln_in, segments=[Wq, Wk, Wv], y=qkv)]
+    for rep in range(2):  # twice: the barrier counters are left zeroed for the next launch
+        h.copy_(h0)
+        o.decode_chain(ph, eps, bars, DEV)
+        torch.cuda.synchronize()
+        assert torch.equal(act_c, act[0]), rep
+        assert torch.equal(h, h2[0]), rep
+        assert torch.equal(qkv, qkv_ref[0]), rep
+        assert int(bars.count_nonzero()) == 0
+    # and the last phase against the oracle's vector-form restatement on the same input
+    wcat = (cat[0].cpu().numpy().view(np.uint32), to_np_bf(cat[1]), to_np_bf(cat[2]))
+    ref = orc.qmatmul(orc.rmsnorm(to_np_bf(h2), to_np_bf(ln_in), eps)[0], *wcat)
+    np.testing.assert_allclose(orc.bf16_to_f32(to_np_bf(qkv)), orc.bf16_to_f32(ref[0]), atol=2e-2,
+                               rtol=1e-2)
+
+
+def test_decode_chain_rejects_bad_phases():
+    from higgs_b200 import ffi
+    o = ops()
+    x = torch.zeros(300, dtype=torch.bfloat16, device=DEV)
+    w = torch.zeros(16, 300 // 8, dtype=torch.int32, device=DEV)
+    s = torch.zeros(16, 4, dtype=torch.bfloat16, device=DEV)
+    y = torch.zeros(16, dtype=torch.bfloat16, device=DEV)
+    bars = torch.zeros(4, dtype=torch.int32, device=DEV)
+    with pytest.raises(ffi.HiggsError, match="limits"):
+        o.decode_chain([o.chain_gemv(x, w, s, s, y=y)], 1e-6, bars, DEV)  # K not a multiple of 256

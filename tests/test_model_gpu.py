@@ -3,6 +3,8 @@
 logits within max-abs 2e-2 / rel 1e-2 (bf16 path, f32 logits)
 and greedy token streams identical for the first 64 tokens.
 """
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -321,3 +323,28 @@ def test_model_loaded_from_mlx_checkpoint(tmp_path):
     a = Engine(m, max_seq_len=128).generate_greedy(list(pr), 16, use_prefix=False)
     b = Engine(m2, max_seq_len=128).generate_greedy(list(pr), 16, use_prefix=False)
     assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("model_type,layers", [("qwen3", 3), ("llama", 2)])
+def test_decode_chain_equals_separate_launches(model_type, layers):
+    """The persistent decode chain (one-token steps on one GPU) runs each GEMV with the same K
+    split and summation order as the separate launches, so logits and tokens are identical
+    bit for bit, including the LM head it computes in the last layer's launch."""
+    from higgs_b200 import ffi
+    from higgs_b200.engine import Engine
+    args, w, m, _ = build(model_type, layers=layers)
+    pr = prompts(args, 1, 21, seed=17)
+    outs = []
+    try:
+        for on in (1, 0):
+            ffi.call("higgs_set_option", b"decode_chain", on)
+            eng = Engine(m, max_seq_len=128, keep_logits=True)
+            toks = eng.generate_greedy(list(pr), 24, use_prefix=False)
+            outs.append((toks, np.stack(eng.step_logits)))
+    finally:
+        ffi.call("higgs_set_option", b"decode_chain", 1)
+    assert np.array_equal(outs[0][0], outs[1][0])
+    assert np.array_equal(outs[0][1].view(np.uint32), outs[1][1].view(np.uint32))
+    v = ctypes.c_int(-1)
+    ffi.call("higgs_tc_error", ffi.ctx(0), ctypes.byref(v))
+    assert v.value == 0, "a decode-chain barrier wait gave up"
