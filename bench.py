@@ -377,7 +377,7 @@ def chain_roofline(model, reps=10):
     act = torch.zeros(a.intermediate_size, dtype=torch.bfloat16, device=dev)
     qkv = torch.zeros((a.num_attention_heads + 2 * a.num_key_value_heads) * a.head_dim,
                       dtype=torch.bfloat16, device=dev)
-    bars = torch.zeros(4 * L, dtype=torch.int32, device=dev)
+    bars = torch.zeros(4 * 64 * L, dtype=torch.int32, device=dev)
 
     def trip(n):
         return w[n + ".weight"], w[n + ".scales"], w[n + ".biases"]
@@ -391,7 +391,7 @@ def chain_roofline(model, reps=10):
               ops.chain_gemv(h, None, None, None, norm_w=w[pn + "input_layernorm.weight"],
                              segments=[trip(pn + "self_attn." + n) for n in ("q_proj", "k_proj", "v_proj")],
                              y=qkv)]
-        launches.append((ph, bars[4 * li:4 * li + 4]))
+        launches.append((ph, bars[256 * li:256 * li + 256]))
         if li == 0:
             for n in ("self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
                 nbytes += sum(t.numel() * t.element_size() for t in trip(p + n))

@@ -117,6 +117,7 @@ cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st);
 // fused RMSNorm of x, SwiGLU over gate (w) / up (w2), q|k|v row segments and a residual
 // epilogue; wk (the K split) is filled in by launch_decode_chain.
 constexpr int kChainMaxPhases = 4;
+constexpr int kChainBarWords = 64;  // u32 barrier words per phase
 struct ChainPhase {
   const uint16_t* x;       // input [K] (bf16), written before the launch or by an earlier phase
   const uint16_t* norm_w;  // fused RMSNorm of x (null: none)
@@ -137,8 +138,8 @@ struct ChainPhase {
 // (higgs_set_option("decode_chain")) and whether a phase fits it.
 bool decode_chain_on();
 bool decode_chain_fits(const ChainPhase& p);
-// nph (<= kChainMaxPhases) phases in one launch; bar: nph zeroed u32 counters this launch
-// leaves zeroed again.  Bounded waits report through the per-device timeout flag.
+// nph (<= kChainMaxPhases) phases in one launch; bar: nph * kChainBarWords zeroed u32 words
+// this launch leaves zeroed again.  Bounded waits report through the per-device timeout flag.
 cudaError_t launch_decode_chain(ChainPhase* ph, int nph, float eps, unsigned* bar, cudaStream_t st);
 void decode_chain_set(int on, int l2_ahead);
 void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);  // -1 leaves a setting as it is

@@ -138,7 +138,7 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
     L.moe_y = take(P * (size_t)c.hidden * 2);
   }
   // decode-chain barrier counters, kChainMaxPhases per layer (zero between launches)
-  L.chain_bar = take((size_t)c.layers * kChainMaxPhases * 4);
+  L.chain_bar = take((size_t)c.layers * kChainMaxPhases * kChainBarWords * 4);
   const size_t aws = higgs_paged_attention_workspace_size(B, Lq, c.heads, c.kv_heads, D, max_seq_len);
   L.attn_ws = take(aws);
   L.total = off;
@@ -448,7 +448,8 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
           head_done = true;
         }
       }
-      HG_CUDA(launch_decode_chain(ph, n, c.rms_eps, chain_bar + (size_t)li * kChainMaxPhases, st));
+      HG_CUDA(launch_decode_chain(ph, n, c.rms_eps,
+                                  chain_bar + (size_t)li * kChainMaxPhases * kChainBarWords, st));
       continue;
     }
     // h = h + o_proj(attn)   (in place: each element read then written by one thread)

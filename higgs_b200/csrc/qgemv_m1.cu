@@ -423,38 +423,63 @@ struct ChainArgs {
   ChainPhase ph[kChainMaxPhases];
   int nph;
   float eps;
-  unsigned* bar;  // nph arrival counters: zero at launch, zeroed again by the last CTA out
+  unsigned* bar;  // kChainBarWords per phase, zero at launch and zeroed again by the launch
   int* err;       // set when a barrier wait gives up
   int l2_ahead;   // 1: a phase's L2 requests are issued while the previous phase runs
 };
+
+// Barrier of one phase, 64 words: arrival counters of CTA groups (kChainGroup CTAs each), the
+// count of finished groups, and the release flag the waiting CTAs poll (its own 128 bytes,
+// apart from the counters the arrivals update).  The last CTA of a group adds its group to
+// the top count; the last group raises the release flag.  Counters are reset by the CTAs that
+// finish them; release flags by the last CTA of the launch.
+constexpr int kChainGroup = 16;
+constexpr int kChainTop = 32;      // word of the finished-group count
+constexpr int kChainRelease = 48;  // word of the release flag
 
 __device__ __forceinline__ unsigned chain_ld_acquire(const unsigned* p) {
   unsigned v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-
-// Arrival of this CTA at counter c (after every thread's writes of the phase).
-__device__ __forceinline__ unsigned chain_arrive(unsigned* c) {
-  __syncthreads();
-  unsigned old = 0;
-  if (threadIdx.x == 0) {
-    __threadfence();
-    old = atomicAdd(c, 1u);
-  }
-  return old;
+__device__ __forceinline__ void chain_st_release(unsigned* p, unsigned v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Wait until every CTA has arrived at c; gives up (and sets *err) after ~2^24 polls.
-__device__ __forceinline__ void chain_wait(const unsigned* c, unsigned n, int* err) {
+// This CTA's arrival at barrier b (after every thread's writes of the phase); true in thread
+// 0 of the CTA that completed the barrier.
+__device__ __forceinline__ bool chain_arrive(unsigned* b) {
+  __syncthreads();
+  bool last = false;
+  if (threadIdx.x == 0) {
+    const unsigned nct = gridDim.x;
+    const unsigned gi = blockIdx.x / kChainGroup;
+    const unsigned ng = (nct + kChainGroup - 1) / kChainGroup;
+    const unsigned gsize = min((unsigned)kChainGroup, nct - gi * kChainGroup);
+    __threadfence();
+    if (atomicAdd(b + gi, 1u) == gsize - 1) {
+      b[gi] = 0u;  // every CTA of the group has arrived
+      __threadfence();
+      if (atomicAdd(b + kChainTop, 1u) == ng - 1) {
+        b[kChainTop] = 0u;
+        chain_st_release(b + kChainRelease, 1u);
+        last = true;
+      }
+    }
+  }
+  return last;
+}
+
+// Wait for barrier b's release; gives up (and sets *err) after ~2^24 polls.
+__device__ __forceinline__ void chain_wait(const unsigned* b, int* err) {
   if (threadIdx.x == 0) {
     unsigned it = 0;
-    while (chain_ld_acquire(c) < n) {
+    while (chain_ld_acquire(b + kChainRelease) == 0u) {
       if (++it > (1u << 24)) {
         if (err) atomicExch(err, 1);
         break;
       }
-      __nanosleep(32);
+      __nanosleep(20);
     }
   }
   __syncthreads();
@@ -568,8 +593,6 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) chain_kernel(const _
   if (a.l2_ahead && a.nph > 1) l2_slice(a.ph[1]);
   bind(a.ph[0], tile_of(a.ph[0], blockIdx.x));
   prologue();
-  const unsigned nct = gridDim.x;
-
 #pragma unroll 1
   for (int p = 0; p < a.nph; ++p) {
     const ChainPhase& P = a.ph[p];
@@ -588,7 +611,7 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) chain_kernel(const _
       pdl_wait();
       pdl_launch();
     } else {
-      chain_wait(a.bar + (p - 1), nct, a.err);
+      chain_wait(a.bar + (p - 1) * kChainBarWords, a.err);
     }
     uint8_t* xf = smem;
     uint8_t* zero = smem + m1_xf_bytes(K) + 64;
@@ -761,10 +784,10 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) chain_kernel(const _
       bind(Q, tile_of(Q, blockIdx.x));
       prologue();
     }
-    const unsigned old = chain_arrive(a.bar + p);
-    if (p + 1 == a.nph && threadIdx.x == 0 && old == nct - 1) {
+    const bool last = chain_arrive(a.bar + p * kChainBarWords);
+    if (p + 1 == a.nph && last) {
       // the last CTA out: every other CTA has passed every wait of this launch
-      for (int i = 0; i < a.nph; ++i) a.bar[i] = 0u;
+      for (int i = 0; i < a.nph; ++i) a.bar[i * kChainBarWords + kChainRelease] = 0u;
       __threadfence();
     }
   }
@@ -905,7 +928,11 @@ void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1) {
 }
 
 // ---- decode chain host side ----
-static bool g_chain_on = true;
+// Off by default: measured on B200 inside the B=1 Qwen3-8B step it is slower than the
+// separate launches (2.64 ms with one arrival counter per phase, 2.84 ms with grouped
+// counters and a release flag, vs 2.14 ms): a grid barrier costs more than a kernel
+// boundary with programmatic dependent launch.
+static bool g_chain_on = false;
 static int g_chain_l2_ahead = 1;
 
 void decode_chain_set(int on, int l2_ahead) {

@@ -97,7 +97,7 @@ def chain_gemv(x, w, scales, biases, *, norm_w=None, up=None, segments=None, y=N
 
 def decode_chain(phases, eps: float, barriers, device):
     """higgs_decode_chain: the phases (chain_gemv) in one persistent launch; barriers is a zeroed
-    int32 tensor of at least len(phases) entries (left zeroed)."""
+    int32 tensor of at least 64 * len(phases) entries (left zeroed)."""
     arr = (ffi.ChainGemv * len(phases))(*phases)
     ffi.call("higgs_decode_chain", ffi.ctx(torch.device(device).index or 0), arr, len(phases),
              float(eps), _p(barriers), _st(torch.device(device)))

@@ -116,7 +116,7 @@ int higgs_version(void);
  * resident CTA slots with CTAs looping over row-tile groups (1: every launch, 2:
  * gate/up launches only); "gemv_m1_l1" (0..16, default 0) prefetches that many
  * weight units into L1 ahead of each warp's register ring.  "decode_chain" (0/1,
- * default 1): a one-token decode step on one GPU runs the GEMVs between two
+ * default 0): a one-token decode step on one GPU runs the GEMVs between two
  * attention launches (o_proj, norm + gate/up, down, norm + the next q|k|v or the
  * final norm + LM head) as one persistent launch with grid barriers, each phase
  * the single-token GEMV with the same K split and summation order (the same
@@ -231,7 +231,7 @@ typedef struct higgs_chain_gemv {
  * separate higgs_qlinear_w4g64 / higgs_rmsnorm_* calls at M = 1), phases
  * separated by grid barriers.  n_phases <= 4; K <= 32768 (8192 with a fused
  * norm), multiples of 256; N multiple of 16 (32 with SwiGLU).  barriers:
- * n_phases u32 counters, zero on entry and left zero.  A phase's input may be
+ * 64 * n_phases u32 words, zero on entry and left zero.  A phase's input may be
  * an earlier phase's output.  The launch's CTAs (two per SM) must all be
  * resident at once, so the GPU must not be running a concurrent kernel that
  * never finishes; a barrier wait that gives up sets the flag higgs_tc_error

@@ -790,7 +790,7 @@ def test_decode_chain_entry_equals_separate_ops(H, Hd, F, Nq, Nkv):
     h = h0.clone()
     act_c = torch.zeros(F, dtype=torch.bfloat16, device=DEV)
     qkv = torch.zeros(Nq + 2 * Nkv, dtype=torch.bfloat16, device=DEV)
-    bars = torch.zeros(4, dtype=torch.int32, device=DEV)
+    bars = torch.zeros(4 * 64, dtype=torch.int32, device=DEV)
     ph = [o.chain_gemv(attn, *Wo, y=h, residual=h),
           o.chain_gemv(h, *Wg, norm_w=ln_post, up=Wu, y=act_c),
           o.chain_gemv(act_c, *Wd, y=h, residual=h),
@@ -817,6 +817,6 @@ def test_decode_chain_rejects_bad_phases():
     w = torch.zeros(16, 300 // 8, dtype=torch.int32, device=DEV)
     s = torch.zeros(16, 4, dtype=torch.bfloat16, device=DEV)
     y = torch.zeros(16, dtype=torch.bfloat16, device=DEV)
-    bars = torch.zeros(4, dtype=torch.int32, device=DEV)
+    bars = torch.zeros(4 * 64, dtype=torch.int32, device=DEV)
     with pytest.raises(ffi.HiggsError, match="limits"):
         o.decode_chain([o.chain_gemv(x, w, s, s, y=y)], 1e-6, bars, DEV)  # K not a multiple of 256

@@ -342,7 +342,7 @@ def test_decode_chain_equals_separate_launches(model_type, layers):
             toks = eng.generate_greedy(list(pr), 24, use_prefix=False)
             outs.append((toks, np.stack(eng.step_logits)))
     finally:
-        ffi.call("higgs_set_option", b"decode_chain", 1)
+        ffi.call("higgs_set_option", b"decode_chain", 0)
     assert np.array_equal(outs[0][0], outs[1][0])
     assert np.array_equal(outs[0][1].view(np.uint32), outs[1][1].view(np.uint32))
     v = ctypes.c_int(-1)
