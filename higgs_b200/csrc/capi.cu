@@ -57,6 +57,7 @@ void qgemv_set_wk(int wk);
 void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);
 void qgemm_tc_prepare();
 void decode_chain_set(int on, int l2_ahead);
+void qgemv_tma_set(int on);
 
 }  // namespace higgs
 
@@ -91,6 +92,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
+    return HIGGS_OK;
+  }
+  if (n == "gemv_tma") {
+    qgemv_tma_set(value != 0);
     return HIGGS_OK;
   }
   if (n == "decode_chain") {

@@ -112,6 +112,10 @@ int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int H
 // M == 1 (decode at batch 1): the register-fed GEMV of qgemv_m1.cu; launch_qgemv_ring routes there itself.
 bool qgemv_m1_supported(const QLinArgs& a);
 cudaError_t launch_qgemv_m1(const QLinArgs& a, int epi, cudaStream_t st);
+// one token, weights streamed by TMA into a shared-memory ring (qgemv_tma.cu)
+bool qgemv_tma_supported(const QLinArgs& a);
+cudaError_t launch_qgemv_tma(const QLinArgs& a, int epi, cudaStream_t st);
+void qgemv_tma_set(int on);
 
 // One GEMV phase of a decode chain (qgemv_m1.cu): y = W x for one token, with an optional
 // fused RMSNorm of x, SwiGLU over gate (w) / up (w2), q|k|v row segments and a residual

@@ -404,6 +404,10 @@ extern "C" int higgs_rmsnorm_qlinear_w4g64(higgs_ctx* ctx, const void* x, int M,
     q.residual = (const uint16_t*)residual;
     q.norm_w = (const uint16_t*)norm_w;
     q.eps = eps;
+    if (qgemv_tma_supported(q)) {
+      HG_CUDA(launch_qgemv_tma(q, EPI_STORE, (cudaStream_t)stream));
+      return HIGGS_OK;
+    }
     if (qgemv_m1_supported(q)) {
       HG_CUDA(launch_qgemv_m1(q, EPI_STORE, (cudaStream_t)stream));
       return HIGGS_OK;
@@ -476,6 +480,10 @@ extern "C" int higgs_rmsnorm_gate_up_swiglu(higgs_ctx* ctx, const void* x, int M
     q.y = (uint16_t*)y;
     q.norm_w = (const uint16_t*)norm_w;
     q.eps = eps;
+    if (qgemv_tma_supported(q)) {
+      HG_CUDA(launch_qgemv_tma(q, EPI_SWIGLU, (cudaStream_t)stream));
+      return HIGGS_OK;
+    }
     if (qgemv_m1_supported(q)) {
       HG_CUDA(launch_qgemv_m1(q, EPI_SWIGLU, (cudaStream_t)stream));
       return HIGGS_OK;
