@@ -22,6 +22,8 @@
 //    expanded to exact bf16 (c - 8) in shared memory with the per-token scale
 //    folded into P, and the merged output is rotated back with the inverse
 //    Hadamard transform.
+#include <cooperative_groups.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -121,7 +123,7 @@ __device__ __forceinline__ void row_stats_update(float (&m)[2], float (&l)[2], f
 // split partial plus the last-CTA merge.  o_sm rows are in "physical" d order;
 // `finish` converts a merged f32 row to the bf16 output (TurboQuant rotates
 // back there).
-template <int D, int MT, typename Finish>
+template <int D, int MT, typename Finish, bool CL = false>
 __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][2],
                                               float (&l)[MT][2], float (&o)[MT][D / 8][4],
                                               float* smem_f, int b, int h, int split, int R,
@@ -177,6 +179,37 @@ __device__ __forceinline__ void attn_epilogue(const AttnArgs& a, float (&m)[MT][
   if (a.splits == 1) {
     finish(sm_o, R, b, h);
     HG_TL_END(3001);
+    return;
+  }
+  if constexpr (CL) {
+    // The splits of this (sequence, kv head) are one thread-block cluster: every CTA merges
+    // a slice of d for every row, reading the splits' normalised partials and log-sum-exps
+    // straight from their shared memory (no workspace round trip, no arrival counter).  The
+    // fold is the one below -- running maximum, weights exp2(lse - M), splits in order.
+    namespace cg = cooperative_groups;
+    cg::cluster_group cl = cg::this_cluster();
+    cl.sync();
+    const int S = (int)cl.num_blocks(), rk = (int)cl.block_rank();
+    const int dper = (D + S - 1) / S, d0 = rk * dper, d1 = min(D, d0 + dper), nd = max(0, d1 - d0);
+    const int G = a.Hq / a.Hkv;
+    for (int i = threadIdx.x; i < R * nd; i += kAttnThreads) {
+      const int row = i / nd, d = d0 + i % nd;
+      float M = -INFINITY;
+      for (int s = 0; s < S; ++s) M = fmaxf(M, cl.map_shared_rank(sm_lse, s)[row]);
+      float W = 0.0f, acc = 0.0f;
+      if (M != -INFINITY) {
+        for (int s = 0; s < S; ++s) {
+          const float ls = cl.map_shared_rank(sm_lse, s)[row];
+          const float w = (ls == -INFINITY) ? 0.0f : exp2f(ls - M);
+          W += w;
+          acc = fmaf(w, cl.map_shared_rank(sm_o, s)[row * D + d], acc);
+        }
+      }
+      const int tq = a.tq0 + row / G, hq = h * G + row % G;
+      a.out[(((size_t)b * a.Lq + tq) * a.Hq + hq) * D + d] = f2bf(W > 0.0f ? acc * (1.0f / W) : 0.0f);
+    }
+    cl.sync();  // the partials stay in shared memory until every CTA has read them
+    HG_TL_END(3004);
     return;
   }
   // write the split partial (valid rows only)
@@ -503,7 +536,7 @@ __device__ __forceinline__ void fa_store_gmem(uint16_t* dst, int lane, const flo
   }
 }
 
-template <int D, int MT, int S>
+template <int D, int MT, int S, bool CL = false>
 __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs a) {
   constexpr int RP = 16 * MT;
   constexpr int PAGE_ELEMS = 16 * D;
@@ -695,7 +728,7 @@ __global__ void __launch_bounds__(kAttnThreads) fused_attn_bf16_kernel(AttnArgs 
   ao.tq0 = 0;
   FinishBf16<D> fin{&ao};
   HG_TL_MARK(5);
-  attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
+  attn_epilogue<D, MT, FinishBf16<D>, CL>(a, m, l, o, smem_f, b, h, split, R, fin);
 }
 
 // ---------------------------------------------------------------------------
@@ -1153,6 +1186,11 @@ constexpr int kFusedStages = 3;
 // higgs_set_option("attn_min_pages", n), n >= 4; the workspace is sized for 4)
 static int g_fused_min_pages = 8;
 void attention_set_min_pages(int n) { g_fused_min_pages = n < 4 ? 4 : (n > 4096 ? 4096 : n); }
+// largest thread-block cluster the fused kernel's splits may form (0 = no clusters): the splits
+// of a (sequence, kv head) then merge through distributed shared memory instead of the
+// workspace and an arrival counter, at up to twice the pages per split
+static int g_attn_cluster = 16;
+void attention_set_cluster(int n) { g_attn_cluster = n >= 16 ? 16 : (n >= 8 ? 8 : (n >= 2 ? n : 0)); }
 
 static size_t smem_fused(int D, int MT, int Lq) {
   const size_t q = (size_t)16 * MT * D * 2;
@@ -1180,6 +1218,15 @@ static cudaError_t attention_prepare_device() {
   set(fused_attn_bf16_kernel<64, 2, kFusedStages>, smem_fused(64, 2, 32));
   set(fused_attn_bf16_kernel<128, 1, kFusedStages>, smem_fused(128, 1, 32));
   set(fused_attn_bf16_kernel<128, 2, kFusedStages>, smem_fused(128, 2, 32));
+  auto setc = [&](void (*k)(AttnArgs), size_t smem) {
+    set(k, smem);
+    const cudaError_t r = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (r != cudaSuccess) e = r;
+  };
+  setc(fused_attn_bf16_kernel<64, 1, kFusedStages, true>, smem_fused(64, 1, 32));
+  setc(fused_attn_bf16_kernel<64, 2, kFusedStages, true>, smem_fused(64, 2, 32));
+  setc(fused_attn_bf16_kernel<128, 1, kFusedStages, true>, smem_fused(128, 1, 32));
+  setc(fused_attn_bf16_kernel<128, 2, kFusedStages, true>, smem_fused(128, 2, 32));
   return e;
 }
 
@@ -1353,10 +1400,24 @@ int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int H
   HG_CHECK_ARG(Hkv > 0 && Hq % Hkv == 0 && (Hq / Hkv) * Lq <= 32,
                "higgs_fused_attention: needs (Hq / Hkv) * Lq <= 32");
   HG_DEVICE(ctx);
-  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len, g_fused_min_pages);
+  SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len, g_fused_min_pages);
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
                          attn_ws_bytes(p, B, Hkv, D), workspace);
   if (rc) return rc;
+  // cluster merge: the split count rounded up to a power of two (at most g_attn_cluster), the
+  // pages spread over it, as long as a split gets at most twice the planned pages
+  int cluster = 0;
+  if (g_attn_cluster >= 2 && p.splits > 1) {
+    int c = 2;
+    while (c < p.splits && c < g_attn_cluster) c *= 2;
+    const int max_pages = (max_seq_len + 15) / 16;
+    const int pps = (max_pages + c - 1) / c;
+    if (pps <= 2 * p.pps) {
+      p.splits = c;
+      p.pps = pps;
+      cluster = c;
+    }
+  }
   AttnArgs a = {};
   a.B = B;
   a.Lq = Lq;
@@ -1392,13 +1453,22 @@ int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int H
   const size_t smem = smem_fused(D, MT, Lq);
   cudaStream_t st = (cudaStream_t)stream;
   const dim3 grid(p.splits, Hkv, B);
+  const dim3 blk(kAttnThreads);
   cudaError_t e;
-  if (D == 64)
-    e = MT == 1 ? launch_pdl(fused_attn_bf16_kernel<64, 1, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a)
-                : launch_pdl(fused_attn_bf16_kernel<64, 2, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a);
-  else
-    e = MT == 1 ? launch_pdl(fused_attn_bf16_kernel<128, 1, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a)
-                : launch_pdl(fused_attn_bf16_kernel<128, 2, kFusedStages>, grid, dim3(kAttnThreads), smem, st, a);
+  if (cluster) {
+    if (D == 64)
+      e = MT == 1 ? launch_pdl_cluster(fused_attn_bf16_kernel<64, 1, kFusedStages, true>, grid, blk, smem, st, cluster, a)
+                  : launch_pdl_cluster(fused_attn_bf16_kernel<64, 2, kFusedStages, true>, grid, blk, smem, st, cluster, a);
+    else
+      e = MT == 1 ? launch_pdl_cluster(fused_attn_bf16_kernel<128, 1, kFusedStages, true>, grid, blk, smem, st, cluster, a)
+                  : launch_pdl_cluster(fused_attn_bf16_kernel<128, 2, kFusedStages, true>, grid, blk, smem, st, cluster, a);
+  } else if (D == 64) {
+    e = MT == 1 ? launch_pdl(fused_attn_bf16_kernel<64, 1, kFusedStages>, grid, blk, smem, st, a)
+                : launch_pdl(fused_attn_bf16_kernel<64, 2, kFusedStages>, grid, blk, smem, st, a);
+  } else {
+    e = MT == 1 ? launch_pdl(fused_attn_bf16_kernel<128, 1, kFusedStages>, grid, blk, smem, st, a)
+                : launch_pdl(fused_attn_bf16_kernel<128, 2, kFusedStages>, grid, blk, smem, st, a);
+  }
   HG_CUDA(e);
   return HIGGS_OK;
 }

@@ -58,6 +58,7 @@ void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);
 void qgemm_tc_prepare();
 void decode_chain_set(int on, int l2_ahead);
 void qgemv_tma_set(int on);
+void attention_set_cluster(int n);
 
 }  // namespace higgs
 
@@ -92,6 +93,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
+    return HIGGS_OK;
+  }
+  if (n == "attn_cluster") {
+    attention_set_cluster(value);
     return HIGGS_OK;
   }
   if (n == "gemv_tma") {

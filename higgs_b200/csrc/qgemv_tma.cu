@@ -431,7 +431,11 @@ bool tw_map(const void* base, int rows, int cols, int elem, int box_cols, CUtens
   return true;
 }
 
-bool g_tw_on = true;
+// Off by default: measured on B200 it streams no faster than the register-fed kernel -- LM head
+// (350 MB) 97.6 vs 88.8 us, gate/up 19.4 vs 18.4 us inside a graph of back-to-back launches,
+// B=1 Qwen3-8B step 2.31 vs 2.14 ms; ncu shows both at 42-47 % DRAM throughput with the same
+// long-scoreboard-dominated stalls (~4.5 cycles per issued instruction) at ~36 % issue.
+bool g_tw_on = false;
 
 // K split for the persistent grid: the smallest per-CTA load, groups x (pairs per warp + 1
 // for the group's reduction), among splits whose per-warp ranges hold whole unit pairs.

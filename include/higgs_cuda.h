@@ -119,9 +119,12 @@ int higgs_version(void);
  * default 0): a one-token decode step on one GPU runs the GEMVs between two
  * attention launches (o_proj, norm + gate/up, down, norm + the next q|k|v or the
  * final norm + LM head) as one persistent launch with grid barriers, each phase
- * the single-token GEMV with the same K split and summation order (the same
- * bits); "decode_chain_l2_ahead" (0/1, default 1): its CTAs ask L2 for the next
- * phase's weights while the current phase runs.
+ * the register-fed single-token GEMV with its K split and summation order (the
+ * same bits as that GEMV); "decode_chain_l2_ahead" (0/1, default 1): its CTAs ask
+ * L2 for the next phase's weights while the current phase runs.  "gemv_tma" (0/1,
+ * default 0): one-token linears (K a multiple of 512, up to 12288) stream their
+ * weights by TMA into a shared-memory ring instead of loading them into
+ * registers.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
@@ -227,8 +230,9 @@ typedef struct higgs_chain_gemv {
  * 345-353) -- h += o_proj(attn); act = swiglu(gate(norm(h)), up(norm(h)));
  * h += down(act); then the next block's norm + q|k|v (or the final norm + LM
  * head) -- each phase an ops::quantized_matmul (qwen3_next.rs:174-183) with
- * the single-token GEMV's K split and summation order (the same bits as
- * separate higgs_qlinear_w4g64 / higgs_rmsnorm_* calls at M = 1), phases
+ * the register-fed single-token GEMV's K split and summation order (the same
+ * bits as separate higgs_qlinear_w4g64 / higgs_rmsnorm_* calls at M = 1 with
+ * the "gemv_tma" option off), phases
  * separated by grid barriers.  n_phases <= 4; K <= 32768 (8192 with a fused
  * norm), multiples of 256; N multiple of 16 (32 with SwiGLU).  barriers:
  * 64 * n_phases u32 words, zero on entry and left zero.  A phase's input may be

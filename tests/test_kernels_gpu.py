@@ -764,9 +764,14 @@ def test_qgemm_tc_no_timeouts():
 @pytest.mark.parametrize("H,Hd,F,Nq,Nkv", [(4096, 4096, 12288, 4096, 1024), (2048, 2048, 8192, 2048, 512),
                                            (512, 512, 768, 512, 256)])
 def test_decode_chain_entry_equals_separate_ops(H, Hd, F, Nq, Nkv):
-    """higgs_decode_chain's four phases equal the separate one-token ops bit for bit (same K
-    split, same summation order): h += o_proj(attn); act = swiglu(gate/up(norm(h))); h +=
-    down(act); qkv = q|k|v(norm(h)) as three row segments vs one concatenated matrix."""
+    """higgs_decode_chain's four phases equal the separate one-token ops on the register-fed
+    single-token GEMV (gemv_tma off) bit for bit -- same K split, same summation order: h +=
+    o_proj(attn); act = swiglu(gate/up(norm(h))); h += down(act); qkv = q|k|v(norm(h)) as three
+    row segments vs one concatenated matrix."""
+    _decode_chain_vs_ops(H, Hd, F, Nq, Nkv)
+
+
+def _decode_chain_vs_ops(H, Hd, F, Nq, Nkv):
     o = ops()
     rng = np.random.default_rng(H + F)
 
@@ -820,3 +825,47 @@ def test_decode_chain_rejects_bad_phases():
     bars = torch.zeros(4 * 64, dtype=torch.int32, device=DEV)
     with pytest.raises(ffi.HiggsError, match="limits"):
         o.decode_chain([o.chain_gemv(x, w, s, s, y=y)], 1e-6, bars, DEV)  # K not a multiple of 256
+
+
+@pytest.mark.parametrize("M_shape", [(4096, 4096, False, None), (4096, 12288, False, None),
+                                     (12288, 4096, True, None), (151936, 4096, False, None),
+                                     (2048, 2048, False, None), (6144, 4096, False, (4096, 1024, 1024))])
+def test_qgemv_tma_vs_oracle(M_shape):
+    """The TMA-fed single-token GEMV (option gemv_tma, off by default) against the oracle's
+    vector form: plain, SwiGLU, fused RMSNorm, q|k|v row segments, the LM head's width."""
+    from higgs_b200 import ffi
+    o = ops()
+    N, K, swiglu, segs = M_shape
+    rng = np.random.default_rng(N + K)
+
+    def wq(n):
+        q, s, b = orc.w4_quantize(rng.normal(0, 0.02, size=(n, K)).astype(np.float32))
+        return q, s, b
+    x = orc.f32_to_bf16(rng.normal(0, 1, size=(1, K)))
+    nw = orc.f32_to_bf16(rng.uniform(0.5, 1.5, K))
+    ffi.call("higgs_set_option", b"gemv_tma", 1)
+    try:
+        if swiglu:
+            g_, u_ = wq(N), wq(N)
+            got = o.gate_up_swiglu(bf(x), t(g_[0].view(np.int32)), bf(g_[1]), bf(g_[2]),
+                                   t(u_[0].view(np.int32)), bf(u_[1]), bf(u_[2]))
+            ref = orc.silu_mul(orc.qmatmul(x, *g_), orc.qmatmul(x, *u_))
+            np.testing.assert_allclose(orc.bf16_to_f32(to_np_bf(got)), orc.bf16_to_f32(ref), atol=2e-2, rtol=1e-2)
+        elif segs:
+            parts = [wq(n) for n in segs]
+            cat = [np.concatenate([p_[i] for p_ in parts]) for i in range(3)]
+            got = o.rmsnorm_quantized_matmul(bf(x), bf(nw), 1e-6, t(cat[0].view(np.int32)), bf(cat[1]),
+                                             bf(cat[2]), out_f32=True)
+            xn = orc.rmsnorm(x, nw, 1e-6)[0]
+            ref = orc.qmatmul(xn, *cat, want_f32=True)[1]
+            np.testing.assert_allclose(got.cpu().numpy(), ref, rtol=1e-3, atol=1e-4 * np.abs(ref).max())
+        else:
+            q, s, b = wq(N)
+            got = o.quantized_matmul(bf(x), t(q.view(np.int32)), bf(s), bf(b), out_f32=True)
+            ref = orc.qmatmul(x, q, s, b, want_f32=True)[1]
+            np.testing.assert_allclose(got.cpu().numpy(), ref, rtol=1e-3, atol=1e-4 * np.abs(ref).max())
+        v = ctypes.c_int(-1)
+        ffi.call("higgs_tc_error", ffi.ctx(0), ctypes.byref(v))
+        assert v.value == 0
+    finally:
+        ffi.call("higgs_set_option", b"gemv_tma", 0)
