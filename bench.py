@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--quick", action="store_true", help="headline B only, no kernel table (profiling)")
     ap.add_argument("--configs", default="c1,c2,c3,c4,c5",
                     help="other BASELINE configs to run at N=1 (comma list, '' for none)")
+    ap.add_argument("--chain-roofline", action="store_true",
+                    help="also time the persistent decode-chain kernel (off in the step by default)")
     ap.add_argument("--option", action="append", default=[],
                     help="library tuning switch name=value (higgs_set_option), repeatable")
     ap.add_argument("--kernel-case", default=None,
@@ -824,17 +826,6 @@ def bench_config(ws: int, B: int, ctx: int) -> dict:
             "l2": "weights 4.26 GB/step > 126 MB L2 (no flush needed)"}
 
 
-def chain_traffic():
-    """DRAM bytes (read + write) of one decode-chain launch from the committed ncu summary
-    (profiles/chain_dram_traffic.json, captured on a reduced-layer model at true widths); null
-    if absent."""
-    try:
-        with open(os.path.join(ROOT, "profiles", "chain_dram_traffic.json")) as f:
-            return int(json.load(f)["dram_bytes_per_launch"])
-    except (OSError, KeyError, ValueError):
-        return None
-
-
 def run_ours(opt):
     import torch
 
@@ -902,24 +893,19 @@ def run_ours(opt):
         tot_bytes = sum(r["bytes"] * r["launches_per_step"] for r in rows)
         tot_us = sum(r["us"] * r["launches_per_step"] for r in rows)
         gemv_achieved = tot_bytes / tot_us / 1e3
-        gemv = {"kernel": "qgemv_m1_kernel (each W4 GEMV shape as a separate launch; per-launch "
-                          "averages, byte-weighted over shapes)", "achieved": round(gemv_achieved, 1),
-                "frac": round(gemv_achieved / hbm, 4), "per_shape": rows}
-        if ws == 1:
+        out["roofline"] = {"kernel": "qgemv_m1_kernel (every W4 GEMV launch of one B=1 step; per-launch "
+                                     "averages, byte-weighted over shapes)",
+                           "bound": "hbm", "achieved": round(gemv_achieved, 1), "peak": hbm,
+                           "peak_kind": peak_kind, "unit": "GB/s", "frac": round(gemv_achieved / hbm, 4),
+                           "algorithmic_bytes": int(tot_bytes / sum(r["launches_per_step"] for r in rows)),
+                           # the committed capture is of one-GPU shapes: no figure for a TP shard
+                           "traffic": ncu_traffic(rows) if ws == 1 else None, "per_shape": rows}
+        if ws == 1 and opt.chain_roofline:
+            # the persistent decode chain (off in the step by default), timed the same way
             cb, cus = chain_roofline(model)
-            achieved = cb / cus / 1e3
-            out["roofline"] = {"kernel": "chain_kernel (one launch per layer: o_proj + gate/up + down + "
-                                         "next q|k|v, 108.6 MB of weights; CUDA events over a graph of "
-                                         "every layer's launch)",
-                               "bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
-                               "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                               "algorithmic_bytes": cb, "us_per_launch": round(cus, 2),
-                               "traffic": chain_traffic(), "gemv_launches": gemv}
-        else:
-            out["roofline"] = dict(gemv, bound="hbm", peak=hbm, peak_kind=peak_kind, unit="GB/s",
-                                   algorithmic_bytes=int(tot_bytes / sum(r["launches_per_step"] for r in rows)),
-                                   # the committed capture is of one-GPU shapes: no figure for a shard
-                                   traffic=None)
+            out["chain_roofline"] = {"kernel": "chain_kernel (o_proj + gate/up + down + next q|k|v)",
+                                     "achieved": round(cb / cus / 1e3, 1), "frac": round(cb / cus / 1e3 / hbm, 4),
+                                     "algorithmic_bytes": cb, "us_per_launch": round(cus, 2)}
         sb = by_batch[str(B)]["step_bytes"]
         out["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": round(sb / (step_ms / 1e3) / 1e9, 1),
                                 "peak": hbm, "frac": by_batch[str(B)]["step_hbm_frac"]}

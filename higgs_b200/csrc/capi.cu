@@ -59,6 +59,7 @@ void qgemm_tc_prepare();
 void decode_chain_set(int on, int l2_ahead);
 void qgemv_tma_set(int on);
 void attention_set_cluster(int n);
+void model_set_tp_fuse(int on);
 
 }  // namespace higgs
 
@@ -93,6 +94,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
+    return HIGGS_OK;
+  }
+  if (n == "tp_fuse") {
+    model_set_tp_fuse(value);
     return HIGGS_OK;
   }
   if (n == "attn_cluster") {

@@ -180,11 +180,25 @@ CommArgs comm_args(const higgs_comm* c) {
 int comm_ctas(const higgs_comm* c, int n_words) {
   int k = (n_words + 2047) / 2048;
   if (k < 1) k = 1;
-  if (k > c->max_ctas) k = c->max_ctas;
+  if (k > c->max_ctas - 2) k = c->max_ctas - 2;  // the last two flag words belong to TpFuse
   return k;
 }
 
 }  // namespace
+
+TpFuse comm_tp_fuse(const higgs_comm* c, int call) {
+  TpFuse t{};
+  for (int q = 0; q < c->world; ++q) t.peer[q] = static_cast<char*>(c->peer[q]);
+  t.rank = c->rank;
+  t.world = c->world;
+  t.call = call;
+  t.max_ctas = c->max_ctas;
+  t.flag_bytes = c->flag_bytes;
+  t.words = c->words;
+  t.step = c->step;
+  t.err = c->err;
+  return t;
+}
 
 cudaError_t comm_step(higgs_comm* c, cudaStream_t st) {
   return launch_pdl(comm_step_kernel, dim3(1), dim3(32), 0, st, c->step);

@@ -23,6 +23,28 @@ cudaError_t comm_allreduce_argmax(higgs_comm* c, int call, const unsigned long l
 cudaError_t launch_argmax_keys(const float* logits, int B, int V, int offset, unsigned long long* keys,
                                cudaStream_t st);
 
+// Tensor-parallel sum fused into a row-parallel one-token GEMV (the producer) and the
+// fused-norm GEMV that consumes its result (comm.cu's buffers and step counter).
+//   producer (push): every CTA writes its f32 output rows straight into slot (call, rank) of
+//     every rank's buffer; the CTA that completes this rank's arrival count publishes flag
+//     (call, rank) = step on every rank.
+//   consumer (pull): waits until flag (call, q) == step for every rank q, then forms
+//     x = bf16(h_in + bf16(sum_q slot_q)) (ranks in order: the all-reduce kernel's bits);
+//     CTA 0 also stores it to h_out, the residual stream of the rest of the step.
+struct TpFuse {
+  char* peer[kMaxRanks];  // each rank's buffer (flags | data)
+  int rank, world, call, max_ctas;
+  size_t flag_bytes, words;
+  const unsigned* step;
+  int* err;
+  const uint16_t* h_in;
+  uint16_t* h_out;
+};
+// flag words of a call's (call, src) flag block used by the fused protocol (the all-reduce
+// kernel uses the block's first max_ctas - 2 words)
+constexpr int kTpFlagWord = 31;   // "rank src has pushed call", value = step
+constexpr int kTpCountWord = 30;  // this rank's arrival count for the call (own buffer only)
+
 struct QLinArgs {
   const uint16_t* x;
   int M, K, N;
@@ -66,7 +88,12 @@ struct QLinArgs {
   int self_prefetch;
   // single-token GEMV: weight units prefetched into L1 ahead of its register ring (0 = off)
   int m1_l1_ahead;
+  // single-token GEMV only: push the f32 output to every rank / pull the ranks' sum into x
+  int tp_push, tp_pull;
+  TpFuse tp;
 };
+// the TpFuse of call `call` of communicator c
+TpFuse comm_tp_fuse(const higgs_comm* c, int call);
 
 // Routing plan of the MoE router (moe.cu), in one buffer:
 //   int  header[4]  {n_items, n_pairs, E, k}

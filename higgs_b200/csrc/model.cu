@@ -51,6 +51,12 @@ struct LayerW {
 
 cudaError_t attention_prepare();
 
+// One-token steps of a dense tensor-parallel model: the sum over ranks after each
+// row-parallel GEMV is pushed by that GEMV's CTAs and pulled by the next fused-norm GEMV
+// (no all-reduce launch; higgs_set_option("tp_fuse")).
+static bool g_tp_fuse = true;
+void model_set_tp_fuse(int on) { g_tp_fuse = on != 0; }
+
 }  // namespace higgs
 
 using namespace higgs;
@@ -87,11 +93,12 @@ constexpr size_t kAlign = 256;
 size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
 struct WsLayout {
-  size_t h, x, qkv, q, attn, act, xl, logits, moe_rl, moe_idx, moe_sc, moe_plan, moe_act, moe_y,
+  size_t h, h2, x, qkv, q, attn, act, xl, logits, moe_rl, moe_idx, moe_sc, moe_plan, moe_act, moe_y,
       tp_part, tp_keys, tc_ws, tc_ws_bytes, chain_bar, attn_ws, total;
 };
 
 int head_rows(const higgs_model_config& c) { return c.tp_world > 1 ? c.head_rows : c.vocab; }
+
 
 
 
@@ -107,6 +114,7 @@ WsLayout layout(const higgs_model_config& c, int B, int Lq, int max_seq_len, boo
     return o;
   };
   L.h = take(T * c.hidden * 2);
+  L.h2 = take(T * c.hidden * 2);  // the other residual buffer of the fused tensor-parallel sum
   L.x = take(T * c.hidden * 2);
   L.qkv = take(T * (size_t)(c.heads + 2 * c.kv_heads) * D * 2);
   L.q = take(T * (size_t)c.heads * D * 2);
@@ -278,6 +286,42 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
   const bool tp = c.tp_world > 1;
   float* part = tp ? (float*)(ws + L.tp_part) : nullptr;
   if (tp) HG_CUDA(comm_step(m->comm, st));
+  // fused tensor-parallel sum (one token, dense layers): the residual stream alternates
+  // between h and h2, each pull writing the other
+  const bool tpf = tp && T == 1 && fuse && g_tp_fuse && c.num_experts == 0;
+  uint16_t* hc = h;
+  uint16_t* ha = (uint16_t*)(ws + L.h2);
+  int pull_call = -1;  // the pushed call the next fused-norm GEMV pulls (-1: none)
+  auto set_pull = [&](QLinArgs& a) {
+    if (pull_call < 0) return;
+    a.tp_pull = 1;
+    a.tp = comm_tp_fuse(m->comm, pull_call);
+    a.tp.h_in = hc;
+    a.tp.h_out = ha;
+    a.x = hc;
+  };
+  auto after_pull = [&](const QLinArgs& a) {
+    if (a.tp_pull) {
+      std::swap(hc, ha);
+      pull_call = -1;
+    }
+  };
+  auto push_row_parallel = [&](const QW& w, const uint16_t* xin, int call) -> int {
+    QLinArgs a{};
+    a.x = xin;
+    a.M = T;
+    a.K = w.K;
+    a.N = w.N;
+    a.w = w.w;
+    a.s = w.s;
+    a.b = w.b;
+    a.nseg = 1;
+    a.tp_push = 1;
+    a.tp = comm_tp_fuse(m->comm, call);
+    HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
+    pull_call = call;
+    return HIGGS_OK;
+  };
   // row-parallel GEMV (o_proj / down_proj): this rank's K slice, then the sum over
   // ranks added to the residual stream, or the residual epilogue on one GPU
   auto row_parallel = [&](const QW& w, const uint16_t* xin, int call, const L2Prefetch* pf) -> int {
@@ -334,6 +378,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       QLinArgs a{};
       a.x = fuse ? h : x;
       a.norm_w = fuse ? Lw.ln_in : nullptr;
+      if (tpf) set_pull(a);
       a.eps = c.rms_eps;
       a.M = T;
       a.K = H;
@@ -369,6 +414,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       }
       if (!attn_fused) a.pf = next_pf;
       HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
+      after_pull(a);
     }
     qkv_ready = false;
     if (tq) {
@@ -453,7 +499,9 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       continue;
     }
     // h = h + o_proj(attn)   (in place: each element read then written by one thread)
-    {
+    if (tpf) {
+      if ((rc = push_row_parallel(Lw.o, attn, 2 * li))) return rc;
+    } else {
       L2Prefetch pf{};
       if (!Lw.moe) add_q(pf, Lw.down);
       if ((rc = row_parallel(Lw.o, attn, 2 * li, &pf))) return rc;
@@ -503,6 +551,7 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
       QLinArgs a{};
       a.x = fuse ? h : x;
       a.norm_w = fuse ? Lw.ln_post : nullptr;
+      if (tpf) set_pull(a);
       a.eps = c.rms_eps;
       a.M = T;
       a.K = H;
@@ -527,14 +576,37 @@ int forward_impl(higgs_model* m, const higgs_forward_args* f, cudaStream_t st) {
         add_q(a.pf, m->head, (size_t)48 << 20);  // the head's leading 48 MB
       }
       HG_CUDA(launch_qgemv_ring(a, EPI_SWIGLU, st));
+      after_pull(a);
     }
-    if ((rc = row_parallel(Lw.down, act, 2 * li + 1, nullptr))) return rc;
+    if (tpf) {
+      if ((rc = push_row_parallel(Lw.down, act, 2 * li + 1))) return rc;
+    } else if ((rc = row_parallel(Lw.down, act, 2 * li + 1, nullptr))) {
+      return rc;
+    }
   }
   // final norm (+ last-token selection) and LM head
   const int rows_lm = f->last_only ? B : T;
   if (fuse && (Lq == 1 || !f->last_only) && !f->hidden_out) {
-    if ((f->logits || f->argmax) && !head_done)
-      HG_CUDA(lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
+    if ((f->logits || f->argmax) && !head_done) {
+      if (pull_call >= 0) {  // the final norm pulls the last layer's sum over ranks
+        QLinArgs a{};
+        a.norm_w = m->final_norm;
+        set_pull(a);
+        a.eps = c.rms_eps;
+        a.M = T;
+        a.K = H;
+        a.N = m->head.N;
+        a.w = m->head.w;
+        a.s = m->head.s;
+        a.b = m->head.b;
+        a.nseg = 1;
+        a.y_f32 = logits;
+        HG_CUDA(launch_qgemv_ring(a, EPI_STORE, st));
+        after_pull(a);
+      } else {
+        HG_CUDA(lin(m->head, h, m->final_norm, nullptr, logits, nullptr));
+      }
+    }
     if (f->argmax) {
       rc = emit_argmax(logits, rows_lm);
       if (rc) return rc;

@@ -689,6 +689,8 @@ cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st) {
   if (a.norm_w && !qgemv_ring_can_fuse_norm(a.M, a.K)) return cudaErrorInvalidValue;
   if (g_gemm_tc && a.M >= g_gemm_tc_rows && qgemm_tc_supported(a))
     return launch_qgemm_tc(a, epi, a.tc_ws, a.tc_ws_bytes, st);
+  if (a.tp_push || a.tp_pull)  // the fused tensor-parallel sum lives in the register-fed kernel
+    return (a.M == 1 && qgemv_m1_supported(a)) ? launch_qgemv_m1(a, epi, st) : cudaErrorInvalidValue;
   if (a.M == 1 && qgemv_tma_supported(a)) return launch_qgemv_tma(a, epi, st);  // qgemv_tma.cu
   if (a.M == 1 && qgemv_m1_supported(a)) return launch_qgemv_m1(a, epi, st);    // qgemv_m1.cu
   QLinArgs c = a;

@@ -92,10 +92,49 @@ __device__ __forceinline__ uint4 m1_frag(uint4 v) {
                     prmt(v.y, v.w, 0x7632));
 }
 
+__device__ __forceinline__ unsigned m1_ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void m1_st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned* m1_tp_flag(const TpFuse& tp, int q, int src, int word) {
+  return reinterpret_cast<unsigned*>(tp.peer[q]) + ((size_t)tp.call * tp.world + src) * tp.max_ctas + word;
+}
+
+// Chunk c (8 elements) of the GEMV input: x itself, or (tensor-parallel pull) the residual
+// stream plus the ranks' pushed partials, h + bf16(sum_q partial_q) with the ranks in order --
+// the all-reduce kernel's formula, so the same bits.  CTA 0 stores the new residual stream.
+template <bool PULL>
+__device__ __forceinline__ uint4 m1_x_chunk(const QLinArgs& a, int c) {
+  if constexpr (!PULL) return *reinterpret_cast<const uint4*>(a.x + 8 * c);
+  const TpFuse& tp = a.tp;
+  const uint4 hv = *reinterpret_cast<const uint4*>(tp.h_in + 8 * c);
+  const float* mine = reinterpret_cast<const float*>(tp.peer[tp.rank] + tp.flag_bytes) +
+                      (size_t)tp.call * tp.world * tp.words + 8 * (size_t)c;
+  float y[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int q = 0; q < tp.world; ++q) {
+    const float4 p0 = __ldcg(reinterpret_cast<const float4*>(mine + (size_t)q * tp.words));
+    const float4 p1 = __ldcg(reinterpret_cast<const float4*>(mine + (size_t)q * tp.words + 4));
+    y[0] += p0.x, y[1] += p0.y, y[2] += p0.z, y[3] += p0.w;
+    y[4] += p1.x, y[5] += p1.y, y[6] += p1.z, y[7] += p1.w;
+  }
+  const uint32_t* hp = &hv.x;
+  uint4 out;
+  uint32_t* op = &out.x;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    op[j] = pack_bf2(bf_lo(hp[j]) + round_bf(y[2 * j]), bf_hi(hp[j]) + round_bf(y[2 * j + 1]));
+  return out;
+}
+
 // WK warps split the K range of each 16-row tile; RT = 8 / WK tiles per CTA (SwiGLU: RT / 2
 // gate/up pairs).  D units of weights in flight per warp (even).
-template <int WK, int EPI, bool NORM, int D>
+template <int WK, int EPI, bool NORM, int D, bool PULL = false>
 __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLinArgs a) {
+  static_assert(!PULL || NORM, "the tensor-parallel pull feeds a fused-norm GEMV");
   static_assert(D % 2 == 0, "units are folded in pairs");
   constexpr int RT = 8 / WK;
   constexpr int ROT = (EPI == EPI_SWIGLU) ? RT / 2 : RT;
@@ -219,6 +258,22 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
   pdl_wait();
   HG_TL_MARK(1);
   pdl_launch();
+  if constexpr (PULL) {
+    // every rank's partial of this call must have landed here (bounded wait, ~1 s)
+    if (threadIdx.x < a.tp.world) {
+      const unsigned s = *a.tp.step;
+      const unsigned* f = m1_tp_flag(a.tp, a.tp.rank, threadIdx.x, kTpFlagWord);
+      const long long t0 = clock64();
+      while (m1_ld_acquire_sys(f) != s) {
+        if (clock64() - t0 > (1ll << 31)) {
+          atomicExch(a.tp.err, 1);
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    __syncthreads();
+  }
 
   if (threadIdx.x < 32) reinterpret_cast<uint4*>(zero)[threadIdx.x] = make_uint4(0, 0, 0, 0);
   const uint16_t* x = a.x;
@@ -233,7 +288,8 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
 #pragma unroll
     for (int r = 0; r < kM1RegChunks; ++r) xr[r] = make_uint4(0, 0, 0, 0);
     for (int c = threadIdx.x, r = 0; c < K / 8; c += kM1Threads, ++r) {
-      const uint4 v = *reinterpret_cast<const uint4*>(x + 8 * c);
+      const uint4 v = m1_x_chunk<PULL>(a, c);
+      if (PULL && blockIdx.x == 0) *reinterpret_cast<uint4*>(a.tp.h_out + 8 * c) = v;
 #pragma unroll
       for (int j = 0; j < kM1RegChunks; ++j)
         if (j == r) xr[j] = v;
@@ -264,7 +320,7 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
 #pragma unroll
       for (int j = 1; j < kM1RegChunks; ++j)
         if (j == r) v = xr[j];
-      if (r >= kM1RegChunks) v = *reinterpret_cast<const uint4*>(x + 8 * c);
+      if (r >= kM1RegChunks) v = m1_x_chunk<PULL>(a, c);
       uint4 wv = nwr[0];
 #pragma unroll
       for (int j = 1; j < kM1NormChunks; ++j)
@@ -398,10 +454,26 @@ __global__ void __launch_bounds__(kM1Threads, kM1CtasPerSm) qgemv_m1_kernel(QLin
             if (a.residual) o = f2bf(bf2f(o) + bf2f(a.residual[row]));
             a.y[row] = o;
           }
+          if (a.tp_push) {  // this row of the partial into slot (call, rank) of every rank
+            for (int q = 0; q < a.tp.world; ++q)
+              reinterpret_cast<float*>(a.tp.peer[q] + a.tp.flag_bytes)
+                  [((size_t)a.tp.call * a.tp.world + a.tp.rank) * a.tp.words + row] = v;
+          }
         }
       }
     }
     __syncthreads();  // red is rewritten by the next group
+  }
+  if (a.tp_push && threadIdx.x == 0) {
+    // the CTA that completes this rank's count publishes "rank pushed call" on every rank
+    __threadfence_system();
+    unsigned* cnt = m1_tp_flag(a.tp, a.tp.rank, a.tp.rank, kTpCountWord);
+    if (atomicAdd(cnt, 1u) == gridDim.x - 1) {
+      *cnt = 0u;
+      __threadfence_system();
+      const unsigned s = *a.tp.step;
+      for (int q = 0; q < a.tp.world; ++q) m1_st_release_sys(m1_tp_flag(a.tp, q, a.tp.rank, kTpFlagWord), s);
+    }
   }
   HG_TL_END(1000 + EPI * 100 + NORM * 10 + WK);
 }
@@ -807,6 +879,17 @@ int g_m1_l1 = 0;  // units ahead of the register ring that are prefetched into L
 
 template <int WK, int EPI, bool NORM, int D>
 cudaError_t m1_launch_cfg(const QLinArgs& a, int ctas, size_t smem, cudaStream_t st) {
+  if constexpr (NORM && D == 2) {
+    if (a.tp_pull) {
+      auto kp = qgemv_m1_kernel<WK, EPI, NORM, D, true>;
+      static PerDeviceOnce attr_p;
+      const cudaError_t e = attr_p.run(
+          [&] { return cudaFuncSetAttribute(kp, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024); });
+      if (e != cudaSuccess) return e;
+      return launch_pdl(kp, dim3(ctas), dim3(kM1Threads), smem, st, a);
+    }
+  }
+  if (a.tp_pull) return cudaErrorInvalidValue;  // pulls run only the fused-norm, depth-2 kernel
   auto k = qgemv_m1_kernel<WK, EPI, NORM, D>;
   static PerDeviceOnce attr;
   const cudaError_t e =
