@@ -169,7 +169,9 @@ def peaks():
 # our arm
 # ---------------------------------------------------------------------------------------------
 def make_tp_group(args_m, rank, world, max_tokens, device):
-    """This rank's peer-memory communicator; IPC handles exchanged over a gloo group."""
+    """This rank's peer-memory communicator; IPC handles exchanged over a gloo group.  Each call
+    region holds at least 64 tokens: tp_parity prefills a 32-token prompt."""
+    max_tokens = max(max_tokens, 64)
     import torch.distributed as dist
 
     from higgs_b200.model import TPGroup
@@ -232,14 +234,17 @@ def time_device_resident(eng, seqs, steps, warmup):
     for s in seqs:  # pages for every position the replays will write
         eng._ensure_pages(s, s.length + total + 1)
     # stage step 0 through the public path, then precompute every step's vectors on device
+    base = [s.length for s in seqs]
     eng.stage_step(seqs, g, first=True)
+    torch.cuda.current_stream().synchronize()
     host = np.zeros((total, 4 * B), np.int32)
     for k in range(total):
         for i, s in enumerate(seqs):
-            L = s.length + k
+            L = base[i] + k
             host[k, i] = L
             host[k, B + i] = L + 1
-        slots = np.array([s.pages[(s.length + k) // 16] * 16 + (s.length + k) % 16 for s in seqs], np.int64)
+        slots = np.array([s.pages[(b + k) // 16] * 16 + (b + k) % 16 for s, b in zip(seqs, base)],
+                         np.int64)
         host[k, 2 * B:] = slots.view(np.int32)
     staged = torch.from_numpy(host).to(g.step_dev.device)
     stream = torch.cuda.current_stream()
@@ -256,8 +261,8 @@ def time_device_resident(eng, seqs, steps, warmup):
     e1.synchronize()
     barrier()
     ms = e0.elapsed_time(e1)
-    for s in seqs:  # the replays wrote KV at these positions
-        s.length += total
+    for s, b in zip(seqs, base):  # the replays wrote KV at these positions
+        s.length = b + total
     return ms, g.graph.num_kernels if g.graph is not None else None
 
 
@@ -477,6 +482,18 @@ def kernel_case(opt):
         for it in range(3):
             for kc, ks, vc, vs in caches:
                 ops.paged_attention_tq4(q, kc, ks, vc, vs, bt, sl, L, signs, workspace=ws)
+    elif case == "tc_rate":  # tensor-core issue rate behind the matrix-form W4 matmul
+        rows = []
+        for n in (32, 64, 128, 256):
+            for nacc in (1, 2, 4):
+                if nacc * n > 512:
+                    continue
+                for spread in ((0, 1) if nacc > 1 else (0,)):
+                    for ce in (0, 1):
+                        ops.tc_mma_rate(n, nacc, spread, 256, ce)  # warm-up
+                        rows.append(ops.tc_mma_rate(n, nacc, spread, 4096, ce))
+        for r in rows:
+            print(json.dumps({k: (round(v, 2) if isinstance(v, float) else v) for k, v in r.items()}))
     elif case == "argmax":
         lg = torch.randn(1, a.vocab_size, device=dev)
         for it in range(3):

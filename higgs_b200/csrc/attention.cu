@@ -830,7 +830,7 @@ struct FinishTq4 {
   }
 };
 
-template <int MT>
+template <int MT, bool PLO = true>
 __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a) {
   constexpr int D = 128;
   constexpr int RP = 16 * MT;
@@ -1090,7 +1090,9 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
         o[mt][dt][2] *= alpha[1];
         o[mt][dt][3] *= alpha[1];
       }
-      // P scaled by the per-token V scale; page a's keys are the first k-step, page b's the second
+      // P scaled by the per-token V scale; page a's keys are the first k-step, page b's the
+      // second.  PLO: P enters the MMA as hi + lo bf16 halves; without it, as its bf16 rounding
+      // (half the P x V MMAs; measured error within the TurboQuant attention bound)
       uint32_t ph[2][4], pl[2][4];
 #pragma unroll
       for (int pp = 0; pp < 2; ++pp) {
@@ -1110,8 +1112,10 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
           ldmatrix_x4_trans(vb, (pp ? vtile1 : vtile0) + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
           mma_bf16_16816(o[mt][2 * d2], ph[pp][0], ph[pp][1], ph[pp][2], ph[pp][3], vb[0], vb[1]);
           mma_bf16_16816(o[mt][2 * d2 + 1], ph[pp][0], ph[pp][1], ph[pp][2], ph[pp][3], vb[2], vb[3]);
-          mma_bf16_16816(o[mt][2 * d2], pl[pp][0], pl[pp][1], pl[pp][2], pl[pp][3], vb[0], vb[1]);
-          mma_bf16_16816(o[mt][2 * d2 + 1], pl[pp][0], pl[pp][1], pl[pp][2], pl[pp][3], vb[2], vb[3]);
+          if constexpr (PLO) {
+            mma_bf16_16816(o[mt][2 * d2], pl[pp][0], pl[pp][1], pl[pp][2], pl[pp][3], vb[0], vb[1]);
+            mma_bf16_16816(o[mt][2 * d2 + 1], pl[pp][0], pl[pp][1], pl[pp][2], pl[pp][3], vb[2], vb[3]);
+          }
         }
       }
     }
@@ -1190,6 +1194,9 @@ void attention_set_min_pages(int n) { g_fused_min_pages = n < 4 ? 4 : (n > 4096 
 // of a (sequence, kv head) then merge through distributed shared memory instead of the
 // workspace and an arrival counter, at up to twice the pages per split
 static int g_attn_cluster = 16;
+// TurboQuant attention: P x V with P's hi + lo bf16 halves (1) or its bf16 rounding only (0)
+static bool g_tq4_p_lo = true;
+void attention_set_tq4_p_lo(int on) { g_tq4_p_lo = on != 0; }
 void attention_set_cluster(int n) { g_attn_cluster = n >= 16 ? 16 : (n >= 8 ? 8 : (n >= 2 ? n : 0)); }
 
 static size_t smem_fused(int D, int MT, int Lq) {
@@ -1214,6 +1221,8 @@ static cudaError_t attention_prepare_device() {
   set(paged_attn_bf16_kernel<128, 2>, smem_bf16(128, 2));
   set(paged_attn_tq4_kernel<1>, smem_tq4(1));
   set(paged_attn_tq4_kernel<2>, smem_tq4(2));
+  set(paged_attn_tq4_kernel<1, false>, smem_tq4(1));
+  set(paged_attn_tq4_kernel<2, false>, smem_tq4(2));
   set(fused_attn_bf16_kernel<64, 1, kFusedStages>, smem_fused(64, 1, 32));
   set(fused_attn_bf16_kernel<64, 2, kFusedStages>, smem_fused(64, 2, 32));
   set(fused_attn_bf16_kernel<128, 1, kFusedStages>, smem_fused(128, 1, 32));
@@ -1370,8 +1379,13 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
   a.ws_o = a.ws_lse + (size_t)B * Hkv * p.splits * p.rows_pad;
   cudaStream_t st = (cudaStream_t)stream;
   const int MT = p.rows_pad / 16;
-  cudaError_t e = MT == 1 ? launch_attn(paged_attn_tq4_kernel<1>, smem_tq4(1), a, p, st)
-                          : launch_attn(paged_attn_tq4_kernel<2>, smem_tq4(2), a, p, st);
+  cudaError_t e;
+  if (g_tq4_p_lo)
+    e = MT == 1 ? launch_attn(paged_attn_tq4_kernel<1>, smem_tq4(1), a, p, st)
+                : launch_attn(paged_attn_tq4_kernel<2>, smem_tq4(2), a, p, st);
+  else
+    e = MT == 1 ? launch_attn(paged_attn_tq4_kernel<1, false>, smem_tq4(1), a, p, st)
+                : launch_attn(paged_attn_tq4_kernel<2, false>, smem_tq4(2), a, p, st);
   HG_CUDA(e);
   return HIGGS_OK;
 }

@@ -60,6 +60,7 @@ void decode_chain_set(int on, int l2_ahead);
 void qgemv_tma_set(int on);
 void attention_set_cluster(int n);
 void model_set_tp_fuse(int on);
+void attention_set_tq4_p_lo(int on);
 
 }  // namespace higgs
 
@@ -94,6 +95,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
+    return HIGGS_OK;
+  }
+  if (n == "tq4_p_lo") {
+    attention_set_tq4_p_lo(value);
     return HIGGS_OK;
   }
   if (n == "tp_fuse") {

@@ -431,6 +431,65 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ---- MMA issue-rate probe ------------------------------------------------------
+// The matmul above issues 4 MMAs (M = 128, N = BN, K = 16) per 64-k weight stage into
+// one accumulator.  This probe times that instruction stream alone: one CTA per SM with
+// zero operands resident in shared memory (the same 128-byte-swizzled K-major tiles and
+// descriptors), `iters` stages of 4 MMAs, a stage's MMAs (spread 0) or each single MMA
+// (spread 1) dealt round-robin to `nacc` TMEM accumulators of N columns, and a
+// tcgen05.commit every `commit_every` stages (0: only the final one).  cycles[cta] =
+// clock64 from the first issue to the final commit's barrier phase, i.e. until every MMA
+// has completed.  Waits are bounded (the device flag higgs_tc_error reports).
+__global__ void __launch_bounds__(128, 1)
+    tc_rate_kernel(int n, int nacc, int spread, int iters, int commit_every, long long* cycles, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ uint32_t tmem_base;
+  const int warp = threadIdx.x >> 5;
+  const int words = (kTileA + n * 128) / 16;
+  for (int i = threadIdx.x; i < words; i += blockDim.x) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  fence_proxy_async();  // the zeros, written by the generic proxy, are read by the MMAs
+  const int commits = commit_every > 0 ? iters / commit_every : 0;
+  if (threadIdx.x == 0) {
+    mbar_init(&bars[0], commits > 0 ? commits : 1);  // one phase: every intermediate commit
+    mbar_init(&bars[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    tc_alloc(&tmem_base, 512);
+    tc_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_base;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
+                           ((uint32_t)(kTcRows >> 4) << 24);
+    const uint32_t sa = smem_u32(smem), sb = smem_u32(smem + kTileA);
+    const long long t0 = clock64();
+    for (int i = 0; i < iters; ++i) {
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int acc = spread ? (i * 4 + kk) % nacc : i % nacc;
+        tc_mma(tbase + acc * n, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, 1u);
+      }
+      if (commit_every > 0 && (i + 1) % commit_every == 0) tc_commit(&bars[0]);
+    }
+    tc_commit(&bars[1]);
+    bool ok = mbar_wait(&bars[1], 0, err);
+    if (commits > 0) ok = mbar_wait(&bars[0], 0, err) && ok;
+    cycles[blockIdx.x] = ok ? clock64() - t0 : -1;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tc_dealloc(tbase, 512);
+  }
+}
+
 // ---- host side ---------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -653,6 +712,27 @@ int qgemm_tc_error_and_clear() {
 }
 
 }  // namespace higgs
+
+extern "C" int higgs_diag_tc_mma_rate(higgs_ctx* ctx, int n, int nacc, int spread, int iters,
+                                      int commit_every, int ctas, long long* cycles, void* stream) {
+  HG_CHECK_ARG(ctx && cycles, "higgs_diag_tc_mma_rate: null argument");
+  HG_CHECK_ARG(n >= 16 && n <= 256 && n % 16 == 0, "higgs_diag_tc_mma_rate: N must be 16..256, a multiple of 16");
+  HG_CHECK_ARG(nacc >= 1 && nacc * n <= 512, "higgs_diag_tc_mma_rate: nacc accumulators of N columns exceed TMEM");
+  HG_CHECK_ARG(iters >= 1 && iters <= (1 << 20) && commit_every >= 0 && (spread == 0 || spread == 1),
+               "higgs_diag_tc_mma_rate: iters 1..2^20, commit_every >= 0, spread 0/1");
+  HG_DEVICE(ctx);
+  HG_CHECK_ARG(ctas >= 1 && ctas <= higgs::sm_count(), "higgs_diag_tc_mma_rate: ctas 1..SM count");
+  // 160 KB of shared memory: at most one CTA per SM, so each holds all 512 TMEM columns
+  const size_t smem = 160 * 1024;
+  static higgs::PerDeviceOnce attr;
+  HG_CUDA(attr.run([&] {
+    return cudaFuncSetAttribute(higgs::tc_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  }));
+  higgs::tc_rate_kernel<<<ctas, 128, smem, (cudaStream_t)stream>>>(n, nacc, spread, iters, commit_every, cycles,
+                                                       higgs::tc_err_ptr());
+  HG_CUDA(cudaGetLastError());
+  return HIGGS_OK;
+}
 
 extern "C" int higgs_tc_error(higgs_ctx* ctx, int* out) {
   HG_CHECK_ARG(ctx && out, "higgs_tc_error: null argument");

@@ -57,13 +57,19 @@ class _DecodeGraph:
         self.tokens = torch.zeros(B, 1, dtype=torch.int32, device=dev)
         # packed per-step vector: positions [B] i32 | seq_lens [B] i32 | slots [B] i64
         self.step_dev = torch.zeros(4 * B, dtype=torch.int32, device=dev)
-        self.step_host = torch.zeros(4 * B, dtype=torch.int32, pin_memory=True)
         self.positions = self.step_dev[:B].view(B, 1)
         self.seq_lens = self.step_dev[B:2 * B]
         self.slots = self.step_dev[2 * B:].view(torch.int64).view(B, 1)
         self.block_table = torch.zeros(B, max_blocks, dtype=torch.int32, device=dev)
-        self.bt_host = np.zeros((B, max_blocks), np.int32)
-        self.out_host = torch.zeros(B, dtype=torch.int32, pin_memory=True)
+        self.bt_host = np.zeros((B, max_blocks), np.int32)  # the host's copy of every row
+        # Two pinned staging slots, so the host can stage step k+1 while step k still runs:
+        # a slot is rewritten only after the event of the step that last used it.
+        self.step_ring = [torch.zeros(4 * B, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self.bt_ring = [torch.zeros(B, max_blocks, dtype=torch.int32, pin_memory=True)
+                        for _ in range(2)]
+        self.out_ring = [torch.zeros(B, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self.done = [None, None]
+        self.k = 0
         self.logits = (torch.empty(B, model.args.vocab_size, dtype=torch.float32, device=dev)
                        if want_logits else None)
         # argmax is written straight into the token buffer: the next step reads it in place
@@ -75,6 +81,28 @@ class _DecodeGraph:
         if use_graph:
             self.stream = torch.cuda.Stream(dev)
             self.graph = model.capture(self.fa, self.stream)
+
+    def acquire(self) -> int:
+        """The staging slot of the next step, once the step that last used it has finished."""
+        i = self.k % 2
+        self.k += 1
+        if self.done[i] is not None:
+            self.done[i].synchronize()
+            self.done[i] = None
+        return i
+
+    def finish(self, i: int, stream):
+        """Queue the D2H read of this step's tokens into slot i and mark the slot busy."""
+        self.out_ring[i].copy_(self.tokens.view(self.B), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.done[i] = ev
+
+    def collect(self, i: int) -> np.ndarray:
+        """Tokens of the step staged in slot i (waits for that step only)."""
+        if self.done[i] is not None:
+            self.done[i].synchronize()
+        return self.out_ring[i].numpy().copy()
 
     def run(self):
         import ctypes
@@ -152,52 +180,67 @@ class Engine:
                                            self.use_graph, self.keep_logits)
         return self._graphs[B]
 
-    def stage_step(self, seqs: list[Sequence], g: _DecodeGraph, first: bool):
-        """Host part of a decode step: pages, positions, slots, lengths -> one H2D copy."""
+    def stage_step(self, seqs: list[Sequence], g: _DecodeGraph, first: bool) -> int:
+        """Host part of a decode step: pages, positions, slots, lengths -> one H2D copy from a
+        pinned staging slot (returned).  Each sequence's length advances here, when the step
+        is staged, so the next step can be staged before this one's tokens are read back."""
         B = len(seqs)
-        sh = g.step_host.numpy()
+        i = g.acquire()
+        sh = g.step_ring[i].numpy()
         bt_dirty = first
-        for i, s in enumerate(seqs):
+        for b, s in enumerate(seqs):
             before = len(s.pages)
             self._ensure_pages(s, s.length + 1)
             if len(s.pages) != before or first:
-                g.bt_host[i, :len(s.pages)] = s.pages
+                g.bt_host[b, :len(s.pages)] = s.pages
                 bt_dirty = True
-            sh[i] = s.length  # position of the token being fed
-            sh[B + i] = s.length + 1
+            sh[b] = s.length  # position of the token being fed
+            sh[B + b] = s.length + 1
         slots = np.array([s.pages[s.length // PAGE] * PAGE + s.length % PAGE for s in seqs], np.int64)
         sh[2 * B:] = slots.view(np.int32)
-        stream = torch.cuda.current_stream(self.model.device)
-        g.step_dev.copy_(g.step_host, non_blocking=True)
+        for s in seqs:
+            s.length += 1
+        g.step_dev.copy_(g.step_ring[i], non_blocking=True)
         if bt_dirty:
-            g.block_table.copy_(torch.from_numpy(g.bt_host), non_blocking=False)
+            g.bt_ring[i].numpy()[:] = g.bt_host
+            g.block_table.copy_(g.bt_ring[i], non_blocking=True)
         if first:
             g.tokens.copy_(torch.tensor([[s.last_token] for s in seqs], dtype=torch.int32))
-        return stream
+        return i
 
     def decode_steps(self, seqs: list[Sequence], steps: int, force=None) -> np.ndarray:
         """`steps` greedy decode steps for all sequences; returns tokens [B, steps].
+
+        Pipelined like the reference's decode loop (crates/higgs-engine/src/simple.rs:539-562:
+        build step N+1, then sync on step N): the argmax lands in the graph's own token buffer,
+        so step k+1 is staged and launched before step k's tokens are read back, and the host's
+        bookkeeping for step k overlaps step k+1 on the device.
 
         With `force` ([B, steps] tokens) step k feeds force[:, k] instead of the previous
         step's argmax (teacher forcing, for parity checks); the argmax is still returned."""
         B = len(seqs)
         g = self._graph_for(B)
         out = np.zeros((B, steps), np.int32)
-        for k in range(steps):
-            self.stage_step(seqs, g, first=(k == 0))
-            if force is not None:
-                g.tokens.copy_(torch.from_numpy(np.ascontiguousarray(force[:, k:k + 1], dtype=np.int32)))
-            g.run()
-            g.out_host.copy_(g.tokens.view(B), non_blocking=True)
-            if self.keep_logits:
-                self.step_logits.append(g.logits.cpu().numpy())
-            torch.cuda.current_stream(self.model.device).synchronize()
-            toks = g.out_host.numpy()
-            for i, s in enumerate(seqs):
-                s.length += 1
-                s.last_token = int(toks[i])
-                s.generated.append(s.last_token)
-            out[:, k] = toks
+        stream = torch.cuda.current_stream(self.model.device)
+        pending = None  # (step, staging slot) launched but not yet read back
+        for k in range(steps + 1):
+            if k < steps:
+                i = self.stage_step(seqs, g, first=(k == 0))
+                if force is not None:
+                    g.tokens.copy_(torch.from_numpy(np.ascontiguousarray(force[:, k:k + 1],
+                                                                         dtype=np.int32)))
+                g.run()
+                if self.keep_logits:
+                    self.step_logits.append(g.logits.cpu().numpy())
+                g.finish(i, stream)
+            if pending is not None:
+                kp, ip = pending
+                toks = g.collect(ip)
+                for b, s in enumerate(seqs):
+                    s.last_token = int(toks[b])
+                    s.generated.append(s.last_token)
+                out[:, kp] = toks
+            pending = (k, i) if k < steps else None
         return out
 
     def decode_steps_sampled(self, seqs: list[Sequence], steps: int, params: SamplingParams,
@@ -260,7 +303,6 @@ class Engine:
                 tids[:, k] = ti.cpu().numpy()
                 tlps[:, k] = tl.cpu().numpy()
             for i, s in enumerate(seqs):
-                s.length += 1
                 s.last_token = int(toks[i])
                 s.generated.append(s.last_token)
             out[:, k] = toks

@@ -134,6 +134,18 @@ int higgs_set_option(const char* name, int value);
  * undefined).  Synchronising. */
 int higgs_tc_error(higgs_ctx* ctx, int* out);
 
+/* Diagnostic (not a reference op): the tensor-core issue rate that bounds the
+ * matrix-form quantized matmul at decode sizes.  One CTA on each of `ctas` SMs
+ * issues `iters` stages of 4 tcgen05.mma (M = 128, N = n, K = 16, bf16 operands
+ * from shared memory, f32 accumulators in TMEM), the stage's MMAs (spread 0) or
+ * each MMA (spread 1) dealt round-robin to `nacc` accumulators, with a
+ * tcgen05.commit every `commit_every` stages (0: only at the end).
+ * cycles: device int64 [ctas], SM clocks from the first issue until every MMA
+ * completed (-1 if a bounded wait gave up; higgs_tc_error then reports it).
+ * n 16..256 (multiple of 16), nacc * n <= 512.  Asynchronous on `stream`. */
+int higgs_diag_tc_mma_rate(higgs_ctx* ctx, int n, int nacc, int spread, int iters,
+                           int commit_every, int ctas, long long* cycles, void* stream);
+
 /* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
 
 /* ops::dequantize (crates/higgs-models/src/qwen3_next.rs:249-256):

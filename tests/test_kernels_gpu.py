@@ -377,10 +377,22 @@ def test_tq4_kv_write_bit_exact():
         assert np.array_equal(vsc[p, :, s].cpu().numpy().view(np.uint16), sv.view(np.uint16))
 
 
+@pytest.mark.parametrize("p_lo", [1, 0])
 @pytest.mark.parametrize("B,Lq,Hq,Hkv,lens", [(1, 1, 32, 8, [1]), (2, 1, 32, 8, [2048, 77]),
                                              (3, 1, 16, 8, [16, 500, 33]), (2, 6, 32, 8, [300, 64]),
                                              (1, 1, 32, 4, [4096])])
-def test_paged_attention_tq4(B, Lq, Hq, Hkv, lens):
+def test_paged_attention_tq4(B, Lq, Hq, Hkv, lens, p_lo):
+    """Against the oracle within the TurboQuant attention bound, with P x V on P's hi + lo
+    bf16 halves (tq4_p_lo 1) and on its bf16 rounding only (0)."""
+    from higgs_b200 import ffi
+    ffi.call("higgs_set_option", b"tq4_p_lo", p_lo)
+    try:
+        _tq4_attention_case(B, Lq, Hq, Hkv, lens)
+    finally:
+        ffi.call("higgs_set_option", b"tq4_p_lo", 1)
+
+
+def _tq4_attention_case(B, Lq, Hq, Hkv, lens):
     rng = np.random.default_rng(B + Lq + Hq + sum(lens))
     signs = np.where(rng.random(128) < 0.5, -1, 1).astype(np.int8)
     maxb = max((l + 15) // 16 for l in lens)
