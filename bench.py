@@ -484,14 +484,17 @@ def kernel_case(opt):
                 ops.paged_attention_tq4(q, kc, ks, vc, vs, bt, sl, L, signs, workspace=ws)
     elif case == "tc_rate":  # tensor-core issue rate behind the matrix-form W4 matmul
         rows = []
-        for n in (32, 64, 128, 256):
-            for nacc in (1, 2, 4):
-                if nacc * n > 512:
-                    continue
-                for spread in ((0, 1) if nacc > 1 else (0,)):
+        for m in (128, 64):
+            for n in (32, 64, 128, 256):
+                for warps in (1, 2, 4):
                     for ce in (0, 1):
-                        ops.tc_mma_rate(n, nacc, spread, 256, ce)  # warm-up
-                        rows.append(ops.tc_mma_rate(n, nacc, spread, 4096, ce))
+                        if warps * n > 512:
+                            continue
+                        ops.tc_mma_rate(n, 1, 0, 256, ce, m=m, warps=warps)  # warm-up
+                        rows.append(ops.tc_mma_rate(n, 1, 0, 4096, ce, m=m, warps=warps))
+        for n in (32, 128):  # several accumulators behind one issuing warp
+            for nacc in (2, 4):
+                rows.append(ops.tc_mma_rate(n, nacc, 1, 4096, 1))
         for r in rows:
             print(json.dumps({k: (round(v, 2) if isinstance(v, float) else v) for k, v in r.items()}))
     elif case == "argmax":
@@ -745,13 +748,30 @@ def config_c3(model, eng, Sequence, device, hbm, steps, ctx):
     ms_plain, _ = time_device_resident(eng, plain, steps, 3)
     for s in plain:
         eng.release(s)
+    # acceptance per draft position alpha (E[accepted] = alpha + ... + alpha^k), and the alpha
+    # at which a speculative step (its measured device parts) yields as many tokens per ms as
+    # the plain step: (1 - alpha^(k+1)) / (1 - alpha) = spec ms / plain ms
+    def tokens(al):
+        return float(sum(al ** i for i in range(k + 1)))
+
+    def solve(target):
+        lo, hi = 0.0, 1.0
+        for _ in range(60):
+            mid = 0.5 * (lo + hi)
+            lo, hi = (mid, hi) if tokens(mid) < target else (lo, mid)
+        return lo
+    spec_ms = sum(parts.values())
+    plain_ms = ms_plain / steps
     return {"workload": "qwen3-8b self-spec B=4 ctx 2048, draft 9 layers, k=5, T=0.7; e2e",
             "tok_s": round(toks / dt, 1), "ms_per_spec_step": round(dt * 1e3 / steps, 3),
             "accepted_per_step_mean": round(float(acc.mean()), 3),
             "tokens_per_step_mean": round(float(acc.mean()) + 1.0, 3),
+            "acceptance_per_draft": round(solve(float(acc.mean()) + 1.0), 3),
+            "break_even_acceptance": (round(solve(spec_ms / plain_ms), 3)
+                                      if spec_ms / plain_ms < k + 1 else None),
             "parts_device": parts,
             "plain_greedy_b4": {"tok_s": round(B * steps / (ms_plain / 1e3), 1),
-                                "ms_per_step": round(ms_plain / steps, 4)}}
+                                "ms_per_step": round(plain_ms, 4)}}
 
 
 def config_c4(device, hbm, steps, world=1, rank=0):

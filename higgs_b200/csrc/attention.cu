@@ -1194,8 +1194,9 @@ void attention_set_min_pages(int n) { g_fused_min_pages = n < 4 ? 4 : (n > 4096 
 // of a (sequence, kv head) then merge through distributed shared memory instead of the
 // workspace and an arrival counter, at up to twice the pages per split
 static int g_attn_cluster = 16;
-// TurboQuant attention: P x V with P's hi + lo bf16 halves (1) or its bf16 rounding only (0)
-static bool g_tq4_p_lo = true;
+// TurboQuant attention: P x V with P's hi + lo bf16 halves (1) or its bf16 rounding only (0,
+// the default: within the same tolerance of the oracle, C5 step 18.7 -> 17.2 ms on a B200)
+static bool g_tq4_p_lo = false;
 void attention_set_tq4_p_lo(int on) { g_tq4_p_lo = on != 0; }
 void attention_set_cluster(int n) { g_attn_cluster = n >= 16 ? 16 : (n >= 8 ? 8 : (n >= 2 ? n : 0)); }
 

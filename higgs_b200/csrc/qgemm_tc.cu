@@ -12,16 +12,18 @@
 //   * loader warp, lane 0: TMA streams the packed weight tile (128 rows x 32
 //     bytes per 64-wide k group) into an 8-stage shared-memory ring, starting
 //     before the grid dependency wait (weights never depend on the previous
-//     kernel); lane 1: TMA brings the x tile (BN tokens x 64 k, 128-byte swizzle)
-//     into the operand stage once the MMAs that read the stage completed;
-//   * 8 producer warps: thread (row, half) takes 16 packed bytes from the ring,
-//     dequantizes them with LOP3 / bf16x2 FMA / PRMT and stores the bf16 row slice
-//     in the 128-byte-swizzled K-major layout the MMA reads;
-//   * 1 MMA warp: one lane issues tcgen05.mma (M=128, N=BN, K=16) x 4 per group
-//     into a TMEM accumulator and tcgen05.commit releases the stage;
-//   * the producers then read TMEM (tcgen05.ld, 32 lanes per warp quarter) and
-//     run the epilogue: bf16 / f32 store, residual add, SwiGLU (gate and up tiles
-//     share the CTA), or a split-K partial reduced in split order by the last CTA.
+//     kernel); lane 1: TMA brings the x tiles (BN tokens x 64 k, 128-byte swizzle)
+//     into their own ring, each as soon as the MMAs of the stage XS earlier completed;
+//   * 8 producer warps: thread (row, half) takes 16 packed bytes per operand tile from
+//     the ring, dequantizes them with LOP3 / bf16x2 FMA / PRMT and stores the bf16 row
+//     slice in the 128-byte-swizzled K-major layout the MMA reads;
+//   * NA x NS MMA warps: one lane each issues tcgen05.mma (M=128, N=BN, K=16) x 4 per
+//     group for one operand tile (gate or up) and the stages i = j (mod NS) into its own
+//     TMEM accumulator; tcgen05.commit releases the operand and x slots;
+//   * the producers then read TMEM (tcgen05.ld, 32 lanes per warp quarter), add the NS
+//     accumulators in order and run the epilogue: bf16 / f32 store, residual add, SwiGLU
+//     (gate and up tiles share the CTA), or a split-K partial reduced in split order by
+//     the last CTA.
 // TMEM is allocated only after griddepcontrol.wait, so a kernel launched early
 // never holds tensor memory that its predecessor still needs.  Every mbarrier
 // wait is bounded (about 2 s): on timeout the kernel records an error that
@@ -43,7 +45,22 @@ namespace {
 
 constexpr int kTcRows = 128;       // weight rows per tile (UMMA M)
 constexpr int kTcProducers = 256;      // 8 warps, thread = (row, half of 64 k)
-constexpr int kTcThreads = kTcProducers + 64;  // + MMA warp + weight-loader warp
+// MMA-issuing warps: one tcgen05.mma issue costs a thread ~140 SM cycles (~190 with a
+// commit per stage) whatever the shape, and several issuing warps overlap (measured on
+// B200 with higgs_diag_tc_mma_rate: 1 / 2 / 4 warps 142 / 71 / 40 cycles per M=128 x N=32
+// MMA), so one issuing thread capped a 64-k weight stage (4 MMAs) at ~770 cycles.  Each
+// operand tile (gate, up) has its own warps, and NS warps per tile take the stages
+// i = j (mod NS) into their own TMEM accumulators; NS divides the operand ring depth, so a
+// ring slot is always consumed by the same warps (its parity waits stay exact).  The
+// epilogue adds a tile's NS accumulators in order j = 0, 1, ... (a fixed summation order).
+constexpr int tc_as(bool swiglu) { return swiglu ? 3 : 4; }  // bf16 operand stages
+// x tiles have their own ring, deeper than the operand ring: a tile is requested as soon as
+// the MMAs of the stage XS earlier completed, instead of when its operand slot frees (that
+// put an L2 -> shared round trip into every slot cycle).  NS divides XS (fixed warps per slot).
+constexpr int tc_xs(int BN, bool swiglu) { return swiglu ? (BN <= 64 ? 6 : 3) : 8; }
+constexpr int tc_ns(int BN, bool swiglu) { return (swiglu ? 2 : 1) * BN * tc_as(swiglu) <= 512 ? tc_as(swiglu) : 1; }
+constexpr int tc_mma_warps(int BN, bool swiglu) { return (swiglu ? 2 : 1) * tc_ns(BN, swiglu); }
+constexpr int tc_threads(int BN, bool swiglu) { return kTcProducers + 32 * (tc_mma_warps(BN, swiglu) + 1); }
 constexpr int kTileA = kTcRows * 128;  // 128 rows x 64 bf16 = 16 KB
 constexpr int kPkTile = kTcRows * 32;  // 128 rows x 64 packed nibbles = 4 KB
 constexpr int kPkStages = 8;           // packed weight stages in flight (TMA)
@@ -182,20 +199,30 @@ struct WMaps {
 };
 
 template <int BN, bool SWIGLU>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(tc_threads(BN, SWIGLU), 1)
     qgemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, const __grid_constant__ WMaps wm, TcArgs a) {
   constexpr int NA = SWIGLU ? 2 : 1;
-  constexpr int AS = SWIGLU ? 3 : 4;  // bf16 operand stages
+  constexpr int AS = tc_as(SWIGLU);  // bf16 operand stages
   constexpr int kTileB = BN * 128;
-  constexpr int kStage = NA * kTileA + kTileB;
+  constexpr int XS = tc_xs(BN, SWIGLU);
+  constexpr int kStage = NA * kTileA;
   constexpr int kPk = NA * kPkTile;  // packed bytes per stage
-  constexpr int TCOLS = (NA * BN <= 32) ? 32 : (NA * BN <= 64) ? 64 : (NA * BN <= 128) ? 128 : 256;
+  constexpr int NS = tc_ns(BN, SWIGLU);         // stage interleave per operand tile
+  constexpr int NMW = tc_mma_warps(BN, SWIGLU);  // NA x NS issuing warps
+  static_assert(AS % NS == 0 && XS % NS == 0, "a ring slot maps to fixed warps");
+  // accumulator (j, t) at TMEM column (j * NA + t) * BN
+  constexpr int TCOLS = (NMW * BN <= 32) ? 32 : (NMW * BN <= 64) ? 64 : (NMW * BN <= 128) ? 128
+                        : (NMW * BN <= 256) ? 256 : 512;
+  static_assert(NMW * BN <= 512, "TMEM columns");
   constexpr int HC = BN / 2;  // accumulator columns read per producer warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* pk = smem + AS * kStage;  // packed ring (1024-aligned: kStage is a multiple of 1024)
+  uint8_t* xr = smem + AS * kStage;  // x ring (1024-aligned: every tile size is a multiple of 1024)
+  uint8_t* pk = xr + XS * kTileB;     // packed ring
   __shared__ __align__(8) uint64_t full_bar[AS];
   __shared__ __align__(8) uint64_t empty_bar[AS];
+  __shared__ __align__(8) uint64_t x_full[XS];
+  __shared__ __align__(8) uint64_t x_empty[XS];
   __shared__ __align__(8) uint64_t pk_full[kPkStages];
   __shared__ __align__(8) uint64_t pk_empty[kPkStages];
   __shared__ __align__(8) uint64_t done_bar;
@@ -217,14 +244,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < AS; ++i) {
-      mbar_init(&full_bar[i], kTcProducers + 1);
-      mbar_init(&empty_bar[i], 1);
+      mbar_init(&full_bar[i], kTcProducers);
+      mbar_init(&empty_bar[i], NA);  // one commit per operand tile's warp
+    }
+    for (int i = 0; i < XS; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], NA);
     }
     for (int i = 0; i < kPkStages; ++i) {
       mbar_init(&pk_full[i], 1);
       mbar_init(&pk_empty[i], kTcProducers);
     }
-    mbar_init(&done_bar, 1);
+    mbar_init(&done_bar, NMW);  // one final commit per MMA warp
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -232,7 +263,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int pid = threadIdx.x;
   const int r = pid >> 1, hf = pid & 1;
   const bool producer = pid < kTcProducers;
-  const int mma_warp = kTcProducers / 32, load_warp = mma_warp + 1;
+  const int mma_warp = kTcProducers / 32, load_warp = mma_warp + NMW;
 
   // weights never depend on the previous kernel: the loader fills the whole packed
   // ring before the grid dependency wait (no waits needed for the first pass)
@@ -291,33 +322,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
     } else if (lane == 1) {
       for (int i = 0; i < nst; ++i) {
-        const int slot = i % AS;
-        if (i >= AS) mbar_wait(&empty_bar[slot], ((i / AS) - 1) & 1, a.err);
-        mbar_arrive_expect_tx(&full_bar[slot], kTileB);
-        tma_load_2d(smem + slot * kStage + NA * kTileA, &xmap, (g0 + i) * 64, m0, &full_bar[slot]);
+        const int xs = i % XS;
+        if (i >= XS) mbar_wait(&x_empty[xs], ((i / XS) - 1) & 1, a.err);
+        mbar_arrive_expect_tx(&x_full[xs], kTileB);
+        tma_load_2d(xr + xs * kTileB, &xmap, (g0 + i) * 64, m0, &x_full[xs]);
       }
     }
     __syncwarp();
-  } else if (warp == mma_warp) {
-    // ---------------- MMA warp: one elected lane issues, commits release the stage ----------------
+  } else if (warp >= mma_warp && warp < load_warp) {
+    // ---------------- MMA warps: warp (j, t) issues operand tile t of the stages i = j (mod NS)
+    // into its own accumulator; its commit is one of the NA arrivals that release the stage
+    const int mw = warp - mma_warp, tj = mw / NA, tt = mw % NA;
     if (lane == 0) {
       const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
                              ((uint32_t)(kTcRows >> 4) << 24);
-      for (int i = 0; i < nst; ++i) {
-        const int slot = i % AS;
+      const uint32_t tacc = tbase + (uint32_t)(tj * NA + tt) * BN;
+      for (int i = tj; i < nst; i += NS) {
+        const int slot = i % AS, xs = i % XS;
+        mbar_wait(&x_full[xs], (i / XS) & 1, a.err);
         mbar_wait(&full_bar[slot], (i / AS) & 1, a.err);
         tc_fence_after();
-        uint8_t* st = smem + slot * kStage;
-        const uint32_t sbx = smem_u32(st + NA * kTileA);
+        const uint32_t sbx = smem_u32(xr + xs * kTileB);
+        const uint32_t sa = smem_u32(smem + slot * kStage + tt * kTileA);
 #pragma unroll
-        for (int t = 0; t < NA; ++t) {
-          const uint32_t sa = smem_u32(st + t * kTileA);
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma(tbase + t * BN, sw128_desc(sa + kk * 32), sw128_desc(sbx + kk * 32), idesc,
-                   (i > 0 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma(tacc, sw128_desc(sa + kk * 32), sw128_desc(sbx + kk * 32), idesc, (i >= NS || kk > 0) ? 1u : 0u);
         tc_commit(&empty_bar[slot]);
+        tc_commit(&x_empty[xs]);
       }
       tc_commit(&done_bar);
     }
@@ -370,6 +401,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       for (int c = 0; c < HC; c += 16)
         tc_ld16(tbase + ((uint32_t)(sub * 32) << 16) + t * BN + chalf * HC + c, &acc[t][c]);
     tc_wait_ld();
+    // the other stage-interleave accumulators (j = 1 .. NS-1 that received a stage), in order
+#pragma unroll
+    for (int j = 1; j < NS; ++j) {
+      if (j >= nst) break;
+#pragma unroll
+      for (int t = 0; t < NA; ++t)
+#pragma unroll
+        for (int c = 0; c < HC; c += 16) {
+          float v[16];
+          tc_ld16(tbase + ((uint32_t)(sub * 32) << 16) + (j * NA + t) * BN + chalf * HC + c, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e) acc[t][c + e] += v[e];
+        }
+    }
     tc_fence_before();
 
     const int tile = m_tile * gridDim.x + n_tile;
@@ -435,25 +481,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // The matmul above issues 4 MMAs (M = 128, N = BN, K = 16) per 64-k weight stage into
 // one accumulator.  This probe times that instruction stream alone: one CTA per SM with
 // zero operands resident in shared memory (the same 128-byte-swizzled K-major tiles and
-// descriptors), `iters` stages of 4 MMAs, a stage's MMAs (spread 0) or each single MMA
-// (spread 1) dealt round-robin to `nacc` TMEM accumulators of N columns, and a
-// tcgen05.commit every `commit_every` stages (0: only the final one).  cycles[cta] =
-// clock64 from the first issue to the final commit's barrier phase, i.e. until every MMA
-// has completed.  Waits are bounded (the device flag higgs_tc_error reports).
-__global__ void __launch_bounds__(128, 1)
-    tc_rate_kernel(int n, int nacc, int spread, int iters, int commit_every, long long* cycles, int* err) {
+// descriptors), `warps` issuing warps (lane 0 of each), each issuing `iters` stages of 4
+// MMAs of M x N x 16, a stage's MMAs (spread 0) or each single MMA (spread 1) dealt
+// round-robin to that warp's `nacc` TMEM accumulators of N columns, and a tcgen05.commit
+// every `commit_every` stages (0: only the final one).  cycles[cta] = clock64 from the
+// first issue to the completion of every warp's last MMA.  Waits are bounded (the
+// device flag higgs_tc_error reports).
+constexpr int kProbeWarps = 4;
+__global__ void __launch_bounds__(32 * kProbeWarps, 1)
+    tc_rate_kernel(int m, int n, int nacc, int spread, int iters, int commit_every, int warps, long long* cycles,
+                   int* err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ __align__(8) uint64_t bars[2 * kProbeWarps];
   __shared__ uint32_t tmem_base;
-  const int warp = threadIdx.x >> 5;
+  __shared__ long long t_first, t_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int words = (kTileA + n * 128) / 16;
   for (int i = threadIdx.x; i < words; i += blockDim.x) reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
   fence_proxy_async();  // the zeros, written by the generic proxy, are read by the MMAs
   const int commits = commit_every > 0 ? iters / commit_every : 0;
   if (threadIdx.x == 0) {
-    mbar_init(&bars[0], commits > 0 ? commits : 1);  // one phase: every intermediate commit
-    mbar_init(&bars[1], 1);
+    for (int w = 0; w < kProbeWarps; ++w) {
+      mbar_init(&bars[2 * w], commits > 0 ? commits : 1);  // one phase: every intermediate commit
+      mbar_init(&bars[2 * w + 1], 1);
+    }
+    t_first = 0x7fffffffffffffffll;
+    t_last = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 0) {
@@ -464,26 +518,31 @@ __global__ void __launch_bounds__(128, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = tmem_base;
-  if (threadIdx.x == 0) {
+  if (warp < warps && lane == 0) {
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) |
-                           ((uint32_t)(kTcRows >> 4) << 24);
+                           ((uint32_t)(m >> 4) << 24);
     const uint32_t sa = smem_u32(smem), sb = smem_u32(smem + kTileA);
+    const uint32_t tw = tbase + warp * nacc * n;
     const long long t0 = clock64();
     for (int i = 0; i < iters; ++i) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) {
         const int acc = spread ? (i * 4 + kk) % nacc : i % nacc;
-        tc_mma(tbase + acc * n, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, 1u);
+        tc_mma(tw + acc * n, sw128_desc(sa + kk * 32), sw128_desc(sb + kk * 32), idesc, 1u);
       }
-      if (commit_every > 0 && (i + 1) % commit_every == 0) tc_commit(&bars[0]);
+      if (commit_every > 0 && (i + 1) % commit_every == 0) tc_commit(&bars[2 * warp]);
     }
-    tc_commit(&bars[1]);
-    bool ok = mbar_wait(&bars[1], 0, err);
-    if (commits > 0) ok = mbar_wait(&bars[0], 0, err) && ok;
-    cycles[blockIdx.x] = ok ? clock64() - t0 : -1;
+    tc_commit(&bars[2 * warp + 1]);
+    bool ok = mbar_wait(&bars[2 * warp + 1], 0, err);
+    if (commits > 0) ok = mbar_wait(&bars[2 * warp], 0, err) && ok;
+    const long long t1 = clock64();
+    atomicMin(reinterpret_cast<unsigned long long*>(&t_first), (unsigned long long)t0);
+    atomicMax(reinterpret_cast<unsigned long long*>(&t_last), ok ? (unsigned long long)t1 : ~0ull);
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0)
+    cycles[blockIdx.x] = t_last == (long long)~0ull ? -1 : t_last - t_first;
   if (warp == 0) {
     tc_fence_after();
     tc_dealloc(tbase, 512);
@@ -570,15 +629,16 @@ int* tc_err_ptr() { return device_state(current_device()).tc_err; }
 template <int BN, bool SWIGLU>
 cudaError_t launch_bn(const CUtensorMap& map, const WMaps& wm, const TcArgs& a, dim3 grid, cudaStream_t st) {
   constexpr int NA = SWIGLU ? 2 : 1;
-  constexpr int AS = SWIGLU ? 3 : 4;
-  constexpr size_t smem = (size_t)AS * (NA * kTileA + BN * 128) + (size_t)kPkStages * NA * kPkTile + 1024;
+  constexpr int AS = tc_as(SWIGLU);
+  constexpr size_t smem = (size_t)AS * NA * kTileA + (size_t)tc_xs(BN, SWIGLU) * BN * 128 +
+                          (size_t)kPkStages * NA * kPkTile + 1024;
   static_assert(smem <= 227 * 1024, "shared memory budget");
   auto k = qgemm_tc_kernel<BN, SWIGLU>;
   static PerDeviceOnce attr;
   cudaError_t e = attr.run(
       [&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); });
   if (e != cudaSuccess) return e;
-  return launch_pdl(k, grid, dim3(kTcThreads), smem, st, map, wm, a);
+  return launch_pdl(k, grid, dim3(tc_threads(BN, SWIGLU)), smem, st, map, wm, a);
 }
 
 int tc_sms() { return sm_count(); }
@@ -713,11 +773,14 @@ int qgemm_tc_error_and_clear() {
 
 }  // namespace higgs
 
-extern "C" int higgs_diag_tc_mma_rate(higgs_ctx* ctx, int n, int nacc, int spread, int iters,
-                                      int commit_every, int ctas, long long* cycles, void* stream) {
+extern "C" int higgs_diag_tc_mma_rate(higgs_ctx* ctx, int m, int n, int nacc, int spread, int iters,
+                                      int commit_every, int warps, int ctas, long long* cycles, void* stream) {
   HG_CHECK_ARG(ctx && cycles, "higgs_diag_tc_mma_rate: null argument");
+  HG_CHECK_ARG(m == 64 || m == 128, "higgs_diag_tc_mma_rate: M must be 64 or 128");
   HG_CHECK_ARG(n >= 16 && n <= 256 && n % 16 == 0, "higgs_diag_tc_mma_rate: N must be 16..256, a multiple of 16");
-  HG_CHECK_ARG(nacc >= 1 && nacc * n <= 512, "higgs_diag_tc_mma_rate: nacc accumulators of N columns exceed TMEM");
+  HG_CHECK_ARG(warps >= 1 && warps <= higgs::kProbeWarps, "higgs_diag_tc_mma_rate: warps 1..4");
+  HG_CHECK_ARG(nacc >= 1 && warps * nacc * n <= 512,
+               "higgs_diag_tc_mma_rate: warps x nacc accumulators of N columns exceed TMEM");
   HG_CHECK_ARG(iters >= 1 && iters <= (1 << 20) && commit_every >= 0 && (spread == 0 || spread == 1),
                "higgs_diag_tc_mma_rate: iters 1..2^20, commit_every >= 0, spread 0/1");
   HG_DEVICE(ctx);
@@ -728,8 +791,8 @@ extern "C" int higgs_diag_tc_mma_rate(higgs_ctx* ctx, int n, int nacc, int sprea
   HG_CUDA(attr.run([&] {
     return cudaFuncSetAttribute(higgs::tc_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   }));
-  higgs::tc_rate_kernel<<<ctas, 128, smem, (cudaStream_t)stream>>>(n, nacc, spread, iters, commit_every, cycles,
-                                                       higgs::tc_err_ptr());
+  higgs::tc_rate_kernel<<<ctas, 32 * higgs::kProbeWarps, smem, (cudaStream_t)stream>>>(
+      m, n, nacc, spread, iters, commit_every, warps, cycles, higgs::tc_err_ptr());
   HG_CUDA(cudaGetLastError());
   return HIGGS_OK;
 }

@@ -26,7 +26,7 @@ SIGNATURES: dict[str, tuple] = {
     "higgs_version": (I, []),
     "higgs_set_option": (I, [ctypes.c_char_p, I]),
     "higgs_tc_error": (I, [P, ctypes.POINTER(I)]),
-    "higgs_diag_tc_mma_rate": (I, [P, I, I, I, I, I, I, P, P]),
+    "higgs_diag_tc_mma_rate": (I, [P, I, I, I, I, I, I, I, I, P, P]),
     "higgs_w4_dequantize": (I, [P, P, P, P, I, I, P, P]),
     "higgs_w4_quantize": (I, [P, P, I64, I, P, P, P, P]),
     "higgs_embed_gather_w4": (I, [P, P, I, P, P, P, I, I, P, P]),

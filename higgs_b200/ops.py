@@ -470,17 +470,17 @@ def moe_combine(y, scores, h):
 # ---- diagnostics ---------------------------------------------------------------
 
 def tc_mma_rate(n: int, nacc: int = 1, spread: int = 0, iters: int = 4096, commit_every: int = 1,
-                ctas: int | None = None, device="cuda:0") -> dict:
+                m: int = 128, warps: int = 1, ctas: int | None = None, device="cuda:0") -> dict:
     """Tensor-core issue rate of the matrix-form quantized matmul's instruction stream
-    (higgs_diag_tc_mma_rate): SM cycles per tcgen05.mma M=128 x N=n x K=16, median over
-    one CTA per SM.  Synchronising."""
+    (higgs_diag_tc_mma_rate): SM cycles per tcgen05.mma m x n x 16 over all issuing warps,
+    median over one CTA per SM.  Synchronising."""
     import ctypes
     dev = torch.device(device)
     if ctas is None:
         ctas = torch.cuda.get_device_properties(dev).multi_processor_count
     cycles = torch.zeros(ctas, dtype=torch.int64, device=dev)
-    ffi.call("higgs_diag_tc_mma_rate", ffi.ctx(dev.index or 0), int(n), int(nacc), int(spread), int(iters),
-             int(commit_every), int(ctas), _p(cycles), _st(dev))
+    ffi.call("higgs_diag_tc_mma_rate", ffi.ctx(dev.index or 0), int(m), int(n), int(nacc), int(spread),
+             int(iters), int(commit_every), int(warps), int(ctas), _p(cycles), _st(dev))
     torch.cuda.synchronize(dev)
     err = ctypes.c_int(0)
     ffi.call("higgs_tc_error", ffi.ctx(dev.index or 0), ctypes.byref(err))
@@ -488,5 +488,6 @@ def tc_mma_rate(n: int, nacc: int = 1, spread: int = 0, iters: int = 4096, commi
     if err.value or (c < 0).any():
         raise RuntimeError("tc_mma_rate: a bounded wait gave up")
     med = float(sorted(c)[len(c) // 2])
-    return {"n": n, "nacc": nacc, "spread": spread, "commit_every": commit_every, "iters": iters,
-            "cycles_per_mma": med / (4 * iters), "flops_per_cycle": 2 * 128 * n * 16 * 4 * iters / med}
+    mmas = 4 * iters * warps
+    return {"m": m, "n": n, "warps": warps, "nacc": nacc, "spread": spread, "commit_every": commit_every,
+            "iters": iters, "cycles_per_mma": med / mmas, "flops_per_cycle": 2 * m * n * 16 * mmas / med}

@@ -124,7 +124,14 @@ int higgs_version(void);
  * L2 for the next phase's weights while the current phase runs.  "gemv_tma" (0/1,
  * default 0): one-token linears (K a multiple of 512, up to 12288) stream their
  * weights by TMA into a shared-memory ring instead of loading them into
- * registers.
+ * registers.  "attn_cluster" (0, 2..16, default 16): the largest thread-block
+ * cluster the splits of one (sequence, kv head) of the fused decode attention
+ * form to merge through distributed shared memory (0: workspace merge by the
+ * last CTA).  "tq4_p_lo" (0/1, default 0): TurboQuant attention multiplies V by
+ * P's hi + lo bf16 halves (1) instead of its bf16 rounding (0).  "tp_fuse" (0/1,
+ * default 1): one-token tensor-parallel decode sums the row-parallel partials
+ * inside the GEMVs (pushed by the producing GEMV, pulled by the next fused-norm
+ * GEMV) instead of all-reduce launches.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
@@ -135,16 +142,17 @@ int higgs_set_option(const char* name, int value);
 int higgs_tc_error(higgs_ctx* ctx, int* out);
 
 /* Diagnostic (not a reference op): the tensor-core issue rate that bounds the
- * matrix-form quantized matmul at decode sizes.  One CTA on each of `ctas` SMs
- * issues `iters` stages of 4 tcgen05.mma (M = 128, N = n, K = 16, bf16 operands
- * from shared memory, f32 accumulators in TMEM), the stage's MMAs (spread 0) or
- * each MMA (spread 1) dealt round-robin to `nacc` accumulators, with a
- * tcgen05.commit every `commit_every` stages (0: only at the end).
+ * matrix-form quantized matmul at decode sizes.  One CTA on each of `ctas` SMs;
+ * lane 0 of each of `warps` (1..4) warps issues `iters` stages of 4 tcgen05.mma
+ * (M = m (64 or 128), N = n, K = 16, bf16 operands from shared memory, f32
+ * accumulators in TMEM), the stage's MMAs (spread 0) or each MMA (spread 1)
+ * dealt round-robin to that warp's `nacc` accumulators, with a tcgen05.commit
+ * every `commit_every` stages (0: only at the end).
  * cycles: device int64 [ctas], SM clocks from the first issue until every MMA
  * completed (-1 if a bounded wait gave up; higgs_tc_error then reports it).
- * n 16..256 (multiple of 16), nacc * n <= 512.  Asynchronous on `stream`. */
-int higgs_diag_tc_mma_rate(higgs_ctx* ctx, int n, int nacc, int spread, int iters,
-                           int commit_every, int ctas, long long* cycles, void* stream);
+ * n 16..256 (multiple of 16), warps * nacc * n <= 512.  Asynchronous on `stream`. */
+int higgs_diag_tc_mma_rate(higgs_ctx* ctx, int m, int n, int nacc, int spread, int iters,
+                           int commit_every, int warps, int ctas, long long* cycles, void* stream);
 
 /* ---- a1/a2: W4 g64 quantized linear and embedding ----------------------- */
 

@@ -389,7 +389,7 @@ def test_paged_attention_tq4(B, Lq, Hq, Hkv, lens, p_lo):
     try:
         _tq4_attention_case(B, Lq, Hq, Hkv, lens)
     finally:
-        ffi.call("higgs_set_option", b"tq4_p_lo", 1)
+        ffi.call("higgs_set_option", b"tq4_p_lo", 0)  # the default
 
 
 def _tq4_attention_case(B, Lq, Hq, Hkv, lens):
