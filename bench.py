@@ -537,21 +537,31 @@ def tp_parity(args_m, full_w, tp_model, device, steps=64, prompt_len=32, seed=7)
     et = Engine(tp_model, max_seq_len=msl, prefix_entries=0, keep_logits=True)
     st = et.prefill(pr[0], use_prefix=False)
     st.last_token = int(one_tok[0])
-    et.decode_steps([st], steps - 1, force=one_tok[None, :steps - 1])
+    # the forced steps' argmax over the whole vocabulary (the TP model's sharded argmax)
+    forced = et.decode_steps([st], steps - 1, force=one_tok[None, :steps - 1])[0]
     shard = args_m.vocab_size // world
     tp_lg = np.stack(et.step_logits)[:, 0, :shard]
     ref = one_lg[:, rank * shard:(rank + 1) * shard]
-    err = float(np.max(np.abs(tp_lg - ref)))
+    err = allmax(float(np.max(np.abs(tp_lg - ref))))
+    std = allmax(float(np.std(tp_lg - ref)))  # a systematic TP error would show here, not just in the max
     rel = float(np.max(np.abs(tp_lg - ref) / (np.abs(ref) + 1e-6)))
     et.release(st)
     diff = np.nonzero(tp_free[0] != one_tok)[0]
     first_diff = int(diff[0]) if diff.size else None
     top2 = np.sort(one_lg, axis=-1)[:, -2:]
-    margin_at = (float(top2[first_diff - 1, 1] - top2[first_diff - 1, 0])
-                 if first_diff is not None and first_diff >= 1 else None)
+    margin = top2[:, 1] - top2[:, 0]  # the one-GPU top-2 margin at each decode step
+    margin_at = (float(margin[first_diff - 1]) if first_diff is not None and first_diff >= 1 else None)
+    # teacher-forced argmax disagreements, and those not explained by the measured logit noise
+    # (a step whose top-2 margin exceeds twice the largest logit difference cannot flip)
+    dis = np.nonzero(forced != one_tok[1:])[0]
+    beyond = [int(k) for k in dis if margin[k] > 2 * err]
     return {"tokens": steps, "tokens_equal": bool(allmax(float(first_diff is not None)) == 0.0),
             "first_diff": first_diff, "margin_at_first_diff": margin_at,
-            "max_logit_abs": round(allmax(err), 6), "max_logit_rel": round(allmax(rel), 6),
+            "max_logit_abs": round(err, 6), "logit_diff_std": round(std, 6),
+            "max_logit_rel": round(allmax(rel), 6),
+            "forced_argmax_disagreements": int(dis.size),
+            "near_tie_steps": int(np.sum(margin <= 2 * err)),
+            "disagreements_beyond_noise": len(beyond),
             "prompt": f"{prompt_len} uniform ids (seed {seed}), B=1, one GPU vs tp{world}"}
 
 

@@ -54,6 +54,7 @@ void set_gemm_tc_rows(int m);
 void set_gemm_tc_waves(int w);
 void set_gemm_tc_wave_cost(int c);
 void qgemv_set_wk(int wk);
+void qgemv_set_xsmem_max(int bytes);
 void qgemv_m1_set(int on, int wk, int depth, int l2, int persist, int l1);
 void qgemm_tc_prepare();
 void decode_chain_set(int on, int l2_ahead);
@@ -71,6 +72,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   const std::string n(name);
   if (n == "gemv_f16") {
     qgemv_set_f16(value != 0);
+    return HIGGS_OK;
+  }
+  if (n == "gemv_xsmem_max") {
+    qgemv_set_xsmem_max(value);
     return HIGGS_OK;
   }
   if (n == "gemv_wk") {

@@ -53,8 +53,9 @@ cudaError_t attention_prepare();
 
 // One-token steps of a dense tensor-parallel model: the sum over ranks after each
 // row-parallel GEMV is pushed by that GEMV's CTAs and pulled by the next fused-norm GEMV
-// (no all-reduce launch; higgs_set_option("tp_fuse")).
-static bool g_tp_fuse = true;
+// (no all-reduce launch; higgs_set_option("tp_fuse")).  Off by default: measured on two
+// B200s it lengthened the B=1 step (2.43 ms against 2.00 with the all-reduce launches).
+static bool g_tp_fuse = false;
 void model_set_tp_fuse(int on) { g_tp_fuse = on != 0; }
 
 }  // namespace higgs

@@ -35,7 +35,9 @@ namespace {
 constexpr int kUnitW = 16 * 128;      // packed weight bytes of a unit
 constexpr int kUnitS = 16 * 4 * 2;    // scale bytes of a unit
 constexpr int kStage = kUnitW + 2 * kUnitS;  // + biases
-constexpr size_t kXsmemMax = 32 * 1024;        // x staged in shared memory up to this size
+// x staged in shared memory (and an input RMSNorm fused into the staging) up to this size;
+// higgs_set_option("gemv_xsmem_max", bytes), at most the grouped kernel's 72 KB
+size_t g_xsmem_max = 32 * 1024;
 constexpr size_t kXsmemGroupedMax = 72 * 1024; // grouped experts always stage 8 pairs
 
 // bytes of the fragment-ordered x tile: per token G groups x 4 lane slots x 32 B, padded
@@ -657,7 +659,7 @@ bool g_gemv_f16 = false;
 
 template <int EPI>
 cudaError_t launch_epi(const QLinArgs& a, cudaStream_t st) {
-  const bool xsmem = a.M <= 8 && xfrag_bytes(a.M, a.K) <= kXsmemMax;
+  const bool xsmem = a.M <= 8 && xfrag_bytes(a.M, a.K) <= g_xsmem_max;
   if (a.M <= 8) {
     if (g_gemv_f16) {
       if (a.norm_w) return launch_wk<1, EPI, 3, true, true, true>(a, st);
@@ -706,7 +708,10 @@ cudaError_t launch_qgemv_ring(const QLinArgs& a, int epi, cudaStream_t st) {
   return cudaSuccess;
 }
 
-bool qgemv_ring_can_fuse_norm(int M, int K) { return M <= 8 && xfrag_bytes(M, K) <= kXsmemMax; }
+bool qgemv_ring_can_fuse_norm(int M, int K) { return M <= 8 && xfrag_bytes(M, K) <= g_xsmem_max; }
+void qgemv_set_xsmem_max(int bytes) {
+  g_xsmem_max = bytes < 0 ? 0 : ((size_t)bytes > kXsmemGroupedMax ? kXsmemGroupedMax : (size_t)bytes);
+}
 
 // Grouped-expert GEMV over a routing plan (a.moe_* set, a.M ignored): one
 // grid row per potential work item, items past the plan's count exit at once.

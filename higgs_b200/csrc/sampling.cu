@@ -70,17 +70,6 @@ struct RowDist {
   float inv_t, mxs;
 };
 
-__device__ RowDist make_dist(const float* logits, int V, float inv_t, float* shf) {
-  float mx = -INFINITY;
-  for (int j = threadIdx.x; j < V; j += blockDim.x) mx = fmaxf(mx, logits[j]);
-  mx = block_max(mx, shf);
-  RowDist d;
-  d.logits = logits;
-  d.inv_t = inv_t;
-  d.mxs = __fmul_rn(mx, inv_t);
-  return d;
-}
-
 // Mass functions: kind 0 = target P, kind 1 = residual max(P/tp - Q/tq, 0) * 2^40
 struct Masses {
   RowDist p, q;
@@ -94,83 +83,6 @@ struct Masses {
     return d > 0.0 ? (uint64_t)__dmul_rn(d, 1099511627776.0) : 0ull;
   }
 };
-
-// Sum of masses over [0, V) (exact).
-template <typename F>
-__device__ uint64_t block_mass_total(const F& f, int V, uint64_t* shu) {
-  const int C = (V + blockDim.x - 1) / blockDim.x;
-  const int j0 = threadIdx.x * C, j1 = min(V, j0 + C);
-  uint64_t s = 0;
-  for (int j = j0; j < j1; ++j) s += f(j);
-  uint64_t tot;
-  block_exscan_u64(s, shu, &tot);
-  return tot;
-}
-
-// Smallest j whose inclusive prefix of masses exceeds floor(u * total).
-template <typename F>
-__device__ int block_inverse_cdf(const F& f, int V, float u, uint64_t* shu, int* shi) {
-  const int C = (V + blockDim.x - 1) / blockDim.x;
-  const int j0 = threadIdx.x * C, j1 = min(V, j0 + C);
-  uint64_t s = 0;
-  for (int j = j0; j < j1; ++j) s += f(j);
-  uint64_t tot;
-  const uint64_t before = block_exscan_u64(s, shu, &tot);
-  uint64_t target = (uint64_t)__dmul_rn((double)u, (double)tot);
-  if (target >= tot) target = tot > 0 ? tot - 1 : 0;
-  __syncthreads();
-  if (threadIdx.x == 0) *shi = V - 1;
-  __syncthreads();
-  if (s > 0 && before <= target && target < before + s) {
-    uint64_t c = before;
-    for (int j = j0; j < j1; ++j) {
-      c += f(j);
-      if (c > target) {
-        *shi = j;
-        break;
-      }
-    }
-  }
-  __syncthreads();
-  return *shi;
-}
-
-__device__ int block_argmax(const float* x, int V, float* shf, int* shi) {
-  float bv = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int j = threadIdx.x; j < V; j += blockDim.x) {
-    const float v = x[j];
-    if (v > bv || (v == bv && j < bi)) {  // NaN never wins
-      bv = v;
-      bi = j;
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) {
-      bv = ov;
-      bi = oi;
-    }
-  }
-  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-  __syncthreads();
-  if (l == 0) {
-    shf[w] = bv;
-    shi[w] = bi;
-  }
-  __syncthreads();
-  float rv = -INFINITY;
-  int ri = 0x7fffffff;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i)
-    if (shf[i] > rv || (shf[i] == rv && shi[i] < ri)) {
-      rv = shf[i];
-      ri = shi[i];
-    }
-  __syncthreads();
-  return ri == 0x7fffffff ? 0 : ri;
-}
 
 // Greedy argmax of one row split across a cluster of kArgmaxCluster CTAs: each
 // CTA reduces a slice to a single u64 key, then CTA 0 reads the others' keys
@@ -256,64 +168,208 @@ __global__ void __cluster_dims__(kArgmaxCluster, 1, 1) __launch_bounds__(kArgmax
   cluster.sync();  // peers keep their shared memory until CTA 0 has read it
 }
 
-__global__ void __launch_bounds__(kSampThreads) sample_kernel(const float* logits, int V,
-                                                              float inv_t, int greedy,
-                                                              const float* uniforms,
-                                                              int32_t* out) {
-  pdl_wait();
-  __shared__ float shf[32];
-  __shared__ int shi[32];
-  __shared__ uint64_t shu[32];
-  __shared__ int sres;
-  const float* row = logits + (size_t)blockIdx.x * V;
-  int r;
-  if (greedy) {
-    r = block_argmax(row, V, shf, shi);
-  } else {
-    Masses m;
-    m.p = make_dist(row, V, inv_t, shf);
-    m.q = m.p;
-    m.tp = m.tq = 1;
-    m.kind = 0;
-    r = block_inverse_cdf(m, V, uniforms[blockIdx.x], shu, &sres);
+// ---- one row over a cluster of CTAs ------------------------------------------
+// Sampling and speculative acceptance of a row spread over the kRowCluster CTAs of a
+// thread-block cluster: CTA r owns the slice [r * per, min(V, (r + 1) * per)) of the
+// vocabulary, reduces it inside the CTA, and the CTAs combine their results through
+// distributed shared memory (each writes its value into its own slot of an alternating
+// pair, the cluster syncs, threads 0-7 read the 8 slots).  Every combined quantity is a
+// maximum, an exact u64 sum or a minimum, so each CTA holds the same bits, equal to the
+// single-CTA kernels' (a draw is the smallest j whose inclusive prefix of masses exceeds
+// floor(u * total), whatever the partition).  One sequence used to be one CTA of the 148
+// SMs walking its row several times per draft position.
+constexpr int kRowCluster = 8;
+constexpr int kRowThreads = 512;
+
+struct ClRow {
+  int j0, j1;  // this CTA's slice of the row
+  int phase;   // exchange slot in use
+  uint64_t* xch;  // [2] this CTA's published values
+  uint64_t* xin;  // [kRowCluster] the values read back
+};
+
+// op 0: u64 sum, 1: u64 max, 2: u64 min
+__device__ uint64_t cl_combine(uint64_t v, int op, ClRow& c) {
+  cg::cluster_group cl = cg::this_cluster();
+  if (threadIdx.x == 0) c.xch[c.phase] = v;
+  cl.sync();
+  if (threadIdx.x < kRowCluster) c.xin[threadIdx.x] = *cl.map_shared_rank(&c.xch[c.phase], threadIdx.x);
+  __syncthreads();
+  uint64_t r = c.xin[0];
+  for (int q = 1; q < kRowCluster; ++q) {
+    const uint64_t o = c.xin[q];
+    r = op == 0 ? r + o : (op == 1 ? (o > r ? o : r) : (o < r ? o : r));
   }
-  if (threadIdx.x == 0) out[blockIdx.x] = r;
-  pdl_launch();
+  c.phase ^= 1;
+  return r;
 }
 
-__global__ void __launch_bounds__(kSampThreads) spec_accept_kernel(
-    const float* target, const float* draft, const int32_t* dtok, int k, int V, float inv_t,
-    int greedy, const float* au, const float* su, int32_t* accepted, int32_t* out_tokens) {
-  pdl_wait();
-  __shared__ float shf[32];
-  __shared__ int shi[32];
-  __shared__ uint64_t shu[32];
-  __shared__ int sres;
-  const int b = blockIdx.x;
-  int32_t* ot = out_tokens + (size_t)b * (k + 1);
-  for (int i = threadIdx.x; i <= k; i += blockDim.x) ot[i] = -1;
+__device__ __forceinline__ uint64_t f2ord(float f) {  // order-preserving map of a float
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? (uint64_t)(~u) : (uint64_t)(u | 0x80000000u);
+}
+__device__ __forceinline__ float ord2f(uint64_t o) {
+  const uint32_t u = (uint32_t)o;
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
+__device__ RowDist cl_make_dist(const float* logits, float inv_t, float* shf, ClRow& c) {
+  float mx = -INFINITY;
+  for (int j = c.j0 + threadIdx.x; j < c.j1; j += blockDim.x) mx = fmaxf(mx, logits[j]);
+  mx = block_max(mx, shf);
+  mx = ord2f(cl_combine(f2ord(mx), 1, c));
+  RowDist d;
+  d.logits = logits;
+  d.inv_t = inv_t;
+  d.mxs = __fmul_rn(mx, inv_t);
+  return d;
+}
+
+template <typename F>
+__device__ uint64_t cl_mass_total(const F& f, uint64_t* shu, ClRow& c) {
+  const int n = c.j1 - c.j0;
+  const int C = (n + blockDim.x - 1) / blockDim.x;
+  const int a = c.j0 + threadIdx.x * C, e = min(c.j1, a + C);
+  uint64_t s = 0;
+  for (int j = a; j < e; ++j) s += f(j);
+  uint64_t tot;
+  block_exscan_u64(s, shu, &tot);
+  return cl_combine(tot, 0, c);
+}
+
+// Smallest j whose inclusive prefix of masses exceeds floor(u * total); V - 1 if none.
+template <typename F>
+__device__ int cl_inverse_cdf(const F& f, int V, float u, uint64_t* shu, int* shi, ClRow& c) {
+  const int n = c.j1 - c.j0;
+  const int C = (n + blockDim.x - 1) / blockDim.x;
+  const int a = c.j0 + threadIdx.x * C, e = min(c.j1, a + C);
+  uint64_t s = 0;
+  for (int j = a; j < e; ++j) s += f(j);
+  uint64_t cta_tot;
+  const uint64_t before = block_exscan_u64(s, shu, &cta_tot);
+  // every CTA's total: the slices before this one and the whole row
+  cg::cluster_group cl = cg::this_cluster();
+  if (threadIdx.x == 0) c.xch[c.phase] = cta_tot;
+  cl.sync();
+  if (threadIdx.x < kRowCluster) c.xin[threadIdx.x] = *cl.map_shared_rank(&c.xch[c.phase], threadIdx.x);
   __syncthreads();
+  c.phase ^= 1;
+  const int rank = (int)cl.block_rank();
+  uint64_t below = 0, tot = 0;
+  for (int q = 0; q < kRowCluster; ++q) {
+    if (q < rank) below += c.xin[q];
+    tot += c.xin[q];
+  }
+  uint64_t target = (uint64_t)__dmul_rn((double)u, (double)tot);
+  if (target >= tot) target = tot > 0 ? tot - 1 : 0;
+  if (threadIdx.x == 0) *shi = 0x7fffffff;
+  __syncthreads();
+  const uint64_t mine = below + before;
+  if (s > 0 && mine <= target && target < mine + s) {
+    uint64_t acc = mine;
+    for (int j = a; j < e; ++j) {
+      acc += f(j);
+      if (acc > target) {
+        *shi = j;
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  const int r = (int)cl_combine((uint64_t)(uint32_t)*shi, 2, c);
+  return r == 0x7fffffff ? V - 1 : r;
+}
+
+__device__ int cl_argmax(const float* x, unsigned long long* shk, ClRow& c) {
+  unsigned long long best = 0ull;
+  for (int j = c.j0 + threadIdx.x; j < c.j1; j += blockDim.x) best = max(best, argmax_key(x[j], j));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) shk[threadIdx.x >> 5] = best;
+  __syncthreads();
+  unsigned long long b = 0ull;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) b = max(b, shk[w]);
+  b = cl_combine(b, 1, c);
+  return (int)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
+}
+
+__device__ __forceinline__ ClRow cl_row(int V, uint64_t* xch, uint64_t* xin) {
+  ClRow c;
+  const int per = (V + kRowCluster - 1) / kRowCluster;
+  const int r = (int)cg::this_cluster().block_rank();
+  c.j0 = min(V, r * per);
+  c.j1 = min(V, c.j0 + per);
+  c.phase = 0;
+  c.xch = xch;
+  c.xin = xin;
+  return c;
+}
+
+// sample() at T > 0 for one row per cluster (the plain draw, no filters)
+__global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kRowThreads)
+    sample_cluster_kernel(const float* logits, int V, float inv_t, const float* uniforms, int32_t* out) {
+  __shared__ float shf[32];
+  __shared__ int shi;
+  __shared__ uint64_t shu[32];
+  __shared__ uint64_t xch[2], xin[kRowCluster];
+  pdl_wait();
+  ClRow c = cl_row(V, xch, xin);
+  const float* row = logits + (size_t)blockIdx.y * V;
+  Masses m;
+  m.p = cl_make_dist(row, inv_t, shf, c);
+  m.q = m.p;
+  m.tp = m.tq = 1;
+  m.kind = 0;
+  const int r = cl_inverse_cdf(m, V, uniforms[blockIdx.y], shu, &shi, c);
+  if (blockIdx.x == 0 && threadIdx.x == 0) out[blockIdx.y] = r;
+  pdl_launch();
+  cg::this_cluster().sync();  // peers keep their shared memory until every read is done
+}
+
+// Speculative acceptance of one sequence per cluster: the rule of spec_accept_kernel with
+// every row reduction spread over the cluster.  draft_stride: elements between the draft
+// rows of consecutive positions of one sequence (V for [B, k, V], B * V for [k, B, V]).
+__global__ void __cluster_dims__(kRowCluster, 1, 1) __launch_bounds__(kRowThreads)
+    spec_accept_cluster_kernel(const float* target, const float* draft, size_t draft_stride,
+                               size_t draft_seq, const int32_t* dtok, int k, int V, float inv_t,
+                               int greedy, const float* au, const float* su, int32_t* accepted,
+                               int32_t* out_tokens) {
+  __shared__ float shf[32];
+  __shared__ int shi;
+  __shared__ uint64_t shu[32];
+  __shared__ unsigned long long shk[kRowThreads / 32];
+  __shared__ uint64_t xch[2], xin[kRowCluster];
+  pdl_wait();
+  const int b = blockIdx.y;
+  const bool writer = blockIdx.x == 0 && threadIdx.x == 0;
+  ClRow c = cl_row(V, xch, xin);
+  int32_t* ot = out_tokens + (size_t)b * (k + 1);
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i <= k; i += blockDim.x) ot[i] = -1;
+  const float* trow = target + (size_t)b * (k + 1) * V;
+  const float* drow = draft ? draft + (size_t)b * draft_seq : nullptr;
   int n = 0;
   int final_tok = -1;
   if (greedy) {
     for (; n < k; ++n) {
-      const int am = block_argmax(target + ((size_t)b * (k + 1) + n) * V, V, shf, shi);
+      const int am = cl_argmax(trow + (size_t)n * V, shk, c);
       if (am != dtok[b * k + n]) break;
-      if (threadIdx.x == 0) ot[n] = am;
+      if (writer) ot[n] = am;
     }
-    final_tok = block_argmax(target + ((size_t)b * (k + 1) + n) * V, V, shf, shi);
+    final_tok = cl_argmax(trow + (size_t)n * V, shk, c);
   } else {
     bool rejected = false;
     for (; n < k; ++n) {
       const int x = dtok[b * k + n];
       Masses m;
-      m.p = make_dist(target + ((size_t)b * (k + 1) + n) * V, V, inv_t, shf);
-      m.q = make_dist(draft + ((size_t)b * k + n) * V, V, inv_t, shf);
+      m.p = cl_make_dist(trow + (size_t)n * V, inv_t, shf, c);
+      m.q = cl_make_dist(drow + (size_t)n * draft_stride, inv_t, shf, c);
       m.kind = 0;
-      m.tp = block_mass_total(m, V, shu);
+      m.tp = cl_mass_total(m, shu, c);
       Masses mq = m;
       mq.p = m.q;
-      const uint64_t tq = block_mass_total(mq, V, shu);
+      const uint64_t tq = cl_mass_total(mq, shu, c);
       m.tq = tq;
       const bool in_range = x >= 0 && x < V;
       const double Px = in_range ? (double)fixed_mass(m.p.logits[x], inv_t, m.p.mxs) : 0.0;
@@ -322,32 +378,29 @@ __global__ void __launch_bounds__(kSampThreads) spec_accept_kernel(
       const double rhs = __dmul_rn(Px, (double)tq);
       if (!(lhs < rhs)) {
         m.kind = 1;
-        const uint64_t rt = block_mass_total(m, V, shu);
-        if (rt == 0) {
-          m.kind = 0;
-          final_tok = block_inverse_cdf(m, V, su[b], shu, &sres);
-        } else {
-          final_tok = block_inverse_cdf(m, V, su[b], shu, &sres);
-        }
+        const uint64_t rt = cl_mass_total(m, shu, c);
+        if (rt == 0) m.kind = 0;  // no residual mass: draw from the target distribution
+        final_tok = cl_inverse_cdf(m, V, su[b], shu, &shi, c);
         rejected = true;
         break;
       }
-      if (threadIdx.x == 0) ot[n] = x;
+      if (writer) ot[n] = x;
     }
     if (!rejected) {
       Masses m;
-      m.p = make_dist(target + ((size_t)b * (k + 1) + k) * V, V, inv_t, shf);
+      m.p = cl_make_dist(trow + (size_t)k * V, inv_t, shf, c);
       m.q = m.p;
       m.tp = m.tq = 1;
       m.kind = 0;
-      final_tok = block_inverse_cdf(m, V, su[b], shu, &sres);
+      final_tok = cl_inverse_cdf(m, V, su[b], shu, &shi, c);
     }
   }
-  if (threadIdx.x == 0) {
+  if (writer) {
     ot[n] = final_tok;
     accepted[b] = n;
   }
   pdl_launch();
+  cg::this_cluster().sync();  // peers keep their shared memory until every read is done
 }
 
 __global__ void penalties_kernel(float* logits, int V, const int32_t* hist, const int32_t* lens,
@@ -737,10 +790,15 @@ extern "C" int higgs_sample(higgs_ctx* ctx, const float* logits, int B, int V, f
   HG_CHECK_ARG(temperature == 0.0f || uniforms, "higgs_sample: uniforms required when T > 0");
   HG_DEVICE(ctx);
   if (B == 0) return HIGGS_OK;
-  const int greedy = temperature == 0.0f;
-  const float inv_t = greedy ? 1.0f : 1.0f / temperature;
-  HG_CUDA(launch_pdl(sample_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream, logits,
-                     V, inv_t, greedy, uniforms, out));
+  HG_CHECK_ARG(B <= 65535, "higgs_sample: B > 65535");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (temperature == 0.0f) {
+    HG_CUDA(launch_pdl(argmax_cluster_kernel, dim3(kArgmaxCluster, B), dim3(kArgmaxThreads), 0, st,
+                       logits, V, 0, out, (unsigned long long*)nullptr));
+    return HIGGS_OK;
+  }
+  HG_CUDA(launch_pdl(sample_cluster_kernel, dim3(kRowCluster, B), dim3(kRowThreads), 0, st, logits, V,
+                     1.0f / temperature, uniforms, out));
   return HIGGS_OK;
 }
 
@@ -757,11 +815,13 @@ extern "C" int higgs_spec_accept(higgs_ctx* ctx, const float* target_logits,
                "higgs_spec_accept: draft logits and uniforms required when T > 0");
   HG_DEVICE(ctx);
   if (B == 0) return HIGGS_OK;
+  HG_CHECK_ARG(B <= 65535, "higgs_spec_accept: B > 65535");
   const int greedy = temperature == 0.0f;
   const float inv_t = greedy ? 1.0f : 1.0f / temperature;
-  HG_CUDA(launch_pdl(spec_accept_kernel, dim3(B), dim3(kSampThreads), 0, (cudaStream_t)stream,
-                     target_logits, draft_logits, draft_tokens, k, V, inv_t, greedy,
-                     accept_uniforms, sample_uniforms, accepted, out_tokens));
+  HG_CUDA(launch_pdl(spec_accept_cluster_kernel, dim3(kRowCluster, B), dim3(kRowThreads), 0,
+                     (cudaStream_t)stream, target_logits, draft_logits, (size_t)V, (size_t)k * V,
+                     draft_tokens, k, V, inv_t, greedy, accept_uniforms, sample_uniforms, accepted,
+                     out_tokens));
   return HIGGS_OK;
 }
 
@@ -803,8 +863,8 @@ extern "C" int higgs_sample_filtered(higgs_ctx* ctx, const float* logits, int B,
   const float inv_t = 1.0f / temperature;
   const bool filt = (top_k >= 1 && top_k < V) || top_p < 1.0f || min_p > 0.0f;
   if (!filt) {  // no filter keeps every token: the plain draw
-    HG_CUDA(launch_pdl(sample_kernel, dim3(B), dim3(kSampThreads), 0, st, logits, V, inv_t, 0,
-                       uniforms, out));
+    HG_CUDA(launch_pdl(sample_cluster_kernel, dim3(kRowCluster, B), dim3(kRowThreads), 0, st, logits, V,
+                       inv_t, uniforms, out));
     return HIGGS_OK;
   }
   static PerDeviceOnce attr;

@@ -129,7 +129,7 @@ int higgs_version(void);
  * form to merge through distributed shared memory (0: workspace merge by the
  * last CTA).  "tq4_p_lo" (0/1, default 0): TurboQuant attention multiplies V by
  * P's hi + lo bf16 halves (1) instead of its bf16 rounding (0).  "tp_fuse" (0/1,
- * default 1): one-token tensor-parallel decode sums the row-parallel partials
+ * default 0): one-token tensor-parallel decode sums the row-parallel partials
  * inside the GEMVs (pushed by the producing GEMV, pulled by the next fused-norm
  * GEMV) instead of all-reduce launches.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */

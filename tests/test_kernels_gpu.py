@@ -459,6 +459,18 @@ def test_sample_bit_exact(golden):
         assert np.array_equal(o.sample(t(lg), T, t(u)).cpu().numpy(), orc.sample(lg, T, u))
 
 
+@pytest.mark.parametrize("V", [1, 5, 9, 1000, 32003])
+def test_sample_small_and_ragged_vocab(V):
+    """The row is spread over an 8-CTA cluster: slices that are empty (V < 8) or ragged."""
+    o = ops()
+    rng = np.random.default_rng(V)
+    lg = rng.normal(0, 2, size=(3, V)).astype(np.float32)
+    u = np.array([0.0, 0.5, 0.99999994], np.float32)
+    for T in (0.7, 1.0):
+        assert np.array_equal(o.sample(t(lg), T, t(u)).cpu().numpy(), orc.sample(lg, T, u))
+    assert np.array_equal(o.sample(t(lg), 0.0).cpu().numpy(), orc.argmax(lg))
+
+
 @pytest.mark.parametrize("T", [0.7, 0.0, 1.3])
 def test_spec_accept_bit_exact(T, golden):
     o = ops()

@@ -26,6 +26,10 @@ def moe_tp_args():
     return dataclasses.replace(tiny_args("qwen3_moe", layers=3), intermediate_size=1024)
 
 
+def n_seqs(kind):
+    return 1 if kind == "dense_fused" else 2
+
+
 def _worker(rank, world, port, q, kind="dense"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -38,9 +42,12 @@ def _worker(rank, world, port, q, kind="dense"):
         from higgs_b200.engine import Engine
         from higgs_b200.model import Model, TPGroup, shard_weights, weights_to_device
         from tests.test_tp_cpu import tp_args
-        args = tp_args() if kind == "dense" else moe_tp_args()
+        args = moe_tp_args() if kind == "moe" else tp_args()
         w = synth_weights_numpy(args, seed=0)
         dev = f"cuda:{rank}"
+        if kind == "dense_fused":  # one sequence: the GEMV-fused sum over ranks (option tp_fuse)
+            from higgs_b200 import ffi
+            ffi.call("higgs_set_option", b"tp_fuse", 1)
         wd = weights_to_device(shard_weights(args, w, rank, world), dev)
 
         def gather(b):
@@ -50,7 +57,7 @@ def _worker(rank, world, port, q, kind="dense"):
         tp = TPGroup(rank, world, words_per_call=32 * args.hidden_size,
                      n_calls=2 * args.num_hidden_layers + 1, all_gather=gather, device=dev)
         m = Model(args, wd, num_pages=128, device=dev, tp=tp)
-        pr = np.random.default_rng(1).integers(0, args.vocab_size, size=(2, 20)).astype(np.int32)
+        pr = np.random.default_rng(1).integers(0, args.vocab_size, size=(n_seqs(kind), 20)).astype(np.int32)
         toks = Engine(m, max_seq_len=256).generate_greedy(list(pr), STEPS, use_prefix=False)
         torch.cuda.synchronize()
         q.put((rank, toks, tp.error()))
@@ -64,16 +71,18 @@ def _worker(rank, world, port, q, kind="dense"):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("kind", ["dense", "moe"])
+@pytest.mark.parametrize("kind", ["dense", "dense_fused", "moe"])
 def test_tp2_greedy_matches_oracle(kind):
-    """Dense: tensor parallel.  MoE: attention tensor parallel, experts split over the two
-    ranks (expert parallelism) with the expert outputs summed by the same all-reduce."""
+    """Dense: tensor parallel.  Dense fused: one sequence with the sum over ranks inside the
+    GEMVs (pushed by the row-parallel GEMV, pulled by the next fused-norm GEMV).  MoE:
+    attention tensor parallel, experts split over the two ranks (expert parallelism) with
+    the expert outputs summed by the same all-reduce."""
     from oracle.model_ref import RefModel, synth_weights_numpy
     from tests.test_tp_cpu import tp_args
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29700 + os.getpid() % 1000 + (7 if kind == "moe" else 0)
+    port = 29700 + os.getpid() % 1000 + {"dense": 0, "dense_fused": 3, "moe": 7}[kind]
     ps = [ctx.Process(target=_worker, args=(r, world, port, q, kind)) for r in range(world)]
     for p_ in ps:
         p_.start()
@@ -84,15 +93,16 @@ def test_tp2_greedy_matches_oracle(kind):
         assert r[1] is not None, r[2]
         assert r[2] == 0, "a collective timed out"
     assert np.array_equal(res[0][1], res[1][1])
-    args = tp_args() if kind == "dense" else moe_tp_args()
+    args = moe_tp_args() if kind == "moe" else tp_args()
     w = synth_weights_numpy(args, seed=0)
-    pr = np.random.default_rng(1).integers(0, args.vocab_size, size=(2, 20)).astype(np.int32)
+    nb = n_seqs(kind)
+    pr = np.random.default_rng(1).integers(0, args.vocab_size, size=(nb, 20)).astype(np.int32)
     ref = RefModel(args, w)
     ref_tok, ref_lg = ref.greedy(pr, STEPS)
     top2 = np.sort(ref_lg, axis=-1)[..., -2:]
     margin = top2[..., 1] - top2[..., 0]  # [steps, B]
     near = ref.step_route_near  # MoE routings within one bf16 ulp of a swap
-    for b in range(2):
+    for b in range(nb):
         d = np.nonzero(res[0][1][b] != ref_tok[b])[0]
         if d.size:
             k = int(d[0])
