@@ -1420,9 +1420,13 @@ int fused_attention_launch(higgs_ctx* ctx, const void* qkv, int B, int Lq, int H
                          attn_ws_bytes(p, B, Hkv, D), workspace);
   if (rc) return rc;
   // cluster merge: the split count rounded up to a power of two (at most g_attn_cluster), the
-  // pages spread over it, as long as a split gets at most twice the planned pages
+  // pages spread over it, as long as a split gets at most twice the planned pages, for launches
+  // of at most kClusterPairs (sequence, kv head) pairs (measured on B200: B=1 step 2.173 -> 2.147
+  // ms; with 32 pairs it was slower: B=4 on one GPU 2.96 -> 3.72 ms, B=8 with 4 kv heads per
+  // rank on two GPUs 2.85 -> 3.65 ms)
+  constexpr int kClusterPairs = 8;
   int cluster = 0;
-  if (g_attn_cluster >= 2 && p.splits > 1) {
+  if (g_attn_cluster >= 2 && p.splits > 1 && B * Hkv <= kClusterPairs) {
     int c = 2;
     while (c < p.splits && c < g_attn_cluster) c *= 2;
     const int max_pages = (max_seq_len + 15) / 16;
