@@ -57,8 +57,26 @@ constexpr int tc_as(bool swiglu) { return swiglu ? 3 : 4; }  // bf16 operand sta
 // x tiles have their own ring, deeper than the operand ring: a tile is requested as soon as
 // the MMAs of the stage XS earlier completed, instead of when its operand slot frees (that
 // put an L2 -> shared round trip into every slot cycle).  NS divides XS (fixed warps per slot).
-constexpr int tc_xs(int BN, bool swiglu) { return swiglu ? (BN <= 64 ? 6 : 3) : 8; }
-constexpr int tc_ns(int BN, bool swiglu) { return (swiglu ? 2 : 1) * BN * tc_as(swiglu) <= 512 ? tc_as(swiglu) : 1; }
+constexpr int tc_xs(int BN, bool swiglu) { return swiglu ? (BN <= 64 ? 6 : (BN <= 128 ? 3 : 2)) : (BN <= 128 ? 8 : 4); }
+// the largest stage interleave (the operand ring depth, else 2, else 1) that divides both
+// rings and fits TMEM
+constexpr int tc_ns(int BN, bool swiglu) {
+  const int na = swiglu ? 2 : 1, as = tc_as(swiglu), xs = tc_xs(BN, swiglu);
+  if (xs % as == 0 && na * as * BN <= 512) return as;
+  if (as % 2 == 0 && xs % 2 == 0 && na * 2 * BN <= 512) return 2;
+  return 1;
+}
+int tc_sms();
+// token-tile width: 256 tokens per MMA (each dequantized weight tile serves twice as many
+// tokens) when that still gives every SM two tiles without a K split; measured on B200: the
+// 2048-token gate/up of Qwen3-8B 700 -> 475 us, but 256- and 512-token prefills of
+// Qwen3-1.7B slower with too few tiles
+inline int tc_bn(int M, int N) {
+  if (M <= 32) return 32;
+  if (M <= 64) return 64;
+  if (M <= 128 || (long long)(N / kTcRows) * ((M + 255) / 256) < 2LL * tc_sms()) return 128;
+  return 256;
+}
 constexpr int tc_mma_warps(int BN, bool swiglu) { return (swiglu ? 2 : 1) * tc_ns(BN, swiglu); }
 constexpr int tc_threads(int BN, bool swiglu) { return kTcProducers + 32 * (tc_mma_warps(BN, swiglu) + 1); }
 constexpr int kTileA = kTcRows * 128;  // 128 rows x 64 bf16 = 16 KB
@@ -389,70 +407,36 @@ __global__ void __launch_bounds__(tc_threads(BN, SWIGLU), 1)
       }
     }
 
-    // ---------------- epilogue ----------------
+    // ---------------- epilogue, in chunks of 16 accumulator columns ----------------
     mbar_wait(&done_bar, 0, a.err);
     tc_fence_after();
     const int sub = warp & 3, chalf = warp >> 2;
     const int row = sub * 32 + lane;
-    float acc[NA][HC];
+    const uint32_t lane_base = tbase + ((uint32_t)(sub * 32) << 16);
+    // columns [c, c + 16) of this warp's half: tile t's accumulators summed over the stage
+    // interleave j = 0, 1, ... (those that received a stage), in that order
+    auto load_chunk = [&](int c, float (&acc)[NA][16]) {
 #pragma unroll
-    for (int t = 0; t < NA; ++t)
+      for (int t = 0; t < NA; ++t) tc_ld16(lane_base + t * BN + chalf * HC + c, acc[t]);
+      tc_wait_ld();
 #pragma unroll
-      for (int c = 0; c < HC; c += 16)
-        tc_ld16(tbase + ((uint32_t)(sub * 32) << 16) + t * BN + chalf * HC + c, &acc[t][c]);
-    tc_wait_ld();
-    // the other stage-interleave accumulators (j = 1 .. NS-1 that received a stage), in order
+      for (int j = 1; j < NS; ++j) {
+        if (j >= nst) break;
 #pragma unroll
-    for (int j = 1; j < NS; ++j) {
-      if (j >= nst) break;
-#pragma unroll
-      for (int t = 0; t < NA; ++t)
-#pragma unroll
-        for (int c = 0; c < HC; c += 16) {
+        for (int t = 0; t < NA; ++t) {
           float v[16];
-          tc_ld16(tbase + ((uint32_t)(sub * 32) << 16) + (j * NA + t) * BN + chalf * HC + c, v);
+          tc_ld16(lane_base + (j * NA + t) * BN + chalf * HC + c, v);
           tc_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 16; ++e) acc[t][c + e] += v[e];
+          for (int e = 0; e < 16; ++e) acc[t][e] += v[e];
         }
-    }
-    tc_fence_before();
-
-    const int tile = m_tile * gridDim.x + n_tile;
-    bool final_cta = true;
-    if (a.splits > 1) {
-      float* mine = a.part + ((size_t)tile * a.splits + split) * NA * kTcRows * BN;
-#pragma unroll
-      for (int t = 0; t < NA; ++t)
-#pragma unroll
-        for (int jj = 0; jj < HC; ++jj) mine[(t * BN + chalf * HC + jj) * kTcRows + row] = acc[t][jj];
-      __threadfence();
-      producers_sync();
-      if (pid == 0) is_last = atomicAdd(a.counters + tile, 1) == a.splits - 1;
-      producers_sync();
-      final_cta = is_last;
-      if (final_cta) {
-        __threadfence();
-        // sum every split in split order (the same bits whichever CTA finishes last)
-#pragma unroll
-        for (int t = 0; t < NA; ++t)
-#pragma unroll
-          for (int jj = 0; jj < HC; ++jj) acc[t][jj] = 0.f;
-        for (int sp = 0; sp < a.splits; ++sp) {
-          const float* p = a.part + ((size_t)tile * a.splits + sp) * NA * kTcRows * BN;
-#pragma unroll
-          for (int t = 0; t < NA; ++t)
-#pragma unroll
-            for (int jj = 0; jj < HC; ++jj) acc[t][jj] += __ldcg(p + (t * BN + chalf * HC + jj) * kTcRows + row);
-        }
-        if (pid == 0) a.counters[tile] = 0;
       }
-    }
-    if (final_cta) {
-      const int n = n0 + row;
+    };
+    const int n = n0 + row;
+    auto store_chunk = [&](int c, const float (&acc)[NA][16]) {
 #pragma unroll
-      for (int jj = 0; jj < HC; ++jj) {
-        const int tok = m0 + chalf * HC + jj;
+      for (int jj = 0; jj < 16; ++jj) {
+        const int tok = m0 + chalf * HC + c + jj;
         if (tok >= a.M) break;
         const size_t o = (size_t)tok * a.N + n;
         if constexpr (SWIGLU) {
@@ -467,6 +451,51 @@ __global__ void __launch_bounds__(tc_threads(BN, SWIGLU), 1)
             a.y[o] = rv;
           }
         }
+      }
+    };
+    const int tile = m_tile * gridDim.x + n_tile;
+    if (a.splits == 1) {
+      for (int c = 0; c < HC; c += 16) {
+        if (m0 + chalf * HC + c >= a.M) break;  // no token of this chunk exists
+        float acc[NA][16];
+        load_chunk(c, acc);
+        store_chunk(c, acc);
+      }
+      tc_fence_before();
+    } else {
+      float* mine = a.part + ((size_t)tile * a.splits + split) * NA * kTcRows * BN;
+      for (int c = 0; c < HC; c += 16) {
+        float acc[NA][16];
+        load_chunk(c, acc);
+#pragma unroll
+        for (int t = 0; t < NA; ++t)
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) mine[(t * BN + chalf * HC + c + jj) * kTcRows + row] = acc[t][jj];
+      }
+      tc_fence_before();
+      __threadfence();
+      producers_sync();
+      if (pid == 0) is_last = atomicAdd(a.counters + tile, 1) == a.splits - 1;
+      producers_sync();
+      if (is_last) {
+        __threadfence();
+        // sum every split in split order (the same bits whichever CTA finishes last)
+        for (int c = 0; c < HC; c += 16) {
+          float acc[NA][16];
+#pragma unroll
+          for (int t = 0; t < NA; ++t)
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) acc[t][jj] = 0.f;
+          for (int sp = 0; sp < a.splits; ++sp) {
+            const float* p = a.part + ((size_t)tile * a.splits + sp) * NA * kTcRows * BN;
+#pragma unroll
+            for (int t = 0; t < NA; ++t)
+#pragma unroll
+              for (int jj = 0; jj < 16; ++jj) acc[t][jj] += __ldcg(p + (t * BN + chalf * HC + c + jj) * kTcRows + row);
+          }
+          store_chunk(c, acc);
+        }
+        if (pid == 0) a.counters[tile] = 0;
       }
     }
   }
@@ -653,7 +682,7 @@ int g_tc_waves = 2;
 int g_tc_wave_cost = 8;
 
 int tc_splits(int M, int K, int N) {
-  const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  const int BN = tc_bn(M, N);
   const long long tiles = (long long)(N / kTcRows) * ((M + BN - 1) / BN);
   const int G = K / 64;
   if (tiles == 0 || M < 1 || tiles > kTcMaxTiles) return 1;  // no tile, or beyond the counters
@@ -692,7 +721,7 @@ bool qgemm_tc_supported(const QLinArgs& a) {
 size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu) {
   (void)K;
   (void)N;
-  const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : 128);
+  const int BN = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));  // the widest tile M may use
   return kTcCounterBytes +
          (size_t)g_tc_waves * tc_sms() * (swiglu ? 2 : 1) * kTcRows * BN * sizeof(float);
 }
@@ -700,7 +729,7 @@ size_t qgemm_tc_workspace(int M, int K, int N, bool swiglu) {
 cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!qgemm_tc_supported(q)) return cudaErrorInvalidValue;
   const bool swiglu = epi == EPI_SWIGLU;
-  const int BN = q.M <= 32 ? 32 : (q.M <= 64 ? 64 : 128);
+  const int BN = tc_bn(q.M, q.N);
   CUtensorMap map;
   if (!x_tensor_map(q.x, q.M, q.K, BN, &map)) return cudaErrorInvalidValue;
   TcArgs a{};
@@ -749,11 +778,13 @@ cudaError_t launch_qgemm_tc(const QLinArgs& q, int epi, void* ws, size_t ws_byte
   if (swiglu) {
     if (BN == 32) return launch_bn<32, true>(map, wm, a, grid, st);
     if (BN == 64) return launch_bn<64, true>(map, wm, a, grid, st);
-    return launch_bn<128, true>(map, wm, a, grid, st);
+    if (BN == 128) return launch_bn<128, true>(map, wm, a, grid, st);
+    return launch_bn<256, true>(map, wm, a, grid, st);
   }
   if (BN == 32) return launch_bn<32, false>(map, wm, a, grid, st);
   if (BN == 64) return launch_bn<64, false>(map, wm, a, grid, st);
-  return launch_bn<128, false>(map, wm, a, grid, st);
+  if (BN == 128) return launch_bn<128, false>(map, wm, a, grid, st);
+  return launch_bn<256, false>(map, wm, a, grid, st);
 }
 
 void set_gemm_tc_waves(int w) { g_tc_waves = w < 1 ? 1 : (w > 8 ? 8 : w); }
