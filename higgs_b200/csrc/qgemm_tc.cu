@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(tc_threads(BN, SWIGLU), 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < AS; ++i) {
-      mbar_init(&full_bar[i], kTcProducers / 32);  // one arrival per producer warp
+      mbar_init(&full_bar[i], kTcProducers);
       mbar_init(&empty_bar[i], NA);  // one commit per operand tile's warp
     }
     for (int i = 0; i < XS; ++i) {
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(tc_threads(BN, SWIGLU), 1)
     }
     for (int i = 0; i < kPkStages; ++i) {
       mbar_init(&pk_full[i], 1);
-      mbar_init(&pk_empty[i], kTcProducers / 32);
+      mbar_init(&pk_empty[i], kTcProducers);
     }
     mbar_init(&done_bar, NMW);  // one final commit per MMA warp
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -400,15 +400,9 @@ __global__ void __launch_bounds__(tc_threads(BN, SWIGLU), 1)
         }
         // release the packed slot only once its words have been consumed: the refill is an
         // async-proxy (TMA) write, which the barrier does not order behind a load in flight
-        // one arrival per warp on each barrier (256 arrivals per stage on one word serialize):
-        // every lane fences its own stores for the async proxy, __syncwarp orders the lanes'
-        // reads and fenced writes before lane 0's arrivals
+        mbar_arrive(&pk_empty[ps]);
         fence_proxy_async();
-        __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&pk_empty[ps]);
-          mbar_arrive(&full_bar[slot]);
-        }
+        mbar_arrive(&full_bar[slot]);
         if (i + kRing < nst) fetch_sb(i + kRing, d);
       }
     }
