@@ -34,6 +34,7 @@ namespace higgs {
 constexpr int kAttnThreads = 128;
 constexpr int kCounterBytes = 4096;
 constexpr int kTargetCtas = 2 * 148;
+constexpr int kTargetCtasTq4 = 3 * 148;  // the swapped-role TurboQuant kernel: three per SM
 constexpr int kTq4Stages = 6;  // per-warp page ring of the TurboQuant kernel (a pair + 4 in flight)
 
 struct AttnArgs {
@@ -1129,6 +1130,335 @@ __global__ void __launch_bounds__(kAttnThreads) paged_attn_tq4_kernel(AttnArgs a
   attn_epilogue<D, MT>(a, m, l, o, smem_f, b, h, split, R, fin);
 }
 
+// TurboQuant decode with the MMA roles swapped, for launches of at most 4 query rows (one
+// token of a GQA group of 4 or fewer heads -- C5's decode).  The kernel above puts the
+// query rows on the 16-row side of m16n8k16, so 12 of its 16 rows are padding, and splits
+// q' into hi + lo halves on separate MMAs.  Here the keys are the 16 rows: a page's scores
+// are S^T = K q'^T with the 8 columns holding the rows' hi halves (columns 0-3) and lo
+// halves (columns 4-7) of q', so one MMA per 16 d does what took eight; the output is
+// O^T = V^T P^T with the head dimension on the rows (8 MMAs per page instead of 16), P^T
+// formed from the score fragments by lane shuffles.  Accumulators: 32 registers of O^T and
+// 16 of q' instead of 64 and 64.  Same page ring, masking and epilogue as the kernel above;
+// V is expanded to 128 + c and the offset removed once per row (results differ from the
+// kernel above only in f32 summation order).
+template <int S>
+__global__ void __launch_bounds__(kAttnThreads, 3) paged_attn_tq4_swap_kernel(AttnArgs a) {
+  constexpr int D = 128;
+  constexpr int STAGE_BYTES = 1024 + 1024 + 32 + 32;
+  constexpr int WARP_BYTES = S * STAGE_BYTES + 2 * 16 * D * 2;  // + two V tiles
+  // smem: qsum [4] | pad | qrot [4][128] f32 | per warp: S stages + two V tiles
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  float* qsum = reinterpret_cast<float*>(smem_raw);
+  float* qrot = qsum + 32;
+  uint8_t* wbase = reinterpret_cast<uint8_t*>(qrot + 4 * D);
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int G = a.Hq / a.Hkv;
+  const int R = G * a.lq_chunk;  // <= 4
+
+  const int L = a.seq_lens[b];
+  const int n_pages = min((L + 15) / 16, a.max_blocks);
+  const int pg0 = split * a.pages_per_split;
+  const int pg1 = min(n_pages, pg0 + a.pages_per_split);
+  uint8_t* my = wbase + warp * WARP_BYTES;
+  auto kcb = [&](int st) { return my + st * STAGE_BYTES; };
+  auto vcb = [&](int st) { return my + st * STAGE_BYTES + 1024; };
+  auto ksb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2048); };
+  auto vsb = [&](int st) { return reinterpret_cast<__half*>(my + st * STAGE_BYTES + 2080); };
+  auto issue = [&](int pg, int st) {
+    const int pid = a.bt[(size_t)b * a.max_blocks + pg];
+    const size_t off = (size_t)pid * a.page_stride + (size_t)h * a.head_stride;
+    const size_t soff = (size_t)pid * (a.page_stride / 64) + (size_t)h * (a.head_stride / 64);
+    const int valid = min(16, L - pg * 16);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int qd = lane + 32 * i;  // 64 chunks of 16 B = 16 rows x 64 B
+      const int r = qd >> 2;
+      const int bytes = r < valid ? 16 : 0;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(kcb(st) + qd * 16)),
+                   "l"(a.kcode + off + qd * 16), "r"(bytes));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vcb(st) + qd * 16)),
+                   "l"(a.vcode + off + qd * 16), "r"(bytes));
+    }
+    if (lane < 2) {
+      const int bytes = (lane * 8 < valid) ? 16 : 0;  // each 16 B chunk = 8 scales
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(ksb(st) + lane * 8)),
+                   "l"(a.kscale + soff + lane * 8), "r"(bytes));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(vsb(st) + lane * 8)),
+                   "l"(a.vscale + soff + lane * 8), "r"(bytes));
+    }
+  };
+  // the first PRO pages of this warp into the ring; pages holding only tokens of earlier
+  // steps are fetched before the dependency wait
+  constexpr int PRO = S - 2;
+  int pre = 0;
+  const int old_end = L - a.Lq;
+  for (; pre < PRO; ++pre) {
+    const int pgs = pg0 + warp + 4 * pre;
+    if (pgs >= pg1 || (pgs + 1) * 16 > old_end) break;
+    issue(pgs, pre);
+    cp_async_commit();
+  }
+  pdl_wait();
+  for (; pre < PRO; ++pre) {
+    const int pgs = pg0 + warp + 4 * pre;
+    if (pgs < pg1) issue(pgs, pre);
+    cp_async_commit();
+  }
+
+  // rotate the query rows (warp w: row w): q' = R q; the scores use its hi + lo bf16 halves
+  // and the code offset correction their exact sum
+  {
+    const int row = warp;
+    float f[4] = {0.f, 0.f, 0.f, 0.f};
+    if (row < R) {
+      const int tq = a.tq0 + row / G, hq = h * G + row % G;
+      const uint16_t* qp = a.q + (((size_t)b * a.Lq + tq) * a.Hq + hq) * D;
+      f[0] = bf2f(qp[2 * lane]);
+      f[1] = bf2f(qp[2 * lane + 1]);
+      f[2] = bf2f(qp[64 + 2 * lane]);
+      f[3] = bf2f(qp[65 + 2 * lane]);
+      tq_rotate_lane(f, a.signs, lane);
+    }
+    float sum = 0.0f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float hi = round_bf(f[e]);
+      sum += hi + round_bf(f[e] - hi);
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) qsum[row] = sum;
+    float* dst = qrot + row * D;
+    dst[2 * lane] = f[0];
+    dst[2 * lane + 1] = f[1];
+    dst[64 + 2 * lane] = f[2];
+    dst[65 + 2 * lane] = f[3];
+  }
+  __syncthreads();
+  // B fragments of q'^T in the code-nibble k order of the K codes (k-step kt, lane (g, t):
+  // lo = 32t + 8(kt>>1) + 2(kt&1), k rows 2t, 2t+1 <-> d lo, lo+4 and 2t+8, 2t+9 <-> lo+1,
+  // lo+5); column g is row g's hi half (g < 4) or row g-4's lo half, zero past R
+  uint32_t qb[8][2];
+  {
+    const int row = g & 3;
+    const bool use_lo = g >= 4;
+    const float* r = qrot + row * D;
+#pragma unroll
+    for (int kt = 0; kt < 8; ++kt) {
+      const int lo = 32 * t + 8 * (kt >> 1) + 2 * (kt & 1);
+      uint32_t h0, l0, h1, l1;
+      split_bf2(r[lo], r[lo + 4], h0, l0);
+      split_bf2(r[lo + 1], r[lo + 5], h1, l1);
+      qb[kt][0] = row < R ? (use_lo ? l0 : h0) : 0u;
+      qb[kt][1] = row < R ? (use_lo ? l1 : h1) : 0u;
+    }
+  }
+  // this lane's score columns after the hi + lo fold: rows ra = 2(t & 1) and ra + 1
+  const int ra = 2 * (t & 1);
+  const float qs0 = qsum[ra], qs1 = qsum[ra + 1];
+  const int qpos0 = L - a.Lq + a.tq0 + ra / G, qpos1 = L - a.Lq + a.tq0 + (ra + 1) / G;
+  float o[D / 16][4];  // O^T: tile d2 = rows d 16 d2 + g (+8), columns = query rows 2t, 2t + 1
+#pragma unroll
+  for (int d2 = 0; d2 < D / 16; ++d2)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) o[d2][c] = 0.0f;
+  float mr[2] = {-INFINITY, -INFINITY}, lr[2] = {0.0f, 0.0f};  // rows ra, ra + 1
+  float pr[2] = {0.0f, 0.0f};  // sum of the bf16 P x V-scale weights this lane fed the MMA
+
+  uint16_t* vtile0 = reinterpret_cast<uint16_t*>(my + S * STAGE_BYTES);
+  uint16_t* vtile1 = vtile0 + 16 * D;
+  auto expand_v = [&](int st, uint16_t* vtile) {
+    // V codes to the exact bf16 128 + c (the offset 136 of the dequantized c - 8 comes off
+    // once per row at the end); lane -> token lane/2, half lane&1, its 16-byte chunks visited
+    // in an order staggered by token pair and half so that neither the code reads nor the
+    // swizzled tile writes of a quarter-warp share a bank
+    const int r = lane >> 1, hlf = lane & 1;
+    const uint4* src = reinterpret_cast<const uint4*>(vcb(st) + r * 64 + hlf * 32);
+#pragma unroll
+    for (int v4i = 0; v4i < 2; ++v4i) {
+      const int v4 = v4i ^ ((r >> 1) & 1);
+      const uint4 w4 = src[v4];
+      const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int wi0 = 0; wi0 < 4; ++wi0) {
+        const uint32_t w = hlf ? ws[wi0 ^ 2] : ws[wi0];
+        const int chunk = hlf * 8 + v4 * 4 + (wi0 ^ (2 * hlf));
+        *reinterpret_cast<uint4*>(vtile + r * D + swz(r, chunk) * 8) =
+            make_uint4(nib_pair_bf16<0>(w), nib_pair_bf16<4>(w), nib_pair_bf16<8>(w), nib_pair_bf16<12>(w));
+      }
+    }
+  };
+
+  int j = 0;  // this warp's local page index (the pair j, j + 1)
+  for (int pg = pg0 + warp; pg < pg1; pg += 8, j += 2) {
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {  // refill the slots the previous pair released
+      const int p2 = pg + 4 * (PRO + u);
+      if (p2 < pg1) issue(p2, (j + PRO + u) % S);
+      cp_async_commit();
+    }
+    cp_async_wait<PRO>();  // pages j and j + 1 have landed
+    __syncwarp();
+    const int st0 = j % S, st1 = (j + 1) % S;
+    const int pgp[2] = {pg, pg + 4};
+    expand_v(st0, vtile0);
+    expand_v(st1, vtile1);
+    __syncwarp();
+    // scores S^T of both pages: sc[pp][c], c = 0 (key g, row ra), 1 (key g, row ra + 1),
+    // 2 (key g + 8, row ra), 3 (key g + 8, row ra + 1)
+    float sc[2][4], vs[2][2];
+#pragma unroll
+    for (int pp = 0; pp < 2; ++pp) {
+      const int st = pp ? st1 : st0;
+      const int valid = pgp[pp] < pg1 ? min(16, L - pgp[pp] * 16) : 0;
+      const uint8_t* kc = kcb(st);
+      const uint4 kv0 = *reinterpret_cast<const uint4*>(kc + g * 64 + 16 * t);
+      const uint4 kv1 = *reinterpret_cast<const uint4*>(kc + (g + 8) * 64 + 16 * t);
+      const uint32_t k0[4] = {kv0.x, kv0.y, kv0.z, kv0.w}, k1[4] = {kv1.x, kv1.y, kv1.z, kv1.w};
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int kt = 0; kt < 8; ++kt) {
+        const uint32_t w0 = k0[kt >> 1], w1 = k1[kt >> 1];
+        const uint32_t a0 = (kt & 1) ? nib_pair_bf16<8>(w0) : nib_pair_bf16<0>(w0);
+        const uint32_t a2 = (kt & 1) ? nib_pair_bf16<12>(w0) : nib_pair_bf16<4>(w0);
+        const uint32_t a1 = (kt & 1) ? nib_pair_bf16<8>(w1) : nib_pair_bf16<0>(w1);
+        const uint32_t a3 = (kt & 1) ? nib_pair_bf16<12>(w1) : nib_pair_bf16<4>(w1);
+        mma_bf16_16816(acc, a0, a1, a2, a3, qb[kt][0], qb[kt][1]);
+      }
+      // the lo-half columns (lanes t ^ 2) onto the hi-half ones: every lane gets rows ra, ra + 1
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[c] += __shfl_xor_sync(0xffffffffu, acc[c], 2);
+      const __half* ks = ksb(st);
+      const __half* vsp = vsb(st);
+      const float kg = g < valid ? __half2float(ks[g]) : 0.0f;
+      const float kg8 = g + 8 < valid ? __half2float(ks[g + 8]) : 0.0f;
+      vs[pp][0] = g < valid ? __half2float(vsp[g]) : 0.0f;
+      vs[pp][1] = g + 8 < valid ? __half2float(vsp[g + 8]) : 0.0f;
+      const int key0 = pgp[pp] * 16 + g, key1 = key0 + 8;
+      const bool inpg = pgp[pp] < pg1;
+      sc[pp][0] = (ra < R && key0 <= qpos0 && inpg) ? (acc[0] - 136.0f * qs0) * kg * a.scale_log2 : -INFINITY;
+      sc[pp][1] = (ra + 1 < R && key0 <= qpos1 && inpg) ? (acc[1] - 136.0f * qs1) * kg * a.scale_log2 : -INFINITY;
+      sc[pp][2] = (ra < R && key1 <= qpos0 && inpg) ? (acc[2] - 136.0f * qs0) * kg8 * a.scale_log2 : -INFINITY;
+      sc[pp][3] = (ra + 1 < R && key1 <= qpos1 && inpg) ? (acc[3] - 136.0f * qs1) * kg8 * a.scale_log2 : -INFINITY;
+    }
+    // online softmax per query row (a column of S^T): the maximum over the 32 keys of the
+    // pair lives across the 8 lanes g of a column pair
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float mx = fmaxf(fmaxf(sc[0][r], sc[0][r + 2]), fmaxf(sc[1][r], sc[1][r + 2]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mn = fmaxf(mr[r], mx);
+      alpha[r] = (mn == -INFINITY) ? 1.0f : exp2f(mr[r] - mn);
+      mr[r] = mn;
+      float rs = 0.0f;
+#pragma unroll
+      for (int pp = 0; pp < 2; ++pp)
+#pragma unroll
+        for (int e = r; e < 4; e += 2) {
+          float& v = sc[pp][e];
+          v = (mn == -INFINITY) ? 0.0f : exp2f(v - mn);
+          rs += v;
+        }
+      lr[r] = lr[r] * alpha[r] + rs;  // this lane's keys; summed over the lanes at the end
+      pr[r] *= alpha[r];
+    }
+#pragma unroll
+    for (int d2 = 0; d2 < D / 16; ++d2) {
+      o[d2][0] *= alpha[0];
+      o[d2][2] *= alpha[0];
+      o[d2][1] *= alpha[1];
+      o[d2][3] *= alpha[1];
+    }
+    // O^T += V^T P^T per page: P (times the key's V scale, rounded to bf16) gathered into the
+    // B fragment of lane (g, t) = column row g, keys 2t, 2t + 1 | 2t + 8, 2t + 9, from the
+    // lanes (2t, g/2) and (2t + 1, g/2) that hold those keys' scores
+#pragma unroll
+    for (int pp = 0; pp < 2; ++pp) {
+      const uint32_t pk0 = pack_bf2(sc[pp][0] * vs[pp][0], sc[pp][1] * vs[pp][0]);
+      const uint32_t pk1 = pack_bf2(sc[pp][2] * vs[pp][1], sc[pp][3] * vs[pp][1]);
+      pr[0] += bf_lo(pk0) + bf_lo(pk1);
+      pr[1] += bf_hi(pk0) + bf_hi(pk1);
+      const int rr = g & 3;
+      const int l1 = (2 * t) * 4 + (rr >> 1), l2 = (2 * t + 1) * 4 + (rr >> 1);
+      const uint32_t u0 = __shfl_sync(0xffffffffu, pk0, l1), u1 = __shfl_sync(0xffffffffu, pk0, l2);
+      const uint32_t u2 = __shfl_sync(0xffffffffu, pk1, l1), u3 = __shfl_sync(0xffffffffu, pk1, l2);
+      const uint32_t sel = (rr & 1) ? 0x7632u : 0x5410u;
+      const uint32_t pb0 = g < R ? prmt(u0, u1, sel) : 0u;
+      const uint32_t pb1 = g < R ? prmt(u2, u3, sel) : 0u;
+      const uint16_t* vt = pp ? vtile1 : vtile0;
+      const int mi = lane >> 3;
+      const int tok = (mi & 1) * 8 + (lane & 7);
+#pragma unroll
+      for (int d2 = 0; d2 < D / 16; ++d2) {
+        uint32_t vb[4];
+        ldmatrix_x4_trans(vb, vt + tok * D + swz(tok, 2 * d2 + (mi >> 1)) * 8);
+        mma_bf16_16816(o[d2], vb[0], vb[2], vb[1], vb[3], pb0, pb1);
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  pdl_launch();
+
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    lr[r] += __shfl_xor_sync(0xffffffffu, lr[r], 4);
+    lr[r] += __shfl_xor_sync(0xffffffffu, lr[r], 8);
+    lr[r] += __shfl_xor_sync(0xffffffffu, lr[r], 16);
+    pr[r] += __shfl_xor_sync(0xffffffffu, pr[r], 4);
+    pr[r] += __shfl_xor_sync(0xffffffffu, pr[r], 8);
+    pr[r] += __shfl_xor_sync(0xffffffffu, pr[r], 16);
+  }
+  // the MMAs saw V as 128 + c: O^T[d][row] -= 136 * (the weights of that row)
+#pragma unroll
+  for (int d2 = 0; d2 < D / 16; ++d2) {
+    o[d2][0] -= 136.0f * pr[0];
+    o[d2][2] -= 136.0f * pr[0];
+    o[d2][1] -= 136.0f * pr[1];
+    o[d2][3] -= 136.0f * pr[1];
+  }
+  // to the kernel above's fragment layout (rows = query rows) through this warp's ring
+  float* ot = reinterpret_cast<float*>(my);  // [4][D] O rows | m [4] | l [4]
+  __syncwarp();
+  if (t < 2) {
+#pragma unroll
+    for (int d2 = 0; d2 < D / 16; ++d2) {
+      const int d = 16 * d2 + g;
+      ot[(2 * t) * D + d] = o[d2][0];
+      ot[(2 * t + 1) * D + d] = o[d2][1];
+      ot[(2 * t) * D + d + 8] = o[d2][2];
+      ot[(2 * t + 1) * D + d + 8] = o[d2][3];
+    }
+    if (g == 0) {
+      ot[4 * D + 2 * t] = mr[0];
+      ot[4 * D + 2 * t + 1] = mr[1];
+      ot[4 * D + 4 + 2 * t] = lr[0];
+      ot[4 * D + 4 + 2 * t + 1] = lr[1];
+    }
+  }
+  __syncwarp();
+  float m[1][2], l[1][2], os[1][D / 8][4];
+  const bool vrow = g < R;
+  m[0][0] = vrow ? ot[4 * D + g] : -INFINITY;
+  m[0][1] = -INFINITY;
+  l[0][0] = (vrow && t == 0) ? ot[4 * D + 4 + g] : 0.0f;  // the epilogue sums l over t
+  l[0][1] = 0.0f;
+#pragma unroll
+  for (int dt = 0; dt < D / 8; ++dt) {
+    os[0][dt][0] = vrow ? ot[g * D + 8 * dt + 2 * t] : 0.0f;
+    os[0][dt][1] = vrow ? ot[g * D + 8 * dt + 2 * t + 1] : 0.0f;
+    os[0][dt][2] = 0.0f;
+    os[0][dt][3] = 0.0f;
+  }
+  float* smem_f = reinterpret_cast<float*>(wbase);  // rings are dead now
+  FinishTq4 fin{&a};
+  attn_epilogue<D, 1>(a, m, l, os, smem_f, b, h, split, R, fin);
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -1136,7 +1466,8 @@ struct SplitPlan {
   int splits, pps, rows_pad, lq_chunk, chunks;
 };
 
-static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len, int min_pps = 4) {
+static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len, int min_pps = 4,
+                            int target = kTargetCtas) {
   SplitPlan p;
   const int G = Hq / Hkv;
   // query tokens per launch so that G * chunk <= 32 rows
@@ -1147,7 +1478,7 @@ static SplitPlan plan_split(int B, int Lq, int Hq, int Hkv, int max_seq_len, int
   // as many splits as keep every CTA in one resident wave (two per SM): a partial
   // second wave costs more than longer splits (measured on B200, Qwen3-8B shapes at
   // ctx 2048: B=8 3.35 vs 3.72 ms per decode step, B=32 7.99 vs 8.44)
-  int want = kTargetCtas / (B * Hkv);
+  int want = target / (B * Hkv);
   if (want < 1) want = 1;
   if (want > 128) want = 128;
   // at least min_pps pages (one per warp) per split (measured: capping the pages per
@@ -1184,6 +1515,10 @@ static size_t smem_tq4(int MT) {
   return head + body;
 }
 
+static size_t smem_tq4_swap(int S) {
+  return (size_t)32 * 4 + (size_t)4 * 128 * 4 + (size_t)4 * (S * (1024 + 1024 + 32 + 32) + 2 * 16 * 128 * 2);
+}
+
 constexpr int kFusedStages = 3;
 // pages per split of the fused kernel: two per warp by default, so the prefetch
 // issued before the grid dependency wait covers a whole split (tunable through
@@ -1198,6 +1533,10 @@ static int g_attn_cluster = 16;
 // the default: within the same tolerance of the oracle, C5 step 18.7 -> 17.2 ms on a B200)
 static bool g_tq4_p_lo = false;
 void attention_set_tq4_p_lo(int on) { g_tq4_p_lo = on != 0; }
+// TurboQuant launches of at most 4 query rows: the swapped-role kernel with this many ring
+// stages per warp (4 or 6), or 0 for the kernel with the query rows on the MMA's 16 rows
+static int g_tq4_swap = 4;
+void attention_set_tq4_swap(int n) { g_tq4_swap = n >= 6 ? 6 : (n >= 4 ? 4 : 0); }
 void attention_set_cluster(int n) { g_attn_cluster = n >= 16 ? 16 : (n >= 8 ? 8 : (n >= 2 ? n : 0)); }
 
 static size_t smem_fused(int D, int MT, int Lq) {
@@ -1224,6 +1563,8 @@ static cudaError_t attention_prepare_device() {
   set(paged_attn_tq4_kernel<2>, smem_tq4(2));
   set(paged_attn_tq4_kernel<1, false>, smem_tq4(1));
   set(paged_attn_tq4_kernel<2, false>, smem_tq4(2));
+  set(paged_attn_tq4_swap_kernel<4>, smem_tq4_swap(4));
+  set(paged_attn_tq4_swap_kernel<6>, smem_tq4_swap(6));
   set(fused_attn_bf16_kernel<64, 1, kFusedStages>, smem_fused(64, 1, 32));
   set(fused_attn_bf16_kernel<64, 2, kFusedStages>, smem_fused(64, 2, 32));
   set(fused_attn_bf16_kernel<128, 1, kFusedStages>, smem_fused(128, 1, 32));
@@ -1266,8 +1607,11 @@ using namespace higgs;
 extern "C" size_t higgs_paged_attention_workspace_size(int B, int Lq, int Hq, int Hkv, int D,
                                                        int max_seq_len) {
   if (B <= 0 || Lq <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv) return 0;
-  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
-  return attn_ws_bytes(p, B, Hkv, D);
+  // the larger of the two split plans (the TurboQuant swapped-role kernel keeps three CTAs
+  // per SM resident), so one workspace serves either kernel
+  const size_t a = attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len), B, Hkv, D);
+  const size_t b = attn_ws_bytes(plan_split(B, Lq, Hq, Hkv, max_seq_len, 4, kTargetCtasTq4), B, Hkv, D);
+  return a > b ? a : b;
 }
 
 extern "C" size_t higgs_paged_attention_tq4_workspace_size(int B, int Lq, int Hq, int Hkv,
@@ -1351,7 +1695,9 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
   HG_CHECK_ARG(page_stride % 64 == 0 && head_stride % 64 == 0,
                "higgs_paged_attention_tq4: strides must be multiples of 64 bytes");
   HG_DEVICE(ctx);
-  const SplitPlan p = plan_split(B, Lq, Hq, Hkv, max_seq_len);
+  const SplitPlan p0 = plan_split(B, Lq, Hq, Hkv, max_seq_len);
+  const bool swap = !g_tq4_p_lo && g_tq4_swap && (Hq / Hkv) * p0.lq_chunk <= 4;
+  const SplitPlan p = swap ? plan_split(B, Lq, Hq, Hkv, max_seq_len, 4, kTargetCtasTq4) : p0;
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
                          attn_ws_bytes(p, B, Hkv, 128), workspace);
   if (rc) return rc;
@@ -1381,7 +1727,10 @@ extern "C" int higgs_paged_attention_tq4(higgs_ctx* ctx, const void* q, int B, i
   cudaStream_t st = (cudaStream_t)stream;
   const int MT = p.rows_pad / 16;
   cudaError_t e;
-  if (g_tq4_p_lo)
+  if (swap)
+    e = g_tq4_swap == 6 ? launch_attn(paged_attn_tq4_swap_kernel<6>, smem_tq4_swap(6), a, p, st)
+                        : launch_attn(paged_attn_tq4_swap_kernel<4>, smem_tq4_swap(4), a, p, st);
+  else if (g_tq4_p_lo)
     e = MT == 1 ? launch_attn(paged_attn_tq4_kernel<1>, smem_tq4(1), a, p, st)
                 : launch_attn(paged_attn_tq4_kernel<2>, smem_tq4(2), a, p, st);
   else

@@ -62,6 +62,7 @@ void qgemv_tma_set(int on);
 void attention_set_cluster(int n);
 void model_set_tp_fuse(int on);
 void attention_set_tq4_p_lo(int on);
+void attention_set_tq4_swap(int n);
 
 }  // namespace higgs
 
@@ -100,6 +101,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
+    return HIGGS_OK;
+  }
+  if (n == "tq4_swap") {
+    attention_set_tq4_swap(value);
     return HIGGS_OK;
   }
   if (n == "tq4_p_lo") {

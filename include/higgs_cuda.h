@@ -128,7 +128,10 @@ int higgs_version(void);
  * cluster the splits of one (sequence, kv head) of the fused decode attention
  * form to merge through distributed shared memory (0: workspace merge by the
  * last CTA).  "tq4_p_lo" (0/1, default 0): TurboQuant attention multiplies V by
- * P's hi + lo bf16 halves (1) instead of its bf16 rounding (0).  "tp_fuse" (0/1,
+ * P's hi + lo bf16 halves (1) instead of its bf16 rounding (0).  "tq4_swap" (0, 4
+ * or 6, default 4): TurboQuant launches of at most 4 query rows run the kernel
+ * with the keys on the MMA's 16 rows and that many page-ring stages per warp
+ * (0: the kernel with the query rows there).  "tp_fuse" (0/1,
  * default 0): one-token tensor-parallel decode sums the row-parallel partials
  * inside the GEMVs (pushed by the producing GEMV, pulled by the next fused-norm
  * GEMV) instead of all-reduce launches.

@@ -377,19 +377,24 @@ def test_tq4_kv_write_bit_exact():
         assert np.array_equal(vsc[p, :, s].cpu().numpy().view(np.uint16), sv.view(np.uint16))
 
 
-@pytest.mark.parametrize("p_lo", [1, 0])
+@pytest.mark.parametrize("variant", ["swap4", "swap6", "rows16", "p_lo"])
 @pytest.mark.parametrize("B,Lq,Hq,Hkv,lens", [(1, 1, 32, 8, [1]), (2, 1, 32, 8, [2048, 77]),
                                              (3, 1, 16, 8, [16, 500, 33]), (2, 6, 32, 8, [300, 64]),
-                                             (1, 1, 32, 4, [4096])])
-def test_paged_attention_tq4(B, Lq, Hq, Hkv, lens, p_lo):
-    """Against the oracle within the TurboQuant attention bound, with P x V on P's hi + lo
-    bf16 halves (tq4_p_lo 1) and on its bf16 rounding only (0)."""
+                                             (1, 1, 32, 4, [4096]), (2, 2, 16, 8, [40, 1000])])
+def test_paged_attention_tq4(B, Lq, Hq, Hkv, lens, variant):
+    """Against the oracle within the TurboQuant attention bound: launches of at most 4 query
+    rows on the swapped-role kernel (4 or 6 ring stages, the default 4), or on the kernel with
+    the query rows on the MMA's 16 rows (tq4_swap 0), with P x V on P's bf16 rounding, and
+    that kernel with P's hi + lo halves (tq4_p_lo 1)."""
     from higgs_b200 import ffi
+    swap, p_lo = {"swap4": (4, 0), "swap6": (6, 0), "rows16": (0, 0), "p_lo": (4, 1)}[variant]
+    ffi.call("higgs_set_option", b"tq4_swap", swap)
     ffi.call("higgs_set_option", b"tq4_p_lo", p_lo)
     try:
         _tq4_attention_case(B, Lq, Hq, Hkv, lens)
     finally:
-        ffi.call("higgs_set_option", b"tq4_p_lo", 0)  # the default
+        ffi.call("higgs_set_option", b"tq4_p_lo", 0)  # the defaults
+        ffi.call("higgs_set_option", b"tq4_swap", 4)
 
 
 def _tq4_attention_case(B, Lq, Hq, Hkv, lens):
