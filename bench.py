@@ -64,7 +64,7 @@ def parse():
                     help="library tuning switch name=value (higgs_set_option), repeatable")
     ap.add_argument("--kernel-case", default=None,
                     help="run one small kernel case for ncu: qkv|o_proj|gate_up_swiglu|down|lm_head[:tokens]"
-                         "|attention|argmax")
+                         "|attention|attention_tq4|argmax|tc_rate|decode_eager:<batch>")
     return ap.parse_args()
 
 
@@ -482,6 +482,11 @@ def kernel_case(opt):
         for it in range(3):
             for kc, ks, vc, vs in caches:
                 ops.paged_attention_tq4(q, kc, ks, vc, vs, bt, sl, L, signs, workspace=ws)
+    elif case == "decode_eager":  # three decode steps of the bench model at batch M, launches not in a graph
+        model, eng, Sequence, _ = setup_model(a, [M], opt.ctx, 8, dev)
+        seqs = make_seqs(eng, Sequence, M, opt.ctx, a.vocab_size)
+        eng.use_graph = False
+        eng.decode_steps(seqs, 3)
     elif case == "tc_rate":  # tensor-core issue rate behind the matrix-form W4 matmul
         rows = []
         for m in (128, 64):
