@@ -64,7 +64,7 @@ def parse():
                     help="library tuning switch name=value (higgs_set_option), repeatable")
     ap.add_argument("--kernel-case", default=None,
                     help="run one small kernel case for ncu: qkv|o_proj|gate_up_swiglu|down|lm_head[:tokens]"
-                         "|attention|attention_tq4|argmax|tc_rate|decode_eager:<batch>")
+                         "|attention|attention_tq4|prefill_attn|argmax|tc_rate|decode_eager:<batch>")
     return ap.parse_args()
 
 
@@ -163,6 +163,71 @@ def peaks():
             d = json.load(f)
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def bf16_peak():
+    """Dense bf16 TFLOP/s (burst: the kernels below are timed alone) and where it came from."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+def prefill_case(a, L, dev, copies=1):
+    """One prompt chunk of L tokens of the bench model's attention shape over a paged cache
+    holding exactly those L tokens (query t at position t): q, caches, block table, lengths."""
+    import torch
+    Hq, Hkv, D = a.num_attention_heads, a.num_key_value_heads, a.head_dim
+    P = (L + 15) // 16
+    q = torch.randn(1, L, Hq, D, device=dev).to(torch.bfloat16)
+    caches = [(torch.randn(P, Hkv, 16, D, device=dev).to(torch.bfloat16),
+               torch.randn(P, Hkv, 16, D, device=dev).to(torch.bfloat16)) for _ in range(copies)]
+    bt = torch.arange(P, dtype=torch.int32, device=dev).view(1, P)
+    sl = torch.tensor([L], dtype=torch.int32, device=dev)
+    return q, caches, bt, sl
+
+
+def prefill_attn_roofline(a, dev, lengths=(2048, 8192)):
+    """Causal prefill attention of one prompt chunk (the bench model's heads), one launch of
+    the tcgen05 kernel against the mma.sync decode kernel's 32-row chunks (option
+    attn_prefill_tc 0) on the same inputs.  FLOPs: 4 * Hq * D * (L (L + 1) / 2) (QK^T and PV
+    over the causal triangle)."""
+    import torch
+
+    from higgs_b200 import ffi
+    from higgs_b200 import ops
+    peak, kind = bf16_peak()
+    Hq, Hkv, D = a.num_attention_heads, a.num_key_value_heads, a.head_dim
+    rows = []
+    for L in lengths:
+        q, caches, bt, sl = prefill_case(a, L, dev)
+        kc, vc = caches[0]
+        ws = ops.attention_workspace(1, L, Hq, Hkv, D, L, dev)
+        flops = 4.0 * Hq * D * (L * (L + 1) / 2)
+
+        def timed(reps):
+            for _ in range(3):
+                ops.paged_attention(q, kc, vc, bt, sl, L, workspace=ws)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                ops.paged_attention(q, kc, vc, bt, sl, L, workspace=ws)
+            e1.record()
+            e1.synchronize()
+            return e0.elapsed_time(e1) * 1e3 / reps
+        us = timed(20)
+        ffi.call("higgs_set_option", b"attn_prefill_tc", 0)
+        try:
+            us_old = timed(3)
+        finally:
+            ffi.call("higgs_set_option", b"attn_prefill_tc", 1)
+        rows.append({"prompt_tokens": L, "us": round(us, 1), "tflops": round(flops / us / 1e6, 1),
+                     "frac": round(flops / us / 1e6 / peak, 4), "us_mma_sync_chunks": round(us_old, 1)})
+        del q, caches, kc, vc, ws
+        torch.cuda.empty_cache()
+    return {"kernel": "prefill_attn_tc_kernel<%d> (causal, Hq %d / Hkv %d)" % (D, Hq, Hkv),
+            "bound": "tensor", "peak": peak, "peak_kind": kind, "unit": "TFLOP/s", "per_length": rows}
 
 
 # ---------------------------------------------------------------------------------------------
@@ -464,6 +529,13 @@ def kernel_case(opt):
             for kc, vc in caches:
                 ops.fused_attention(qkv, Hq, Hkv, D, qn, qn, a.rms_norm_eps, pos, inv, slots, kc, vc, bt,
                                     sl, L)
+    elif case == "prefill_attn":  # one prompt chunk of --ctx tokens on the tcgen05 prefill kernel
+        L = opt.ctx
+        q, caches, bt, sl = prefill_case(a, L, dev, copies=2)
+        ws = ops.attention_workspace(1, L, a.num_attention_heads, a.num_key_value_heads, a.head_dim, L, dev)
+        for it in range(3):
+            for kc, vc in caches:
+                ops.paged_attention(q, kc, vc, bt, sl, L, workspace=ws)
     elif case == "attention_tq4":  # C5 shapes: B=16, ctx 32768, TurboQuant pages
         B, Hq, Hkv, L = 16, a.num_attention_heads, a.num_key_value_heads, 32768
         maxb = L // 16
@@ -958,6 +1030,8 @@ def run_ours(opt):
             out["chain_roofline"] = {"kernel": "chain_kernel (o_proj + gate/up + down + next q|k|v)",
                                      "achieved": round(cb / cus / 1e3, 1), "frac": round(cb / cus / 1e3 / hbm, 4),
                                      "algorithmic_bytes": cb, "us_per_launch": round(cus, 2)}
+        if ws == 1:
+            out["prefill_attention"] = prefill_attn_roofline(a, device)
         sb = by_batch[str(B)]["step_bytes"]
         out["step_roofline"] = {"bytes_per_step": sb, "achieved_gbs": round(sb / (step_ms / 1e3) / 1e9, 1),
                                 "peak": hbm, "frac": by_batch[str(B)]["step_hbm_frac"]}

@@ -27,6 +27,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kernels.cuh"
 #include "timeline.cuh"
 
 namespace higgs {
@@ -1648,6 +1649,13 @@ extern "C" int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int L
   int rc = validate_attn(B, Lq, Hq, Hkv, max_blocks, max_seq_len, workspace_bytes,
                          attn_ws_bytes(p, B, Hkv, D), workspace);
   if (rc) return rc;
+  if (prefill_attn_tc_fits(Lq, Hq, Hkv, D, q, k_cache, v_cache, out, page_stride, head_stride)) {
+    // prefill chunks: 128-row query tiles on the tensor cores, one launch, no workspace
+    HG_CUDA(launch_prefill_attn_tc(q, B, Lq, Hq, Hkv, D, k_cache, v_cache, page_stride, head_stride,
+                                   block_table, max_blocks, seq_lens, scale, out, tc_err_ptr(),
+                                   (cudaStream_t)stream));
+    return HIGGS_OK;
+  }
   AttnArgs a = {};
   a.q = (const uint16_t*)q;
   a.B = B;

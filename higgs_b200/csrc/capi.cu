@@ -63,6 +63,7 @@ void attention_set_cluster(int n);
 void model_set_tp_fuse(int on);
 void attention_set_tq4_p_lo(int on);
 void attention_set_tq4_swap(int n);
+void prefill_attn_tc_set(int on);
 
 }  // namespace higgs
 
@@ -101,6 +102,10 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
+    return HIGGS_OK;
+  }
+  if (n == "attn_prefill_tc") {
+    prefill_attn_tc_set(value);
     return HIGGS_OK;
   }
   if (n == "tq4_swap") {

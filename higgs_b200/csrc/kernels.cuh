@@ -210,4 +210,13 @@ struct SkArgs {
 size_t qgemv_sk_workspace(int M, int K, int n_tiles);
 cudaError_t launch_qgemv_sk(SkArgs a, void* workspace, cudaStream_t st);
 
+// prefill_attn.cu: causal paged attention of prefill chunks on the tcgen05 tensor cores
+bool prefill_attn_tc_fits(int Lq, int Hq, int Hkv, int D, const void* q, const void* kc, const void* vc,
+                          const void* out, int64_t page_stride, int64_t head_stride);
+cudaError_t launch_prefill_attn_tc(const void* q, int B, int Lq, int Hq, int Hkv, int D, const void* kc,
+                                   const void* vc, int64_t page_stride, int64_t head_stride, const int32_t* bt,
+                                   int max_blocks, const int32_t* seq_lens, float scale, void* out, int* err,
+                                   cudaStream_t st);
+int* tc_err_ptr();
+
 }  // namespace higgs

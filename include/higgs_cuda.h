@@ -134,7 +134,11 @@ int higgs_version(void);
  * (0: the kernel with the query rows there).  "tp_fuse" (0/1,
  * default 0): one-token tensor-parallel decode sums the row-parallel partials
  * inside the GEMVs (pushed by the producing GEMV, pulled by the next fused-norm
- * GEMV) instead of all-reduce launches.
+ * GEMV) instead of all-reduce launches.  "attn_prefill_tc" (0/1, default 1):
+ * higgs_paged_attention launches of more than 64 query rows (Hq / Hkv x Lq; G =
+ * Hq / Hkv dividing 128, 16-byte aligned buffers and strides) run the tcgen05
+ * prefill kernel (128-row tiles of tokens x GQA heads, S and O in tensor memory)
+ * instead of the decode kernel's 32-row query chunks.
  * Unknown names return HIGGS_ERR_INVALID_ARG. */
 int higgs_set_option(const char* name, int value);
 
@@ -308,7 +312,8 @@ int higgs_qknorm_rope_kv_write(higgs_ctx* ctx, const void* qkv, int T, int Hq, i
 
 /* fast::scaled_dot_product_attention with GQA (crates/higgs-models/src/utils.rs:45-60)
  * and the masks of utils.rs:64-125, over a paged KV cache.
- *   q   bf16 [B, Lq, Hq, D] (D = 64 or 128; Hq / Hkv * Lq <= 64)
+ *   q   bf16 [B, Lq, Hq, D] (D = 64 or 128; launches of more than 64 query rows,
+ *       Hq / Hkv * Lq, run the tensor-core prefill kernel: option "attn_prefill_tc")
  *   query t of sequence b sits at position seq_lens[b] - Lq + t and attends
  *   to keys 0..that position (causal, includes itself).
  *   block_table int32 [B, max_blocks]; page p of the cache holds key/value

@@ -271,6 +271,39 @@ def test_paged_attention(B, Lq, Hq, Hkv, D, lens):
     assert np.array_equal(a1, a2)
 
 
+@pytest.mark.parametrize("B,Lq,Hq,Hkv,D,lens", [
+    (1, 128, 32, 8, 128, [128]),         # a whole prompt in one chunk
+    (1, 300, 32, 8, 128, [300]),         # a partial last query tile and key block
+    (2, 200, 16, 8, 128, [200, 1000]),   # a chunk after 800 cached tokens
+    (1, 512, 32, 8, 128, [512]),
+    (2, 96, 16, 16, 64, [96, 130]),      # G = 1, D = 64
+    (1, 40, 32, 4, 128, [2100]),         # G = 8, deep into the context
+    (3, 17, 32, 8, 64, [17, 40, 333]),   # 68 rows: the smallest launch the kernel takes
+])
+def test_prefill_attention_tc(B, Lq, Hq, Hkv, D, lens):
+    """Launches of more than 64 query rows run the tcgen05 prefill kernel (128-row tiles of
+    tokens x GQA heads, S and O in tensor memory): against the oracle, against the mma.sync
+    decode kernel on the same inputs (option attn_prefill_tc 0), and run to run."""
+    from higgs_b200 import ffi
+    rng = np.random.default_rng(B * 11 + Lq + D + sum(lens))
+    q, kc, vc, bt, sl = _paged_case(rng, B, Lq, Hq, Hkv, D, lens)
+    ref = orc.bf16_to_f32(orc.paged_attention(q, kc, vc, bt, sl))
+    o = ops()
+    args = (bf(q), bf(kc), bf(vc), t(bt), t(sl), max(lens))
+    got = to_np_bf(o.paged_attention(*args))
+    np.testing.assert_allclose(orc.bf16_to_f32(got), ref, atol=1e-2, rtol=1e-2)
+    assert np.array_equal(got, to_np_bf(o.paged_attention(*args)))
+    ffi.call("higgs_set_option", b"attn_prefill_tc", 0)
+    try:
+        old = to_np_bf(o.paged_attention(*args))
+    finally:
+        ffi.call("higgs_set_option", b"attn_prefill_tc", 1)
+    np.testing.assert_allclose(orc.bf16_to_f32(got), orc.bf16_to_f32(old), atol=1e-2, rtol=1e-2)
+    v = ctypes.c_int(-1)
+    ffi.call("higgs_tc_error", ffi.ctx(0), ctypes.byref(v))
+    assert v.value == 0
+
+
 def test_paged_attention_golden(golden):
     g = golden
     got = ops().paged_attention(bf(g["at_q"]), bf(g["at_k"]), bf(g["at_v"]), t(g["at_bt"]),
