@@ -15,9 +15,11 @@
 //   * 1 MMA warp, one lane: S_j = Q K_j^T (M = 128 rows, N = 128 keys, K = D) into one of two
 //     TMEM buffers, then O += P_{j-1} V_{j-1} (M = 128, N = D, K = 128 keys) with P read from
 //     TMEM, so S_j is computed while the softmax of block j - 1 runs;
-//   * 4 softmax warps, thread = query row = TMEM lane: the causal mask, the running maximum and
-//     sum in the exp2 domain, P as bf16 into TMEM, and the rescale of O in TMEM when a row's
-//     maximum grew; at the end O / l as bf16.
+//   * 8 softmax warps, two threads per query row (TMEM lane), one per half of the block's keys,
+//     exchanging the block maximum through shared memory: the causal mask, the running maximum
+//     and sum in the exp2 domain, P as bf16 into TMEM, and the rescale of O in TMEM (each
+//     thread half of the row's columns) when a row's maximum grew by more than 2^8; at the end
+//     O / l as bf16.
 // Tiles with the longest key ranges are scheduled first.  TMEM is allocated after
 // griddepcontrol.wait.  Every mbarrier wait is bounded (about 2 s; the first timeout makes the
 // CTA's other waits give up too, and sets the flag higgs_tc_error reports).
@@ -31,9 +33,9 @@ namespace {
 
 constexpr int kPfRows = 128;     // query rows per CTA (UMMA M)
 constexpr int kPfKeys = 128;     // keys per block (N of S, K of P V)
-constexpr int kPfSoftmax = 128;  // warps 0-3: one thread per row / TMEM lane
-constexpr int kPfMmaWarp = 4;
-constexpr int kPfLoaders = 128;  // warps 5-8
+constexpr int kPfSoftmax = 256;  // warps 0-7: warp w takes rows (TMEM lanes) 32 (w % 4).., keys half w / 4
+constexpr int kPfMmaWarp = 8;
+constexpr int kPfLoaders = 128;  // warps 9-12
 constexpr int kPfThreads = kPfSoftmax + 32 + kPfLoaders;
 constexpr int kPfTmemCols = 512;
 constexpr int pf_stages(int D) { return D == 128 ? 3 : 4; }
@@ -85,6 +87,22 @@ __device__ __forceinline__ bool pf_wait(uint64_t* bar, unsigned parity, volatile
   *abort = 1;
   atomicExch(err, 1);
   return false;
+}
+
+// 2^x (PTX ex2.approx, flush-to-zero: 2^x for x <= -126 is 0, which P rounds to anyway)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The running maximum m of a row moves only when a block's maximum exceeds it by more than
+// kPfSlack (log2 units): P = 2^(s - m) then stays below 2^kPfSlack and O is rescaled in TMEM
+// for only a few blocks.  O / l is the same softmax whatever m is.
+constexpr float kPfSlack = 8.0f;
+
+__device__ __forceinline__ void pf_pair_sync(int quarter) {  // warps q and q + 4 (one row quarter)
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -226,77 +244,92 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     }
     __syncwarp();
   } else {
-    // ---------------- softmax: thread = query row = TMEM lane ----------------
-    const int r = threadIdx.x;
+    // ---------------- softmax: thread = (query row = TMEM lane, half hf of the keys) ----------------
+    // [half][row]: block maxima, then the sums (a second pair barrier after each read keeps the
+    // next write behind the partner's read: the dynamic shared memory leaves 2 KB for this)
+    __shared__ float xch[2][kPfRows];
+    const int quarter = warp & 3, hf = warp >> 2;
+    const int r = quarter * 32 + lane;
     const int t = t0 + r / G;
     const bool valid = t < t_end;
     const int pos = valid ? pos0 + t : -1;  // keys 0 .. pos are visible
-    const uint32_t lrow = tb + ((uint32_t)(warp * 32) << 16);
-    float m = -INFINITY, l = 0.f;
+    const uint32_t lrow = tb + ((uint32_t)(quarter * 32) << 16);
+    constexpr int HK = kPfKeys / 2;  // keys (S columns) per thread
+    constexpr int HD = D / 2;        // O columns rescaled / stored per thread
+    float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
     for (int j = 0; j < nkb; ++j) {
       const int sb = j & 1;
       pf_wait(&s_full[sb], (j >> 1) & 1, abort, a.err);
       tc_fence_after();
-      float v[kPfKeys];
+      float v[HK];
 #pragma unroll
-      for (int c = 0; c < kPfKeys / 16; ++c) tc_ld16(lrow + COL_S + sb * kPfKeys + 16 * c, v + 16 * c);
+      for (int c = 0; c < HK / 16; ++c) tc_ld16(lrow + COL_S + sb * kPfKeys + hf * HK + 16 * c, v + 16 * c);
       tc_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[sb]);  // S buffer sb may take S_{j+2}
-      const int lim = pos - j * kPfKeys;  // key i of the block is visible iff i <= lim
-      float mx = -INFINITY;
+      const int lim = pos - j * kPfKeys - hf * HK;  // key i of this half is visible iff i <= lim
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < kPfKeys; ++i) {
+      for (int i = 0; i < HK; ++i) {
         v[i] = i <= lim ? v[i] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, v[i]);
+        mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
       }
-      const float mn = fmaxf(m, mx);
-      const float alpha = (mn == -INFINITY) ? 1.f : exp2f(m - mn);
-      float sum = 0.f;
-      uint32_t pk[kPfKeys / 2];
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      xch[hf][r] = mx;
+      pf_pair_sync(quarter);
+      mx = fmaxf(mx, xch[hf ^ 1][r]);  // the block maximum of the whole row
+      pf_pair_sync(quarter);
+      // both threads of a row take the same decision from the same (m, mx)
+      const bool grow = mx > m + kPfSlack || (m == -INFINITY && mx != -INFINITY);
+      const float alpha = grow ? ex2(m - mx) : 1.f;  // m = -inf: 0 (O and l are still zero)
+      if (grow) m = mx;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[HK / 2];
 #pragma unroll
-      for (int i = 0; i < kPfKeys / 2; ++i) {
-        const float p0 = (mn == -INFINITY) ? 0.f : exp2f(v[2 * i] - mn);
-        const float p1 = (mn == -INFINITY) ? 0.f : exp2f(v[2 * i + 1] - mn);
-        sum += p0 + p1;
+      for (int i = 0; i < HK / 2; ++i) {
+        const float p0 = m == -INFINITY ? 0.f : ex2(v[2 * i] - m);
+        const float p1 = m == -INFINITY ? 0.f : ex2(v[2 * i + 1] - m);
+        sum4[i & 3] += p0 + p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
-      l = l * alpha + sum;
-      m = mn;
+      l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
       if (j >= 1) {  // P_{j-1} V_{j-1} has finished with P and O
         pf_wait(&pv_done, (j - 1) & 1, abort, a.err);
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll
-          for (int c = 0; c < D / 16; ++c) {
+          for (int c = 0; c < HD / 16; ++c) {
             float o[16];
-            tc_ld16(lrow + COL_O + 16 * c, o);
+            tc_ld16(lrow + COL_O + hf * HD + 16 * c, o);
             tc_wait_ld();
             uint32_t w[16];
 #pragma unroll
             for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
-            tc_st16(lrow + COL_O + 16 * c, w);
+            tc_st16(lrow + COL_O + hf * HD + 16 * c, w);
           }
         }
       }
 #pragma unroll
-      for (int c = 0; c < kPfKeys / 32; ++c) tc_st16(lrow + COL_P + 16 * c, pk + 16 * c);
+      for (int c = 0; c < HK / 32; ++c) tc_st16(lrow + COL_P + hf * (HK / 2) + 16 * c, pk + 16 * c);
       tc_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full);
     }
-    // ---- O / l -> bf16 ----
+    // ---- O / l -> bf16 (this thread: columns [hf D / 2, (hf + 1) D / 2) of its row) ----
+    xch[hf][r] = l;
+    pf_pair_sync(quarter);
+    const float lt = hf == 0 ? l + xch[1][r] : xch[0][r] + l;  // l0 + l1 in both
     if (nkb > 0) {
       pf_wait(&pv_done, (nkb - 1) & 1, abort, a.err);
       tc_fence_after();
     }
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    uint16_t* dst = a.out + (((size_t)b * a.Lq + (valid ? t : 0)) * a.Hq + hkv * G + r % G) * D;
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    uint16_t* dst = a.out + (((size_t)b * a.Lq + (valid ? t : 0)) * a.Hq + hkv * G + r % G) * D + hf * HD;
 #pragma unroll
-    for (int c = 0; c < D / 16; ++c) {
+    for (int c = 0; c < HD / 16; ++c) {
       float o[16];
       if (nkb > 0) {
-        tc_ld16(lrow + COL_O + 16 * c, o);
+        tc_ld16(lrow + COL_O + hf * HD + 16 * c, o);
         tc_wait_ld();
       } else {
 #pragma unroll
