@@ -187,26 +187,44 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     fence_proxy_async();  // generic-proxy writes -> the tensor core's (async proxy) reads
     mbar_arrive(&q_full);
     const int32_t* btr = a.bt + (size_t)b * a.max_blocks;
+    // this thread's 16-byte column dc of keys k0, k0 + KSTEP, ... of every block
+    constexpr int KSTEP = kPfLoaders / DC, KPT = kPfKeys / KSTEP;
+    const int dc = lt % DC, k0 = lt / DC;
+    const size_t col = (size_t)hkv * a.head_stride + dc * 8;
+    const uint32_t so0 = (dc >> 3) * (kPfKeys * 128) + (((dc & 7) ^ (k0 & 7)) << 4);  // KSTEP % 8 == 0
+    // block j is released once block j + 1 is in flight (wait for all but the newest copy
+    // group): with S >= 3 stages the release never waits on a stage that needs it
+    static_assert(S >= 3 && KSTEP % 8 == 0, "loader pipeline");
     for (int j = 0; j < nkb; ++j) {
       const int s = j % S;
       if (j >= S) pf_wait(&kv_empty[s], ((j / S) - 1) & 1, abort, a.err);
       uint8_t* ks = kvs + (size_t)s * 2 * kKV;
       uint8_t* vs = ks + kKV;
-      for (int e = lt; e < kPfKeys * DC; e += kPfLoaders) {
-        const int key = e / DC, dc = e % DC;
-        const int kg = j * kPfKeys + key;
-        const bool ok = kg < kv_len;
-        size_t off = 0;
-        if (ok)
-          off = (size_t)btr[kg >> 4] * a.page_stride + (size_t)hkv * a.head_stride + (size_t)(kg & 15) * D + dc * 8;
-        const uint32_t so = (dc >> 3) * (kPfKeys * 128) + key * 128 + (((dc & 7) ^ (key & 7)) << 4);
-        cp_async16_zfill(ks + so, a.kc + off, ok);
-        cp_async16_zfill(vs + so, a.vc + off, ok);
+      int pg[KPT];
+#pragma unroll
+      for (int i = 0; i < KPT; ++i) {
+        const int kg = j * kPfKeys + k0 + i * KSTEP;
+        pg[i] = kg < kv_len ? btr[kg >> 4] : -1;
+      }
+#pragma unroll
+      for (int i = 0; i < KPT; ++i) {
+        const int kg = j * kPfKeys + k0 + i * KSTEP;
+        const size_t off = pg[i] >= 0 ? (size_t)pg[i] * a.page_stride + col + (size_t)(kg & 15) * D : 0;
+        const uint32_t so = so0 + (k0 + i * KSTEP) * 128;
+        cp_async16_zfill(ks + so, a.kc + off, pg[i] >= 0);
+        cp_async16_zfill(vs + so, a.vc + off, pg[i] >= 0);
       }
       cp_async_commit();
+      if (j >= 1) {
+        cp_async_wait<1>();
+        fence_proxy_async();  // generic-proxy writes -> the tensor core's (async proxy) reads
+        mbar_arrive(&kv_full[(j - 1) % S]);
+      }
+    }
+    if (nkb > 0) {
       cp_async_wait<0>();
       fence_proxy_async();
-      mbar_arrive(&kv_full[s]);
+      mbar_arrive(&kv_full[(nkb - 1) % S]);
     }
   } else if (warp == kPfMmaWarp) {
     // ---------------- MMA issue (one lane) ----------------
@@ -269,12 +287,18 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
       mbar_arrive(&s_free[sb]);  // S buffer sb may take S_{j+2}
       const int lim = pos - j * kPfKeys - hf * HK;  // key i of this half is visible iff i <= lim
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (lim >= HK - 1) {  // every key of this half visible: no mask
 #pragma unroll
-      for (int i = 0; i < HK; ++i) {
-        v[i] = i <= lim ? v[i] * a.scale_log2 : -INFINITY;
-        mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
+        for (int i = 0; i < HK; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < HK; ++i) {
+          v[i] = i <= lim ? v[i] : -INFINITY;
+          mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
+        }
       }
-      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      // raw scores: the scale (> 0) is applied to the maximum and folded into the exponent's FMA
+      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
       xch[hf][r] = mx;
       pf_pair_sync(quarter);
       mx = fmaxf(mx, xch[hf ^ 1][r]);  // the block maximum of the whole row
@@ -287,8 +311,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
       uint32_t pk[HK / 2];
 #pragma unroll
       for (int i = 0; i < HK / 2; ++i) {
-        const float p0 = m == -INFINITY ? 0.f : ex2(v[2 * i] - m);
-        const float p1 = m == -INFINITY ? 0.f : ex2(v[2 * i + 1] - m);
+        const float p0 = m == -INFINITY ? 0.f : ex2(fmaf(v[2 * i], a.scale_log2, -m));
+        const float p1 = m == -INFINITY ? 0.f : ex2(fmaf(v[2 * i + 1], a.scale_log2, -m));
         sum4[i & 3] += p0 + p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
