@@ -12,9 +12,10 @@
 //   * 4 loader warps: 16-byte cp.async copies of the block's pages of K and V (zero-filled past
 //     the keys the tile can see) into 128-byte-swizzled shared tiles with the keys as rows,
 //     which is K-major for S = Q K^T and MN-major for O += P V; a 3-stage ring (4 at D = 64);
-//   * 1 MMA warp, one lane: S_j = Q K_j^T (M = 128 rows, N = 128 keys, K = D) into one of two
-//     TMEM buffers, then O += P_{j-1} V_{j-1} (M = 128, N = D, K = 128 keys) with P read from
-//     TMEM, so S_j is computed while the softmax of block j - 1 runs;
+//   * 2 MMA warps, one issuing lane each: S_j = Q K_j^T (M = 128 rows, N = 128 keys, K = D) into
+//     one of two TMEM buffers, and O += P_j V_j (M = 128, N = D, K = 128 keys) with P read from
+//     one of two TMEM buffers, so S_{j+1} is computed while the softmax of block j runs and the
+//     softmax waits for P V only where it rescales O;
 //   * 8 softmax warps, two threads per query row (TMEM lane), one per half of the block's keys,
 //     exchanging the block maximum through shared memory: the causal mask, the running maximum
 //     and sum in the exp2 domain, P as bf16 into TMEM, and the rescale of O in TMEM (each
@@ -33,10 +34,13 @@ namespace {
 
 constexpr int kPfRows = 128;     // query rows per CTA (UMMA M)
 constexpr int kPfKeys = 128;     // keys per block (N of S, K of P V)
-constexpr int kPfSoftmax = 256;  // warps 0-7: warp w takes rows (TMEM lanes) 32 (w % 4).., keys half w / 4
-constexpr int kPfMmaWarp = 8;
-constexpr int kPfLoaders = 128;  // warps 9-12
-constexpr int kPfThreads = kPfSoftmax + 32 + kPfLoaders;
+// NG softmax threads per query row: warps 0 .. 4 NG - 1, warp w takes rows (TMEM lanes)
+// 32 (w % 4).. and key group w / 4 (kPfKeys / NG keys of each block, D / NG columns of O);
+// then two MMA-issuing warps (S = Q K^T; O += P V), then the loader warps
+constexpr int pf_softmax(int NG) { return 128 * NG; }
+constexpr int pf_mma_warp(int NG) { return 4 * NG; }
+constexpr int kPfLoaders = 128;
+constexpr int pf_threads(int NG) { return pf_softmax(NG) + 64 + kPfLoaders; }  // + 2 MMA warps
 constexpr int kPfTmemCols = 512;
 constexpr int pf_stages(int D) { return D == 128 ? 3 : 4; }
 constexpr uint32_t pf_q_bytes(int D) { return (uint32_t)kPfRows * D * 2; }
@@ -45,6 +49,7 @@ constexpr size_t pf_smem(int D) { return 1024 + pf_q_bytes(D) + (size_t)pf_stage
 static_assert(pf_smem(128) <= 227 * 1024 && pf_smem(64) <= 227 * 1024, "shared memory budget");
 
 bool g_prefill_tc = true;
+int g_prefill_ng = 2;  // softmax threads per query row (2 or 4)
 
 struct PfArgs {
   const uint16_t* q;
@@ -101,8 +106,17 @@ __device__ __forceinline__ float ex2(float x) {
 // for only a few blocks.  O / l is the same softmax whatever m is.
 constexpr float kPfSlack = 8.0f;
 
-__device__ __forceinline__ void pf_pair_sync(int quarter) {  // warps q and q + 4 (one row quarter)
-  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+// the NG softmax warps of one row quarter (warps q, q + 4, ...)
+__device__ __forceinline__ void pf_group_sync(int quarter, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(nthreads) : "memory");
+}
+
+// x rounded up to a bf16 (toward +inf), as its bits: the threads of a row exchange block maxima
+// this way, and all of them take the maximum of the same rounded values
+__device__ __forceinline__ uint16_t bf16_up(float x) {
+  uint32_t u = __float_as_uint(x);
+  if ((u & 0xFFFFu) != 0 && (u >> 31) == 0) u += 0x10000u;  // positive and inexact: next bf16 up
+  return (uint16_t)(u >> 16);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -110,13 +124,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int D>
-__global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a) {
+template <int D, int NG>
+__global__ void __launch_bounds__(pf_threads(NG), 1) prefill_attn_tc_kernel(PfArgs a) {
+  constexpr int kPfSoftmax = pf_softmax(NG), kPfMmaWarp = pf_mma_warp(NG);
   constexpr int S = pf_stages(D);
   constexpr uint32_t kQ = pf_q_bytes(D), kKV = pf_kv_bytes(D);
   constexpr int DC = D / 8;  // 16-byte chunks per row
-  // TMEM columns: S double buffer, P (bf16 pairs), O
-  constexpr int COL_S = 0, COL_P = 2 * kPfKeys, COL_O = COL_P + kPfKeys / 2;
+  // TMEM columns: S double buffer, P double buffer (bf16 pairs), O
+  constexpr int COL_S = 0, COL_P = 2 * kPfKeys, COL_O = COL_P + kPfKeys;
   static_assert(COL_O + D <= kPfTmemCols, "TMEM columns");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -127,8 +142,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
   __shared__ __align__(8) uint64_t kv_empty[S];
   __shared__ __align__(8) uint64_t s_full[2];
   __shared__ __align__(8) uint64_t s_free[2];
-  __shared__ __align__(8) uint64_t p_full;
-  __shared__ __align__(8) uint64_t pv_done;
+  __shared__ __align__(8) uint64_t p_full[2];
+  __shared__ __align__(8) uint64_t pv_done[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -150,8 +165,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kPfSoftmax);
     }
-    mbar_init(&p_full, kPfSoftmax);
-    mbar_init(&pv_done, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], kPfSoftmax);
+      mbar_init(&pv_done[i], 1);
+    }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -171,9 +188,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
   const uint32_t tb = tmem_base;
   pdl_launch();
 
-  if (warp > kPfMmaWarp) {
+  if (warp > kPfMmaWarp + 1) {
     // ---------------- loaders ----------------
-    const int lt = threadIdx.x - (kPfSoftmax + 32);
+    const int lt = threadIdx.x - (kPfSoftmax + 64);
     // Q row r = (token t0 + r / G, query head hkv G + r % G)
     for (int e = lt; e < kPfRows * DC; e += kPfLoaders) {
       const int r = e / DC, dc = e % DC;
@@ -227,67 +244,72 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
       mbar_arrive(&kv_full[(nkb - 1) % S]);
     }
   } else if (warp == kPfMmaWarp) {
-    // ---------------- MMA issue (one lane) ----------------
+    // ---------------- S_j = Q K_j^T (one lane) ----------------
+    // A thread issues one tcgen05.mma every ~140 cycles whatever its shape (measured on B200),
+    // about twice the tensor pipe's time for M = 128 x N = 128 x K = 16: QK^T and PV each get
+    // their own issuing warp.  They share no accumulator; P_j (softmax, after S_j completed)
+    // orders S_j before P_j V_j, so the PV warp's commit also covers the K half of a stage.
     if (lane == 0) {
       constexpr uint32_t idS = tc_idesc_bf16(kPfRows, kPfKeys);
-      constexpr uint32_t idO = tc_idesc_bf16(kPfRows, D, true);
       const uint32_t sq = smem_u32(qs);
       pf_wait(&q_full, 0, abort, a.err);
-      for (int j = 0; j <= nkb; ++j) {
-        if (j < nkb) {  // S_j = Q K_j^T
-          const int s = j % S, sb = j & 1;
-          pf_wait(&kv_full[s], (j / S) & 1, abort, a.err);
-          if (j >= 2) pf_wait(&s_free[sb], ((j >> 1) - 1) & 1, abort, a.err);
-          tc_fence_after();
-          const uint32_t sk = smem_u32(kvs + (size_t)s * 2 * kKV);
+      for (int j = 0; j < nkb; ++j) {
+        const int s = j % S, sb = j & 1;
+        pf_wait(&kv_full[s], (j / S) & 1, abort, a.err);
+        if (j >= 2) pf_wait(&s_free[sb], ((j >> 1) - 1) & 1, abort, a.err);
+        tc_fence_after();
+        const uint32_t sk = smem_u32(kvs + (size_t)s * 2 * kKV);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk)
-            tc_mma(tb + COL_S + sb * kPfKeys, sw128_desc(sq + (kk >> 2) * (kPfRows * 128) + (kk & 3) * 32),
-                   sw128_desc(sk + (kk >> 2) * (kPfKeys * 128) + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
-          tc_commit(&s_full[sb]);
-        }
-        if (j >= 1) {  // O += P_{j-1} V_{j-1}
-          const int jp = j - 1, s = jp % S;
-          pf_wait(&p_full, jp & 1, abort, a.err);
-          tc_fence_after();
-          const uint32_t sv = smem_u32(kvs + (size_t)s * 2 * kKV + kKV);
+        for (int kk = 0; kk < D / 16; ++kk)
+          tc_mma(tb + COL_S + sb * kPfKeys, sw128_desc(sq + (kk >> 2) * (kPfRows * 128) + (kk & 3) * 32),
+                 sw128_desc(sk + (kk >> 2) * (kPfKeys * 128) + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
+        tc_commit(&s_full[sb]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPfMmaWarp + 1) {
+    // ---------------- O += P_j V_j (one lane) ----------------
+    if (lane == 0) {
+      constexpr uint32_t idO = tc_idesc_bf16(kPfRows, D, true);
+      for (int jp = 0; jp < nkb; ++jp) {
+        const int s = jp % S;
+        pf_wait(&p_full[jp & 1], (jp >> 1) & 1, abort, a.err);
+        tc_fence_after();
+        const uint32_t sv = smem_u32(kvs + (size_t)s * 2 * kKV + kKV);
 #pragma unroll
-          for (int kk = 0; kk < kPfKeys / 16; ++kk)  // 16 keys = two 8-row atoms = 2 KB
-            tc_mma_ta(tb + COL_O, tb + COL_P + kk * 8, sw128_mn_desc(sv + kk * 2048, kPfKeys * 128), idO,
-                      (jp > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(&pv_done);
-          tc_commit(&kv_empty[s]);
-        }
+        for (int kk = 0; kk < kPfKeys / 16; ++kk)  // 16 keys = two 8-row atoms = 2 KB
+          tc_mma_ta(tb + COL_O, tb + COL_P + (jp & 1) * (kPfKeys / 2) + kk * 8,
+                    sw128_mn_desc(sv + kk * 2048, kPfKeys * 128), idO, (jp > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&pv_done[jp & 1]);
+        tc_commit(&kv_empty[s]);
       }
     }
     __syncwarp();
   } else {
-    // ---------------- softmax: thread = (query row = TMEM lane, half hf of the keys) ----------------
-    // [half][row]: block maxima, then the sums (a second pair barrier after each read keeps the
-    // next write behind the partner's read: the dynamic shared memory leaves 2 KB for this)
-    __shared__ float xch[2][kPfRows];
-    const int quarter = warp & 3, hf = warp >> 2;
+    // ---------------- softmax: thread = (query row = TMEM lane, key group g) ----------------
+    __shared__ uint16_t xch[NG][kPfRows];  // [group][row]: block maxima rounded up to bf16
+    const int quarter = warp & 3, g = warp >> 2;
     const int r = quarter * 32 + lane;
     const int t = t0 + r / G;
     const bool valid = t < t_end;
     const int pos = valid ? pos0 + t : -1;  // keys 0 .. pos are visible
     const uint32_t lrow = tb + ((uint32_t)(quarter * 32) << 16);
-    constexpr int HK = kPfKeys / 2;  // keys (S columns) per thread
-    constexpr int HD = D / 2;        // O columns rescaled / stored per thread
-    float m = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+    constexpr int HK = kPfKeys / NG;  // keys (S columns) per thread
+    constexpr int HD = D / NG;        // O columns rescaled / stored per thread
+    float m = -INFINITY, l = 0.f;  // l: this group's share of the row sum
     for (int j = 0; j < nkb; ++j) {
       const int sb = j & 1;
       pf_wait(&s_full[sb], (j >> 1) & 1, abort, a.err);
       tc_fence_after();
       float v[HK];
 #pragma unroll
-      for (int c = 0; c < HK / 16; ++c) tc_ld16(lrow + COL_S + sb * kPfKeys + hf * HK + 16 * c, v + 16 * c);
+      for (int c = 0; c < HK / 16; ++c) tc_ld16(lrow + COL_S + sb * kPfKeys + g * HK + 16 * c, v + 16 * c);
       tc_wait_ld();
       tc_fence_before();
       mbar_arrive(&s_free[sb]);  // S buffer sb may take S_{j+2}
-      const int lim = pos - j * kPfKeys - hf * HK;  // key i of this half is visible iff i <= lim
+      const int lim = pos - j * kPfKeys - g * HK;  // key i of this group is visible iff i <= lim
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (lim >= HK - 1) {  // every key of this half visible: no mask
+      if (lim >= HK - 1) {  // every key of this group visible: no mask
 #pragma unroll
         for (int i = 0; i < HK; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
       } else {
@@ -297,63 +319,78 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
           mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
         }
       }
-      // raw scores: the scale (> 0) is applied to the maximum and folded into the exponent's FMA
-      float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
-      xch[hf][r] = mx;
-      pf_pair_sync(quarter);
-      mx = fmaxf(mx, xch[hf ^ 1][r]);  // the block maximum of the whole row
-      pf_pair_sync(quarter);
-      // both threads of a row take the same decision from the same (m, mx)
+      // raw scores: the scale (> 0) is applied to the maximum and folded into the exponent's FMA;
+      // the row's block maximum, rounded up to bf16 (an upper bound is all the reference needs)
+      xch[g][r] = bf16_up(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2);
+      pf_group_sync(quarter, 32 * NG);
+      float mx = -INFINITY;
+#pragma unroll
+      for (int q = 0; q < NG; ++q) mx = fmaxf(mx, __uint_as_float((uint32_t)xch[q][r] << 16));
+      pf_group_sync(quarter, 32 * NG);  // every read done before the next block's writes
+      // all threads of a row take the same decision from the same (m, mx)
       const bool grow = mx > m + kPfSlack || (m == -INFINITY && mx != -INFINITY);
       const float alpha = grow ? ex2(m - mx) : 1.f;  // m = -inf: 0 (O and l are still zero)
       if (grow) m = mx;
       float sum4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[HK / 2];
+      if (m == -INFINITY) {  // nothing visible yet in this row
 #pragma unroll
-      for (int i = 0; i < HK / 2; ++i) {
-        const float p0 = m == -INFINITY ? 0.f : ex2(fmaf(v[2 * i], a.scale_log2, -m));
-        const float p1 = m == -INFINITY ? 0.f : ex2(fmaf(v[2 * i + 1], a.scale_log2, -m));
-        sum4[i & 3] += p0 + p1;
-        pk[i] = pack_bf16x2(p0, p1);
+        for (int i = 0; i < HK / 2; ++i) pk[i] = 0u;
+      } else {
+#pragma unroll
+        for (int i = 0; i < HK / 2; ++i) {
+          const float p0 = ex2(fmaf(v[2 * i], a.scale_log2, -m));
+          const float p1 = ex2(fmaf(v[2 * i + 1], a.scale_log2, -m));
+          sum4[i & 3] += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
       }
       l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-      if (j >= 1) {  // P_{j-1} V_{j-1} has finished with P and O
-        pf_wait(&pv_done, (j - 1) & 1, abort, a.err);
+      if (j >= 2) {  // P buffer sb is free once P_{j-2} V_{j-2} is done
+        pf_wait(&pv_done[sb], ((j >> 1) - 1) & 1, abort, a.err);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+      }
+      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {  // a row maximum grew: O *= alpha
+        pf_wait(&pv_done[sb ^ 1], ((j - 1) >> 1) & 1, abort, a.err);  // after P_{j-1} V_{j-1}
+        tc_fence_after();
 #pragma unroll
-          for (int c = 0; c < HD / 16; ++c) {
-            float o[16];
-            tc_ld16(lrow + COL_O + hf * HD + 16 * c, o);
-            tc_wait_ld();
-            uint32_t w[16];
+        for (int c = 0; c < HD / 16; ++c) {
+          float o[16];
+          tc_ld16(lrow + COL_O + g * HD + 16 * c, o);
+          tc_wait_ld();
+          uint32_t w[16];
 #pragma unroll
-            for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
-            tc_st16(lrow + COL_O + hf * HD + 16 * c, w);
-          }
+          for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
+          tc_st16(lrow + COL_O + g * HD + 16 * c, w);
         }
       }
 #pragma unroll
-      for (int c = 0; c < HK / 32; ++c) tc_st16(lrow + COL_P + hf * (HK / 2) + 16 * c, pk + 16 * c);
+      for (int c = 0; c < HK / 32; ++c)
+        tc_st16(lrow + COL_P + sb * (kPfKeys / 2) + g * (HK / 2) + 16 * c, pk + 16 * c);
       tc_wait_st();
       tc_fence_before();
-      mbar_arrive(&p_full);
+      mbar_arrive(&p_full[sb]);
     }
-    // ---- O / l -> bf16 (this thread: columns [hf D / 2, (hf + 1) D / 2) of its row) ----
-    xch[hf][r] = l;
-    pf_pair_sync(quarter);
-    const float lt = hf == 0 ? l + xch[1][r] : xch[0][r] + l;  // l0 + l1 in both
+    // ---- O / l -> bf16 (this thread: columns [g D / NG, (g + 1) D / NG) of its row) ----
     if (nkb > 0) {
-      pf_wait(&pv_done, (nkb - 1) & 1, abort, a.err);
+      pf_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, abort, a.err);
       tc_fence_after();
     }
+    // the row's sum over the groups, in group order, through the K / V ring (every copy into it
+    // and every MMA reading it has completed by now)
+    float* xl = reinterpret_cast<float*>(kvs);
+    xl[g * kPfRows + r] = l;
+    pf_group_sync(quarter, 32 * NG);
+    float lt = 0.f;
+#pragma unroll
+    for (int q = 0; q < NG; ++q) lt += xl[q * kPfRows + r];
     const float inv = lt > 0.f ? 1.f / lt : 0.f;
-    uint16_t* dst = a.out + (((size_t)b * a.Lq + (valid ? t : 0)) * a.Hq + hkv * G + r % G) * D + hf * HD;
+    uint16_t* dst = a.out + (((size_t)b * a.Lq + (valid ? t : 0)) * a.Hq + hkv * G + r % G) * D + g * HD;
 #pragma unroll
     for (int c = 0; c < HD / 16; ++c) {
       float o[16];
       if (nkb > 0) {
-        tc_ld16(lrow + COL_O + hf * HD + 16 * c, o);
+        tc_ld16(lrow + COL_O + g * HD + 16 * c, o);
         tc_wait_ld();
       } else {
 #pragma unroll
@@ -379,20 +416,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
   }
 }
 
-template <int D>
+template <int D, int NG>
 cudaError_t launch_pf(const PfArgs& a, cudaStream_t st) {
-  auto k = prefill_attn_tc_kernel<D>;
+  auto k = prefill_attn_tc_kernel<D, NG>;
   static PerDeviceOnce attr;
   const cudaError_t e =
       attr.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(D)); });
   if (e != cudaSuccess) return e;
   const int TQ = kPfRows / (a.Hq / a.Hkv);
-  return launch_pdl(k, dim3((a.Lq + TQ - 1) / TQ, a.Hkv, a.B), dim3(kPfThreads), pf_smem(D), st, a);
+  return launch_pdl(k, dim3((a.Lq + TQ - 1) / TQ, a.Hkv, a.B), dim3(pf_threads(NG)), pf_smem(D), st, a);
 }
 
 }  // namespace
 
 void prefill_attn_tc_set(int on) { g_prefill_tc = on != 0; }
+void prefill_attn_tc_set_groups(int ng) { g_prefill_ng = ng <= 2 ? 2 : 4; }
 
 // Launches of more than 64 query rows (the decode kernel would take three or more launches of
 // 32 rows, each over every page), G dividing 128, 16-byte aligned rows and pages.
@@ -426,7 +464,8 @@ cudaError_t launch_prefill_attn_tc(const void* q, int B, int Lq, int Hq, int Hkv
   a.scale_log2 = scale * 1.4426950408889634f;
   a.out = (uint16_t*)out;
   a.err = err;
-  return D == 64 ? launch_pf<64>(a, st) : launch_pf<128>(a, st);
+  if (g_prefill_ng == 2) return D == 64 ? launch_pf<64, 2>(a, st) : launch_pf<128, 2>(a, st);
+  return D == 64 ? launch_pf<64, 4>(a, st) : launch_pf<128, 4>(a, st);
 }
 
 }  // namespace higgs

@@ -293,6 +293,12 @@ def test_prefill_attention_tc(B, Lq, Hq, Hkv, D, lens):
     got = to_np_bf(o.paged_attention(*args))
     np.testing.assert_allclose(orc.bf16_to_f32(got), ref, atol=1e-2, rtol=1e-2)
     assert np.array_equal(got, to_np_bf(o.paged_attention(*args)))
+    ffi.call("higgs_set_option", b"attn_prefill_groups", 2)  # two softmax threads per row
+    try:
+        g2 = to_np_bf(o.paged_attention(*args))
+    finally:
+        ffi.call("higgs_set_option", b"attn_prefill_groups", 4)
+    np.testing.assert_allclose(orc.bf16_to_f32(g2), ref, atol=1e-2, rtol=1e-2)
     ffi.call("higgs_set_option", b"attn_prefill_tc", 0)
     try:
         old = to_np_bf(o.paged_attention(*args))
