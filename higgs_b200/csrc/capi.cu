@@ -64,7 +64,6 @@ void model_set_tp_fuse(int on);
 void attention_set_tq4_p_lo(int on);
 void attention_set_tq4_swap(int n);
 void prefill_attn_tc_set(int on);
-void prefill_attn_tc_set_groups(int ng);
 
 }  // namespace higgs
 
@@ -103,10 +102,6 @@ extern "C" int higgs_set_option(const char* name, int value) {
   }
   if (n == "gemv_m1_l1") {
     qgemv_m1_set(-1, -1, -1, -1, -1, value);
-    return HIGGS_OK;
-  }
-  if (n == "attn_prefill_groups") {
-    prefill_attn_tc_set_groups(value);
     return HIGGS_OK;
   }
   if (n == "attn_prefill_tc") {

@@ -6,24 +6,30 @@
 // Attention::forward, crates/higgs-models/src/transformer.rs:246-294).  Behind
 // higgs_paged_attention for launches of more than 64 query rows (G x Lq, G = Hq / Hkv).
 //
-// One CTA takes 128 query rows of one (sequence, kv head) -- TQ = 128 / G consecutive tokens
-// x the G query heads that share the kv head, so every K / V tile serves all of them -- and
-// walks the keys 0 .. its last token's position in blocks of 128 (8 pages):
-//   * 4 loader warps: 16-byte cp.async copies of the block's pages of K and V (zero-filled past
-//     the keys the tile can see) into 128-byte-swizzled shared tiles with the keys as rows,
-//     which is K-major for S = Q K^T and MN-major for O += P V; a 3-stage ring (4 at D = 64);
-//   * 2 MMA warps, one issuing lane each: S_j = Q K_j^T (M = 128 rows, N = 128 keys, K = D) into
-//     one of two TMEM buffers, and O += P_j V_j (M = 128, N = D, K = 128 keys) with P read from
-//     one of two TMEM buffers, so S_{j+1} is computed while the softmax of block j runs and the
-//     softmax waits for P V only where it rescales O;
+// A tile is 128 query rows of one (sequence, kv head) -- TQ = 128 / G consecutive tokens x the
+// G query heads that share the kv head, so every K / V tile serves all of them -- walking the
+// keys 0 .. its last token's position in blocks of 128 (8 pages).  The kernel is persistent:
+// one CTA per SM takes tiles blockIdx.x, + gridDim.x, ..., and every ring runs on across its
+// tiles, so the next tile's Q load and first S = Q K^T overlap the current tile's last blocks
+// and its epilogue.
+//   * 4 loader warps: 16-byte cp.async copies of Q and of each block's pages of K and V (zero-
+//     filled past the keys the tile can see) into 128-byte-swizzled shared tiles with the keys
+//     as rows, which is K-major for S = Q K^T and MN-major for O += P V; a 3-stage ring (4 at
+//     D = 64);
+//   * 2 MMA warps, one issuing lane each: S_J = Q K_J^T (M = 128 rows, N = 128 keys, K = D)
+//     into one of two TMEM S buffers, and O += P_J V_J (M = 128, N = D, K = 128 keys) with P
+//     read from one of two TMEM P buffers, so S_{J+1} is computed while the softmax of block J
+//     runs and the softmax waits for P V only where it rescales O;
 //   * 8 softmax warps, two threads per query row (TMEM lane), one per half of the block's keys,
 //     exchanging the block maximum through shared memory: the causal mask, the running maximum
 //     and sum in the exp2 domain, P as bf16 into TMEM, and the rescale of O in TMEM (each
 //     thread half of the row's columns) when a row's maximum grew by more than 2^8; at the end
-//     O / l as bf16.
-// Tiles with the longest key ranges are scheduled first.  TMEM is allocated after
+//     of a tile O / l as bf16.
+// Tiles with the longest key ranges come first.  TMEM is allocated once, after
 // griddepcontrol.wait.  Every mbarrier wait is bounded (about 2 s; the first timeout makes the
 // CTA's other waits give up too, and sets the flag higgs_tc_error reports).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 #include "tcgen05.cuh"
@@ -34,13 +40,14 @@ namespace {
 
 constexpr int kPfRows = 128;     // query rows per CTA (UMMA M)
 constexpr int kPfKeys = 128;     // keys per block (N of S, K of P V)
-// NG softmax threads per query row: warps 0 .. 4 NG - 1, warp w takes rows (TMEM lanes)
-// 32 (w % 4).. and key group w / 4 (kPfKeys / NG keys of each block, D / NG columns of O);
-// then two MMA-issuing warps (S = Q K^T; O += P V), then the loader warps
-constexpr int pf_softmax(int NG) { return 128 * NG; }
-constexpr int pf_mma_warp(int NG) { return 4 * NG; }
+// Two softmax threads per query row: warps 0-7, warp w takes rows (TMEM lanes) 32 (w % 4)..
+// and key half w / 4 of each block (D / 2 columns of O at the end); warp 8 issues S = Q K^T,
+// warp 9 O += P V; warps 10-13 load.  (Four threads per row measured no faster on B200.)
+constexpr int kPfHalves = 2;
+constexpr int kPfSoftmax = 128 * kPfHalves;
+constexpr int kPfQkWarp = kPfSoftmax / 32, kPfPvWarp = kPfQkWarp + 1;
 constexpr int kPfLoaders = 128;
-constexpr int pf_threads(int NG) { return pf_softmax(NG) + 64 + kPfLoaders; }  // + 2 MMA warps
+constexpr int kPfThreads = kPfSoftmax + 64 + kPfLoaders;
 constexpr int kPfTmemCols = 512;
 constexpr int pf_stages(int D) { return D == 128 ? 3 : 4; }
 constexpr uint32_t pf_q_bytes(int D) { return (uint32_t)kPfRows * D * 2; }
@@ -49,7 +56,6 @@ constexpr size_t pf_smem(int D) { return 1024 + pf_q_bytes(D) + (size_t)pf_stage
 static_assert(pf_smem(128) <= 227 * 1024 && pf_smem(64) <= 227 * 1024, "shared memory budget");
 
 bool g_prefill_tc = true;
-int g_prefill_ng = 2;  // softmax threads per query row (2 or 4)
 
 struct PfArgs {
   const uint16_t* q;
@@ -106,17 +112,9 @@ __device__ __forceinline__ float ex2(float x) {
 // for only a few blocks.  O / l is the same softmax whatever m is.
 constexpr float kPfSlack = 8.0f;
 
-// the NG softmax warps of one row quarter (warps q, q + 4, ...)
-__device__ __forceinline__ void pf_group_sync(int quarter, int nthreads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(1 + quarter), "r"(nthreads) : "memory");
-}
-
-// x rounded up to a bf16 (toward +inf), as its bits: the threads of a row exchange block maxima
-// this way, and all of them take the maximum of the same rounded values
-__device__ __forceinline__ uint16_t bf16_up(float x) {
-  uint32_t u = __float_as_uint(x);
-  if ((u & 0xFFFFu) != 0 && (u >> 31) == 0) u += 0x10000u;  // positive and inexact: next bf16 up
-  return (uint16_t)(u >> 16);
+// the two softmax threads of a row quarter (warps q and q + 4)
+__device__ __forceinline__ void pf_pair_sync(int quarter) {
+  asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -124,9 +122,27 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-template <int D, int NG>
-__global__ void __launch_bounds__(pf_threads(NG), 1) prefill_attn_tc_kernel(PfArgs a) {
-  constexpr int kPfSoftmax = pf_softmax(NG), kPfMmaWarp = pf_mma_warp(NG);
+// Tile i of a launch: query tile nqt - 1 - i / (B Hkv) (the longest causal ranges first) of
+// (sequence, kv head) i % (B Hkv)
+struct PfTile {
+  int b, hkv, t0, t_end, pos0, kv_len, nkb;
+};
+__device__ __forceinline__ PfTile pf_tile(const PfArgs& a, int i, int nqt) {
+  PfTile T;
+  const int TQ = kPfRows / (a.Hq / a.Hkv), bh = a.B * a.Hkv;
+  const int qt = nqt - 1 - i / bh;
+  T.b = (i % bh) / a.Hkv;
+  T.hkv = i % a.Hkv;
+  T.t0 = qt * TQ;
+  T.t_end = min(a.Lq, T.t0 + TQ);              // the tile's tokens [t0, t_end)
+  T.pos0 = a.seq_lens[T.b] - a.Lq;             // position of query token 0
+  T.kv_len = max(0, T.pos0 + T.t_end);         // keys seen by the tile's last token
+  T.nkb = (T.kv_len + kPfKeys - 1) / kPfKeys;  // 128-key blocks
+  return T;
+}
+
+template <int D>
+__global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a) {
   constexpr int S = pf_stages(D);
   constexpr uint32_t kQ = pf_q_bytes(D), kKV = pf_kv_bytes(D);
   constexpr int DC = D / 8;  // 16-byte chunks per row
@@ -135,28 +151,34 @@ __global__ void __launch_bounds__(pf_threads(NG), 1) prefill_attn_tc_kernel(PfAr
   static_assert(COL_O + D <= kPfTmemCols, "TMEM columns");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint8_t* qs = smem;       // [D / 64 panels][128 rows][128 B], 128-byte swizzle
+  uint8_t* qs = smem;        // [D / 64 panels][128 rows][128 B], 128-byte swizzle
   uint8_t* kvs = smem + kQ;  // stage s: K at kvs + 2 s kKV, V after it; [D / 64][128 keys][128 B]
-  __shared__ __align__(8) uint64_t q_full;
+  // Every ring counts blocks J over the CTA's whole tile sequence, so the phases carry across
+  // tiles: q_full / q_empty (the S MMAs of a tile are done with Q) and o_free (the softmax
+  // threads have read a tile's O) have one phase per tile.
+  __shared__ __align__(8) uint64_t q_full, q_empty, o_free;
   __shared__ __align__(8) uint64_t kv_full[S];
   __shared__ __align__(8) uint64_t kv_empty[S];
   __shared__ __align__(8) uint64_t s_full[2];
   __shared__ __align__(8) uint64_t s_free[2];
   __shared__ __align__(8) uint64_t p_full[2];
   __shared__ __align__(8) uint64_t pv_done[2];
+  // [half][row]: block maxima, then the sums (a second pair barrier after each read keeps the
+  // next write behind the partner's read)
+  __shared__ float xch[kPfHalves][kPfRows];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.Hq / a.Hkv, TQ = kPfRows / G;
-  const int tile = gridDim.x - 1 - blockIdx.x;  // the longest key ranges first
-  const int hkv = blockIdx.y, b = blockIdx.z;
-  const int t0 = tile * TQ;
-  const int t_end = min(a.Lq, t0 + TQ);  // this CTA's tokens [t0, t_end)
+  const int nqt = (a.Lq + TQ - 1) / TQ;
+  const int ntiles = nqt * a.B * a.Hkv;
   volatile int* abort = &abort_flag;
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, kPfLoaders);
+    mbar_init(&q_empty, 1);
+    mbar_init(&o_free, kPfSoftmax);
     for (int s = 0; s < S; ++s) {
       mbar_init(&kv_full[s], kPfLoaders);
       mbar_init(&kv_empty[s], 1);
@@ -164,8 +186,6 @@ __global__ void __launch_bounds__(pf_threads(NG), 1) prefill_attn_tc_kernel(PfAr
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], kPfSoftmax);
-    }
-    for (int i = 0; i < 2; ++i) {
       mbar_init(&p_full[i], kPfSoftmax);
       mbar_init(&pv_done[i], 1);
     }
@@ -175,10 +195,7 @@ __global__ void __launch_bounds__(pf_threads(NG), 1) prefill_attn_tc_kernel(PfAr
   __syncthreads();
 
   pdl_wait();  // q, the cache and the lengths come from earlier kernels
-  const int pos0 = a.seq_lens[b] - a.Lq;  // position of query token 0
-  const int kv_len = max(0, pos0 + t_end);  // keys seen by the CTA's last token
-  const int nkb = (kv_len + kPfKeys - 1) / kPfKeys;
-  if (warp == kPfMmaWarp) {
+  if (warp == kPfQkWarp) {
     tc_alloc(&tmem_base, kPfTmemCols);
     tc_relinquish();
   }
@@ -188,249 +205,266 @@ __global__ void __launch_bounds__(pf_threads(NG), 1) prefill_attn_tc_kernel(PfAr
   const uint32_t tb = tmem_base;
   pdl_launch();
 
-  if (warp > kPfMmaWarp + 1) {
+  if (warp > kPfPvWarp) {
     // ---------------- loaders ----------------
     const int lt = threadIdx.x - (kPfSoftmax + 64);
-    // Q row r = (token t0 + r / G, query head hkv G + r % G)
-    for (int e = lt; e < kPfRows * DC; e += kPfLoaders) {
-      const int r = e / DC, dc = e % DC;
-      const int t = t0 + r / G;
-      const bool ok = t < t_end;
-      const uint16_t* src = a.q + (((size_t)b * a.Lq + (ok ? t : 0)) * a.Hq + hkv * G + r % G) * D + dc * 8;
-      cp_async16_zfill(qs + (dc >> 3) * (kPfRows * 128) + r * 128 + (((dc & 7) ^ (r & 7)) << 4), src, ok);
-    }
-    cp_async_commit();
-    cp_async_wait<0>();
-    fence_proxy_async();  // generic-proxy writes -> the tensor core's (async proxy) reads
-    mbar_arrive(&q_full);
-    const int32_t* btr = a.bt + (size_t)b * a.max_blocks;
     // this thread's 16-byte column dc of keys k0, k0 + KSTEP, ... of every block
     constexpr int KSTEP = kPfLoaders / DC, KPT = kPfKeys / KSTEP;
     const int dc = lt % DC, k0 = lt / DC;
-    const size_t col = (size_t)hkv * a.head_stride + dc * 8;
     const uint32_t so0 = (dc >> 3) * (kPfKeys * 128) + (((dc & 7) ^ (k0 & 7)) << 4);  // KSTEP % 8 == 0
-    // block j is released once block j + 1 is in flight (wait for all but the newest copy
+    // block J is released once block J + 1 is in flight (wait for all but the newest copy
     // group): with S >= 3 stages the release never waits on a stage that needs it
     static_assert(S >= 3 && KSTEP % 8 == 0, "loader pipeline");
-    for (int j = 0; j < nkb; ++j) {
-      const int s = j % S;
-      if (j >= S) pf_wait(&kv_empty[s], ((j / S) - 1) & 1, abort, a.err);
-      uint8_t* ks = kvs + (size_t)s * 2 * kKV;
-      uint8_t* vs = ks + kKV;
-      int pg[KPT];
-#pragma unroll
-      for (int i = 0; i < KPT; ++i) {
-        const int kg = j * kPfKeys + k0 + i * KSTEP;
-        pg[i] = kg < kv_len ? btr[kg >> 4] : -1;
-      }
-#pragma unroll
-      for (int i = 0; i < KPT; ++i) {
-        const int kg = j * kPfKeys + k0 + i * KSTEP;
-        const size_t off = pg[i] >= 0 ? (size_t)pg[i] * a.page_stride + col + (size_t)(kg & 15) * D : 0;
-        const uint32_t so = so0 + (k0 + i * KSTEP) * 128;
-        cp_async16_zfill(ks + so, a.kc + off, pg[i] >= 0);
-        cp_async16_zfill(vs + so, a.vc + off, pg[i] >= 0);
+    int J = 0;
+    for (int i = blockIdx.x, k = 0; i < ntiles; i += gridDim.x, ++k) {
+      const PfTile T = pf_tile(a, i, nqt);
+      // Q row r = (token t0 + r / G, query head hkv G + r % G), once the previous tile's
+      // S MMAs are done with the buffer
+      if (k >= 1) pf_wait(&q_empty, (k - 1) & 1, abort, a.err);
+      for (int e = lt; e < kPfRows * DC; e += kPfLoaders) {
+        const int r = e / DC, c = e % DC;
+        const int t = T.t0 + r / G;
+        const bool ok = t < T.t_end;
+        const uint16_t* src = a.q + (((size_t)T.b * a.Lq + (ok ? t : 0)) * a.Hq + T.hkv * G + r % G) * D + c * 8;
+        cp_async16_zfill(qs + (c >> 3) * (kPfRows * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4), src, ok);
       }
       cp_async_commit();
-      if (j >= 1) {
-        cp_async_wait<1>();
-        fence_proxy_async();  // generic-proxy writes -> the tensor core's (async proxy) reads
-        mbar_arrive(&kv_full[(j - 1) % S]);
+      cp_async_wait<0>();
+      fence_proxy_async();  // generic-proxy writes -> the tensor core's (async proxy) reads
+      mbar_arrive(&q_full);
+      const int32_t* btr = a.bt + (size_t)T.b * a.max_blocks;
+      const size_t col = (size_t)T.hkv * a.head_stride + dc * 8;
+      for (int j = 0; j < T.nkb; ++j, ++J) {
+        const int s = J % S;
+        if (J >= S) pf_wait(&kv_empty[s], ((J / S) - 1) & 1, abort, a.err);
+        uint8_t* ks = kvs + (size_t)s * 2 * kKV;
+        uint8_t* vs = ks + kKV;
+        int pg[KPT];
+#pragma unroll
+        for (int q = 0; q < KPT; ++q) {
+          const int kg = j * kPfKeys + k0 + q * KSTEP;
+          pg[q] = kg < T.kv_len ? btr[kg >> 4] : -1;
+        }
+#pragma unroll
+        for (int q = 0; q < KPT; ++q) {
+          const int kg = j * kPfKeys + k0 + q * KSTEP;
+          const size_t off = pg[q] >= 0 ? (size_t)pg[q] * a.page_stride + col + (size_t)(kg & 15) * D : 0;
+          const uint32_t so = so0 + (k0 + q * KSTEP) * 128;
+          cp_async16_zfill(ks + so, a.kc + off, pg[q] >= 0);
+          cp_async16_zfill(vs + so, a.vc + off, pg[q] >= 0);
+        }
+        cp_async_commit();
+        if (j >= 1) {
+          cp_async_wait<1>();
+          fence_proxy_async();
+          mbar_arrive(&kv_full[(J - 1) % S]);
+        }
+      }
+      if (T.nkb > 0) {
+        cp_async_wait<0>();
+        fence_proxy_async();
+        mbar_arrive(&kv_full[(J - 1) % S]);
       }
     }
-    if (nkb > 0) {
-      cp_async_wait<0>();
-      fence_proxy_async();
-      mbar_arrive(&kv_full[(nkb - 1) % S]);
-    }
-  } else if (warp == kPfMmaWarp) {
-    // ---------------- S_j = Q K_j^T (one lane) ----------------
+  } else if (warp == kPfQkWarp) {
+    // ---------------- S_J = Q K_J^T (one lane) ----------------
     // A thread issues one tcgen05.mma every ~140 cycles whatever its shape (measured on B200),
     // about twice the tensor pipe's time for M = 128 x N = 128 x K = 16: QK^T and PV each get
-    // their own issuing warp.  They share no accumulator; P_j (softmax, after S_j completed)
-    // orders S_j before P_j V_j, so the PV warp's commit also covers the K half of a stage.
+    // their own issuing warp.  They share no accumulator; P_J (softmax, after S_J completed)
+    // orders S_J before P_J V_J, so the PV warp's commit also covers the K half of a stage.
     if (lane == 0) {
       constexpr uint32_t idS = tc_idesc_bf16(kPfRows, kPfKeys);
       const uint32_t sq = smem_u32(qs);
-      pf_wait(&q_full, 0, abort, a.err);
-      for (int j = 0; j < nkb; ++j) {
-        const int s = j % S, sb = j & 1;
-        pf_wait(&kv_full[s], (j / S) & 1, abort, a.err);
-        if (j >= 2) pf_wait(&s_free[sb], ((j >> 1) - 1) & 1, abort, a.err);
-        tc_fence_after();
-        const uint32_t sk = smem_u32(kvs + (size_t)s * 2 * kKV);
+      int J = 0;
+      for (int i = blockIdx.x, k = 0; i < ntiles; i += gridDim.x, ++k) {
+        const PfTile T = pf_tile(a, i, nqt);
+        pf_wait(&q_full, k & 1, abort, a.err);
+        for (int j = 0; j < T.nkb; ++j, ++J) {
+          const int s = J % S, sb = J & 1;
+          pf_wait(&kv_full[s], (J / S) & 1, abort, a.err);
+          if (J >= 2) pf_wait(&s_free[sb], ((J >> 1) - 1) & 1, abort, a.err);
+          tc_fence_after();
+          const uint32_t sk = smem_u32(kvs + (size_t)s * 2 * kKV);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          tc_mma(tb + COL_S + sb * kPfKeys, sw128_desc(sq + (kk >> 2) * (kPfRows * 128) + (kk & 3) * 32),
-                 sw128_desc(sk + (kk >> 2) * (kPfKeys * 128) + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
-        tc_commit(&s_full[sb]);
+          for (int kk = 0; kk < D / 16; ++kk)
+            tc_mma(tb + COL_S + sb * kPfKeys, sw128_desc(sq + (kk >> 2) * (kPfRows * 128) + (kk & 3) * 32),
+                   sw128_desc(sk + (kk >> 2) * (kPfKeys * 128) + (kk & 3) * 32), idS, kk > 0 ? 1u : 0u);
+          tc_commit(&s_full[sb]);
+        }
+        tc_commit(&q_empty);  // once this tile's S MMAs completed (at once if it had none)
       }
     }
     __syncwarp();
-  } else if (warp == kPfMmaWarp + 1) {
-    // ---------------- O += P_j V_j (one lane) ----------------
+  } else if (warp == kPfPvWarp) {
+    // ---------------- O += P_J V_J (one lane) ----------------
     if (lane == 0) {
       constexpr uint32_t idO = tc_idesc_bf16(kPfRows, D, true);
-      for (int jp = 0; jp < nkb; ++jp) {
-        const int s = jp % S;
-        pf_wait(&p_full[jp & 1], (jp >> 1) & 1, abort, a.err);
-        tc_fence_after();
-        const uint32_t sv = smem_u32(kvs + (size_t)s * 2 * kKV + kKV);
+      int J = 0;
+      for (int i = blockIdx.x, k = 0; i < ntiles; i += gridDim.x, ++k) {
+        const PfTile T = pf_tile(a, i, nqt);
+        for (int j = 0; j < T.nkb; ++j, ++J) {
+          const int s = J % S;
+          // a tile's first P V overwrites O: the softmax threads have read the previous tile's
+          if (j == 0 && k >= 1) pf_wait(&o_free, (k - 1) & 1, abort, a.err);
+          pf_wait(&p_full[J & 1], (J >> 1) & 1, abort, a.err);
+          tc_fence_after();
+          const uint32_t sv = smem_u32(kvs + (size_t)s * 2 * kKV + kKV);
 #pragma unroll
-        for (int kk = 0; kk < kPfKeys / 16; ++kk)  // 16 keys = two 8-row atoms = 2 KB
-          tc_mma_ta(tb + COL_O, tb + COL_P + (jp & 1) * (kPfKeys / 2) + kk * 8,
-                    sw128_mn_desc(sv + kk * 2048, kPfKeys * 128), idO, (jp > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(&pv_done[jp & 1]);
-        tc_commit(&kv_empty[s]);
+          for (int kk = 0; kk < kPfKeys / 16; ++kk)  // 16 keys = two 8-row atoms = 2 KB
+            tc_mma_ta(tb + COL_O, tb + COL_P + (J & 1) * (kPfKeys / 2) + kk * 8,
+                      sw128_mn_desc(sv + kk * 2048, kPfKeys * 128), idO, (j > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(&pv_done[J & 1]);
+          tc_commit(&kv_empty[s]);
+        }
       }
     }
     __syncwarp();
   } else {
-    // ---------------- softmax: thread = (query row = TMEM lane, key group g) ----------------
-    __shared__ uint16_t xch[NG][kPfRows];  // [group][row]: block maxima rounded up to bf16
-    const int quarter = warp & 3, g = warp >> 2;
+    // ---------------- softmax: thread = (query row = TMEM lane, key half hf) ----------------
+    const int quarter = warp & 3, hf = warp >> 2;
     const int r = quarter * 32 + lane;
-    const int t = t0 + r / G;
-    const bool valid = t < t_end;
-    const int pos = valid ? pos0 + t : -1;  // keys 0 .. pos are visible
     const uint32_t lrow = tb + ((uint32_t)(quarter * 32) << 16);
-    constexpr int HK = kPfKeys / NG;  // keys (S columns) per thread
-    constexpr int HD = D / NG;        // O columns rescaled / stored per thread
-    float m = -INFINITY, l = 0.f;  // l: this group's share of the row sum
-    for (int j = 0; j < nkb; ++j) {
-      const int sb = j & 1;
-      pf_wait(&s_full[sb], (j >> 1) & 1, abort, a.err);
-      tc_fence_after();
-      float v[HK];
+    constexpr int HK = kPfKeys / 2;  // keys (S columns) per thread
+    constexpr int HD = D / 2;        // O columns rescaled / stored per thread
+    int J = 0;
+    for (int i = blockIdx.x; i < ntiles; i += gridDim.x) {
+      const PfTile T = pf_tile(a, i, nqt);
+      const int t = T.t0 + r / G;
+      const bool valid = t < T.t_end;
+      const int pos = valid ? T.pos0 + t : -1;  // keys 0 .. pos are visible
+      float m = -INFINITY, l = 0.f;             // l: this half's share of the row sum
+      for (int j = 0; j < T.nkb; ++j, ++J) {
+        const int sb = J & 1;
+        pf_wait(&s_full[sb], (J >> 1) & 1, abort, a.err);
+        tc_fence_after();
+        float v[HK];
 #pragma unroll
-      for (int c = 0; c < HK / 16; ++c) tc_ld16(lrow + COL_S + sb * kPfKeys + g * HK + 16 * c, v + 16 * c);
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&s_free[sb]);  // S buffer sb may take S_{j+2}
-      const int lim = pos - j * kPfKeys - g * HK;  // key i of this group is visible iff i <= lim
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (lim >= HK - 1) {  // every key of this group visible: no mask
+        for (int c = 0; c < HK / 16; ++c) tc_ld16(lrow + COL_S + sb * kPfKeys + hf * HK + 16 * c, v + 16 * c);
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&s_free[sb]);  // S buffer sb may take S_{J+2}
+        const int lim = pos - j * kPfKeys - hf * HK;  // key i of this half is visible iff i <= lim
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        if (lim >= HK - 1) {  // every key of this half visible: no mask
 #pragma unroll
-        for (int i = 0; i < HK; ++i) mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
-      } else {
+          for (int q = 0; q < HK; ++q) mx4[q & 3] = fmaxf(mx4[q & 3], v[q]);
+        } else {
 #pragma unroll
-        for (int i = 0; i < HK; ++i) {
-          v[i] = i <= lim ? v[i] : -INFINITY;
-          mx4[i & 3] = fmaxf(mx4[i & 3], v[i]);
+          for (int q = 0; q < HK; ++q) {
+            v[q] = q <= lim ? v[q] : -INFINITY;
+            mx4[q & 3] = fmaxf(mx4[q & 3], v[q]);
+          }
         }
-      }
-      // raw scores: the scale (> 0) is applied to the maximum and folded into the exponent's FMA;
-      // the row's block maximum, rounded up to bf16 (an upper bound is all the reference needs)
-      xch[g][r] = bf16_up(fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2);
-      pf_group_sync(quarter, 32 * NG);
-      float mx = -INFINITY;
+        // raw scores: the scale (> 0) is applied to the maximum and folded into the exponent's FMA
+        float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
+        xch[hf][r] = mx;
+        pf_pair_sync(quarter);
+        mx = fmaxf(mx, xch[hf ^ 1][r]);  // the block maximum of the whole row
+        pf_pair_sync(quarter);
+        // both threads of a row take the same decision from the same (m, mx)
+        const bool grow = mx > m + kPfSlack || (m == -INFINITY && mx != -INFINITY);
+        const float alpha = grow ? ex2(m - mx) : 1.f;  // m = -inf: 0 (O and l are still zero)
+        if (grow) m = mx;
+        float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t pk[HK / 2];
+        if (m == -INFINITY) {  // nothing visible yet in this row
 #pragma unroll
-      for (int q = 0; q < NG; ++q) mx = fmaxf(mx, __uint_as_float((uint32_t)xch[q][r] << 16));
-      pf_group_sync(quarter, 32 * NG);  // every read done before the next block's writes
-      // all threads of a row take the same decision from the same (m, mx)
-      const bool grow = mx > m + kPfSlack || (m == -INFINITY && mx != -INFINITY);
-      const float alpha = grow ? ex2(m - mx) : 1.f;  // m = -inf: 0 (O and l are still zero)
-      if (grow) m = mx;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
-      uint32_t pk[HK / 2];
-      if (m == -INFINITY) {  // nothing visible yet in this row
+          for (int q = 0; q < HK / 2; ++q) pk[q] = 0u;
+        } else {
 #pragma unroll
-        for (int i = 0; i < HK / 2; ++i) pk[i] = 0u;
-      } else {
-#pragma unroll
-        for (int i = 0; i < HK / 2; ++i) {
-          const float p0 = ex2(fmaf(v[2 * i], a.scale_log2, -m));
-          const float p1 = ex2(fmaf(v[2 * i + 1], a.scale_log2, -m));
-          sum4[i & 3] += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
+          for (int q = 0; q < HK / 2; ++q) {
+            const float p0 = ex2(fmaf(v[2 * q], a.scale_log2, -m));
+            const float p1 = ex2(fmaf(v[2 * q + 1], a.scale_log2, -m));
+            sum4[q & 3] += p0 + p1;
+            pk[q] = pack_bf16x2(p0, p1);
+          }
         }
+        l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
+        if (J >= 2) {  // P buffer sb is free once P_{J-2} V_{J-2} is done
+          pf_wait(&pv_done[sb], ((J >> 1) - 1) & 1, abort, a.err);
+          tc_fence_after();
+        }
+        if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {  // a row maximum grew: O *= alpha
+          pf_wait(&pv_done[sb ^ 1], ((J - 1) >> 1) & 1, abort, a.err);  // after P_{J-1} V_{J-1}
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < HD / 16; ++c) {
+            float o[16];
+            tc_ld16(lrow + COL_O + hf * HD + 16 * c, o);
+            tc_wait_ld();
+            uint32_t w[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) w[q] = __float_as_uint(o[q] * alpha);
+            tc_st16(lrow + COL_O + hf * HD + 16 * c, w);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < HK / 32; ++c)
+          tc_st16(lrow + COL_P + sb * (kPfKeys / 2) + hf * (HK / 2) + 16 * c, pk + 16 * c);
+        tc_wait_st();
+        tc_fence_before();
+        mbar_arrive(&p_full[sb]);
       }
-      l = l * alpha + ((sum4[0] + sum4[1]) + (sum4[2] + sum4[3]));
-      if (j >= 2) {  // P buffer sb is free once P_{j-2} V_{j-2} is done
-        pf_wait(&pv_done[sb], ((j >> 1) - 1) & 1, abort, a.err);
+      // ---- O / l -> bf16 (this thread: columns [hf D / 2, (hf + 1) D / 2) of its row) ----
+      if (T.nkb > 0) {
+        pf_wait(&pv_done[(J - 1) & 1], ((J - 1) >> 1) & 1, abort, a.err);
         tc_fence_after();
       }
-      if (j >= 1 && __any_sync(0xffffffffu, alpha != 1.f)) {  // a row maximum grew: O *= alpha
-        pf_wait(&pv_done[sb ^ 1], ((j - 1) >> 1) & 1, abort, a.err);  // after P_{j-1} V_{j-1}
-        tc_fence_after();
+      xch[hf][r] = l;
+      pf_pair_sync(quarter);
+      const float lt = hf == 0 ? l + xch[1][r] : xch[0][r] + l;  // l0 + l1 in both
+      pf_pair_sync(quarter);
+      const float inv = lt > 0.f ? 1.f / lt : 0.f;
+      float o[HD];
+      if (T.nkb > 0) {
 #pragma unroll
-        for (int c = 0; c < HD / 16; ++c) {
-          float o[16];
-          tc_ld16(lrow + COL_O + g * HD + 16 * c, o);
-          tc_wait_ld();
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) w[i] = __float_as_uint(o[i] * alpha);
-          tc_st16(lrow + COL_O + g * HD + 16 * c, w);
-        }
-      }
-#pragma unroll
-      for (int c = 0; c < HK / 32; ++c)
-        tc_st16(lrow + COL_P + sb * (kPfKeys / 2) + g * (HK / 2) + 16 * c, pk + 16 * c);
-      tc_wait_st();
-      tc_fence_before();
-      mbar_arrive(&p_full[sb]);
-    }
-    // ---- O / l -> bf16 (this thread: columns [g D / NG, (g + 1) D / NG) of its row) ----
-    if (nkb > 0) {
-      pf_wait(&pv_done[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1, abort, a.err);
-      tc_fence_after();
-    }
-    // the row's sum over the groups, in group order, through the K / V ring (every copy into it
-    // and every MMA reading it has completed by now)
-    float* xl = reinterpret_cast<float*>(kvs);
-    xl[g * kPfRows + r] = l;
-    pf_group_sync(quarter, 32 * NG);
-    float lt = 0.f;
-#pragma unroll
-    for (int q = 0; q < NG; ++q) lt += xl[q * kPfRows + r];
-    const float inv = lt > 0.f ? 1.f / lt : 0.f;
-    uint16_t* dst = a.out + (((size_t)b * a.Lq + (valid ? t : 0)) * a.Hq + hkv * G + r % G) * D + g * HD;
-#pragma unroll
-    for (int c = 0; c < HD / 16; ++c) {
-      float o[16];
-      if (nkb > 0) {
-        tc_ld16(lrow + COL_O + g * HD + 16 * c, o);
+        for (int c = 0; c < HD / 16; ++c) tc_ld16(lrow + COL_O + hf * HD + 16 * c, o + 16 * c);
         tc_wait_ld();
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = 0.f;
+        for (int q = 0; q < HD; ++q) o[q] = 0.f;
       }
-      uint4 w0, w1;
-      w0.x = pack_bf16x2(o[0] * inv, o[1] * inv), w0.y = pack_bf16x2(o[2] * inv, o[3] * inv);
-      w0.z = pack_bf16x2(o[4] * inv, o[5] * inv), w0.w = pack_bf16x2(o[6] * inv, o[7] * inv);
-      w1.x = pack_bf16x2(o[8] * inv, o[9] * inv), w1.y = pack_bf16x2(o[10] * inv, o[11] * inv);
-      w1.z = pack_bf16x2(o[12] * inv, o[13] * inv), w1.w = pack_bf16x2(o[14] * inv, o[15] * inv);
+      tc_fence_before();
+      mbar_arrive(&o_free);  // the next tile's first P V may overwrite O
       if (valid) {
-        reinterpret_cast<uint4*>(dst + 16 * c)[0] = w0;
-        reinterpret_cast<uint4*>(dst + 16 * c)[1] = w1;
+        uint4* dst = reinterpret_cast<uint4*>(
+            a.out + (((size_t)T.b * a.Lq + t) * a.Hq + T.hkv * G + r % G) * D + hf * HD);
+#pragma unroll
+        for (int c = 0; c < HD / 8; ++c)
+          dst[c] = make_uint4(pack_bf16x2(o[8 * c] * inv, o[8 * c + 1] * inv),
+                              pack_bf16x2(o[8 * c + 2] * inv, o[8 * c + 3] * inv),
+                              pack_bf16x2(o[8 * c + 4] * inv, o[8 * c + 5] * inv),
+                              pack_bf16x2(o[8 * c + 6] * inv, o[8 * c + 7] * inv));
       }
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == kPfMmaWarp) {
+  if (warp == kPfQkWarp) {
     tc_fence_after();
     tc_dealloc(tb, kPfTmemCols);
   }
 }
 
-template <int D, int NG>
+template <int D>
 cudaError_t launch_pf(const PfArgs& a, cudaStream_t st) {
-  auto k = prefill_attn_tc_kernel<D, NG>;
+  auto k = prefill_attn_tc_kernel<D>;
   static PerDeviceOnce attr;
   const cudaError_t e =
       attr.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(D)); });
   if (e != cudaSuccess) return e;
+  // persistent: one CTA per SM (shared memory and TMEM allow one), each walking the tiles
+  // blockIdx.x, + gridDim.x, ... (the longest causal ranges first)
   const int TQ = kPfRows / (a.Hq / a.Hkv);
-  return launch_pdl(k, dim3((a.Lq + TQ - 1) / TQ, a.Hkv, a.B), dim3(pf_threads(NG)), pf_smem(D), st, a);
+  const long long ntiles = (long long)((a.Lq + TQ - 1) / TQ) * a.B * a.Hkv;
+  const int grid = (int)std::min<long long>(ntiles, sm_count());
+  return launch_pdl(k, dim3(grid), dim3(kPfThreads), pf_smem(D), st, a);
 }
 
 }  // namespace
 
 void prefill_attn_tc_set(int on) { g_prefill_tc = on != 0; }
-void prefill_attn_tc_set_groups(int ng) { g_prefill_ng = ng <= 2 ? 2 : 4; }
 
 // Launches of more than 64 query rows (the decode kernel would take three or more launches of
 // 32 rows, each over every page), G dividing 128, 16-byte aligned rows and pages.
@@ -464,8 +498,7 @@ cudaError_t launch_prefill_attn_tc(const void* q, int B, int Lq, int Hq, int Hkv
   a.scale_log2 = scale * 1.4426950408889634f;
   a.out = (uint16_t*)out;
   a.err = err;
-  if (g_prefill_ng == 2) return D == 64 ? launch_pf<64, 2>(a, st) : launch_pf<128, 2>(a, st);
-  return D == 64 ? launch_pf<64, 4>(a, st) : launch_pf<128, 4>(a, st);
+  return D == 64 ? launch_pf<64>(a, st) : launch_pf<128>(a, st);
 }
 
 }  // namespace higgs
