@@ -9,7 +9,7 @@
 // A tile is 128 query rows of one (sequence, kv head) -- TQ = 128 / G consecutive tokens x the
 // G query heads that share the kv head, so every K / V tile serves all of them -- walking the
 // keys 0 .. its last token's position in blocks of 128 (8 pages).  The kernel is persistent:
-// one CTA per SM takes tiles blockIdx.x, + gridDim.x, ..., and every ring runs on across its
+// one CTA per SM takes one tile per round (snake order over the CTAs), and every ring runs on across its
 // tiles, so the next tile's Q load and first S = Q K^T overlap the current tile's last blocks
 // and its epilogue.
 //   * 4 loader warps: 16-byte cp.async copies of Q and of each block's pages of K and V (zero-
@@ -141,6 +141,13 @@ __device__ __forceinline__ PfTile pf_tile(const PfArgs& a, int i, int nqt) {
   return T;
 }
 
+// This CTA's tile of round k, or -1 past the last: rounds alternate direction over the CTAs
+// (snake order), so the CTA given a round's longest tile gets the next round's shortest
+__device__ __forceinline__ int pf_tile_index(int k, int ntiles) {
+  const int i = k * gridDim.x + ((k & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
+  return i < ntiles ? i : -1;
+}
+
 template <int D>
 __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a) {
   constexpr int S = pf_stages(D);
@@ -216,7 +223,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     // group): with S >= 3 stages the release never waits on a stage that needs it
     static_assert(S >= 3 && KSTEP % 8 == 0, "loader pipeline");
     int J = 0;
-    for (int i = blockIdx.x, k = 0; i < ntiles; i += gridDim.x, ++k) {
+    for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
       const PfTile T = pf_tile(a, i, nqt);
       // Q row r = (token t0 + r / G, query head hkv G + r % G), once the previous tile's
       // S MMAs are done with the buffer
@@ -276,7 +283,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
       constexpr uint32_t idS = tc_idesc_bf16(kPfRows, kPfKeys);
       const uint32_t sq = smem_u32(qs);
       int J = 0;
-      for (int i = blockIdx.x, k = 0; i < ntiles; i += gridDim.x, ++k) {
+      for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
         const PfTile T = pf_tile(a, i, nqt);
         pf_wait(&q_full, k & 1, abort, a.err);
         for (int j = 0; j < T.nkb; ++j, ++J) {
@@ -300,7 +307,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     if (lane == 0) {
       constexpr uint32_t idO = tc_idesc_bf16(kPfRows, D, true);
       int J = 0;
-      for (int i = blockIdx.x, k = 0; i < ntiles; i += gridDim.x, ++k) {
+      for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
         const PfTile T = pf_tile(a, i, nqt);
         for (int j = 0; j < T.nkb; ++j, ++J) {
           const int s = J % S;
@@ -327,7 +334,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     constexpr int HK = kPfKeys / 2;  // keys (S columns) per thread
     constexpr int HD = D / 2;        // O columns rescaled / stored per thread
     int J = 0;
-    for (int i = blockIdx.x; i < ntiles; i += gridDim.x) {
+    for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
       const PfTile T = pf_tile(a, i, nqt);
       const int t = T.t0 + r / G;
       const bool valid = t < T.t_end;
@@ -454,8 +461,8 @@ cudaError_t launch_pf(const PfArgs& a, cudaStream_t st) {
   const cudaError_t e =
       attr.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(D)); });
   if (e != cudaSuccess) return e;
-  // persistent: one CTA per SM (shared memory and TMEM allow one), each walking the tiles
-  // blockIdx.x, + gridDim.x, ... (the longest causal ranges first)
+  // persistent: one CTA per SM (shared memory and TMEM allow one), each taking one tile per
+  // round (the longest causal ranges first)
   const int TQ = kPfRows / (a.Hq / a.Hkv);
   const long long ntiles = (long long)((a.Lq + TQ - 1) / TQ) * a.B * a.Hkv;
   const int grid = (int)std::min<long long>(ntiles, sm_count());
