@@ -21,7 +21,8 @@
 //     read from one of two TMEM P buffers, so S_{J+1} is computed while the softmax of block J
 //     runs and the softmax waits for P V only where it rescales O;
 //   * 8 softmax warps, two threads per query row (TMEM lane), one per half of the block's keys,
-//     exchanging the block maximum through shared memory: the causal mask, the running maximum
+//     exchanging the block maximum through shared memory when it may move the row's running
+//     maximum (a barrier reduction tells): the causal mask, the running maximum
 //     and sum in the exp2 domain, P as bf16 into TMEM, and the rescale of O in TMEM (each
 //     thread half of the row's columns) when a row's maximum grew by more than 2^8; at the end
 //     of a tile O / l as bf16.
@@ -115,6 +116,16 @@ constexpr float kPfSlack = 8.0f;
 // the two softmax threads of a row quarter (warps q and q + 4)
 __device__ __forceinline__ void pf_pair_sync(int quarter) {
   asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+}
+// the same barrier, returning whether `pred` held for any of the 64 threads
+__device__ __forceinline__ bool pf_pair_any(int quarter, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, 64, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(1 + quarter)
+      : "memory");
+  return r != 0;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -364,12 +375,17 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
         }
         // raw scores: the scale (> 0) is applied to the maximum and folded into the exponent's FMA
         float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * a.scale_log2;
-        xch[hf][r] = mx;
-        pf_pair_sync(quarter);
-        mx = fmaxf(mx, xch[hf ^ 1][r]);  // the block maximum of the whole row
-        pf_pair_sync(quarter);
-        // both threads of a row take the same decision from the same (m, mx)
-        const bool grow = mx > m + kPfSlack || (m == -INFINITY && mx != -INFINITY);
+        // the row maximum moves only if one half's block maximum exceeds m + slack: one barrier
+        // tells the 32 rows of the quarter whether any does; only then are the halves' maxima
+        // exchanged (both threads of a row then take the same decision from the same (m, mx))
+        bool grow = false;
+        if (pf_pair_any(quarter, mx > m + kPfSlack || (m == -INFINITY && mx != -INFINITY))) {
+          xch[hf][r] = mx;
+          pf_pair_sync(quarter);
+          mx = fmaxf(mx, xch[hf ^ 1][r]);  // the block maximum of the whole row
+          pf_pair_sync(quarter);
+          grow = mx > m + kPfSlack || (m == -INFINITY && mx != -INFINITY);
+        }
         const float alpha = grow ? ex2(m - mx) : 1.f;  // m = -inf: 0 (O and l are still zero)
         if (grow) m = mx;
         float sum4[4] = {0.f, 0.f, 0.f, 0.f};
