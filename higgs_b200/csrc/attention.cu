@@ -1652,7 +1652,7 @@ extern "C" int higgs_paged_attention(higgs_ctx* ctx, const void* q, int B, int L
   if (prefill_attn_tc_fits(Lq, Hq, Hkv, D, q, k_cache, v_cache, out, page_stride, head_stride)) {
     // prefill chunks: 128-row query tiles on the tensor cores, one launch, no workspace
     HG_CUDA(launch_prefill_attn_tc(q, B, Lq, Hq, Hkv, D, k_cache, v_cache, page_stride, head_stride,
-                                   block_table, max_blocks, seq_lens, scale, out, tc_err_ptr(),
+                                   block_table, max_blocks, seq_lens, scale, out, (int*)workspace, tc_err_ptr(),
                                    (cudaStream_t)stream));
     return HIGGS_OK;
   }

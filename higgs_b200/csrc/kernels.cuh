@@ -215,8 +215,8 @@ bool prefill_attn_tc_fits(int Lq, int Hq, int Hkv, int D, const void* q, const v
                           const void* out, int64_t page_stride, int64_t head_stride);
 cudaError_t launch_prefill_attn_tc(const void* q, int B, int Lq, int Hq, int Hkv, int D, const void* kc,
                                    const void* vc, int64_t page_stride, int64_t head_stride, const int32_t* bt,
-                                   int max_blocks, const int32_t* seq_lens, float scale, void* out, int* err,
-                                   cudaStream_t st);
+                                   int max_blocks, const int32_t* seq_lens, float scale, void* out, int* counters,
+                                   int* err, cudaStream_t st);
 int* tc_err_ptr();
 
 }  // namespace higgs

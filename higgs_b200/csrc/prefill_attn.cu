@@ -9,7 +9,7 @@
 // A tile is 128 query rows of one (sequence, kv head) -- TQ = 128 / G consecutive tokens x the
 // G query heads that share the kv head, so every K / V tile serves all of them -- walking the
 // keys 0 .. its last token's position in blocks of 128 (8 pages).  The kernel is persistent:
-// one CTA per SM takes one tile per round (snake order over the CTAs), and every ring runs on across its
+// one CTA per SM takes the next tile left (a global counter) whenever it starts one, and every ring runs on across its
 // tiles, so the next tile's Q load and first S = Q K^T overlap the current tile's last blocks
 // and its epilogue.
 //   * 4 loader warps: 16-byte cp.async copies of Q and of each block's pages of K and V (zero-
@@ -70,6 +70,7 @@ struct PfArgs {
   float scale_log2;
   uint16_t* out;
   int* err;
+  int* counters;  // [0] next tile, [1] CTAs finished: zero before the launch, zero after it
 };
 
 // 16 bytes global -> shared, or 16 zero bytes when !ok (nothing is read then)
@@ -152,11 +153,10 @@ __device__ __forceinline__ PfTile pf_tile(const PfArgs& a, int i, int nqt) {
   return T;
 }
 
-// This CTA's tile of round k, or -1 past the last: rounds alternate direction over the CTAs
-// (snake order), so the CTA given a round's longest tile gets the next round's shortest
-__device__ __forceinline__ int pf_tile_index(int k, int ntiles) {
-  const int i = k * gridDim.x + ((k & 1) ? gridDim.x - 1 - blockIdx.x : blockIdx.x);
-  return i < ntiles ? i : -1;
+constexpr int kPfTileRing = 4;  // tile indices handed from the scheduling thread to the roles
+
+__device__ __forceinline__ void pf_loaders_sync() {
+  asm volatile("bar.sync 5, %0;" ::"n"(kPfLoaders) : "memory");
 }
 
 template <int D>
@@ -184,6 +184,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
   // [half][row]: block maxima, then the sums (a second pair barrier after each read keeps the
   // next write behind the partner's read)
   __shared__ float xch[kPfHalves][kPfRows];
+  // tiles are taken dynamically, the longest causal ranges first: the first loader thread takes
+  // the CTA's next tile index from a global counter (the first round's is blockIdx.x) and hands
+  // it to the MMA lanes and the softmax threads through a small ring
+  __shared__ int tile_ring[kPfTileRing];
+  __shared__ __align__(8) uint64_t t_full[kPfTileRing];
+  __shared__ __align__(8) uint64_t t_empty[kPfTileRing];
+  __shared__ int loader_tile;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
 
@@ -207,10 +214,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
       mbar_init(&p_full[i], kPfSoftmax);
       mbar_init(&pv_done[i], 1);
     }
+    for (int i = 0; i < kPfTileRing; ++i) {
+      mbar_init(&t_full[i], 1);
+      mbar_init(&t_empty[i], kPfSoftmax + 2);
+    }
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+
+  // the tile of round k for the MMA lanes and the softmax threads (ntiles once none is left)
+  auto next_tile = [&](int k) {
+    pf_wait(&t_full[k % kPfTileRing], (k / kPfTileRing) & 1, abort, a.err);
+    const int i = *abort ? ntiles : tile_ring[k % kPfTileRing];
+    mbar_arrive(&t_empty[k % kPfTileRing]);
+    return i;
+  };
 
   pdl_wait();  // q, the cache and the lengths come from earlier kernels
   if (warp == kPfQkWarp) {
@@ -234,7 +253,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     // group): with S >= 3 stages the release never waits on a stage that needs it
     static_assert(S >= 3 && KSTEP % 8 == 0, "loader pipeline");
     int J = 0;
-    for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
+    for (int k = 0;; ++k) {
+      if (lt == 0) {
+        int i = k == 0 ? blockIdx.x : gridDim.x + atomicAdd(a.counters, 1);
+        if (i > ntiles || *abort) i = ntiles;
+        if (k >= kPfTileRing) pf_wait(&t_empty[k % kPfTileRing], ((k / kPfTileRing) - 1) & 1, abort, a.err);
+        tile_ring[k % kPfTileRing] = i;
+        mbar_arrive(&t_full[k % kPfTileRing]);
+        loader_tile = i;
+      }
+      pf_loaders_sync();
+      const int i = loader_tile;
+      pf_loaders_sync();  // every loader has read it before the next round's write
+      if (i >= ntiles) break;
       const PfTile T = pf_tile(a, i, nqt);
       // Q row r = (token t0 + r / G, query head hkv G + r % G), once the previous tile's
       // S MMAs are done with the buffer
@@ -294,7 +325,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
       constexpr uint32_t idS = tc_idesc_bf16(kPfRows, kPfKeys);
       const uint32_t sq = smem_u32(qs);
       int J = 0;
-      for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
+      for (int k = 0;; ++k) {
+        const int i = next_tile(k);
+        if (i >= ntiles) break;
         const PfTile T = pf_tile(a, i, nqt);
         pf_wait(&q_full, k & 1, abort, a.err);
         for (int j = 0; j < T.nkb; ++j, ++J) {
@@ -318,7 +351,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     if (lane == 0) {
       constexpr uint32_t idO = tc_idesc_bf16(kPfRows, D, true);
       int J = 0;
-      for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
+      for (int k = 0;; ++k) {
+        const int i = next_tile(k);
+        if (i >= ntiles) break;
         const PfTile T = pf_tile(a, i, nqt);
         for (int j = 0; j < T.nkb; ++j, ++J) {
           const int s = J % S;
@@ -345,7 +380,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     constexpr int HK = kPfKeys / 2;  // keys (S columns) per thread
     constexpr int HD = D / 2;        // O columns rescaled / stored per thread
     int J = 0;
-    for (int k = 0, i; (i = pf_tile_index(k, ntiles)) >= 0; ++k) {
+    for (int k = 0;; ++k) {
+      const int i = next_tile(k);
+      if (i >= ntiles) break;
       const PfTile T = pf_tile(a, i, nqt);
       const int t = T.t0 + r / G;
       const bool valid = t < T.t_end;
@@ -468,6 +505,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) prefill_attn_tc_kernel(PfArgs a
     tc_fence_after();
     tc_dealloc(tb, kPfTmemCols);
   }
+  if (threadIdx.x == 0) {  // the last CTA to finish leaves the tile counters at zero
+    __threadfence();
+    if (atomicAdd(a.counters + 1, 1) == (int)gridDim.x - 1) {
+      a.counters[0] = 0;
+      a.counters[1] = 0;
+      __threadfence();
+    }
+  }
 }
 
 template <int D>
@@ -477,8 +522,8 @@ cudaError_t launch_pf(const PfArgs& a, cudaStream_t st) {
   const cudaError_t e =
       attr.run([&] { return cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pf_smem(D)); });
   if (e != cudaSuccess) return e;
-  // persistent: one CTA per SM (shared memory and TMEM allow one), each taking one tile per
-  // round (the longest causal ranges first)
+  // persistent: one CTA per SM (shared memory and TMEM allow one), each taking the next tile
+  // left (the longest causal ranges first)
   const int TQ = kPfRows / (a.Hq / a.Hkv);
   const long long ntiles = (long long)((a.Lq + TQ - 1) / TQ) * a.B * a.Hkv;
   const int grid = (int)std::min<long long>(ntiles, sm_count());
@@ -503,8 +548,8 @@ bool prefill_attn_tc_fits(int Lq, int Hq, int Hkv, int D, const void* q, const v
 
 cudaError_t launch_prefill_attn_tc(const void* q, int B, int Lq, int Hq, int Hkv, int D, const void* kc,
                                    const void* vc, int64_t page_stride, int64_t head_stride, const int32_t* bt,
-                                   int max_blocks, const int32_t* seq_lens, float scale, void* out, int* err,
-                                   cudaStream_t st) {
+                                   int max_blocks, const int32_t* seq_lens, float scale, void* out, int* counters,
+                                   int* err, cudaStream_t st) {
   PfArgs a;
   a.q = (const uint16_t*)q;
   a.kc = (const uint16_t*)kc;
@@ -521,6 +566,7 @@ cudaError_t launch_prefill_attn_tc(const void* q, int B, int Lq, int Hq, int Hkv
   a.scale_log2 = scale * 1.4426950408889634f;
   a.out = (uint16_t*)out;
   a.err = err;
+  a.counters = counters;
   return D == 64 ? launch_pf<64>(a, st) : launch_pf<128>(a, st);
 }
 

@@ -294,7 +294,11 @@ def test_prefill_attention_tc(B, Lq, Hq, Hkv, D, lens):
     args = (bf(q), bf(kc), bf(vc), t(bt), t(sl), max(lens))
     got = to_np_bf(o.paged_attention(*args))
     np.testing.assert_allclose(orc.bf16_to_f32(got), ref, atol=1e-2, rtol=1e-2)
-    assert np.array_equal(got, to_np_bf(o.paged_attention(*args)))
+    # one workspace twice: the tile counters in its first 4 KB are left at zero
+    ws = o.attention_workspace(B, Lq, Hq, Hkv, D, max(lens), DEV)
+    assert np.array_equal(got, to_np_bf(o.paged_attention(*args, workspace=ws)))
+    assert np.array_equal(got, to_np_bf(o.paged_attention(*args, workspace=ws)))
+    assert int(ws[:4096].count_nonzero()) == 0
     ffi.call("higgs_set_option", b"attn_prefill_tc", 0)
     try:
         old = to_np_bf(o.paged_attention(*args))
