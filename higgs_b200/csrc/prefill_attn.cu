@@ -9,9 +9,9 @@
 // A tile is 128 query rows of one (sequence, kv head) -- TQ = 128 / G consecutive tokens x the
 // G query heads that share the kv head, so every K / V tile serves all of them -- walking the
 // keys 0 .. its last token's position in blocks of 128 (8 pages).  The kernel is persistent:
-// one CTA per SM takes the next tile left (a global counter) whenever it starts one, and every ring runs on across its
-// tiles, so the next tile's Q load and first S = Q K^T overlap the current tile's last blocks
-// and its epilogue.
+// one CTA per SM takes the next tile left (a global counter, tiles ordered longest causal
+// range first) whenever it starts one, and every ring runs on across its tiles, so the next
+// tile's Q load and first S = Q K^T overlap the current tile's last blocks and its epilogue.
 //   * 4 loader warps: 16-byte cp.async copies of Q and of each block's pages of K and V (zero-
 //     filled past the keys the tile can see) into 128-byte-swizzled shared tiles with the keys
 //     as rows, which is K-major for S = Q K^T and MN-major for O += P V; a 3-stage ring (4 at
@@ -22,11 +22,11 @@
 //     runs and the softmax waits for P V only where it rescales O;
 //   * 8 softmax warps, two threads per query row (TMEM lane), one per half of the block's keys,
 //     exchanging the block maximum through shared memory when it may move the row's running
-//     maximum (a barrier reduction tells): the causal mask, the running maximum
-//     and sum in the exp2 domain, P as bf16 into TMEM, and the rescale of O in TMEM (each
-//     thread half of the row's columns) when a row's maximum grew by more than 2^8; at the end
-//     of a tile O / l as bf16.
-// Tiles with the longest key ranges come first.  TMEM is allocated once, after
+//     maximum (a barrier reduction tells): the causal mask, the running maximum and sum in the
+//     exp2 domain, P as bf16 into TMEM, and the rescale of O in TMEM (each thread half of the
+//     row's columns) when a row's maximum grew by more than 2^8; at the end of a tile O / l as
+//     bf16.
+// TMEM is allocated once, after
 // griddepcontrol.wait.  Every mbarrier wait is bounded (about 2 s; the first timeout makes the
 // CTA's other waits give up too, and sets the flag higgs_tc_error reports).
 #include <algorithm>
